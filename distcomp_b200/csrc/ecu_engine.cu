@@ -1,0 +1,1261 @@
+// ecu_engine.cu -- the llama token loop on one B200, behind engine_cuda.h.
+//
+// One context = one stage (EMBED / a LAYERS range / HEAD, src/engine.h:23-27)
+// or the whole model (FULL) resident on one device.  A step is a fixed
+// sequence of kernels on the context's stream, launched with programmatic
+// dependent launch so that each GEMV starts streaming its weights while the
+// previous kernel drains, and captured once into a CUDA graph that every
+// later token replays.  Per-token inputs (token, position) live in device
+// StepState, so the graph is position independent.
+#include "../../include/engine_cuda.h"
+#include "ecu_attn.cuh"
+#include "ecu_gemv.cuh"
+#include "ecu_misc.cuh"
+#include "ecu_model.h"
+
+#include <atomic>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+static std::atomic<uint64_t> g_launches{0};
+
+#define CK(call)                                                                        \
+    do {                                                                                \
+        cudaError_t e_ = (call);                                                        \
+        if (e_ != cudaSuccess) {                                                        \
+            ecu_set_error(nullptr, 0, "%s failed: %s", #call, cudaGetErrorString(e_)); \
+            return -1;                                                                  \
+        }                                                                               \
+    } while (0)
+
+// ------------------------------------------------------------ launching --
+
+struct Launcher {
+    cudaStream_t stream = nullptr;
+    bool         pdl = true;
+    int          count = 0;       // kernels enqueued since the last reset
+    cudaError_t  err = cudaSuccess;
+
+    template <typename... KArgs, typename... Args>
+    void operator()(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, Args &&...args)
+    {
+        cudaLaunchConfig_t   cfg = {};
+        cudaLaunchAttribute  attr[1];
+        cfg.gridDim = grid;
+        cfg.blockDim = block;
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = stream;
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = pdl ? 1 : 0;
+        cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+        if (e != cudaSuccess && err == cudaSuccess) err = e;
+        count++;
+    }
+};
+
+static int num_sms(int dev)
+{
+    static int cache[64] = {0};
+    if (dev >= 0 && dev < 64 && cache[dev]) return cache[dev];
+    int n = 148;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (dev >= 0 && dev < 64) cache[dev] = n;
+    return n;
+}
+
+// ------------------------------------------------------------- GEMV plan --
+
+static bool fast_ok(const DevMat &m)
+{
+    return !m.zero && (m.layout == LAY_SPLIT4 || m.layout == LAY_SPLIT8) && m.n_in % 1024 == 0 &&
+           m.n_in / 1024 <= 31;
+}
+
+template <int FMT, bool NORM, int EPI>
+static void fast_attr_once()
+{
+    static std::atomic<uint64_t> done{0};     // one bit per device
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(done.load() & bit)) {
+        cudaFuncSetAttribute(k_gemv_fast<FMT, NORM, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             227 * 1024);
+        done |= bit;
+    }
+}
+
+struct FastPlan {
+    int    grid, threads, rows_per_cta, stage_rows;
+    size_t smem;
+};
+
+static FastPlan plan_fast(const DevMat &m, int epi, int sms)
+{
+    FastPlan p;
+    const int nkg = m.n_in / 1024;
+    int rowpar = 16 / nkg;
+    if (rowpar < 1) rowpar = 1;
+    if (rowpar > 4) rowpar = 4;
+    while (32 * (nkg * rowpar + 1) > 1024) rowpar--;
+    p.threads = 32 * (nkg * rowpar + 1);
+    int grid = sms;
+    for (;;) {
+        int rpc = (m.n_out + grid - 1) / grid;
+        if (epi == EPI_SWIGLU) rpc = (rpc + 1) & ~1;
+        if ((size_t)rpc * nkg * sizeof(float) <= 48 * 1024 || grid >= m.n_out) {
+            p.rows_per_cta = rpc;
+            break;
+        }
+        grid += sms;
+    }
+    p.grid = (m.n_out + p.rows_per_cta - 1) / p.rows_per_cta;
+    int sr = (int)(20480 / m.row_bytes);
+    if (sr < 1) sr = 1;
+    if (sr > p.rows_per_cta) sr = p.rows_per_cta;
+    p.stage_rows = sr;
+    p.smem = fast_smem_plan(m.row_bytes, sr, p.rows_per_cta, nkg).total;
+    return p;
+}
+
+template <int FMT, bool NORM, int EPI>
+static void launch_fast_t(Launcher &L, const GemvArgs &a, const FastPlan &p)
+{
+    fast_attr_once<FMT, NORM, EPI>();
+    L(k_gemv_fast<FMT, NORM, EPI>, dim3(p.grid), dim3(p.threads), p.smem, a);
+}
+
+template <int FMT, bool NORM>
+static void launch_fast_e(Launcher &L, const GemvArgs &a, const FastPlan &p, int epi)
+{
+    switch (epi) {
+    case EPI_STORE:  launch_fast_t<FMT, NORM, EPI_STORE>(L, a, p); break;
+    case EPI_ADD:    launch_fast_t<FMT, NORM, EPI_ADD>(L, a, p); break;
+    case EPI_SWIGLU: launch_fast_t<FMT, NORM, EPI_SWIGLU>(L, a, p); break;
+    default:         launch_fast_t<FMT, NORM, EPI_ARGMAX>(L, a, p); break;
+    }
+}
+
+// Scratch a GEMV launch may need (argmax partials/counter, normed input).
+struct GemvScratch {
+    float    *xn = nullptr;        // >= max n_in floats (generic-path RMSNorm)
+    float    *part_val = nullptr;  // >= grid
+    int      *part_idx = nullptr;
+    unsigned *counter = nullptr;
+    int      *status = nullptr;
+};
+
+// y (epi) W * rmsnorm?(x).  norm_w null = no prologue.  For the argmax
+// epilogue `a` carries the extra outputs.
+static void enqueue_gemv(Launcher &L, int sms, const DevMat &m, const float *x, const float *norm_w,
+                         float eps, float *y, int epi, const GemvScratch &s, GemvArgs a)
+{
+    a.m = m;
+    a.eps = eps;
+    a.y = y;
+    a.part_val = s.part_val;
+    a.part_idx = s.part_idx;
+    a.counter = s.counter;
+    a.status = s.status;
+    if (fast_ok(m) && (epi != EPI_SWIGLU || m.n_out % 2 == 0)) {
+        FastPlan p = plan_fast(m, epi, sms);
+        a.x = x;
+        a.norm_w = norm_w;
+        a.rows_per_cta = p.rows_per_cta;
+        a.stage_rows = p.stage_rows;
+        const bool norm = norm_w != nullptr;
+        if (m.layout == LAY_SPLIT4) {
+            if (norm) launch_fast_e<4, true>(L, a, p, epi);
+            else launch_fast_e<4, false>(L, a, p, epi);
+        } else {
+            if (norm) launch_fast_e<8, true>(L, a, p, epi);
+            else launch_fast_e<8, false>(L, a, p, epi);
+        }
+        return;
+    }
+    const float *in = x;
+    if (norm_w) {
+        L(k_rmsnorm, dim3(1), dim3(256), 0, x, norm_w, m.n_in, eps, s.xn);
+        in = s.xn;
+    }
+    a.x = in;
+    const int warps = 8, grid = (m.n_out + warps - 1) / warps;
+    const int g = grid < 4 * sms ? grid : 4 * sms;
+    switch (epi) {
+    case EPI_STORE: L(k_gemv_generic<EPI_STORE>, dim3(g), dim3(32 * warps), 0, a); break;
+    case EPI_ADD:   L(k_gemv_generic<EPI_ADD>, dim3(g), dim3(32 * warps), 0, a); break;
+    default:        L(k_gemv_generic<EPI_ARGMAX>, dim3(g), dim3(32 * warps), 0, a); break;
+    }
+}
+
+// ------------------------------------------------------------- context --
+
+struct LayerDev {
+    // attention projections: one fused matrix (rows q|k|v) or three
+    std::vector<DevMat> qkv;       // each writes rows [qkv_off[i], ...) of the qkv buffer
+    std::vector<int>    qkv_off;
+    DevMat              o;
+    bool                gu_fused = false;
+    DevMat              gu, g, u;  // fused: interleaved rows (gate j = 2j, up j = 2j+1)
+    DevMat              d;
+    float *attn_norm = nullptr, *ffn_norm = nullptr;
+    float *bq = nullptr, *bk = nullptr, *bv = nullptr;
+    // source tensors, for ecu_dequant_tensor
+    struct Src { std::string name; const DevMat *m; int row0, rstride, n_in; size_t elems; };
+};
+
+struct ecu_ctx {
+    int         device = 0, sms = 148;
+    int         stage = 0, first = 0, last = 0, pos = 0;
+    EcuGeom     g;
+    cudaStream_t stream = nullptr;
+    bool        pdl = true, use_graph = true;
+    std::vector<void *> allocs;
+    size_t      bytes = 0;
+
+    std::vector<LayerDev> layers;
+    DevMat   emb, out;            // EMBED/FULL: emb; HEAD/FULL: out (logits matrix)
+    float   *out_norm = nullptr;
+    float   *rope_cs = nullptr;
+    float   *kc = nullptr, *vc = nullptr;   // [layers][nkv][n_ctx][hd]
+    float   *state = nullptr;     // n_embd + 1
+    float   *qkv = nullptr, *att = nullptr, *h = nullptr, *gtmp = nullptr, *utmp = nullptr;
+    float   *logits = nullptr;
+    float   *attn_part = nullptr;
+    unsigned *attn_cnt = nullptr;
+    int      n_split = 1;
+    GemvScratch scr;
+    StepState *st = nullptr;      // device
+    StepState *h_st = nullptr;    // pinned host slots, one per position: an
+                                  // async copy may still be reading slot p
+                                  // while the host fills slot p+1
+    int        n_hslots = 0;
+    float    *h_state = nullptr;  // pinned host staging, n_embd + 1
+    int      *tok_hist = nullptr; // device [n_ctx]
+    bool      have_logits = false;
+    int       last_pick = 0;
+
+    cudaGraphExec_t graph = nullptr;   // the full step
+    int             graph_kernels = 0;
+
+    struct SrcRef { std::string name; DevMat m; int row0, rstride; size_t elems; int n_in; };
+    std::vector<SrcRef> srcs;
+
+    template <class T> T *dalloc(size_t n)
+    {
+        // 256 bytes of zeroed slack: the reference's Q8_K decoder reads its
+        // 32 scales 28 bytes past a 292-byte block (src/gguf.c:655), so a
+        // device copy of a Q8_K tensor must be readable that far past its end
+        void *p = nullptr;
+        if (cudaMalloc(&p, n * sizeof(T) + 256) != cudaSuccess) return nullptr;
+        cudaMemset((uint8_t *)p + n * sizeof(T), 0, 256);
+        allocs.push_back(p);
+        bytes += n * sizeof(T);
+        return (T *)p;
+    }
+};
+
+static size_t align16(size_t v) { return (v + 15) & ~(size_t)15; }
+
+// Device row length of a matrix of type t with n_in inputs in `layout`.
+static size_t dev_row_bytes(int t, int n_in, int layout)
+{
+    if (layout == LAY_SPLIT4) return align16((size_t)n_in / 32 * 18);
+    if (layout == LAY_SPLIT8) return align16((size_t)n_in / 32 * 34);
+    if (t == GT_F32) return (size_t)n_in * 4;
+    if (t == GT_F16) return (size_t)n_in * 2;
+    return (size_t)(n_in / blk_elems(t)) * blk_bytes(t);
+}
+
+static int choose_layout(int t, int n_in)
+{
+    if (n_in % 1024 == 0 && n_in / 1024 <= 31) {
+        if (t == GT_Q4_0) return LAY_SPLIT4;
+        if (t == GT_Q8_0) return LAY_SPLIT8;
+    }
+    return LAY_RAW;
+}
+
+// Zero-output rule of the reference matvec: a quantised tensor whose n_in
+// is not a multiple of its block (engine.c:317-320) or a type gguf_dequant
+// rejects (engine.c:332-337) contributes zeros.
+static bool zero_rule(int t, int n_in)
+{
+    if (t == GT_F32 || t == GT_F16) return false;
+    if (n_in % blk_elems(t)) return true;
+    return !dq_supported(t);
+}
+
+// Upload `rows` rows of tensor `src` (n_in inputs each) into device matrix
+// `m` at rows row0, row0+rstride, ...  `stage` is a device staging buffer.
+static int upload_rows(ecu_ctx *c, const EcuTensor *src, int n_in, int rows, DevMat &m, int row0,
+                       int rstride, uint8_t *stage)
+{
+    if (m.zero) return 0;
+    const size_t src_row = (size_t)ecu_type_nbytes(src->type, (size_t)n_in);
+    const size_t nbytes = src_row * (size_t)rows;
+    CK(cudaMemcpyAsync(stage, src->data, nbytes, cudaMemcpyHostToDevice, c->stream));
+    const int nb = n_in / 32;
+    const int grid = 4 * c->sms, blk = 256;
+    uint8_t  *dst = const_cast<uint8_t *>(m.data);
+    if (m.layout == LAY_SPLIT4)
+        k_repack_q4_0<<<grid, blk, 0, c->stream>>>(stage, nb, rows, dst, m.row_bytes, row0, rstride);
+    else if (m.layout == LAY_SPLIT8)
+        k_repack_q8_0<<<grid, blk, 0, c->stream>>>(stage, nb, rows, dst, m.row_bytes, row0, rstride);
+    else
+        k_copy_rows<<<grid, blk, 0, c->stream>>>(stage, src_row, rows, dst, m.row_bytes, row0, rstride);
+    CK(cudaGetLastError());
+    CK(cudaStreamSynchronize(c->stream));   // the staging buffer is reused
+    return 0;
+}
+
+static DevMat make_mat(ecu_ctx *c, int type, int n_in, int n_out, bool allow_split)
+{
+    DevMat m;
+    m.type = type;
+    m.n_in = n_in;
+    m.n_out = n_out;
+    m.zero = zero_rule(type, n_in);
+    m.layout = allow_split ? choose_layout(type, n_in) : LAY_RAW;
+    m.row_bytes = dev_row_bytes(type, n_in, m.layout);
+    m.total = (size_t)n_in * n_out;
+    if (!m.zero) m.data = c->dalloc<uint8_t>(m.row_bytes * (size_t)n_out);
+    return m;
+}
+
+// fp32 copy of the first n elements of a small tensor (norms, biases);
+// zeros when the reference's row_to_float would fail (engine.c:360-364).
+static float *upload_vec(ecu_ctx *c, const EcuTensor *t, size_t n, uint8_t *stage)
+{
+    float *d = c->dalloc<float>(n);
+    if (!d) return nullptr;
+    cudaMemsetAsync(d, 0, n * sizeof(float), c->stream);
+    const int   ty = (int)t->type;
+    const size_t total = t->elems();
+    const bool  ok = dq_supported(ty) && n <= total &&
+                    (ty == GT_F32 || ty == GT_F16 || (n + blk_elems(ty) - 1) / blk_elems(ty) <= total / blk_elems(ty));
+    if (ok && n > 0) {
+        size_t nbytes = (ty == GT_F32 || ty == GT_F16)
+                            ? ecu_type_nbytes(ty, n)
+                            : ((n + blk_elems(ty) - 1) / blk_elems(ty)) * blk_bytes(ty);
+        cudaMemcpyAsync(stage, t->data, nbytes, cudaMemcpyHostToDevice, c->stream);
+        k_dequant_raw<<<64, 256, 0, c->stream>>>(ty, stage, 0, n, d);
+    }
+    cudaStreamSynchronize(c->stream);
+    return d;
+}
+
+static void ctx_free(ecu_ctx *c)
+{
+    if (!c) return;
+    if (c->device >= 0) cudaSetDevice(c->device);
+    if (c->graph) cudaGraphExecDestroy(c->graph);
+    for (void *p : c->allocs) cudaFree(p);
+    if (c->h_st) cudaFreeHost(c->h_st);
+    if (c->h_state) cudaFreeHost(c->h_state);
+    if (c->stream) cudaStreamDestroy(c->stream);
+    delete c;
+}
+
+// ------------------------------------------------------------- the step --
+
+static void enqueue_layer(ecu_ctx *c, Launcher &L, int li)
+{
+    LayerDev   &ly = c->layers[li];
+    const EcuGeom &g = c->g;
+    const int   hd = g.head_dim, qdim = g.n_head * hd, kvdim = g.n_head_kv * hd;
+    GemvArgs    a = {};
+    a.st = c->st;
+
+    // (1) RMSNorm + Q/K/V projections
+    if (ly.qkv.size() == 1) {
+        enqueue_gemv(L, c->sms, ly.qkv[0], c->state, ly.attn_norm, g.eps, c->qkv, EPI_STORE, c->scr, a);
+    } else {
+        L(k_rmsnorm, dim3(1), dim3(256), 0, (const float *)c->state, (const float *)ly.attn_norm,
+          g.n_embd, g.eps, c->scr.xn);
+        for (size_t i = 0; i < ly.qkv.size(); i++)
+            enqueue_gemv(L, c->sms, ly.qkv[i], c->scr.xn, nullptr, g.eps, c->qkv + ly.qkv_off[i],
+                         EPI_STORE, c->scr, a);
+    }
+    // (2) bias + RoPE + KV append + attention
+    AttnArgs aa;
+    aa.qkv = c->qkv;
+    aa.bq = ly.bq;
+    aa.bk = ly.bk;
+    aa.bv = ly.bv;
+    aa.rope_cs = c->rope_cs;
+    const size_t plane = (size_t)g.n_head_kv * g.n_ctx * hd;
+    aa.kc = c->kc + (size_t)li * plane;
+    aa.vc = c->vc + (size_t)li * plane;
+    aa.att = c->att;
+    aa.part = c->attn_part;
+    aa.counter = c->attn_cnt;
+    aa.st = c->st;
+    aa.n_head = g.n_head;
+    aa.n_kv = g.n_head_kv;
+    aa.n_rep = g.n_rep;
+    aa.n_ctx = g.n_ctx;
+    aa.n_split = c->n_split;
+    aa.kscale = 1.0f / sqrtf((float)hd);
+    dim3 ag(g.n_head_kv, c->n_split);
+#define ATT_CASE(HD_, R_) \
+    if (hd == HD_ && g.n_rep == R_) { L(k_attention<HD_, R_>, ag, dim3(ATT_THREADS), 0, aa); } else
+    ATT_CASE(128, 1) ATT_CASE(128, 2) ATT_CASE(128, 4) ATT_CASE(128, 8)
+    ATT_CASE(64, 1) ATT_CASE(64, 2) ATT_CASE(64, 4) ATT_CASE(64, 8)
+    ATT_CASE(32, 1) ATT_CASE(32, 2) ATT_CASE(32, 4) ATT_CASE(32, 8) {}
+#undef ATT_CASE
+    (void)qdim;
+    (void)kvdim;
+    // (3) x += Wo * att
+    enqueue_gemv(L, c->sms, ly.o, c->att, nullptr, g.eps, c->state, EPI_ADD, c->scr, a);
+    // (4) RMSNorm + gate/up + SwiGLU
+    if (ly.gu_fused) {
+        enqueue_gemv(L, c->sms, ly.gu, c->state, ly.ffn_norm, g.eps, c->h, EPI_SWIGLU, c->scr, a);
+    } else {
+        L(k_rmsnorm, dim3(1), dim3(256), 0, (const float *)c->state, (const float *)ly.ffn_norm,
+          g.n_embd, g.eps, c->scr.xn);
+        enqueue_gemv(L, c->sms, ly.g, c->scr.xn, nullptr, g.eps, c->gtmp, EPI_STORE, c->scr, a);
+        enqueue_gemv(L, c->sms, ly.u, c->scr.xn, nullptr, g.eps, c->utmp, EPI_STORE, c->scr, a);
+        L(k_swiglu, dim3((g.n_ff + 255) / 256), dim3(256), 0, (const float *)c->gtmp,
+          (const float *)c->utmp, c->h, g.n_ff);
+    }
+    // (5) x += Wd * h
+    enqueue_gemv(L, c->sms, ly.d, c->h, nullptr, g.eps, c->state, EPI_ADD, c->scr, a);
+}
+
+static void enqueue_head(ecu_ctx *c, Launcher &L, bool advance)
+{
+    const EcuGeom &g = c->g;
+    // normed state in place: it is both HEAD's out[0..n_embd) and the GEMV input
+    L(k_rmsnorm, dim3(1), dim3(256), 0, (const float *)c->state, (const float *)c->out_norm, g.n_embd,
+      g.eps, c->state);
+    GemvArgs a = {};
+    a.st = c->st;
+    a.tok_hist = c->tok_hist;
+    a.tok_out = c->state + g.n_embd;
+    a.advance_pos = advance ? 1 : 0;
+    enqueue_gemv(L, c->sms, c->out, c->state, nullptr, g.eps, c->logits, EPI_ARGMAX, c->scr, a);
+}
+
+// Kernels of one step of the stage: nl layers (LAYERS/FULL) from layer 0.
+static void enqueue_step(ecu_ctx *c, Launcher &L, int nl)
+{
+    if (c->stage == ECU_STAGE_EMBED || c->stage == ECU_STAGE_FULL)
+        L(k_embed, dim3(8), dim3(256), 0, c->emb, (const StepState *)c->st, c->state, c->g.n_embd);
+    if (c->stage == ECU_STAGE_LAYERS || c->stage == ECU_STAGE_FULL)
+        for (int i = 0; i < nl; i++) enqueue_layer(c, L, i);
+    if (c->stage == ECU_STAGE_LAYERS) L(k_step_advance, dim3(1), dim3(32), 0, c->st);
+    if (c->stage == ECU_STAGE_HEAD || c->stage == ECU_STAGE_FULL)
+        enqueue_head(c, L, c->stage == ECU_STAGE_FULL);
+}
+
+static int n_stage_layers(const ecu_ctx *c)
+{
+    return (c->stage == ECU_STAGE_LAYERS || c->stage == ECU_STAGE_FULL) ? c->last - c->first + 1 : 0;
+}
+
+// Enqueue one full step: graph replay when enabled (captured on first use).
+static int run_step(ecu_ctx *c)
+{
+    if (c->use_graph) {
+        if (!c->graph) {
+            cudaGraph_t gr;
+            CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+            Launcher L{c->stream, c->pdl};
+            enqueue_step(c, L, n_stage_layers(c));
+            cudaError_t e = cudaStreamEndCapture(c->stream, &gr);
+            if (L.err != cudaSuccess || e != cudaSuccess) {
+                ecu_set_error(nullptr, 0, "graph capture failed: %s",
+                              cudaGetErrorString(L.err != cudaSuccess ? L.err : e));
+                if (e == cudaSuccess) cudaGraphDestroy(gr);
+                return -1;
+            }
+            e = cudaGraphInstantiate(&c->graph, gr, 0);
+            cudaGraphDestroy(gr);
+            if (e != cudaSuccess) {
+                ecu_set_error(nullptr, 0, "graph instantiate failed: %s", cudaGetErrorString(e));
+                c->graph = nullptr;
+                return -1;
+            }
+            c->graph_kernels = L.count;
+        }
+        CK(cudaGraphLaunch(c->graph, c->stream));
+        g_launches += (uint64_t)c->graph_kernels;
+        return 0;
+    }
+    Launcher L{c->stream, c->pdl};
+    enqueue_step(c, L, n_stage_layers(c));
+    g_launches += (uint64_t)L.count;
+    if (L.err != cudaSuccess) {
+        ecu_set_error(nullptr, 0, "kernel launch failed: %s", cudaGetErrorString(L.err));
+        return -1;
+    }
+    return 0;
+}
+
+static int check_status(ecu_ctx *c)
+{
+    CK(cudaStreamSynchronize(c->stream));
+    StepState s;
+    CK(cudaMemcpy(&s, c->st, sizeof s, cudaMemcpyDeviceToHost));
+    if (s.status) {
+        ecu_set_error(nullptr, 0, "a kernel gave up on a bounded wait (status %d)", s.status);
+        return -1;
+    }
+    return 0;
+}
+
+// ----------------------------------------------------------------- C ABI --
+
+extern "C" {
+
+const char *ecu_last_error(void) { return ecu_get_error(); }
+uint64_t    ecu_kernel_launches(void) { return g_launches.load(); }
+const char *ecu_version(void) { return "distcomp-b200 0.1 (sm_100a)"; }
+
+int ecu_model_open(ecu_model **out, const void *file, size_t size, char *err, size_t errlen)
+{
+    if (!out || !file) { ecu_set_error(err, errlen, "null argument"); return -1; }
+    ecu_model *m = new ecu_model();
+    if (ecu_model_parse(m, file, size, err, errlen) != 0) {
+        delete m;
+        *out = nullptr;
+        return -1;
+    }
+    *out = m;
+    return 0;
+}
+
+ecu_model *ecu_model_new(void) { return new ecu_model(); }
+
+static int set_kv(ecu_model *m, const char *key, unsigned type, double num, const char *str)
+{
+    if (!m || !key) return -1;
+    for (auto &k : m->kv)
+        if (k.key == key) { k.type = type; k.num = num; k.str = str ? str : ""; return 0; }
+    EcuKv k;
+    k.key = key;
+    k.type = type;
+    k.num = num;
+    if (str) k.str = str;
+    m->kv.push_back(k);
+    return 0;
+}
+
+int ecu_model_set_str(ecu_model *m, const char *key, const char *val) { return set_kv(m, key, 8, 0, val); }
+int ecu_model_set_u32(ecu_model *m, const char *key, unsigned long v) { return set_kv(m, key, 4, (double)v, nullptr); }
+int ecu_model_set_f32(ecu_model *m, const char *key, float v) { return set_kv(m, key, 6, (double)v, nullptr); }
+
+int ecu_model_add_tensor(ecu_model *m, const char *name, unsigned n_dims, const uint64_t *dims,
+                         unsigned ggml_type, const void *data, size_t nbytes)
+{
+    if (!m || !name || n_dims > 4 || (n_dims && !dims)) {
+        ecu_set_error(nullptr, 0, "ecu_model_add_tensor: bad arguments");
+        return -1;
+    }
+    EcuTensor t;
+    t.name = name;
+    t.n_dims = n_dims;
+    for (unsigned i = 0; i < n_dims; i++) t.dims[i] = dims[i];
+    t.type = ggml_type;
+    t.data = (const uint8_t *)data;
+    t.nbytes = nbytes;
+    size_t want = ecu_type_nbytes(ggml_type, t.elems());
+    if (want && nbytes < want) {
+        ecu_set_error(nullptr, 0, "tensor %s: %zu bytes given, %zu needed", name, nbytes, want);
+        return -1;
+    }
+    m->t.push_back(t);
+    m->index();
+    return 0;
+}
+
+void ecu_model_close(ecu_model *m) { delete m; }
+size_t ecu_model_n_tensors(const ecu_model *m) { return m ? m->t.size() : 0; }
+
+int ecu_model_tensor(const ecu_model *m, const char *name, unsigned *type, unsigned *n_dims,
+                     uint64_t dims[4], const void **data, size_t *nbytes)
+{
+    const EcuTensor *t = m ? m->find(name) : nullptr;
+    if (!t) return -1;
+    if (type) *type = t->type;
+    if (n_dims) *n_dims = t->n_dims;
+    if (dims) for (int i = 0; i < 4; i++) dims[i] = t->dims[i];
+    if (data) *data = t->data;
+    if (nbytes) *nbytes = t->nbytes;
+    return 0;
+}
+
+// Tensors a stage needs and their check (src/engine.c:169-213).
+struct StageTensors {
+    const EcuTensor *emb = nullptr, *out_norm = nullptr, *out = nullptr;
+    struct L { const EcuTensor *an, *q, *k, *v, *o, *fn, *g, *u, *d, *bq, *bk, *bv; };
+    std::vector<L> layers;
+};
+
+static int stage_tensors(const ecu_model *m, const EcuGeom &g, int stage, int first, int last,
+                         StageTensors *st, char *err, size_t errlen)
+{
+    if ((stage == ECU_STAGE_LAYERS || stage == ECU_STAGE_FULL) &&
+        (last < first || last >= g.n_layer || first < 0)) {
+        ecu_set_error(err, errlen, "layers %d..%d outside the model: it has %d layers", first, last, g.n_layer);
+        return -1;
+    }
+    if (stage != ECU_STAGE_LAYERS && g.n_vocab <= 0) {
+        ecu_set_error(err, errlen, "cannot determine the vocabulary size (n_vocab) for stage %d", stage);
+        return -1;
+    }
+    if (stage == ECU_STAGE_EMBED || stage == ECU_STAGE_FULL) {
+        st->emb = m->find("token_embd.weight");
+        if (!st->emb) { ecu_set_error(err, errlen, "model has no token_embd.weight"); return -1; }
+    }
+    if (stage == ECU_STAGE_HEAD || stage == ECU_STAGE_FULL) {
+        st->out_norm = m->find("output_norm.weight");
+        if (!st->out_norm) { ecu_set_error(err, errlen, "model has no output_norm.weight"); return -1; }
+        st->out = m->find("output.weight");
+        if (!st->out) st->out = m->find("token_embd.weight");
+        if (!st->out) { ecu_set_error(err, errlen, "model has neither output.weight nor token_embd.weight"); return -1; }
+    }
+    if (stage == ECU_STAGE_LAYERS || stage == ECU_STAGE_FULL) {
+        static const char *sfx[9] = {"attn_norm.weight", "attn_q.weight", "attn_k.weight",
+                                     "attn_v.weight", "attn_output.weight", "ffn_norm.weight",
+                                     "ffn_gate.weight", "ffn_up.weight", "ffn_down.weight"};
+        for (int i = first; i <= last; i++) {
+            StageTensors::L l{};
+            const EcuTensor **slot[9] = {&l.an, &l.q, &l.k, &l.v, &l.o, &l.fn, &l.g, &l.u, &l.d};
+            char name[160];
+            for (int k = 0; k < 9; k++) {
+                snprintf(name, sizeof name, "blk.%d.%s", i, sfx[k]);
+                if (!(*slot[k] = m->find(name))) { ecu_set_error(err, errlen, "model has no tensor %s", name); return -1; }
+            }
+            snprintf(name, sizeof name, "blk.%d.attn_q.bias", i); l.bq = m->find(name);
+            snprintf(name, sizeof name, "blk.%d.attn_k.bias", i); l.bk = m->find(name);
+            snprintf(name, sizeof name, "blk.%d.attn_v.bias", i); l.bv = m->find(name);
+            st->layers.push_back(l);
+        }
+    }
+    return 0;
+}
+
+// The weight matrices must have the shapes the layer loop multiplies by
+// (the reference trusts the file; a mismatch there reads past the tensor).
+static int check_shape(const EcuTensor *t, int n_in, int n_out, char *err, size_t errlen)
+{
+    const uint64_t rows = t->n_dims >= 2 ? t->elems() / t->dims[0] : 1;
+    if ((int64_t)t->dims[0] != n_in || (int64_t)rows < n_out) {
+        ecu_set_error(err, errlen, "tensor %s is %llux%llu, the layer needs %dx%d", t->name.c_str(),
+                      (unsigned long long)t->dims[0], (unsigned long long)rows, n_in, n_out);
+        return -1;
+    }
+    return 0;
+}
+
+static int attn_supported(int hd, int rep)
+{
+    return (hd == 32 || hd == 64 || hd == 128) && (rep == 1 || rep == 2 || rep == 4 || rep == 8);
+}
+
+size_t ecu_ctx_bytes(const ecu_model *m, int stage, int first, int last, int n_ctx)
+{
+    if (!m) return 0;
+    EcuGeom g;
+    if (ecu_read_geom(m, &g, nullptr, 0) != 0) return 0;
+    if (n_ctx > 0) g.n_ctx = n_ctx;
+    StageTensors st;
+    if (stage_tensors(m, g, stage, first, last, &st, nullptr, 0) != 0) return 0;
+    size_t b = 0;
+    auto mat = [&](const EcuTensor *t, int n_in, int n_out) {
+        int lay = choose_layout((int)t->type, n_in);
+        b += dev_row_bytes((int)t->type, n_in, lay) * (size_t)n_out;
+    };
+    const int hd = g.head_dim, qd = g.n_head * hd, kvd = g.n_head_kv * hd;
+    for (auto &l : st.layers) {
+        mat(l.q, g.n_embd, qd); mat(l.k, g.n_embd, kvd); mat(l.v, g.n_embd, kvd);
+        mat(l.o, qd, g.n_embd); mat(l.g, g.n_embd, g.n_ff); mat(l.u, g.n_embd, g.n_ff);
+        mat(l.d, g.n_ff, g.n_embd);
+        b += (size_t)(2 * g.n_embd + qd + 2 * kvd) * 4;
+    }
+    b += 2 * st.layers.size() * (size_t)g.n_ctx * kvd * 4;          // KV cache
+    if (st.emb) b += dev_row_bytes((int)st.emb->type, g.n_embd, LAY_RAW) * (size_t)g.n_vocab;
+    if (st.out) mat(st.out, g.n_embd, g.n_vocab);
+    b += (size_t)g.n_ctx * hd * 4;                                    // RoPE table
+    b += (size_t)(4 * g.n_embd + 4 * g.n_ff + 2 * qd + 2 * kvd + g.n_vocab + g.n_ctx) * 4;
+    return b;
+}
+
+int ecu_ctx_open(ecu_ctx **out, const ecu_model *m, int stage, int first, int last, int n_ctx,
+                 int device, char *err, size_t errlen)
+{
+    if (!out || !m) { ecu_set_error(err, errlen, "null argument"); return -1; }
+    *out = nullptr;
+    if (stage < ECU_STAGE_EMBED || stage > ECU_STAGE_FULL) { ecu_set_error(err, errlen, "unknown stage %d", stage); return -1; }
+    EcuGeom g;
+    if (ecu_read_geom(m, &g, err, errlen) != 0) return -1;
+    if (n_ctx > 0) g.n_ctx = n_ctx;
+    if (stage == ECU_STAGE_FULL) { first = 0; last = g.n_layer - 1; }
+    if (stage == ECU_STAGE_EMBED || stage == ECU_STAGE_HEAD) { first = 0; last = 0; }
+    StageTensors st;
+    if (stage_tensors(m, g, stage, first, last, &st, err, errlen) != 0) return -1;
+    const int hd = g.head_dim, qd = g.n_head * hd, kvd = g.n_head_kv * hd;
+    if (!st.layers.empty()) {
+        if (!attn_supported(hd, g.n_rep)) {
+            ecu_set_error(err, errlen, "head_dim %d with %d query heads per KV head is not built", hd, g.n_rep);
+            return -1;
+        }
+        if (hd % 2) { ecu_set_error(err, errlen, "odd head_dim %d", hd); return -1; }
+        for (auto &l : st.layers) {
+            if (check_shape(l.q, g.n_embd, qd, err, errlen) || check_shape(l.k, g.n_embd, kvd, err, errlen) ||
+                check_shape(l.v, g.n_embd, kvd, err, errlen) || check_shape(l.o, qd, g.n_embd, err, errlen) ||
+                check_shape(l.g, g.n_embd, g.n_ff, err, errlen) || check_shape(l.u, g.n_embd, g.n_ff, err, errlen) ||
+                check_shape(l.d, g.n_ff, g.n_embd, err, errlen))
+                return -1;
+        }
+    }
+    if (st.out && check_shape(st.out, g.n_embd, g.n_vocab, err, errlen)) return -1;
+    if (st.emb && (st.emb->dims[0] != (uint64_t)g.n_embd)) {
+        ecu_set_error(err, errlen, "token_embd.weight has %llu inputs, n_embd is %d",
+                      (unsigned long long)st.emb->dims[0], g.n_embd);
+        return -1;
+    }
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) {
+        ecu_set_error(err, errlen, "CUDA device %d not available (%d devices)", device, ndev);
+        return -1;
+    }
+    if (cudaSetDevice(device) != cudaSuccess) { ecu_set_error(err, errlen, "cudaSetDevice(%d) failed", device); return -1; }
+
+    std::unique_ptr<ecu_ctx, void (*)(ecu_ctx *)> c(new ecu_ctx(), ctx_free);
+    c->device = device;
+    c->sms = num_sms(device);
+    c->stage = stage;
+    c->first = first;
+    c->last = last;
+    c->g = g;
+    const char *e = getenv("ECU_PDL");
+    c->pdl = !(e && e[0] == '0');
+    e = getenv("ECU_GRAPH");
+    c->use_graph = !(e && e[0] == '0');
+    if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
+        ecu_set_error(err, errlen, "cudaStreamCreate failed");
+        return -1;
+    }
+
+    // staging buffer for raw uploads: the largest tensor this stage reads
+    size_t stage_bytes = 1 << 20;
+    auto need = [&](const EcuTensor *t) { if (t && t->nbytes > stage_bytes) stage_bytes = t->nbytes; };
+    need(st.emb); need(st.out); need(st.out_norm);
+    for (auto &l : st.layers) { need(l.an); need(l.q); need(l.k); need(l.v); need(l.o); need(l.fn); need(l.g); need(l.u); need(l.d); need(l.bq); need(l.bk); need(l.bv); }
+    uint8_t *stage_buf = nullptr;
+    if (cudaMalloc(&stage_buf, stage_bytes + 256) != cudaSuccess ||
+        cudaMemset(stage_buf, 0, stage_bytes + 256) != cudaSuccess) {
+        ecu_set_error(err, errlen, "out of device memory for a %zu-byte staging buffer", stage_bytes);
+        return -1;
+    }
+    struct Freer { uint8_t *p; ~Freer() { cudaFree(p); } } freer{stage_buf};
+
+    auto fail_oom = [&](const char *what) {
+        ecu_set_error(err, errlen, "out of device memory (%s) after %zu bytes", what, c->bytes);
+        return -1;
+    };
+    const int wide = g.n_ff > g.n_embd ? g.n_ff : g.n_embd;
+
+    // work buffers
+    c->state = c->dalloc<float>((size_t)g.n_embd + 4);
+    c->st = c->dalloc<StepState>(1);
+    c->tok_hist = c->dalloc<int>((size_t)g.n_ctx + 1);
+    c->scr.xn = c->dalloc<float>((size_t)wide + 4);
+    c->scr.part_val = c->dalloc<float>(4096);
+    c->scr.part_idx = c->dalloc<int>(4096);
+    c->scr.counter = c->dalloc<unsigned>(4);
+    c->scr.status = &c->st->status;
+    if (!c->state || !c->st || !c->tok_hist || !c->scr.xn || !c->scr.part_val || !c->scr.part_idx || !c->scr.counter)
+        return fail_oom("work buffers");
+    cudaMemset(c->st, 0, sizeof(StepState));
+    cudaMemset(c->scr.counter, 0, 4 * sizeof(unsigned));
+    cudaMemset(c->state, 0, ((size_t)g.n_embd + 4) * sizeof(float));
+    c->n_hslots = g.n_ctx + 1;
+    if (cudaMallocHost(&c->h_st, sizeof(StepState) * (size_t)c->n_hslots) != cudaSuccess ||
+        cudaMallocHost(&c->h_state, ((size_t)g.n_embd + 4) * sizeof(float)) != cudaSuccess)
+        return fail_oom("pinned host staging");
+    memset(c->h_st, 0, sizeof(StepState) * (size_t)c->n_hslots);
+
+    if (st.emb) {
+        c->emb = make_mat(c.get(), (int)st.emb->type, g.n_embd, g.n_vocab, false);
+        if (!c->emb.zero && !c->emb.data) return fail_oom("token_embd");
+        if (upload_rows(c.get(), st.emb, g.n_embd, g.n_vocab, c->emb, 0, 1, stage_buf)) return -1;
+        c->srcs.push_back({"token_embd.weight", c->emb, 0, 1, (size_t)g.n_embd * g.n_vocab, g.n_embd});
+    }
+    if (st.out) {
+        c->out = make_mat(c.get(), (int)st.out->type, g.n_embd, g.n_vocab, true);
+        if (!c->out.zero && !c->out.data) return fail_oom("output");
+        if (upload_rows(c.get(), st.out, g.n_embd, g.n_vocab, c->out, 0, 1, stage_buf)) return -1;
+        c->out_norm = upload_vec(c.get(), st.out_norm, (size_t)g.n_embd, stage_buf);
+        c->logits = c->dalloc<float>((size_t)g.n_vocab + 4);
+        if (!c->out_norm || !c->logits) return fail_oom("head buffers");
+        if (st.out->name == "output.weight" || !st.emb)
+            c->srcs.push_back({st.out->name, c->out, 0, 1, (size_t)g.n_embd * g.n_vocab, g.n_embd});
+    }
+    if (!st.layers.empty()) {
+        const size_t nl = st.layers.size();
+        c->qkv = c->dalloc<float>((size_t)qd + 2 * kvd + 4);
+        c->att = c->dalloc<float>((size_t)qd + 4);
+        c->h = c->dalloc<float>((size_t)g.n_ff + 4);
+        c->gtmp = c->dalloc<float>((size_t)g.n_ff + 4);
+        c->utmp = c->dalloc<float>((size_t)g.n_ff + 4);
+        const size_t plane = (size_t)g.n_head_kv * g.n_ctx * hd;
+        c->kc = c->dalloc<float>(plane * nl);
+        c->vc = c->dalloc<float>(plane * nl);
+        c->n_split = (2 * c->sms + g.n_head_kv - 1) / g.n_head_kv;
+        if (c->n_split > g.n_ctx) c->n_split = g.n_ctx;
+        c->attn_part = c->dalloc<float>((size_t)g.n_head_kv * c->n_split * g.n_rep * (hd + 2));
+        c->attn_cnt = c->dalloc<unsigned>((size_t)g.n_head_kv);
+        c->rope_cs = c->dalloc<float>((size_t)g.n_ctx * hd);
+        if (!c->qkv || !c->att || !c->h || !c->gtmp || !c->utmp || !c->kc || !c->vc || !c->attn_part ||
+            !c->attn_cnt || !c->rope_cs)
+            return fail_oom("KV cache and layer buffers");
+        cudaMemset(c->attn_cnt, 0, (size_t)g.n_head_kv * sizeof(unsigned));
+        // RoPE table with the host libm, exactly as src/engine.c:371-373
+        {
+            std::vector<float> cs((size_t)g.n_ctx * hd);
+            const int half = hd / 2;
+            for (int p = 0; p < g.n_ctx; p++)
+                for (int i = 0; i < half; i++) {
+                    float freq = powf(g.rope_base, -2.0f * (float)i / (float)hd);
+                    float ang = (float)p * freq;
+                    cs[((size_t)p * half + i) * 2] = cosf(ang);
+                    cs[((size_t)p * half + i) * 2 + 1] = sinf(ang);
+                }
+            cudaMemcpy(c->rope_cs, cs.data(), cs.size() * sizeof(float), cudaMemcpyHostToDevice);
+        }
+        c->layers.resize(nl);
+        for (size_t i = 0; i < nl; i++) {
+            const auto &l = st.layers[i];
+            LayerDev   &ly = c->layers[i];
+            char        nm[160];
+            const int   li = first + (int)i;
+            // Q/K/V: fused when all three share a fast layout
+            const int lq = choose_layout((int)l.q->type, g.n_embd);
+            const bool fuse_qkv = lq != LAY_RAW && l.k->type == l.q->type && l.v->type == l.q->type;
+            if (fuse_qkv) {
+                DevMat mq = make_mat(c.get(), (int)l.q->type, g.n_embd, qd + 2 * kvd, true);
+                if (!mq.data) return fail_oom("attn_qkv");
+                if (upload_rows(c.get(), l.q, g.n_embd, qd, mq, 0, 1, stage_buf) ||
+                    upload_rows(c.get(), l.k, g.n_embd, kvd, mq, qd, 1, stage_buf) ||
+                    upload_rows(c.get(), l.v, g.n_embd, kvd, mq, qd + kvd, 1, stage_buf))
+                    return -1;
+                ly.qkv.push_back(mq);
+                ly.qkv_off.push_back(0);
+                snprintf(nm, sizeof nm, "blk.%d.attn_q.weight", li); c->srcs.push_back({nm, mq, 0, 1, (size_t)g.n_embd * qd, g.n_embd});
+                snprintf(nm, sizeof nm, "blk.%d.attn_k.weight", li); c->srcs.push_back({nm, mq, qd, 1, (size_t)g.n_embd * kvd, g.n_embd});
+                snprintf(nm, sizeof nm, "blk.%d.attn_v.weight", li); c->srcs.push_back({nm, mq, qd + kvd, 1, (size_t)g.n_embd * kvd, g.n_embd});
+            } else {
+                const EcuTensor *ts[3] = {l.q, l.k, l.v};
+                const int        rows[3] = {qd, kvd, kvd}, offs[3] = {0, qd, qd + kvd};
+                const char      *sf[3] = {"attn_q", "attn_k", "attn_v"};
+                for (int k = 0; k < 3; k++) {
+                    DevMat mm = make_mat(c.get(), (int)ts[k]->type, g.n_embd, rows[k], true);
+                    if (!mm.zero && !mm.data) return fail_oom("attn_q/k/v");
+                    if (upload_rows(c.get(), ts[k], g.n_embd, rows[k], mm, 0, 1, stage_buf)) return -1;
+                    ly.qkv.push_back(mm);
+                    ly.qkv_off.push_back(offs[k]);
+                    snprintf(nm, sizeof nm, "blk.%d.%s.weight", li, sf[k]);
+                    c->srcs.push_back({nm, mm, 0, 1, (size_t)g.n_embd * rows[k], g.n_embd});
+                }
+            }
+            ly.o = make_mat(c.get(), (int)l.o->type, qd, g.n_embd, true);
+            if (!ly.o.zero && !ly.o.data) return fail_oom("attn_output");
+            if (upload_rows(c.get(), l.o, qd, g.n_embd, ly.o, 0, 1, stage_buf)) return -1;
+            snprintf(nm, sizeof nm, "blk.%d.attn_output.weight", li);
+            c->srcs.push_back({nm, ly.o, 0, 1, (size_t)qd * g.n_embd, qd});
+            const int lg = choose_layout((int)l.g->type, g.n_embd);
+            ly.gu_fused = lg != LAY_RAW && l.u->type == l.g->type;
+            if (ly.gu_fused) {
+                ly.gu = make_mat(c.get(), (int)l.g->type, g.n_embd, 2 * g.n_ff, true);
+                if (!ly.gu.data) return fail_oom("ffn_gate/up");
+                if (upload_rows(c.get(), l.g, g.n_embd, g.n_ff, ly.gu, 0, 2, stage_buf) ||
+                    upload_rows(c.get(), l.u, g.n_embd, g.n_ff, ly.gu, 1, 2, stage_buf))
+                    return -1;
+                snprintf(nm, sizeof nm, "blk.%d.ffn_gate.weight", li); c->srcs.push_back({nm, ly.gu, 0, 2, (size_t)g.n_embd * g.n_ff, g.n_embd});
+                snprintf(nm, sizeof nm, "blk.%d.ffn_up.weight", li); c->srcs.push_back({nm, ly.gu, 1, 2, (size_t)g.n_embd * g.n_ff, g.n_embd});
+            } else {
+                ly.g = make_mat(c.get(), (int)l.g->type, g.n_embd, g.n_ff, true);
+                ly.u = make_mat(c.get(), (int)l.u->type, g.n_embd, g.n_ff, true);
+                if ((!ly.g.zero && !ly.g.data) || (!ly.u.zero && !ly.u.data)) return fail_oom("ffn_gate/up");
+                if (upload_rows(c.get(), l.g, g.n_embd, g.n_ff, ly.g, 0, 1, stage_buf) ||
+                    upload_rows(c.get(), l.u, g.n_embd, g.n_ff, ly.u, 0, 1, stage_buf))
+                    return -1;
+                snprintf(nm, sizeof nm, "blk.%d.ffn_gate.weight", li); c->srcs.push_back({nm, ly.g, 0, 1, (size_t)g.n_embd * g.n_ff, g.n_embd});
+                snprintf(nm, sizeof nm, "blk.%d.ffn_up.weight", li); c->srcs.push_back({nm, ly.u, 0, 1, (size_t)g.n_embd * g.n_ff, g.n_embd});
+            }
+            ly.d = make_mat(c.get(), (int)l.d->type, g.n_ff, g.n_embd, true);
+            if (!ly.d.zero && !ly.d.data) return fail_oom("ffn_down");
+            if (upload_rows(c.get(), l.d, g.n_ff, g.n_embd, ly.d, 0, 1, stage_buf)) return -1;
+            snprintf(nm, sizeof nm, "blk.%d.ffn_down.weight", li);
+            c->srcs.push_back({nm, ly.d, 0, 1, (size_t)g.n_ff * g.n_embd, g.n_ff});
+            ly.attn_norm = upload_vec(c.get(), l.an, (size_t)g.n_embd, stage_buf);
+            ly.ffn_norm = upload_vec(c.get(), l.fn, (size_t)g.n_embd, stage_buf);
+            if (l.bq) ly.bq = upload_vec(c.get(), l.bq, (size_t)qd, stage_buf);
+            if (l.bk) ly.bk = upload_vec(c.get(), l.bk, (size_t)kvd, stage_buf);
+            if (l.bv) ly.bv = upload_vec(c.get(), l.bv, (size_t)kvd, stage_buf);
+            if (!ly.attn_norm || !ly.ffn_norm) return fail_oom("norm weights");
+        }
+    }
+    if (cudaStreamSynchronize(c->stream) != cudaSuccess || cudaGetLastError() != cudaSuccess) {
+        ecu_set_error(err, errlen, "upload failed: %s", cudaGetErrorString(cudaGetLastError()));
+        return -1;
+    }
+    *out = c.release();
+    return 0;
+}
+
+void ecu_ctx_close(ecu_ctx *c) { ctx_free(c); }
+
+int ecu_ctx_info(const ecu_ctx *c, ecu_info *i)
+{
+    if (!c || !i) return -1;
+    i->n_layer = c->g.n_layer; i->n_embd = c->g.n_embd; i->n_head = c->g.n_head;
+    i->n_head_kv = c->g.n_head_kv; i->n_ff = c->g.n_ff; i->head_dim = c->g.head_dim;
+    i->n_vocab = c->g.n_vocab; i->n_rep = c->g.n_rep; i->n_ctx = c->g.n_ctx;
+    i->stage = c->stage; i->first = c->first; i->last = c->last; i->pos = c->pos;
+    i->device = c->device; i->rms_eps = c->g.eps; i->rope_base = c->g.rope_base;
+    i->device_bytes = c->bytes;
+    return 0;
+}
+
+void ecu_reset(ecu_ctx *c)
+{
+    if (c) c->pos = 0;
+}
+
+int ecu_set_pos(ecu_ctx *c, int pos)
+{
+    if (!c || pos < 0 || pos > c->g.n_ctx) return -1;
+    c->pos = pos;
+    return 0;
+}
+
+float *ecu_state_ptr(ecu_ctx *c) { return c ? c->state : nullptr; }
+void  *ecu_stream(ecu_ctx *c) { return c ? (void *)c->stream : nullptr; }
+
+// Host-side checks of llm_forward (src/engine.c:468-515) before enqueueing.
+static int step_check(ecu_ctx *c, int token)
+{
+    if (c->stage == ECU_STAGE_EMBED || c->stage == ECU_STAGE_FULL) {
+        if (token < 0 || token >= c->g.n_vocab) {
+            ecu_set_error(nullptr, 0, "token %d outside the vocabulary (%d)", token, c->g.n_vocab);
+            return -1;
+        }
+    }
+    if ((c->stage == ECU_STAGE_LAYERS || c->stage == ECU_STAGE_FULL) && c->pos >= c->g.n_ctx) {
+        ecu_set_error(nullptr, 0, "context exhausted (%d positions)", c->g.n_ctx);
+        return -1;
+    }
+    return 0;
+}
+
+// Enqueue input state + one step on `stream` (the context's own stream).
+static int enqueue_forward(ecu_ctx *c, int token)
+{
+    StepState *slot = c->h_st + (c->pos % c->n_hslots);
+    slot->pos = c->pos;
+    slot->token = token;
+    slot->status = 0;
+    CK(cudaMemcpyAsync(c->st, slot, sizeof(StepState), cudaMemcpyHostToDevice, c->stream));
+    if (run_step(c) != 0) return -1;
+    if (c->stage == ECU_STAGE_LAYERS || c->stage == ECU_STAGE_FULL) c->pos++;
+    if (c->stage == ECU_STAGE_HEAD || c->stage == ECU_STAGE_FULL) c->have_logits = true;
+    return 0;
+}
+
+int ecu_forward(ecu_ctx *c, int token, float *out)
+{
+    if (!c || !out) return -1;
+    cudaSetDevice(c->device);
+    if (step_check(c, token) != 0) return -1;
+    const size_t ne = (size_t)c->g.n_embd;
+    if (c->stage == ECU_STAGE_LAYERS || c->stage == ECU_STAGE_HEAD) {
+        memcpy(c->h_state, out, ne * sizeof(float));
+        CK(cudaMemcpyAsync(c->state, c->h_state, ne * sizeof(float), cudaMemcpyHostToDevice, c->stream));
+    }
+    if (enqueue_forward(c, token) != 0) return -1;
+    const size_t nout = (c->stage == ECU_STAGE_HEAD || c->stage == ECU_STAGE_FULL) ? ne + 1 : ne;
+    CK(cudaMemcpyAsync(c->h_state, c->state, nout * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
+    if (check_status(c) != 0) return -1;
+    memcpy(out, c->h_state, nout * sizeof(float));
+    if (nout == ne + 1) c->last_pick = (int)c->h_state[ne];
+    return 0;
+}
+
+int ecu_forward_dev(ecu_ctx *c, int token, void *stream)
+{
+    if (!c) return -1;
+    cudaSetDevice(c->device);
+    if (step_check(c, token) != 0) return -1;
+    cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
+    if (s != c->stream) {
+        // order the context's stream after the caller's work, and back
+        cudaEvent_t ev;
+        CK(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+        CK(cudaEventRecord(ev, s));
+        CK(cudaStreamWaitEvent(c->stream, ev, 0));
+        if (enqueue_forward(c, token) != 0) { cudaEventDestroy(ev); return -1; }
+        CK(cudaEventRecord(ev, c->stream));
+        CK(cudaStreamWaitEvent(s, ev, 0));
+        cudaEventDestroy(ev);
+        return 0;
+    }
+    return enqueue_forward(c, token);
+}
+
+// Eager (non-graph) run of an explicit layer list; pos unchanged.
+static int run_layers_eager(ecu_ctx *c, int from, int to, float *out)
+{
+    const size_t ne = (size_t)c->g.n_embd;
+    memcpy(c->h_state, out, ne * sizeof(float));
+    CK(cudaMemcpyAsync(c->state, c->h_state, ne * sizeof(float), cudaMemcpyHostToDevice, c->stream));
+    StepState *slot = c->h_st + (c->pos % c->n_hslots);
+    slot->pos = c->pos;
+    slot->token = 0;
+    slot->status = 0;
+    CK(cudaMemcpyAsync(c->st, slot, sizeof(StepState), cudaMemcpyHostToDevice, c->stream));
+    Launcher L{c->stream, c->pdl};
+    for (int i = from; i < to; i++) enqueue_layer(c, L, i);
+    g_launches += (uint64_t)L.count;
+    if (L.err != cudaSuccess) { ecu_set_error(nullptr, 0, "kernel launch failed: %s", cudaGetErrorString(L.err)); return -1; }
+    CK(cudaMemcpyAsync(c->h_state, c->state, ne * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
+    if (check_status(c) != 0) return -1;
+    memcpy(out, c->h_state, ne * sizeof(float));
+    return 0;
+}
+
+int ecu_layer_once(ecu_ctx *c, int idx, float *out)
+{
+    if (!c || c->stage != ECU_STAGE_LAYERS || !out) return -1;
+    if (idx < 0 || idx > c->last - c->first) return -1;
+    if (c->pos >= c->g.n_ctx) { ecu_set_error(nullptr, 0, "position %d outside the cache", c->pos); return -1; }
+    cudaSetDevice(c->device);
+    return run_layers_eager(c, idx, idx + 1, out);
+}
+
+int ecu_step_layers(ecu_ctx *c, int n, float *out)
+{
+    if (!c || c->stage != ECU_STAGE_LAYERS || !out) return -1;
+    const int all = c->last - c->first + 1;
+    if (n <= 0) n = all;
+    if (n > all) n = all;
+    if (c->pos >= c->g.n_ctx) { ecu_set_error(nullptr, 0, "context exhausted (%d positions)", c->g.n_ctx); return -1; }
+    cudaSetDevice(c->device);
+    if (n == all) return ecu_forward(c, 0, out);
+    if (run_layers_eager(c, 0, n, out) != 0) return -1;
+    c->pos++;
+    return 0;
+}
+
+int ecu_pick(const ecu_ctx *c)
+{
+    if (!c || !c->have_logits) return 0;
+    return c->last_pick;
+}
+
+int ecu_get_logits(const ecu_ctx *c, float *out, size_t n)
+{
+    if (!c || !out || !c->logits || n > (size_t)c->g.n_vocab) return -1;
+    cudaSetDevice(c->device);
+    CK(cudaStreamSynchronize(c->stream));
+    CK(cudaMemcpy(out, c->logits, n * sizeof(float), cudaMemcpyDeviceToHost));
+    return 0;
+}
+
+int ecu_sync(ecu_ctx *c)
+{
+    if (!c) return -1;
+    cudaSetDevice(c->device);
+    if (check_status(c) != 0) return -1;
+    // the device-side loop leaves the argmax in state[n_embd]
+    if (c->stage == ECU_STAGE_FULL || c->stage == ECU_STAGE_HEAD) {
+        float t;
+        CK(cudaMemcpy(&t, c->state + c->g.n_embd, sizeof t, cudaMemcpyDeviceToHost));
+        c->last_pick = (int)t;
+    }
+    return 0;
+}
+
+int ecu_decode_async(ecu_ctx *c, int n_steps)
+{
+    if (!c || c->stage != ECU_STAGE_FULL || n_steps < 0) return -1;
+    if (c->pos + n_steps > c->g.n_ctx) { ecu_set_error(nullptr, 0, "context exhausted"); return -1; }
+    cudaSetDevice(c->device);
+    for (int i = 0; i < n_steps; i++) {
+        if (run_step(c) != 0) return -1;
+        c->pos++;
+    }
+    c->have_logits = c->have_logits || n_steps > 0;
+    return 0;
+}
+
+int ecu_generate(ecu_ctx *c, const int *prompt, int n_prompt, int n_gen, int *out_tokens)
+{
+    if (!c || c->stage != ECU_STAGE_FULL || n_prompt < 1 || n_gen < 0 || !prompt) return -1;
+    if (c->pos + n_prompt + n_gen > c->g.n_ctx + 1) {
+        ecu_set_error(nullptr, 0, "prompt + generation exceed the context (%d)", c->g.n_ctx);
+        return -1;
+    }
+    for (int i = 0; i < n_prompt; i++)
+        if (prompt[i] < 0 || prompt[i] >= c->g.n_vocab) {
+            ecu_set_error(nullptr, 0, "prompt token %d outside the vocabulary", prompt[i]);
+            return -1;
+        }
+    cudaSetDevice(c->device);
+    // prompt tokens: host-fed, no sync between them
+    for (int i = 0; i < n_prompt; i++)
+        if (enqueue_forward(c, prompt[i]) != 0) return -1;
+    // the last prompt step's argmax is generated token 0; each later step
+    // consumes the previous argmax from device state
+    const int start = c->pos;      // tok_hist[start - 1] = first generated token
+    const int more = n_gen > 0 ? n_gen - 1 : 0;
+    if (ecu_decode_async(c, more) != 0) return -1;
+    if (check_status(c) != 0) return -1;
+    if (n_gen > 0) {
+        CK(cudaMemcpy(out_tokens, c->tok_hist + (start - 1), (size_t)n_gen * sizeof(int),
+                      cudaMemcpyDeviceToHost));
+        c->last_pick = out_tokens[n_gen - 1];
+    }
+    // state[n_embd] holds the last argmax for ecu_forward-style readers
+    return 0;
+}
+
+int ecu_dequant(unsigned type, const void *raw, size_t total, size_t off, size_t n, float *dst,
+                int device)
+{
+    if (!raw || !dst) return -1;
+    if (off > total || n > total - off) { ecu_set_error(nullptr, 0, "range outside the tensor"); return -1; }
+    if (n == 0) return 0;
+    const int t = (int)type;
+    if (!dq_supported(t)) { ecu_set_error(nullptr, 0, "type %u not supported", type); return -1; }
+    size_t first_byte, nbytes, rel_off;
+    if (t == GT_F32 || t == GT_F16) {
+        const size_t es = t == GT_F32 ? 4 : 2;
+        first_byte = off * es;
+        nbytes = n * es;
+        rel_off = 0;
+    } else {
+        const size_t be = (size_t)blk_elems(t), bb = (size_t)blk_bytes(t);
+        if (off % be) { ecu_set_error(nullptr, 0, "offset %zu not on a block boundary", off); return -1; }
+        const size_t nblk = (n + be - 1) / be;
+        if (off / be + nblk > total / be) { ecu_set_error(nullptr, 0, "blocks outside the tensor"); return -1; }
+        first_byte = off / be * bb;
+        nbytes = nblk * bb;
+        rel_off = 0;
+    }
+    CK(cudaSetDevice(device));
+    // bytes the decoder may touch past the last block (Q8_K, see dalloc):
+    // the following bytes of the caller's tensor where there are any, zeros
+    // after its end
+    const size_t valid = ecu_type_nbytes(type, total);
+    size_t tail = valid > first_byte + nbytes ? valid - first_byte - nbytes : 0;
+    if (tail > 64) tail = 64;
+    uint8_t *d_raw = nullptr;
+    float   *d_out = nullptr;
+    CK(cudaMalloc(&d_raw, nbytes + 256));
+    if (cudaMalloc(&d_out, n * sizeof(float)) != cudaSuccess) { cudaFree(d_raw); ecu_set_error(nullptr, 0, "out of memory"); return -1; }
+    int rc = 0;
+    if (cudaMemset(d_raw, 0, nbytes + 256) != cudaSuccess ||
+        cudaMemcpy(d_raw, (const uint8_t *)raw + first_byte, nbytes + tail, cudaMemcpyHostToDevice) != cudaSuccess)
+        rc = -1;
+    if (!rc) {
+        k_dequant_raw<<<256, 256>>>(t, d_raw, rel_off, n, d_out);
+        g_launches++;
+        if (cudaDeviceSynchronize() != cudaSuccess ||
+            cudaMemcpy(dst, d_out, n * sizeof(float), cudaMemcpyDeviceToHost) != cudaSuccess)
+            rc = -1;
+    }
+    cudaFree(d_raw);
+    cudaFree(d_out);
+    if (rc) ecu_set_error(nullptr, 0, "ecu_dequant: CUDA error %s", cudaGetErrorString(cudaGetLastError()));
+    return rc;
+}
+
+int ecu_dequant_tensor(ecu_ctx *c, const char *name, size_t off, size_t n, float *dst)
+{
+    if (!c || !name || !dst) return -1;
+    for (auto &s : c->srcs) {
+        if (s.name != name) continue;
+        if (off > s.elems || n > s.elems - off) return -1;
+        if (s.m.zero) { ecu_set_error(nullptr, 0, "tensor %s is not resident (zero rule)", name); return -1; }
+        cudaSetDevice(c->device);
+        float *d = nullptr;
+        CK(cudaMalloc(&d, n * sizeof(float) + 256));
+        k_dequant_mat<<<256, 256, 0, c->stream>>>(s.m, s.row0, s.rstride, s.n_in, off, n, d);
+        g_launches++;
+        int rc = 0;
+        if (cudaStreamSynchronize(c->stream) != cudaSuccess ||
+            cudaMemcpy(dst, d, n * sizeof(float), cudaMemcpyDeviceToHost) != cudaSuccess)
+            rc = -1;
+        cudaFree(d);
+        return rc;
+    }
+    ecu_set_error(nullptr, 0, "no resident tensor named %s", name);
+    return -1;
+}
+
+int ecu_matvec(unsigned type, const void *w_raw, int n_in, int n_out, const float *x, float *y,
+               int device)
+{
+    if (!w_raw || !x || !y || n_in <= 0 || n_out <= 0) return -1;
+    CK(cudaSetDevice(device));
+    ecu_ctx tmp;               // borrow the allocator/stream helpers
+    tmp.device = device;
+    tmp.sms = num_sms(device);
+    CK(cudaStreamCreateWithFlags(&tmp.stream, cudaStreamNonBlocking));
+    struct Cleanup {
+        ecu_ctx *c;
+        ~Cleanup()
+        {
+            for (void *p : c->allocs) cudaFree(p);
+            c->allocs.clear();
+            cudaStreamDestroy(c->stream);
+            c->stream = nullptr;
+        }
+    } cleanup{&tmp};
+    EcuTensor t;
+    t.type = type;
+    t.n_dims = 2;
+    t.dims[0] = (uint64_t)n_in;
+    t.dims[1] = (uint64_t)n_out;
+    t.data = (const uint8_t *)w_raw;
+    t.nbytes = ecu_type_nbytes(type, (size_t)n_in * n_out);
+    DevMat m = make_mat(&tmp, (int)type, n_in, n_out, true);
+    uint8_t *stage = tmp.dalloc<uint8_t>(t.nbytes + 16);
+    float   *dx = tmp.dalloc<float>((size_t)n_in + 4);
+    float   *dy = tmp.dalloc<float>((size_t)n_out + 4);
+    GemvScratch s;
+    s.xn = tmp.dalloc<float>((size_t)n_in + 4);
+    s.part_val = tmp.dalloc<float>(4096);
+    s.part_idx = tmp.dalloc<int>(4096);
+    s.counter = tmp.dalloc<unsigned>(4);
+    s.status = tmp.dalloc<int>(4);
+    if ((!m.zero && !m.data) || !stage || !dx || !dy || !s.xn) { ecu_set_error(nullptr, 0, "out of memory"); return -1; }
+    cudaMemset(s.status, 0, 4 * sizeof(int));
+    if (!m.zero && t.nbytes && upload_rows(&tmp, &t, n_in, n_out, m, 0, 1, stage) != 0) return -1;
+    CK(cudaMemcpy(dx, x, (size_t)n_in * sizeof(float), cudaMemcpyHostToDevice));
+    Launcher L{tmp.stream, false};
+    GemvArgs a = {};
+    enqueue_gemv(L, tmp.sms, m, dx, nullptr, 0.0f, dy, EPI_STORE, s, a);
+    g_launches += (uint64_t)L.count;
+    if (L.err != cudaSuccess) { ecu_set_error(nullptr, 0, "launch failed: %s", cudaGetErrorString(L.err)); return -1; }
+    CK(cudaStreamSynchronize(tmp.stream));
+    int st = 0;
+    CK(cudaMemcpy(&st, s.status, sizeof st, cudaMemcpyDeviceToHost));
+    if (st) { ecu_set_error(nullptr, 0, "bounded wait expired in the GEMV"); return -1; }
+    CK(cudaMemcpy(y, dy, (size_t)n_out * sizeof(float), cudaMemcpyDeviceToHost));
+    return 0;
+}
+
+}  // extern "C"

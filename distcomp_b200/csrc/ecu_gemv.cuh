@@ -1,0 +1,466 @@
+// ecu_gemv.cuh -- fused dequant + GEMV kernels (batch-1 decode).
+//
+// y[o] = sum_i W[i + o*n_in] * x[i] over GGUF-quantised W (the quantised
+// matvec of src/engine.c:287-357), with the neighbours of each matvec in the
+// reference's layer loop fused in:
+//   prologue  RMSNorm of x (src/engine.c:256-262), recomputed per CTA
+//   epilogues y = acc | y += acc (residual, engine.c:453,465) |
+//             SwiGLU on interleaved gate/up rows (engine.c:458-463) |
+//             logits + argmax (engine.c:491-496, 517-526)
+//
+// Two paths:
+//  * k_gemv_fast: Q4_0 / Q8_0 in the SPLIT layouts with n_in a multiple of
+//    1024.  One CTA per SM streams its contiguous run of rows through a
+//    4-stage shared-memory ring filled by bulk async copies (one producer
+//    thread, mbarriers), so each SM keeps ~70 KB of weights in flight.  The
+//    input vector is held in registers as three exact int8 "digit planes"
+//    per 32-element block (x = s*(d0 + d1/128 + d2/16384), s a power of 2),
+//    so one 4-bit or 8-bit code block costs 24 dp4a instead of 32 int->float
+//    conversions and FMAs.  Each lane owns one block column; warps split the
+//    row's 32-block groups and their partial sums meet in shared memory.
+//  * k_gemv_generic: any supported format/layout, one warp per row, with
+//    the bit-exact per-element decoder; used for F32/F16, K-quants, and
+//    shapes the fast path does not take.
+#pragma once
+#include "ecu_dequant.cuh"
+#include "ecu_pipe.cuh"
+
+enum Epi : int { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2, EPI_ARGMAX = 3 };
+
+// Inputs of a GEMV launch (both paths).
+struct GemvArgs {
+    DevMat       m;
+    const float *x;            // input vector, n_in floats
+    const float *norm_w;       // RMSNorm weights (n_in) when the prologue is on
+    float        eps;
+    float       *y;            // output (STORE/ADD/ARGMAX: n_out; SWIGLU: n_out/2)
+    float       *xn_out;       // optional: CTA 0 stores the normed input here
+    // argmax epilogue
+    float       *part_val;     // [gridDim.x]
+    int         *part_idx;     // [gridDim.x]
+    unsigned    *counter;      // zero between launches
+    StepState   *st;           // token <- argmax; pos advanced if advance_pos
+    int         *tok_hist;     // tok_hist[pos] <- argmax (nullable)
+    float       *tok_out;      // *tok_out <- (float)argmax (nullable)
+    int          advance_pos;
+    int         *status;
+    // fast-path geometry (set by the host planner)
+    int          rows_per_cta;
+    int          stage_rows;
+};
+
+// ---------------------------------------------------------------- RMSNorm --
+// 1/sqrt(mean(x^2)+eps) with the sum of squares in double (src/engine.c:258-
+// 260).  The double sum runs over 256 fixed strided partials combined by a
+// fixed tree, so every kernel that calls this gets the same bits whatever its
+// block size.  Threads [0, nthreads) must all call it; `bar` synchronises them.
+template <class Bar>
+__device__ float rms_scale(const float *x, int n, float eps, double *dsum, int tid,
+                           int nthreads, Bar bar)
+{
+    for (int v = tid; v < 256; v += nthreads) {
+        double p = 0.0;
+        for (int i = v; i < n; i += 256) {
+            double xv = (double)x[i];
+            p += xv * xv;
+        }
+        dsum[v] = p;
+    }
+    bar();
+    for (int stride = 128; stride > 0; stride >>= 1) {
+        for (int v = tid; v < stride; v += nthreads) dsum[v] += dsum[v + stride];
+        bar();
+    }
+    const double ss = dsum[0];
+    const float  ms = (float)(ss / (double)n);
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
+}
+
+// ----------------------------------------------------------- argmax tail --
+// First maximum in index order, NaN never selected, and the reference's
+// fallback to 0 when logits[0] is NaN or nothing beats -inf
+// (src/engine.c:517-526 scans with a strict >).
+struct ArgBest {
+    float v;
+    int   i;
+};
+
+__device__ __forceinline__ ArgBest arg_better(ArgBest a, ArgBest b)
+{
+    if (b.i >= 0 && (b.v > a.v || (b.v == a.v && (a.i < 0 || b.i < a.i)))) return b;
+    return a;
+}
+
+// Block-wide argmax of (v, i) pairs; every thread of the block calls it.
+__device__ ArgBest block_argmax(ArgBest mine, ArgBest *sh)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        ArgBest other;
+        other.v = __shfl_xor_sync(0xffffffffu, mine.v, o);
+        other.i = __shfl_xor_sync(0xffffffffu, mine.i, o);
+        mine = arg_better(mine, other);
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    __syncthreads();
+    if (lane == 0) sh[warp] = mine;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        ArgBest b = sh[0];
+        for (int w = 1; w < nw; w++) b = arg_better(b, sh[w]);
+        sh[0] = b;
+    }
+    __syncthreads();
+    return sh[0];
+}
+
+// Per-CTA partial -> last CTA reduces all partials in CTA order and publishes.
+__device__ void argmax_finish(const GemvArgs &a, ArgBest cta_best, ArgBest *sh)
+{
+    __shared__ unsigned s_last;
+    if (threadIdx.x == 0) {
+        a.part_val[blockIdx.x] = cta_best.v;
+        a.part_idx[blockIdx.x] = cta_best.i;
+        __threadfence();
+        unsigned t = atomicAdd(a.counter, 1u);
+        s_last = (t == gridDim.x - 1);
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    if (threadIdx.x == 0) {
+        ArgBest b{-INFINITY, -1};
+        for (unsigned c = 0; c < gridDim.x; c++) {
+            ArgBest p{((volatile float *)a.part_val)[c], ((volatile int *)a.part_idx)[c]};
+            b = arg_better(b, p);
+        }
+        const float l0 = ((volatile float *)a.y)[0];
+        const int   tok = (b.i < 0 || isnan(l0)) ? 0 : b.i;
+        if (a.st) {
+            if (a.tok_hist) a.tok_hist[a.st->pos] = tok;
+            a.st->token = tok;
+            if (a.advance_pos) a.st->pos = a.st->pos + 1;
+        }
+        if (a.tok_out) *a.tok_out = (float)tok;
+        *a.counter = 0u;
+    }
+}
+
+__device__ __forceinline__ float silu_mul(float g, float u)
+{
+    // (g / (1 + expf(-g))) * u with IEEE division, as src/engine.c:462
+    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+}
+
+// ============================================================ generic =====
+
+// Warp per output row; lanes stride the row's elements / blocks.
+template <int EPI>
+__global__ void __launch_bounds__(256) k_gemv_generic(GemvArgs a)
+{
+    pdl_wait();
+    pdl_trigger();
+    const DevMat &m = a.m;
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const int nwarps = (gridDim.x * blockDim.x) >> 5;
+    __shared__ ArgBest sh[32];
+    ArgBest best{-INFINITY, -1};
+    for (int row = warp; row < m.n_out; row += nwarps) {
+        float acc = 0.0f;
+        if (!m.zero) {
+            const uint8_t *r = m.data + (size_t)row * m.row_bytes;
+            if (m.type == GT_F32) {
+                const float *w = reinterpret_cast<const float *>(r);
+                for (int k = lane; k < m.n_in; k += 32) acc = fmaf(w[k], a.x[k], acc);
+            } else if (m.type == GT_F16) {
+                for (int k = lane; k < m.n_in; k += 32) acc = fmaf(f16x(r + 2 * k), a.x[k], acc);
+            } else {
+                const int be = blk_elems(m.type), bb = blk_bytes(m.type), nb = m.n_in / be;
+                for (int b = lane; b < nb; b += 32) {
+                    const uint8_t *blk = r + (size_t)b * bb;
+                    const float   *xs = a.x + (size_t)b * be;
+                    float part = 0.0f;
+                    for (int i = 0; i < be; i++) part = fmaf(dq_elem(m.type, blk, i), xs[i], part);
+                    acc += part;
+                }
+            }
+            acc = warp_sum(acc);
+        }
+        if (lane == 0) {
+            if (EPI == EPI_ADD) a.y[row] = a.y[row] + acc;
+            else a.y[row] = acc;
+        }
+        if (EPI == EPI_ARGMAX && lane == 0) best = arg_better(best, ArgBest{acc, row});
+    }
+    if (EPI == EPI_ARGMAX) {
+        ArgBest b = block_argmax(best, sh);
+        argmax_finish(a, b, sh);
+    }
+}
+
+// Standalone RMSNorm (generic path and HEAD's normed-state output):
+// out[i] = x[i] * scale * w[i], single CTA.
+__global__ void __launch_bounds__(256) k_rmsnorm(const float *x, const float *w, int n,
+                                                 float eps, float *out)
+{
+    pdl_wait();
+    pdl_trigger();
+    __shared__ double dsum[256];
+    const float s = rms_scale(x, n, eps, dsum, threadIdx.x, blockDim.x, [] { __syncthreads(); });
+    for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = __fmul_rn(__fmul_rn(x[i], s), w[i]);
+}
+
+// h[j] = silu(g[j]) * u[j] for the unfused gate/up path.
+__global__ void k_swiglu(const float *g, const float *u, float *h, int n)
+{
+    pdl_wait();
+    pdl_trigger();
+    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < n; j += gridDim.x * blockDim.x)
+        h[j] = silu_mul(g[j], u[j]);
+}
+
+// =============================================================== fast =====
+
+#define FAST_STAGES 4
+
+// Exact three-plane int8 decomposition of one 32-element block of x.
+// FMT 4: word j<4 packs elements 4j..4j+3 (low nibbles of Q4_0 code word j),
+//        word 4+j packs 16+4j..16+4j+3 (its high nibbles).
+// FMT 8: word j packs elements 4j..4j+3.
+template <int FMT>
+__device__ __forceinline__ void make_digits(const float *xv, int (&xw)[3][8], int (&off)[3],
+                                            float &sxs)
+{
+    float amax = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 32; k++) amax = fmaxf(amax, fabsf(xv[k]));
+    int   e = 0;
+    float inv = 0.0f;
+    if (!(amax < INFINITY)) {
+        sxs = __int_as_float(0x7fc00000);   // inf/NaN in x: let the row come out NaN
+    } else if (amax > 1e-30f) {
+        frexpf(amax, &e);                   // amax < 2^e
+        if (amax >= ldexpf(127.5f, e - 7)) e += 1;
+        inv = ldexpf(1.0f, 7 - e);          // |x * inv| <= 127.5: d0 fits int8
+        sxs = ldexpf(1.0f, e - 7 - 14);
+    } else {
+        sxs = 0.0f;                         // all-zero (or negligible) block
+    }
+    int d[3][32];
+#pragma unroll
+    for (int k = 0; k < 32; k++) {
+        const float v  = __fmul_rn(xv[k], inv);         // exact: power-of-2 scale
+        const float q0 = rintf(v);
+        const float r0 = __fmul_rn(__fsub_rn(v, q0), 128.0f);
+        const float q1 = rintf(r0);
+        const float r1 = __fmul_rn(__fsub_rn(r0, q1), 128.0f);
+        const float q2 = rintf(r1);
+        d[0][k] = (int)q0;
+        d[1][k] = (int)q1;
+        d[2][k] = (int)q2;
+    }
+#pragma unroll
+    for (int p = 0; p < 3; p++) {
+        int s = 0;
+#pragma unroll
+        for (int k = 0; k < 32; k++) s += d[p][k];
+        off[p] = (FMT == 4) ? -8 * s : 0;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const int base = (FMT == 4) ? ((j < 4) ? 4 * j : 16 + 4 * (j - 4)) : 4 * j;
+            xw[p][j] = (d[p][base] & 0xFF) | ((d[p][base + 1] & 0xFF) << 8) |
+                       ((d[p][base + 2] & 0xFF) << 16) | ((d[p][base + 3] & 0xFF) << 24);
+        }
+    }
+}
+
+// Dot of the lane's block in `row` (shared memory) with its digit planes.
+template <int FMT>
+__device__ __forceinline__ float block_dot(const uint8_t *row, int nb, int b,
+                                           const int (&xw)[3][8], const int (&off)[3], float sxs)
+{
+    int a0 = off[0], a1 = off[1], a2 = off[2];
+    float d;
+    if (FMT == 4) {
+        const uint4 q = *reinterpret_cast<const uint4 *>(row + (size_t)b * 16);
+        d = __half2float(*reinterpret_cast<const __half *>(row + (size_t)nb * 16 + 2 * b));
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int lo = (int)(w[j] & 0x0F0F0F0Fu), hi = (int)((w[j] >> 4) & 0x0F0F0F0Fu);
+            a0 = __dp4a(lo, xw[0][j], a0);
+            a0 = __dp4a(hi, xw[0][4 + j], a0);
+            a1 = __dp4a(lo, xw[1][j], a1);
+            a1 = __dp4a(hi, xw[1][4 + j], a1);
+            a2 = __dp4a(lo, xw[2][j], a2);
+            a2 = __dp4a(hi, xw[2][4 + j], a2);
+        }
+    } else {
+        // SPLIT8 rows keep the first and second 16 code bytes of every block
+        // in two separate runs, so both 16-byte loads are conflict-free
+        const uint4 q0 = *reinterpret_cast<const uint4 *>(row + (size_t)b * 16);
+        const uint4 q1 = *reinterpret_cast<const uint4 *>(row + (size_t)(nb + b) * 16);
+        d = __half2float(*reinterpret_cast<const __half *>(row + (size_t)nb * 32 + 2 * b));
+        const int w[8] = {(int)q0.x, (int)q0.y, (int)q0.z, (int)q0.w,
+                          (int)q1.x, (int)q1.y, (int)q1.z, (int)q1.w};
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            a0 = __dp4a(w[j], xw[0][j], a0);
+            a1 = __dp4a(w[j], xw[1][j], a1);
+            a2 = __dp4a(w[j], xw[2][j], a2);
+        }
+    }
+    const float t = fmaf((float)a1, 128.0f, (float)a2);
+    const float v = fmaf((float)a0, 16384.0f, t);
+    return v * (d * sxs);
+}
+
+// Shared-memory plan of one fast launch (host and device agree on it).
+struct FastSmem {
+    size_t stage_bytes, ring, bars, red, dsum, argsh, total;
+};
+
+__host__ __device__ inline FastSmem fast_smem_plan(size_t row_bytes, int stage_rows,
+                                                   int rows_per_cta, int nkg)
+{
+    FastSmem p;
+    p.stage_bytes = ((size_t)stage_rows * row_bytes + 127) & ~(size_t)127;
+    p.ring = 0;
+    p.bars = p.ring + FAST_STAGES * p.stage_bytes;
+    p.red = p.bars + 2 * FAST_STAGES * sizeof(uint64_t);
+    p.dsum = (p.red + (size_t)rows_per_cta * nkg * sizeof(float) + 15) & ~(size_t)15;
+    p.argsh = p.dsum + 256 * sizeof(double);
+    p.total = p.argsh + 32 * sizeof(ArgBest);
+    return p;
+}
+
+// blockDim = 32 * (nkg * rowpar + 1): consumer warps first, producer last.
+template <int FMT, bool NORM, int EPI>
+__global__ void __launch_bounds__(1024, 1) k_gemv_fast(GemvArgs a)
+{
+    extern __shared__ __align__(128) uint8_t smem[];
+    const DevMat &m = a.m;
+    const int nb = m.n_in / 32, nkg = nb / 32;
+    const int nw = blockDim.x >> 5, ncw = nw - 1, rowpar = ncw / nkg;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r0 = blockIdx.x * a.rows_per_cta;
+    const int nrows = max(0, min(m.n_out, r0 + a.rows_per_cta) - r0);
+    const int SR = a.stage_rows;
+    const int nstages = (nrows + SR - 1) / SR;
+    const FastSmem P = fast_smem_plan(m.row_bytes, SR, a.rows_per_cta, nkg);
+    uint8_t  *ring = smem + P.ring;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + P.bars);
+    uint64_t *empty = full + FAST_STAGES;
+    float    *red = reinterpret_cast<float *>(smem + P.red);
+    double   *dsum = reinterpret_cast<double *>(smem + P.dsum);
+    ArgBest  *argsh = reinterpret_cast<ArgBest *>(smem + P.argsh);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < FAST_STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], ncw);
+        }
+        mbar_init_fence();
+    }
+    __syncthreads();
+
+    if (warp == ncw) {
+        // ---- producer: stream this CTA's rows through the ring ----------
+        if (lane == 0) {
+            const uint8_t *src = m.data + (size_t)r0 * m.row_bytes;
+            for (int s = 0; s < nstages; s++) {
+                const int slot = s % FAST_STAGES;
+                if (s >= FAST_STAGES &&
+                    !mbar_wait(&empty[slot], ((s / FAST_STAGES) - 1) & 1, a.status))
+                    break;
+                const int      rows = min(SR, nrows - s * SR);
+                const uint32_t bytes = (uint32_t)(rows * m.row_bytes);
+                mbar_expect_tx(&full[slot], bytes);
+                bulk_g2s(ring + (size_t)slot * P.stage_bytes, src + (size_t)s * SR * m.row_bytes,
+                         bytes, &full[slot]);
+                if (s == FAST_STAGES - 1 || s == nstages - 1) pdl_trigger();
+            }
+            if (nstages == 0) pdl_trigger();
+        }
+        pdl_wait();                       // before this warp joins the epilogue writes
+    } else {
+        // ---- consumers ---------------------------------------------------
+        const int nct = ncw * 32, ctid = threadIdx.x;
+        const int g = warp % nkg, rp = warp / nkg;
+        pdl_wait();                       // x comes from the previous kernel
+        float scale = 1.0f;
+        if (NORM)
+            scale = rms_scale(a.x, m.n_in, a.eps, dsum, ctid, nct, [nct] { named_bar(1, nct); });
+        const int b = g * 32 + lane;      // this lane's block column
+        int   xw[3][8], off[3];
+        float sxs;
+        {
+            float xv[32];
+            const float4 *x4 = reinterpret_cast<const float4 *>(a.x + (size_t)b * 32);
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                float4 t = x4[k];
+                xv[4 * k] = t.x; xv[4 * k + 1] = t.y; xv[4 * k + 2] = t.z; xv[4 * k + 3] = t.w;
+            }
+            if (NORM) {
+                const float4 *w4 = reinterpret_cast<const float4 *>(a.norm_w + (size_t)b * 32);
+#pragma unroll
+                for (int k = 0; k < 8; k++) {
+                    float4 t = w4[k];
+                    xv[4 * k]     = __fmul_rn(__fmul_rn(xv[4 * k], scale), t.x);
+                    xv[4 * k + 1] = __fmul_rn(__fmul_rn(xv[4 * k + 1], scale), t.y);
+                    xv[4 * k + 2] = __fmul_rn(__fmul_rn(xv[4 * k + 2], scale), t.z);
+                    xv[4 * k + 3] = __fmul_rn(__fmul_rn(xv[4 * k + 3], scale), t.w);
+                }
+                if (a.xn_out && blockIdx.x == 0 && rp == 0) {
+                    float4 *o4 = reinterpret_cast<float4 *>(a.xn_out + (size_t)b * 32);
+#pragma unroll
+                    for (int k = 0; k < 8; k++)
+                        o4[k] = make_float4(xv[4 * k], xv[4 * k + 1], xv[4 * k + 2], xv[4 * k + 3]);
+                }
+            }
+            make_digits<FMT>(xv, xw, off, sxs);
+        }
+        for (int s = 0; s < nstages; s++) {
+            const int slot = s % FAST_STAGES;
+            if (!mbar_wait(&full[slot], (s / FAST_STAGES) & 1, a.status)) break;
+            const uint8_t *stage = ring + (size_t)slot * P.stage_bytes;
+            const int      rows = min(SR, nrows - s * SR);
+            for (int i = rp; i < rows; i += rowpar) {
+                float v = block_dot<FMT>(stage + (size_t)i * m.row_bytes, nb, b, xw, off, sxs);
+                v = warp_sum(v);
+                if (lane == 0) red[(s * SR + i) * nkg + g] = v;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+        }
+    }
+    __syncthreads();
+
+    // ---- epilogue ----------------------------------------------------------
+    const int nthr = blockDim.x;
+    ArgBest   best{-INFINITY, -1};
+    if (EPI == EPI_SWIGLU) {
+        for (int j = threadIdx.x; j < nrows / 2; j += nthr) {
+            float gsum = 0.0f, usum = 0.0f;
+            for (int q = 0; q < nkg; q++) {
+                gsum += red[(2 * j) * nkg + q];
+                usum += red[(2 * j + 1) * nkg + q];
+            }
+            a.y[r0 / 2 + j] = silu_mul(gsum, usum);
+        }
+    } else {
+        for (int r = threadIdx.x; r < nrows; r += nthr) {
+            float acc = 0.0f;
+            for (int q = 0; q < nkg; q++) acc += red[r * nkg + q];
+            if (EPI == EPI_ADD) a.y[r0 + r] = a.y[r0 + r] + acc;
+            else a.y[r0 + r] = acc;
+            if (EPI == EPI_ARGMAX) best = arg_better(best, ArgBest{acc, r0 + r});
+        }
+    }
+    if (EPI == EPI_ARGMAX) {
+        ArgBest b = block_argmax(best, argsh);
+        argmax_finish(a, b, argsh);
+    }
+}

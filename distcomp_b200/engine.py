@@ -1,0 +1,265 @@
+"""Python host mirror of the reference engine API over the CUDA library.
+
+The classes mirror src/engine.h:72-101 and src/gguf.h:52-90 name for name:
+
+    GgufModel(buf)                 gguf_open            (gguf.h:52)
+    LlmCtx(model, stage, first, last, n_ctx, device)
+                                   llm_ctx_open         (engine.h:79)
+    ctx.forward(token, out)        llm_forward          (engine.h:88)
+    ctx.reset()                    llm_reset            (engine.h:90)
+    ctx.layer_once(i, out)         llm_layer_once       (engine.h:94)
+    ctx.step_layers(n, out)        llm_step_layers      (engine.h:98)
+    ctx.pick()                     llm_pick             (engine.h:101)
+    ctx_floats(...) / ctx_bytes    llm_ctx_floats       (engine.h:74)
+    dequant(type, raw, total, off, n)
+                                   gguf_dequant         (gguf.h:86)
+
+Errors follow the reference: open raises EngineError with the message the C
+side wrote into `err`; forward/step/layer_once return 0 or -1.  Everything
+runs in libdcb200.so on the GPU: there is no CPU path here, and loading
+fails loudly when the library is missing.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+import numpy as np
+
+STAGE_EMBED, STAGE_LAYERS, STAGE_HEAD, STAGE_FULL = 0, 1, 2, 3
+
+_LIB = None
+_LIB_PATH = Path(__file__).resolve().parent / "libdcb200.so"
+
+
+class EngineError(RuntimeError):
+    pass
+
+
+class EcuInfo(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("n_layer", "n_embd", "n_head", "n_head_kv", "n_ff", "head_dim",
+                                       "n_vocab", "n_rep", "n_ctx", "stage", "first", "last", "pos",
+                                       "device")] + [("rms_eps", C.c_float), ("rope_base", C.c_float),
+                                                     ("device_bytes", C.c_size_t)]
+
+
+# (name, restype, argtypes) of every symbol include/engine_cuda.h declares
+SIGNATURES = [
+    ("ecu_model_open", C.c_int, [C.POINTER(C.c_void_p), C.c_void_p, C.c_size_t, C.c_char_p, C.c_size_t]),
+    ("ecu_model_new", C.c_void_p, []),
+    ("ecu_model_set_str", C.c_int, [C.c_void_p, C.c_char_p, C.c_char_p]),
+    ("ecu_model_set_u32", C.c_int, [C.c_void_p, C.c_char_p, C.c_ulong]),
+    ("ecu_model_set_f32", C.c_int, [C.c_void_p, C.c_char_p, C.c_float]),
+    ("ecu_model_add_tensor", C.c_int, [C.c_void_p, C.c_char_p, C.c_uint, C.POINTER(C.c_uint64), C.c_uint,
+                                       C.c_void_p, C.c_size_t]),
+    ("ecu_model_close", None, [C.c_void_p]),
+    ("ecu_model_n_tensors", C.c_size_t, [C.c_void_p]),
+    ("ecu_model_tensor", C.c_int, [C.c_void_p, C.c_char_p, C.POINTER(C.c_uint), C.POINTER(C.c_uint),
+                                   C.POINTER(C.c_uint64), C.POINTER(C.c_void_p), C.POINTER(C.c_size_t)]),
+    ("ecu_ctx_bytes", C.c_size_t, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int]),
+    ("ecu_ctx_open", C.c_int, [C.POINTER(C.c_void_p), C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                               C.c_char_p, C.c_size_t]),
+    ("ecu_ctx_close", None, [C.c_void_p]),
+    ("ecu_ctx_info", C.c_int, [C.c_void_p, C.POINTER(EcuInfo)]),
+    ("ecu_forward", C.c_int, [C.c_void_p, C.c_int, C.c_void_p]),
+    ("ecu_reset", None, [C.c_void_p]),
+    ("ecu_layer_once", C.c_int, [C.c_void_p, C.c_int, C.c_void_p]),
+    ("ecu_step_layers", C.c_int, [C.c_void_p, C.c_int, C.c_void_p]),
+    ("ecu_pick", C.c_int, [C.c_void_p]),
+    ("ecu_get_logits", C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t]),
+    ("ecu_set_pos", C.c_int, [C.c_void_p, C.c_int]),
+    ("ecu_state_ptr", C.c_void_p, [C.c_void_p]),
+    ("ecu_forward_dev", C.c_int, [C.c_void_p, C.c_int, C.c_void_p]),
+    ("ecu_generate", C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
+    ("ecu_decode_async", C.c_int, [C.c_void_p, C.c_int]),
+    ("ecu_sync", C.c_int, [C.c_void_p]),
+    ("ecu_stream", C.c_void_p, [C.c_void_p]),
+    ("ecu_dequant", C.c_int, [C.c_uint, C.c_void_p, C.c_size_t, C.c_size_t, C.c_size_t, C.c_void_p, C.c_int]),
+    ("ecu_dequant_tensor", C.c_int, [C.c_void_p, C.c_char_p, C.c_size_t, C.c_size_t, C.c_void_p]),
+    ("ecu_matvec", C.c_int, [C.c_uint, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_int]),
+    ("ecu_last_error", C.c_char_p, []),
+    ("ecu_kernel_launches", C.c_uint64, []),
+    ("ecu_version", C.c_char_p, []),
+]
+
+
+def lib() -> C.CDLL:
+    """Load libdcb200.so (building it first if the sources are newer)."""
+    global _LIB
+    if _LIB is None:
+        if os.environ.get("DCB200_NO_BUILD") != "1":
+            from . import build
+            build.build()
+        if not _LIB_PATH.exists():
+            raise EngineError(f"{_LIB_PATH} is missing: run python -m distcomp_b200.build")
+        L = C.CDLL(str(_LIB_PATH))
+        for name, res, args in SIGNATURES:
+            f = getattr(L, name)
+            f.restype = res
+            f.argtypes = args
+        _LIB = L
+    return _LIB
+
+
+def last_error() -> str:
+    return (lib().ecu_last_error() or b"").decode(errors="replace")
+
+
+def kernel_launches() -> int:
+    return int(lib().ecu_kernel_launches())
+
+
+def _ptr(a: np.ndarray) -> C.c_void_p:
+    return C.c_void_p(a.ctypes.data)
+
+
+class GgufModel:
+    """Host view of a GGUF image (the buffer must outlive every LlmCtx opened
+    from it until the open call returns; weights are copied to the device)."""
+
+    def __init__(self, buf):
+        self._buf = np.frombuffer(buf, dtype=np.uint8) if not isinstance(buf, np.ndarray) else buf
+        self.h = C.c_void_p()
+        err = C.create_string_buffer(512)
+        rc = lib().ecu_model_open(C.byref(self.h), _ptr(self._buf), self._buf.nbytes, err, 512)
+        if rc != 0:
+            raise EngineError(err.value.decode(errors="replace"))
+
+    def tensor(self, name: str):
+        t, nd = C.c_uint(), C.c_uint()
+        dims = (C.c_uint64 * 4)()
+        data, nb = C.c_void_p(), C.c_size_t()
+        if lib().ecu_model_tensor(self.h, name.encode(), C.byref(t), C.byref(nd), dims, C.byref(data),
+                                  C.byref(nb)) != 0:
+            raise KeyError(name)
+        return int(t.value), [int(dims[i]) for i in range(nd.value)], int(data.value), int(nb.value)
+
+    def n_tensors(self) -> int:
+        return int(lib().ecu_model_n_tensors(self.h))
+
+    def close(self):
+        if self.h:
+            lib().ecu_model_close(self.h)
+            self.h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def ctx_bytes(model: GgufModel, stage: int, first: int = 0, last: int = 0, n_ctx: int = 0) -> int:
+    return int(lib().ecu_ctx_bytes(model.h, stage, first, last, n_ctx))
+
+
+class LlmCtx:
+    """One engine stage resident on one GPU (llm_ctx, src/engine.h:46-70)."""
+
+    def __init__(self, model: GgufModel, stage: int, first: int = 0, last: int = 0, n_ctx: int = 0,
+                 device: int = 0):
+        self.h = C.c_void_p()
+        err = C.create_string_buffer(512)
+        rc = lib().ecu_ctx_open(C.byref(self.h), model.h, stage, first, last, n_ctx, device, err, 512)
+        if rc != 0:
+            raise EngineError(err.value.decode(errors="replace"))
+        i = EcuInfo()
+        lib().ecu_ctx_info(self.h, C.byref(i))
+        self.info = i
+        self.n_embd, self.n_vocab, self.n_ctx = i.n_embd, i.n_vocab, i.n_ctx
+        self.stage = stage
+
+    # --- reference API ---------------------------------------------------
+    def forward(self, token: int, out: np.ndarray) -> int:
+        assert out.dtype == np.float32 and out.flags.c_contiguous
+        return int(lib().ecu_forward(self.h, int(token), _ptr(out)))
+
+    def reset(self) -> None:
+        lib().ecu_reset(self.h)
+
+    def layer_once(self, idx: int, out: np.ndarray) -> int:
+        return int(lib().ecu_layer_once(self.h, int(idx), _ptr(out)))
+
+    def step_layers(self, n: int, out: np.ndarray) -> int:
+        return int(lib().ecu_step_layers(self.h, int(n), _ptr(out)))
+
+    def pick(self) -> int:
+        return int(lib().ecu_pick(self.h))
+
+    # --- extras ----------------------------------------------------------
+    def logits(self) -> np.ndarray:
+        out = np.empty(self.n_vocab, dtype=np.float32)
+        if lib().ecu_get_logits(self.h, _ptr(out), self.n_vocab) != 0:
+            raise EngineError(last_error())
+        return out
+
+    def set_pos(self, pos: int) -> None:
+        if lib().ecu_set_pos(self.h, int(pos)) != 0:
+            raise EngineError("bad position")
+
+    @property
+    def pos(self) -> int:
+        i = EcuInfo()
+        lib().ecu_ctx_info(self.h, C.byref(i))
+        return int(i.pos)
+
+    def generate(self, prompt, n_gen: int) -> list[int]:
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.zeros(max(n_gen, 1), dtype=np.int32)
+        if lib().ecu_generate(self.h, _ptr(p), len(p), int(n_gen), _ptr(out)) != 0:
+            raise EngineError(last_error())
+        return [int(t) for t in out[:n_gen]]
+
+    def decode_async(self, n: int) -> None:
+        if lib().ecu_decode_async(self.h, int(n)) != 0:
+            raise EngineError(last_error())
+
+    def sync(self) -> None:
+        if lib().ecu_sync(self.h) != 0:
+            raise EngineError(last_error())
+
+    def forward_dev(self, token: int, stream: int | None = None) -> None:
+        if lib().ecu_forward_dev(self.h, int(token), C.c_void_p(stream or 0)) != 0:
+            raise EngineError(last_error())
+
+    def state_ptr(self) -> int:
+        return int(lib().ecu_state_ptr(self.h) or 0)
+
+    def stream(self) -> int:
+        return int(lib().ecu_stream(self.h) or 0)
+
+    def dequant_tensor(self, name: str, off: int, n: int) -> np.ndarray:
+        out = np.empty(n, dtype=np.float32)
+        if lib().ecu_dequant_tensor(self.h, name.encode(), off, n, _ptr(out)) != 0:
+            raise EngineError(last_error())
+        return out
+
+    def close(self) -> None:
+        if self.h:
+            lib().ecu_ctx_close(self.h)
+            self.h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def dequant(gtype: int, raw: np.ndarray, total: int, off: int, n: int, device: int = 0) -> tuple[int, np.ndarray]:
+    """gguf_dequant on the GPU: (rc, values)."""
+    raw = np.ascontiguousarray(raw, dtype=np.uint8)
+    out = np.zeros(max(n, 1), dtype=np.float32)
+    rc = lib().ecu_dequant(gtype, _ptr(raw), total, off, n, _ptr(out), device)
+    return int(rc), out[:n]
+
+
+def matvec(gtype: int, raw: np.ndarray, n_in: int, n_out: int, x: np.ndarray, device: int = 0) -> np.ndarray:
+    """y = W x for a raw GGUF weight (uploads per call)."""
+    raw = np.ascontiguousarray(raw, dtype=np.uint8)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty(n_out, dtype=np.float32)
+    if lib().ecu_matvec(gtype, _ptr(raw), n_in, n_out, _ptr(x), _ptr(y), device) != 0:
+        raise EngineError(last_error())
+    return y

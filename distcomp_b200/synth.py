@@ -1,0 +1,240 @@
+"""Seeded synthetic llama-shaped GGUF models and prompts.
+
+Weights are N(0, 0.02) per tensor (the generator is seeded by the model seed
+and the CRC-32 of the tensor name, so any subset of tensors can be rebuilt
+independently), quantised to the requested GGUF block type; norm weights
+are 1.0 in F32.  Tensors whose input length is not a whole number of blocks
+are stored as F32 (the tiny shape's 688-wide ffn_down cannot be Q8_0: the
+reference matvec would return zeros for it, src/engine.c:317-320).
+
+Two generation paths with the same quantisation rule:
+  * ``device="cpu"``: numpy PCG64 normals, quantised by gguf-py (the
+    reference's scripts use the same package); stable across machines, used
+    for the fixtures and CPU-checkable models.
+  * ``device="cuda"``: torch normals on the GPU and the torch restatement of
+    the same Q4_0/Q8_0 rule in ``quantize_torch``; used for the 4.6 GB
+    8B-shaped model, which would take minutes on the host.
+"""
+from __future__ import annotations
+
+import zlib
+from dataclasses import dataclass, replace
+
+import numpy as np
+
+from . import gguf as G
+
+
+@dataclass(frozen=True)
+class LlamaSpec:
+    n_layer: int
+    n_embd: int
+    n_head: int
+    n_head_kv: int
+    n_ff: int
+    n_vocab: int
+    n_ctx: int
+    rope_base: float = 10000.0
+    eps: float = 1e-5
+    wtype: int = G.Q8_0          # attention / FFN weights
+    emb_type: int = G.Q8_0       # token_embd
+    out_type: int = G.Q8_0       # output
+    arch: str = "llama"
+    tied: bool = False           # no output.weight: the head reuses token_embd
+    qkv_bias: bool = False       # qwen2-style attention biases
+    head_dim: int | None = None  # writes rope.dimension_count when set
+    sigma: float = 0.02
+
+
+SPECS = {
+    # single-node CPU shape: dim 256, 4 layers, 8 heads, FFN 688, vocab 4096
+    "tiny": LlamaSpec(4, 256, 8, 8, 688, 4096, 256, 10000.0),
+    # Llama-3-8B shape, Q4_0 layers, Q8_0 embedding and head
+    "llama3-8b": LlamaSpec(32, 4096, 32, 8, 14336, 128256, 4096, 500000.0, wtype=G.Q4_0),
+    # Llama-2-70B shape (Q4_K layers)
+    "llama2-70b": LlamaSpec(80, 8192, 64, 8, 28672, 32000, 8448, 10000.0, wtype=G.Q4_K),
+    # small shapes that still exercise the fast Q4_0/Q8_0 GEMV path (n_in % 1024 == 0)
+    "mini-q4": LlamaSpec(2, 1024, 8, 2, 2048, 2048, 128, 500000.0, wtype=G.Q4_0),
+    "mini-q8": LlamaSpec(2, 1024, 16, 4, 3072, 1536, 96, 10000.0, wtype=G.Q8_0),
+}
+
+
+def spec(name: str, **over) -> LlamaSpec:
+    return replace(SPECS[name], **over)
+
+
+def tensor_list(s: LlamaSpec):
+    """[(name, dims, ggml type)] in file order; dims are ggml's [n_in, n_out]."""
+    hd = s.head_dim or s.n_embd // s.n_head
+    qd, kvd = s.n_head * hd, s.n_head_kv * hd
+
+    def wt(n_in, t):
+        if t in (G.F32, G.F16):
+            return t
+        return t if n_in % G.BLOCK[t][0] == 0 else G.F32
+
+    out = [("token_embd.weight", (s.n_embd, s.n_vocab), wt(s.n_embd, s.emb_type))]
+    for i in range(s.n_layer):
+        p = f"blk.{i}."
+        out += [
+            (p + "attn_norm.weight", (s.n_embd,), G.F32),
+            (p + "attn_q.weight", (s.n_embd, qd), wt(s.n_embd, s.wtype)),
+            (p + "attn_k.weight", (s.n_embd, kvd), wt(s.n_embd, s.wtype)),
+            (p + "attn_v.weight", (s.n_embd, kvd), wt(s.n_embd, s.wtype)),
+            (p + "attn_output.weight", (qd, s.n_embd), wt(qd, s.wtype)),
+            (p + "ffn_norm.weight", (s.n_embd,), G.F32),
+            (p + "ffn_gate.weight", (s.n_embd, s.n_ff), wt(s.n_embd, s.wtype)),
+            (p + "ffn_up.weight", (s.n_embd, s.n_ff), wt(s.n_embd, s.wtype)),
+            (p + "ffn_down.weight", (s.n_ff, s.n_embd), wt(s.n_ff, s.wtype)),
+        ]
+        if s.qkv_bias:
+            out += [(p + "attn_q.bias", (qd,), G.F32), (p + "attn_k.bias", (kvd,), G.F32),
+                    (p + "attn_v.bias", (kvd,), G.F32)]
+    out.append(("output_norm.weight", (s.n_embd,), G.F32))
+    if not s.tied:
+        out.append(("output.weight", (s.n_embd, s.n_vocab), wt(s.n_embd, s.out_type)))
+    return out
+
+
+def name_seed(seed: int, name: str) -> list[int]:
+    return [int(seed), zlib.crc32(name.encode()) & 0xFFFFFFFF]
+
+
+# ------------------------------------------------------------ quantisation --
+
+def quantize_numpy(w: np.ndarray, gtype: int) -> np.ndarray:
+    """float32 [.., n_in] -> GGUF block bytes (gguf-py, the ggml rule)."""
+    if gtype == G.F32:
+        return np.ascontiguousarray(w, dtype=np.float32).view(np.uint8).reshape(-1)
+    if gtype == G.F16:
+        return np.ascontiguousarray(w, dtype=np.float16).view(np.uint8).reshape(-1)
+    from gguf import quants, GGMLQuantizationType as QT
+    qt = {G.Q4_0: QT.Q4_0, G.Q8_0: QT.Q8_0, G.Q4_1: QT.Q4_1, G.Q5_0: QT.Q5_0, G.Q5_1: QT.Q5_1}[gtype]
+    return np.ascontiguousarray(quants.quantize(w.astype(np.float32), qt)).view(np.uint8).reshape(-1)
+
+
+def quantize_torch(w, gtype: int):
+    """Torch restatement of the same rule (runs on CUDA).  Returns uint8.
+
+    Q4_0 (ggml quantize_row_q4_0_ref, as gguf-py states it): per 32-block,
+    m = the element of largest magnitude (first one on ties), d = m / -8,
+    id = 1/d (0 when d == 0), q = min(15, trunc(x*id + 8.5)); bytes =
+    fp16(d), then q[i] | q[i+16] << 4 for i < 16.
+    Q8_0: d = max|x| / 127, id = 1/d (0 when d == 0), q = round-half-away(x*id)
+    as int8; bytes = fp16(d), q[0..31].
+    Every step is a single fp32 operation, so the result is bit-identical to
+    gguf-py's numpy code (checked in tests/test_synth.py)."""
+    import torch
+    x = w.reshape(-1, 32).to(torch.float32)
+    nblk = x.shape[0]
+    if gtype == G.Q4_0:
+        idx = x.abs().argmax(dim=1, keepdim=True)
+        m = torch.gather(x, 1, idx)
+        d = m / -8.0
+        inv = torch.where(d == 0, torch.zeros_like(d), 1.0 / d)
+        q = torch.trunc(x * inv + 8.5).clamp(0, 15).to(torch.uint8)
+        packed = q[:, :16] | (q[:, 16:] << 4)
+        dh = d.to(torch.float16).view(torch.uint8).reshape(nblk, 2)
+        return torch.cat([dh, packed], dim=1).reshape(-1)
+    if gtype == G.Q8_0:
+        d = x.abs().amax(dim=1, keepdim=True) / 127.0
+        inv = torch.where(d == 0, torch.zeros_like(d), 1.0 / d)
+        v = x * inv
+        a = v.abs()
+        fl = a.floor()
+        r = (fl + (2.0 * (a - fl)).floor()) * v.sign()
+        q = r.to(torch.int8).view(torch.uint8)
+        dh = d.to(torch.float16).view(torch.uint8).reshape(nblk, 2)
+        return torch.cat([dh, q], dim=1).reshape(-1)
+    raise ValueError(f"quantize_torch: type {gtype} not supported")
+
+
+def random_kquant_blocks(rng: np.random.Generator, gtype: int, nblk: int, sigma: float = 0.02):
+    """Random K-quant blocks: uniform code/scale bytes, fp16 super-block scales
+    drawn as |N(0, sigma)| / 64 so that weights land around sigma.  (gguf-py
+    cannot quantise K-quants; any bytes are valid blocks.)"""
+    be, bb = G.BLOCK[gtype]
+    raw = rng.integers(0, 256, size=(nblk, bb), dtype=np.uint8)
+    scale = (np.abs(rng.standard_normal((nblk, 2))) * sigma / 64).astype(np.float16)
+    if gtype in (G.Q4_K, G.Q5_K):
+        raw[:, 0:4] = scale.view(np.uint8)
+    elif gtype == G.Q2_K:
+        raw[:, 80:84] = scale.view(np.uint8)
+    elif gtype == G.Q3_K:
+        raw[:, 108:110] = scale[:, :1].view(np.uint8)
+    elif gtype == G.Q6_K:
+        raw[:, 208:210] = scale[:, :1].view(np.uint8)
+    elif gtype == G.Q8_K:
+        # the reference's Q8_K reads 32 fp16 scales at bytes 256..319 of a
+        # 292-byte block (src/gguf.c:650-659), i.e. 28 of them overlap the
+        # next block; only the first 18 lie inside the block
+        s = (np.abs(rng.standard_normal((nblk, 18))) * sigma / 64).astype(np.float16)
+        raw[:, 256:292] = s.view(np.uint8).reshape(nblk, 36)
+    return raw.reshape(-1)
+
+
+# --------------------------------------------------------------- builders --
+
+def _meta(b: G.GGUFBuilder, s: LlamaSpec):
+    a = s.arch
+    b.add_kv("general.architecture", G.T_STR, a)
+    b.add_kv("general.alignment", G.T_U32, G.ALIGN)
+    b.add_kv(f"{a}.block_count", G.T_U32, s.n_layer)
+    b.add_kv(f"{a}.context_length", G.T_U32, s.n_ctx)
+    b.add_kv(f"{a}.embedding_length", G.T_U32, s.n_embd)
+    b.add_kv(f"{a}.feed_forward_length", G.T_U32, s.n_ff)
+    b.add_kv(f"{a}.attention.head_count", G.T_U32, s.n_head)
+    b.add_kv(f"{a}.attention.head_count_kv", G.T_U32, s.n_head_kv)
+    b.add_kv(f"{a}.attention.layer_norm_rms_epsilon", G.T_F32, s.eps)
+    b.add_kv(f"{a}.rope.freq_base", G.T_F32, s.rope_base)
+    if s.head_dim:
+        b.add_kv(f"{a}.rope.dimension_count", G.T_U32, s.head_dim)
+    b.add_kv(f"{a}.vocab_size", G.T_U32, s.n_vocab)
+
+
+def build_model(s: LlamaSpec, seed: int = 0, device: str = "cpu") -> np.ndarray:
+    """The whole GGUF image as a numpy uint8 array."""
+    b = G.GGUFBuilder()
+    _meta(b, s)
+    tl = tensor_list(s)
+    for name, dims, gt in tl:
+        b.add_tensor(name, dims, gt)
+    b.finalize()
+    if device != "cpu":
+        import torch
+        dev = torch.device(device)
+    for name, dims, gt in tl:
+        view = b.tensor_view(name)
+        n = int(np.prod(dims))
+        if name.endswith("norm.weight"):
+            view[:] = np.ones(n, dtype=np.float32).view(np.uint8)
+            continue
+        if gt in (G.Q2_K, G.Q3_K, G.Q4_K, G.Q5_K, G.Q6_K, G.Q8_K):
+            rng = np.random.default_rng(name_seed(seed, name))
+            view[:] = random_kquant_blocks(rng, gt, n // G.BLOCK[gt][0], s.sigma)
+            continue
+        if device == "cpu":
+            rng = np.random.default_rng(name_seed(seed, name))
+            w = (rng.standard_normal(n, dtype=np.float32) * np.float32(s.sigma)).reshape(dims[::-1])
+            view[:] = quantize_numpy(w, gt)
+        else:
+            import torch
+            gen = torch.Generator(device=dev)
+            ns = name_seed(seed, name)
+            gen.manual_seed(ns[0] * 1_000_003 + ns[1])
+            w = torch.randn(n, generator=gen, device=dev, dtype=torch.float32) * s.sigma
+            if gt == G.F32:
+                qb = w.view(torch.uint8)
+            elif gt == G.F16:
+                qb = w.to(torch.float16).view(torch.uint8)
+            else:
+                qb = quantize_torch(w, gt)
+            torch.from_numpy(view).copy_(qb.cpu())
+            del w, qb
+    return b.buf
+
+
+def prompt_tokens(n: int, n_vocab: int, seed: int = 0) -> list[int]:
+    """Uniform token ids in [3, n_vocab)."""
+    rng = np.random.default_rng([int(seed), 0x70726F6D])
+    return [int(t) for t in rng.integers(3, n_vocab, size=n)]

@@ -1,0 +1,160 @@
+/*
+ * engine_cuda.h -- C ABI of the B200 (sm_100a) llama token loop.
+ *
+ * Drop-in for distcomp's CPU engine (src/engine.h:74-101) and its GGUF block
+ * dequant (src/gguf.h:86).  Plain C types only: no CUDA or torch types cross
+ * this boundary; streams are passed as `void *` (a cudaStream_t, or NULL for
+ * the context's own stream).
+ *
+ * Contract kept from the reference:
+ *   - errors are int 0 / -1; open functions write a message into err[errlen]
+ *     (src/engine.c:23-27), ecu_last_error() returns the last one per thread;
+ *   - a context serves one stage: EMBED, a contiguous LAYERS range or HEAD
+ *     (src/engine.h:23-27); ECU_STAGE_FULL is an addition that runs all three
+ *     back to back on one device;
+ *   - ecu_forward has llm_forward's `out` contract (src/engine.h:83-88):
+ *       EMBED  out[0..n_embd)  = embedding row of `token`
+ *       LAYERS out in and out  = the state after this stage's layers
+ *       HEAD   out[0..n_embd)  = normed state, out[n_embd] = argmax token
+ *       FULL   as HEAD, from `token` alone;
+ *   - a context is single-threaded, like llm_ctx.
+ * Weights are uploaded (and repacked for coalesced loads, values unchanged)
+ * once at open; the caller's file buffer may be released afterwards.
+ */
+#ifndef DC_ENGINE_CUDA_H
+#define DC_ENGINE_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    ECU_STAGE_EMBED  = 0,   /* src/engine.h:24 LLM_STAGE_EMBED  */
+    ECU_STAGE_LAYERS = 1,   /* src/engine.h:25 LLM_STAGE_LAYERS */
+    ECU_STAGE_HEAD   = 2,   /* src/engine.h:26 LLM_STAGE_HEAD   */
+    ECU_STAGE_FULL   = 3    /* new: embed + all layers + head on one device */
+};
+
+typedef struct ecu_model ecu_model;   /* host view of a GGUF file (borrowed bytes) */
+typedef struct ecu_ctx   ecu_ctx;     /* one stage resident on one device           */
+
+/* Geometry of an open context (the fields of llm_ctx, src/engine.h:46-70). */
+typedef struct {
+    int   n_layer, n_embd, n_head, n_head_kv, n_ff, head_dim, n_vocab, n_rep, n_ctx;
+    int   stage, first, last, pos, device;
+    float rms_eps, rope_base;
+    size_t device_bytes;      /* weights + KV cache + work buffers on the device */
+} ecu_info;
+
+/* ---- GGUF view --------------------------------------------------------- */
+
+/* Parse a GGUF v2/v3 image held by the caller (replaces gguf_open,
+ * src/gguf.h:52).  Tensor data stay in `file` until a context is opened. */
+int  ecu_model_open(ecu_model **out, const void *file, size_t size, char *err, size_t errlen);
+
+/* Assemble a model from tensor views and metadata instead of a file image,
+ * as dcd's shard role does when it builds a gguf_file from received tensors
+ * (src/daemon.c:963-1019). */
+ecu_model *ecu_model_new(void);
+int  ecu_model_set_str(ecu_model *m, const char *key, const char *val);
+int  ecu_model_set_u32(ecu_model *m, const char *key, unsigned long val);
+int  ecu_model_set_f32(ecu_model *m, const char *key, float val);
+int  ecu_model_add_tensor(ecu_model *m, const char *name, unsigned n_dims, const uint64_t *dims,
+                          unsigned ggml_type, const void *data, size_t nbytes);
+void ecu_model_close(ecu_model *m);
+/* Number of tensors, and lookup by name (gguf_tensor_find, src/gguf.h:72). */
+size_t ecu_model_n_tensors(const ecu_model *m);
+int  ecu_model_tensor(const ecu_model *m, const char *name, unsigned *ggml_type,
+                      unsigned *n_dims, uint64_t dims[4], const void **data, size_t *nbytes);
+
+/* ---- engine (src/engine.h:72-101) -------------------------------------- */
+
+/* Device bytes a stage needs at context length n_ctx (0 = the model's);
+ * the device counterpart of llm_ctx_floats (src/engine.h:74).  0 on error. */
+size_t ecu_ctx_bytes(const ecu_model *m, int stage, int first, int last, int n_ctx);
+
+/* Open a stage on CUDA device `device` (replaces llm_ctx_open,
+ * src/engine.h:79).  The same geometry and error rules as the reference. */
+int  ecu_ctx_open(ecu_ctx **out, const ecu_model *m, int stage, int first, int last, int n_ctx,
+                  int device, char *err, size_t errlen);
+void ecu_ctx_close(ecu_ctx *c);
+int  ecu_ctx_info(const ecu_ctx *c, ecu_info *info);
+
+/* One token through the stage, host `out` (replaces llm_forward,
+ * src/engine.h:88).  -1 for a token outside the vocabulary (EMBED/FULL) or
+ * an exhausted context (LAYERS/FULL). */
+int  ecu_forward(ecu_ctx *c, int token, float *out);
+/* Rewind the KV cache (replaces llm_reset, src/engine.h:90). */
+void ecu_reset(ecu_ctx *c);
+/* Exactly one layer at the current position, position unchanged
+ * (replaces llm_layer_once, src/engine.h:94). */
+int  ecu_layer_once(ecu_ctx *c, int layer_idx, float *out);
+/* The first n layers of the stage (0 = all), then pos++ (replaces
+ * llm_step_layers, src/engine.h:98). */
+int  ecu_step_layers(ecu_ctx *c, int n, float *out);
+/* Argmax of the last HEAD/FULL logits, lowest index on ties (replaces
+ * llm_pick, src/engine.h:101). */
+int  ecu_pick(const ecu_ctx *c);
+/* Copy the last logits to host memory (n floats, n <= n_vocab). */
+int  ecu_get_logits(const ecu_ctx *c, float *out, size_t n);
+/* Set the cache position directly (what engine_stages.c does with lay.pos). */
+int  ecu_set_pos(ecu_ctx *c, int pos);
+
+/* ---- device-resident chaining (no host hop between stages) ------------- */
+
+/* Device pointer of the stage's state buffer (n_embd + 1 floats).  LAYERS
+ * and HEAD read their input there; every stage leaves its output there. */
+float *ecu_state_ptr(ecu_ctx *c);
+/* ecu_forward without host copies: input/output in ecu_state_ptr(c),
+ * enqueued on `stream` (NULL = the context's stream), not synchronised.
+ * The token is read from host memory at enqueue time. */
+int  ecu_forward_dev(ecu_ctx *c, int token, void *stream);
+/* Greedy decode on a FULL context without host round trips: feeds
+ * prompt[0..n_prompt) token by token, then generates n_gen tokens, each one
+ * fed back on the device.  out_tokens receives the n_gen generated ids.
+ * Returns 0, or -1 when the context runs out. */
+int  ecu_generate(ecu_ctx *c, const int *prompt, int n_prompt, int n_gen, int *out_tokens);
+/* Decode steps on a FULL context continuing from the token in the state
+ * buffer, on the context's stream, without synchronising; used to time the
+ * device-side loop.  Returns 0 or -1. */
+int  ecu_decode_async(ecu_ctx *c, int n_steps);
+/* Wait for the context's stream; returns -1 if a kernel reported an error. */
+int  ecu_sync(ecu_ctx *c);
+/* The context's CUDA stream (as void *). */
+void *ecu_stream(ecu_ctx *c);
+
+/* ---- block dequant on the device (replaces gguf_dequant, src/gguf.h:86) - */
+
+/* Dequantise elements [off, off+n) of a tensor of `total` elements and ggml
+ * type `ggml_type` whose raw GGUF blocks are at host pointer `raw`, on
+ * device `device`, into host `dst`.  Same rejection rules as the reference
+ * (range, block-aligned off, supported types).  Bit-exact with it. */
+int  ecu_dequant(unsigned ggml_type, const void *raw, size_t total, size_t off, size_t n,
+                 float *dst, int device);
+/* The same from a context's uploaded (repacked) copy of tensor `name`,
+ * proving the device layout holds the file's values. */
+int  ecu_dequant_tensor(ecu_ctx *c, const char *name, size_t off, size_t n, float *dst);
+
+/* ---- single-GEMV entry point (the quantised matvec of src/engine.c:348) - */
+
+/* y[o] = sum_i W[i + o*n_in] x[i] for a raw GGUF weight at host pointer
+ * `w_raw` on `device`; x and y are host arrays.  Uploads per call: for
+ * tests and one-off use, not the token loop. */
+int  ecu_matvec(unsigned ggml_type, const void *w_raw, int n_in, int n_out, const float *x,
+                float *y, int device);
+
+/* ---- misc -------------------------------------------------------------- */
+
+const char *ecu_last_error(void);
+/* Number of kernels this process has launched through the engine. */
+uint64_t ecu_kernel_launches(void);
+/* Library version string. */
+const char *ecu_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,325 @@
+#!/usr/bin/env python3
+"""Batch-1 greedy decode throughput of the 8B-shaped Q4_0 llama on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (the 8B decode configuration): dim 4096, 32 layers, 32/8 heads,
+FFN 14336, vocab 128256, RoPE theta 5e5; N(0,0.02) weights quantised to
+Q4_0 (embedding and head Q8_0), generated on the GPU from a fixed seed;
+KV cache fp32 for 4096 positions.  A 512-token random prompt is fed
+first, then W untimed and K timed greedy decode steps.  One step = one
+token through embed -> 32 layers -> head -> argmax, the next token fed back
+on the device (one CUDA-graph replay per token).  The 4.5 GB of weights
+stream from HBM every step, far above the 126 MB L2, so no flush is needed.
+
+One JSON line: value = tokens/s from CUDA events around the K steps; e2e =
+the same through ecu_forward with host buffers (token in, state + token
+out, pinned copies inside the timed region); roofline = the dominant
+kernel (fused gate/up GEMV + SwiGLU) from CUDA events of a profiling
+replay; cpu_baseline = the reference engine (oracle/_ref, compiled from the
+reference's sources) on this host's cores on a bounded sample.
+
+--impl reference times that reference CPU engine alone (rank 0) on the
+same config and prints the same line with "impl": "reference".
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "decode tokens/s (batch 1) + % HBM roofline, 8B-shape Q4_0, 1/2/4/8 B200 vs host CPU"
+CONFIG = "llama3-8b"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=4)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--prompt", type=int, default=512)
+    ap.add_argument("--n-ctx", type=int, default=4096)
+    ap.add_argument("--profile-steps", type=int, default=2)
+    ap.add_argument("--cpu-sample-s", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--seed", type=int, default=0)
+    return ap.parse_args()
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons while the timed region runs."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"dcb200_clocks_{os.getpid()}.csv"
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        self.proc.wait(timeout=10)
+        sm, mx, reasons = [], None, set()
+        names = ["active", "hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.path.read_text().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names[1:], f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        self.path.unlink(missing_ok=True)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+def algorithmic_bytes_per_token(spec, pos_mean: float) -> float:
+    """Weights as stored + KV rows read (positions 0..pos) and written."""
+    from distcomp_b200 import synth
+    from distcomp_b200 import gguf as G
+    w = 0
+    for name, dims, gt in synth.tensor_list(spec):
+        n = 1
+        for d in dims:
+            n *= d
+        if name == "token_embd.weight":
+            w += G.type_nbytes(gt, dims[0])        # one embedding row
+        else:
+            w += G.type_nbytes(gt, n)
+    hd = spec.n_embd // spec.n_head
+    kv_row = 2 * spec.n_head_kv * hd * 4 * spec.n_layer
+    return w + kv_row * (pos_mean + 1) + kv_row
+
+
+def cpu_reference_tokens_per_s(buf, spec, budget_s: float, max_tokens: int, threads: int | None = None):
+    """The reference engine (three stages, as src/shard.c's local run) on the
+    host cores: decode tokens from position 0 until the budget is used.
+    Returns (tokens/s, tokens timed, threads, kind)."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import numpy as np
+    import oracle
+    kind = "reference" if oracle.available("ref") else "port"
+    lib = oracle.get("ref" if kind == "reference" else "port")
+    n_thr = 1
+    if kind == "reference":
+        n_thr = min(64, threads or os.cpu_count() or 1)
+        lib.set_threads(n_thr)
+    m = lib.model(buf)
+    emb, lay, head = m.ctx(0), m.ctx(1, 0, spec.n_layer - 1, 64), m.ctx(2)
+    st = np.zeros(spec.n_embd + 8, dtype=np.float32)
+    tok = 3
+
+    def step(t):
+        assert emb.forward(t, st) == 0 and lay.forward(t, st) == 0 and head.forward(t, st) == 0
+        return int(st[spec.n_embd])
+
+    tok = step(tok)                      # warm-up: thread pool, page-in
+    n, t0 = 0, time.perf_counter()
+    while n < max_tokens:
+        tok = step(tok)
+        n += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return n / dt, n, n_thr, kind
+
+
+def build_model_gpu(spec, seed, device):
+    from distcomp_b200 import synth
+    import torch
+    torch.cuda.set_device(device)
+    buf = synth.build_model(spec, seed=seed, device=f"cuda:{device}")
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return buf
+
+
+def load_traffic():
+    """dram bytes per launch of the dominant kernel from the committed ncu
+    summary, when one exists."""
+    p = ROOT / "profiles" / "gemv_gate_up_q4_0_8b.json"
+    if p.exists():
+        try:
+            d = json.loads(p.read_text())
+            return d.get("dram_bytes_per_launch"), d.get("scaled_from")
+        except Exception:
+            pass
+    return None, None
+
+
+def our_arm(args, rank, world, local):
+    import numpy as np
+    import torch
+    from distcomp_b200 import engine as E
+    from distcomp_b200 import synth
+
+    if world > 1:
+        from distcomp_b200 import pipeline
+        return pipeline.bench_main(args, rank, world, local)
+
+    spec = synth.spec(CONFIG)
+    t_build = time.perf_counter()
+    buf = build_model_gpu(spec, args.seed, local)
+    t_build = time.perf_counter() - t_build
+    model = E.GgufModel(buf)
+    t_up = time.perf_counter()
+    ctx = E.LlmCtx(model, E.STAGE_FULL, n_ctx=args.n_ctx, device=local)
+    t_up = time.perf_counter() - t_up
+    prompt = synth.prompt_tokens(args.prompt, spec.n_vocab, seed=args.seed)
+    need = args.prompt + args.warmup + 2 * args.steps + args.profile_steps + 2
+    if need > args.n_ctx:
+        raise SystemExit(f"prompt + steps need {need} positions > n_ctx {args.n_ctx}")
+
+    ctx.generate(prompt, 1)                         # prompt token by token, as the reference does
+    ctx.decode_async(args.warmup)
+    ctx.sync()
+    stream = torch.cuda.ExternalStream(ctx.stream(), device=f"cuda:{local}")
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(local)
+    clocks.start()
+    pos0 = ctx.pos
+    torch.cuda.synchronize(local)
+    l0 = E.kernel_launches()
+    e0.record(stream)
+    ctx.decode_async(args.steps)
+    e1.record(stream)
+    ctx.sync()
+    torch.cuda.synchronize(local)
+    launches = E.kernel_launches() - l0
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    tps = args.steps / (ms / 1e3)
+
+    # dominant-kernel roofline from a profiling replay (events per launch)
+    prof = ctx.profile_steps(args.profile_steps)
+    peak, peak_kind = peaks()
+    dom = "gemv_gate_up"
+    n_l, tot_ms, bpl = prof[dom]
+    avg_ms = tot_ms / n_l
+    achieved = bpl / (avg_ms / 1e3) / 1e9
+    traffic, scaled = load_traffic()
+
+    # end to end through the C ABI with host buffers
+    out = np.zeros(spec.n_embd + 1, dtype=np.float32)
+    tok = ctx.pick()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        if ctx.forward(tok, out) != 0:
+            raise SystemExit("ecu_forward failed: " + E.last_error())
+        tok = int(out[spec.n_embd])
+    e2e_s = time.perf_counter() - t0
+    e2e = args.steps / e2e_s
+
+    bpt = algorithmic_bytes_per_token(spec, pos0 + (args.steps - 1) / 2)
+    line = {
+        "metric": METRIC, "value": round(tps, 2), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "q4_0 codes x int8 digit planes, fp32 accumulate",
+        "data": "synthetic: seeded N(0,0.02) weights quantised to Q4_0/Q8_0 on the GPU, random prompt",
+        "config": {"workload": "llama3-8b-shape Q4_0 decode, batch 1 (dim 4096, 32 layers, 32/8 heads, "
+                               "ffn 14336, vocab 128256, theta 5e5, KV fp32 4096)",
+                   "prompt_tokens": args.prompt, "decode_positions": [pos0, pos0 + args.steps - 1],
+                   "l2": "inputs larger than L2 (4.49 GB of weights per step)", "n_ctx": args.n_ctx},
+        "token_roofline": {"bytes_per_token": bpt, "achieved_gbs": round(bpt * tps / 1e9, 1),
+                           "peak_gbs": peak, "frac": round(bpt * tps / 1e9 / peak, 4),
+                           "frac_of_8tbs_nominal": round(bpt * tps / 1e9 / 8000, 4), "peak_kind": peak_kind},
+        "roofline": {"kernel": "k_gemv_fast<Q4_0, rmsnorm, swiglu> (fused ffn_gate+ffn_up)", "bound": "hbm",
+                     "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "bytes_per_launch": bpl, "avg_launch_us": round(avg_ms * 1e3, 2),
+                     "peak_kind": peak_kind, "traffic_scaled_from": scaled},
+        "kernels_per_token": {k: {"launches": v[0] / args.profile_steps, "us": round(v[1] / args.profile_steps * 1e3, 1),
+                                  "gbs": round(v[2] * v[0] / (v[1] / 1e3) / 1e9, 1) if v[1] > 0 else None}
+                              for k, v in prof.items()},
+        "e2e": {"value": round(e2e, 2), "unit": "tokens/s", "h2d_bytes_per_step": 8,
+                "d2h_bytes_per_step": (spec.n_embd + 1) * 4, "api": "ecu_forward (FULL context)"},
+        "gpu_launches": int(launches),
+        "clocks": clk,
+        "setup_s": {"model_build": round(t_build, 1), "upload": round(t_up, 1)},
+    }
+    if not args.no_cpu_baseline:
+        v, n, thr, kind = cpu_reference_tokens_per_s(buf, spec, args.cpu_sample_s, 64)
+        line["cpu_baseline"] = {"value": round(v, 4), "unit": "tokens/s", "cores": thr, "kind": kind,
+                                "sample": f"{n} decode tokens at positions 1..{n} of the same 8B Q4_0 model "
+                                          f"(embed+32 layers+head, three stages like shard.c's local run); "
+                                          f"KV reads differ from positions 512..767 by <4% of the bytes"}
+    print(json.dumps(line), flush=True)
+    ctx.close()
+    return 0
+
+
+def reference_arm(args, rank, world, local):
+    if rank != 0:
+        return 0
+    from distcomp_b200 import synth
+    spec = synth.spec(CONFIG)
+    buf = build_model_gpu(spec, args.seed, local)
+    budget = max(30.0, min(240.0, 2.0 * args.steps))
+    v, n, thr, kind = cpu_reference_tokens_per_s(buf, spec, budget, max(1, args.steps))
+    line = {
+        "metric": METRIC, "value": round(v, 4), "unit": "tokens/s", "n_gpus": world, "steps": n,
+        "warmup": 1, "ms_per_step": round(1e3 / v, 2), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp32 (dequantised per block)", "impl": "reference",
+        "data": "synthetic: seeded N(0,0.02) weights quantised to Q4_0/Q8_0, random prompt",
+        "config": {"workload": "llama3-8b-shape Q4_0 decode, batch 1 (dim 4096, 32 layers, 32/8 heads, "
+                               "ffn 14336, vocab 128256, theta 5e5)"},
+        "cpu_baseline": {"value": round(v, 4), "unit": "tokens/s", "cores": thr, "kind": kind,
+                         "sample": f"{n} decode tokens (bounded to {budget:.0f} s) from position 1, "
+                                   "reference engine.c/gguf.c/thread.c compiled from its sources"},
+        "e2e": {"value": round(v, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if "WORLD_SIZE" not in os.environ:
+        world = 1 if args.gpus == 1 else args.gpus
+        if world > 1:
+            raise SystemExit("launch N>1 with torch.distributed.run (one process per GPU)")
+    if args.impl == "reference":
+        return reference_arm(args, rank, world, local)
+    return our_arm(args, rank, world, local)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -41,7 +41,7 @@ __device__ __forceinline__ void rope_pair(float &a, float &b, float c, float s)
 #define ATT_THREADS 128
 #define ATT_CHUNK 64      // positions scored per pass
 
-// HD = head_dim (32, 64 or 128), NREP = query heads per KV head.
+// HD = head_dim (16, 32, 64 or 128), NREP = query heads per KV head.
 template <int HD, int NREP>
 __global__ void __launch_bounds__(ATT_THREADS) k_attention(AttnArgs a)
 {

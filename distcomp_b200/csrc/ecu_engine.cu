@@ -35,11 +35,25 @@ static std::atomic<uint64_t> g_launches{0};
 
 // ------------------------------------------------------------ launching --
 
+// One timed launch of the profiling replay.
+struct ProfRec {
+    const char *kind;
+    double      bytes;
+    cudaEvent_t e0, e1;
+};
+
 struct Launcher {
     cudaStream_t stream = nullptr;
     bool         pdl = true;
     int          count = 0;       // kernels enqueued since the last reset
     cudaError_t  err = cudaSuccess;
+    // Profiling replay: events around every launch, tagged with the kind
+    // and algorithmic bytes the enqueue code sets just before the launch.
+    std::vector<ProfRec> *prof = nullptr;
+    const char *kind = "kernel";
+    double      bytes = 0;
+    // The first kernel of a sequence follows host copies, not a kernel, so
+    // it never gets a programmatic (early-start) dependency.
 
     template <typename... KArgs, typename... Args>
     void operator()(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, Args &&...args)
@@ -53,9 +67,21 @@ struct Launcher {
         attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
-        cfg.numAttrs = pdl ? 1 : 0;
+        cfg.numAttrs = (pdl && count > 0 && !prof) ? 1 : 0;
+        ProfRec r{kind, bytes, nullptr, nullptr};
+        if (prof) {
+            cudaEventCreate(&r.e0);
+            cudaEventCreate(&r.e1);
+            cudaEventRecord(r.e0, stream);
+        }
         cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
         if (e != cudaSuccess && err == cudaSuccess) err = e;
+        if (prof) {
+            cudaEventRecord(r.e1, stream);
+            prof->push_back(r);
+        }
+        kind = "kernel";
+        bytes = 0;
         count++;
     }
 };
@@ -78,6 +104,10 @@ static bool fast_ok(const DevMat &m)
            m.n_in / 1024 <= 31;
 }
 
+// Largest dynamic shared memory a fast-GEMV launch may ask for: the
+// opt-in per-block limit minus the kernel's own static shared memory.
+static size_t g_fast_smem_max = 0;
+
 template <int FMT, bool NORM, int EPI>
 static void fast_attr_once()
 {
@@ -86,8 +116,14 @@ static void fast_attr_once()
     cudaGetDevice(&dev);
     const uint64_t bit = 1ull << (dev & 63);
     if (!(done.load() & bit)) {
+        int optin = 0;
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        cudaFuncAttributes fa;
+        cudaFuncGetAttributes(&fa, k_gemv_fast<FMT, NORM, EPI>);
+        const size_t dyn = (size_t)optin - fa.sharedSizeBytes;
         cudaFuncSetAttribute(k_gemv_fast<FMT, NORM, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             227 * 1024);
+                             (int)dyn);
+        if (g_fast_smem_max == 0 || dyn < g_fast_smem_max) g_fast_smem_max = dyn;
         done |= bit;
     }
 }
@@ -125,6 +161,18 @@ static FastPlan plan_fast(const DevMat &m, int epi, int sms)
     return p;
 }
 
+static void fast_attrs_all()
+{
+    fast_attr_once<4, false, EPI_STORE>(); fast_attr_once<4, false, EPI_ADD>();
+    fast_attr_once<4, false, EPI_SWIGLU>(); fast_attr_once<4, false, EPI_ARGMAX>();
+    fast_attr_once<4, true, EPI_STORE>(); fast_attr_once<4, true, EPI_ADD>();
+    fast_attr_once<4, true, EPI_SWIGLU>(); fast_attr_once<4, true, EPI_ARGMAX>();
+    fast_attr_once<8, false, EPI_STORE>(); fast_attr_once<8, false, EPI_ADD>();
+    fast_attr_once<8, false, EPI_SWIGLU>(); fast_attr_once<8, false, EPI_ARGMAX>();
+    fast_attr_once<8, true, EPI_STORE>(); fast_attr_once<8, true, EPI_ADD>();
+    fast_attr_once<8, true, EPI_SWIGLU>(); fast_attr_once<8, true, EPI_ARGMAX>();
+}
+
 template <int FMT, bool NORM, int EPI>
 static void launch_fast_t(Launcher &L, const GemvArgs &a, const FastPlan &p)
 {
@@ -143,6 +191,14 @@ static void launch_fast_e(Launcher &L, const GemvArgs &a, const FastPlan &p, int
     }
 }
 
+// Algorithmic bytes of y = W x: W as stored in the file, x read, y written.
+static double gemv_bytes(const DevMat &m, int epi)
+{
+    const double w = m.zero ? 0.0 : (double)ecu_type_nbytes(m.type, (size_t)m.n_in * m.n_out);
+    const double y = epi == EPI_SWIGLU ? m.n_out / 2 : (epi == EPI_ADD ? 2.0 * m.n_out : m.n_out);
+    return w + 4.0 * m.n_in + 4.0 * y;
+}
+
 // Scratch a GEMV launch may need (argmax partials/counter, normed input).
 struct GemvScratch {
     float    *xn = nullptr;        // >= max n_in floats (generic-path RMSNorm)
@@ -157,6 +213,7 @@ struct GemvScratch {
 static void enqueue_gemv(Launcher &L, int sms, const DevMat &m, const float *x, const float *norm_w,
                          float eps, float *y, int epi, const GemvScratch &s, GemvArgs a)
 {
+    if (L.bytes == 0) L.bytes = gemv_bytes(m, epi);
     a.m = m;
     a.eps = eps;
     a.y = y;
@@ -164,8 +221,9 @@ static void enqueue_gemv(Launcher &L, int sms, const DevMat &m, const float *x, 
     a.part_idx = s.part_idx;
     a.counter = s.counter;
     a.status = s.status;
-    if (fast_ok(m) && (epi != EPI_SWIGLU || m.n_out % 2 == 0)) {
-        FastPlan p = plan_fast(m, epi, sms);
+    FastPlan p{};
+    if (fast_ok(m) && (epi != EPI_SWIGLU || m.n_out % 2 == 0)) p = plan_fast(m, epi, sms);
+    if (p.grid > 0 && p.grid <= 4096 && p.smem <= g_fast_smem_max) {
         a.x = x;
         a.norm_w = norm_w;
         a.rows_per_cta = p.rows_per_cta;
@@ -182,7 +240,13 @@ static void enqueue_gemv(Launcher &L, int sms, const DevMat &m, const float *x, 
     }
     const float *in = x;
     if (norm_w) {
+        const char *k = L.kind;
+        const double b = L.bytes;
+        L.kind = "rmsnorm";
+        L.bytes = 12.0 * m.n_in;
         L(k_rmsnorm, dim3(1), dim3(256), 0, x, norm_w, m.n_in, eps, s.xn);
+        L.kind = k;
+        L.bytes = b;
         in = s.xn;
     }
     a.x = in;
@@ -376,13 +440,18 @@ static void enqueue_layer(ecu_ctx *c, Launcher &L, int li)
 
     // (1) RMSNorm + Q/K/V projections
     if (ly.qkv.size() == 1) {
+        L.kind = "gemv_qkv";
         enqueue_gemv(L, c->sms, ly.qkv[0], c->state, ly.attn_norm, g.eps, c->qkv, EPI_STORE, c->scr, a);
     } else {
+        L.kind = "rmsnorm";
+        L.bytes = 12.0 * g.n_embd;
         L(k_rmsnorm, dim3(1), dim3(256), 0, (const float *)c->state, (const float *)ly.attn_norm,
           g.n_embd, g.eps, c->scr.xn);
-        for (size_t i = 0; i < ly.qkv.size(); i++)
+        for (size_t i = 0; i < ly.qkv.size(); i++) {
+            L.kind = "gemv_qkv";
             enqueue_gemv(L, c->sms, ly.qkv[i], c->scr.xn, nullptr, g.eps, c->qkv + ly.qkv_off[i],
                          EPI_STORE, c->scr, a);
+        }
     }
     // (2) bias + RoPE + KV append + attention
     AttnArgs aa;
@@ -405,28 +474,41 @@ static void enqueue_layer(ecu_ctx *c, Launcher &L, int li)
     aa.n_split = c->n_split;
     aa.kscale = 1.0f / sqrtf((float)hd);
     dim3 ag(g.n_head_kv, c->n_split);
+    L.kind = "attention";
+    // K and V rows of positions 0..pos read, one row of each written, q/att
+    L.bytes = 2.0 * 4.0 * kvdim * (c->pos + 2) + 8.0 * qdim + 4.0 * (qdim + 2 * kvdim);
 #define ATT_CASE(HD_, R_) \
     if (hd == HD_ && g.n_rep == R_) { L(k_attention<HD_, R_>, ag, dim3(ATT_THREADS), 0, aa); } else
     ATT_CASE(128, 1) ATT_CASE(128, 2) ATT_CASE(128, 4) ATT_CASE(128, 8)
     ATT_CASE(64, 1) ATT_CASE(64, 2) ATT_CASE(64, 4) ATT_CASE(64, 8)
-    ATT_CASE(32, 1) ATT_CASE(32, 2) ATT_CASE(32, 4) ATT_CASE(32, 8) {}
+    ATT_CASE(32, 1) ATT_CASE(32, 2) ATT_CASE(32, 4) ATT_CASE(32, 8)
+    ATT_CASE(16, 1) ATT_CASE(16, 2) ATT_CASE(16, 4) ATT_CASE(16, 8) {}
 #undef ATT_CASE
     (void)qdim;
     (void)kvdim;
     // (3) x += Wo * att
+    L.kind = "gemv_o";
     enqueue_gemv(L, c->sms, ly.o, c->att, nullptr, g.eps, c->state, EPI_ADD, c->scr, a);
     // (4) RMSNorm + gate/up + SwiGLU
     if (ly.gu_fused) {
+        L.kind = "gemv_gate_up";
         enqueue_gemv(L, c->sms, ly.gu, c->state, ly.ffn_norm, g.eps, c->h, EPI_SWIGLU, c->scr, a);
     } else {
+        L.kind = "rmsnorm";
+        L.bytes = 12.0 * g.n_embd;
         L(k_rmsnorm, dim3(1), dim3(256), 0, (const float *)c->state, (const float *)ly.ffn_norm,
           g.n_embd, g.eps, c->scr.xn);
+        L.kind = "gemv_gate";
         enqueue_gemv(L, c->sms, ly.g, c->scr.xn, nullptr, g.eps, c->gtmp, EPI_STORE, c->scr, a);
+        L.kind = "gemv_up";
         enqueue_gemv(L, c->sms, ly.u, c->scr.xn, nullptr, g.eps, c->utmp, EPI_STORE, c->scr, a);
+        L.kind = "swiglu";
+        L.bytes = 12.0 * g.n_ff;
         L(k_swiglu, dim3((g.n_ff + 255) / 256), dim3(256), 0, (const float *)c->gtmp,
           (const float *)c->utmp, c->h, g.n_ff);
     }
     // (5) x += Wd * h
+    L.kind = "gemv_down";
     enqueue_gemv(L, c->sms, ly.d, c->h, nullptr, g.eps, c->state, EPI_ADD, c->scr, a);
 }
 
@@ -434,6 +516,8 @@ static void enqueue_head(ecu_ctx *c, Launcher &L, bool advance)
 {
     const EcuGeom &g = c->g;
     // normed state in place: it is both HEAD's out[0..n_embd) and the GEMV input
+    L.kind = "rmsnorm";
+    L.bytes = 12.0 * g.n_embd;
     L(k_rmsnorm, dim3(1), dim3(256), 0, (const float *)c->state, (const float *)c->out_norm, g.n_embd,
       g.eps, c->state);
     GemvArgs a = {};
@@ -441,17 +525,24 @@ static void enqueue_head(ecu_ctx *c, Launcher &L, bool advance)
     a.tok_hist = c->tok_hist;
     a.tok_out = c->state + g.n_embd;
     a.advance_pos = advance ? 1 : 0;
+    L.kind = "gemv_head_argmax";
     enqueue_gemv(L, c->sms, c->out, c->state, nullptr, g.eps, c->logits, EPI_ARGMAX, c->scr, a);
 }
 
 // Kernels of one step of the stage: nl layers (LAYERS/FULL) from layer 0.
 static void enqueue_step(ecu_ctx *c, Launcher &L, int nl)
 {
-    if (c->stage == ECU_STAGE_EMBED || c->stage == ECU_STAGE_FULL)
+    if (c->stage == ECU_STAGE_EMBED || c->stage == ECU_STAGE_FULL) {
+        L.kind = "embed";
+        L.bytes = 8.0 * c->g.n_embd + (double)ecu_type_nbytes(c->emb.type, (size_t)c->g.n_embd);
         L(k_embed, dim3(8), dim3(256), 0, c->emb, (const StepState *)c->st, c->state, c->g.n_embd);
+    }
     if (c->stage == ECU_STAGE_LAYERS || c->stage == ECU_STAGE_FULL)
         for (int i = 0; i < nl; i++) enqueue_layer(c, L, i);
-    if (c->stage == ECU_STAGE_LAYERS) L(k_step_advance, dim3(1), dim3(32), 0, c->st);
+    if (c->stage == ECU_STAGE_LAYERS) {
+        L.kind = "step_advance";
+        L(k_step_advance, dim3(1), dim3(32), 0, c->st);
+    }
     if (c->stage == ECU_STAGE_HEAD || c->stage == ECU_STAGE_FULL)
         enqueue_head(c, L, c->stage == ECU_STAGE_FULL);
 }
@@ -507,6 +598,7 @@ static int check_status(ecu_ctx *c)
     CK(cudaMemcpy(&s, c->st, sizeof s, cudaMemcpyDeviceToHost));
     if (s.status) {
         ecu_set_error(nullptr, 0, "a kernel gave up on a bounded wait (status %d)", s.status);
+        CK(cudaMemset(&c->st->status, 0, sizeof(int)));
         return -1;
     }
     return 0;
@@ -659,7 +751,7 @@ static int check_shape(const EcuTensor *t, int n_in, int n_out, char *err, size_
 
 static int attn_supported(int hd, int rep)
 {
-    return (hd == 32 || hd == 64 || hd == 128) && (rep == 1 || rep == 2 || rep == 4 || rep == 8);
+    return (hd == 16 || hd == 32 || hd == 64 || hd == 128) && (rep == 1 || rep == 2 || rep == 4 || rep == 8);
 }
 
 size_t ecu_ctx_bytes(const ecu_model *m, int stage, int first, int last, int n_ctx)
@@ -690,8 +782,21 @@ size_t ecu_ctx_bytes(const ecu_model *m, int stage, int first, int last, int n_c
     return b;
 }
 
+static int ctx_open_impl(ecu_ctx **out, const ecu_model *m, int stage, int first, int last, int n_ctx,
+                         int device, char *err, size_t errlen);
+
 int ecu_ctx_open(ecu_ctx **out, const ecu_model *m, int stage, int first, int last, int n_ctx,
                  int device, char *err, size_t errlen)
+{
+    if (err && errlen) err[0] = '\0';
+    const int rc = ctx_open_impl(out, m, stage, first, last, n_ctx, device, err, errlen);
+    // CUDA failures deep in the upload only set the thread's last error
+    if (rc != 0 && err && errlen && !err[0]) snprintf(err, errlen, "%s", ecu_get_error());
+    return rc;
+}
+
+static int ctx_open_impl(ecu_ctx **out, const ecu_model *m, int stage, int first, int last, int n_ctx,
+                         int device, char *err, size_t errlen)
 {
     if (!out || !m) { ecu_set_error(err, errlen, "null argument"); return -1; }
     *out = nullptr;
@@ -730,6 +835,11 @@ int ecu_ctx_open(ecu_ctx **out, const ecu_model *m, int stage, int first, int la
         return -1;
     }
     if (cudaSetDevice(device) != cudaSuccess) { ecu_set_error(err, errlen, "cudaSetDevice(%d) failed", device); return -1; }
+    fast_attrs_all();
+    {
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) { ecu_set_error(err, errlen, "kernel attribute setup failed: %s", cudaGetErrorString(e)); return -1; }
+    }
 
     std::unique_ptr<ecu_ctx, void (*)(ecu_ctx *)> c(new ecu_ctx(), ctx_free);
     c->device = device;
@@ -907,7 +1017,9 @@ int ecu_ctx_open(ecu_ctx **out, const ecu_model *m, int stage, int first, int la
             if (!ly.attn_norm || !ly.ffn_norm) return fail_oom("norm weights");
         }
     }
-    if (cudaStreamSynchronize(c->stream) != cudaSuccess || cudaGetLastError() != cudaSuccess) {
+    // setup memsets/copies ran on the legacy stream, which does not order
+    // against the context's non-blocking stream: finish them all here
+    if (cudaDeviceSynchronize() != cudaSuccess || cudaGetLastError() != cudaSuccess) {
         ecu_set_error(err, errlen, "upload failed: %s", cudaGetErrorString(cudaGetLastError()));
         return -1;
     }
@@ -966,8 +1078,7 @@ static int enqueue_forward(ecu_ctx *c, int token)
     StepState *slot = c->h_st + (c->pos % c->n_hslots);
     slot->pos = c->pos;
     slot->token = token;
-    slot->status = 0;
-    CK(cudaMemcpyAsync(c->st, slot, sizeof(StepState), cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(c->st, slot, 2 * sizeof(int), cudaMemcpyHostToDevice, c->stream));
     if (run_step(c) != 0) return -1;
     if (c->stage == ECU_STAGE_LAYERS || c->stage == ECU_STAGE_FULL) c->pos++;
     if (c->stage == ECU_STAGE_HEAD || c->stage == ECU_STAGE_FULL) c->have_logits = true;
@@ -1023,8 +1134,7 @@ static int run_layers_eager(ecu_ctx *c, int from, int to, float *out)
     StepState *slot = c->h_st + (c->pos % c->n_hslots);
     slot->pos = c->pos;
     slot->token = 0;
-    slot->status = 0;
-    CK(cudaMemcpyAsync(c->st, slot, sizeof(StepState), cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(c->st, slot, 2 * sizeof(int), cudaMemcpyHostToDevice, c->stream));
     Launcher L{c->stream, c->pdl};
     for (int i = from; i < to; i++) enqueue_layer(c, L, i);
     g_launches += (uint64_t)L.count;
@@ -1131,6 +1241,43 @@ int ecu_generate(ecu_ctx *c, const int *prompt, int n_prompt, int n_gen, int *ou
     return 0;
 }
 
+int ecu_profile_steps(ecu_ctx *c, int n_steps, ecu_kprof *out, int max_kinds)
+{
+    if (!c || n_steps < 1 || !out || max_kinds < 1) return -1;
+    if (c->stage != ECU_STAGE_FULL && c->stage != ECU_STAGE_LAYERS) return -1;
+    if (c->pos + n_steps > c->g.n_ctx) { ecu_set_error(nullptr, 0, "context exhausted"); return -1; }
+    cudaSetDevice(c->device);
+    std::vector<ProfRec> recs;
+    for (int i = 0; i < n_steps; i++) {
+        Launcher L{c->stream, false};
+        L.prof = &recs;
+        enqueue_step(c, L, n_stage_layers(c));
+        g_launches += (uint64_t)L.count;
+        if (L.err != cudaSuccess) { ecu_set_error(nullptr, 0, "launch failed: %s", cudaGetErrorString(L.err)); return -1; }
+        c->pos++;
+    }
+    if (check_status(c) != 0) return -1;
+    int nk = 0;
+    for (auto &r : recs) {
+        float ms = 0;
+        cudaEventElapsedTime(&ms, r.e0, r.e1);
+        cudaEventDestroy(r.e0);
+        cudaEventDestroy(r.e1);
+        int k = 0;
+        while (k < nk && strncmp(out[k].kind, r.kind, sizeof out[k].kind) != 0) k++;
+        if (k == nk) {
+            if (nk == max_kinds) continue;
+            memset(&out[k], 0, sizeof out[k]);
+            snprintf(out[k].kind, sizeof out[k].kind, "%s", r.kind);
+            out[k].bytes_per_launch = r.bytes;
+            nk++;
+        }
+        out[k].launches++;
+        out[k].total_ms += ms;
+    }
+    return nk;
+}
+
 int ecu_dequant(unsigned type, const void *raw, size_t total, size_t off, size_t n, float *dst,
                 int device)
 {
@@ -1210,6 +1357,8 @@ int ecu_matvec(unsigned type, const void *w_raw, int n_in, int n_out, const floa
 {
     if (!w_raw || !x || !y || n_in <= 0 || n_out <= 0) return -1;
     CK(cudaSetDevice(device));
+    fast_attrs_all();
+    CK(cudaGetLastError());
     ecu_ctx tmp;               // borrow the allocator/stream helpers
     tmp.device = device;
     tmp.sms = num_sms(device);
@@ -1243,6 +1392,8 @@ int ecu_matvec(unsigned type, const void *w_raw, int n_in, int n_out, const floa
     s.status = tmp.dalloc<int>(4);
     if ((!m.zero && !m.data) || !stage || !dx || !dy || !s.xn) { ecu_set_error(nullptr, 0, "out of memory"); return -1; }
     cudaMemset(s.status, 0, 4 * sizeof(int));
+    cudaMemset(s.counter, 0, 4 * sizeof(unsigned));
+    CK(cudaDeviceSynchronize());     // legacy-stream memsets before the non-blocking stream
     if (!m.zero && t.nbytes && upload_rows(&tmp, &t, n_in, n_out, m, 0, 1, stage) != 0) return -1;
     CK(cudaMemcpy(dx, x, (size_t)n_in * sizeof(float), cudaMemcpyHostToDevice));
     Launcher L{tmp.stream, false};

@@ -44,6 +44,11 @@ class EcuInfo(C.Structure):
                                                      ("device_bytes", C.c_size_t)]
 
 
+class EcuKprof(C.Structure):
+    _fields_ = [("kind", C.c_char * 32), ("launches", C.c_int), ("total_ms", C.c_double),
+                ("bytes_per_launch", C.c_double)]
+
+
 # (name, restype, argtypes) of every symbol include/engine_cuda.h declares
 SIGNATURES = [
     ("ecu_model_open", C.c_int, [C.POINTER(C.c_void_p), C.c_void_p, C.c_size_t, C.c_char_p, C.c_size_t]),
@@ -78,6 +83,7 @@ SIGNATURES = [
     ("ecu_dequant", C.c_int, [C.c_uint, C.c_void_p, C.c_size_t, C.c_size_t, C.c_size_t, C.c_void_p, C.c_int]),
     ("ecu_dequant_tensor", C.c_int, [C.c_void_p, C.c_char_p, C.c_size_t, C.c_size_t, C.c_void_p]),
     ("ecu_matvec", C.c_int, [C.c_uint, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_int]),
+    ("ecu_profile_steps", C.c_int, [C.c_void_p, C.c_int, C.POINTER(EcuKprof), C.c_int]),
     ("ecu_last_error", C.c_char_p, []),
     ("ecu_kernel_launches", C.c_uint64, []),
     ("ecu_version", C.c_char_p, []),
@@ -163,7 +169,7 @@ class LlmCtx:
         err = C.create_string_buffer(512)
         rc = lib().ecu_ctx_open(C.byref(self.h), model.h, stage, first, last, n_ctx, device, err, 512)
         if rc != 0:
-            raise EngineError(err.value.decode(errors="replace"))
+            raise EngineError(err.value.decode(errors="replace") or last_error())
         i = EcuInfo()
         lib().ecu_ctx_info(self.h, C.byref(i))
         self.info = i
@@ -228,6 +234,16 @@ class LlmCtx:
 
     def stream(self) -> int:
         return int(lib().ecu_stream(self.h) or 0)
+
+    def profile_steps(self, n_steps: int) -> dict:
+        """{kind: (launches, total_ms, bytes_per_launch)} over n_steps eager
+        decode steps with CUDA events around every kernel."""
+        arr = (EcuKprof * 64)()
+        k = lib().ecu_profile_steps(self.h, int(n_steps), arr, 64)
+        if k < 0:
+            raise EngineError(last_error())
+        return {arr[i].kind.decode(): (arr[i].launches, arr[i].total_ms, arr[i].bytes_per_launch)
+                for i in range(k)}
 
     def dequant_tensor(self, name: str, off: int, n: int) -> np.ndarray:
         out = np.empty(n, dtype=np.float32)

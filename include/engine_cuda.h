@@ -146,6 +146,24 @@ int  ecu_dequant_tensor(ecu_ctx *c, const char *name, size_t off, size_t n, floa
 int  ecu_matvec(unsigned ggml_type, const void *w_raw, int n_in, int n_out, const float *x,
                 float *y, int device);
 
+/* ---- measurement --------------------------------------------------------- */
+
+/* Per-kernel-kind totals of a profiling replay. */
+typedef struct {
+    char   kind[32];          /* "gemv_gate_up", "attention", ...               */
+    int    launches;
+    double total_ms;          /* sum of CUDA-event durations of those launches  */
+    double bytes_per_launch;  /* algorithmic bytes: weights as stored in the
+                                 file + vectors read and written                 */
+} ecu_kprof;
+
+/* Run n_steps decode steps of a FULL (or LAYERS) context without the graph,
+ * with a pair of CUDA events around every kernel on the context's stream,
+ * and aggregate the durations per kernel kind into out[0..max_kinds).  The
+ * steps are real decode steps (the position advances).  Returns the number
+ * of kinds written, or -1. */
+int  ecu_profile_steps(ecu_ctx *c, int n_steps, ecu_kprof *out, int max_kinds);
+
 /* ---- misc -------------------------------------------------------------- */
 
 const char *ecu_last_error(void);

@@ -27,6 +27,19 @@ def _has_gpu() -> bool:
 HAS_GPU = _has_gpu()
 
 
+def bits_equal(a, b) -> bool:
+    """Bit-for-bit equality of two float32 arrays, except that any NaN
+    matches any NaN: x86 SSE propagates an operand's NaN payload through
+    a product, the GPU returns its canonical NaN, and the reference's
+    decoder does produce NaNs for NaN/inf fp16 scales."""
+    a = np.asarray(a, dtype=np.float32)
+    b = np.asarray(b, dtype=np.float32)
+    if a.shape != b.shape:
+        return False
+    same = a.view(np.uint32) == b.view(np.uint32)
+    return bool(np.all(same | (np.isnan(a) & np.isnan(b))))
+
+
 def pytest_collection_modifyitems(config, items):
     if HAS_GPU:
         return

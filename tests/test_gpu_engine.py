@@ -5,6 +5,7 @@ position / error contract of llm_forward, and the repacked device copy of
 every weight bit-exact with the file."""
 import numpy as np
 import pytest
+from conftest import bits_equal
 
 from distcomp_b200 import gguf as G
 from distcomp_b200 import synth
@@ -198,4 +199,4 @@ def test_repacked_weights_bit_exact(eng, oracle_port, model_buf):
             got = c.dequant_tensor(name, 0, total)
             rc, want = oracle_port.dequant(gt, np.frombuffer(tab[name][2], np.uint8), total, 0, total)
             assert rc == 0
-            assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), name
+            assert bits_equal(got, want), name

@@ -3,6 +3,7 @@ block dequant bit-exact for every format, the quantised matvec within the
 GEMV tolerance on every format and on the microbenchmark shapes."""
 import numpy as np
 import pytest
+from conftest import bits_equal
 
 from distcomp_b200 import gguf as G
 
@@ -20,7 +21,7 @@ def test_dequant_fixture_blocks_bit_exact(eng, golden):
         total, n = (int(v) for v in d[f"n_{t}"])
         rc, got = eng.dequant(t, d[f"raw_{t}"], total, 0, n)
         assert rc == 0, t
-        assert np.array_equal(got.view(np.uint32), d[f"out_{t}"].view(np.uint32)), f"type {t}"
+        assert bits_equal(got, d[f"out_{t}"]), f"type {t}"
 
 
 @pytest.mark.parametrize("t", ALL_TYPES)
@@ -39,7 +40,7 @@ def test_dequant_ranges_bit_exact(eng, oracle_port, t):
         r1, a = eng.dequant(t, raw, total, off, n)
         r2, b = oracle_port.dequant(t, raw, total, off, n)
         assert r1 == r2 == 0
-        assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), (t, off, n)
+        assert bits_equal(a, b), (t, off, n)
 
 
 def test_dequant_rejects_like_reference(eng):
@@ -51,9 +52,15 @@ def test_dequant_rejects_like_reference(eng):
 
 
 def gemv_tol_ok(y, ref64, w_norms, x):
-    """|y - ref| <= 1e-4 * (|ref| + 1e-4 * ||w_o|| * ||x||): relative where
-    the row sum is large, absolute on the scale of the row where it cancels."""
-    bound = 1e-4 * (np.abs(ref64) + 1e-4 * w_norms * np.linalg.norm(x.astype(np.float64)))
+    """|y - ref| <= 1e-4 * |ref| + 1e-6 * ||w_o|| * ||x||, ref in double.
+
+    Relative 1e-4 where the row sum is large; where it cancels, an absolute
+    floor on the scale of the row (Cauchy-Schwarz bound).  The reference's
+    own sequential fp32 matvec is off by up to ~1.6e-7 * ||w_o|| * ||x||
+    (16% relative on cancelling rows) on these shapes, so the floor is set a
+    few times above that, and every test checks the reference's fp32 result
+    against the same bound."""
+    bound = 1e-4 * np.abs(ref64) + 1e-6 * w_norms * np.linalg.norm(x.astype(np.float64))
     err = np.abs(y.astype(np.float64) - ref64)
     return bool(np.all(err <= bound)), float(np.max(err / (np.abs(ref64) + 1e-30)))
 
@@ -131,8 +138,10 @@ def test_matvec_microbench_shapes(eng, oracle_port, t, n_out, n_in):
     x = rng.standard_normal(n_in).astype(np.float32)
     y = eng.matvec(t, raw, n_in, n_out, x)
     ref = oracle_port.matvec_f64(t, raw, n_in, n_out, x)
-    ok, worst = gemv_tol_ok(y, ref, row_norms(oracle_port, t, raw, n_in, n_out), x)
+    wn = row_norms(oracle_port, t, raw, n_in, n_out)
+    ok, worst = gemv_tol_ok(y, ref, wn, x)
     assert ok, f"worst rel {worst:.3e}"
+    assert gemv_tol_ok(oracle_port.matvec(t, raw, n_in, n_out, x), ref, wn, x)[0]
 
 
 def test_matvec_extreme_inputs(eng, oracle_port):

@@ -92,7 +92,7 @@ __device__ __forceinline__ ArgBest arg_better(ArgBest a, ArgBest b)
 }
 
 // Block-wide argmax of (v, i) pairs; every thread of the block calls it.
-__device__ ArgBest block_argmax(ArgBest mine, ArgBest *sh)
+static __device__ ArgBest block_argmax(ArgBest mine, ArgBest *sh)
 {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -115,7 +115,7 @@ __device__ ArgBest block_argmax(ArgBest mine, ArgBest *sh)
 }
 
 // Per-CTA partial -> last CTA reduces all partials in CTA order and publishes.
-__device__ void argmax_finish(const GemvArgs &a, ArgBest cta_best, ArgBest *sh)
+static __device__ void argmax_finish(const GemvArgs &a, ArgBest cta_best, ArgBest *sh)
 {
     __shared__ unsigned s_last;
     if (threadIdx.x == 0) {
@@ -201,7 +201,7 @@ __global__ void __launch_bounds__(256) k_gemv_generic(GemvArgs a)
 
 // Standalone RMSNorm (generic path and HEAD's normed-state output):
 // out[i] = x[i] * scale * w[i], single CTA.
-__global__ void __launch_bounds__(256) k_rmsnorm(const float *x, const float *w, int n,
+static __global__ void __launch_bounds__(256) k_rmsnorm(const float *x, const float *w, int n,
                                                  float eps, float *out)
 {
     pdl_wait();
@@ -212,7 +212,7 @@ __global__ void __launch_bounds__(256) k_rmsnorm(const float *x, const float *w,
 }
 
 // h[j] = silu(g[j]) * u[j] for the unfused gate/up path.
-__global__ void k_swiglu(const float *g, const float *u, float *h, int n)
+static __global__ void k_swiglu(const float *g, const float *u, float *h, int n)
 {
     pdl_wait();
     pdl_trigger();

@@ -6,7 +6,7 @@
 // out[i] = element token*n + i of the embedding tensor (src/engine.c:472-484:
 // row_to_float(t, out, token*ne, ne)).  The token comes from device state so
 // that a graph replay picks up the argmax of the previous step.
-__global__ void k_embed(DevMat emb, const StepState *st, float *out, int n)
+static __global__ void k_embed(DevMat emb, const StepState *st, float *out, int n)
 {
     pdl_wait();
     pdl_trigger();
@@ -18,7 +18,7 @@ __global__ void k_embed(DevMat emb, const StepState *st, float *out, int n)
 }
 
 // dst[e] = element off+e of a raw GGUF block stream of type t (bit-exact).
-__global__ void k_dequant_raw(int t, const uint8_t *raw, size_t off, size_t n, float *dst)
+static __global__ void k_dequant_raw(int t, const uint8_t *raw, size_t off, size_t n, float *dst)
 {
     const size_t stride = (size_t)gridDim.x * blockDim.x;
     for (size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += stride) {
@@ -39,7 +39,7 @@ __global__ void k_dequant_raw(int t, const uint8_t *raw, size_t off, size_t n, f
 // dst[e] = element off+e of a device matrix, read back through its layout;
 // `row_map` lets fused matrices expose one source tensor: source row r lives
 // at device row row0 + r*rstride.
-__global__ void k_dequant_mat(DevMat m, int row0, int rstride, int n_in, size_t off, size_t n,
+static __global__ void k_dequant_mat(DevMat m, int row0, int rstride, int n_in, size_t off, size_t n,
                               float *dst)
 {
     const size_t stride = (size_t)gridDim.x * blockDim.x;
@@ -52,7 +52,7 @@ __global__ void k_dequant_mat(DevMat m, int row0, int rstride, int n_in, size_t 
 
 // Q4_0 rows (18-byte blocks) -> SPLIT4 rows.  Source row r goes to device
 // row row0 + r*rstride.  One thread per block.
-__global__ void k_repack_q4_0(const uint8_t *src, int nb, int n_rows, uint8_t *dst,
+static __global__ void k_repack_q4_0(const uint8_t *src, int nb, int n_rows, uint8_t *dst,
                               size_t dst_row_bytes, int row0, int rstride)
 {
     const size_t total = (size_t)nb * n_rows;
@@ -68,7 +68,7 @@ __global__ void k_repack_q4_0(const uint8_t *src, int nb, int n_rows, uint8_t *d
 }
 
 // Q8_0 rows (34-byte blocks) -> SPLIT8 rows.
-__global__ void k_repack_q8_0(const uint8_t *src, int nb, int n_rows, uint8_t *dst,
+static __global__ void k_repack_q8_0(const uint8_t *src, int nb, int n_rows, uint8_t *dst,
                               size_t dst_row_bytes, int row0, int rstride)
 {
     const size_t total = (size_t)nb * n_rows;
@@ -87,7 +87,7 @@ __global__ void k_repack_q8_0(const uint8_t *src, int nb, int n_rows, uint8_t *d
 }
 
 // Raw rows copied to device row row0 + r*rstride (formats kept as is).
-__global__ void k_copy_rows(const uint8_t *src, size_t src_row_bytes, int n_rows, uint8_t *dst,
+static __global__ void k_copy_rows(const uint8_t *src, size_t src_row_bytes, int n_rows, uint8_t *dst,
                             size_t dst_row_bytes, int row0, int rstride)
 {
     const size_t total = src_row_bytes * (size_t)n_rows;
@@ -99,7 +99,7 @@ __global__ void k_copy_rows(const uint8_t *src, size_t src_row_bytes, int n_rows
 }
 
 // LAYERS-only stages advance the position at the end of a step.
-__global__ void k_step_advance(StepState *st)
+static __global__ void k_step_advance(StepState *st)
 {
     pdl_wait();
     pdl_trigger();

@@ -83,6 +83,8 @@ SIGNATURES = [
     ("ecu_dequant", C.c_int, [C.c_uint, C.c_void_p, C.c_size_t, C.c_size_t, C.c_size_t, C.c_void_p, C.c_int]),
     ("ecu_dequant_tensor", C.c_int, [C.c_void_p, C.c_char_p, C.c_size_t, C.c_size_t, C.c_void_p]),
     ("ecu_matvec", C.c_int, [C.c_uint, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_int]),
+    ("ecu_matvec_argmax_noalloc", C.c_int, [C.c_uint, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
+                                            C.c_void_p, C.c_void_p]),
     ("ecu_profile_steps", C.c_int, [C.c_void_p, C.c_int, C.POINTER(EcuKprof), C.c_int]),
     ("ecu_last_error", C.c_char_p, []),
     ("ecu_kernel_launches", C.c_uint64, []),

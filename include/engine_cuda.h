@@ -146,6 +146,24 @@ int  ecu_dequant_tensor(ecu_ctx *c, const char *name, size_t off, size_t n, floa
 int  ecu_matvec(unsigned ggml_type, const void *w_raw, int n_in, int n_out, const float *x,
                 float *y, int device);
 
+/* ---- without device allocation ------------------------------------------ */
+
+/* y = W x over raw GGUF blocks already in device memory (n_out rows of
+ * n_in inputs, the file's block order), and *d_token = the first maximum of
+ * y with llm_pick's rules, enqueued on `stream` (NULL = the legacy default
+ * stream) without synchronising.  All pointers are device pointers the
+ * caller owns.  No counterpart in the reference: it is for callers that
+ * cannot allocate device memory -- a shard node held to a fixed memory
+ * budget, a host that hands out device memory from its own pool, a loop
+ * that cannot take cudaMalloc's device synchronisation.  It allocates
+ * nothing: its scratch is one fixed 16 KiB array inside the library, which
+ * limits n_out to 524288 rows (more returns -1 with a message).  The first
+ * call on a device looks that array up with cudaGetSymbolAddress; make it
+ * before any stream capture.  Every call shares the array, so calls that
+ * may overlap on the GPU (two streams, two threads) race: serialise them. */
+int  ecu_matvec_argmax_noalloc(unsigned ggml_type, const void *d_w, int n_in, int n_out,
+                               const float *d_x, float *d_y, int *d_token, void *stream);
+
 /* ---- measurement --------------------------------------------------------- */
 
 /* Per-kernel-kind totals of a profiling replay. */

@@ -52,6 +52,8 @@ def parse():
     ap.add_argument("--cpu-sample-s", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--layers", type=int, default=0,
+                    help="override n_layer (reduced-depth runs for profiler captures; not a bench line)")
     return ap.parse_args()
 
 
@@ -192,7 +194,7 @@ def our_arm(args, rank, world, local):
         from distcomp_b200 import pipeline
         return pipeline.bench_main(args, rank, world, local)
 
-    spec = synth.spec(CONFIG)
+    spec = synth.spec(CONFIG, **({"n_layer": args.layers} if args.layers else {}))
     t_build = time.perf_counter()
     buf = build_model_gpu(spec, args.seed, local)
     t_build = time.perf_counter() - t_build

@@ -161,6 +161,21 @@ static FastPlan plan_fast(const DevMat &m, int epi, int sms)
     return p;
 }
 
+template <int HD, int R>
+static void attn_attr()
+{
+    cudaFuncSetAttribute(k_attention<HD, R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)attn_smem_bytes<HD>());
+}
+
+static void attn_attrs_all()
+{
+    attn_attr<128, 1>(); attn_attr<128, 2>(); attn_attr<128, 4>(); attn_attr<128, 8>();
+    attn_attr<64, 1>(); attn_attr<64, 2>(); attn_attr<64, 4>(); attn_attr<64, 8>();
+    attn_attr<32, 1>(); attn_attr<32, 2>(); attn_attr<32, 4>(); attn_attr<32, 8>();
+    attn_attr<16, 1>(); attn_attr<16, 2>(); attn_attr<16, 4>(); attn_attr<16, 8>();
+}
+
 static void fast_attrs_all()
 {
     fast_attr_once<4, false, EPI_STORE>(); fast_attr_once<4, false, EPI_ADD>();
@@ -467,6 +482,7 @@ static void enqueue_layer(ecu_ctx *c, Launcher &L, int li)
     aa.part = c->attn_part;
     aa.counter = c->attn_cnt;
     aa.st = c->st;
+    aa.status = &c->st->status;
     aa.n_head = g.n_head;
     aa.n_kv = g.n_head_kv;
     aa.n_rep = g.n_rep;
@@ -478,7 +494,7 @@ static void enqueue_layer(ecu_ctx *c, Launcher &L, int li)
     // K and V rows of positions 0..pos read, one row of each written, q/att
     L.bytes = 2.0 * 4.0 * kvdim * (c->pos + 2) + 8.0 * qdim + 4.0 * (qdim + 2 * kvdim);
 #define ATT_CASE(HD_, R_) \
-    if (hd == HD_ && g.n_rep == R_) { L(k_attention<HD_, R_>, ag, dim3(ATT_THREADS), 0, aa); } else
+    if (hd == HD_ && g.n_rep == R_) { L(k_attention<HD_, R_>, ag, dim3(ATT_THREADS), attn_smem_bytes<HD_>(), aa); } else
     ATT_CASE(128, 1) ATT_CASE(128, 2) ATT_CASE(128, 4) ATT_CASE(128, 8)
     ATT_CASE(64, 1) ATT_CASE(64, 2) ATT_CASE(64, 4) ATT_CASE(64, 8)
     ATT_CASE(32, 1) ATT_CASE(32, 2) ATT_CASE(32, 4) ATT_CASE(32, 8)
@@ -836,6 +852,7 @@ static int ctx_open_impl(ecu_ctx **out, const ecu_model *m, int stage, int first
     }
     if (cudaSetDevice(device) != cudaSuccess) { ecu_set_error(err, errlen, "cudaSetDevice(%d) failed", device); return -1; }
     fast_attrs_all();
+    attn_attrs_all();
     {
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) { ecu_set_error(err, errlen, "kernel attribute setup failed: %s", cudaGetErrorString(e)); return -1; }
@@ -922,8 +939,14 @@ static int ctx_open_impl(ecu_ctx **out, const ecu_model *m, int stage, int first
         const size_t plane = (size_t)g.n_head_kv * g.n_ctx * hd;
         c->kc = c->dalloc<float>(plane * nl);
         c->vc = c->dalloc<float>(plane * nl);
-        c->n_split = (2 * c->sms + g.n_head_kv - 1) / g.n_head_kv;
+        // about one CTA per SM; the merge reuses the K/V staging buffers,
+        // which bounds n_split*n_rep*(hd+2) by 2*2*ATT_SUB*hd floats
+        c->n_split = c->sms / g.n_head_kv;
+        const int cap = (4 * ATT_SUB * hd) / (g.n_rep * (hd + 2));
+        if (c->n_split > cap) c->n_split = cap;
+        if (c->n_split > ATT_MAX_SPLIT) c->n_split = ATT_MAX_SPLIT;
         if (c->n_split > g.n_ctx) c->n_split = g.n_ctx;
+        if (c->n_split < 1) c->n_split = 1;
         c->attn_part = c->dalloc<float>((size_t)g.n_head_kv * c->n_split * g.n_rep * (hd + 2));
         c->attn_cnt = c->dalloc<unsigned>((size_t)g.n_head_kv);
         c->rope_cs = c->dalloc<float>((size_t)g.n_ctx * hd);

@@ -51,18 +51,43 @@ struct GemvArgs {
 
 // ---------------------------------------------------------------- RMSNorm --
 // 1/sqrt(mean(x^2)+eps) with the sum of squares in double (src/engine.c:258-
-// 260).  The double sum runs over 256 fixed strided partials combined by a
+// 260).  The double sum runs over 256 fixed partials -- partial v covers the
+// contiguous segment [v*seg, (v+1)*seg), seg = ceil(n/256) -- combined by a
 // fixed tree, so every kernel that calls this gets the same bits whatever its
-// block size.  Threads [0, nthreads) must all call it; `bar` synchronises them.
+// block size.  Each partial's loads are independent (one memory round trip).
+// Threads [0, nthreads) must all call it; `bar` synchronises them.
 template <class Bar>
 __device__ float rms_scale(const float *x, int n, float eps, double *dsum, int tid,
                            int nthreads, Bar bar)
 {
+    const int seg = (n + 255) / 256;
     for (int v = tid; v < 256; v += nthreads) {
+        const int lo = min(n, v * seg), hi = min(n, lo + seg);
         double p = 0.0;
-        for (int i = v; i < n; i += 256) {
-            double xv = (double)x[i];
-            p += xv * xv;
+        if (seg % 4 == 0 && hi - lo == seg) {
+            const float4 *x4 = reinterpret_cast<const float4 *>(x + lo);
+            float4 buf[8];
+            const int nq = seg / 4;
+            for (int base = 0; base < nq; base += 8) {
+                const int m = min(8, nq - base);
+#pragma unroll
+                for (int k = 0; k < 8; k++)
+                    if (k < m) buf[k] = x4[base + k];
+#pragma unroll
+                for (int k = 0; k < 8; k++)
+                    if (k < m) {
+                        const double a = buf[k].x, b = buf[k].y, c = buf[k].z, d = buf[k].w;
+                        p += a * a;
+                        p += b * b;
+                        p += c * c;
+                        p += d * d;
+                    }
+            }
+        } else {
+            for (int i = lo; i < hi; i++) {
+                const double xv = (double)x[i];
+                p += xv * xv;
+            }
         }
         dsum[v] = p;
     }

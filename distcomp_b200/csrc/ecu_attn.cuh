@@ -9,16 +9,21 @@
 // the current position were written by earlier steps).  The CTA ropes the
 // n_rep query heads of the group once, scores its slice against each of them
 // (each K row read once for the whole group), and keeps an exact-max softmax
-// partial (m, l, acc) per query head.  The last CTA of a head to finish
-// (atomic ticket, no waiting) merges the partials in split order, so results
-// are deterministic.  CTA (g, 0) writes the roped K row and the raw V row of
-// the current position into the cache; the CTA whose slice holds the current
-// position uses its own copy, so no CTA reads a row another CTA writes.
+// partial (m, l, acc) per query head in shared memory.  The n_split CTAs of a
+// head form one thread-block cluster; each pushes its partial into rank 0's
+// shared memory (distributed shared memory stores), and after a cluster
+// barrier rank 0 merges them in split order (deterministic).  CTA
+// (g, 0) writes the roped K row and the raw V row of the current position
+// into the cache; the CTA whose slice holds the current position uses its own
+// copy, so no CTA reads a row another CTA writes.
 //
 // Cache layout: [layer][kv head][n_ctx][head_dim] fp32.
 #pragma once
 #include "ecu_common.cuh"
 #include "ecu_pipe.cuh"
+
+#include <cooperative_groups.h>
+namespace cg = cooperative_groups;
 
 struct AttnArgs {
     const float *qkv;        // q [n_head*hd] | k [nkv*hd] | v [nkv*hd], pre-bias, pre-RoPE
@@ -26,8 +31,6 @@ struct AttnArgs {
     const float *rope_cs;    // [n_ctx][hd/2][2] cos, sin
     float       *kc, *vc;    // this layer's cache, [nkv][n_ctx][hd]
     float       *att;        // out [n_head*hd]
-    float       *part;       // scratch [nkv][n_split][n_rep][hd + 2]
-    unsigned    *counter;    // [nkv], zero between launches
     const StepState *st;
     int         *status;
     int          n_head, n_kv, n_rep, n_ctx, n_split;
@@ -44,33 +47,55 @@ __device__ __forceinline__ void rope_pair(float &a, float &b, float c, float s)
 }
 
 #define ATT_THREADS 128
-#define ATT_SUB 32        // positions per shared-memory buffer
-#define ATT_MAX_SPLIT 64
+#define ATT_SUB 32        // positions per shared-memory buffer (one per lane)
+#define ATT_MAX_SPLIT 16  // one cluster per KV head
+
+// K/V rows sit in shared memory with a 16-byte pad, so that the 32 lanes of
+// a warp reading the same column of 32 different rows hit distinct banks.
+template <int HD>
+__host__ __device__ constexpr int attn_row_stride()
+{
+    return HD + 4;
+}
 
 template <int HD>
 __host__ __device__ constexpr size_t attn_smem_bytes()
 {
-    return (size_t)2 * 2 * ATT_SUB * HD * sizeof(float);   // 2 buffers x (K, V)
+    return (size_t)2 * 2 * ATT_SUB * attn_row_stride<HD>() * sizeof(float);   // 2 buffers x (K, V)
+}
+
+__device__ __forceinline__ float warp_max(float v)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
 }
 
 // HD = head_dim (16, 32, 64 or 128), NREP = query heads per KV head.
-// Needs n_split <= ATT_MAX_SPLIT and n_split*NREP*(HD+2) floats to fit the
-// K/V buffers (the merge reuses them); the host planner guarantees both.
+// Launched with clusters of n_split CTAs along y (one cluster per KV head):
+// the split partials meet in rank 0's shared memory.
+// Work split inside a CTA: warp w owns query heads w, w+4, ...; for scores a
+// lane owns a position, for the V accumulation a lane owns 4 dimensions.
 template <int HD, int NREP>
 __global__ void __launch_bounds__(ATT_THREADS) k_attention(AttnArgs a)
 {
-    constexpr int LPP = HD / 4;              // lanes per position (float4 each)
-    constexpr int PPW = 32 / LPP;            // positions per warp pass
     constexpr int NW = ATT_THREADS / 32;
-    extern __shared__ __align__(128) float kvbuf[];   // [2][K|V][ATT_SUB][HD]
+    constexpr int RS = attn_row_stride<HD>();
+    constexpr int LPR = HD / 4;                 // lanes per V row (float4 each)
+    constexpr int RPW = 32 / LPR;               // V rows per warp pass
+    constexpr int HPW = (NREP + NW - 1) / NW;   // query heads per warp
+    extern __shared__ __align__(128) float kvbuf[];   // [2][K|V][ATT_SUB][RS]
     __shared__ __align__(16) float q_s[NREP][HD];
     __shared__ __align__(16) float knew[HD], vnew[HD];
-    __shared__ float sc[NREP][ATT_SUB];
-    __shared__ __align__(16) float acc_s[NW][NREP][HD];
+    __shared__ float cs_s[HD];
+    // this CTA's (acc[HD], m, l) per head; rows padded to a 16-byte multiple
+    // for the float4 stores
+    __shared__ __align__(16) float part_s[NREP][HD + 4];
     __shared__ float wsplit[NREP][ATT_MAX_SPLIT];
+    __shared__ float invl[NREP];
     __shared__ __align__(8) uint64_t bar[2];
-    __shared__ unsigned s_last;
 
+    cg::cluster_group cluster = cg::this_cluster();
     const int g = blockIdx.x, split = blockIdx.y;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     // the position is stable for the whole step (set before the graph runs)
@@ -81,27 +106,33 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(AttnArgs a)
     float *kbase = a.kc + (size_t)g * a.n_ctx * HD;
     float *vbase = a.vc + (size_t)g * a.n_ctx * HD;
 
-    // rows [c0, c0+ATT_SUB) of the slice that lie below the current position
+    // rows [c0, c0+ATT_SUB) of the slice below the current position, one row
+    // per lane of warp 0, into padded rows; lane 0 first announces the bytes
     auto issue = [&](int sb) {
         const int c0 = t0 + sb * ATT_SUB;
         const int c1 = min(min(t1, c0 + ATT_SUB), pos);
-        const uint32_t bytes = c1 > c0 ? (uint32_t)((c1 - c0) * HD * sizeof(float)) : 0u;
-        float *kb = kvbuf + (size_t)(sb & 1) * 2 * ATT_SUB * HD;
-        mbar_expect_tx(&bar[sb & 1], 2 * bytes);
-        if (bytes) {
-            bulk_g2s(kb, kbase + (size_t)c0 * HD, bytes, &bar[sb & 1]);
-            bulk_g2s(kb + ATT_SUB * HD, vbase + (size_t)c0 * HD, bytes, &bar[sb & 1]);
+        const int nr = c1 > c0 ? c1 - c0 : 0;
+        float *kb = kvbuf + (size_t)(sb & 1) * 2 * ATT_SUB * RS;
+        if (lane == 0) mbar_expect_tx(&bar[sb & 1], (uint32_t)(2 * nr * HD * sizeof(float)));
+        __syncwarp();
+        if (lane < nr) {
+            bulk_g2s(kb + lane * RS, kbase + (size_t)(c0 + lane) * HD, HD * sizeof(float), &bar[sb & 1]);
+            bulk_g2s(kb + ATT_SUB * RS + lane * RS, vbase + (size_t)(c0 + lane) * HD, HD * sizeof(float),
+                     &bar[sb & 1]);
         }
     };
     if (tid == 0) {
         mbar_init(&bar[0], 1);
         mbar_init(&bar[1], 1);
         mbar_init_fence();
-        if (nsub > 0) issue(0);
     }
+    __syncthreads();
+    if (warp == 0 && nsub > 0) issue(0);
+    // the RoPE row depends only on the position: fetch it before waiting
+    for (int j = tid; j < HD; j += ATT_THREADS) cs_s[j] = a.rope_cs[(size_t)pos * HD + j];
     pdl_wait();
     pdl_trigger();
-    const float *cs = a.rope_cs + (size_t)pos * HD;   // HD/2 (cos, sin) pairs
+    __syncthreads();
     const int qdim = a.n_head * HD, kvdim = a.n_kv * HD;
 
     // queries of this group, biased and roped; the new K (roped) and V
@@ -109,7 +140,7 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(AttnArgs a)
         const int h = i / (HD / 2), j = i % (HD / 2), row = (g * NREP + h) * HD;
         float x0 = a.qkv[row + j], x1 = a.qkv[row + j + HD / 2];
         if (a.bq) { x0 = __fadd_rn(x0, a.bq[row + j]); x1 = __fadd_rn(x1, a.bq[row + j + HD / 2]); }
-        rope_pair(x0, x1, cs[2 * j], cs[2 * j + 1]);
+        rope_pair(x0, x1, cs_s[2 * j], cs_s[2 * j + 1]);
         q_s[h][j] = x0;
         q_s[h][j + HD / 2] = x1;
     }
@@ -119,7 +150,7 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(AttnArgs a)
         float v0 = a.qkv[vr + j], v1 = a.qkv[vr + j + HD / 2];
         if (a.bk) { k0 = __fadd_rn(k0, a.bk[g * HD + j]); k1 = __fadd_rn(k1, a.bk[g * HD + j + HD / 2]); }
         if (a.bv) { v0 = __fadd_rn(v0, a.bv[g * HD + j]); v1 = __fadd_rn(v1, a.bv[g * HD + j + HD / 2]); }
-        rope_pair(k0, k1, cs[2 * j], cs[2 * j + 1]);
+        rope_pair(k0, k1, cs_s[2 * j], cs_s[2 * j + 1]);
         knew[j] = k0; knew[j + HD / 2] = k1;
         vnew[j] = v0; vnew[j + HD / 2] = v1;
     }
@@ -130,128 +161,119 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(AttnArgs a)
             vbase[(size_t)pos * HD + j] = vnew[j];
         }
 
-    float  m_run[NREP], l_run[NREP];
-    float4 acc[NREP];     // dims [4*(lane%LPP), +4) of this lane's positions
+    // running softmax state of this warp's heads (identical in all lanes)
+    float  m_run[HPW], l_run[HPW];
+    float4 acc[HPW];      // dims [4*(lane%LPR), +4) over this lane's V rows
 #pragma unroll
-    for (int h = 0; h < NREP; h++) {
-        m_run[h] = -INFINITY;
-        l_run[h] = 0.0f;
-        acc[h] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k = 0; k < HPW; k++) {
+        m_run[k] = -INFINITY;
+        l_run[k] = 0.0f;
+        acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    const int sub_slot = lane / LPP, dl = lane % LPP;
     for (int sb = 0; sb < nsub; sb++) {
-        if (tid == 0 && sb + 1 < nsub) issue(sb + 1);   // that buffer was released below
+        if (warp == 0 && sb + 1 < nsub) issue(sb + 1);   // that buffer was released below
         // on a timeout the status word is set and the stale buffer is used;
-        // the step's result is then reported as an error by the host
+        // the host then reports the step as failed
         mbar_wait(&bar[sb & 1], (sb >> 1) & 1, a.status);
-        const float *kb = kvbuf + (size_t)(sb & 1) * 2 * ATT_SUB * HD;
-        const float *vb = kb + ATT_SUB * HD;
+        const float *kb = kvbuf + (size_t)(sb & 1) * 2 * ATT_SUB * RS;
+        const float *vb = kb + ATT_SUB * RS;
         const int    c0 = t0 + sb * ATT_SUB, cn = min(ATT_SUB, t1 - c0);
-        // scores: warp w handles positions w*PPW + sub_slot, stride NW*PPW
-        for (int p = warp * PPW + sub_slot; p < ((cn + PPW - 1) / PPW) * PPW; p += NW * PPW) {
-            const bool   ok = p < cn;
-            const int    pp = ok ? p : 0;
-            const float4 kv = (c0 + pp == pos) ? reinterpret_cast<const float4 *>(knew)[dl]
-                                               : reinterpret_cast<const float4 *>(kb + pp * HD)[dl];
+        const float *krow = (c0 + lane == pos) ? knew : kb + lane * RS;
 #pragma unroll
-            for (int h = 0; h < NREP; h++) {
-                const float4 qv = reinterpret_cast<const float4 *>(q_s[h])[dl];
-                float d = qv.x * kv.x;
-                d = fmaf(qv.y, kv.y, d);
-                d = fmaf(qv.z, kv.z, d);
-                d = fmaf(qv.w, kv.w, d);
-#pragma unroll
-                for (int o = LPP / 2; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-                if (ok && dl == 0) sc[h][p] = d * a.kscale;
+        for (int k = 0; k < HPW; k++) {
+            const int h = warp + k * NW;
+            if (h >= NREP) break;
+            // score of position c0 + lane against head h
+            float s = -INFINITY;
+            if (lane < cn) {
+                const float4 *k4 = reinterpret_cast<const float4 *>(krow);
+                const float4 *q4 = reinterpret_cast<const float4 *>(q_s[h]);
+                float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
+#pragma unroll 8
+                for (int j = 0; j < HD / 4; j++) {
+                    const float4 kv = k4[j], qv = q4[j];
+                    d0 = fmaf(qv.x, kv.x, d0);
+                    d1 = fmaf(qv.y, kv.y, d1);
+                    d2 = fmaf(qv.z, kv.z, d2);
+                    d3 = fmaf(qv.w, kv.w, d3);
+                }
+                s = ((d0 + d1) + (d2 + d3)) * a.kscale;
             }
-        }
-        __syncthreads();
-#pragma unroll
-        for (int h = 0; h < NREP; h++) {
-            float mx = -INFINITY;
-            for (int p = 0; p < cn; p++) mx = fmaxf(mx, sc[h][p]);
-            const float mnew = fmaxf(m_run[h], mx);
-            const float f = expf(m_run[h] - mnew);   // 0 when m_run was -inf
-            l_run[h] *= f;
-            acc[h].x *= f; acc[h].y *= f; acc[h].z *= f; acc[h].w *= f;
-            m_run[h] = mnew;
-        }
-        for (int p = warp * PPW + sub_slot; p < cn; p += NW * PPW) {
-            const float4 vv = (c0 + p == pos) ? reinterpret_cast<const float4 *>(vnew)[dl]
-                                              : reinterpret_cast<const float4 *>(vb + p * HD)[dl];
-#pragma unroll
-            for (int h = 0; h < NREP; h++) {
-                const float e = expf(sc[h][p] - m_run[h]);
-                l_run[h] += e;
-                acc[h].x = fmaf(e, vv.x, acc[h].x);
-                acc[h].y = fmaf(e, vv.y, acc[h].y);
-                acc[h].z = fmaf(e, vv.z, acc[h].z);
-                acc[h].w = fmaf(e, vv.w, acc[h].w);
+            const float mnew = fmaxf(m_run[k], warp_max(s));
+            const float f = expf(m_run[k] - mnew);          // 0 while m_run is -inf
+            const float e = lane < cn ? expf(s - mnew) : 0.0f;
+            l_run[k] = l_run[k] * f + warp_sum(e);
+            m_run[k] = mnew;
+            acc[k].x *= f; acc[k].y *= f; acc[k].z *= f; acc[k].w *= f;
+            // the same trip count in every lane: the shuffle needs all 32
+            const int dq = lane % LPR;
+            for (int pb = 0; pb < cn; pb += RPW) {
+                const int   p = pb + lane / LPR;
+                const float ep = __shfl_sync(0xffffffffu, e, p & 31);
+                if (p < cn) {
+                    const float4 vv = (c0 + p == pos) ? reinterpret_cast<const float4 *>(vnew)[dq]
+                                                      : reinterpret_cast<const float4 *>(vb + p * RS)[dq];
+                    acc[k].x = fmaf(ep, vv.x, acc[k].x);
+                    acc[k].y = fmaf(ep, vv.y, acc[k].y);
+                    acc[k].z = fmaf(ep, vv.z, acc[k].z);
+                    acc[k].w = fmaf(ep, vv.w, acc[k].w);
+                }
             }
         }
         __syncthreads();      // buffer sb&1 is free for sub-chunk sb+2
     }
-    // reduce over sub-slots (shuffles) and warps (shared memory)
+    // this CTA's partial per head: acc summed over the RPW row groups
 #pragma unroll
-    for (int h = 0; h < NREP; h++) {
-        float l = l_run[h];
-        for (int o = LPP; o < 32; o <<= 1) {
-            l += __shfl_xor_sync(0xffffffffu, l, o);
-            acc[h].x += __shfl_xor_sync(0xffffffffu, acc[h].x, o);
-            acc[h].y += __shfl_xor_sync(0xffffffffu, acc[h].y, o);
-            acc[h].z += __shfl_xor_sync(0xffffffffu, acc[h].z, o);
-            acc[h].w += __shfl_xor_sync(0xffffffffu, acc[h].w, o);
+    for (int k = 0; k < HPW; k++) {
+        const int h = warp + k * NW;
+        if (h >= NREP) break;
+#pragma unroll
+        for (int o = LPR; o < 32; o <<= 1) {
+            acc[k].x += __shfl_xor_sync(0xffffffffu, acc[k].x, o);
+            acc[k].y += __shfl_xor_sync(0xffffffffu, acc[k].y, o);
+            acc[k].z += __shfl_xor_sync(0xffffffffu, acc[k].z, o);
+            acc[k].w += __shfl_xor_sync(0xffffffffu, acc[k].w, o);
         }
-        if (sub_slot == 0) reinterpret_cast<float4 *>(acc_s[warp][h])[dl] = acc[h];
-        if (lane == 0) sc[h][warp] = l;       // per-warp l
+        if (lane < LPR) reinterpret_cast<float4 *>(part_s[h])[lane] = acc[k];
+        if (lane == 0) {
+            part_s[h][HD] = m_run[k];
+            part_s[h][HD + 1] = l_run[k];
+        }
     }
+    // ---- merge: every CTA pushes its partial into rank 0's K/V buffer -----
+    // (rank 0's buffer is free once every CTA of the cluster is past its
+    // loop), then rank 0 merges from local shared memory in split order.
+    constexpr int PER = NREP * (HD + 4);        // floats of one partial
+    const int ns = a.n_split;
+    cluster.sync();                             // all CTAs done with their K/V buffers
     __syncthreads();
-    float *mypart = a.part + ((size_t)g * a.n_split + split) * NREP * (HD + 2);
-    for (int i = tid; i < NREP * HD; i += ATT_THREADS) {
-        const int h = i / HD, d = i % HD;
-        float s = 0.0f;
-#pragma unroll
-        for (int w = 0; w < NW; w++) s += acc_s[w][h][d];
-        mypart[h * (HD + 2) + d] = s;
+    {
+        float *dst = cluster.map_shared_rank(kvbuf, 0) + (size_t)split * PER;
+        const float4 *src4 = reinterpret_cast<const float4 *>(&part_s[0][0]);
+        float4 *dst4 = reinterpret_cast<float4 *>(dst);
+        for (int i = tid; i < PER / 4; i += ATT_THREADS) dst4[i] = src4[i];
     }
-    if (tid < NREP) {
-        float l = 0.0f;
-#pragma unroll
-        for (int w = 0; w < NW; w++) l += sc[tid][w];
-        mypart[tid * (HD + 2) + HD] = m_run[tid];
-        mypart[tid * (HD + 2) + HD + 1] = l;
-    }
-    // ---- the last CTA of this head merges the n_split partials ----------
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) s_last = (atomicAdd(&a.counter[g], 1u) == (unsigned)a.n_split - 1);
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    const float *hp = a.part + (size_t)g * a.n_split * NREP * (HD + 2);
-    const int    per = NREP * (HD + 2), total = a.n_split * per;
-    float       *pm = kvbuf;                  // reuse the K/V buffers
-    for (int i = tid; i < total; i += ATT_THREADS) pm[i] = __ldcg(hp + i);
-    __syncthreads();
+    cluster.sync();                             // the pushes are visible to rank 0
+    if (cluster.block_rank() != 0) return;
+    const float *gath = kvbuf;                  // [ns][NREP][HD + 4]
     if (tid < NREP) {
         const int h = tid;
         float M = -INFINITY;
-        for (int s = 0; s < a.n_split; s++) M = fmaxf(M, pm[s * per + h * (HD + 2) + HD]);
+        for (int r = 0; r < ns; r++) M = fmaxf(M, gath[r * PER + h * (HD + 4) + HD]);
         float L = 0.0f;
-        for (int s = 0; s < a.n_split; s++) {
-            const float ms = pm[s * per + h * (HD + 2) + HD];
+        for (int r = 0; r < ns; r++) {
+            const float ms = gath[r * PER + h * (HD + 4) + HD];
             const float w = ms > -INFINITY ? expf(ms - M) : 0.0f;
-            wsplit[h][s] = w;
-            L += pm[s * per + h * (HD + 2) + HD + 1] * w;
+            wsplit[h][r] = w;
+            L += gath[r * PER + h * (HD + 4) + HD + 1] * w;
         }
-        sc[h][0] = L > 0.0f ? 1.0f / L : 0.0f;
+        invl[h] = L > 0.0f ? 1.0f / L : 0.0f;
     }
     __syncthreads();
     for (int i = tid; i < NREP * HD; i += ATT_THREADS) {
         const int h = i / HD, d = i % HD;
         float o = 0.0f;
-        for (int s = 0; s < a.n_split; s++) o = fmaf(pm[s * per + h * (HD + 2) + d], wsplit[h][s], o);
-        a.att[(g * NREP + h) * HD + d] = o * sc[h][0];
+        for (int r = 0; r < ns; r++) o = fmaf(gath[r * PER + h * (HD + 4) + d], wsplit[h][r], o);
+        a.att[(g * NREP + h) * HD + d] = o * invl[h];
     }
-    if (tid == 0) a.counter[g] = 0u;
 }

@@ -52,6 +52,7 @@ struct Launcher {
     std::vector<ProfRec> *prof = nullptr;
     const char *kind = "kernel";
     double      bytes = 0;
+    unsigned    cluster_y = 1;   // next launch: thread-block clusters of (1, cluster_y, 1)
     // The first kernel of a sequence follows host copies, not a kernel, so
     // it never gets a programmatic (early-start) dependency.
 
@@ -59,15 +60,26 @@ struct Launcher {
     void operator()(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, Args &&...args)
     {
         cudaLaunchConfig_t   cfg = {};
-        cudaLaunchAttribute  attr[1];
+        cudaLaunchAttribute  attr[2];
         cfg.gridDim = grid;
         cfg.blockDim = block;
         cfg.dynamicSmemBytes = smem;
         cfg.stream = stream;
-        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        unsigned na = 0;
+        if (pdl && count > 0 && !prof) {
+            attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            attr[na].val.programmaticStreamSerializationAllowed = 1;
+            na++;
+        }
+        if (cluster_y > 1) {
+            attr[na].id = cudaLaunchAttributeClusterDimension;
+            attr[na].val.clusterDim.x = 1;
+            attr[na].val.clusterDim.y = cluster_y;
+            attr[na].val.clusterDim.z = 1;
+            na++;
+        }
         cfg.attrs = attr;
-        cfg.numAttrs = (pdl && count > 0 && !prof) ? 1 : 0;
+        cfg.numAttrs = na;
         ProfRec r{kind, bytes, nullptr, nullptr};
         if (prof) {
             cudaEventCreate(&r.e0);
@@ -82,6 +94,7 @@ struct Launcher {
         }
         kind = "kernel";
         bytes = 0;
+        cluster_y = 1;
         count++;
     }
 };
@@ -101,7 +114,7 @@ static int num_sms(int dev)
 static bool fast_ok(const DevMat &m)
 {
     return !m.zero && (m.layout == LAY_SPLIT4 || m.layout == LAY_SPLIT8) && m.n_in % 1024 == 0 &&
-           m.n_in / 1024 <= 31;
+           m.n_in / 1024 <= FAST_MAX_NKG;
 }
 
 // Largest dynamic shared memory a fast-GEMV launch may ask for: the
@@ -140,7 +153,7 @@ static FastPlan plan_fast(const DevMat &m, int epi, int sms)
     int rowpar = 16 / nkg;
     if (rowpar < 1) rowpar = 1;
     if (rowpar > 4) rowpar = 4;
-    while (32 * (nkg * rowpar + 1) > 1024) rowpar--;
+    while (rowpar > 1 && 32 * (nkg * rowpar + 1) > FAST_MAX_THREADS) rowpar--;
     p.threads = 32 * (nkg * rowpar + 1);
     int grid = sms;
     for (;;) {
@@ -153,11 +166,14 @@ static FastPlan plan_fast(const DevMat &m, int epi, int sms)
         grid += sms;
     }
     p.grid = (m.n_out + p.rows_per_cta - 1) / p.rows_per_cta;
-    int sr = (int)(20480 / m.row_bytes);
-    if (sr < 1) sr = 1;
-    if (sr > p.rows_per_cta) sr = p.rows_per_cta;
+    // ~40 KB stages, a whole number of row groups (one row per consumer warp)
+    int sr = (int)(40960 / m.row_bytes);
+    sr -= sr % rowpar;
+    if (sr < rowpar) sr = rowpar;
+    const int cap = ((p.rows_per_cta + rowpar - 1) / rowpar) * rowpar;
+    if (sr > cap) sr = cap;
     p.stage_rows = sr;
-    p.smem = fast_smem_plan(m.row_bytes, sr, p.rows_per_cta, nkg).total;
+    p.smem = fast_smem_plan(m.row_bytes, sr, p.rows_per_cta, nkg, rowpar).total;
     return p;
 }
 
@@ -166,6 +182,42 @@ static void attn_attr()
 {
     cudaFuncSetAttribute(k_attention<HD, R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)attn_smem_bytes<HD>());
+    cudaFuncSetAttribute(k_attention<HD, R>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+}
+
+// Largest cluster (= number of position splits per KV head, <= 16) of which
+// n_kv can be resident at once.
+template <int HD, int R>
+static int attn_cluster_for(int n_kv, int max_split)
+{
+    for (int cs = ATT_MAX_SPLIT; cs >= 1; cs >>= 1) {
+        if (cs > max_split) continue;
+        cudaLaunchConfig_t  cfg = {};
+        cudaLaunchAttribute at;
+        cfg.gridDim = dim3(n_kv, cs);
+        cfg.blockDim = dim3(ATT_THREADS);
+        cfg.dynamicSmemBytes = attn_smem_bytes<HD>();
+        at.id = cudaLaunchAttributeClusterDimension;
+        at.val.clusterDim.x = 1;
+        at.val.clusterDim.y = cs;
+        at.val.clusterDim.z = 1;
+        cfg.attrs = &at;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, k_attention<HD, R>, &cfg) == cudaSuccess && n >= n_kv)
+            return cs;
+        cudaGetLastError();
+    }
+    return 1;
+}
+
+static int attn_cluster(int hd, int rep, int n_kv, int max_split)
+{
+#define CL(HD_, R_) if (hd == HD_ && rep == R_) return attn_cluster_for<HD_, R_>(n_kv, max_split);
+    CL(128, 1) CL(128, 2) CL(128, 4) CL(128, 8) CL(64, 1) CL(64, 2) CL(64, 4) CL(64, 8)
+    CL(32, 1) CL(32, 2) CL(32, 4) CL(32, 8) CL(16, 1) CL(16, 2) CL(16, 4) CL(16, 8)
+#undef CL
+    return 1;
 }
 
 static void attn_attrs_all()
@@ -226,8 +278,17 @@ struct GemvScratch {
 // y (epi) W * rmsnorm?(x).  norm_w null = no prologue.  For the argmax
 // epilogue `a` carries the extra outputs.
 static void enqueue_gemv(Launcher &L, int sms, const DevMat &m, const float *x, const float *norm_w,
-                         float eps, float *y, int epi, const GemvScratch &s, GemvArgs a)
+                         float eps, float *y, int epi, const GemvScratch &s, GemvArgs a,
+                         const DevMat *next = nullptr, int next_epi = EPI_STORE)
 {
+    if (next && fast_ok(*next) && next->data) {
+        const FastPlan np = plan_fast(*next, next_epi, sms);
+        a.pf_ptr = next->data;
+        a.pf_end = next->data + (size_t)next->n_out * next->row_bytes;
+        a.pf_stride = (size_t)np.rows_per_cta * next->row_bytes;
+        const size_t per = a.pf_stride < (size_t)65536 ? a.pf_stride : (size_t)65536;
+        a.pf_bytes = (uint32_t)(per & ~(size_t)15);
+    }
     if (L.bytes == 0) L.bytes = gemv_bytes(m, epi);
     a.m = m;
     a.eps = eps;
@@ -307,8 +368,6 @@ struct ecu_ctx {
     float   *state = nullptr;     // n_embd + 1
     float   *qkv = nullptr, *att = nullptr, *h = nullptr, *gtmp = nullptr, *utmp = nullptr;
     float   *logits = nullptr;
-    float   *attn_part = nullptr;
-    unsigned *attn_cnt = nullptr;
     int      n_split = 1;
     GemvScratch scr;
     StepState *st = nullptr;      // device
@@ -355,7 +414,7 @@ static size_t dev_row_bytes(int t, int n_in, int layout)
 
 static int choose_layout(int t, int n_in)
 {
-    if (n_in % 1024 == 0 && n_in / 1024 <= 31) {
+    if (n_in % 1024 == 0 && n_in / 1024 <= FAST_MAX_NKG) {
         if (t == GT_Q4_0) return LAY_SPLIT4;
         if (t == GT_Q8_0) return LAY_SPLIT8;
     }
@@ -445,9 +504,19 @@ static void ctx_free(ecu_ctx *c)
 
 // ------------------------------------------------------------- the step --
 
-static void enqueue_layer(ecu_ctx *c, Launcher &L, int li)
+// First weight matrix the step touches after layer li's down projection.
+static const DevMat *after_layer(const ecu_ctx *c, int li, int nl)
 {
+    if (li + 1 < nl) return &c->layers[li + 1].qkv[0];
+    if (c->stage == ECU_STAGE_FULL) return &c->out;
+    return nullptr;
+}
+
+static void enqueue_layer(ecu_ctx *c, Launcher &L, int li, int nl = -1)
+{
+    if (nl < 0) nl = (int)c->layers.size();
     LayerDev   &ly = c->layers[li];
+    const DevMat *gu_first = ly.gu_fused ? &ly.gu : &ly.g;
     const EcuGeom &g = c->g;
     const int   hd = g.head_dim, qdim = g.n_head * hd, kvdim = g.n_head_kv * hd;
     GemvArgs    a = {};
@@ -456,7 +525,8 @@ static void enqueue_layer(ecu_ctx *c, Launcher &L, int li)
     // (1) RMSNorm + Q/K/V projections
     if (ly.qkv.size() == 1) {
         L.kind = "gemv_qkv";
-        enqueue_gemv(L, c->sms, ly.qkv[0], c->state, ly.attn_norm, g.eps, c->qkv, EPI_STORE, c->scr, a);
+        enqueue_gemv(L, c->sms, ly.qkv[0], c->state, ly.attn_norm, g.eps, c->qkv, EPI_STORE, c->scr, a,
+                     &ly.o, EPI_ADD);
     } else {
         L.kind = "rmsnorm";
         L.bytes = 12.0 * g.n_embd;
@@ -479,8 +549,6 @@ static void enqueue_layer(ecu_ctx *c, Launcher &L, int li)
     aa.kc = c->kc + (size_t)li * plane;
     aa.vc = c->vc + (size_t)li * plane;
     aa.att = c->att;
-    aa.part = c->attn_part;
-    aa.counter = c->attn_cnt;
     aa.st = c->st;
     aa.status = &c->st->status;
     aa.n_head = g.n_head;
@@ -491,6 +559,7 @@ static void enqueue_layer(ecu_ctx *c, Launcher &L, int li)
     aa.kscale = 1.0f / sqrtf((float)hd);
     dim3 ag(g.n_head_kv, c->n_split);
     L.kind = "attention";
+    L.cluster_y = (unsigned)c->n_split;
     // K and V rows of positions 0..pos read, one row of each written, q/att
     L.bytes = 2.0 * 4.0 * kvdim * (c->pos + 2) + 8.0 * qdim + 4.0 * (qdim + 2 * kvdim);
 #define ATT_CASE(HD_, R_) \
@@ -504,11 +573,13 @@ static void enqueue_layer(ecu_ctx *c, Launcher &L, int li)
     (void)kvdim;
     // (3) x += Wo * att
     L.kind = "gemv_o";
-    enqueue_gemv(L, c->sms, ly.o, c->att, nullptr, g.eps, c->state, EPI_ADD, c->scr, a);
+    enqueue_gemv(L, c->sms, ly.o, c->att, nullptr, g.eps, c->state, EPI_ADD, c->scr, a, gu_first,
+                 ly.gu_fused ? EPI_SWIGLU : EPI_STORE);
     // (4) RMSNorm + gate/up + SwiGLU
     if (ly.gu_fused) {
         L.kind = "gemv_gate_up";
-        enqueue_gemv(L, c->sms, ly.gu, c->state, ly.ffn_norm, g.eps, c->h, EPI_SWIGLU, c->scr, a);
+        enqueue_gemv(L, c->sms, ly.gu, c->state, ly.ffn_norm, g.eps, c->h, EPI_SWIGLU, c->scr, a, &ly.d,
+                     EPI_ADD);
     } else {
         L.kind = "rmsnorm";
         L.bytes = 12.0 * g.n_embd;
@@ -525,7 +596,9 @@ static void enqueue_layer(ecu_ctx *c, Launcher &L, int li)
     }
     // (5) x += Wd * h
     L.kind = "gemv_down";
-    enqueue_gemv(L, c->sms, ly.d, c->h, nullptr, g.eps, c->state, EPI_ADD, c->scr, a);
+    const DevMat *nx = after_layer(c, li, nl);
+    enqueue_gemv(L, c->sms, ly.d, c->h, nullptr, g.eps, c->state, EPI_ADD, c->scr, a, nx,
+                 nx == &c->out ? EPI_ARGMAX : EPI_STORE);
 }
 
 static void enqueue_head(ecu_ctx *c, Launcher &L, bool advance)
@@ -542,7 +615,10 @@ static void enqueue_head(ecu_ctx *c, Launcher &L, bool advance)
     a.tok_out = c->state + g.n_embd;
     a.advance_pos = advance ? 1 : 0;
     L.kind = "gemv_head_argmax";
-    enqueue_gemv(L, c->sms, c->out, c->state, nullptr, g.eps, c->logits, EPI_ARGMAX, c->scr, a);
+    // a FULL context's next token starts with layer 0's Q/K/V projection
+    const DevMat *nx = (c->stage == ECU_STAGE_FULL && !c->layers.empty()) ? &c->layers[0].qkv[0] : nullptr;
+    enqueue_gemv(L, c->sms, c->out, c->state, nullptr, g.eps, c->logits, EPI_ARGMAX, c->scr, a, nx,
+                 EPI_STORE);
 }
 
 // Kernels of one step of the stage: nl layers (LAYERS/FULL) from layer 0.
@@ -554,7 +630,7 @@ static void enqueue_step(ecu_ctx *c, Launcher &L, int nl)
         L(k_embed, dim3(8), dim3(256), 0, c->emb, (const StepState *)c->st, c->state, c->g.n_embd);
     }
     if (c->stage == ECU_STAGE_LAYERS || c->stage == ECU_STAGE_FULL)
-        for (int i = 0; i < nl; i++) enqueue_layer(c, L, i);
+        for (int i = 0; i < nl; i++) enqueue_layer(c, L, i, nl);
     if (c->stage == ECU_STAGE_LAYERS) {
         L.kind = "step_advance";
         L(k_step_advance, dim3(1), dim3(32), 0, c->st);
@@ -939,21 +1015,16 @@ static int ctx_open_impl(ecu_ctx **out, const ecu_model *m, int stage, int first
         const size_t plane = (size_t)g.n_head_kv * g.n_ctx * hd;
         c->kc = c->dalloc<float>(plane * nl);
         c->vc = c->dalloc<float>(plane * nl);
-        // about one CTA per SM; the merge reuses the K/V staging buffers,
-        // which bounds n_split*n_rep*(hd+2) by 2*2*ATT_SUB*hd floats
-        c->n_split = c->sms / g.n_head_kv;
-        const int cap = (4 * ATT_SUB * hd) / (g.n_rep * (hd + 2));
-        if (c->n_split > cap) c->n_split = cap;
-        if (c->n_split > ATT_MAX_SPLIT) c->n_split = ATT_MAX_SPLIT;
-        if (c->n_split > g.n_ctx) c->n_split = g.n_ctx;
-        if (c->n_split < 1) c->n_split = 1;
-        c->attn_part = c->dalloc<float>((size_t)g.n_head_kv * c->n_split * g.n_rep * (hd + 2));
-        c->attn_cnt = c->dalloc<unsigned>((size_t)g.n_head_kv);
+        // position splits per KV head = the cluster size (<= 16, <= one
+        // CTA per SM over all heads, all clusters resident at once)
+        int max_split = c->sms / g.n_head_kv;
+        if (max_split > g.n_ctx) max_split = g.n_ctx;
+        if (max_split < 1) max_split = 1;
+        c->n_split = attn_cluster(hd, g.n_rep, g.n_head_kv, max_split);
+        cudaGetLastError();
         c->rope_cs = c->dalloc<float>((size_t)g.n_ctx * hd);
-        if (!c->qkv || !c->att || !c->h || !c->gtmp || !c->utmp || !c->kc || !c->vc || !c->attn_part ||
-            !c->attn_cnt || !c->rope_cs)
+        if (!c->qkv || !c->att || !c->h || !c->gtmp || !c->utmp || !c->kc || !c->vc || !c->rope_cs)
             return fail_oom("KV cache and layer buffers");
-        cudaMemset(c->attn_cnt, 0, (size_t)g.n_head_kv * sizeof(unsigned));
         // RoPE table with the host libm, exactly as src/engine.c:371-373
         {
             std::vector<float> cs((size_t)g.n_ctx * hd);

@@ -47,6 +47,12 @@ struct GemvArgs {
     // fast-path geometry (set by the host planner)
     int          rows_per_cta;
     int          stage_rows;
+    // L2 prefetch of the next GEMV's weights: CTA i warms
+    // [pf_ptr + i*pf_stride, + pf_bytes), clipped to pf_end
+    const uint8_t *pf_ptr;
+    const uint8_t *pf_end;
+    size_t       pf_stride;
+    uint32_t     pf_bytes;
 };
 
 // ---------------------------------------------------------------- RMSNorm --
@@ -248,11 +254,28 @@ static __global__ void k_swiglu(const float *g, const float *u, float *h, int n)
 // =============================================================== fast =====
 
 #define FAST_STAGES 4
+#define FAST_MAX_THREADS 640    // nkg * rowpar <= 19 consumer warps + 1 producer
+#define FAST_MAX_NKG 19         // n_in <= 19 * 1024 on the fast path
+#define FAST_RB 4               // rows per consumer-warp batch
 
-// Exact three-plane int8 decomposition of one 32-element block of x.
+// 1.5 * 2^23: for |v| <= 2^22, v + M rounds v to the nearest integer (ties to
+// even) and that integer, two's complement, sits in the low bits of the sum.
+#define RND_MAGIC 12582912.0f
+
+// Low bytes of four words -> one word [a.b0, b.b0, c.b0, d.b0].
+__device__ __forceinline__ uint32_t pack_lo_bytes(uint32_t a, uint32_t b, uint32_t c, uint32_t d)
+{
+    return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
+}
+
+// Exact three-plane int8 decomposition of one 32-element block of x:
+// x = s * (d0 + d1/128 + d2/16384) + r, s = 2^k, |r| <= s / 32768, each
+// digit in [-127, 127] (d0) or [-64, 64] (d1, d2).  No float->int
+// conversions: each digit is the low byte of v + RND_MAGIC.
 // FMT 4: word j<4 packs elements 4j..4j+3 (low nibbles of Q4_0 code word j),
 //        word 4+j packs 16+4j..16+4j+3 (its high nibbles).
 // FMT 8: word j packs elements 4j..4j+3.
+// off[p] = -8 * (sum of plane p's digits) for Q4_0 (the code offset), else 0.
 template <int FMT>
 __device__ __forceinline__ void make_digits(const float *xv, int (&xw)[3][8], int (&off)[3],
                                             float &sxs)
@@ -272,32 +295,31 @@ __device__ __forceinline__ void make_digits(const float *xv, int (&xw)[3][8], in
     } else {
         sxs = 0.0f;                         // all-zero (or negligible) block
     }
-    int d[3][32];
+    int sum[3] = {0, 0, 0};
 #pragma unroll
-    for (int k = 0; k < 32; k++) {
-        const float v  = __fmul_rn(xv[k], inv);         // exact: power-of-2 scale
-        const float q0 = rintf(v);
-        const float r0 = __fmul_rn(__fsub_rn(v, q0), 128.0f);
-        const float q1 = rintf(r0);
-        const float r1 = __fmul_rn(__fsub_rn(r0, q1), 128.0f);
-        const float q2 = rintf(r1);
-        d[0][k] = (int)q0;
-        d[1][k] = (int)q1;
-        d[2][k] = (int)q2;
-    }
+    for (int j = 0; j < 8; j++) {
+        const int base = (FMT == 4) ? ((j < 4) ? 4 * j : 16 + 4 * (j - 4)) : 4 * j;
+        uint32_t b[3][4];
 #pragma unroll
-    for (int p = 0; p < 3; p++) {
-        int s = 0;
+        for (int i = 0; i < 4; i++) {
+            const float v  = __fmul_rn(xv[base + i], inv);            // exact
+            const float t0 = __fadd_rn(v, RND_MAGIC);
+            const float r0 = __fmul_rn(__fsub_rn(v, __fsub_rn(t0, RND_MAGIC)), 128.0f);
+            const float t1 = __fadd_rn(r0, RND_MAGIC);
+            const float r1 = __fmul_rn(__fsub_rn(r0, __fsub_rn(t1, RND_MAGIC)), 128.0f);
+            const float t2 = __fadd_rn(r1, RND_MAGIC);
+            b[0][i] = __float_as_uint(t0);
+            b[1][i] = __float_as_uint(t1);
+            b[2][i] = __float_as_uint(t2);
+        }
 #pragma unroll
-        for (int k = 0; k < 32; k++) s += d[p][k];
-        off[p] = (FMT == 4) ? -8 * s : 0;
-#pragma unroll
-        for (int j = 0; j < 8; j++) {
-            const int base = (FMT == 4) ? ((j < 4) ? 4 * j : 16 + 4 * (j - 4)) : 4 * j;
-            xw[p][j] = (d[p][base] & 0xFF) | ((d[p][base + 1] & 0xFF) << 8) |
-                       ((d[p][base + 2] & 0xFF) << 16) | ((d[p][base + 3] & 0xFF) << 24);
+        for (int p = 0; p < 3; p++) {
+            xw[p][j] = (int)pack_lo_bytes(b[p][0], b[p][1], b[p][2], b[p][3]);
+            sum[p] = __dp4a(xw[p][j], 0x01010101, sum[p]);
         }
     }
+#pragma unroll
+    for (int p = 0; p < 3; p++) off[p] = (FMT == 4) ? -8 * sum[p] : 0;
 }
 
 // Dot of the lane's block in `row` (shared memory) with its digit planes.
@@ -305,12 +327,11 @@ template <int FMT>
 __device__ __forceinline__ float block_dot(const uint8_t *row, int nb, int b,
                                            const int (&xw)[3][8], const int (&off)[3], float sxs)
 {
-    int a0 = off[0], a1 = off[1], a2 = off[2];
-    float d;
     if (FMT == 4) {
         const uint4 q = *reinterpret_cast<const uint4 *>(row + (size_t)b * 16);
-        d = __half2float(*reinterpret_cast<const __half *>(row + (size_t)nb * 16 + 2 * b));
+        const float d = __half2float(*reinterpret_cast<const __half *>(row + (size_t)nb * 16 + 2 * b));
         const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+        int a0 = off[0], a1 = off[1], a2 = off[2];
 #pragma unroll
         for (int j = 0; j < 4; j++) {
             const int lo = (int)(w[j] & 0x0F0F0F0Fu), hi = (int)((w[j] >> 4) & 0x0F0F0F0Fu);
@@ -321,48 +342,82 @@ __device__ __forceinline__ float block_dot(const uint8_t *row, int nb, int b,
             a2 = __dp4a(lo, xw[2][j], a2);
             a2 = __dp4a(hi, xw[2][4 + j], a2);
         }
+        // |a0| <= 32*8*127, |a1|,|a2| <= 32*8*64: the merged value fits int32
+        const int t = a0 * 16384 + a1 * 128 + a2;
+        return (float)t * (d * sxs);
     } else {
         // SPLIT8 rows keep the first and second 16 code bytes of every block
         // in two separate runs, so both 16-byte loads are conflict-free
         const uint4 q0 = *reinterpret_cast<const uint4 *>(row + (size_t)b * 16);
         const uint4 q1 = *reinterpret_cast<const uint4 *>(row + (size_t)(nb + b) * 16);
-        d = __half2float(*reinterpret_cast<const __half *>(row + (size_t)nb * 32 + 2 * b));
+        const float d = __half2float(*reinterpret_cast<const __half *>(row + (size_t)nb * 32 + 2 * b));
         const int w[8] = {(int)q0.x, (int)q0.y, (int)q0.z, (int)q0.w,
                           (int)q1.x, (int)q1.y, (int)q1.z, (int)q1.w};
+        int a0 = 0, a1 = 0, a2 = 0;
 #pragma unroll
         for (int j = 0; j < 8; j++) {
             a0 = __dp4a(w[j], xw[0][j], a0);
             a1 = __dp4a(w[j], xw[1][j], a1);
             a2 = __dp4a(w[j], xw[2][j], a2);
         }
+        const float t = fmaf((float)a1, 128.0f, (float)a2);
+        return fmaf((float)a0, 16384.0f, t) * (d * sxs);
     }
-    const float t = fmaf((float)a1, 128.0f, (float)a2);
-    const float v = fmaf((float)a0, 16384.0f, t);
-    return v * (d * sxs);
+}
+
+// Four per-lane row partials -> four row sums: afterwards lane l holds the
+// sum of row (l >> 3) & 3 (a transposed butterfly: 6 shuffles for 4 rows).
+__device__ __forceinline__ float warp_sum4(float v0, float v1, float v2, float v3, int lane)
+{
+    const bool up = lane & 16;
+    float a0 = up ? v2 : v0, a1 = up ? v3 : v1;
+    const float b0 = up ? v0 : v2, b1 = up ? v1 : v3;
+    a0 += __shfl_xor_sync(0xffffffffu, b0, 16);
+    a1 += __shfl_xor_sync(0xffffffffu, b1, 16);
+    const bool mid = lane & 8;
+    float c = mid ? a1 : a0;
+    const float dd = mid ? a0 : a1;
+    c += __shfl_xor_sync(0xffffffffu, dd, 8);
+    c += __shfl_xor_sync(0xffffffffu, c, 4);
+    c += __shfl_xor_sync(0xffffffffu, c, 2);
+    c += __shfl_xor_sync(0xffffffffu, c, 1);
+    return c;
 }
 
 // Shared-memory plan of one fast launch (host and device agree on it).
 struct FastSmem {
-    size_t stage_bytes, ring, bars, red, dsum, argsh, total;
+    size_t stage_bytes, ring, bars, red, dig, dsum, argsh, total;
 };
 
 __host__ __device__ inline FastSmem fast_smem_plan(size_t row_bytes, int stage_rows,
-                                                   int rows_per_cta, int nkg)
+                                                   int rows_per_cta, int nkg, int rowpar)
 {
     FastSmem p;
     p.stage_bytes = ((size_t)stage_rows * row_bytes + 127) & ~(size_t)127;
     p.ring = 0;
     p.bars = p.ring + FAST_STAGES * p.stage_bytes;
     p.red = p.bars + 2 * FAST_STAGES * sizeof(uint64_t);
-    p.dsum = (p.red + (size_t)rows_per_cta * nkg * sizeof(float) + 15) & ~(size_t)15;
+    p.dig = (p.red + (size_t)rows_per_cta * nkg * sizeof(float) + 15) & ~(size_t)15;
+    // digit planes shared by the rowpar warps of a k-group: 28 words per block
+    const size_t dig_bytes = rowpar > 1 ? (size_t)nkg * 32 * 28 * sizeof(int) : 0;
+    p.dsum = p.dig + dig_bytes;
     p.argsh = p.dsum + 256 * sizeof(double);
     p.total = p.argsh + 32 * sizeof(ArgBest);
     return p;
 }
 
+// L2 prefetch (no shared memory, no completion to wait for).
+__device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes)
+{
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // blockDim = 32 * (nkg * rowpar + 1): consumer warps first, producer last.
+// Consumer warp w serves k-group g = w % nkg (32 blocks = 1024 inputs of
+// every row) and takes the stage's rows rp, rp + rowpar, ... (rp = w / nkg)
+// four at a time.
 template <int FMT, bool NORM, int EPI>
-__global__ void __launch_bounds__(1024, 1) k_gemv_fast(GemvArgs a)
+__global__ void __launch_bounds__(FAST_MAX_THREADS, 1) k_gemv_fast(GemvArgs a)
 {
     extern __shared__ __align__(128) uint8_t smem[];
     const DevMat &m = a.m;
@@ -373,11 +428,12 @@ __global__ void __launch_bounds__(1024, 1) k_gemv_fast(GemvArgs a)
     const int nrows = max(0, min(m.n_out, r0 + a.rows_per_cta) - r0);
     const int SR = a.stage_rows;
     const int nstages = (nrows + SR - 1) / SR;
-    const FastSmem P = fast_smem_plan(m.row_bytes, SR, a.rows_per_cta, nkg);
+    const FastSmem P = fast_smem_plan(m.row_bytes, SR, a.rows_per_cta, nkg, rowpar);
     uint8_t  *ring = smem + P.ring;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + P.bars);
     uint64_t *empty = full + FAST_STAGES;
     float    *red = reinterpret_cast<float *>(smem + P.red);
+    int      *dig = reinterpret_cast<int *>(smem + P.dig);
     double   *dsum = reinterpret_cast<double *>(smem + P.dsum);
     ArgBest  *argsh = reinterpret_cast<ArgBest *>(smem + P.argsh);
 
@@ -407,6 +463,15 @@ __global__ void __launch_bounds__(1024, 1) k_gemv_fast(GemvArgs a)
                 if (s == FAST_STAGES - 1 || s == nstages - 1) pdl_trigger();
             }
             if (nstages == 0) pdl_trigger();
+            // warm L2 with the start of the next GEMV's weights
+            if (a.pf_ptr && a.pf_bytes) {
+                const uint8_t *p = a.pf_ptr + (size_t)blockIdx.x * a.pf_stride;
+                for (uint32_t o = 0; o < a.pf_bytes && p + o < a.pf_end; o += 32768) {
+                    const uint32_t sz =
+                        (uint32_t)min((size_t)min(32768u, a.pf_bytes - o), (size_t)(a.pf_end - (p + o))) & ~15u;
+                    if (sz >= 16) prefetch_l2(p + o, sz);
+                }
+            }
         }
         pdl_wait();                       // before this warp joins the epilogue writes
     } else {
@@ -420,7 +485,7 @@ __global__ void __launch_bounds__(1024, 1) k_gemv_fast(GemvArgs a)
         const int b = g * 32 + lane;      // this lane's block column
         int   xw[3][8], off[3];
         float sxs;
-        {
+        if (rp == 0) {
             float xv[32];
             const float4 *x4 = reinterpret_cast<const float4 *>(a.x + (size_t)b * 32);
 #pragma unroll
@@ -438,7 +503,7 @@ __global__ void __launch_bounds__(1024, 1) k_gemv_fast(GemvArgs a)
                     xv[4 * k + 2] = __fmul_rn(__fmul_rn(xv[4 * k + 2], scale), t.z);
                     xv[4 * k + 3] = __fmul_rn(__fmul_rn(xv[4 * k + 3], scale), t.w);
                 }
-                if (a.xn_out && blockIdx.x == 0 && rp == 0) {
+                if (a.xn_out && blockIdx.x == 0) {
                     float4 *o4 = reinterpret_cast<float4 *>(a.xn_out + (size_t)b * 32);
 #pragma unroll
                     for (int k = 0; k < 8; k++)
@@ -446,16 +511,47 @@ __global__ void __launch_bounds__(1024, 1) k_gemv_fast(GemvArgs a)
                 }
             }
             make_digits<FMT>(xv, xw, off, sxs);
+            if (rowpar > 1) {
+                int4 *d4 = reinterpret_cast<int4 *>(dig + (size_t)b * 28);
+#pragma unroll
+                for (int p = 0; p < 3; p++) {
+                    d4[2 * p] = make_int4(xw[p][0], xw[p][1], xw[p][2], xw[p][3]);
+                    d4[2 * p + 1] = make_int4(xw[p][4], xw[p][5], xw[p][6], xw[p][7]);
+                }
+                d4[6] = make_int4(off[0], off[1], off[2], __float_as_int(sxs));
+            }
+        }
+        if (rowpar > 1) {
+            named_bar(1, nct);
+            if (rp != 0) {
+                const int4 *d4 = reinterpret_cast<const int4 *>(dig + (size_t)b * 28);
+#pragma unroll
+                for (int p = 0; p < 3; p++) {
+                    const int4 u = d4[2 * p], v = d4[2 * p + 1];
+                    xw[p][0] = u.x; xw[p][1] = u.y; xw[p][2] = u.z; xw[p][3] = u.w;
+                    xw[p][4] = v.x; xw[p][5] = v.y; xw[p][6] = v.z; xw[p][7] = v.w;
+                }
+                const int4 t = d4[6];
+                off[0] = t.x; off[1] = t.y; off[2] = t.z;
+                sxs = __int_as_float(t.w);
+            }
         }
         for (int s = 0; s < nstages; s++) {
             const int slot = s % FAST_STAGES;
             if (!mbar_wait(&full[slot], (s / FAST_STAGES) & 1, a.status)) break;
             const uint8_t *stage = ring + (size_t)slot * P.stage_bytes;
             const int      rows = min(SR, nrows - s * SR);
-            for (int i = rp; i < rows; i += rowpar) {
-                float v = block_dot<FMT>(stage + (size_t)i * m.row_bytes, nb, b, xw, off, sxs);
-                v = warp_sum(v);
-                if (lane == 0) red[(s * SR + i) * nkg + g] = v;
+            for (int i0 = rp; i0 < rows; i0 += FAST_RB * rowpar) {
+                float v[FAST_RB];
+#pragma unroll
+                for (int k = 0; k < FAST_RB; k++) {
+                    const int i = i0 + k * rowpar;
+                    v[k] = i < rows ? block_dot<FMT>(stage + (size_t)i * m.row_bytes, nb, b, xw, off, sxs)
+                                    : 0.0f;
+                }
+                const float sum = warp_sum4(v[0], v[1], v[2], v[3], lane);
+                const int   k = (lane >> 3) & 3, i = i0 + k * rowpar;
+                if ((lane & 7) == 0 && i < rows) red[(s * SR + i) * nkg + g] = sum;
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
@@ -485,7 +581,7 @@ __global__ void __launch_bounds__(1024, 1) k_gemv_fast(GemvArgs a)
         }
     }
     if (EPI == EPI_ARGMAX) {
-        ArgBest b = block_argmax(best, argsh);
-        argmax_finish(a, b, argsh);
+        ArgBest bb = block_argmax(best, argsh);
+        argmax_finish(a, bb, argsh);
     }
 }

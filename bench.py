@@ -52,6 +52,11 @@ def parse():
     ap.add_argument("--cpu-sample-s", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--seqs", type=int, default=8,
+                    help="N > 1: independent sequences interleaved through the layer pipeline")
+    ap.add_argument("--split", choices=["bytes", "ref"], default="bytes",
+                    help="N > 1: layer ranges balancing bytes per stage (head on the last GPU) or "
+                         "shard.c's ceil(layers/stages) rule")
     ap.add_argument("--layers", type=int, default=0,
                     help="override n_layer (reduced-depth runs for profiler captures; not a bench line)")
     return ap.parse_args()
@@ -192,7 +197,7 @@ def our_arm(args, rank, world, local):
 
     if world > 1:
         from distcomp_b200 import pipeline
-        return pipeline.bench_main(args, rank, world, local)
+        return pipeline.bench_main(args, rank, world, local, sys.modules[__name__])
 
     spec = synth.spec(CONFIG, **({"n_layer": args.layers} if args.layers else {}))
     t_build = time.perf_counter()

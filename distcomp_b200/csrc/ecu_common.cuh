@@ -71,11 +71,12 @@ struct DevMat {
 struct StepState {
     int pos;        // cache position of the current token
     int token;      // current input token
-    int status;     // nonzero: a kernel reported a bounded-wait timeout
+    int status;     // nonzero: a kernel gave up on a bounded wait, or read a bad token
     int pad;
 };
 
 #define ECU_STATUS_TIMEOUT 1
+#define ECU_STATUS_BADTOKEN 2
 
 // -------------------------------------------------------------- helpers ----
 

@@ -351,13 +351,28 @@ struct LayerDev {
     struct Src { std::string name; const DevMat *m; int row0, rstride, n_in; size_t elems; };
 };
 
+// Device allocations shared by a context and its forks (weights, norms, the
+// RoPE table): freed when the last context holding them closes.
+struct SharedAllocs {
+    int                 device = 0;
+    std::vector<void *> p;
+    ~SharedAllocs()
+    {
+        if (p.empty()) return;
+        cudaSetDevice(device);
+        for (void *q : p) cudaFree(q);
+    }
+};
+
 struct ecu_ctx {
     int         device = 0, sms = 148;
     int         stage = 0, first = 0, last = 0, pos = 0;
     EcuGeom     g;
     cudaStream_t stream = nullptr;
     bool        pdl = true, use_graph = true;
-    std::vector<void *> allocs;
+    std::vector<void *> allocs;           // this context's own buffers
+    std::shared_ptr<SharedAllocs> shared; // read-only tensors, shared with forks
+    bool        to_shared = false;        // dalloc target while uploading weights
     size_t      bytes = 0;
 
     std::vector<LayerDev> layers;
@@ -394,7 +409,8 @@ struct ecu_ctx {
         void *p = nullptr;
         if (cudaMalloc(&p, n * sizeof(T) + 256) != cudaSuccess) return nullptr;
         cudaMemset((uint8_t *)p + n * sizeof(T), 0, 256);
-        allocs.push_back(p);
+        if (to_shared) shared->p.push_back(p);
+        else allocs.push_back(p);
         bytes += n * sizeof(T);
         return (T *)p;
     }
@@ -627,7 +643,7 @@ static void enqueue_step(ecu_ctx *c, Launcher &L, int nl)
     if (c->stage == ECU_STAGE_EMBED || c->stage == ECU_STAGE_FULL) {
         L.kind = "embed";
         L.bytes = 8.0 * c->g.n_embd + (double)ecu_type_nbytes(c->emb.type, (size_t)c->g.n_embd);
-        L(k_embed, dim3(8), dim3(256), 0, c->emb, (const StepState *)c->st, c->state, c->g.n_embd);
+        L(k_embed, dim3(8), dim3(256), 0, c->emb, c->st, c->state, c->g.n_embd);
     }
     if (c->stage == ECU_STAGE_LAYERS || c->stage == ECU_STAGE_FULL)
         for (int i = 0; i < nl; i++) enqueue_layer(c, L, i, nl);
@@ -689,10 +705,30 @@ static int check_status(ecu_ctx *c)
     StepState s;
     CK(cudaMemcpy(&s, c->st, sizeof s, cudaMemcpyDeviceToHost));
     if (s.status) {
-        ecu_set_error(nullptr, 0, "a kernel gave up on a bounded wait (status %d)", s.status);
+        if (s.status & ECU_STATUS_BADTOKEN)
+            ecu_set_error(nullptr, 0, "the device-resident token is outside the vocabulary (%d)", c->g.n_vocab);
+        else
+            ecu_set_error(nullptr, 0, "a kernel gave up on a bounded wait (status %d)", s.status);
         CK(cudaMemset(&c->st->status, 0, sizeof(int)));
         return -1;
     }
+    return 0;
+}
+
+// Run `enq` on the context's stream ordered after the caller's stream s, and
+// order s after it.
+template <class F> static int on_stream(ecu_ctx *c, void *stream, F enq)
+{
+    cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
+    if (s == c->stream) return enq();
+    cudaEvent_t ev;
+    CK(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+    CK(cudaEventRecord(ev, s));
+    CK(cudaStreamWaitEvent(c->stream, ev, 0));
+    if (enq() != 0) { cudaEventDestroy(ev); return -1; }
+    CK(cudaEventRecord(ev, c->stream));
+    CK(cudaStreamWaitEvent(s, ev, 0));
+    cudaEventDestroy(ev);
     return 0;
 }
 
@@ -874,6 +910,52 @@ size_t ecu_ctx_bytes(const ecu_model *m, int stage, int first, int last, int n_c
     return b;
 }
 
+// A context's own device buffers: step state, token history, GEMV scratch,
+// pinned host staging, and with layers the activations and the KV cache,
+// with a head the logits.  Returns what failed, or nullptr.
+static const char *alloc_buffers(ecu_ctx *c, bool layers, bool head)
+{
+    const EcuGeom &g = c->g;
+    const int wide = g.n_ff > g.n_embd ? g.n_ff : g.n_embd;
+    const int hd = g.head_dim, qd = g.n_head * hd, kvd = g.n_head_kv * hd;
+    c->state = c->dalloc<float>((size_t)g.n_embd + 4);
+    c->st = c->dalloc<StepState>(1);
+    c->tok_hist = c->dalloc<int>((size_t)g.n_ctx + 1);
+    c->scr.xn = c->dalloc<float>((size_t)wide + 4);
+    c->scr.part_val = c->dalloc<float>(4096);
+    c->scr.part_idx = c->dalloc<int>(4096);
+    c->scr.counter = c->dalloc<unsigned>(4);
+    c->scr.status = c->st ? &c->st->status : nullptr;
+    if (!c->state || !c->st || !c->tok_hist || !c->scr.xn || !c->scr.part_val || !c->scr.part_idx || !c->scr.counter)
+        return "work buffers";
+    cudaMemset(c->st, 0, sizeof(StepState));
+    cudaMemset(c->scr.counter, 0, 4 * sizeof(unsigned));
+    cudaMemset(c->state, 0, ((size_t)g.n_embd + 4) * sizeof(float));
+    c->n_hslots = g.n_ctx + 1;
+    if (cudaMallocHost(&c->h_st, sizeof(StepState) * (size_t)c->n_hslots) != cudaSuccess ||
+        cudaMallocHost(&c->h_state, ((size_t)g.n_embd + 4) * sizeof(float)) != cudaSuccess)
+        return "pinned host staging";
+    memset(c->h_st, 0, sizeof(StepState) * (size_t)c->n_hslots);
+    if (head) {
+        c->logits = c->dalloc<float>((size_t)g.n_vocab + 4);
+        if (!c->logits) return "logits";
+    }
+    if (layers) {
+        const size_t nl = (size_t)(c->last - c->first + 1);
+        c->qkv = c->dalloc<float>((size_t)qd + 2 * kvd + 4);
+        c->att = c->dalloc<float>((size_t)qd + 4);
+        c->h = c->dalloc<float>((size_t)g.n_ff + 4);
+        c->gtmp = c->dalloc<float>((size_t)g.n_ff + 4);
+        c->utmp = c->dalloc<float>((size_t)g.n_ff + 4);
+        const size_t plane = (size_t)g.n_head_kv * g.n_ctx * hd;
+        c->kc = c->dalloc<float>(plane * nl);
+        c->vc = c->dalloc<float>(plane * nl);
+        if (!c->qkv || !c->att || !c->h || !c->gtmp || !c->utmp || !c->kc || !c->vc)
+            return "KV cache and layer buffers";
+    }
+    return nullptr;
+}
+
 static int ctx_open_impl(ecu_ctx **out, const ecu_model *m, int stage, int first, int last, int n_ctx,
                          int device, char *err, size_t errlen);
 
@@ -967,27 +1049,10 @@ static int ctx_open_impl(ecu_ctx **out, const ecu_model *m, int stage, int first
         ecu_set_error(err, errlen, "out of device memory (%s) after %zu bytes", what, c->bytes);
         return -1;
     };
-    const int wide = g.n_ff > g.n_embd ? g.n_ff : g.n_embd;
-
-    // work buffers
-    c->state = c->dalloc<float>((size_t)g.n_embd + 4);
-    c->st = c->dalloc<StepState>(1);
-    c->tok_hist = c->dalloc<int>((size_t)g.n_ctx + 1);
-    c->scr.xn = c->dalloc<float>((size_t)wide + 4);
-    c->scr.part_val = c->dalloc<float>(4096);
-    c->scr.part_idx = c->dalloc<int>(4096);
-    c->scr.counter = c->dalloc<unsigned>(4);
-    c->scr.status = &c->st->status;
-    if (!c->state || !c->st || !c->tok_hist || !c->scr.xn || !c->scr.part_val || !c->scr.part_idx || !c->scr.counter)
-        return fail_oom("work buffers");
-    cudaMemset(c->st, 0, sizeof(StepState));
-    cudaMemset(c->scr.counter, 0, 4 * sizeof(unsigned));
-    cudaMemset(c->state, 0, ((size_t)g.n_embd + 4) * sizeof(float));
-    c->n_hslots = g.n_ctx + 1;
-    if (cudaMallocHost(&c->h_st, sizeof(StepState) * (size_t)c->n_hslots) != cudaSuccess ||
-        cudaMallocHost(&c->h_state, ((size_t)g.n_embd + 4) * sizeof(float)) != cudaSuccess)
-        return fail_oom("pinned host staging");
-    memset(c->h_st, 0, sizeof(StepState) * (size_t)c->n_hslots);
+    if (const char *what = alloc_buffers(c.get(), !st.layers.empty(), st.out != nullptr)) return fail_oom(what);
+    c->shared = std::make_shared<SharedAllocs>();
+    c->shared->device = device;
+    c->to_shared = true;
 
     if (st.emb) {
         c->emb = make_mat(c.get(), (int)st.emb->type, g.n_embd, g.n_vocab, false);
@@ -1000,21 +1065,12 @@ static int ctx_open_impl(ecu_ctx **out, const ecu_model *m, int stage, int first
         if (!c->out.zero && !c->out.data) return fail_oom("output");
         if (upload_rows(c.get(), st.out, g.n_embd, g.n_vocab, c->out, 0, 1, stage_buf)) return -1;
         c->out_norm = upload_vec(c.get(), st.out_norm, (size_t)g.n_embd, stage_buf);
-        c->logits = c->dalloc<float>((size_t)g.n_vocab + 4);
-        if (!c->out_norm || !c->logits) return fail_oom("head buffers");
+        if (!c->out_norm) return fail_oom("head buffers");
         if (st.out->name == "output.weight" || !st.emb)
             c->srcs.push_back({st.out->name, c->out, 0, 1, (size_t)g.n_embd * g.n_vocab, g.n_embd});
     }
     if (!st.layers.empty()) {
         const size_t nl = st.layers.size();
-        c->qkv = c->dalloc<float>((size_t)qd + 2 * kvd + 4);
-        c->att = c->dalloc<float>((size_t)qd + 4);
-        c->h = c->dalloc<float>((size_t)g.n_ff + 4);
-        c->gtmp = c->dalloc<float>((size_t)g.n_ff + 4);
-        c->utmp = c->dalloc<float>((size_t)g.n_ff + 4);
-        const size_t plane = (size_t)g.n_head_kv * g.n_ctx * hd;
-        c->kc = c->dalloc<float>(plane * nl);
-        c->vc = c->dalloc<float>(plane * nl);
         // position splits per KV head = the cluster size (<= 16, <= one
         // CTA per SM over all heads, all clusters resident at once)
         int max_split = c->sms / g.n_head_kv;
@@ -1023,8 +1079,7 @@ static int ctx_open_impl(ecu_ctx **out, const ecu_model *m, int stage, int first
         c->n_split = attn_cluster(hd, g.n_rep, g.n_head_kv, max_split);
         cudaGetLastError();
         c->rope_cs = c->dalloc<float>((size_t)g.n_ctx * hd);
-        if (!c->qkv || !c->att || !c->h || !c->gtmp || !c->utmp || !c->kc || !c->vc || !c->rope_cs)
-            return fail_oom("KV cache and layer buffers");
+        if (!c->rope_cs) return fail_oom("RoPE table");
         // RoPE table with the host libm, exactly as src/engine.c:371-373
         {
             std::vector<float> cs((size_t)g.n_ctx * hd);
@@ -1203,20 +1258,71 @@ int ecu_forward_dev(ecu_ctx *c, int token, void *stream)
     if (!c) return -1;
     cudaSetDevice(c->device);
     if (step_check(c, token) != 0) return -1;
-    cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
-    if (s != c->stream) {
-        // order the context's stream after the caller's work, and back
-        cudaEvent_t ev;
-        CK(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
-        CK(cudaEventRecord(ev, s));
-        CK(cudaStreamWaitEvent(c->stream, ev, 0));
-        if (enqueue_forward(c, token) != 0) { cudaEventDestroy(ev); return -1; }
-        CK(cudaEventRecord(ev, c->stream));
-        CK(cudaStreamWaitEvent(s, ev, 0));
-        cudaEventDestroy(ev);
-        return 0;
+    return on_stream(c, stream, [&] { return enqueue_forward(c, token); });
+}
+
+int *ecu_token_ptr(ecu_ctx *c) { return c && c->st ? &c->st->token : nullptr; }
+
+int ecu_step_dev(ecu_ctx *c, void *stream)
+{
+    if (!c) return -1;
+    cudaSetDevice(c->device);
+    if ((c->stage == ECU_STAGE_LAYERS || c->stage == ECU_STAGE_FULL) && c->pos >= c->g.n_ctx) {
+        ecu_set_error(nullptr, 0, "context exhausted (%d positions)", c->g.n_ctx);
+        return -1;
     }
-    return enqueue_forward(c, token);
+    return on_stream(c, stream, [&] {
+        // the position comes from the host; the token stays where the
+        // previous step (or the caller) left it in device memory
+        StepState *slot = c->h_st + (c->pos % c->n_hslots);
+        slot->pos = c->pos;
+        CK(cudaMemcpyAsync(&c->st->pos, &slot->pos, sizeof(int), cudaMemcpyHostToDevice, c->stream));
+        if (run_step(c) != 0) return -1;
+        if (c->stage == ECU_STAGE_LAYERS || c->stage == ECU_STAGE_FULL) c->pos++;
+        if (c->stage == ECU_STAGE_HEAD || c->stage == ECU_STAGE_FULL) c->have_logits = true;
+        return 0;
+    });
+}
+
+int ecu_ctx_fork(ecu_ctx **out, ecu_ctx *base, char *err, size_t errlen)
+{
+    if (err && errlen) err[0] = '\0';
+    if (!out || !base) { ecu_set_error(err, errlen, "null argument"); return -1; }
+    *out = nullptr;
+    if (cudaSetDevice(base->device) != cudaSuccess) { ecu_set_error(err, errlen, "cudaSetDevice(%d) failed", base->device); return -1; }
+    std::unique_ptr<ecu_ctx, void (*)(ecu_ctx *)> c(new ecu_ctx(), ctx_free);
+    c->device = base->device;
+    c->sms = base->sms;
+    c->stage = base->stage;
+    c->first = base->first;
+    c->last = base->last;
+    c->g = base->g;
+    c->pdl = base->pdl;
+    c->use_graph = base->use_graph;
+    c->shared = base->shared;
+    c->layers = base->layers;
+    c->emb = base->emb;
+    c->out = base->out;
+    c->out_norm = base->out_norm;
+    c->rope_cs = base->rope_cs;
+    c->n_split = base->n_split;
+    c->srcs = base->srcs;
+    if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
+        ecu_set_error(err, errlen, "cudaStreamCreate failed");
+        return -1;
+    }
+    const bool layers = c->stage == ECU_STAGE_LAYERS || c->stage == ECU_STAGE_FULL;
+    const bool head = c->stage == ECU_STAGE_HEAD || c->stage == ECU_STAGE_FULL;
+    if (const char *what = alloc_buffers(c.get(), layers, head)) {
+        ecu_set_error(err, errlen, "out of device memory (%s) after %zu bytes", what, c->bytes);
+        return -1;
+    }
+    if (cudaDeviceSynchronize() != cudaSuccess || cudaGetLastError() != cudaSuccess) {
+        ecu_set_error(err, errlen, "fork failed: %s", cudaGetErrorString(cudaGetLastError()));
+        return -1;
+    }
+    *out = c.release();
+    return 0;
 }
 
 // Eager (non-graph) run of an explicit layer list; pos unchanged.

@@ -61,7 +61,9 @@ struct GemvArgs {
 // contiguous segment [v*seg, (v+1)*seg), seg = ceil(n/256) -- combined by a
 // fixed tree, so every kernel that calls this gets the same bits whatever its
 // block size.  Each partial's loads are independent (one memory round trip).
-// Threads [0, nthreads) must all call it; `bar` synchronises them.
+// Threads [0, nthreads) must all call it; `bar` synchronises them.  x is
+// read through L2 (ld.global.cg): in the persistent step kernel other CTAs
+// wrote it since this SM last looked.
 template <class Bar>
 __device__ float rms_scale(const float *x, int n, float eps, double *dsum, int tid,
                            int nthreads, Bar bar)
@@ -78,7 +80,7 @@ __device__ float rms_scale(const float *x, int n, float eps, double *dsum, int t
                 const int m = min(8, nq - base);
 #pragma unroll
                 for (int k = 0; k < 8; k++)
-                    if (k < m) buf[k] = x4[base + k];
+                    if (k < m) buf[k] = __ldcg(x4 + base + k);
 #pragma unroll
                 for (int k = 0; k < 8; k++)
                     if (k < m) {
@@ -91,7 +93,7 @@ __device__ float rms_scale(const float *x, int n, float eps, double *dsum, int t
             }
         } else {
             for (int i = lo; i < hi; i++) {
-                const double xv = (double)x[i];
+                const double xv = (double)__ldcg(x + i);
                 p += xv * xv;
             }
         }
@@ -281,11 +283,15 @@ __device__ __forceinline__ void make_digits(const float *xv, int (&xw)[3][8], in
                                             float &sxs)
 {
     float amax = 0.0f;
+    bool  nan = false;
 #pragma unroll
-    for (int k = 0; k < 32; k++) amax = fmaxf(amax, fabsf(xv[k]));
+    for (int k = 0; k < 32; k++) {
+        amax = fmaxf(amax, fabsf(xv[k]));
+        nan |= xv[k] != xv[k];
+    }
     int   e = 0;
     float inv = 0.0f;
-    if (!(amax < INFINITY)) {
+    if (nan || !(amax < INFINITY)) {
         sxs = __int_as_float(0x7fc00000);   // inf/NaN in x: let the row come out NaN
     } else if (amax > 1e-30f) {
         frexpf(amax, &e);                   // amax < 2^e

@@ -6,11 +6,19 @@
 // out[i] = element token*n + i of the embedding tensor (src/engine.c:472-484:
 // row_to_float(t, out, token*ne, ne)).  The token comes from device state so
 // that a graph replay picks up the argmax of the previous step.
-static __global__ void k_embed(DevMat emb, const StepState *st, float *out, int n)
+static __global__ void k_embed(DevMat emb, StepState *st, float *out, int n)
 {
     pdl_wait();
     pdl_trigger();
-    const size_t base = (size_t)st->token * (size_t)n;
+    // the token may come from device memory (another stage's argmax, a
+    // receive): one outside the vocabulary flags the step instead of reading
+    // past the table
+    const int tok = st->token;
+    if (tok < 0 || tok >= emb.n_out) {
+        if (blockIdx.x == 0 && threadIdx.x == 0) atomicOr(&st->status, ECU_STATUS_BADTOKEN);
+        return;
+    }
+    const size_t base = (size_t)tok * (size_t)n;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
         const size_t a = base + (size_t)i;
         out[i] = mat_elem(emb, (int)(a / (size_t)emb.n_in), (int)(a % (size_t)emb.n_in));

@@ -76,6 +76,9 @@ SIGNATURES = [
     ("ecu_set_pos", C.c_int, [C.c_void_p, C.c_int]),
     ("ecu_state_ptr", C.c_void_p, [C.c_void_p]),
     ("ecu_forward_dev", C.c_int, [C.c_void_p, C.c_int, C.c_void_p]),
+    ("ecu_token_ptr", C.c_void_p, [C.c_void_p]),
+    ("ecu_step_dev", C.c_int, [C.c_void_p, C.c_void_p]),
+    ("ecu_ctx_fork", C.c_int, [C.POINTER(C.c_void_p), C.c_void_p, C.c_char_p, C.c_size_t]),
     ("ecu_generate", C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
     ("ecu_decode_async", C.c_int, [C.c_void_p, C.c_int]),
     ("ecu_sync", C.c_int, [C.c_void_p]),
@@ -165,18 +168,22 @@ def ctx_bytes(model: GgufModel, stage: int, first: int = 0, last: int = 0, n_ctx
 class LlmCtx:
     """One engine stage resident on one GPU (llm_ctx, src/engine.h:46-70)."""
 
-    def __init__(self, model: GgufModel, stage: int, first: int = 0, last: int = 0, n_ctx: int = 0,
-                 device: int = 0):
+    def __init__(self, model: GgufModel | None, stage: int, first: int = 0, last: int = 0, n_ctx: int = 0,
+                 device: int = 0, fork_of: "LlmCtx | None" = None):
         self.h = C.c_void_p()
         err = C.create_string_buffer(512)
-        rc = lib().ecu_ctx_open(C.byref(self.h), model.h, stage, first, last, n_ctx, device, err, 512)
+        if fork_of is not None:
+            rc = lib().ecu_ctx_fork(C.byref(self.h), fork_of.h, err, 512)
+        else:
+            rc = lib().ecu_ctx_open(C.byref(self.h), model.h, stage, first, last, n_ctx, device, err, 512)
         if rc != 0:
             raise EngineError(err.value.decode(errors="replace") or last_error())
         i = EcuInfo()
         lib().ecu_ctx_info(self.h, C.byref(i))
         self.info = i
         self.n_embd, self.n_vocab, self.n_ctx = i.n_embd, i.n_vocab, i.n_ctx
-        self.stage = stage
+        self.stage = i.stage
+        self.device = i.device
 
     # --- reference API ---------------------------------------------------
     def forward(self, token: int, out: np.ndarray) -> int:
@@ -229,6 +236,19 @@ class LlmCtx:
 
     def forward_dev(self, token: int, stream: int | None = None) -> None:
         if lib().ecu_forward_dev(self.h, int(token), C.c_void_p(stream or 0)) != 0:
+            raise EngineError(last_error())
+
+    def fork(self) -> "LlmCtx":
+        """A context of the same stage sharing this one's weights, with its
+        own KV cache and stream (one per concurrent sequence)."""
+        return LlmCtx(None, self.stage, fork_of=self)
+
+    def token_ptr(self) -> int:
+        return int(lib().ecu_token_ptr(self.h) or 0)
+
+    def step_dev(self, stream: int | None = None) -> None:
+        """One step from device-resident input (ecu_step_dev)."""
+        if lib().ecu_step_dev(self.h, C.c_void_p(stream or 0)) != 0:
             raise EngineError(last_error())
 
     def state_ptr(self) -> int:

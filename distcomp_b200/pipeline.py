@@ -1,0 +1,481 @@
+"""Layer-pipelined decode over the GPUs of one node.
+
+The reference splits a model over nodes by contiguous layer ranges
+(split_stages, src/shard.c:358-437): an EMBED node, LAYERS nodes with
+ceil(remaining layers / remaining nodes) layers each, a HEAD node, with the
+fp32 state forwarded node to node over UDP and the argmax token sent back
+to the entry node (src/shard.c:865-966).  Here every GPU is one stage: the
+embedding folds into the first GPU and the head into the last (the
+reference's separate EMBED/HEAD nodes are a memory policy,
+src/shard.c:369-370, that 180 GB per GPU does not need), and the hops are
+NCCL send/recv over NVLink of the n_embd fp32 state (16 KB for dim 4096)
+and of the 4-byte token.
+
+Several independent sequences can be interleaved to keep every stage busy:
+each stage keeps one KV cache per sequence (ecu_ctx_fork shares the
+weights).  All ranks follow one tick schedule: in tick t, rank r works on
+sequence (t - r) mod P, P = max(n_seq, n_ranks), then every rank exchanges
+the messages the schedule names for that tick as one NCCL group.  The
+schedule is pure host arithmetic, identical on every rank, so sends and
+receives always pair up and no rank waits for a message nobody sends.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+
+# ----------------------------------------------------------------- layout --
+
+def split_stages(n_layer: int, n_nodes: int, cost=None, cap=None) -> list[tuple[int, int]]:
+    """Contiguous layer ranges for n_nodes LAYERS stages, by the rule of
+    src/shard.c:384-413: each stage takes ceil(remaining layers / remaining
+    stages), at most what leaves one layer for every later stage, shrunk
+    while cost(first, last) exceeds that stage's cap[k].  Raises ValueError
+    where the reference returns its errors (a stage that holds no layer,
+    layers left over)."""
+    if n_nodes < 1:
+        raise ValueError("need at least one stage")
+    out, l = [], 0
+    for k in range(n_nodes):
+        if l >= n_layer:
+            break
+        rem_layers, rem_nodes = n_layer - l, n_nodes - k
+        give = -(-rem_layers // rem_nodes)
+        give = min(give, rem_layers - (rem_nodes - 1))
+        give = max(give, 1)
+        if cost is not None and cap is not None:
+            while give >= 1 and cost(l, l + give - 1) > cap[k]:
+                give -= 1
+            if give < 1:
+                raise ValueError(f"stage {k} cannot hold layer {l}")
+        out.append((l, l + give - 1))
+        l += give
+    if l < n_layer:
+        raise ValueError(f"{l} of {n_layer} layers placed: add devices")
+    return out
+
+
+def split_by_bytes(layer_bytes: list[int], n_stages: int, head_bytes: int = 0,
+                   embed_bytes: int = 0) -> list[tuple[int, int]]:
+    """Contiguous layer ranges for n_stages GPUs that minimise the largest
+    per-token byte stream of a stage, when the first stage also reads the
+    embedding row and the last the output head.  Every stage gets at least
+    one layer.  (The reference's rule balances layer counts; with the head
+    folded into the last GPU, balancing bytes keeps that GPU from setting
+    the pipeline's pace.)"""
+    n = len(layer_bytes)
+    if not 1 <= n_stages <= n:
+        raise ValueError(f"{n_stages} stages for {n} layers")
+    pre = [0]
+    for b in layer_bytes:
+        pre.append(pre[-1] + b)
+
+    def stage_cost(k, a, b):            # layers a..b-1 on stage k
+        c = pre[b] - pre[a]
+        if k == 0:
+            c += embed_bytes
+        if k == n_stages - 1:
+            c += head_bytes
+        return c
+
+    def feasible(limit):
+        cuts, a = [], 0
+        for k in range(n_stages):
+            left = n_stages - k - 1          # stages after this one, one layer each at least
+            if k == n_stages - 1:
+                b = n
+                if b <= a or stage_cost(k, a, b) > limit:
+                    return None
+            else:
+                b = a + 1
+                if stage_cost(k, a, b) > limit:
+                    return None
+                while b + 1 <= n - left and stage_cost(k, a, b + 1) <= limit:
+                    b += 1
+            cuts.append((a, b - 1))
+            a = b
+        return cuts if a == n else None
+
+    lo = max(max(layer_bytes), head_bytes)
+    hi = pre[n] + head_bytes + embed_bytes
+    best = feasible(hi)
+    while lo < hi:                        # smallest feasible limit (integer bytes)
+        mid = (lo + hi) // 2
+        f = feasible(mid)
+        if f is not None:
+            best, hi = f, mid
+        else:
+            lo = mid + 1
+    f = feasible(lo)
+    return f if f is not None else best
+
+
+# --------------------------------------------------------------- schedule --
+
+@dataclass(frozen=True)
+class Msg:
+    src: int
+    dst: int
+    seq: int
+    kind: str            # "state" (rank r -> r+1) or "token" (last -> 0)
+
+
+class Schedule:
+    """Tick schedule of n_seq sequences through n_ranks stages, n_steps
+    tokens each (the first n_prompt of them fed from the prompt)."""
+
+    def __init__(self, n_ranks: int, n_seq: int, n_steps: int, n_prompt: int = 0, first_step: int = 0):
+        if n_ranks < 2:
+            raise ValueError("a pipeline needs at least two stages")
+        self.n_ranks, self.n_seq, self.n_steps = n_ranks, n_seq, n_steps
+        self.n_prompt, self.first_step = n_prompt, first_step
+        self.period = max(n_seq, n_ranks)
+        self.n_ticks = (n_steps - 1) * self.period + (n_seq - 1) + (n_ranks - 1) + 1 if n_steps > 0 else 0
+
+    def work(self, rank: int, tick: int):
+        """(seq, step) rank works on in this tick, or None."""
+        u = tick - rank
+        if u < 0:
+            return None
+        k, s = divmod(u, self.period)
+        if s >= self.n_seq or k >= self.n_steps:
+            return None
+        return s, self.first_step + k
+
+    def messages(self, tick: int) -> list[Msg]:
+        out = []
+        last = self.n_ranks - 1
+        for r in range(self.n_ranks):
+            w = self.work(r, tick)
+            if w is None:
+                continue
+            s, k = w
+            if r < last:
+                out.append(Msg(r, r + 1, s, "state"))
+            elif self.n_prompt <= k + 1 < self.first_step + self.n_steps:
+                # the next input token of s is this argmax (not a prompt token)
+                out.append(Msg(last, 0, s, "token"))
+        return out
+
+    def step_ticks(self, step: int) -> tuple[int, int]:
+        """Ticks [t0, t1) in which the ranks do `step` of every sequence in
+        steady state (P ticks per step)."""
+        t0 = (step - self.first_step) * self.period
+        return t0, t0 + self.period
+
+
+# ---------------------------------------------------------------- runtime --
+
+class Exchanger:
+    """Carries one tick's messages between stage runtimes."""
+
+    def exchange(self, msgs: list[Msg], stages: dict) -> None:
+        raise NotImplementedError
+
+
+class LoopbackExchanger(Exchanger):
+    """All ranks in this process: a message is a copy between their buffers."""
+
+    def exchange(self, msgs, stages):
+        for m in msgs:
+            src, dst = stages[m.src], stages[m.dst]
+            ss, ds = getattr(src, "stream", None), getattr(dst, "stream", None)
+            if ss is None:
+                dst.recv_buf(m.seq, m.kind).copy_(src.send_buf(m.seq, m.kind))
+                continue
+            import torch
+            # the receiver's stream copies once the sender's output is
+            # written; the sender reuses its buffer only after the copy
+            ds.wait_stream(ss)
+            with torch.cuda.stream(ds):
+                dst.recv_buf(m.seq, m.kind).copy_(src.send_buf(m.seq, m.kind))
+            ss.wait_stream(ds)
+
+
+class DistExchanger(Exchanger):
+    """One rank per process over torch.distributed (NCCL between GPUs, gloo
+    on the host): the tick's sends and receives of this rank as one group."""
+
+    def __init__(self, rank: int):
+        self.rank = rank
+
+    def exchange(self, msgs, stages):
+        import torch.distributed as dist
+        me = stages[self.rank]
+        ops = []
+        for m in msgs:
+            if m.src == self.rank:
+                ops.append(dist.P2POp(dist.isend, me.send_buf(m.seq, m.kind), m.dst))
+            elif m.dst == self.rank:
+                ops.append(dist.P2POp(dist.irecv, me.recv_buf(m.seq, m.kind), m.src))
+        if ops:
+            for w in dist.batch_isend_irecv(ops):
+                w.wait()
+
+
+def run_ticks(sched: Schedule, stages: dict, exchanger: Exchanger, prompts=None, t0: int = 0,
+              t1: int | None = None, on_tick=None) -> None:
+    """Drive the local stages through ticks [t0, t1) of the schedule.
+    stages: {rank: runtime} for the ranks of this process.  prompts[s][k] is
+    fed as input token of step k of sequence s while k < sched.n_prompt."""
+    t1 = sched.n_ticks if t1 is None else t1
+    for t in range(t0, t1):
+        for r, st in stages.items():
+            w = sched.work(r, t)
+            if w is None:
+                continue
+            s, k = w
+            if r == 0 and k < sched.n_prompt:
+                st.set_token(s, k)
+            st.run(s, k)
+        exchanger.exchange(sched.messages(t), stages)
+        if on_tick is not None:
+            on_tick(t)
+
+
+class GpuStage:
+    """One rank's stage on one GPU: per sequence a chain of engine contexts
+    [EMBED] + LAYERS(first..last) + [HEAD], forks of sequence 0's chain, all
+    enqueued on one torch stream.  Input/output buffers are zero-copy torch
+    views of the contexts' device state (ecu_state_ptr / ecu_token_ptr)."""
+
+    def __init__(self, model, rank: int, n_ranks: int, first: int, last: int, n_layer: int, n_seq: int,
+                 n_ctx: int, device: int, prompts=None):
+        import torch
+        from . import engine as E
+        self.rank, self.n_ranks, self.device = rank, n_ranks, device
+        self.torch = torch
+        self.dev = torch.device("cuda", device)
+        base = []
+        if first == 0:
+            base.append(E.LlmCtx(model, E.STAGE_EMBED, 0, 0, n_ctx, device))
+        base.append(E.LlmCtx(model, E.STAGE_LAYERS, first, last, n_ctx, device))
+        if last == n_layer - 1:
+            base.append(E.LlmCtx(model, E.STAGE_HEAD, 0, 0, n_ctx, device))
+        self.chains = [base] + [[c.fork() for c in base] for _ in range(n_seq - 1)]
+        self.n_embd = base[0].n_embd
+        self.has_embed, self.has_head = first == 0, last == n_layer - 1
+        self.stream = torch.cuda.Stream(device=self.dev)
+        self._state = [[device_view(c.state_ptr(), self.n_embd + 1, "<f4", device) for c in ch]
+                       for ch in self.chains]
+        self._token = [[device_view(c.token_ptr(), 1, "<i4", device) for c in ch] for ch in self.chains]
+        self.prompts = None
+        if prompts is not None:
+            self.prompts = torch.tensor(prompts, dtype=torch.int32, device=self.dev)
+        self.history = None
+
+    def record_tokens(self, n_steps: int):
+        """Keep every argmax in a device table [n_seq, n_steps] (last stage)."""
+        self.history = self.torch.zeros((len(self.chains), n_steps), dtype=self.torch.int32, device=self.dev)
+
+    # buffers the exchanger reads and writes
+    def send_buf(self, s: int, kind: str):
+        return self._token[s][-1] if kind == "token" else self._state[s][-1][: self.n_embd]
+
+    def recv_buf(self, s: int, kind: str):
+        return self._token[s][0] if kind == "token" else self._state[s][0][: self.n_embd]
+
+    def set_token(self, s: int, k: int):
+        with self.torch.cuda.stream(self.stream):
+            self._token[s][0].copy_(self.prompts[s, k: k + 1])
+
+    def run(self, s: int, k: int):
+        torch = self.torch
+        ch = self.chains[s]
+        sp = self.stream.cuda_stream
+        with torch.cuda.stream(self.stream):
+            for i, c in enumerate(ch):
+                if i > 0:
+                    self._state[s][i][: self.n_embd].copy_(self._state[s][i - 1][: self.n_embd])
+                c.step_dev(sp)
+            if self.has_head and self.history is not None and k < self.history.shape[1]:
+                self.history[s, k: k + 1].copy_(self._token[s][-1])
+
+    def reset(self):
+        for ch in self.chains:
+            for c in ch:
+                c.reset()
+
+    def sync(self):
+        self.stream.synchronize()
+        for ch in self.chains:
+            for c in ch:
+                c.sync()
+
+    def close(self):
+        for ch in reversed(self.chains):
+            for c in ch:
+                c.close()
+
+
+def device_view(ptr: int, n: int, typestr: str, device: int):
+    """A torch tensor over n elements of device memory owned by the engine
+    (no copy, no ownership)."""
+    import torch
+
+    class _View:
+        __cuda_array_interface__ = {"shape": (n,), "typestr": typestr, "data": (int(ptr), False),
+                                    "version": 3, "strides": None}
+
+    if not ptr:
+        raise ValueError("null device pointer")
+    return torch.as_tensor(_View(), device=torch.device("cuda", device))
+
+
+# ------------------------------------------------------------------ bench --
+
+def bench_main(args, rank: int, world: int, local: int, B) -> int:
+    """bench.py at N > 1: the 8B decode pipelined over `world` GPUs.  B is
+    the bench module (metric, config, clock sampler, byte counts)."""
+    import datetime
+    import json
+    import time
+    import torch
+    import torch.distributed as dist
+    from . import engine as E
+    from . import synth
+
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", local),
+                            timeout=datetime.timedelta(seconds=180))
+    try:
+        spec = synth.spec(B.CONFIG, **({"n_layer": args.layers} if args.layers else {}))
+        buf = B.build_model_gpu(spec, args.seed, local)
+        model = E.GgufModel(buf)
+        lb = layer_bytes(spec)
+        head_b = tensor_bytes(spec, "output.weight") + tensor_bytes(spec, "output_norm.weight")
+        emb_row = tensor_bytes(spec, "token_embd.weight") // spec.n_vocab
+        if args.split == "ref":
+            plan = split_stages(spec.n_layer, world)
+        else:
+            plan = split_by_bytes(lb, world, head_bytes=head_b, embed_bytes=emb_row)
+        first, last = plan[rank]
+        n_seq = args.seqs
+        prompts = [synth.prompt_tokens(args.prompt, spec.n_vocab, seed=args.seed + 1 + s) for s in range(n_seq)]
+        n_tok = args.prompt + args.warmup + 2 * args.steps + 2
+        if n_tok > args.n_ctx:
+            raise SystemExit(f"prompt + steps need {n_tok} positions > n_ctx {args.n_ctx}")
+        st = GpuStage(model, rank, world, first, last, spec.n_layer, n_seq, args.n_ctx, local,
+                      prompts=prompts if rank == 0 else None)
+        del buf
+        torch.cuda.empty_cache()
+        ex = DistExchanger(rank)
+        stages = {rank: st}
+        dist.barrier()
+
+        def timed(sched, t0, t1, host_tokens=False):
+            """Device time of ticks [t0, t1) on this rank, max over ranks (ms)."""
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            dist.barrier()
+            torch.cuda.synchronize(local)
+            h0 = time.perf_counter()
+            ev0.record(st.stream)
+            if host_tokens and st.has_head:
+                pinned = torch.zeros(n_seq, dtype=torch.int32, pin_memory=True)
+
+                def tick(t):
+                    w = sched.work(rank, t)
+                    if w is not None and w[0] == n_seq - 1:      # a step of every sequence done
+                        with torch.cuda.stream(st.stream):
+                            for s in range(n_seq):
+                                pinned[s: s + 1].copy_(st._token[s][-1], non_blocking=True)
+                        st.stream.synchronize()
+                run_ticks(sched, stages, ex, t0=t0, t1=t1, on_tick=tick)
+            else:
+                run_ticks(sched, stages, ex, t0=t0, t1=t1)
+            ev1.record(st.stream)
+            torch.cuda.synchronize(local)
+            host_s = time.perf_counter() - h0
+            dist.barrier()
+            ms = torch.tensor([ev0.elapsed_time(ev1), host_s * 1e3], dtype=torch.float64, device=st.dev)
+            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+            return float(ms[0]), float(ms[1])
+
+        # (1) one sequence alone: the batch-1 latency through all stages
+        s1 = Schedule(world, 1, args.prompt + args.warmup + args.steps, n_prompt=args.prompt)
+        w0 = s1.step_ticks(args.prompt + args.warmup)[0]
+        run_ticks(s1, stages, ex, t0=0, t1=w0)
+        ms1, _ = timed(s1, w0, s1.n_ticks)
+        b1_tps = args.steps / (ms1 / 1e3)
+        st.sync()
+        st.reset()
+
+        # (2) n_seq interleaved sequences: prompt, warm-up, timed, end-to-end
+        total = args.prompt + args.warmup + 2 * args.steps
+        sched = Schedule(world, n_seq, total, n_prompt=args.prompt)
+        ta = sched.step_ticks(args.prompt + args.warmup)[0]
+        tb = sched.step_ticks(args.prompt + args.warmup + args.steps)[0]
+        run_ticks(sched, stages, ex, t0=0, t1=ta)
+        l0 = E.kernel_launches()
+        clocks = B.ClockSampler(local)
+        if rank == 0:
+            clocks.start()
+        ms, _ = timed(sched, ta, tb)
+        launches = E.kernel_launches() - l0
+        clk = clocks.stop() if rank == 0 else None
+        _, e2e_ms = timed(sched, tb, sched.n_ticks, host_tokens=True)
+        st.sync()
+        lt = torch.tensor([launches], dtype=torch.int64, device=st.dev)
+        dist.all_reduce(lt)
+        tps = n_seq * args.steps / (ms / 1e3)
+        # tokens completed in the end-to-end window: every step after tb
+        e2e_steps = total - (args.prompt + args.warmup + args.steps)
+        e2e = n_seq * e2e_steps / (e2e_ms / 1e3)
+
+        if rank == 0:
+            peak, peak_kind = B.peaks()
+            bpt = B.algorithmic_bytes_per_token(spec, args.prompt + args.warmup + (args.steps - 1) / 2)
+            line = {
+                "metric": B.METRIC, "value": round(tps, 2), "unit": "tokens/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+                "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "q4_0 codes x int8 digit planes, fp32 accumulate",
+                "data": "synthetic: seeded N(0,0.02) weights quantised to Q4_0/Q8_0 on the GPU, random prompts",
+                "config": {"workload": f"llama3-8b-shape Q4_0 decode, layer pipeline over {world} GPUs "
+                                       f"(shard.c stage layout, NCCL send/recv hops), {n_seq} interleaved "
+                                       f"sequences; a step = one token of every sequence",
+                           "stages": [list(p) for p in plan], "split": args.split,
+                           "sequences": n_seq, "prompt_tokens": args.prompt, "n_ctx": args.n_ctx,
+                           "l2": "inputs larger than L2 (4.49 GB of weights per token)"},
+                "token_roofline": {"bytes_per_token": bpt, "achieved_gbs": round(bpt * tps / 1e9, 1),
+                                   "peak_gbs": peak * world, "frac": round(bpt * tps / 1e9 / (peak * world), 4),
+                                   "peak_kind": peak_kind},
+                "pp_batch1": {"value": round(b1_tps, 2), "unit": "tokens/s",
+                              "frac": round(bpt * b1_tps / 1e9 / peak, 4),
+                              "note": "one sequence: one stage busy at a time"},
+                "e2e": {"value": round(e2e, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 4 * n_seq,
+                        "api": "ecu_step_dev chain per stage; the last stage copies every step's tokens to "
+                               "host and waits for them"},
+                "gpu_launches": int(lt.item()),
+                "clocks": clk,
+            }
+            print(json.dumps(line), flush=True)
+        st.close()
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+    return 0
+
+
+def layer_bytes(spec) -> list[int]:
+    from . import synth
+    from . import gguf as G
+    per = [0] * spec.n_layer
+    for name, dims, gt in synth.tensor_list(spec):
+        if name.startswith("blk."):
+            i = int(name.split(".")[1])
+            per[i] += G.type_nbytes(gt, math.prod(dims))
+    return per
+
+
+def tensor_bytes(spec, name: str) -> int:
+    from . import synth
+    from . import gguf as G
+    for n, dims, gt in synth.tensor_list(spec):
+        if n == name:
+            return G.type_nbytes(gt, math.prod(dims))
+    if name == "output.weight":                # tied: the head reads token_embd
+        return tensor_bytes(spec, "token_embd.weight")
+    return 0

@@ -112,6 +112,26 @@ float *ecu_state_ptr(ecu_ctx *c);
  * enqueued on `stream` (NULL = the context's stream), not synchronised.
  * The token is read from host memory at enqueue time. */
 int  ecu_forward_dev(ecu_ctx *c, int token, void *stream);
+/* Device address of the context's current token (one int).  EMBED and FULL
+ * steps read their input token there; HEAD and FULL steps write their argmax
+ * there.  A pipeline hands the token from the last stage to the first by
+ * writing this address (a device copy or an NCCL receive), the way the
+ * reference's shard.c sends the argmax back to the entry node. */
+int *ecu_token_ptr(ecu_ctx *c);
+/* One step from device-resident input only: the token at ecu_token_ptr(c)
+ * (EMBED/FULL) or the state at ecu_state_ptr(c) (LAYERS/HEAD), output left
+ * in the state buffer (and the token word for HEAD/FULL), position advanced.
+ * Enqueued on `stream` (NULL = the context's stream), not synchronised; a
+ * token outside the vocabulary is reported by the next ecu_sync.  -1 when
+ * the context is exhausted. */
+int  ecu_step_dev(ecu_ctx *c, void *stream);
+/* A second context of the same stage on the same device that shares the
+ * first one's uploaded weights and keeps its own KV cache, position, work
+ * buffers and stream: one per concurrent sequence (the reference keeps one
+ * llm_ctx per process, src/daemon.c:757; a GPU stage serving several
+ * interleaved sequences needs one cache each).  The weights are freed when
+ * the last context holding them closes. */
+int  ecu_ctx_fork(ecu_ctx **out, ecu_ctx *base, char *err, size_t errlen);
 /* Greedy decode on a FULL context without host round trips: feeds
  * prompt[0..n_prompt) token by token, then generates n_gen tokens, each one
  * fed back on the device.  out_tokens receives the n_gen generated ids.

@@ -1,0 +1,110 @@
+"""The layer pipeline on real kernels.
+
+On one GPU, the stages of a 2-, 3- and 4-way split run as separate stage
+runtimes in one process (their messages are device copies between the
+stages' streams); the interleaved sequences must produce exactly the
+greedy tokens and final logits of a FULL context fed the same prompt: a
+stage boundary moves the state between buffers but changes no arithmetic.
+With two or more GPUs, the same check runs as torchrun ranks over NCCL.
+"""
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from distcomp_b200 import pipeline as P
+from distcomp_b200 import synth
+
+pytestmark = pytest.mark.gpu
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def full_greedy(eng, m, prompt, n_gen, n_ctx):
+    c = eng.LlmCtx(m, eng.STAGE_FULL, n_ctx=n_ctx)
+    toks = c.generate(prompt, n_gen)
+    logits = c.logits()
+    c.close()
+    return toks, logits
+
+
+@pytest.mark.parametrize("n_ranks,n_seq", [(2, 1), (2, 3), (3, 2), (4, 4)])
+def test_loopback_pipeline_matches_full_context(eng, model_buf, n_ranks, n_seq):
+    key, over = "mini-q4", {"n_layer": 4}
+    s = synth.spec(key, **over)
+    buf = model_buf(key, **over)
+    m = eng.GgufModel(buf)
+    n_prompt, n_gen, n_ctx = 5, 12, 64
+    prompts = [synth.prompt_tokens(n_prompt, s.n_vocab, seed=11 + q) for q in range(n_seq)]
+    plan = P.split_stages(s.n_layer, n_ranks)
+    stages = {r: P.GpuStage(m, r, n_ranks, a, b, s.n_layer, n_seq, n_ctx, 0, prompts=prompts)
+              for r, (a, b) in enumerate(plan)}
+    n_steps = n_prompt + n_gen - 1
+    stages[n_ranks - 1].record_tokens(n_steps)
+    S = P.Schedule(n_ranks, n_seq, n_steps, n_prompt=n_prompt)
+    P.run_ticks(S, stages, P.LoopbackExchanger())
+    for st in stages.values():
+        st.sync()
+    hist = stages[n_ranks - 1].history.cpu().numpy()
+    last = stages[n_ranks - 1]
+    for q in range(n_seq):
+        want, want_logits = full_greedy(eng, m, prompts[q], n_gen, n_ctx)
+        got = [int(t) for t in hist[q, n_prompt - 1:]]
+        assert got == want, (q, got, want)
+        got_logits = last.chains[q][-1].logits()
+        assert np.array_equal(got_logits.view(np.uint32), want_logits.view(np.uint32))
+    for st in stages.values():
+        st.close()
+
+
+def test_step_dev_rejects_bad_device_token(eng, model_buf):
+    """A token outside the vocabulary that arrives in device memory (not
+    through the host checks) is reported by ecu_sync instead of read."""
+    buf = model_buf("mini-q4")
+    m = eng.GgufModel(buf)
+    c = eng.LlmCtx(m, eng.STAGE_EMBED, n_ctx=16)
+    tok = P.device_view(c.token_ptr(), 1, "<i4", 0)
+    tok.fill_(10 ** 6)
+    torch.cuda.synchronize()
+    c.step_dev()
+    with pytest.raises(eng.EngineError, match="vocabulary"):
+        c.sync()
+    tok.fill_(7)
+    torch.cuda.synchronize()
+    c.step_dev()
+    c.sync()
+    c.close()
+
+
+def test_fork_shares_weights_and_keeps_own_cache(eng, model_buf):
+    s = synth.spec("mini-q4")
+    m = eng.GgufModel(model_buf("mini-q4"))
+    a = eng.LlmCtx(m, eng.STAGE_FULL, n_ctx=32)
+    b = a.fork()
+    assert b.info.device_bytes < a.info.device_bytes / 2
+    pa, pb = synth.prompt_tokens(4, s.n_vocab, seed=1), synth.prompt_tokens(4, s.n_vocab, seed=2)
+    ta = a.generate(pa, 6)
+    tb = b.generate(pb, 6)
+    a.close()                       # the fork keeps the shared weights alive
+    assert b.generate(pa, 6) != [] and b.pos == 18
+    ref = eng.LlmCtx(m, eng.STAGE_FULL, n_ctx=32)
+    assert ref.generate(pb, 6) == tb
+    ref.reset()
+    assert ref.generate(pa, 6) == ta
+    b.close()
+    ref.close()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_nccl_pipeline_two_gpus(tmp_path):
+    """bench.py's pipeline path at a small size over two real ranks."""
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr=127.0.0.1", "--master-port=29531", str(ROOT / "tests" / "pipeline_ranks.py"),
+           str(tmp_path)]
+    r = subprocess.run(["timeout", "-k", "30", "600"] + cmd, env=env, capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
+    assert (tmp_path / "ok").exists()

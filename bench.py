@@ -176,10 +176,10 @@ def build_model_gpu(spec, seed, device):
     return buf
 
 
-def load_traffic():
+def load_traffic(name: str):
     """dram bytes per launch of the dominant kernel from the committed ncu
     summary, when one exists."""
-    p = ROOT / "profiles" / "gemv_gate_up_q4_0_8b.json"
+    p = ROOT / "profiles" / name
     if p.exists():
         try:
             d = json.loads(p.read_text())
@@ -232,14 +232,20 @@ def our_arm(args, rank, world, local):
     ms = e0.elapsed_time(e1)
     tps = args.steps / (ms / 1e3)
 
-    # dominant-kernel roofline from a profiling replay (events per launch)
+    # dominant-kernel roofline from a profiling replay: the persistent step
+    # kernel when the context runs one (events around each launch), else the
+    # fused gate/up GEMV (events around every kernel)
     prof = ctx.profile_steps(args.profile_steps)
     peak, peak_kind = peaks()
-    dom = "gemv_gate_up"
+    if "decode_step" in prof:
+        dom, kname = "decode_step", "k_decode_mega<128, 4> (persistent kernel: the whole token step)"
+        traffic, scaled = load_traffic("decode_step_mega_8b.json")
+    else:
+        dom, kname = "gemv_gate_up", "k_gemv_fast<Q4_0, rmsnorm, swiglu> (fused ffn_gate+ffn_up)"
+        traffic, scaled = load_traffic("gemv_gate_up_q4_0_8b.json")
     n_l, tot_ms, bpl = prof[dom]
     avg_ms = tot_ms / n_l
     achieved = bpl / (avg_ms / 1e3) / 1e9
-    traffic, scaled = load_traffic()
 
     # end to end through the C ABI with host buffers
     out = np.zeros(spec.n_embd + 1, dtype=np.float32)
@@ -265,7 +271,7 @@ def our_arm(args, rank, world, local):
         "token_roofline": {"bytes_per_token": bpt, "achieved_gbs": round(bpt * tps / 1e9, 1),
                            "peak_gbs": peak, "frac": round(bpt * tps / 1e9 / peak, 4),
                            "frac_of_8tbs_nominal": round(bpt * tps / 1e9 / 8000, 4), "peak_kind": peak_kind},
-        "roofline": {"kernel": "k_gemv_fast<Q4_0, rmsnorm, swiglu> (fused ffn_gate+ffn_up)", "bound": "hbm",
+        "roofline": {"kernel": kname, "bound": "hbm",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic,
                      "bytes_per_launch": bpl, "avg_launch_us": round(avg_ms * 1e3, 2),
@@ -276,6 +282,7 @@ def our_arm(args, rank, world, local):
         "e2e": {"value": round(e2e, 2), "unit": "tokens/s", "h2d_bytes_per_step": 8,
                 "d2h_bytes_per_step": (spec.n_embd + 1) * 4, "api": "ecu_forward (FULL context)"},
         "gpu_launches": int(launches),
+        "step_path": ctx.path(),
         "clocks": clk,
         "setup_s": {"model_build": round(t_build, 1), "upload": round(t_up, 1)},
     }

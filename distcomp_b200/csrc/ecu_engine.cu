@@ -10,6 +10,7 @@
 #include "../../include/engine_cuda.h"
 #include "ecu_attn.cuh"
 #include "ecu_gemv.cuh"
+#include "ecu_mega.cuh"
 #include "ecu_misc.cuh"
 #include "ecu_model.h"
 
@@ -398,6 +399,16 @@ struct ecu_ctx {
     cudaGraphExec_t graph = nullptr;   // the full step
     int             graph_kernels = 0;
 
+    // persistent whole-step kernel (LAYERS / FULL stages that qualify)
+    bool        mega = false;
+    std::string path = "kernels";         // which step implementation runs, and why
+    void      (*mega_fn)(MegaArgs) = nullptr;
+    MegaArgs    margs{};
+    int         mega_grid = 0;
+    size_t      mega_smem = 0;
+    std::vector<const char *> ph_kind;    // per phase, for the profile
+    std::vector<double>       ph_bytes;
+
     struct SrcRef { std::string name; DevMat m; int row0, rstride; size_t elems; int n_in; };
     std::vector<SrcRef> srcs;
 
@@ -660,9 +671,18 @@ static int n_stage_layers(const ecu_ctx *c)
     return (c->stage == ECU_STAGE_LAYERS || c->stage == ECU_STAGE_FULL) ? c->last - c->first + 1 : 0;
 }
 
-// Enqueue one full step: graph replay when enabled (captured on first use).
+static int mega_launch(ecu_ctx *c, cudaStream_t s, unsigned long long *phase_ns,
+                       unsigned long long *detail = nullptr);
+
+// Enqueue one full step: the persistent kernel when the stage has one, else
+// a graph replay when enabled (captured on first use).
 static int run_step(ecu_ctx *c)
 {
+    if (c->mega) {
+        if (mega_launch(c, c->stream, nullptr) != 0) return -1;
+        g_launches += 1;
+        return 0;
+    }
     if (c->use_graph) {
         if (!c->graph) {
             cudaGraph_t gr;
@@ -705,6 +725,7 @@ static int check_status(ecu_ctx *c)
     StepState s;
     CK(cudaMemcpy(&s, c->st, sizeof s, cudaMemcpyDeviceToHost));
     if (s.status) {
+        if (c->mega) CK(cudaMemset(c->margs.bar, 0, (4 + (size_t)c->g.n_head_kv) * sizeof(unsigned)));
         if (s.status & ECU_STATUS_BADTOKEN)
             ecu_set_error(nullptr, 0, "the device-resident token is outside the vocabulary (%d)", c->g.n_vocab);
         else
@@ -730,6 +751,316 @@ template <class F> static int on_stream(ecu_ctx *c, void *stream, F enq)
     CK(cudaStreamWaitEvent(s, ev, 0));
     cudaEventDestroy(ev);
     return 0;
+}
+
+// ------------------------------------------------ persistent step kernel --
+
+typedef void (*MegaFn)(MegaArgs);
+
+static MegaFn mega_lookup(int hd, int rep)
+{
+    if (hd == 128 && rep == 4) return k_decode_mega<128, 4>;
+    if (hd == 128 && rep == 8) return k_decode_mega<128, 8>;
+    if (hd == 64 && rep == 4) return k_decode_mega<64, 4>;
+    return nullptr;
+}
+
+static size_t mega_smem_total(int hd, int red_floats)
+{
+    return hd == 128 ? mega_smem_plan<128>(red_floats).total : mega_smem_plan<64>(red_floats).total;
+}
+
+// Q4_0 rows in SPLIT4 or Q8_0 rows in SPLIT8, n_in a multiple of 1024.
+static bool mega_mat_ok(const DevMat &m)
+{
+    return fast_ok(m) && m.n_in / 32 <= MEGA_MAX_NB && m.row_bytes <= MEGA_RING_BYTES / 2 &&
+           ((m.type == GT_Q4_0 && m.layout == LAY_SPLIT4) || (m.type == GT_Q8_0 && m.layout == LAY_SPLIT8));
+}
+
+static MegaPhase mega_gemv_phase(const DevMat &m, int grid, unsigned stage_bytes, int norm, int epi,
+                                 const float *x, const float *norm_w, float *y, float *xn)
+{
+    MegaPhase p = {};
+    p.kind = PH_GEMV;
+    p.fmt = m.layout == LAY_SPLIT4 ? 4 : 8;
+    p.norm = norm;
+    p.epi = epi;
+    p.w = m.data;
+    p.row_bytes = (unsigned)m.row_bytes;
+    p.n_in = m.n_in;
+    p.n_out = m.n_out;
+    int rpc = (m.n_out + grid - 1) / grid;
+    if (epi == EPI_SWIGLU && (rpc & 1)) rpc++;        // whole gate/up pairs per CTA
+    p.rpc = rpc;
+    p.sr = (int)std::min<size_t>((size_t)rpc, stage_bytes / m.row_bytes);
+    p.nkg = m.n_in / 1024;
+    p.rowpar = std::max(1, MEGA_NCW / p.nkg);
+    p.x = x;
+    p.norm_w = norm_w;
+    p.y = y;
+    p.xn = xn;
+    return p;
+}
+
+// Build the phase list and buffers of the persistent kernel when the stage
+// qualifies (every projection fused and in a fast layout, an instantiated
+// head geometry, cooperative launch, the shared-memory plan fits).  Leaves
+// c->mega false otherwise: the per-kernel step serves the stage.
+static int mega_setup(ecu_ctx *c)
+{
+    c->mega = false;
+    auto no = [c](const char *why) {
+        c->path = std::string("kernels: ") + why;
+        return 0;
+    };
+    // opt-in (ECU_MEGA=1) until it beats the per-kernel step on the 8B shape
+    const char *env = getenv("ECU_MEGA");
+    if (!env || env[0] != '1') return no("ECU_MEGA=0");
+    if ((c->stage != ECU_STAGE_FULL && c->stage != ECU_STAGE_LAYERS) || c->layers.empty())
+        return no("stage without layers");
+    const EcuGeom &g = c->g;
+    const int hd = g.head_dim, qdim = g.n_head * hd, kvdim = g.n_head_kv * hd;
+    MegaFn fn = mega_lookup(hd, g.n_rep);
+    if (!fn) return no("head_dim / query heads per KV head not instantiated");
+    for (auto &ly : c->layers)
+        if (ly.qkv.size() != 1 || !ly.gu_fused || !mega_mat_ok(ly.qkv[0]) || !mega_mat_ok(ly.o) ||
+            !mega_mat_ok(ly.gu) || !mega_mat_ok(ly.d))
+            return no("a layer matrix is not Q4_0/Q8_0 in a fast layout");
+    const bool full = c->stage == ECU_STAGE_FULL;
+    if (full && !mega_mat_ok(c->out)) return no("output head not Q4_0/Q8_0 in a fast layout");
+    int coop = 0;
+    cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, c->device);
+    if (!coop) return no("no cooperative launch");
+    const int grid = c->sms;
+    // ring geometry: ECU_MEGA_RING stages (default 3) over MEGA_RING_BYTES
+    int nst = 3;
+    if (const char *r = getenv("ECU_MEGA_RING")) nst = std::max(2, std::min(MEGA_MAX_STAGES, atoi(r)));
+    const unsigned stage_bytes = (unsigned)(MEGA_RING_BYTES / nst) & ~127u;
+    for (auto &ly : c->layers)
+        if (ly.qkv[0].row_bytes > stage_bytes || ly.o.row_bytes > stage_bytes || ly.gu.row_bytes > stage_bytes ||
+            ly.d.row_bytes > stage_bytes)
+            return no("a weight row does not fit a ring stage");
+    if (full && c->out.row_bytes > stage_bytes) return no("a head row does not fit a ring stage");
+    // position splits per KV head: one item per CTA at most, and the split
+    // partials of a head group must fit the shared K/V buffers for the merge
+    const size_t un = std::max((size_t)MEGA_MAX_NB * 28 * sizeof(int),
+                               hd == 128 ? attn_smem_bytes<128>() : attn_smem_bytes<64>());
+    int n_split = std::min(MEGA_MAX_SPLIT, grid / g.n_head_kv);
+    n_split = std::min(n_split, (int)(un / ((size_t)g.n_rep * (hd + 4) * sizeof(float))));
+    n_split = std::max(1, std::min(n_split, g.n_ctx));
+
+    std::vector<MegaPhase> ph;
+    c->ph_kind.clear();
+    c->ph_bytes.clear();
+    auto add = [&](const MegaPhase &p, const char *kind, double bytes) {
+        ph.push_back(p);
+        c->ph_kind.push_back(kind);
+        c->ph_bytes.push_back(bytes);
+    };
+    c->to_shared = false;
+    float *xn_tmp = full ? c->dalloc<float>((size_t)g.n_embd + 4) : nullptr;
+    if (full) {
+        MegaPhase p = {};
+        p.kind = PH_EMBED;
+        add(p, "embed", 8.0 * g.n_embd + (double)ecu_type_nbytes(c->emb.type, (size_t)g.n_embd));
+    }
+    const size_t plane = (size_t)g.n_head_kv * g.n_ctx * hd;
+    for (size_t li = 0; li < c->layers.size(); li++) {
+        LayerDev &ly = c->layers[li];
+        add(mega_gemv_phase(ly.qkv[0], grid, stage_bytes, 1, EPI_STORE, c->state, ly.attn_norm, c->qkv, nullptr), "gemv_qkv",
+            gemv_bytes(ly.qkv[0], EPI_STORE));
+        MegaPhase at = {};
+        at.kind = PH_ATTN;
+        at.kc = c->kc + li * plane;
+        at.vc = c->vc + li * plane;
+        at.bq = ly.bq;
+        at.bk = ly.bk;
+        at.bv = ly.bv;
+        add(at, "attention", -1.0);                 // position dependent: filled in by the profile
+        add(mega_gemv_phase(ly.o, grid, stage_bytes, 0, EPI_ADD, c->att, nullptr, c->state, nullptr), "gemv_o",
+            gemv_bytes(ly.o, EPI_ADD));
+        add(mega_gemv_phase(ly.gu, grid, stage_bytes, 1, EPI_SWIGLU, c->state, ly.ffn_norm, c->h, nullptr), "gemv_gate_up",
+            gemv_bytes(ly.gu, EPI_SWIGLU));
+        add(mega_gemv_phase(ly.d, grid, stage_bytes, 0, EPI_ADD, c->h, nullptr, c->state, nullptr), "gemv_down",
+            gemv_bytes(ly.d, EPI_ADD));
+    }
+    (void)kvdim;
+    if (full)
+        add(mega_gemv_phase(c->out, grid, stage_bytes, 1, EPI_ARGMAX, c->state, c->out_norm, c->logits, xn_tmp),
+            "gemv_head_argmax", gemv_bytes(c->out, EPI_ARGMAX) + 4.0 * g.n_embd);
+    int red = 0;
+    for (auto &p : ph)
+        if (p.kind == PH_GEMV) red = std::max(red, p.rpc * p.nkg);
+    const size_t smem = mega_smem_total(hd, red);
+    cudaFuncAttributes fa;
+    int optin = 0;
+    if (cudaFuncGetAttributes(&fa, fn) != cudaSuccess ||
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, c->device) != cudaSuccess ||
+        smem + fa.sharedSizeBytes > (size_t)optin ||
+        cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
+        cudaGetLastError();
+        static char buf[160];
+        snprintf(buf, sizeof buf, "shared memory %zu + %zu B over the %d B limit", smem,
+                 (size_t)fa.sharedSizeBytes, optin);
+        return no(buf);
+    }
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, MEGA_THREADS, smem) != cudaSuccess ||
+        per_sm < 1) {
+        cudaGetLastError();
+        return no("no SM can hold one CTA of the persistent kernel");
+    }
+    MegaPhase *d_ph = c->dalloc<MegaPhase>(ph.size());
+    float *apart = c->dalloc<float>((size_t)g.n_head_kv * n_split * g.n_rep * (hd + 4));
+    float *pval = c->dalloc<float>((size_t)grid);
+    int *pidx = c->dalloc<int>((size_t)grid);
+    unsigned *ctr = c->dalloc<unsigned>(4 + (size_t)g.n_head_kv);
+    if (!d_ph || !apart || !pval || !pidx || !ctr || (full && !xn_tmp)) return -1;
+    CK(cudaMemcpy(d_ph, ph.data(), ph.size() * sizeof(MegaPhase), cudaMemcpyHostToDevice));
+    CK(cudaMemset(ctr, 0, (4 + (size_t)g.n_head_kv) * sizeof(unsigned)));
+    MegaArgs &a = c->margs;
+    a = MegaArgs{};
+    a.ph = d_ph;
+    a.n_ph = (int)ph.size();
+    a.emb = c->emb;
+    a.state = c->state;
+    a.qkv = c->qkv;
+    a.att = c->att;
+    a.apart = apart;
+    a.xn_tmp = xn_tmp;
+    a.part_val = pval;
+    a.part_idx = pidx;
+    a.bar = ctr;
+    a.ticket = ctr + 2;
+    a.att_ticket = ctr + 4;
+    a.st = c->st;
+    a.tok_hist = c->tok_hist;
+    a.status = &c->st->status;
+    a.rope_cs = c->rope_cs;
+    a.phase_ns = nullptr;
+    a.phase_detail = nullptr;
+    a.advance_pos = full ? 1 : 0;
+    a.layers_advance = full ? 0 : 1;
+    a.n_embd = g.n_embd;
+    a.n_head = g.n_head;
+    a.n_kv = g.n_head_kv;
+    a.n_ctx = g.n_ctx;
+    a.n_split = n_split;
+    a.red_floats = red;
+    a.nst = nst;
+    a.stage_bytes = stage_bytes;
+    a.eps = g.eps;
+    a.kscale = 1.0f / sqrtf((float)hd);
+    c->mega_fn = fn;
+    c->mega_grid = grid;
+    c->mega_smem = smem;
+    c->mega = true;
+    c->path = "persistent";
+    return 0;
+}
+
+// One step: a cooperative launch of the whole-step kernel on s.
+static int mega_launch(ecu_ctx *c, cudaStream_t s, unsigned long long *phase_ns, unsigned long long *detail)
+{
+    MegaArgs a = c->margs;
+    a.phase_ns = phase_ns;
+    a.phase_detail = detail;
+    cudaLaunchConfig_t  cfg = {};
+    cudaLaunchAttribute at;
+    cfg.gridDim = dim3((unsigned)c->mega_grid);
+    cfg.blockDim = dim3(MEGA_THREADS);
+    cfg.dynamicSmemBytes = c->mega_smem;
+    cfg.stream = s;
+    at.id = cudaLaunchAttributeCooperative;
+    at.val.cooperative = 1;
+    cfg.attrs = &at;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, c->mega_fn, a);
+    if (e != cudaSuccess) {
+        ecu_set_error(nullptr, 0, "persistent step launch failed: %s", cudaGetErrorString(e));
+        return -1;
+    }
+    return 0;
+}
+
+// Profiling replay of the persistent kernel: CUDA events around each launch
+// ("decode_step") and CTA 0's exit time of every grid barrier, attributed to
+// the phase that ended there.
+static int mega_profile(ecu_ctx *c, int n_steps, ecu_kprof *out, int max_kinds)
+{
+    const int np = c->margs.n_ph;
+    unsigned long long *d_ns = nullptr;
+    CK(cudaMalloc(&d_ns, sizeof(unsigned long long) * (size_t)(np + 1 + 4 * np)));
+    CK(cudaMemset(d_ns, 0, sizeof(unsigned long long) * (size_t)(np + 1 + 4 * np)));
+    std::vector<unsigned long long> ns((size_t)np + 1 + 4 * np);
+    unsigned long long *d_det = d_ns + np + 1;
+    int nk = 0;
+    auto slot = [&](const char *kind, double bytes) -> ecu_kprof * {
+        int k = 0;
+        while (k < nk && strncmp(out[k].kind, kind, sizeof out[k].kind) != 0) k++;
+        if (k == nk) {
+            if (nk == max_kinds) return nullptr;
+            memset(&out[k], 0, sizeof out[k]);
+            snprintf(out[k].kind, sizeof out[k].kind, "%s", kind);
+            out[k].bytes_per_launch = bytes;
+            nk++;
+        }
+        return &out[k];
+    };
+    const EcuGeom &g = c->g;
+    const int kvdim = g.n_head_kv * g.head_dim, qdim = g.n_head * g.head_dim;
+    int rc = 0;
+    for (int i = 0; i < n_steps && rc == 0; i++) {
+        cudaEvent_t e0, e1;
+        cudaEventCreate(&e0);
+        cudaEventCreate(&e1);
+        cudaEventRecord(e0, c->stream);
+        rc = mega_launch(c, c->stream, d_ns, d_det);
+        cudaEventRecord(e1, c->stream);
+        g_launches += 1;
+        if (rc == 0 && check_status(c) != 0) rc = -1;
+        float ms = 0;
+        cudaEventElapsedTime(&ms, e0, e1);
+        cudaEventDestroy(e0);
+        cudaEventDestroy(e1);
+        if (rc != 0) break;
+        cudaMemcpy(ns.data(), d_ns, ns.size() * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
+        const double att_bytes = 2.0 * 4.0 * kvdim * (c->pos + 2) + 8.0 * qdim + 4.0 * (qdim + 2 * kvdim);
+        double step_bytes = 0;
+        for (int p = 0; p < np; p++) {
+            const double b = c->ph_bytes[p] < 0 ? att_bytes : c->ph_bytes[p];
+            step_bytes += b;
+            if (ecu_kprof *k = slot(c->ph_kind[p], b)) {
+                k->launches++;
+                k->total_ms += (double)(ns[p + 1] - ns[p]) * 1e-6;
+                if (c->ph_bytes[p] < 0) k->bytes_per_launch = b;
+            }
+            // GEMV phases: where CTA 0 spent the phase (barrier + prologue,
+            // main loop, waiting for ring stages inside it, epilogue)
+            const unsigned long long *dt = ns.data() + np + 1 + 4 * (size_t)p;
+            if (dt[0] && dt[1] && dt[2]) {
+                const char *part[4] = {"prologue", "main", "epilogue", "ring_wait"};
+                const double v[4] = {(double)(dt[0] - ns[p]), (double)(dt[1] - dt[0]), (double)(dt[2] - dt[1]),
+                                     (double)dt[3]};
+                for (int q = 0; q < 4; q++) {
+                    char nm[32];
+                    snprintf(nm, sizeof nm, "%.20s:%s", c->ph_kind[p], part[q]);
+                    if (ecu_kprof *k = slot(nm, 0.0)) {
+                        k->launches++;
+                        k->total_ms += v[q] * 1e-6;
+                    }
+                }
+            }
+        }
+        if (ecu_kprof *k = slot("decode_step", step_bytes)) {
+            k->launches++;
+            k->total_ms += ms;
+            k->bytes_per_launch = step_bytes;
+        }
+        c->pos++;
+    }
+    cudaFree(d_ns);
+    return rc == 0 ? nk : -1;
 }
 
 // ----------------------------------------------------------------- C ABI --
@@ -1166,6 +1497,7 @@ static int ctx_open_impl(ecu_ctx **out, const ecu_model *m, int stage, int first
             if (!ly.attn_norm || !ly.ffn_norm) return fail_oom("norm weights");
         }
     }
+    if (mega_setup(c.get()) != 0) return fail_oom("persistent step buffers");
     // setup memsets/copies ran on the legacy stream, which does not order
     // against the context's non-blocking stream: finish them all here
     if (cudaDeviceSynchronize() != cudaSuccess || cudaGetLastError() != cudaSuccess) {
@@ -1203,6 +1535,7 @@ int ecu_set_pos(ecu_ctx *c, int pos)
 }
 
 float *ecu_state_ptr(ecu_ctx *c) { return c ? c->state : nullptr; }
+const char *ecu_ctx_path(const ecu_ctx *c) { return c ? c->path.c_str() : ""; }
 void  *ecu_stream(ecu_ctx *c) { return c ? (void *)c->stream : nullptr; }
 
 // Host-side checks of llm_forward (src/engine.c:468-515) before enqueueing.
@@ -1315,6 +1648,10 @@ int ecu_ctx_fork(ecu_ctx **out, ecu_ctx *base, char *err, size_t errlen)
     const bool head = c->stage == ECU_STAGE_HEAD || c->stage == ECU_STAGE_FULL;
     if (const char *what = alloc_buffers(c.get(), layers, head)) {
         ecu_set_error(err, errlen, "out of device memory (%s) after %zu bytes", what, c->bytes);
+        return -1;
+    }
+    if (mega_setup(c.get()) != 0) {
+        ecu_set_error(err, errlen, "out of device memory (persistent step buffers)");
         return -1;
     }
     if (cudaDeviceSynchronize() != cudaSuccess || cudaGetLastError() != cudaSuccess) {
@@ -1447,6 +1784,7 @@ int ecu_profile_steps(ecu_ctx *c, int n_steps, ecu_kprof *out, int max_kinds)
     if (c->stage != ECU_STAGE_FULL && c->stage != ECU_STAGE_LAYERS) return -1;
     if (c->pos + n_steps > c->g.n_ctx) { ecu_set_error(nullptr, 0, "context exhausted"); return -1; }
     cudaSetDevice(c->device);
+    if (c->mega) return mega_profile(c, n_steps, out, max_kinds);
     std::vector<ProfRec> recs;
     for (int i = 0; i < n_steps; i++) {
         Launcher L{c->stream, false};

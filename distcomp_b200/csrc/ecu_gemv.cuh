@@ -64,9 +64,8 @@ struct GemvArgs {
 // Threads [0, nthreads) must all call it; `bar` synchronises them.  x is
 // read through L2 (ld.global.cg): in the persistent step kernel other CTAs
 // wrote it since this SM last looked.
-template <class Bar>
-__device__ float rms_scale(const float *x, int n, float eps, double *dsum, int tid,
-                           int nthreads, Bar bar)
+// Partial v of the sum of squares: segment [v*seg, (v+1)*seg), seg = ceil(n/256).
+__device__ __forceinline__ void rms_partials(const float *x, int n, double *dsum, int tid, int nthreads)
 {
     const int seg = (n + 255) / 256;
     for (int v = tid; v < 256; v += nthreads) {
@@ -99,14 +98,53 @@ __device__ float rms_scale(const float *x, int n, float eps, double *dsum, int t
         }
         dsum[v] = p;
     }
+}
+
+__device__ __forceinline__ float rms_from_sum(double ss, int n, float eps)
+{
+    const float ms = (float)(ss / (double)n);
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
+}
+
+template <class Bar>
+__device__ float rms_scale(const float *x, int n, float eps, double *dsum, int tid,
+                           int nthreads, Bar bar)
+{
+    rms_partials(x, n, dsum, tid, nthreads);
     bar();
     for (int stride = 128; stride > 0; stride >>= 1) {
         for (int v = tid; v < stride; v += nthreads) dsum[v] += dsum[v + stride];
         bar();
     }
-    const double ss = dsum[0];
-    const float  ms = (float)(ss / (double)n);
-    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
+    return rms_from_sum(dsum[0], n, eps);
+}
+
+// The same value with the same additions in the same order, the tree run by
+// warp 0 in registers and shuffles: two barriers instead of nine.  Lane l
+// holds partials l + 32k; strides 128, 64, 32 pair registers, strides 16..1
+// pair lanes (shfl_down), exactly dsum[v] += dsum[v + stride] for v < stride.
+template <class Bar>
+__device__ float rms_scale_w0(const float *x, int n, float eps, double *dsum, int tid,
+                              int nthreads, Bar bar)
+{
+    rms_partials(x, n, dsum, tid, nthreads);
+    bar();
+    if (tid < 32) {
+        double p[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) p[k] = dsum[tid + 32 * k];
+#pragma unroll
+        for (int k = 0; k < 4; k++) p[k] += p[k + 4];
+        p[0] += p[2];
+        p[1] += p[3];
+        p[0] += p[1];
+        double v = p[0];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_down_sync(0xffffffffu, v, o);
+        if (tid == 0) dsum[256] = v;
+    }
+    bar();
+    return rms_from_sum(dsum[256], n, eps);
 }
 
 // ----------------------------------------------------------- argmax tail --

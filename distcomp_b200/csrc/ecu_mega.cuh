@@ -1,0 +1,759 @@
+// ecu_mega.cuh -- one decode step of a LAYERS or FULL stage as one persistent
+// kernel.
+//
+// The step is a list of phases (built on the host from the stage's layers):
+//
+//   [embed]  per layer: Q/K/V GEMV (RMSNorm prologue) | attention over
+//   (KV head, position split) items | merge of the splits per query head |
+//   O GEMV (+ residual) | gate/up GEMV (RMSNorm prologue, SwiGLU epilogue) |
+//   down GEMV (+ residual);  [head: RMSNorm + logits GEMV + argmax]
+//
+// -- the order of src/engine.c:380-497.  One CTA per SM, all resident
+// (cooperative launch); the phases are separated by a grid barrier (one
+// atomic counter, bounded spin), and activations cross CTAs through L2 only
+// (ld.global.cg).  Every weight row this CTA multiplies during the whole
+// step streams through a shared-memory ring of bulk async copies in phase
+// order; the warp that releases a ring stage last issues the copy that
+// refills it with the next chunk of the list, so there is no producer warp
+// (16 warps of 128 registers rather than 17 of 96).  Weights do not depend
+// on activations, so the weight stream runs straight through the barriers:
+// while the grid synchronises, the next phase's rows are already landing.  The GEMV arithmetic is the one
+// of k_gemv_fast (int8 digit planes of the input, dp4a, the same row
+// partials in the same order), so its results are the same bits.
+//
+// The phase loop holds one copy of each phase body (the GEMV for Q4_0 and
+// for Q8_0 rows, attention, merge, embed), whatever the layer count.
+#pragma once
+#include "ecu_attn.cuh"
+#include "ecu_gemv.cuh"
+
+#define MEGA_NCW 16                      // warps (all of them consume the ring)
+#define MEGA_THREADS (32 * MEGA_NCW)
+#define MEGA_RING_BYTES (111 * 1024)    // the weight ring, split into nst stages
+#define MEGA_MAX_STAGES 8
+#define MEGA_MAX_NB 512                  // input blocks of a GEMV (n_in <= 16384)
+#define MEGA_MAX_SPLIT 64                // position splits per KV head
+
+enum MegaKind : int { PH_EMBED = 0, PH_GEMV = 1, PH_ATTN = 2 };
+
+// One phase of the step.
+struct MegaPhase {
+    int            kind;
+    int            fmt;        // GEMV: 4 = Q4_0 SPLIT4 rows, 8 = Q8_0 SPLIT8 rows
+    int            norm;       // GEMV: RMSNorm of x (weights norm_w) first
+    int            epi;        // GEMV: Epi
+    const uint8_t *w;
+    unsigned       row_bytes;
+    int            n_in, n_out;
+    int            rpc;        // rows per CTA (even for SwiGLU)
+    int            sr;         // rows per ring stage
+    int            nkg;        // n_in / 1024
+    int            rowpar;     // consumer warps per k-group
+    const float   *x;
+    const float   *norm_w;
+    float         *y;
+    float         *xn;         // GEMV with norm: CTA 0 stores the normed input here
+    float         *kc, *vc;    // ATTN: this layer's cache planes [nkv][n_ctx][hd]
+    const float   *bq, *bk, *bv;
+};
+
+struct MegaArgs {
+    const MegaPhase *ph;
+    int              n_ph;
+    DevMat           emb;           // PH_EMBED: the RAW embedding matrix
+    float           *state;         // residual stream, n_embd (+1: token as float)
+    float           *qkv, *att;
+    float           *apart;         // attention partials [n_kv][n_split][NREP][HD + 4]
+    float           *xn_tmp;        // head: normed state, copied to state at the end
+    float           *part_val;      // argmax: per-CTA best
+    int             *part_idx;
+    unsigned        *ticket;        // argmax ticket, zero between steps
+    unsigned        *bar;           // grid-barrier counters [2], zero between launches
+    unsigned        *att_ticket;    // per KV head: splits done, zero between phases
+    StepState       *st;
+    int             *tok_hist;
+    int             *status;
+    const float     *rope_cs;
+    unsigned long long *phase_ns;   // optional: CTA 0's time at the end of each phase
+    unsigned long long *phase_detail; // optional, GEMV phases [n_ph][4]: CTA 0's time after the
+                                    // prologue, after the main loop, after the epilogue, and the
+                                    // ns its warp 0 waited for ring stages
+    int              advance_pos;   // argmax epilogue advances st->pos (FULL)
+    int              layers_advance;// LAYERS: st->pos++ once the last phase is done
+    int              n_embd, n_head, n_kv, n_ctx, n_split;
+    int              red_floats;    // max rpc * nkg over the GEMV phases
+    int              nst;           // ring stages (<= MEGA_MAX_STAGES)
+    unsigned         stage_bytes;   // bytes per ring stage (multiple of 128)
+    float            eps, kscale;
+};
+
+// ------------------------------------------------------------ grid barrier --
+
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p)
+{
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// All consumer threads of every CTA call this with the same k (0, 1, 2, ...).
+// Writes before it are visible to every CTA after it.  The spin gives up
+// after ECU_WAIT_NS and flags the step as failed.  phase_ns[k + 1] = CTA 0's
+// exit time (phase_ns[0] is the kernel's start).
+__device__ __forceinline__ void grid_sync(const MegaArgs &a, int k, int nct)
+{
+    named_bar(1, nct);
+    if (threadIdx.x == 0) {
+        __threadfence();
+        atomicAdd(a.bar, 1u);
+        const unsigned target = (unsigned)(k + 1) * gridDim.x;
+        if (ld_acquire_u32(a.bar) < target) {
+            const uint64_t t0 = globaltimer_ns();
+            while (ld_acquire_u32(a.bar) < target) {
+                __nanosleep(32);
+                if (*reinterpret_cast<volatile int *>(a.status) != 0) break;   // the step already failed
+                if (globaltimer_ns() - t0 > ECU_WAIT_NS) {
+                    atomicOr(a.status, ECU_STATUS_TIMEOUT);
+                    break;
+                }
+            }
+        }
+        __threadfence();
+        if (a.phase_ns && blockIdx.x == 0) a.phase_ns[k + 1] = globaltimer_ns();
+    }
+    named_bar(1, nct);
+}
+
+// ------------------------------------------------------------ smem layout --
+
+struct MegaSmem {
+    size_t ring, bars, abar, red, un, dsum, argsh, total;
+};
+
+template <int HD>
+__host__ __device__ inline MegaSmem mega_smem_plan(int red_floats)
+{
+    MegaSmem p;
+    p.ring = 0;
+    p.bars = p.ring + (size_t)MEGA_RING_BYTES;
+    p.abar = p.bars + MEGA_MAX_STAGES * sizeof(uint64_t);
+    p.red = (p.abar + 2 * sizeof(uint64_t) + 15) & ~(size_t)15;
+    p.un = (p.red + (size_t)red_floats * sizeof(float) + 127) & ~(size_t)127;
+    // union: digit planes of the GEMV input | attention K/V buffers
+    const size_t dig = (size_t)MEGA_MAX_NB * 28 * sizeof(int);
+    const size_t att = attn_smem_bytes<HD>();
+    p.dsum = p.un + (dig > att ? dig : att);
+    p.argsh = p.dsum + 264 * sizeof(double);      // 256 partials + the total
+    p.total = p.argsh + 32 * sizeof(ArgBest);
+    return p;
+}
+
+// ---------------------------------------------------------------- digits ---
+
+// The digit planes of make_digits, computed by 8 lanes per 32-element block:
+// lane q of the group holds elements 4q..4q+3 (x4), which are word q of each
+// plane in both the Q4_0 and the Q8_0 word order.  The block maximum is one
+// 8-lane reduction of |x| as integer bits (for non-negative floats the bit
+// order is the value order, and inf/NaN bits sort above every finite value),
+// and frexpf/ldexpf are read off the exponent field: e = E - 126 for a normal
+// amax with biased exponent E, e + 1 when its mantissa is >= 127/128 (amax >=
+// 127.5 * 2^(e-7)), inv = 2^(7-e), sxs = 2^(e-21) -- the same values
+// make_digits computes.  The Q4_0 code offsets are left to the consumer
+// (digit_offsets).  All 32 lanes of the warp must call it.
+__device__ __forceinline__ void digits_quad(float4 x4, int (&w)[3], float &sxs)
+{
+    unsigned ab = max(max(__float_as_uint(x4.x) & 0x7fffffffu, __float_as_uint(x4.y) & 0x7fffffffu),
+                      max(__float_as_uint(x4.z) & 0x7fffffffu, __float_as_uint(x4.w) & 0x7fffffffu));
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) ab = max(ab, __shfl_xor_sync(0xffffffffu, ab, o));
+    float inv = 0.0f;
+    if (ab >= 0x7f800000u) {                         // inf or NaN in the block
+        sxs = __int_as_float(0x7fc00000);
+    } else if (__uint_as_float(ab) > 1e-30f) {
+        int e = (int)(ab >> 23) - 126;
+        if ((ab & 0x7fffffu) >= 0x7f0000u) e += 1;
+        inv = __int_as_float((127 + 7 - e) << 23);
+        sxs = __int_as_float((127 + e - 21) << 23);
+    } else {
+        sxs = 0.0f;
+    }
+    const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
+    uint32_t    b[3][4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const float v  = __fmul_rn(xv[i], inv);
+        const float t0 = __fadd_rn(v, RND_MAGIC);
+        const float r0 = __fmul_rn(__fsub_rn(v, __fsub_rn(t0, RND_MAGIC)), 128.0f);
+        const float t1 = __fadd_rn(r0, RND_MAGIC);
+        const float r1 = __fmul_rn(__fsub_rn(r0, __fsub_rn(t1, RND_MAGIC)), 128.0f);
+        const float t2 = __fadd_rn(r1, RND_MAGIC);
+        b[0][i] = __float_as_uint(t0);
+        b[1][i] = __float_as_uint(t1);
+        b[2][i] = __float_as_uint(t2);
+    }
+#pragma unroll
+    for (int p = 0; p < 3; p++) w[p] = (int)pack_lo_bytes(b[p][0], b[p][1], b[p][2], b[p][3]);
+}
+
+// -8 * (sum of the block's digits of plane p): the Q4_0 code offset
+// (codes are stored as c = q + 8), from the lane's own digit words.
+__device__ __forceinline__ void digit_offsets(const int (&xw)[3][8], int (&off)[3])
+{
+#pragma unroll
+    for (int p = 0; p < 3; p++) {
+        int s = 0;
+#pragma unroll
+        for (int j = 0; j < 8; j++) s = __dp4a(xw[p][j], 0x01010101, s);
+        off[p] = -8 * s;
+    }
+}
+
+// ---------------------------------------------------------------- phases ---
+
+// The ring's refill cursor: the next chunk to copy (phase, row offset) and
+// how many chunks were issued; per slot, the warps done with it.
+struct MegaRing {
+    int      p, i, issued;
+    unsigned done[MEGA_MAX_STAGES];
+};
+
+struct MegaShared {
+    uint8_t  *ring;
+    MegaRing *rc;
+    uint64_t *full, *abar;
+    float    *red;
+    int      *dig;
+    float    *kvbuf;
+    double   *dsum;
+    ArgBest  *argsh;
+};
+
+// This CTA's weight chunks (one ring stage each) in phase order.
+struct MegaChunks {
+    const MegaPhase *ph;
+    int              n_ph, p, i;
+
+    __device__ __forceinline__ bool next(const uint8_t *&src, uint32_t &bytes)
+    {
+        for (; p < n_ph; p++, i = 0) {
+            const MegaPhase &q = ph[p];
+            if (q.kind != PH_GEMV) continue;
+            const int r0 = blockIdx.x * q.rpc;
+            const int nrows = max(0, min(q.n_out, r0 + q.rpc) - r0);
+            if (i < nrows) {
+                src = q.w + (size_t)(r0 + i) * q.row_bytes;
+                bytes = (uint32_t)(min(q.sr, nrows - i) * q.row_bytes);
+                i += q.sr;
+                return true;
+            }
+        }
+        return false;
+    }
+};
+
+// Copy the next chunk of the list into ring slot `slot` (one thread).
+__device__ __forceinline__ void ring_issue(const MegaArgs &a, const MegaShared &S, int slot)
+{
+    MegaChunks     c{a.ph, a.n_ph, S.rc->p, S.rc->i};
+    const uint8_t *src;
+    uint32_t       bytes;
+    if (c.next(src, bytes)) {
+        mbar_expect_tx(&S.full[slot], bytes);
+        bulk_g2s(S.ring + (size_t)slot * a.stage_bytes, src, bytes, &S.full[slot]);
+        S.rc->issued++;
+    }
+    S.rc->p = c.p;
+    S.rc->i = c.i;
+}
+
+// Lane 0 of a warp that is done with ring slot `slot` (after __syncwarp).
+// The arrivals count up forever; the warp whose arrival makes a multiple of
+// MEGA_NCW is the last reader of this use of the slot and refills it.  The
+// acq_rel atomic orders every warp's reads of the slot (and the previous
+// refill's cursor update) before the refill; the proxy fence orders them
+// before the bulk copy's writes.  Refills happen in chunk order: the last
+// release of slot s+1 comes after every warp's release of slot s.
+__device__ __forceinline__ void ring_release(const MegaArgs &a, const MegaShared &S, int slot)
+{
+    unsigned old;
+    asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], 1;"
+                 : "=r"(old)
+                 : "r"(smem_addr(&S.rc->done[slot]))
+                 : "memory");
+    if ((old + 1) % MEGA_NCW == 0) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        ring_issue(a, S, slot);
+    }
+}
+
+// Rows [0, rows) of one ring stage against this lane's block column: warp
+// (g, rp) takes rows rp, rp + rowpar, ... four at a time; row partials of
+// k-group g land in red[row * nkg + g].
+template <int FMT>
+__device__ __forceinline__ void mega_stage_rows(const uint8_t *stage, int rows, unsigned row_bytes, int nb,
+                                                int b, int g, int rp, int rowpar, int nkg, int lane,
+                                                const int (&xw)[3][8], const int (&off)[3], float sxs,
+                                                float *red)
+{
+    for (int i0 = rp; i0 < rows; i0 += FAST_RB * rowpar) {
+        float v[FAST_RB];
+#pragma unroll
+        for (int k = 0; k < FAST_RB; k++) {
+            const int ii = i0 + k * rowpar;
+            v[k] = ii < rows ? block_dot<FMT>(stage + (size_t)ii * row_bytes, nb, b, xw, off, sxs) : 0.0f;
+        }
+        const float sum = warp_sum4(v[0], v[1], v[2], v[3], lane);
+        const int   k = (lane >> 3) & 3, ii = i0 + k * rowpar;
+        if ((lane & 7) == 0 && ii < rows) red[ii * nkg + g] = sum;
+    }
+}
+
+// One GEMV phase on the consumer side: digit planes of the (normed) input
+// into shared memory, this CTA's ring stages of the matrix, the epilogue.
+// `ring_s` counts ring stages consumed over the whole step.  One body for
+// both row formats: only the innermost loop depends on it.
+__device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShared &S, int &ring_s, int p_idx)
+{
+    unsigned long long *det = (a.phase_detail && blockIdx.x == 0 && threadIdx.x == 0)
+                                  ? a.phase_detail + (size_t)p_idx * 4 : nullptr;
+    unsigned long long waited = 0;
+    const bool q4 = ph.fmt == 4;
+    const int nct = MEGA_NCW * 32, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int nkg = ph.nkg, rowpar = ph.rowpar, nb = ph.n_in / 32;
+    const int r0 = blockIdx.x * ph.rpc;
+    const int nrows = max(0, min(ph.n_out, r0 + ph.rpc) - r0);
+    const unsigned row_bytes = ph.row_bytes;
+
+    // ---- prologue: digit planes of every input block -----------------------
+    float scale = 1.0f;
+    if (ph.norm) scale = rms_scale_w0(ph.x, ph.n_in, a.eps, S.dsum, tid, nct, [nct] { named_bar(1, nct); });
+    {
+        const float4 *x4 = reinterpret_cast<const float4 *>(ph.x);
+        const float4 *w4 = reinterpret_cast<const float4 *>(ph.norm_w);
+        float4 *xn4 = (ph.xn && blockIdx.x == 0) ? reinterpret_cast<float4 *>(ph.xn) : nullptr;
+        for (int t = tid; t < nb * 8; t += nct) {      // whole warps: nb is a multiple of 32
+            float4 xq = __ldcg(x4 + t);
+            if (ph.norm) {
+                const float4 wq = __ldg(w4 + t);
+                xq.x = __fmul_rn(__fmul_rn(xq.x, scale), wq.x);
+                xq.y = __fmul_rn(__fmul_rn(xq.y, scale), wq.y);
+                xq.z = __fmul_rn(__fmul_rn(xq.z, scale), wq.z);
+                xq.w = __fmul_rn(__fmul_rn(xq.w, scale), wq.w);
+                if (xn4) xn4[t] = xq;
+            }
+            int   w[3];
+            float sxs;
+            digits_quad(xq, w, sxs);
+            const int b = t >> 3, q = t & 7;
+            int *d = S.dig + (size_t)b * 28;
+            d[q] = w[0];
+            d[8 + q] = w[1];
+            d[16 + q] = w[2];
+            if (q == 0) d[27] = __float_as_int(sxs);
+        }
+    }
+    named_bar(1, nct);
+
+    if (det) det[0] = globaltimer_ns();
+    // ---- main loop ------------------------------------------------------------
+    const bool active = warp < nkg * rowpar;
+    const int  g = active ? warp % nkg : 0, rp = active ? warp / nkg : 0;
+    const int  b = g * 32 + lane;
+    int   xw[3][8], off[3];
+    float sxs;
+    {
+        const int4 *d4 = reinterpret_cast<const int4 *>(S.dig + (size_t)b * 28);
+#pragma unroll
+        for (int p = 0; p < 3; p++) {
+            const int4 u = d4[2 * p], v = d4[2 * p + 1];
+            xw[p][0] = u.x; xw[p][1] = u.y; xw[p][2] = u.z; xw[p][3] = u.w;
+            xw[p][4] = v.x; xw[p][5] = v.y; xw[p][6] = v.z; xw[p][7] = v.w;
+        }
+        sxs = __int_as_float(S.dig[(size_t)b * 28 + 27]);
+        if (q4) digit_offsets(xw, off);
+        else off[0] = off[1] = off[2] = 0;
+    }
+    const int sr = ph.sr;
+    for (int i = 0; i < nrows; i += sr) {
+        const int slot = ring_s % a.nst;
+        const unsigned par = (unsigned)(ring_s / a.nst) & 1u;
+        if (det && !mbar_test(&S.full[slot], par)) {
+            const unsigned long long t0 = globaltimer_ns();
+            mbar_wait<true>(&S.full[slot], par, a.status);
+            waited += globaltimer_ns() - t0;
+        } else {
+            mbar_wait<true>(&S.full[slot], par, a.status);
+        }
+        const uint8_t *stage = S.ring + (size_t)slot * a.stage_bytes;
+        const int      rows = min(sr, nrows - i);
+        if (active) {
+            if (q4)
+                mega_stage_rows<4>(stage, rows, row_bytes, nb, b, g, rp, rowpar, nkg, lane, xw, off, sxs,
+                                   S.red + (size_t)i * nkg);
+            else
+                mega_stage_rows<8>(stage, rows, row_bytes, nb, b, g, rp, rowpar, nkg, lane, xw, off, sxs,
+                                   S.red + (size_t)i * nkg);
+        }
+        __syncwarp();
+        if (lane == 0) ring_release(a, S, slot);
+        ring_s++;
+    }
+    // the digit planes share bytes with the attention K/V buffers, which bulk
+    // copies (the async proxy) fill later: order these generic accesses first
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    named_bar(1, nct);
+    if (det) {
+        det[1] = globaltimer_ns();
+        det[3] = waited;
+    }
+
+    // ---- epilogue over this CTA's rows --------------------------------------
+    const int epi = ph.epi;
+    float    *y = ph.y;
+    if (epi == EPI_SWIGLU) {
+        for (int j = tid; j < nrows / 2; j += nct) {
+            float gs = 0.0f, us = 0.0f;
+            for (int q = 0; q < nkg; q++) {
+                gs += S.red[(2 * j) * nkg + q];
+                us += S.red[(2 * j + 1) * nkg + q];
+            }
+            y[r0 / 2 + j] = silu_mul(gs, us);
+        }
+        if (det) det[2] = globaltimer_ns();
+        return;
+    }
+    ArgBest best{-INFINITY, -1};
+    for (int r = tid; r < nrows; r += nct) {
+        float acc = 0.0f;
+        for (int q = 0; q < nkg; q++) acc += S.red[r * nkg + q];
+        if (epi == EPI_ADD) y[r0 + r] = __ldcg(y + r0 + r) + acc;
+        else y[r0 + r] = acc;
+        if (epi == EPI_ARGMAX) best = arg_better(best, ArgBest{acc, r0 + r});
+    }
+    if (det) det[2] = globaltimer_ns();
+    if (epi != EPI_ARGMAX) return;
+    // per-CTA best -> the CTA that takes the last ticket reduces in CTA order
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        ArgBest other;
+        other.v = __shfl_xor_sync(0xffffffffu, best.v, o);
+        other.i = __shfl_xor_sync(0xffffffffu, best.i, o);
+        best = arg_better(best, other);
+    }
+    if (lane == 0) S.argsh[warp] = best;
+    named_bar(1, nct);
+    __shared__ unsigned s_last;
+    if (tid == 0) {
+        ArgBest bb = S.argsh[0];
+        for (int w = 1; w < MEGA_NCW; w++) bb = arg_better(bb, S.argsh[w]);
+        a.part_val[blockIdx.x] = bb.v;
+        a.part_idx[blockIdx.x] = bb.i;
+        __threadfence();
+        s_last = atomicAdd(a.ticket, 1u) == gridDim.x - 1;
+    }
+    named_bar(1, nct);
+    if (!s_last) return;
+    __threadfence();
+    // every CTA is past its prologue: the normed state may replace the
+    // residual stream (the stage's output, src/engine.c:489)
+    if (a.xn_tmp)
+        for (int i = tid; i < a.n_embd; i += nct) a.state[i] = __ldcg(a.xn_tmp + i);
+    if (tid == 0) {
+        ArgBest bb{-INFINITY, -1};
+        for (unsigned c = 0; c < gridDim.x; c++)
+            bb = arg_better(bb, ArgBest{__ldcg(a.part_val + c), __ldcg(a.part_idx + c)});
+        const float l0 = __ldcg(y);
+        const int   tok = (bb.i < 0 || isnan(l0)) ? 0 : bb.i;
+        const int   pos = a.st->pos;
+        if (a.tok_hist) a.tok_hist[pos] = tok;
+        a.st->token = tok;
+        if (a.advance_pos) a.st->pos = pos + 1;
+        a.state[a.n_embd] = (float)tok;
+        *a.ticket = 0u;
+    }
+}
+
+// Attention work item (KV head g, position split sp) = this CTA's index;
+// query head h of the group on warp h.  Same arithmetic per split as
+// k_attention; partials go to global memory for the merge phase.
+template <int HD, int NREP>
+__device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const MegaShared &S, int &att_sb)
+{
+    constexpr int RS = attn_row_stride<HD>();
+    constexpr int LPR = HD / 4, RPW = 32 / LPR;
+    __shared__ __align__(16) float q_s[NREP * HD];
+    __shared__ __align__(16) float knew[HD], vnew[HD], cs_s[HD];
+    const int nct = MEGA_NCW * 32, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int item = blockIdx.x;
+    const bool has = item < a.n_kv * a.n_split;
+    const int g = has ? item / a.n_split : 0, sp = has ? item % a.n_split : 0;
+    const int pos = a.st->pos, npos = pos + 1;
+    const int chunk = (npos + a.n_split - 1) / a.n_split;
+    const int t0 = min(npos, sp * chunk), t1 = has ? min(npos, t0 + chunk) : t0;
+    const int nsub = (t1 - t0 + ATT_SUB - 1) / ATT_SUB;
+    float *kbase = ph.kc + (size_t)g * a.n_ctx * HD;
+    float *vbase = ph.vc + (size_t)g * a.n_ctx * HD;
+    // rows of the slice below the current position, one per lane of warp 0
+    auto issue = [&](int sbl) {
+        const int gsb = att_sb + sbl;
+        const int c0 = t0 + sbl * ATT_SUB;
+        const int c1 = min(min(t1, c0 + ATT_SUB), pos);
+        const int nr = c1 > c0 ? c1 - c0 : 0;
+        float *kb = S.kvbuf + (size_t)(gsb & 1) * 2 * ATT_SUB * RS;
+        if (lane == 0) mbar_expect_tx(&S.abar[gsb & 1], (uint32_t)(2 * nr * HD * sizeof(float)));
+        __syncwarp();
+        if (lane < nr) {
+            bulk_g2s(kb + lane * RS, kbase + (size_t)(c0 + lane) * HD, HD * sizeof(float), &S.abar[gsb & 1]);
+            bulk_g2s(kb + ATT_SUB * RS + lane * RS, vbase + (size_t)(c0 + lane) * HD, HD * sizeof(float),
+                     &S.abar[gsb & 1]);
+        }
+    };
+    if (warp == 0 && nsub > 0) issue(0);
+    for (int j = tid; j < HD; j += nct) cs_s[j] = a.rope_cs[(size_t)pos * HD + j];
+    named_bar(1, nct);
+    const int qdim = a.n_head * HD, kvdim = a.n_kv * HD;
+    for (int i = tid; i < NREP * (HD / 2); i += nct) {
+        const int h = i / (HD / 2), j = i % (HD / 2), row = (g * NREP + h) * HD;
+        float x0 = __ldcg(a.qkv + row + j), x1 = __ldcg(a.qkv + row + j + HD / 2);
+        if (ph.bq) { x0 = __fadd_rn(x0, ph.bq[row + j]); x1 = __fadd_rn(x1, ph.bq[row + j + HD / 2]); }
+        rope_pair(x0, x1, cs_s[2 * j], cs_s[2 * j + 1]);
+        q_s[h * HD + j] = x0;
+        q_s[h * HD + j + HD / 2] = x1;
+    }
+    for (int j = tid; j < HD / 2; j += nct) {
+        const int kr = qdim + g * HD, vr = qdim + kvdim + g * HD;
+        float k0 = __ldcg(a.qkv + kr + j), k1 = __ldcg(a.qkv + kr + j + HD / 2);
+        float v0 = __ldcg(a.qkv + vr + j), v1 = __ldcg(a.qkv + vr + j + HD / 2);
+        if (ph.bk) { k0 = __fadd_rn(k0, ph.bk[g * HD + j]); k1 = __fadd_rn(k1, ph.bk[g * HD + j + HD / 2]); }
+        if (ph.bv) { v0 = __fadd_rn(v0, ph.bv[g * HD + j]); v1 = __fadd_rn(v1, ph.bv[g * HD + j + HD / 2]); }
+        rope_pair(k0, k1, cs_s[2 * j], cs_s[2 * j + 1]);
+        knew[j] = k0; knew[j + HD / 2] = k1;
+        vnew[j] = v0; vnew[j + HD / 2] = v1;
+    }
+    named_bar(1, nct);
+    if (has && sp == 0)
+        for (int j = tid; j < HD; j += nct) {
+            kbase[(size_t)pos * HD + j] = knew[j];
+            vbase[(size_t)pos * HD + j] = vnew[j];
+        }
+    const int  h = warp;              // one query head per warp
+    const bool hw = warp < NREP;
+    float  m_run = -INFINITY, l_run = 0.0f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int sbl = 0; sbl < nsub; sbl++) {
+        const int gsb = att_sb + sbl;
+        if (warp == 0 && sbl + 1 < nsub) issue(sbl + 1);
+        mbar_wait<true>(&S.abar[gsb & 1], (gsb >> 1) & 1, a.status);
+        const float *kb = S.kvbuf + (size_t)(gsb & 1) * 2 * ATT_SUB * RS;
+        const float *vb = kb + ATT_SUB * RS;
+        const int    c0 = t0 + sbl * ATT_SUB, cn = min(ATT_SUB, t1 - c0);
+        if (hw) {
+            const float *krow = (c0 + lane == pos) ? knew : kb + lane * RS;
+            float s = -INFINITY;
+            if (lane < cn) {
+                const float4 *k4 = reinterpret_cast<const float4 *>(krow);
+                const float4 *q4 = reinterpret_cast<const float4 *>(q_s + h * HD);
+                float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
+#pragma unroll 8
+                for (int j = 0; j < HD / 4; j++) {
+                    const float4 kv = k4[j], qv = q4[j];
+                    d0 = fmaf(qv.x, kv.x, d0);
+                    d1 = fmaf(qv.y, kv.y, d1);
+                    d2 = fmaf(qv.z, kv.z, d2);
+                    d3 = fmaf(qv.w, kv.w, d3);
+                }
+                s = ((d0 + d1) + (d2 + d3)) * a.kscale;
+            }
+            const float mnew = fmaxf(m_run, warp_max(s));
+            const float f = expf(m_run - mnew);
+            const float e = lane < cn ? expf(s - mnew) : 0.0f;
+            l_run = l_run * f + warp_sum(e);
+            m_run = mnew;
+            acc.x *= f; acc.y *= f; acc.z *= f; acc.w *= f;
+            const int dq = lane % LPR;
+#pragma unroll 4
+            for (int pb = 0; pb < cn; pb += RPW) {
+                const int   p = pb + lane / LPR;
+                const float ep = __shfl_sync(0xffffffffu, e, p & 31);
+                if (p < cn) {
+                    const float4 vv = (c0 + p == pos) ? reinterpret_cast<const float4 *>(vnew)[dq]
+                                                      : reinterpret_cast<const float4 *>(vb + p * RS)[dq];
+                    acc.x = fmaf(ep, vv.x, acc.x);
+                    acc.y = fmaf(ep, vv.y, acc.y);
+                    acc.z = fmaf(ep, vv.z, acc.z);
+                    acc.w = fmaf(ep, vv.w, acc.w);
+                }
+            }
+        }
+        named_bar(1, nct);            // the buffer is free for sub-chunk sbl + 2
+    }
+    att_sb += nsub;
+    if (has && hw) {
+#pragma unroll
+        for (int o = LPR; o < 32; o <<= 1) {
+            acc.x += __shfl_xor_sync(0xffffffffu, acc.x, o);
+            acc.y += __shfl_xor_sync(0xffffffffu, acc.y, o);
+            acc.z += __shfl_xor_sync(0xffffffffu, acc.z, o);
+            acc.w += __shfl_xor_sync(0xffffffffu, acc.w, o);
+        }
+        float *dst = a.apart + ((size_t)(g * a.n_split + sp) * NREP + h) * (HD + 4);
+        if (lane < LPR) reinterpret_cast<float4 *>(dst)[lane] = acc;
+        if (lane == 0) {
+            dst[HD] = m_run;
+            dst[HD + 1] = l_run;
+        }
+    }
+    // the K/V buffers were filled by the async proxy and read here; the next
+    // phase writes the same bytes with ordinary stores
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+
+    // ---- the split that finishes last merges its KV head's n_rep query heads,
+    // in split order (the combination k_attention's cluster rank 0 performs)
+    __shared__ unsigned s_last;
+    __shared__ float wsp[NREP][MEGA_MAX_SPLIT], invl[NREP];
+    named_bar(1, nct);                       // every warp's partial is written
+    if (tid == 0) {
+        bool last = false;
+        if (has) {
+            __threadfence();
+            last = atomicAdd(a.att_ticket + g, 1u) == (unsigned)a.n_split - 1;
+        }
+        s_last = last;
+    }
+    named_bar(1, nct);
+    if (!s_last) return;
+    __threadfence();
+    // all partials of the head group into shared memory at once (the K/V
+    // buffers are free), then the merge reads only shared memory
+    const int    ns = a.n_split;
+    constexpr int PER = NREP * (HD + 4);     // floats of one split's partials
+    const float4 *src4 = reinterpret_cast<const float4 *>(a.apart + (size_t)g * ns * PER);
+    float4       *gat4 = reinterpret_cast<float4 *>(S.kvbuf);
+    for (int i = tid; i < ns * PER / 4; i += nct) gat4[i] = __ldcg(src4 + i);
+    named_bar(1, nct);
+    const float *gat = S.kvbuf;
+    if (tid < NREP) {
+        const int hh = tid;
+        float M = -INFINITY;
+        for (int r = 0; r < ns; r++) M = fmaxf(M, gat[r * PER + hh * (HD + 4) + HD]);
+        float L = 0.0f;
+        for (int r = 0; r < ns; r++) {
+            const float ms = gat[r * PER + hh * (HD + 4) + HD];
+            const float w = ms > -INFINITY ? expf(ms - M) : 0.0f;
+            wsp[hh][r] = w;
+            L += gat[r * PER + hh * (HD + 4) + HD + 1] * w;
+        }
+        invl[hh] = L > 0.0f ? 1.0f / L : 0.0f;
+    }
+    named_bar(1, nct);
+    for (int i = tid; i < NREP * HD; i += nct) {
+        const int hh = i / HD, d = i % HD;
+        float o = 0.0f;
+        for (int r = 0; r < ns; r++) o = fmaf(gat[r * PER + hh * (HD + 4) + d], wsp[hh][r], o);
+        a.att[(g * NREP + hh) * HD + d] = o * invl[hh];
+    }
+    if (tid == 0) a.att_ticket[g] = 0u;     // for the next layer (after a grid barrier)
+}
+
+// L2 prefetch of the K and V rows this CTA's attention item will read (the
+// positions below the current one of its split), issued a phase early.
+template <int HD>
+__device__ __forceinline__ void attn_prefetch(const MegaArgs &a, const MegaPhase &ph)
+{
+    const int item = blockIdx.x;
+    if (item >= a.n_kv * a.n_split) return;
+    const int g = item / a.n_split, sp = item % a.n_split;
+    const int pos = a.st->pos, npos = pos + 1;
+    const int chunk = (npos + a.n_split - 1) / a.n_split;
+    const int t0 = min(npos, sp * chunk), t1 = min(min(npos, t0 + chunk), pos);
+    if (t1 <= t0) return;
+    const size_t   off = ((size_t)g * a.n_ctx + t0) * HD;
+    const uint32_t bytes = (uint32_t)((t1 - t0) * HD * sizeof(float));
+    prefetch_l2(ph.kc + off, bytes);
+    prefetch_l2(ph.vc + off, bytes);
+}
+
+__device__ void mega_embed(const MegaArgs &a)
+{
+    const int    nct = MEGA_NCW * 32, n = a.n_embd;
+    const int    tok = a.st->token;
+    if (tok < 0 || tok >= a.emb.n_out) {
+        if (blockIdx.x == 0 && threadIdx.x == 0) atomicOr(&a.st->status, ECU_STATUS_BADTOKEN);
+        return;
+    }
+    const size_t base = (size_t)tok * (size_t)n;
+    for (int i = blockIdx.x * nct + threadIdx.x; i < n; i += gridDim.x * nct) {
+        const size_t e = base + (size_t)i;
+        a.state[i] = mat_elem(a.emb, (int)(e / (size_t)a.emb.n_in), (int)(e % (size_t)a.emb.n_in));
+    }
+}
+
+template <int HD, int NREP>
+__global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a)
+{
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int      nct = MEGA_NCW * 32, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const MegaSmem P = mega_smem_plan<HD>(a.red_floats);
+    MegaShared S;
+    S.ring = smem + P.ring;
+    S.full = reinterpret_cast<uint64_t *>(smem + P.bars);
+    S.abar = reinterpret_cast<uint64_t *>(smem + P.abar);
+    S.red = reinterpret_cast<float *>(smem + P.red);
+    S.dig = reinterpret_cast<int *>(smem + P.un);
+    S.kvbuf = reinterpret_cast<float *>(smem + P.un);
+    S.dsum = reinterpret_cast<double *>(smem + P.dsum);
+    S.argsh = reinterpret_cast<ArgBest *>(smem + P.argsh);
+    __shared__ MegaRing ring_state;
+    S.rc = &ring_state;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < a.nst; s++) mbar_init(&S.full[s], 1);
+        mbar_init(&S.abar[0], 1);
+        mbar_init(&S.abar[1], 1);
+        mbar_init_fence();
+        S.rc->p = S.rc->i = S.rc->issued = 0;
+        for (int s = 0; s < a.nst; s++) S.rc->done[s] = 0u;
+        for (int s = 0; s < a.nst; s++) ring_issue(a, S, s);     // the first chunks
+    }
+    __syncthreads();
+
+    // ---- consumers -------------------------------------------------------------
+    if (a.phase_ns && blockIdx.x == 0 && threadIdx.x == 0) a.phase_ns[0] = globaltimer_ns();
+    int ring_s = 0, att_sb = 0;
+    for (int p = 0; p < a.n_ph; p++) {
+        const MegaPhase &ph = a.ph[p];
+        const int        kind = ph.kind;
+        if (kind == PH_GEMV) {
+            if (threadIdx.x == 0 && p + 1 < a.n_ph && a.ph[p + 1].kind == PH_ATTN) attn_prefetch<HD>(a, a.ph[p + 1]);
+            mega_gemv(a, ph, S, ring_s, p);
+        } else if (kind == PH_ATTN) {
+            mega_attention<HD, NREP>(a, ph, S, att_sb);
+        } else {
+            mega_embed(a);
+        }
+        if (p + 1 < a.n_ph) grid_sync(a, p, nct);
+    }
+    // ring and K/V copies still in flight (none, unless a wait gave up) land
+    // before this CTA may exit
+    named_bar(1, nct);
+    if (threadIdx.x == 0) {
+        const int n = S.rc->issued;
+        for (int j = max(0, n - a.nst); j < n; j++)
+            mbar_drain(&S.full[j % a.nst], (unsigned)(j / a.nst) & 1u, ECU_WAIT_NS);
+        for (int j = max(0, att_sb - 2); j < att_sb; j++) mbar_drain(&S.abar[j & 1], (j >> 1) & 1, ECU_WAIT_NS);
+    }
+    // a LAYERS stage advances its position once every phase is done; no
+    // CTA reads it after the last attention phase
+    if (a.layers_advance && blockIdx.x == 0 && threadIdx.x == 0) a.st->pos = a.st->pos + 1;
+    if (a.phase_ns && blockIdx.x == 0 && threadIdx.x == 0) a.phase_ns[a.n_ph] = globaltimer_ns();
+    // the last CTA out rewinds the barrier counter for the next launch: every
+    // CTA that counted itself here has left its last grid barrier
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(a.bar + 1, 1u) == gridDim.x - 1) {
+            a.bar[0] = 0u;
+            a.bar[1] = 0u;
+            __threadfence();
+        }
+    }
+}

@@ -58,8 +58,25 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity)
     return ok != 0;
 }
 
+// Non-blocking probe: has phase `parity` of `bar` completed?
+__device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 // Wait for phase `parity` of `bar` to complete, at most ECU_WAIT_NS.
-// Returns false (and flags *status) on timeout.
+// Returns false (and flags *status) on timeout.  With FAIL_FAST, a wait that
+// finds the step already flagged (by any wait) gives up at once: a kernel
+// with thousands of waits then ends after one timeout, not one per wait.
+template <bool FAIL_FAST = false>
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *status)
 {
     if (mbar_try_wait(bar, parity)) return true;
@@ -67,10 +84,24 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *s
     for (;;) {
         for (int i = 0; i < 64; i++)
             if (mbar_try_wait(bar, parity)) return true;
+        if (FAIL_FAST && status && *reinterpret_cast<volatile int *>(status) != 0) return false;
         if (globaltimer_ns() - t0 > ECU_WAIT_NS) {
             if (status) atomicOr(status, ECU_STATUS_TIMEOUT);
             return false;
         }
+    }
+}
+
+// Wait for a CTA's own bulk copies before it exits, whatever the status word
+// says; gives up after limit_ns.
+__device__ __forceinline__ bool mbar_drain(uint64_t *bar, uint32_t parity, uint64_t limit_ns)
+{
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (;;) {
+        for (int i = 0; i < 64; i++)
+            if (mbar_try_wait(bar, parity)) return true;
+        if (globaltimer_ns() - t0 > limit_ns) return false;
     }
 }
 

@@ -67,6 +67,7 @@ SIGNATURES = [
                                C.c_char_p, C.c_size_t]),
     ("ecu_ctx_close", None, [C.c_void_p]),
     ("ecu_ctx_info", C.c_int, [C.c_void_p, C.POINTER(EcuInfo)]),
+    ("ecu_ctx_path", C.c_char_p, [C.c_void_p]),
     ("ecu_forward", C.c_int, [C.c_void_p, C.c_int, C.c_void_p]),
     ("ecu_reset", None, [C.c_void_p]),
     ("ecu_layer_once", C.c_int, [C.c_void_p, C.c_int, C.c_void_p]),
@@ -250,6 +251,10 @@ class LlmCtx:
         """One step from device-resident input (ecu_step_dev)."""
         if lib().ecu_step_dev(self.h, C.c_void_p(stream or 0)) != 0:
             raise EngineError(last_error())
+
+    def path(self) -> str:
+        """"persistent" or "kernels: <why not>" (ecu_ctx_path)."""
+        return (lib().ecu_ctx_path(self.h) or b"").decode()
 
     def state_ptr(self) -> int:
         return int(lib().ecu_state_ptr(self.h) or 0)

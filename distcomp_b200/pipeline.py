@@ -209,7 +209,17 @@ class DistExchanger(Exchanger):
                 ops.append(dist.P2POp(dist.isend, me.send_buf(m.seq, m.kind), m.dst))
             elif m.dst == self.rank:
                 ops.append(dist.P2POp(dist.irecv, me.recv_buf(m.seq, m.kind), m.src))
-        if ops:
+        if not ops:
+            return
+        stream = getattr(me, "stream", None)
+        if stream is None:
+            for w in dist.batch_isend_irecv(ops):
+                w.wait()
+            return
+        import torch
+        # NCCL orders itself after the current stream and w.wait() orders the
+        # current stream after NCCL: make the stage's stream the current one
+        with torch.cuda.stream(stream):
             for w in dist.batch_isend_irecv(ops):
                 w.wait()
 

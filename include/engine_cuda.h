@@ -82,6 +82,11 @@ int  ecu_ctx_open(ecu_ctx **out, const ecu_model *m, int stage, int first, int l
                   int device, char *err, size_t errlen);
 void ecu_ctx_close(ecu_ctx *c);
 int  ecu_ctx_info(const ecu_ctx *c, ecu_info *info);
+/* How the context runs a step: "persistent" (one cooperative kernel per
+ * token, every phase of the stage inside it) or "kernels: <reason>" (one
+ * kernel per operation, and why the persistent kernel does not apply).
+ * No reference counterpart (the CPU engine has one implementation). */
+const char *ecu_ctx_path(const ecu_ctx *c);
 
 /* One token through the stage, host `out` (replaces llm_forward,
  * src/engine.h:88).  -1 for a token outside the vocabulary (EMBED/FULL) or

@@ -832,8 +832,8 @@ static int mega_setup(ecu_ctx *c)
     cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, c->device);
     if (!coop) return no("no cooperative launch");
     const int grid = c->sms;
-    // ring geometry: ECU_MEGA_RING stages (default 3) over MEGA_RING_BYTES
-    int nst = 3;
+    // ring geometry: ECU_MEGA_RING stages (default 2) over MEGA_RING_BYTES
+    int nst = 2;
     if (const char *r = getenv("ECU_MEGA_RING")) nst = std::max(2, std::min(MEGA_MAX_STAGES, atoi(r)));
     const unsigned stage_bytes = (unsigned)(MEGA_RING_BYTES / nst) & ~127u;
     for (auto &ly : c->layers)
@@ -890,7 +890,11 @@ static int mega_setup(ecu_ctx *c)
             "gemv_head_argmax", gemv_bytes(c->out, EPI_ARGMAX) + 4.0 * g.n_embd);
     int red = 0;
     for (auto &p : ph)
-        if (p.kind == PH_GEMV) red = std::max(red, p.rpc * p.nkg);
+        if (p.kind == PH_GEMV) {
+            // Q4_0 phases keep 8 partials per row and k-group when they fit
+            p.red8 = (p.fmt == 4 && p.rpc * p.nkg * 8 <= MEGA_RED8_MAX) ? 1 : 0;
+            red = std::max(red, p.rpc * p.nkg * (p.red8 ? 8 : 1));
+        }
     const size_t smem = mega_smem_total(hd, red);
     cudaFuncAttributes fa;
     int optin = 0;

@@ -17,9 +17,10 @@
 // refills it with the next chunk of the list, so there is no producer warp
 // (16 warps of 128 registers rather than 17 of 96).  Weights do not depend
 // on activations, so the weight stream runs straight through the barriers:
-// while the grid synchronises, the next phase's rows are already landing.  The GEMV arithmetic is the one
-// of k_gemv_fast (int8 digit planes of the input, dp4a, the same row
-// partials in the same order), so its results are the same bits.
+// while the grid synchronises, the next phase's rows are already landing.
+// The GEMV arithmetic is the one of k_gemv_fast (int8 digit planes of the
+// input, dp4a, the same row partials added in the same order), so its
+// results are the same bits.
 //
 // The phase loop holds one copy of each phase body (the GEMV for Q4_0 and
 // for Q8_0 rows, attention, merge, embed), whatever the layer count.
@@ -33,6 +34,7 @@
 #define MEGA_MAX_STAGES 8
 #define MEGA_MAX_NB 512                  // input blocks of a GEMV (n_in <= 16384)
 #define MEGA_MAX_SPLIT 64                // position splits per KV head
+#define MEGA_RED8_MAX 6400               // floats of 8-lane row partials a GEMV phase may keep
 
 enum MegaKind : int { PH_EMBED = 0, PH_GEMV = 1, PH_ATTN = 2 };
 
@@ -49,6 +51,7 @@ struct MegaPhase {
     int            sr;         // rows per ring stage
     int            nkg;        // n_in / 1024
     int            rowpar;     // consumer warps per k-group
+    int            red8;       // row partials kept per 8-lane group (8 per row and k-group)
     const float   *x;
     const float   *norm_w;
     float         *y;
@@ -81,7 +84,7 @@ struct MegaArgs {
     int              advance_pos;   // argmax epilogue advances st->pos (FULL)
     int              layers_advance;// LAYERS: st->pos++ once the last phase is done
     int              n_embd, n_head, n_kv, n_ctx, n_split;
-    int              red_floats;    // max rpc * nkg over the GEMV phases
+    int              red_floats;    // row-partial floats the largest GEMV phase keeps
     int              nst;           // ring stages (<= MEGA_MAX_STAGES)
     unsigned         stage_bytes;   // bytes per ring stage (multiple of 128)
     float            eps, kscale;
@@ -104,21 +107,22 @@ __device__ __forceinline__ void grid_sync(const MegaArgs &a, int k, int nct)
 {
     named_bar(1, nct);
     if (threadIdx.x == 0) {
-        __threadfence();
-        atomicAdd(a.bar, 1u);
+        // release: this CTA's writes (ordered before by the named barrier)
+        // are visible before its arrival is counted; acquire in the spin
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.bar) : "memory");
         const unsigned target = (unsigned)(k + 1) * gridDim.x;
         if (ld_acquire_u32(a.bar) < target) {
             const uint64_t t0 = globaltimer_ns();
-            while (ld_acquire_u32(a.bar) < target) {
-                __nanosleep(32);
-                if (*reinterpret_cast<volatile int *>(a.status) != 0) break;   // the step already failed
-                if (globaltimer_ns() - t0 > ECU_WAIT_NS) {
-                    atomicOr(a.status, ECU_STATUS_TIMEOUT);
-                    break;
+            for (unsigned it = 1; ld_acquire_u32(a.bar) < target; it++) {
+                if ((it & 255u) == 0) {
+                    if (*reinterpret_cast<volatile int *>(a.status) != 0) break;   // the step already failed
+                    if (globaltimer_ns() - t0 > ECU_WAIT_NS) {
+                        atomicOr(a.status, ECU_STATUS_TIMEOUT);
+                        break;
+                    }
                 }
             }
         }
-        __threadfence();
         if (a.phase_ns && blockIdx.x == 0) a.phase_ns[k + 1] = globaltimer_ns();
     }
     named_bar(1, nct);
@@ -213,8 +217,13 @@ __device__ __forceinline__ void digit_offsets(const int (&xw)[3][8], int (&off)[
 // The ring's refill cursor: the next chunk to copy (phase, row offset) and
 // how many chunks were issued; per slot, the warps done with it.
 struct MegaRing {
-    int      p, i, issued;
-    unsigned done[MEGA_MAX_STAGES];
+    int            p, i, issued;
+    // the current GEMV phase's rows of this CTA, cached so that a refill
+    // reads global memory only when it moves on to the next phase
+    const uint8_t *w;           // first row of this CTA
+    unsigned       row_bytes;
+    int            nrows, sr;
+    unsigned       done[MEGA_MAX_STAGES];
 };
 
 struct MegaShared {
@@ -228,42 +237,34 @@ struct MegaShared {
     ArgBest  *argsh;
 };
 
-// This CTA's weight chunks (one ring stage each) in phase order.
-struct MegaChunks {
-    const MegaPhase *ph;
-    int              n_ph, p, i;
+// Load phase p's geometry for this CTA into the ring cursor.
+__device__ __forceinline__ void ring_load_phase(const MegaArgs &a, MegaRing *rc, int p)
+{
+    rc->p = p;
+    rc->i = 0;
+    rc->nrows = 0;
+    if (p >= a.n_ph) return;
+    const MegaPhase &q = a.ph[p];
+    if (q.kind != PH_GEMV) return;
+    const int r0 = blockIdx.x * q.rpc;
+    rc->nrows = max(0, min(q.n_out, r0 + q.rpc) - r0);
+    rc->w = q.w + (size_t)r0 * q.row_bytes;
+    rc->row_bytes = q.row_bytes;
+    rc->sr = q.sr;
+}
 
-    __device__ __forceinline__ bool next(const uint8_t *&src, uint32_t &bytes)
-    {
-        for (; p < n_ph; p++, i = 0) {
-            const MegaPhase &q = ph[p];
-            if (q.kind != PH_GEMV) continue;
-            const int r0 = blockIdx.x * q.rpc;
-            const int nrows = max(0, min(q.n_out, r0 + q.rpc) - r0);
-            if (i < nrows) {
-                src = q.w + (size_t)(r0 + i) * q.row_bytes;
-                bytes = (uint32_t)(min(q.sr, nrows - i) * q.row_bytes);
-                i += q.sr;
-                return true;
-            }
-        }
-        return false;
-    }
-};
-
-// Copy the next chunk of the list into ring slot `slot` (one thread).
+// Copy the next chunk of this CTA's weight rows (phase order) into ring
+// slot `slot` (one thread; refills are serialised).
 __device__ __forceinline__ void ring_issue(const MegaArgs &a, const MegaShared &S, int slot)
 {
-    MegaChunks     c{a.ph, a.n_ph, S.rc->p, S.rc->i};
-    const uint8_t *src;
-    uint32_t       bytes;
-    if (c.next(src, bytes)) {
-        mbar_expect_tx(&S.full[slot], bytes);
-        bulk_g2s(S.ring + (size_t)slot * a.stage_bytes, src, bytes, &S.full[slot]);
-        S.rc->issued++;
-    }
-    S.rc->p = c.p;
-    S.rc->i = c.i;
+    MegaRing *rc = S.rc;
+    while (rc->p < a.n_ph && rc->i >= rc->nrows) ring_load_phase(a, rc, rc->p + 1);
+    if (rc->p >= a.n_ph) return;
+    const uint32_t bytes = (uint32_t)(min(rc->sr, rc->nrows - rc->i) * rc->row_bytes);
+    mbar_expect_tx(&S.full[slot], bytes);
+    bulk_g2s(S.ring + (size_t)slot * a.stage_bytes, rc->w + (size_t)rc->i * rc->row_bytes, bytes, &S.full[slot]);
+    rc->i += rc->sr;
+    rc->issued++;
 }
 
 // Lane 0 of a warp that is done with ring slot `slot` (after __syncwarp).
@@ -286,10 +287,34 @@ __device__ __forceinline__ void ring_release(const MegaArgs &a, const MegaShared
     }
 }
 
+// The first two levels of warp_sum4: lane l then holds the partial of row
+// (l >> 3) & 3 over lanes {l, l^8, l^16, l^24}; the 8 partials of an 8-lane
+// group added as ((p0+p4)+(p2+p6)) + ((p1+p5)+(p3+p7)) give the value
+// warp_sum4 returns (its last three levels add in exactly that order).
+__device__ __forceinline__ float warp_sum4_part(float v0, float v1, float v2, float v3, int lane)
+{
+    const bool up = lane & 16;
+    float a0 = up ? v2 : v0, a1 = up ? v3 : v1;
+    const float b0 = up ? v0 : v2, b1 = up ? v1 : v3;
+    a0 += __shfl_xor_sync(0xffffffffu, b0, 16);
+    a1 += __shfl_xor_sync(0xffffffffu, b1, 16);
+    const bool mid = lane & 8;
+    const float c = mid ? a1 : a0;
+    const float dd = mid ? a0 : a1;
+    return c + __shfl_xor_sync(0xffffffffu, dd, 8);
+}
+
+__device__ __forceinline__ float sum8_tree(const float *p)
+{
+    return ((p[0] + p[4]) + (p[2] + p[6])) + ((p[1] + p[5]) + (p[3] + p[7]));
+}
+
 // Rows [0, rows) of one ring stage against this lane's block column: warp
-// (g, rp) takes rows rp, rp + rowpar, ... four at a time; row partials of
-// k-group g land in red[row * nkg + g].
-template <int FMT>
+// (g, rp) takes rows rp, rp + rowpar, ... four at a time.  Row partials of
+// k-group g land in red[row * nkg + g], or with RED8 (the last three levels
+// of the warp reduction left to the epilogue's sum8_tree) in
+// red[(row * nkg + g) * 8 + lane % 8].
+template <int FMT, bool RED8>
 __device__ __forceinline__ void mega_stage_rows(const uint8_t *stage, int rows, unsigned row_bytes, int nb,
                                                 int b, int g, int rp, int rowpar, int nkg, int lane,
                                                 const int (&xw)[3][8], const int (&off)[3], float sxs,
@@ -302,10 +327,26 @@ __device__ __forceinline__ void mega_stage_rows(const uint8_t *stage, int rows, 
             const int ii = i0 + k * rowpar;
             v[k] = ii < rows ? block_dot<FMT>(stage + (size_t)ii * row_bytes, nb, b, xw, off, sxs) : 0.0f;
         }
-        const float sum = warp_sum4(v[0], v[1], v[2], v[3], lane);
-        const int   k = (lane >> 3) & 3, ii = i0 + k * rowpar;
-        if ((lane & 7) == 0 && ii < rows) red[ii * nkg + g] = sum;
+        const int k = (lane >> 3) & 3, ii = i0 + k * rowpar;
+        if (RED8) {
+            const float part = warp_sum4_part(v[0], v[1], v[2], v[3], lane);
+            if (ii < rows) red[(ii * nkg + g) * 8 + (lane & 7)] = part;
+        } else {
+            const float sum = warp_sum4(v[0], v[1], v[2], v[3], lane);
+            if ((lane & 7) == 0 && ii < rows) red[ii * nkg + g] = sum;
+        }
     }
+}
+
+// Sum of row r's k-group partials, in k-group order.
+__device__ __forceinline__ float row_total(const float *red, int r, int nkg, bool red8)
+{
+    float acc = 0.0f;
+    if (red8)
+        for (int q = 0; q < nkg; q++) acc += sum8_tree(red + (size_t)(r * nkg + q) * 8);
+    else
+        for (int q = 0; q < nkg; q++) acc += red[r * nkg + q];
+    return acc;
 }
 
 // One GEMV phase on the consumer side: digit planes of the (normed) input
@@ -317,7 +358,7 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
     unsigned long long *det = (a.phase_detail && blockIdx.x == 0 && threadIdx.x == 0)
                                   ? a.phase_detail + (size_t)p_idx * 4 : nullptr;
     unsigned long long waited = 0;
-    const bool q4 = ph.fmt == 4;
+    const bool q4 = ph.fmt == 4, red8 = q4 && ph.red8;
     const int nct = MEGA_NCW * 32, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nkg = ph.nkg, rowpar = ph.rowpar, nb = ph.n_in / 32;
     const int r0 = blockIdx.x * ph.rpc;
@@ -387,12 +428,15 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
         const uint8_t *stage = S.ring + (size_t)slot * a.stage_bytes;
         const int      rows = min(sr, nrows - i);
         if (active) {
-            if (q4)
-                mega_stage_rows<4>(stage, rows, row_bytes, nb, b, g, rp, rowpar, nkg, lane, xw, off, sxs,
-                                   S.red + (size_t)i * nkg);
+            if (q4 && red8)
+                mega_stage_rows<4, true>(stage, rows, row_bytes, nb, b, g, rp, rowpar, nkg, lane, xw, off, sxs,
+                                         S.red + (size_t)i * nkg * 8);
+            else if (q4)
+                mega_stage_rows<4, false>(stage, rows, row_bytes, nb, b, g, rp, rowpar, nkg, lane, xw, off, sxs,
+                                          S.red + (size_t)i * nkg);
             else
-                mega_stage_rows<8>(stage, rows, row_bytes, nb, b, g, rp, rowpar, nkg, lane, xw, off, sxs,
-                                   S.red + (size_t)i * nkg);
+                mega_stage_rows<8, false>(stage, rows, row_bytes, nb, b, g, rp, rowpar, nkg, lane, xw, off, sxs,
+                                          S.red + (size_t)i * nkg);
         }
         __syncwarp();
         if (lane == 0) ring_release(a, S, slot);
@@ -412,11 +456,7 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
     float    *y = ph.y;
     if (epi == EPI_SWIGLU) {
         for (int j = tid; j < nrows / 2; j += nct) {
-            float gs = 0.0f, us = 0.0f;
-            for (int q = 0; q < nkg; q++) {
-                gs += S.red[(2 * j) * nkg + q];
-                us += S.red[(2 * j + 1) * nkg + q];
-            }
+            const float gs = row_total(S.red, 2 * j, nkg, red8), us = row_total(S.red, 2 * j + 1, nkg, red8);
             y[r0 / 2 + j] = silu_mul(gs, us);
         }
         if (det) det[2] = globaltimer_ns();
@@ -424,8 +464,7 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
     }
     ArgBest best{-INFINITY, -1};
     for (int r = tid; r < nrows; r += nct) {
-        float acc = 0.0f;
-        for (int q = 0; q < nkg; q++) acc += S.red[r * nkg + q];
+        const float acc = row_total(S.red, r, nkg, red8);
         if (epi == EPI_ADD) y[r0 + r] = __ldcg(y + r0 + r) + acc;
         else y[r0 + r] = acc;
         if (epi == EPI_ARGMAX) best = arg_better(best, ArgBest{acc, r0 + r});
@@ -711,7 +750,8 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a)
         mbar_init(&S.abar[0], 1);
         mbar_init(&S.abar[1], 1);
         mbar_init_fence();
-        S.rc->p = S.rc->i = S.rc->issued = 0;
+        S.rc->issued = 0;
+        ring_load_phase(a, S.rc, 0);
         for (int s = 0; s < a.nst; s++) S.rc->done[s] = 0u;
         for (int s = 0; s < a.nst; s++) ring_issue(a, S, s);     // the first chunks
     }

@@ -84,8 +84,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *s
     for (;;) {
         for (int i = 0; i < 64; i++)
             if (mbar_try_wait(bar, parity)) return true;
-        if (FAIL_FAST && status && *reinterpret_cast<volatile int *>(status) != 0) return false;
-        if (globaltimer_ns() - t0 > ECU_WAIT_NS) {
+        const uint64_t dt = globaltimer_ns() - t0;
+        // the status word is global memory: look at it only once a wait has
+        // lasted long enough to suggest trouble, not on every pass
+        if (FAIL_FAST && status && dt > 20000 && *reinterpret_cast<volatile int *>(status) != 0) return false;
+        if (dt > ECU_WAIT_NS) {
             if (status) atomicOr(status, ECU_STATUS_TIMEOUT);
             return false;
         }

@@ -888,6 +888,7 @@ static int mega_setup(ecu_ctx *c)
     if (full)
         add(mega_gemv_phase(c->out, grid, stage_bytes, 1, EPI_ARGMAX, c->state, c->out_norm, c->logits, xn_tmp),
             "gemv_head_argmax", gemv_bytes(c->out, EPI_ARGMAX) + 4.0 * g.n_embd);
+    for (size_t i = 0; i + 1 < ph.size(); i++) ph[i].next_attn = ph[i + 1].kind == PH_ATTN ? 1 : 0;
     int red = 0;
     for (auto &p : ph)
         if (p.kind == PH_GEMV) {

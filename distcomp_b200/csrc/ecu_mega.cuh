@@ -58,7 +58,10 @@ struct MegaPhase {
     float         *xn;         // GEMV with norm: CTA 0 stores the normed input here
     float         *kc, *vc;    // ATTN: this layer's cache planes [nkv][n_ctx][hd]
     const float   *bq, *bk, *bv;
+    int            next_attn;  // the next phase is attention
+    int            pad_[3];
 };
+static_assert(sizeof(MegaPhase) % 16 == 0, "phase descriptors are copied in 16-byte pieces");
 
 struct MegaArgs {
     const MegaPhase *ph;
@@ -227,12 +230,14 @@ struct MegaRing {
 };
 
 struct MegaShared {
+    int       pos;         // cache position of this step (read once at kernel start)
     uint8_t  *ring;
     MegaRing *rc;
     uint64_t *full, *abar;
     float    *red;
     int      *dig;
     float    *kvbuf;
+    float    *cs;          // RoPE (cos, sin) row of the current position, staged a phase early
     double   *dsum;
     ArgBest  *argsh;
 };
@@ -353,7 +358,12 @@ __device__ __forceinline__ float row_total(const float *red, int r, int nkg, boo
 // into shared memory, this CTA's ring stages of the matrix, the epilogue.
 // `ring_s` counts ring stages consumed over the whole step.  One body for
 // both row formats: only the innermost loop depends on it.
-__device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShared &S, int &ring_s, int p_idx)
+__device__ __forceinline__ void attn_prefetch(const MegaArgs &a, const MegaPhase &ph, int pos, int hd);
+
+// next: the following phase's descriptor when it is attention (its K/V rows
+// are warmed in L2 and the RoPE row staged once the main loop is done).
+__device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShared &S, int &ring_s, int p_idx,
+                          const MegaPhase *next, int hd)
 {
     unsigned long long *det = (a.phase_detail && blockIdx.x == 0 && threadIdx.x == 0)
                                   ? a.phase_detail + (size_t)p_idx * 4 : nullptr;
@@ -372,30 +382,47 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
         const float4 *x4 = reinterpret_cast<const float4 *>(ph.x);
         const float4 *w4 = reinterpret_cast<const float4 *>(ph.norm_w);
         float4 *xn4 = (ph.xn && blockIdx.x == 0) ? reinterpret_cast<float4 *>(ph.xn) : nullptr;
-        for (int t = tid; t < nb * 8; t += nct) {      // whole warps: nb is a multiple of 32
-            float4 xq = __ldcg(x4 + t);
-            if (ph.norm) {
-                const float4 wq = __ldg(w4 + t);
-                xq.x = __fmul_rn(__fmul_rn(xq.x, scale), wq.x);
-                xq.y = __fmul_rn(__fmul_rn(xq.y, scale), wq.y);
-                xq.z = __fmul_rn(__fmul_rn(xq.z, scale), wq.z);
-                xq.w = __fmul_rn(__fmul_rn(xq.w, scale), wq.w);
-                if (xn4) xn4[t] = xq;
+        const int nq = nb * 8;                          // float4s of x; whole warps (nb % 32 == 0)
+        for (int base = tid; base < nq; base += 4 * nct) {
+            // the loads of up to four items first: one memory round trip
+            float4 xq[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int t = base + u * nct;
+                if (t < nq) xq[u] = __ldcg(x4 + t);
             }
-            int   w[3];
-            float sxs;
-            digits_quad(xq, w, sxs);
-            const int b = t >> 3, q = t & 7;
-            int *d = S.dig + (size_t)b * 28;
-            d[q] = w[0];
-            d[8 + q] = w[1];
-            d[16 + q] = w[2];
-            if (q == 0) d[27] = __float_as_int(sxs);
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int t = base + u * nct;
+                if (t >= nq) break;                     // uniform across the warp
+                float4 v = xq[u];
+                if (ph.norm) {
+                    const float4 wq = __ldg(w4 + t);
+                    v.x = __fmul_rn(__fmul_rn(v.x, scale), wq.x);
+                    v.y = __fmul_rn(__fmul_rn(v.y, scale), wq.y);
+                    v.z = __fmul_rn(__fmul_rn(v.z, scale), wq.z);
+                    v.w = __fmul_rn(__fmul_rn(v.w, scale), wq.w);
+                    if (xn4) xn4[t] = v;
+                }
+                int   w[3];
+                float sxs;
+                digits_quad(v, w, sxs);
+                const int b = t >> 3, q = t & 7;
+                int *d = S.dig + (size_t)b * 28;
+                d[q] = w[0];
+                d[8 + q] = w[1];
+                d[16 + q] = w[2];
+                if (q == 0) d[27] = __float_as_int(sxs);
+            }
         }
     }
     named_bar(1, nct);
 
     if (det) det[0] = globaltimer_ns();
+    // the residual this CTA's rows add to (its own rows: no other CTA writes
+    // them in this phase), fetched now so the epilogue does not wait for it
+    float yprev = 0.0f;
+    if (ph.epi == EPI_ADD && tid < nrows) yprev = __ldcg(ph.y + r0 + tid);
     // ---- main loop ------------------------------------------------------------
     const bool active = warp < nkg * rowpar;
     const int  g = active ? warp % nkg : 0, rp = active ? warp / nkg : 0;
@@ -450,6 +477,10 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
         det[1] = globaltimer_ns();
         det[3] = waited;
     }
+    if (next) {
+        if (tid == 0) attn_prefetch(a, *next, S.pos, hd);
+        for (int j = tid; j < hd; j += nct) S.cs[j] = a.rope_cs[(size_t)S.pos * hd + j];
+    }
 
     // ---- epilogue over this CTA's rows --------------------------------------
     const int epi = ph.epi;
@@ -465,7 +496,7 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
     ArgBest best{-INFINITY, -1};
     for (int r = tid; r < nrows; r += nct) {
         const float acc = row_total(S.red, r, nkg, red8);
-        if (epi == EPI_ADD) y[r0 + r] = __ldcg(y + r0 + r) + acc;
+        if (epi == EPI_ADD) y[r0 + r] = (r == tid ? yprev : __ldcg(y + r0 + r)) + acc;
         else y[r0 + r] = acc;
         if (epi == EPI_ARGMAX) best = arg_better(best, ArgBest{acc, r0 + r});
     }
@@ -503,7 +534,7 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
             bb = arg_better(bb, ArgBest{__ldcg(a.part_val + c), __ldcg(a.part_idx + c)});
         const float l0 = __ldcg(y);
         const int   tok = (bb.i < 0 || isnan(l0)) ? 0 : bb.i;
-        const int   pos = a.st->pos;
+        const int   pos = S.pos;
         if (a.tok_hist) a.tok_hist[pos] = tok;
         a.st->token = tok;
         if (a.advance_pos) a.st->pos = pos + 1;
@@ -516,40 +547,47 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
 // query head h of the group on warp h.  Same arithmetic per split as
 // k_attention; partials go to global memory for the merge phase.
 template <int HD, int NREP>
-__device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const MegaShared &S, int &att_sb)
+__device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const MegaShared &S, int &att_sb, int p_idx)
 {
-    constexpr int RS = attn_row_stride<HD>();
-    constexpr int LPR = HD / 4, RPW = 32 / LPR;
+    // profiling (CTA 0): after the Q/K/V prologue, after the position loop,
+    // after the split ticket, and the time its merge took (0 unless last)
+    unsigned long long *det = (a.phase_detail && blockIdx.x == 0 && threadIdx.x == 0)
+                                  ? a.phase_detail + (size_t)p_idx * 4 : nullptr;
+    // K/V rows sit unpadded in shared memory (one bulk copy per sub-chunk
+    // and matrix); the score loop reads a row's float4 columns in an order
+    // rotated by the lane, so the 32 lanes' rows still spread over the banks
+    constexpr int RS = HD;
+    constexpr int LPR = HD / 4, RPW = 32 / LPR, NC4 = HD / 4;
+    static_assert((NC4 & (NC4 - 1)) == 0, "head_dim / 4 a power of two");
     __shared__ __align__(16) float q_s[NREP * HD];
-    __shared__ __align__(16) float knew[HD], vnew[HD], cs_s[HD];
+    __shared__ __align__(16) float knew[HD], vnew[HD];
     const int nct = MEGA_NCW * 32, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int item = blockIdx.x;
     const bool has = item < a.n_kv * a.n_split;
     const int g = has ? item / a.n_split : 0, sp = has ? item % a.n_split : 0;
-    const int pos = a.st->pos, npos = pos + 1;
+    const int pos = S.pos, npos = pos + 1;
     const int chunk = (npos + a.n_split - 1) / a.n_split;
     const int t0 = min(npos, sp * chunk), t1 = has ? min(npos, t0 + chunk) : t0;
     const int nsub = (t1 - t0 + ATT_SUB - 1) / ATT_SUB;
     float *kbase = ph.kc + (size_t)g * a.n_ctx * HD;
     float *vbase = ph.vc + (size_t)g * a.n_ctx * HD;
-    // rows of the slice below the current position, one per lane of warp 0
+    // rows of the slice below the current position (contiguous in the
+    // head-major cache): one bulk copy for K, one for V, by one thread
     auto issue = [&](int sbl) {
         const int gsb = att_sb + sbl;
         const int c0 = t0 + sbl * ATT_SUB;
         const int c1 = min(min(t1, c0 + ATT_SUB), pos);
         const int nr = c1 > c0 ? c1 - c0 : 0;
         float *kb = S.kvbuf + (size_t)(gsb & 1) * 2 * ATT_SUB * RS;
-        if (lane == 0) mbar_expect_tx(&S.abar[gsb & 1], (uint32_t)(2 * nr * HD * sizeof(float)));
-        __syncwarp();
-        if (lane < nr) {
-            bulk_g2s(kb + lane * RS, kbase + (size_t)(c0 + lane) * HD, HD * sizeof(float), &S.abar[gsb & 1]);
-            bulk_g2s(kb + ATT_SUB * RS + lane * RS, vbase + (size_t)(c0 + lane) * HD, HD * sizeof(float),
-                     &S.abar[gsb & 1]);
+        const uint32_t bytes = (uint32_t)(nr * HD * sizeof(float));
+        mbar_expect_tx(&S.abar[gsb & 1], 2 * bytes);
+        if (nr > 0) {
+            bulk_g2s(kb, kbase + (size_t)c0 * HD, bytes, &S.abar[gsb & 1]);
+            bulk_g2s(kb + ATT_SUB * RS, vbase + (size_t)c0 * HD, bytes, &S.abar[gsb & 1]);
         }
     };
-    if (warp == 0 && nsub > 0) issue(0);
-    for (int j = tid; j < HD; j += nct) cs_s[j] = a.rope_cs[(size_t)pos * HD + j];
-    named_bar(1, nct);
+    if (tid == 0 && nsub > 0) issue(0);
+    const float *cs_s = S.cs;
     const int qdim = a.n_head * HD, kvdim = a.n_kv * HD;
     for (int i = tid; i < NREP * (HD / 2); i += nct) {
         const int h = i / (HD / 2), j = i % (HD / 2), row = (g * NREP + h) * HD;
@@ -570,6 +608,7 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
         vnew[j] = v0; vnew[j + HD / 2] = v1;
     }
     named_bar(1, nct);
+    if (det) det[0] = globaltimer_ns();
     if (has && sp == 0)
         for (int j = tid; j < HD; j += nct) {
             kbase[(size_t)pos * HD + j] = knew[j];
@@ -581,7 +620,7 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int sbl = 0; sbl < nsub; sbl++) {
         const int gsb = att_sb + sbl;
-        if (warp == 0 && sbl + 1 < nsub) issue(sbl + 1);
+        if (tid == 0 && sbl + 1 < nsub) issue(sbl + 1);
         mbar_wait<true>(&S.abar[gsb & 1], (gsb >> 1) & 1, a.status);
         const float *kb = S.kvbuf + (size_t)(gsb & 1) * 2 * ATT_SUB * RS;
         const float *vb = kb + ATT_SUB * RS;
@@ -594,7 +633,8 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
                 const float4 *q4 = reinterpret_cast<const float4 *>(q_s + h * HD);
                 float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
 #pragma unroll 8
-                for (int j = 0; j < HD / 4; j++) {
+                for (int j0 = 0; j0 < NC4; j0++) {
+                    const int    j = (j0 + lane) & (NC4 - 1);
                     const float4 kv = k4[j], qv = q4[j];
                     d0 = fmaf(qv.x, kv.x, d0);
                     d1 = fmaf(qv.y, kv.y, d1);
@@ -627,6 +667,7 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
         named_bar(1, nct);            // the buffer is free for sub-chunk sbl + 2
     }
     att_sb += nsub;
+    if (det) det[1] = globaltimer_ns();
     if (has && hw) {
 #pragma unroll
         for (int o = LPR; o < 32; o <<= 1) {
@@ -660,7 +701,11 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
         s_last = last;
     }
     named_bar(1, nct);
-    if (!s_last) return;
+    if (det) det[2] = globaltimer_ns();
+    if (!s_last) {
+        if (det) det[3] = 0;
+        return;
+    }
     __threadfence();
     // all partials of the head group into shared memory at once (the K/V
     // buffers are free), then the merge reads only shared memory
@@ -668,21 +713,33 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
     constexpr int PER = NREP * (HD + 4);     // floats of one split's partials
     const float4 *src4 = reinterpret_cast<const float4 *>(a.apart + (size_t)g * ns * PER);
     float4       *gat4 = reinterpret_cast<float4 *>(S.kvbuf);
-    for (int i = tid; i < ns * PER / 4; i += nct) gat4[i] = __ldcg(src4 + i);
+    {
+        const int n4 = ns * PER / 4;
+        for (int base = tid; base < n4; base += 2 * nct) {   // two loads in flight per thread
+            const float4 t0 = __ldcg(src4 + base);
+            const bool   two = base + nct < n4;
+            float4       t1 = t0;
+            if (two) t1 = __ldcg(src4 + base + nct);
+            gat4[base] = t0;
+            if (two) gat4[base + nct] = t1;
+        }
+    }
     named_bar(1, nct);
     const float *gat = S.kvbuf;
-    if (tid < NREP) {
-        const int hh = tid;
+    if (warp < NREP) {                         // warp hh: its head's split weights, lanes over splits
+        const int hh = warp;
         float M = -INFINITY;
-        for (int r = 0; r < ns; r++) M = fmaxf(M, gat[r * PER + hh * (HD + 4) + HD]);
+        for (int r = lane; r < ns; r += 32) M = fmaxf(M, gat[r * PER + hh * (HD + 4) + HD]);
+        M = warp_max(M);
         float L = 0.0f;
-        for (int r = 0; r < ns; r++) {
+        for (int r = lane; r < ns; r += 32) {
             const float ms = gat[r * PER + hh * (HD + 4) + HD];
             const float w = ms > -INFINITY ? expf(ms - M) : 0.0f;
             wsp[hh][r] = w;
             L += gat[r * PER + hh * (HD + 4) + HD + 1] * w;
         }
-        invl[hh] = L > 0.0f ? 1.0f / L : 0.0f;
+        L = warp_sum(L);
+        if (lane == 0) invl[hh] = L > 0.0f ? 1.0f / L : 0.0f;
     }
     named_bar(1, nct);
     for (int i = tid; i < NREP * HD; i += nct) {
@@ -692,22 +749,22 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
         a.att[(g * NREP + hh) * HD + d] = o * invl[hh];
     }
     if (tid == 0) a.att_ticket[g] = 0u;     // for the next layer (after a grid barrier)
+    if (det) det[3] = globaltimer_ns() - det[2];
 }
 
 // L2 prefetch of the K and V rows this CTA's attention item will read (the
 // positions below the current one of its split), issued a phase early.
-template <int HD>
-__device__ __forceinline__ void attn_prefetch(const MegaArgs &a, const MegaPhase &ph)
+__device__ __forceinline__ void attn_prefetch(const MegaArgs &a, const MegaPhase &ph, int pos, int hd)
 {
     const int item = blockIdx.x;
     if (item >= a.n_kv * a.n_split) return;
     const int g = item / a.n_split, sp = item % a.n_split;
-    const int pos = a.st->pos, npos = pos + 1;
+    const int npos = pos + 1;
     const int chunk = (npos + a.n_split - 1) / a.n_split;
     const int t0 = min(npos, sp * chunk), t1 = min(min(npos, t0 + chunk), pos);
     if (t1 <= t0) return;
-    const size_t   off = ((size_t)g * a.n_ctx + t0) * HD;
-    const uint32_t bytes = (uint32_t)((t1 - t0) * HD * sizeof(float));
+    const size_t   off = ((size_t)g * a.n_ctx + t0) * hd;
+    const uint32_t bytes = (uint32_t)((t1 - t0) * hd * sizeof(float));
     prefetch_l2(ph.kc + off, bytes);
     prefetch_l2(ph.vc + off, bytes);
 }
@@ -743,31 +800,50 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a)
     S.dsum = reinterpret_cast<double *>(smem + P.dsum);
     S.argsh = reinterpret_cast<ArgBest *>(smem + P.argsh);
     __shared__ MegaRing ring_state;
+    __shared__ int pos_s;
+    __shared__ __align__(16) MegaPhase ph_s[2];
+    __shared__ __align__(8) uint64_t desc_bar;
+    __shared__ __align__(16) float cs_row[HD];
     S.rc = &ring_state;
+    S.cs = cs_row;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < a.nst; s++) mbar_init(&S.full[s], 1);
         mbar_init(&S.abar[0], 1);
         mbar_init(&S.abar[1], 1);
+        mbar_init(&desc_bar, 1);
         mbar_init_fence();
+        pos_s = a.st->pos;            // stable for the whole step
+        ph_s[0] = a.ph[0];
         S.rc->issued = 0;
         ring_load_phase(a, S.rc, 0);
         for (int s = 0; s < a.nst; s++) S.rc->done[s] = 0u;
         for (int s = 0; s < a.nst; s++) ring_issue(a, S, s);     // the first chunks
     }
     __syncthreads();
+    S.pos = pos_s;
 
     // ---- consumers -------------------------------------------------------------
     if (a.phase_ns && blockIdx.x == 0 && threadIdx.x == 0) a.phase_ns[0] = globaltimer_ns();
     int ring_s = 0, att_sb = 0;
     for (int p = 0; p < a.n_ph; p++) {
-        const MegaPhase &ph = a.ph[p];
-        const int        kind = ph.kind;
+        // descriptors live in shared memory: phase p's arrived by a bulk
+        // copy issued at the start of phase p-1, and phase p+1's is issued
+        // now, so no phase starts with a global-memory round trip
+        if (p > 0) mbar_wait<true>(&desc_bar, (unsigned)(p - 1) & 1u, a.status);
+        const MegaPhase &ph = ph_s[p & 1];
+        if (threadIdx.x == 0 && p + 1 < a.n_ph) {
+            // the reads of that buffer (phase p-1's descriptor) are done:
+            // every thread has passed the grid barrier
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            mbar_expect_tx(&desc_bar, (uint32_t)sizeof(MegaPhase));
+            bulk_g2s(&ph_s[(p + 1) & 1], a.ph + p + 1, (uint32_t)sizeof(MegaPhase), &desc_bar);
+        }
+        const int kind = ph.kind;
         if (kind == PH_GEMV) {
-            if (threadIdx.x == 0 && p + 1 < a.n_ph && a.ph[p + 1].kind == PH_ATTN) attn_prefetch<HD>(a, a.ph[p + 1]);
-            mega_gemv(a, ph, S, ring_s, p);
+            mega_gemv(a, ph, S, ring_s, p, ph.next_attn ? &ph_s[(p + 1) & 1] : nullptr, HD);
         } else if (kind == PH_ATTN) {
-            mega_attention<HD, NREP>(a, ph, S, att_sb);
+            mega_attention<HD, NREP>(a, ph, S, att_sb, p);
         } else {
             mega_embed(a);
         }
@@ -784,7 +860,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a)
     }
     // a LAYERS stage advances its position once every phase is done; no
     // CTA reads it after the last attention phase
-    if (a.layers_advance && blockIdx.x == 0 && threadIdx.x == 0) a.st->pos = a.st->pos + 1;
+    if (a.layers_advance && blockIdx.x == 0 && threadIdx.x == 0) a.st->pos = S.pos + 1;
     if (a.phase_ns && blockIdx.x == 0 && threadIdx.x == 0) a.phase_ns[a.n_ph] = globaltimer_ns();
     // the last CTA out rewinds the barrier counter for the next launch: every
     // CTA that counted itself here has left its last grid barrier

@@ -725,7 +725,10 @@ static int check_status(ecu_ctx *c)
     StepState s;
     CK(cudaMemcpy(&s, c->st, sizeof s, cudaMemcpyDeviceToHost));
     if (s.status) {
-        if (c->mega) CK(cudaMemset(c->margs.bar, 0, (4 + (size_t)c->g.n_head_kv) * sizeof(unsigned)));
+        if (c->mega) {
+            CK(cudaMemset(c->margs.bar, 0, (4 + (size_t)c->g.n_head_kv) * sizeof(unsigned)));
+            CK(cudaMemset(c->margs.flags, 0, (size_t)c->mega_grid * 16 * sizeof(unsigned long long)));
+        }
         if (s.status & ECU_STATUS_BADTOKEN)
             ecu_set_error(nullptr, 0, "the device-resident token is outside the vocabulary (%d)", c->g.n_vocab);
         else
@@ -832,6 +835,7 @@ static int mega_setup(ecu_ctx *c)
     cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, c->device);
     if (!coop) return no("no cooperative launch");
     const int grid = c->sms;
+    if (grid > MEGA_THREADS) return no("more SMs than threads to poll the grid barrier");
     // ring geometry: ECU_MEGA_RING stages (default 2) over MEGA_RING_BYTES
     int nst = 2;
     if (const char *r = getenv("ECU_MEGA_RING")) nst = std::max(2, std::min(MEGA_MAX_STAGES, atoi(r)));
@@ -889,7 +893,7 @@ static int mega_setup(ecu_ctx *c)
         add(mega_gemv_phase(c->out, grid, stage_bytes, 1, EPI_ARGMAX, c->state, c->out_norm, c->logits, xn_tmp),
             "gemv_head_argmax", gemv_bytes(c->out, EPI_ARGMAX) + 4.0 * g.n_embd);
     for (size_t i = 0; i + 1 < ph.size(); i++) ph[i].next_attn = ph[i + 1].kind == PH_ATTN ? 1 : 0;
-    int red = 0;
+    int red = MEGA_NCW * (hd + 4);          // attention: the position groups' partials
     for (auto &p : ph)
         if (p.kind == PH_GEMV) {
             // Q4_0 phases keep 8 partials per row and k-group when they fit
@@ -920,7 +924,9 @@ static int mega_setup(ecu_ctx *c)
     float *pval = c->dalloc<float>((size_t)grid);
     int *pidx = c->dalloc<int>((size_t)grid);
     unsigned *ctr = c->dalloc<unsigned>(4 + (size_t)g.n_head_kv);
-    if (!d_ph || !apart || !pval || !pidx || !ctr || (full && !xn_tmp)) return -1;
+    unsigned long long *flags = c->dalloc<unsigned long long>((size_t)grid * 16);
+    if (!d_ph || !apart || !pval || !pidx || !ctr || !flags || (full && !xn_tmp)) return -1;
+    CK(cudaMemset(flags, 0, (size_t)grid * 16 * sizeof(unsigned long long)));
     CK(cudaMemcpy(d_ph, ph.data(), ph.size() * sizeof(MegaPhase), cudaMemcpyHostToDevice));
     CK(cudaMemset(ctr, 0, (4 + (size_t)g.n_head_kv) * sizeof(unsigned)));
     MegaArgs &a = c->margs;
@@ -936,6 +942,7 @@ static int mega_setup(ecu_ctx *c)
     a.part_val = pval;
     a.part_idx = pidx;
     a.bar = ctr;
+    a.flags = flags;
     a.ticket = ctr + 2;
     a.att_ticket = ctr + 4;
     a.st = c->st;
@@ -1044,9 +1051,11 @@ static int mega_profile(ecu_ctx *c, int n_steps, ecu_kprof *out, int max_kinds)
             // main loop, waiting for ring stages inside it, epilogue)
             const unsigned long long *dt = ns.data() + np + 1 + 4 * (size_t)p;
             if (dt[0] && dt[1] && dt[2]) {
-                const char *part[4] = {"prologue", "main", "epilogue", "ring_wait"};
+                // attention phases: [3] is when KV head 0's merge ended
+                const bool att = c->ph_bytes[p] < 0;
+                const char *part[4] = {"prologue", "main", "epilogue", att ? "merged" : "ring_wait"};
                 const double v[4] = {(double)(dt[0] - ns[p]), (double)(dt[1] - dt[0]), (double)(dt[2] - dt[1]),
-                                     (double)dt[3]};
+                                     att ? (dt[3] > ns[p] ? (double)(dt[3] - ns[p]) : 0.0) : (double)dt[3]};
                 for (int q = 0; q < 4; q++) {
                     char nm[32];
                     snprintf(nm, sizeof nm, "%.20s:%s", c->ph_kind[p], part[q]);

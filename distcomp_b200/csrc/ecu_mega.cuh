@@ -74,7 +74,8 @@ struct MegaArgs {
     float           *part_val;      // argmax: per-CTA best
     int             *part_idx;
     unsigned        *ticket;        // argmax ticket, zero between steps
-    unsigned        *bar;           // grid-barrier counters [2], zero between launches
+    unsigned        *bar;           // [1]: CTAs done with the launch, [3]: launches so far
+    unsigned long long *flags;      // grid barrier: per CTA a 128-byte line holding its last epoch
     unsigned        *att_ticket;    // per KV head: splits done, zero between phases
     StepState       *st;
     int             *tok_hist;
@@ -102,21 +103,33 @@ __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p)
     return v;
 }
 
-// All consumer threads of every CTA call this with the same k (0, 1, 2, ...).
-// Writes before it are visible to every CTA after it.  The spin gives up
-// after ECU_WAIT_NS and flags the step as failed.  phase_ns[k + 1] = CTA 0's
-// exit time (phase_ns[0] is the kernel's start).
-__device__ __forceinline__ void grid_sync(const MegaArgs &a, int k, int nct)
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long *p)
+{
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// All threads of every CTA call this with the same k (0, 1, 2, ...).
+// Writes before it are visible to every CTA after it.  Each CTA publishes
+// its arrival as an epoch number in its own 128-byte flag (a release store,
+// no atomic to serialise on), and thread i < gridDim.x polls CTA i's flag
+// (acquire), so one round of polling sees every arrival.  The epoch is the
+// launch number << 20 plus k + 1, so flags never need resetting between
+// launches.  The spin gives up after ECU_WAIT_NS and flags the step as
+// failed.  phase_ns[k + 1] = CTA 0's exit time (phase_ns[0] the start).
+__device__ __forceinline__ void grid_sync(const MegaArgs &a, int k, int nct, unsigned long long epoch)
 {
     named_bar(1, nct);
-    if (threadIdx.x == 0) {
-        // release: this CTA's writes (ordered before by the named barrier)
-        // are visible before its arrival is counted; acquire in the spin
-        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.bar) : "memory");
-        const unsigned target = (unsigned)(k + 1) * gridDim.x;
-        if (ld_acquire_u32(a.bar) < target) {
+    const unsigned long long want = epoch + (unsigned long long)(k + 1);
+    if (threadIdx.x == 0)
+        asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(a.flags + (size_t)blockIdx.x * 16), "l"(want)
+                     : "memory");
+    if (threadIdx.x < gridDim.x) {
+        const unsigned long long *f = a.flags + (size_t)threadIdx.x * 16;
+        if (ld_acquire_u64(f) < want) {
             const uint64_t t0 = globaltimer_ns();
-            for (unsigned it = 1; ld_acquire_u32(a.bar) < target; it++) {
+            for (unsigned it = 1; ld_acquire_u64(f) < want; it++) {
                 if ((it & 255u) == 0) {
                     if (*reinterpret_cast<volatile int *>(a.status) != 0) break;   // the step already failed
                     if (globaltimer_ns() - t0 > ECU_WAIT_NS) {
@@ -126,9 +139,9 @@ __device__ __forceinline__ void grid_sync(const MegaArgs &a, int k, int nct)
                 }
             }
         }
-        if (a.phase_ns && blockIdx.x == 0) a.phase_ns[k + 1] = globaltimer_ns();
     }
     named_bar(1, nct);
+    if (a.phase_ns && blockIdx.x == 0 && threadIdx.x == 0) a.phase_ns[k + 1] = globaltimer_ns();
 }
 
 // ------------------------------------------------------------ smem layout --
@@ -550,7 +563,7 @@ template <int HD, int NREP>
 __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const MegaShared &S, int &att_sb, int p_idx)
 {
     // profiling (CTA 0): after the Q/K/V prologue, after the position loop,
-    // after the split ticket, and the time its merge took (0 unless last)
+    // after the split ticket; and when KV head 0's merge ended
     unsigned long long *det = (a.phase_detail && blockIdx.x == 0 && threadIdx.x == 0)
                                   ? a.phase_detail + (size_t)p_idx * 4 : nullptr;
     // K/V rows sit unpadded in shared memory (one bulk copy per sub-chunk
@@ -568,25 +581,26 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
     const int pos = S.pos, npos = pos + 1;
     const int chunk = (npos + a.n_split - 1) / a.n_split;
     const int t0 = min(npos, sp * chunk), t1 = has ? min(npos, t0 + chunk) : t0;
-    const int nsub = (t1 - t0 + ATT_SUB - 1) / ATT_SUB;
+    const int nround = (t1 - t0 + 2 * ATT_SUB - 1) / (2 * ATT_SUB);   // 64 positions a round
     float *kbase = ph.kc + (size_t)g * a.n_ctx * HD;
     float *vbase = ph.vc + (size_t)g * a.n_ctx * HD;
-    // rows of the slice below the current position (contiguous in the
-    // head-major cache): one bulk copy for K, one for V, by one thread
-    auto issue = [&](int sbl) {
-        const int gsb = att_sb + sbl;
-        const int c0 = t0 + sbl * ATT_SUB;
+    // half hf (32 rows) of round r of the slice below the current position
+    // (contiguous in the head-major cache): one bulk copy for K, one for V;
+    // thread 0 issues half 0, thread 32 half 1
+    auto issue = [&](int r, int hf) {
+        const int c0 = t0 + r * 2 * ATT_SUB + hf * ATT_SUB;
         const int c1 = min(min(t1, c0 + ATT_SUB), pos);
         const int nr = c1 > c0 ? c1 - c0 : 0;
-        float *kb = S.kvbuf + (size_t)(gsb & 1) * 2 * ATT_SUB * RS;
+        float *kb = S.kvbuf + (size_t)hf * ATT_SUB * RS;
+        float *vb = S.kvbuf + (size_t)(2 + hf) * ATT_SUB * RS;
         const uint32_t bytes = (uint32_t)(nr * HD * sizeof(float));
-        mbar_expect_tx(&S.abar[gsb & 1], 2 * bytes);
+        mbar_expect_tx(&S.abar[hf], 2 * bytes);
         if (nr > 0) {
-            bulk_g2s(kb, kbase + (size_t)c0 * HD, bytes, &S.abar[gsb & 1]);
-            bulk_g2s(kb + ATT_SUB * RS, vbase + (size_t)c0 * HD, bytes, &S.abar[gsb & 1]);
+            bulk_g2s(kb, kbase + (size_t)c0 * HD, bytes, &S.abar[hf]);
+            bulk_g2s(vb, vbase + (size_t)c0 * HD, bytes, &S.abar[hf]);
         }
     };
-    if (tid == 0 && nsub > 0) issue(0);
+    if (nround > 0 && (tid & 31) == 0 && tid < 64) issue(0, tid >> 5);
     const float *cs_s = S.cs;
     const int qdim = a.n_head * HD, kvdim = a.n_kv * HD;
     for (int i = tid; i < NREP * (HD / 2); i += nct) {
@@ -614,18 +628,20 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
             kbase[(size_t)pos * HD + j] = knew[j];
             vbase[(size_t)pos * HD + j] = vnew[j];
         }
-    const int  h = warp;              // one query head per warp
-    const bool hw = warp < NREP;
+    // warp (h, grp): query head h, positions grp*Q .. grp*Q+Q-1 of each
+    // round's 64 (G = 16/NREP groups), so the serial V accumulation is Q long
+    constexpr int G = MEGA_NCW / NREP, Q = 2 * ATT_SUB / G;
+    static_assert(G >= 1 && Q >= 1 && Q <= ATT_SUB, "position groups");
+    const int h = warp % NREP, grp = warp / NREP;
+    const int hf = (grp * Q) / ATT_SUB, off = grp * Q - hf * ATT_SUB;
     float  m_run = -INFINITY, l_run = 0.0f;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int sbl = 0; sbl < nsub; sbl++) {
-        const int gsb = att_sb + sbl;
-        if (tid == 0 && sbl + 1 < nsub) issue(sbl + 1);
-        mbar_wait<true>(&S.abar[gsb & 1], (gsb >> 1) & 1, a.status);
-        const float *kb = S.kvbuf + (size_t)(gsb & 1) * 2 * ATT_SUB * RS;
-        const float *vb = kb + ATT_SUB * RS;
-        const int    c0 = t0 + sbl * ATT_SUB, cn = min(ATT_SUB, t1 - c0);
-        if (hw) {
+    for (int r = 0; r < nround; r++) {
+        const int c0 = t0 + r * 2 * ATT_SUB + grp * Q, cn = max(0, min(Q, t1 - c0));
+        if (cn > 0) {
+            mbar_wait<true>(&S.abar[hf], (unsigned)(att_sb + r) & 1u, a.status);
+            const float *kb = S.kvbuf + (size_t)hf * ATT_SUB * RS + (size_t)off * RS;
+            const float *vb = S.kvbuf + (size_t)(2 + hf) * ATT_SUB * RS + (size_t)off * RS;
             const float *krow = (c0 + lane == pos) ? knew : kb + lane * RS;
             float s = -INFINITY;
             if (lane < cn) {
@@ -664,23 +680,55 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
                 }
             }
         }
-        named_bar(1, nct);            // the buffer is free for sub-chunk sbl + 2
+        named_bar(1, nct);                          // both halves are free
+        if (r + 1 < nround && (tid & 31) == 0 && tid < 64) issue(r + 1, tid >> 5);
     }
-    att_sb += nsub;
+    att_sb += nround;                               // one phase of each half barrier per round
     if (det) det[1] = globaltimer_ns();
-    if (has && hw) {
+    // this warp's partial into shared memory; group 0 of each head merges
+    // the G group partials in group order into the CTA's partial
+    float *gpart = S.red;                           // [G][NREP][HD + 4]
 #pragma unroll
-        for (int o = LPR; o < 32; o <<= 1) {
-            acc.x += __shfl_xor_sync(0xffffffffu, acc.x, o);
-            acc.y += __shfl_xor_sync(0xffffffffu, acc.y, o);
-            acc.z += __shfl_xor_sync(0xffffffffu, acc.z, o);
-            acc.w += __shfl_xor_sync(0xffffffffu, acc.w, o);
+    for (int o = LPR; o < 32; o <<= 1) {
+        acc.x += __shfl_xor_sync(0xffffffffu, acc.x, o);
+        acc.y += __shfl_xor_sync(0xffffffffu, acc.y, o);
+        acc.z += __shfl_xor_sync(0xffffffffu, acc.z, o);
+        acc.w += __shfl_xor_sync(0xffffffffu, acc.w, o);
+    }
+    {
+        float *gp = gpart + (size_t)(grp * NREP + h) * (HD + 4);
+        if (lane < LPR) reinterpret_cast<float4 *>(gp)[lane] = acc;
+        if (lane == 0) {
+            gp[HD] = m_run;
+            gp[HD + 1] = l_run;
+        }
+    }
+    named_bar(1, nct);
+    if (has && grp == 0) {
+        float M = -INFINITY;
+#pragma unroll
+        for (int q = 0; q < G; q++) M = fmaxf(M, gpart[(q * NREP + h) * (HD + 4) + HD]);
+        float  L = 0.0f;
+        float4 o4 = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int q = 0; q < G; q++) {
+            const float *gp = gpart + (size_t)(q * NREP + h) * (HD + 4);
+            const float  mq = gp[HD];
+            const float  w = mq > -INFINITY ? expf(mq - M) : 0.0f;
+            L += gp[HD + 1] * w;
+            if (lane < LPR) {
+                const float4 v = reinterpret_cast<const float4 *>(gp)[lane];
+                o4.x = fmaf(v.x, w, o4.x);
+                o4.y = fmaf(v.y, w, o4.y);
+                o4.z = fmaf(v.z, w, o4.z);
+                o4.w = fmaf(v.w, w, o4.w);
+            }
         }
         float *dst = a.apart + ((size_t)(g * a.n_split + sp) * NREP + h) * (HD + 4);
-        if (lane < LPR) reinterpret_cast<float4 *>(dst)[lane] = acc;
+        if (lane < LPR) reinterpret_cast<float4 *>(dst)[lane] = o4;
         if (lane == 0) {
-            dst[HD] = m_run;
-            dst[HD + 1] = l_run;
+            dst[HD] = M;
+            dst[HD + 1] = L;
         }
     }
     // the K/V buffers were filled by the async proxy and read here; the next
@@ -702,10 +750,7 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
     }
     named_bar(1, nct);
     if (det) det[2] = globaltimer_ns();
-    if (!s_last) {
-        if (det) det[3] = 0;
-        return;
-    }
+    if (!s_last) return;
     __threadfence();
     // all partials of the head group into shared memory at once (the K/V
     // buffers are free), then the merge reads only shared memory
@@ -749,7 +794,8 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
         a.att[(g * NREP + hh) * HD + d] = o * invl[hh];
     }
     if (tid == 0) a.att_ticket[g] = 0u;     // for the next layer (after a grid barrier)
-    if (det) det[3] = globaltimer_ns() - det[2];
+    // profiling: when KV head 0's merge was done (whichever CTA did it)
+    if (a.phase_detail && g == 0 && tid == 0) a.phase_detail[(size_t)p_idx * 4 + 3] = globaltimer_ns();
 }
 
 // L2 prefetch of the K and V rows this CTA's attention item will read (the
@@ -801,6 +847,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a)
     S.argsh = reinterpret_cast<ArgBest *>(smem + P.argsh);
     __shared__ MegaRing ring_state;
     __shared__ int pos_s;
+    __shared__ unsigned launch_s;
     __shared__ __align__(16) MegaPhase ph_s[2];
     __shared__ __align__(8) uint64_t desc_bar;
     __shared__ __align__(16) float cs_row[HD];
@@ -814,6 +861,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a)
         mbar_init(&desc_bar, 1);
         mbar_init_fence();
         pos_s = a.st->pos;            // stable for the whole step
+        launch_s = a.bar[3];
         ph_s[0] = a.ph[0];
         S.rc->issued = 0;
         ring_load_phase(a, S.rc, 0);
@@ -822,6 +870,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a)
     }
     __syncthreads();
     S.pos = pos_s;
+    const unsigned long long epoch = (unsigned long long)launch_s << 20;
 
     // ---- consumers -------------------------------------------------------------
     if (a.phase_ns && blockIdx.x == 0 && threadIdx.x == 0) a.phase_ns[0] = globaltimer_ns();
@@ -847,7 +896,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a)
         } else {
             mega_embed(a);
         }
-        if (p + 1 < a.n_ph) grid_sync(a, p, nct);
+        if (p + 1 < a.n_ph) grid_sync(a, p, nct, epoch);
     }
     // ring and K/V copies still in flight (none, unless a wait gave up) land
     // before this CTA may exit
@@ -856,7 +905,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a)
         const int n = S.rc->issued;
         for (int j = max(0, n - a.nst); j < n; j++)
             mbar_drain(&S.full[j % a.nst], (unsigned)(j / a.nst) & 1u, ECU_WAIT_NS);
-        for (int j = max(0, att_sb - 2); j < att_sb; j++) mbar_drain(&S.abar[j & 1], (j >> 1) & 1, ECU_WAIT_NS);
+        for (int k = 0; k < 2 && att_sb > 0; k++) mbar_drain(&S.abar[k], (unsigned)(att_sb - 1) & 1u, ECU_WAIT_NS);
     }
     // a LAYERS stage advances its position once every phase is done; no
     // CTA reads it after the last attention phase
@@ -867,8 +916,8 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a)
     if (threadIdx.x == 0) {
         __threadfence();
         if (atomicAdd(a.bar + 1, 1u) == gridDim.x - 1) {
-            a.bar[0] = 0u;
             a.bar[1] = 0u;
+            a.bar[3] = a.bar[3] + 1u;       // the next launch's epochs are above every flag
             __threadfence();
         }
     }

@@ -795,9 +795,11 @@ static MegaPhase mega_gemv_phase(const DevMat &m, int grid, unsigned stage_bytes
     int rpc = (m.n_out + grid - 1) / grid;
     if (epi == EPI_SWIGLU && (rpc & 1)) rpc++;        // whole gate/up pairs per CTA
     p.rpc = rpc;
-    p.sr = (int)std::min<size_t>((size_t)rpc, stage_bytes / m.row_bytes);
     p.nkg = m.n_in / 1024;
     p.rowpar = std::max(1, MEGA_NCW / p.nkg);
+    // rows per stage: as many as the stage holds (bytes in flight matter more
+    // than a partly empty last batch of 4 rows)
+    p.sr = (int)std::min<size_t>((size_t)rpc, stage_bytes / m.row_bytes);
     p.x = x;
     p.norm_w = norm_w;
     p.y = y;
@@ -897,8 +899,8 @@ static int mega_setup(ecu_ctx *c)
     for (auto &p : ph)
         if (p.kind == PH_GEMV) {
             // Q4_0 phases keep 8 partials per row and k-group when they fit
-            p.red8 = (p.fmt == 4 && p.rpc * p.nkg * 8 <= MEGA_RED8_MAX) ? 1 : 0;
-            red = std::max(red, p.rpc * p.nkg * (p.red8 ? 8 : 1));
+            p.red8 = (p.fmt == 4 && p.rpc * (p.nkg * 8 + 1) <= MEGA_RED8_MAX) ? 1 : 0;
+            red = std::max(red, p.red8 ? p.rpc * (p.nkg * 8 + 1) : p.rpc * p.nkg);
         }
     const size_t smem = mega_smem_total(hd, red);
     cudaFuncAttributes fa;
@@ -950,6 +952,7 @@ static int mega_setup(ecu_ctx *c)
     a.status = &c->st->status;
     a.rope_cs = c->rope_cs;
     a.phase_ns = nullptr;
+    a.phase_clk = nullptr;
     a.phase_detail = nullptr;
     a.advance_pos = full ? 1 : 0;
     a.layers_advance = full ? 0 : 1;
@@ -960,6 +963,8 @@ static int mega_setup(ecu_ctx *c)
     a.n_split = n_split;
     a.red_floats = red;
     a.nst = nst;
+    const char *pfe = getenv("ECU_MEGA_PF");
+    a.pf_stages = pfe ? std::max(0, atoi(pfe)) : 0;
     a.stage_bytes = stage_bytes;
     a.eps = g.eps;
     a.kscale = 1.0f / sqrtf((float)hd);
@@ -976,6 +981,7 @@ static int mega_launch(ecu_ctx *c, cudaStream_t s, unsigned long long *phase_ns,
 {
     MegaArgs a = c->margs;
     a.phase_ns = phase_ns;
+    a.phase_clk = phase_ns ? phase_ns + a.n_ph + 1 : nullptr;   // the profile buffer's second row
     a.phase_detail = detail;
     cudaLaunchConfig_t  cfg = {};
     cudaLaunchAttribute at;
@@ -1002,10 +1008,12 @@ static int mega_profile(ecu_ctx *c, int n_steps, ecu_kprof *out, int max_kinds)
 {
     const int np = c->margs.n_ph;
     unsigned long long *d_ns = nullptr;
-    CK(cudaMalloc(&d_ns, sizeof(unsigned long long) * (size_t)(np + 1 + 4 * np)));
-    CK(cudaMemset(d_ns, 0, sizeof(unsigned long long) * (size_t)(np + 1 + 4 * np)));
-    std::vector<unsigned long long> ns((size_t)np + 1 + 4 * np);
-    unsigned long long *d_det = d_ns + np + 1;
+    // [np + 1] global ns, [np + 1] CTA 0's SM clock at the same points, [np][4] detail
+    const size_t nbuf = 2 * ((size_t)np + 1) + 4 * (size_t)np;
+    CK(cudaMalloc(&d_ns, sizeof(unsigned long long) * nbuf));
+    CK(cudaMemset(d_ns, 0, sizeof(unsigned long long) * nbuf));
+    std::vector<unsigned long long> ns(nbuf);
+    unsigned long long *d_det = d_ns + 2 * (np + 1);
     int nk = 0;
     auto slot = [&](const char *kind, double bytes) -> ecu_kprof * {
         int k = 0;
@@ -1049,12 +1057,16 @@ static int mega_profile(ecu_ctx *c, int n_steps, ecu_kprof *out, int max_kinds)
             }
             // GEMV phases: where CTA 0 spent the phase (barrier + prologue,
             // main loop, waiting for ring stages inside it, epilogue)
-            const unsigned long long *dt = ns.data() + np + 1 + 4 * (size_t)p;
+            const unsigned long long *dt = ns.data() + 2 * ((size_t)np + 1) + 4 * (size_t)p;
+            const unsigned long long *clk = ns.data() + np + 1;
+            // CTA 0's SM cycles per ns over this launch
+            const double f = (double)(clk[np] - clk[0]) / (double)std::max<unsigned long long>(1, ns[np] - ns[0]);
             if (dt[0] && dt[1] && dt[2]) {
                 // attention phases: [3] is when KV head 0's merge ended
                 const bool att = c->ph_bytes[p] < 0;
                 const char *part[4] = {"prologue", "main", "epilogue", att ? "merged" : "ring_wait"};
-                const double v[4] = {(double)(dt[0] - ns[p]), (double)(dt[1] - dt[0]), (double)(dt[2] - dt[1]),
+                const double v[4] = {(double)(dt[0] - clk[p]) / f, (double)(dt[1] - dt[0]) / f,
+                                     (double)(dt[2] - dt[1]) / f,
                                      att ? (dt[3] > ns[p] ? (double)(dt[3] - ns[p]) : 0.0) : (double)dt[3]};
                 for (int q = 0; q < 4; q++) {
                     char nm[32];

@@ -34,7 +34,7 @@
 #define MEGA_MAX_STAGES 8
 #define MEGA_MAX_NB 512                  // input blocks of a GEMV (n_in <= 16384)
 #define MEGA_MAX_SPLIT 64                // position splits per KV head
-#define MEGA_RED8_MAX 6400               // floats of 8-lane row partials a GEMV phase may keep
+#define MEGA_RED8_MAX 6600               // floats of 8-lane row partials a GEMV phase may keep
 
 enum MegaKind : int { PH_EMBED = 0, PH_GEMV = 1, PH_ATTN = 2 };
 
@@ -82,14 +82,16 @@ struct MegaArgs {
     int             *status;
     const float     *rope_cs;
     unsigned long long *phase_ns;   // optional: CTA 0's time at the end of each phase
-    unsigned long long *phase_detail; // optional, GEMV phases [n_ph][4]: CTA 0's time after the
-                                    // prologue, after the main loop, after the epilogue, and the
-                                    // ns its warp 0 waited for ring stages
+    unsigned long long *phase_clk;  // optional, with phase_ns: CTA 0's SM clock at the same points
+    unsigned long long *phase_detail; // optional, [n_ph][4]: CTA 0's SM clock after the prologue,
+                                    // after the main loop, after the epilogue; [3]: GEMV: ns its
+                                    // warp 0 waited for ring stages, attention: when head 0 merged
     int              advance_pos;   // argmax epilogue advances st->pos (FULL)
     int              layers_advance;// LAYERS: st->pos++ once the last phase is done
     int              n_embd, n_head, n_kv, n_ctx, n_split;
     int              red_floats;    // row-partial floats the largest GEMV phase keeps
     int              nst;           // ring stages (<= MEGA_MAX_STAGES)
+    int              pf_stages;     // chunks warmed in L2 ahead of the ring
     unsigned         stage_bytes;   // bytes per ring stage (multiple of 128)
     float            eps, kscale;
 };
@@ -141,7 +143,10 @@ __device__ __forceinline__ void grid_sync(const MegaArgs &a, int k, int nct, uns
         }
     }
     named_bar(1, nct);
-    if (a.phase_ns && blockIdx.x == 0 && threadIdx.x == 0) a.phase_ns[k + 1] = globaltimer_ns();
+    if (a.phase_ns && blockIdx.x == 0 && threadIdx.x == 0) {
+        a.phase_ns[k + 1] = globaltimer_ns();
+        a.phase_clk[k + 1] = clock64();
+    }
 }
 
 // ------------------------------------------------------------ smem layout --
@@ -232,14 +237,23 @@ __device__ __forceinline__ void digit_offsets(const int (&xw)[3][8], int (&off)[
 
 // The ring's refill cursor: the next chunk to copy (phase, row offset) and
 // how many chunks were issued; per slot, the warps done with it.
-struct MegaRing {
-    int            p, i, issued;
-    // the current GEMV phase's rows of this CTA, cached so that a refill
-    // reads global memory only when it moves on to the next phase
-    const uint8_t *w;           // first row of this CTA
+// A position in this CTA's list of weight chunks (phase order), with the
+// current GEMV phase's rows cached so that moving on reads global memory
+// only at a phase change.
+struct ChunkCursor {
+    int            p, i;
+    const uint8_t *w;           // first row of this CTA in phase p
     unsigned       row_bytes;
     int            nrows, sr;
-    unsigned       done[MEGA_MAX_STAGES];
+};
+
+// The ring's cursors -- the next chunk to copy and, pf_stages chunks
+// further on, the next chunk to warm in L2 -- the chunks issued, and per
+// slot the warps done with it.
+struct MegaRing {
+    ChunkCursor cp, pf;
+    int         issued;
+    unsigned    done[MEGA_MAX_STAGES];
 };
 
 struct MegaShared {
@@ -256,33 +270,45 @@ struct MegaShared {
 };
 
 // Load phase p's geometry for this CTA into the ring cursor.
-__device__ __forceinline__ void ring_load_phase(const MegaArgs &a, MegaRing *rc, int p)
+__device__ __forceinline__ void cursor_load_phase(const MegaArgs &a, ChunkCursor *c, int p)
 {
-    rc->p = p;
-    rc->i = 0;
-    rc->nrows = 0;
+    c->p = p;
+    c->i = 0;
+    c->nrows = 0;
     if (p >= a.n_ph) return;
     const MegaPhase &q = a.ph[p];
     if (q.kind != PH_GEMV) return;
     const int r0 = blockIdx.x * q.rpc;
-    rc->nrows = max(0, min(q.n_out, r0 + q.rpc) - r0);
-    rc->w = q.w + (size_t)r0 * q.row_bytes;
-    rc->row_bytes = q.row_bytes;
-    rc->sr = q.sr;
+    c->nrows = max(0, min(q.n_out, r0 + q.rpc) - r0);
+    c->w = q.w + (size_t)r0 * q.row_bytes;
+    c->row_bytes = q.row_bytes;
+    c->sr = q.sr;
+}
+
+// The chunk at the cursor, and advance it; false at the end of the list.
+__device__ __forceinline__ bool cursor_next(const MegaArgs &a, ChunkCursor *c, const uint8_t *&src, uint32_t &bytes)
+{
+    while (c->p < a.n_ph && c->i >= c->nrows) cursor_load_phase(a, c, c->p + 1);
+    if (c->p >= a.n_ph) return false;
+    bytes = (uint32_t)(min(c->sr, c->nrows - c->i) * c->row_bytes);
+    src = c->w + (size_t)c->i * c->row_bytes;
+    c->i += c->sr;
+    return true;
 }
 
 // Copy the next chunk of this CTA's weight rows (phase order) into ring
-// slot `slot` (one thread; refills are serialised).
-__device__ __forceinline__ void ring_issue(const MegaArgs &a, const MegaShared &S, int slot)
+// slot `slot`, and warm the chunk pf_stages further on in L2 (one thread;
+// refills are serialised).
+__device__ __forceinline__ void ring_issue(const MegaArgs &a, const MegaShared &S, int slot, bool warm = true)
 {
-    MegaRing *rc = S.rc;
-    while (rc->p < a.n_ph && rc->i >= rc->nrows) ring_load_phase(a, rc, rc->p + 1);
-    if (rc->p >= a.n_ph) return;
-    const uint32_t bytes = (uint32_t)(min(rc->sr, rc->nrows - rc->i) * rc->row_bytes);
+    MegaRing      *rc = S.rc;
+    const uint8_t *src;
+    uint32_t       bytes;
+    if (!cursor_next(a, &rc->cp, src, bytes)) return;
     mbar_expect_tx(&S.full[slot], bytes);
-    bulk_g2s(S.ring + (size_t)slot * a.stage_bytes, rc->w + (size_t)rc->i * rc->row_bytes, bytes, &S.full[slot]);
-    rc->i += rc->sr;
+    bulk_g2s(S.ring + (size_t)slot * a.stage_bytes, src, bytes, &S.full[slot]);
     rc->issued++;
+    if (warm && a.pf_stages > 0 && cursor_next(a, &rc->pf, src, bytes)) prefetch_l2(src, bytes);
 }
 
 // Lane 0 of a warp that is done with ring slot `slot` (after __syncwarp).
@@ -331,7 +357,8 @@ __device__ __forceinline__ float sum8_tree(const float *p)
 // (g, rp) takes rows rp, rp + rowpar, ... four at a time.  Row partials of
 // k-group g land in red[row * nkg + g], or with RED8 (the last three levels
 // of the warp reduction left to the epilogue's sum8_tree) in
-// red[(row * nkg + g) * 8 + lane % 8].
+// red[row * (8 * nkg + 1) + 8 * g + lane % 8]: the odd row stride keeps the
+// epilogue, one thread per row, free of bank conflicts.
 template <int FMT, bool RED8>
 __device__ __forceinline__ void mega_stage_rows(const uint8_t *stage, int rows, unsigned row_bytes, int nb,
                                                 int b, int g, int rp, int rowpar, int nkg, int lane,
@@ -348,7 +375,7 @@ __device__ __forceinline__ void mega_stage_rows(const uint8_t *stage, int rows, 
         const int k = (lane >> 3) & 3, ii = i0 + k * rowpar;
         if (RED8) {
             const float part = warp_sum4_part(v[0], v[1], v[2], v[3], lane);
-            if (ii < rows) red[(ii * nkg + g) * 8 + (lane & 7)] = part;
+            if (ii < rows) red[ii * (8 * nkg + 1) + 8 * g + (lane & 7)] = part;
         } else {
             const float sum = warp_sum4(v[0], v[1], v[2], v[3], lane);
             if ((lane & 7) == 0 && ii < rows) red[ii * nkg + g] = sum;
@@ -361,7 +388,7 @@ __device__ __forceinline__ float row_total(const float *red, int r, int nkg, boo
 {
     float acc = 0.0f;
     if (red8)
-        for (int q = 0; q < nkg; q++) acc += sum8_tree(red + (size_t)(r * nkg + q) * 8);
+        for (int q = 0; q < nkg; q++) acc += sum8_tree(red + (size_t)r * (8 * nkg + 1) + 8 * q);
     else
         for (int q = 0; q < nkg; q++) acc += red[r * nkg + q];
     return acc;
@@ -371,6 +398,84 @@ __device__ __forceinline__ float row_total(const float *red, int r, int nkg, boo
 // into shared memory, this CTA's ring stages of the matrix, the epilogue.
 // `ring_s` counts ring stages consumed over the whole step.  One body for
 // both row formats: only the innermost loop depends on it.
+// Digit planes of the digit store for the input block of 8 lanes (t = b*8 + q).
+__device__ __forceinline__ void store_digits(const MegaShared &S, int t, float4 v)
+{
+    int   w[3];
+    float sxs;
+    digits_quad(v, w, sxs);
+    const int b = t >> 3, q = t & 7;
+    int *d = S.dig + (size_t)b * 28;
+    d[q] = w[0];
+    d[8 + q] = w[1];
+    d[16 + q] = w[2];
+    if (q == 0) d[27] = __float_as_int(sxs);
+}
+
+// The RMSNorm prologue when x has exactly two float4s per thread (n_in =
+// 8 * nct): x and the norm weights are loaded once, in one round trip; x is
+// parked in shared memory (above the digit planes) so that partial v of the
+// sum of squares adds its 16 elements in the order rms_partials does, and the
+// tree is rms_scale_w0's -- the same scale, bit for bit.
+__device__ __forceinline__ void norm_digits_two(const MegaArgs &a, const MegaPhase &ph, const MegaShared &S,
+                                                int tid, int nct)
+{
+    const float4 *x4 = reinterpret_cast<const float4 *>(ph.x);
+    const float4 *w4 = reinterpret_cast<const float4 *>(ph.norm_w);
+    const float4  xa = __ldcg(x4 + tid), xb = __ldcg(x4 + tid + nct);
+    const float4  wa = __ldg(w4 + tid), wb = __ldg(w4 + tid + nct);
+    float4 *xs = reinterpret_cast<float4 *>(S.kvbuf) + 2 * nct;   // past the digit planes of 2*nct/8 blocks
+    xs[tid] = xa;
+    xs[tid + nct] = xb;
+    named_bar(1, nct);
+    if (tid < 256) {
+        const int seg4 = (2 * nct) / 256;                          // float4s per partial
+        double p = 0.0;
+        for (int k = 0; k < seg4; k++) {
+            const float4 v = xs[tid * seg4 + k];
+            const double e0 = v.x, e1 = v.y, e2 = v.z, e3 = v.w;
+            p += e0 * e0;
+            p += e1 * e1;
+            p += e2 * e2;
+            p += e3 * e3;
+        }
+        S.dsum[tid] = p;
+    }
+    named_bar(1, nct);
+    if (tid < 32) {
+        double q[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) q[k] = S.dsum[tid + 32 * k];
+#pragma unroll
+        for (int k = 0; k < 4; k++) q[k] += q[k + 4];
+        q[0] += q[2];
+        q[1] += q[3];
+        q[0] += q[1];
+        double v = q[0];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_down_sync(0xffffffffu, v, o);
+        if (tid == 0) S.dsum[256] = v;
+    }
+    named_bar(1, nct);
+    const float scale = rms_from_sum(S.dsum[256], ph.n_in, a.eps);
+    float4 *xn4 = (ph.xn && blockIdx.x == 0) ? reinterpret_cast<float4 *>(ph.xn) : nullptr;
+    float4  va = xa, vb = xb;
+    va.x = __fmul_rn(__fmul_rn(va.x, scale), wa.x);
+    va.y = __fmul_rn(__fmul_rn(va.y, scale), wa.y);
+    va.z = __fmul_rn(__fmul_rn(va.z, scale), wa.z);
+    va.w = __fmul_rn(__fmul_rn(va.w, scale), wa.w);
+    vb.x = __fmul_rn(__fmul_rn(vb.x, scale), wb.x);
+    vb.y = __fmul_rn(__fmul_rn(vb.y, scale), wb.y);
+    vb.z = __fmul_rn(__fmul_rn(vb.z, scale), wb.z);
+    vb.w = __fmul_rn(__fmul_rn(vb.w, scale), wb.w);
+    if (xn4) {
+        xn4[tid] = va;
+        xn4[tid + nct] = vb;
+    }
+    store_digits(S, tid, va);
+    store_digits(S, tid + nct, vb);
+}
+
 __device__ __forceinline__ void attn_prefetch(const MegaArgs &a, const MegaPhase &ph, int pos, int hd);
 
 // next: the following phase's descriptor when it is attention (its K/V rows
@@ -389,9 +494,11 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
     const unsigned row_bytes = ph.row_bytes;
 
     // ---- prologue: digit planes of every input block -----------------------
-    float scale = 1.0f;
-    if (ph.norm) scale = rms_scale_w0(ph.x, ph.n_in, a.eps, S.dsum, tid, nct, [nct] { named_bar(1, nct); });
-    {
+    if (ph.norm && nb * 8 == 2 * nct) {
+        norm_digits_two(a, ph, S, tid, nct);
+    } else {
+        float scale = 1.0f;
+        if (ph.norm) scale = rms_scale_w0(ph.x, ph.n_in, a.eps, S.dsum, tid, nct, [nct] { named_bar(1, nct); });
         const float4 *x4 = reinterpret_cast<const float4 *>(ph.x);
         const float4 *w4 = reinterpret_cast<const float4 *>(ph.norm_w);
         float4 *xn4 = (ph.xn && blockIdx.x == 0) ? reinterpret_cast<float4 *>(ph.xn) : nullptr;
@@ -431,7 +538,7 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
     }
     named_bar(1, nct);
 
-    if (det) det[0] = globaltimer_ns();
+    if (det) det[0] = clock64();
     // the residual this CTA's rows add to (its own rows: no other CTA writes
     // them in this phase), fetched now so the epilogue does not wait for it
     float yprev = 0.0f;
@@ -470,7 +577,7 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
         if (active) {
             if (q4 && red8)
                 mega_stage_rows<4, true>(stage, rows, row_bytes, nb, b, g, rp, rowpar, nkg, lane, xw, off, sxs,
-                                         S.red + (size_t)i * nkg * 8);
+                                         S.red + (size_t)i * (8 * nkg + 1));
             else if (q4)
                 mega_stage_rows<4, false>(stage, rows, row_bytes, nb, b, g, rp, rowpar, nkg, lane, xw, off, sxs,
                                           S.red + (size_t)i * nkg);
@@ -487,7 +594,7 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     named_bar(1, nct);
     if (det) {
-        det[1] = globaltimer_ns();
+        det[1] = clock64();
         det[3] = waited;
     }
     if (next) {
@@ -503,7 +610,7 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
             const float gs = row_total(S.red, 2 * j, nkg, red8), us = row_total(S.red, 2 * j + 1, nkg, red8);
             y[r0 / 2 + j] = silu_mul(gs, us);
         }
-        if (det) det[2] = globaltimer_ns();
+        if (det) det[2] = clock64();
         return;
     }
     ArgBest best{-INFINITY, -1};
@@ -513,7 +620,7 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
         else y[r0 + r] = acc;
         if (epi == EPI_ARGMAX) best = arg_better(best, ArgBest{acc, r0 + r});
     }
-    if (det) det[2] = globaltimer_ns();
+    if (det) det[2] = clock64();
     if (epi != EPI_ARGMAX) return;
     // per-CTA best -> the CTA that takes the last ticket reduces in CTA order
 #pragma unroll
@@ -622,7 +729,7 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
         vnew[j] = v0; vnew[j + HD / 2] = v1;
     }
     named_bar(1, nct);
-    if (det) det[0] = globaltimer_ns();
+    if (det) det[0] = clock64();
     if (has && sp == 0)
         for (int j = tid; j < HD; j += nct) {
             kbase[(size_t)pos * HD + j] = knew[j];
@@ -684,7 +791,7 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
         if (r + 1 < nround && (tid & 31) == 0 && tid < 64) issue(r + 1, tid >> 5);
     }
     att_sb += nround;                               // one phase of each half barrier per round
-    if (det) det[1] = globaltimer_ns();
+    if (det) det[1] = clock64();
     // this warp's partial into shared memory; group 0 of each head merges
     // the G group partials in group order into the CTA's partial
     float *gpart = S.red;                           // [G][NREP][HD + 4]
@@ -749,7 +856,7 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
         s_last = last;
     }
     named_bar(1, nct);
-    if (det) det[2] = globaltimer_ns();
+    if (det) det[2] = clock64();
     if (!s_last) return;
     __threadfence();
     // all partials of the head group into shared memory at once (the K/V
@@ -864,16 +971,25 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a)
         launch_s = a.bar[3];
         ph_s[0] = a.ph[0];
         S.rc->issued = 0;
-        ring_load_phase(a, S.rc, 0);
+        cursor_load_phase(a, &S.rc->cp, 0);
         for (int s = 0; s < a.nst; s++) S.rc->done[s] = 0u;
-        for (int s = 0; s < a.nst; s++) ring_issue(a, S, s);     // the first chunks
+        for (int s = 0; s < a.nst; s++) ring_issue(a, S, s, false);     // the first chunks
+        // the prefetch cursor starts where the copies are and runs
+        // pf_stages chunks ahead of them
+        S.rc->pf = S.rc->cp;
+        const uint8_t *src;
+        uint32_t       bytes;
+        for (int s = 0; s < a.pf_stages && cursor_next(a, &S.rc->pf, src, bytes); s++) prefetch_l2(src, bytes);
     }
     __syncthreads();
     S.pos = pos_s;
     const unsigned long long epoch = (unsigned long long)launch_s << 20;
 
     // ---- consumers -------------------------------------------------------------
-    if (a.phase_ns && blockIdx.x == 0 && threadIdx.x == 0) a.phase_ns[0] = globaltimer_ns();
+    if (a.phase_ns && blockIdx.x == 0 && threadIdx.x == 0) {
+        a.phase_ns[0] = globaltimer_ns();
+        a.phase_clk[0] = clock64();
+    }
     int ring_s = 0, att_sb = 0;
     for (int p = 0; p < a.n_ph; p++) {
         // descriptors live in shared memory: phase p's arrived by a bulk
@@ -910,7 +1026,10 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a)
     // a LAYERS stage advances its position once every phase is done; no
     // CTA reads it after the last attention phase
     if (a.layers_advance && blockIdx.x == 0 && threadIdx.x == 0) a.st->pos = S.pos + 1;
-    if (a.phase_ns && blockIdx.x == 0 && threadIdx.x == 0) a.phase_ns[a.n_ph] = globaltimer_ns();
+    if (a.phase_ns && blockIdx.x == 0 && threadIdx.x == 0) {
+        a.phase_ns[a.n_ph] = globaltimer_ns();
+        a.phase_clk[a.n_ph] = clock64();
+    }
     // the last CTA out rewinds the barrier counter for the next launch: every
     // CTA that counted itself here has left its last grid barrier
     if (threadIdx.x == 0) {

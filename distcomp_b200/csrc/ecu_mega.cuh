@@ -162,7 +162,7 @@ __host__ __device__ inline MegaSmem mega_smem_plan(int red_floats)
     p.ring = 0;
     p.bars = p.ring + (size_t)MEGA_RING_BYTES;
     p.abar = p.bars + MEGA_MAX_STAGES * sizeof(uint64_t);
-    p.red = (p.abar + 2 * sizeof(uint64_t) + 15) & ~(size_t)15;
+    p.red = (p.abar + 4 * sizeof(uint64_t) + 15) & ~(size_t)15;    // K/V halves, partial gather
     p.un = (p.red + (size_t)red_floats * sizeof(float) + 127) & ~(size_t)127;
     // union: digit planes of the GEMV input | attention K/V buffers
     const size_t dig = (size_t)MEGA_MAX_NB * 28 * sizeof(int);
@@ -667,7 +667,8 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
 // query head h of the group on warp h.  Same arithmetic per split as
 // k_attention; partials go to global memory for the merge phase.
 template <int HD, int NREP>
-__device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const MegaShared &S, int &att_sb, int p_idx)
+__device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const MegaShared &S, int &att_sb, int &merges,
+                               int p_idx)
 {
     // profiling (CTA 0): after the Q/K/V prologue, after the position loop,
     // after the split ticket; and when KV head 0's merge ended
@@ -863,20 +864,17 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
     // buffers are free), then the merge reads only shared memory
     const int    ns = a.n_split;
     constexpr int PER = NREP * (HD + 4);     // floats of one split's partials
-    const float4 *src4 = reinterpret_cast<const float4 *>(a.apart + (size_t)g * ns * PER);
-    float4       *gat4 = reinterpret_cast<float4 *>(S.kvbuf);
-    {
-        const int n4 = ns * PER / 4;
-        for (int base = tid; base < n4; base += 2 * nct) {   // two loads in flight per thread
-            const float4 t0 = __ldcg(src4 + base);
-            const bool   two = base + nct < n4;
-            float4       t1 = t0;
-            if (two) t1 = __ldcg(src4 + base + nct);
-            gat4[base] = t0;
-            if (two) gat4[base + nct] = t1;
-        }
+    // the group's partials are one contiguous run: one bulk copy (the other
+    // CTAs' stores were released before their tickets and acquired here;
+    // the proxy fence orders them for the async-proxy read)
+    if (tid == 0) {
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        const uint32_t bytes = (uint32_t)(ns * PER * sizeof(float));
+        mbar_expect_tx(&S.abar[2], bytes);
+        bulk_g2s(S.kvbuf, a.apart + (size_t)g * ns * PER, bytes, &S.abar[2]);
     }
-    named_bar(1, nct);
+    mbar_wait<true>(&S.abar[2], (unsigned)merges & 1u, a.status);
+    merges++;
     const float *gat = S.kvbuf;
     if (warp < NREP) {                         // warp hh: its head's split weights, lanes over splits
         const int hh = warp;
@@ -965,6 +963,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a)
         for (int s = 0; s < a.nst; s++) mbar_init(&S.full[s], 1);
         mbar_init(&S.abar[0], 1);
         mbar_init(&S.abar[1], 1);
+        mbar_init(&S.abar[2], 1);
         mbar_init(&desc_bar, 1);
         mbar_init_fence();
         pos_s = a.st->pos;            // stable for the whole step
@@ -990,7 +989,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a)
         a.phase_ns[0] = globaltimer_ns();
         a.phase_clk[0] = clock64();
     }
-    int ring_s = 0, att_sb = 0;
+    int ring_s = 0, att_sb = 0, merges = 0;
     for (int p = 0; p < a.n_ph; p++) {
         // descriptors live in shared memory: phase p's arrived by a bulk
         // copy issued at the start of phase p-1, and phase p+1's is issued
@@ -1008,7 +1007,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a)
         if (kind == PH_GEMV) {
             mega_gemv(a, ph, S, ring_s, p, ph.next_attn ? &ph_s[(p + 1) & 1] : nullptr, HD);
         } else if (kind == PH_ATTN) {
-            mega_attention<HD, NREP>(a, ph, S, att_sb, p);
+            mega_attention<HD, NREP>(a, ph, S, att_sb, merges, p);
         } else {
             mega_embed(a);
         }

@@ -9,15 +9,17 @@ Q4_0 (embedding and head Q8_0), generated on the GPU from a fixed seed;
 KV cache fp32 for 4096 positions.  A 512-token random prompt is fed
 first, then W untimed and K timed greedy decode steps.  One step = one
 token through embed -> 32 layers -> head -> argmax, the next token fed back
-on the device (one CUDA-graph replay per token).  The 4.5 GB of weights
+on the device (one persistent-kernel launch per token).  The 4.5 GB of weights
 stream from HBM every step, far above the 126 MB L2, so no flush is needed.
 
 One JSON line: value = tokens/s from CUDA events around the K steps; e2e =
 the same through ecu_forward with host buffers (token in, state + token
 out, pinned copies inside the timed region); roofline = the dominant
-kernel (fused gate/up GEMV + SwiGLU) from CUDA events of a profiling
-replay; cpu_baseline = the reference engine (oracle/_ref, compiled from the
-reference's sources) on this host's cores on a bounded sample.
+kernel from CUDA events of a profiling replay: the persistent whole-step
+kernel (one launch per token, the default path), or with ECU_MEGA=0 the
+fused gate/up GEMV + SwiGLU of the per-kernel step; cpu_baseline = the
+reference engine (oracle/_ref, compiled from the reference's sources) on
+this host's cores on a bounded sample.
 
 --impl reference times that reference CPU engine alone (rank 0) on the
 same config and prints the same line with "impl": "reference".

@@ -406,6 +406,8 @@ struct ecu_ctx {
     MegaArgs    margs{};
     int         mega_grid = 0;
     size_t      mega_smem = 0;
+    unsigned long long *mega_ll = nullptr;   // the tagged activation vectors, one block
+    size_t      mega_ll_words = 0;
     std::vector<const char *> ph_kind;    // per phase, for the profile
     std::vector<double>       ph_bytes;
 
@@ -726,8 +728,10 @@ static int check_status(ecu_ctx *c)
     CK(cudaMemcpy(&s, c->st, sizeof s, cudaMemcpyDeviceToHost));
     if (s.status) {
         if (c->mega) {
+            // counters and launch number restart at zero: the tagged vectors
+            // must not hold words of an earlier launch with the same number
             CK(cudaMemset(c->margs.bar, 0, (4 + (size_t)c->g.n_head_kv) * sizeof(unsigned)));
-            CK(cudaMemset(c->margs.flags, 0, (size_t)c->mega_grid * 16 * sizeof(unsigned long long)));
+            CK(cudaMemset(c->mega_ll, 0, c->mega_ll_words * sizeof(unsigned long long)));
         }
         if (s.status & ECU_STATUS_BADTOKEN)
             ecu_set_error(nullptr, 0, "the device-resident token is outside the vocabulary (%d)", c->g.n_vocab);
@@ -788,6 +792,7 @@ static MegaPhase mega_gemv_phase(const DevMat &m, int grid, unsigned stage_bytes
     p.fmt = m.layout == LAY_SPLIT4 ? 4 : 8;
     p.norm = norm;
     p.epi = epi;
+    p.in_ep = p.y_ep = -1;                           // plain input / residual unless set
     p.w = m.data;
     p.row_bytes = (unsigned)m.row_bytes;
     p.n_in = m.n_in;
@@ -818,9 +823,9 @@ static int mega_setup(ecu_ctx *c)
         c->path = std::string("kernels: ") + why;
         return 0;
     };
-    // opt-in (ECU_MEGA=1) until it beats the per-kernel step on the 8B shape
+    // ECU_MEGA=0 selects the per-kernel step
     const char *env = getenv("ECU_MEGA");
-    if (!env || env[0] != '1') return no("ECU_MEGA=0");
+    if (env && env[0] == '0') return no("ECU_MEGA=0");
     if ((c->stage != ECU_STAGE_FULL && c->stage != ECU_STAGE_LAYERS) || c->layers.empty())
         return no("stage without layers");
     const EcuGeom &g = c->g;
@@ -837,7 +842,6 @@ static int mega_setup(ecu_ctx *c)
     cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, c->device);
     if (!coop) return no("no cooperative launch");
     const int grid = c->sms;
-    if (grid > MEGA_THREADS) return no("more SMs than threads to poll the grid barrier");
     // ring geometry: ECU_MEGA_RING stages (default 2) over MEGA_RING_BYTES
     int nst = 2;
     if (const char *r = getenv("ECU_MEGA_RING")) nst = std::max(2, std::min(MEGA_MAX_STAGES, atoi(r)));
@@ -854,6 +858,9 @@ static int mega_setup(ecu_ctx *c)
     int n_split = std::min(MEGA_MAX_SPLIT, grid / g.n_head_kv);
     n_split = std::min(n_split, (int)(un / ((size_t)g.n_rep * (hd + 4) * sizeof(float))));
     n_split = std::max(1, std::min(n_split, g.n_ctx));
+    // the RMSNorm prologue stages x and the norm weights above the digit planes
+    if ((size_t)g.n_embd / 32 * 28 * sizeof(int) + 2 * (size_t)g.n_embd * sizeof(float) > un)
+        return no("n_embd too large for the staged RMSNorm prologue");
 
     std::vector<MegaPhase> ph;
     c->ph_kind.clear();
@@ -865,16 +872,36 @@ static int mega_setup(ecu_ctx *c)
     };
     c->to_shared = false;
     float *xn_tmp = full ? c->dalloc<float>((size_t)g.n_embd + 4) : nullptr;
+    // tagged vectors: residual stream, fused Q/K/V, attention output, SwiGLU
+    // output; 4-word padded so every vector starts 32-byte aligned
+    auto pad4 = [](size_t n) { return (n + 7) & ~(size_t)3; };
+    const size_t w_x = pad4(g.n_embd), w_qkv = pad4((size_t)qdim + 2 * kvdim), w_att = pad4(qdim),
+                 w_h = pad4(g.n_ff);
+    c->mega_ll_words = w_x + w_qkv + w_att + w_h;
+    c->mega_ll = c->dalloc<unsigned long long>(c->mega_ll_words);
+    if (!c->mega_ll) return -1;
+    CK(cudaMemset(c->mega_ll, 0, c->mega_ll_words * sizeof(unsigned long long)));
+    unsigned long long *x_ll = c->mega_ll, *qkv_ll = x_ll + w_x, *att_ll = qkv_ll + w_qkv, *h_ll = att_ll + w_att;
+    // x_w: the phase that last wrote the residual stream (-1: the plain
+    // input state of a LAYERS stage)
+    int x_w = -1;
     if (full) {
         MegaPhase p = {};
         p.kind = PH_EMBED;
+        p.y_ll = x_ll;
+        x_w = (int)ph.size();
         add(p, "embed", 8.0 * g.n_embd + (double)ecu_type_nbytes(c->emb.type, (size_t)g.n_embd));
     }
     const size_t plane = (size_t)g.n_head_kv * g.n_ctx * hd;
     for (size_t li = 0; li < c->layers.size(); li++) {
         LayerDev &ly = c->layers[li];
-        add(mega_gemv_phase(ly.qkv[0], grid, stage_bytes, 1, EPI_STORE, c->state, ly.attn_norm, c->qkv, nullptr), "gemv_qkv",
-            gemv_bytes(ly.qkv[0], EPI_STORE));
+        const bool last = li + 1 == c->layers.size();
+        MegaPhase q = mega_gemv_phase(ly.qkv[0], grid, stage_bytes, 1, EPI_STORE, c->state, ly.attn_norm, c->qkv, nullptr);
+        q.in_ep = x_w;
+        q.x_ll = x_ll;
+        q.y_ll = qkv_ll;
+        const int p_qkv = (int)ph.size();
+        add(q, "gemv_qkv", gemv_bytes(ly.qkv[0], EPI_STORE));
         MegaPhase at = {};
         at.kind = PH_ATTN;
         at.kc = c->kc + li * plane;
@@ -882,18 +909,39 @@ static int mega_setup(ecu_ctx *c)
         at.bq = ly.bq;
         at.bk = ly.bk;
         at.bv = ly.bv;
+        at.in_ep = p_qkv;
+        at.y_ll = att_ll;
+        const int p_at = (int)ph.size();
         add(at, "attention", -1.0);                 // position dependent: filled in by the profile
-        add(mega_gemv_phase(ly.o, grid, stage_bytes, 0, EPI_ADD, c->att, nullptr, c->state, nullptr), "gemv_o",
-            gemv_bytes(ly.o, EPI_ADD));
-        add(mega_gemv_phase(ly.gu, grid, stage_bytes, 1, EPI_SWIGLU, c->state, ly.ffn_norm, c->h, nullptr), "gemv_gate_up",
-            gemv_bytes(ly.gu, EPI_SWIGLU));
-        add(mega_gemv_phase(ly.d, grid, stage_bytes, 0, EPI_ADD, c->h, nullptr, c->state, nullptr), "gemv_down",
-            gemv_bytes(ly.d, EPI_ADD));
+        MegaPhase o = mega_gemv_phase(ly.o, grid, stage_bytes, 0, EPI_ADD, c->att, nullptr, c->state, nullptr);
+        o.in_ep = p_at;
+        o.x_ll = att_ll;
+        o.y_ep = x_w;
+        o.y_ll = x_ll;
+        x_w = (int)ph.size();
+        add(o, "gemv_o", gemv_bytes(ly.o, EPI_ADD));
+        MegaPhase gu = mega_gemv_phase(ly.gu, grid, stage_bytes, 1, EPI_SWIGLU, c->state, ly.ffn_norm, c->h, nullptr);
+        gu.in_ep = x_w;
+        gu.x_ll = x_ll;
+        gu.y_ll = h_ll;
+        const int p_gu = (int)ph.size();
+        add(gu, "gemv_gate_up", gemv_bytes(ly.gu, EPI_SWIGLU));
+        MegaPhase d = mega_gemv_phase(ly.d, grid, stage_bytes, 0, EPI_ADD, c->h, nullptr, c->state, nullptr);
+        d.in_ep = p_gu;
+        d.x_ll = h_ll;
+        d.y_ep = x_w;
+        d.y_ll = x_ll;
+        d.out_plain = (!full && last) ? 1 : 0;     // a LAYERS stage's output state
+        x_w = (int)ph.size();
+        add(d, "gemv_down", gemv_bytes(ly.d, EPI_ADD));
     }
-    (void)kvdim;
-    if (full)
-        add(mega_gemv_phase(c->out, grid, stage_bytes, 1, EPI_ARGMAX, c->state, c->out_norm, c->logits, xn_tmp),
-            "gemv_head_argmax", gemv_bytes(c->out, EPI_ARGMAX) + 4.0 * g.n_embd);
+    if (full) {
+        MegaPhase hp = mega_gemv_phase(c->out, grid, stage_bytes, 1, EPI_ARGMAX, c->state, c->out_norm, c->logits, xn_tmp);
+        hp.in_ep = x_w;
+        hp.x_ll = x_ll;
+        add(hp, "gemv_head_argmax", gemv_bytes(c->out, EPI_ARGMAX) + 4.0 * g.n_embd);
+    }
+    if (ph.size() >= 4095) return no("more phases than the tagged vectors' epochs count");
     for (size_t i = 0; i + 1 < ph.size(); i++) ph[i].next_attn = ph[i + 1].kind == PH_ATTN ? 1 : 0;
     int red = MEGA_NCW * (hd + 4);          // attention: the position groups' partials
     for (auto &p : ph)
@@ -926,9 +974,7 @@ static int mega_setup(ecu_ctx *c)
     float *pval = c->dalloc<float>((size_t)grid);
     int *pidx = c->dalloc<int>((size_t)grid);
     unsigned *ctr = c->dalloc<unsigned>(4 + (size_t)g.n_head_kv);
-    unsigned long long *flags = c->dalloc<unsigned long long>((size_t)grid * 16);
-    if (!d_ph || !apart || !pval || !pidx || !ctr || !flags || (full && !xn_tmp)) return -1;
-    CK(cudaMemset(flags, 0, (size_t)grid * 16 * sizeof(unsigned long long)));
+    if (!d_ph || !apart || !pval || !pidx || !ctr || (full && !xn_tmp)) return -1;
     CK(cudaMemcpy(d_ph, ph.data(), ph.size() * sizeof(MegaPhase), cudaMemcpyHostToDevice));
     CK(cudaMemset(ctr, 0, (4 + (size_t)g.n_head_kv) * sizeof(unsigned)));
     MegaArgs &a = c->margs;
@@ -944,7 +990,10 @@ static int mega_setup(ecu_ctx *c)
     a.part_val = pval;
     a.part_idx = pidx;
     a.bar = ctr;
-    a.flags = flags;
+    a.x_ll = x_ll;
+    a.qkv_ll = qkv_ll;
+    a.att_ll = att_ll;
+    a.h_ll = h_ll;
     a.ticket = ctr + 2;
     a.att_ticket = ctr + 4;
     a.st = c->st;

@@ -9,15 +9,17 @@
 //   down GEMV (+ residual);  [head: RMSNorm + logits GEMV + argmax]
 //
 // -- the order of src/engine.c:380-497.  One CTA per SM, all resident
-// (cooperative launch); the phases are separated by a grid barrier (one
-// atomic counter, bounded spin), and activations cross CTAs through L2 only
-// (ld.global.cg).  Every weight row this CTA multiplies during the whole
-// step streams through a shared-memory ring of bulk async copies in phase
-// order; the warp that releases a ring stage last issues the copy that
-// refills it with the next chunk of the list, so there is no producer warp
-// (16 warps of 128 registers rather than 17 of 96).  Weights do not depend
-// on activations, so the weight stream runs straight through the barriers:
-// while the grid synchronises, the next phase's rows are already landing.
+// (cooperative launch).  There is no grid barrier: the vectors that cross
+// CTAs (residual stream, Q/K/V, attention output, SwiGLU output) are
+// epoch-tagged words (ll_put), and each phase starts on its input as soon as
+// the words it reads carry the epoch of the phase that writes them.  Every
+// weight row this CTA multiplies during the whole step streams through a
+// shared-memory ring of bulk async copies in phase order; the warp that
+// releases a ring stage last issues the copy that refills it with the next
+// chunk of the list, so there is no producer warp (16 warps of 128 registers
+// rather than 17 of 96).  Weights do not depend on activations, so the
+// weight stream runs ahead of the phase boundaries: while a CTA waits for
+// its next input, that phase's rows are already landing.
 // The GEMV arithmetic is the one of k_gemv_fast (int8 digit planes of the
 // input, dp4a, the same row partials added in the same order), so its
 // results are the same bits.
@@ -59,7 +61,12 @@ struct MegaPhase {
     float         *kc, *vc;    // ATTN: this layer's cache planes [nkv][n_ctx][hd]
     const float   *bq, *bk, *bv;
     int            next_attn;  // the next phase is attention
-    int            pad_[3];
+    // epoch-tagged vectors (see ll_put): the phase that wrote this phase's
+    // input (in_ep) and, for a residual add, the residual (y_ep); -1 = the
+    // plain kernel input.  out_plain: also store the output as plain floats
+    int            in_ep, y_ep, out_plain;
+    const unsigned long long *x_ll;    // input vector, tagged
+    unsigned long long       *y_ll;    // output vector, tagged
 };
 static_assert(sizeof(MegaPhase) % 16 == 0, "phase descriptors are copied in 16-byte pieces");
 
@@ -75,7 +82,7 @@ struct MegaArgs {
     int             *part_idx;
     unsigned        *ticket;        // argmax ticket, zero between steps
     unsigned        *bar;           // [1]: CTAs done with the launch, [3]: launches so far
-    unsigned long long *flags;      // grid barrier: per CTA a 128-byte line holding its last epoch
+    unsigned long long *x_ll, *qkv_ll, *att_ll, *h_ll;   // tagged activation vectors
     unsigned        *att_ticket;    // per KV head: splits done, zero between phases
     StepState       *st;
     int             *tok_hist;
@@ -96,57 +103,75 @@ struct MegaArgs {
     float            eps, kscale;
 };
 
-// ------------------------------------------------------------ grid barrier --
+// ------------------------------------------------------- tagged vectors --
+// The phases hand vectors to each other without grid barriers: every element
+// is one 8-byte word {float, epoch of the phase that wrote it}, stored and
+// loaded whole (single-copy atomic), so a reader that sees the epoch it
+// expects also sees the value.  A reader spins on words that still carry an
+// older epoch.  Epoch = (launch number mod 2^20) << 12 | (phase + 1): unique
+// within a launch and against the previous one, which wrote every word.
+// Every phase's input depends on all CTAs' output of an earlier phase, so
+// these waits also order each buffer's reuse one layer later.
 
-__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p)
+__device__ __forceinline__ unsigned ll_epoch(unsigned launch, int phase)
 {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
+    return ((launch & 0xFFFFFu) << 12) | (unsigned)(phase + 1);
 }
 
-__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long *p)
+__device__ __forceinline__ void ll_put(unsigned long long *p, float v, unsigned e)
 {
-    unsigned long long v;
-    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
+    const unsigned long long w = ((unsigned long long)e << 32) | __float_as_uint(v);
+    asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
 
-// All threads of every CTA call this with the same k (0, 1, 2, ...).
-// Writes before it are visible to every CTA after it.  Each CTA publishes
-// its arrival as an epoch number in its own 128-byte flag (a release store,
-// no atomic to serialise on), and thread i < gridDim.x polls CTA i's flag
-// (acquire), so one round of polling sees every arrival.  The epoch is the
-// launch number << 20 plus k + 1, so flags never need resetting between
-// launches.  The spin gives up after ECU_WAIT_NS and flags the step as
-// failed.  phase_ns[k + 1] = CTA 0's exit time (phase_ns[0] the start).
-__device__ __forceinline__ void grid_sync(const MegaArgs &a, int k, int nct, unsigned long long epoch)
+__device__ __forceinline__ unsigned long long ll_word(const unsigned long long *p)
 {
-    named_bar(1, nct);
-    const unsigned long long want = epoch + (unsigned long long)(k + 1);
-    if (threadIdx.x == 0)
-        asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(a.flags + (size_t)blockIdx.x * 16), "l"(want)
-                     : "memory");
-    if (threadIdx.x < gridDim.x) {
-        const unsigned long long *f = a.flags + (size_t)threadIdx.x * 16;
-        if (ld_acquire_u64(f) < want) {
-            const uint64_t t0 = globaltimer_ns();
-            for (unsigned it = 1; ld_acquire_u64(f) < want; it++) {
-                if ((it & 255u) == 0) {
-                    if (*reinterpret_cast<volatile int *>(a.status) != 0) break;   // the step already failed
-                    if (globaltimer_ns() - t0 > ECU_WAIT_NS) {
-                        atomicOr(a.status, ECU_STATUS_TIMEOUT);
-                        break;
-                    }
-                }
-            }
-        }
+    unsigned long long w;
+    asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
+
+__device__ __forceinline__ ulonglong2 ll_word2(const unsigned long long *p)
+{
+    ulonglong2 w;
+    asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(w.x), "=l"(w.y) : "l"(p) : "memory");
+    return w;
+}
+
+// Spin helper: true while waiting is still allowed (bounded; gives up at
+// once when the step is already flagged as failed).
+__device__ __forceinline__ bool ll_keep_waiting(unsigned it, uint64_t &t0, int *status)
+{
+    if ((it & 255u) != 0) return true;
+    if (it == 256) t0 = globaltimer_ns();
+    if (*reinterpret_cast<volatile int *>(status) != 0) return false;
+    if (globaltimer_ns() - t0 > ECU_WAIT_NS) {
+        atomicOr(status, ECU_STATUS_TIMEOUT);
+        return false;
     }
-    named_bar(1, nct);
-    if (a.phase_ns && blockIdx.x == 0 && threadIdx.x == 0) {
-        a.phase_ns[k + 1] = globaltimer_ns();
-        a.phase_clk[k + 1] = clock64();
+    return true;
+}
+
+__device__ __forceinline__ float ll_get(const unsigned long long *p, unsigned e, int *status)
+{
+    unsigned long long w = ll_word(p);
+    uint64_t t0 = 0;
+    for (unsigned it = 1; (unsigned)(w >> 32) != e && ll_keep_waiting(it, t0, status); it++) w = ll_word(p);
+    return __uint_as_float((unsigned)w);
+}
+
+// Four consecutive tagged words (16-byte aligned) as a float4.
+__device__ __forceinline__ float4 ll_get4(const unsigned long long *p, unsigned e, int *status)
+{
+    ulonglong2 a = ll_word2(p), b = ll_word2(p + 2);
+    uint64_t t0 = 0;
+    for (unsigned it = 1; ((unsigned)(a.x >> 32) != e || (unsigned)(a.y >> 32) != e || (unsigned)(b.x >> 32) != e ||
+                           (unsigned)(b.y >> 32) != e) && ll_keep_waiting(it, t0, status); it++) {
+        a = ll_word2(p);
+        b = ll_word2(p + 2);
     }
+    return make_float4(__uint_as_float((unsigned)a.x), __uint_as_float((unsigned)a.y),
+                       __uint_as_float((unsigned)b.x), __uint_as_float((unsigned)b.y));
 }
 
 // ------------------------------------------------------------ smem layout --
@@ -258,6 +283,7 @@ struct MegaRing {
 
 struct MegaShared {
     int       pos;         // cache position of this step (read once at kernel start)
+    unsigned  launch;      // launch number (epochs of the tagged vectors)
     uint8_t  *ring;
     MegaRing *rc;
     uint64_t *full, *abar;
@@ -265,6 +291,7 @@ struct MegaShared {
     int      *dig;
     float    *kvbuf;
     float    *cs;          // RoPE (cos, sin) row of the current position, staged a phase early
+    uint64_t *dbar;        // completes when the next phase's descriptor has arrived
     double   *dsum;
     ArgBest  *argsh;
 };
@@ -412,34 +439,41 @@ __device__ __forceinline__ void store_digits(const MegaShared &S, int t, float4 
     if (q == 0) d[27] = __float_as_int(sxs);
 }
 
-// The RMSNorm prologue when x has exactly two float4s per thread (n_in =
-// 8 * nct): x and the norm weights are loaded once, in one round trip; x is
-// parked in shared memory (above the digit planes) so that partial v of the
-// sum of squares adds its 16 elements in the order rms_partials does, and the
-// tree is rms_scale_w0's -- the same scale, bit for bit.
-__device__ __forceinline__ void norm_digits_two(const MegaArgs &a, const MegaPhase &ph, const MegaShared &S,
-                                                int tid, int nct)
+// Element t4 (a float4) of this phase's input: tagged (written by phase
+// in_ep of this launch) or the plain kernel input.
+__device__ __forceinline__ float4 input4(const MegaArgs &a, const MegaPhase &ph, int t4, unsigned ein)
 {
-    const float4 *x4 = reinterpret_cast<const float4 *>(ph.x);
+    if (ph.in_ep >= 0) return ll_get4(ph.x_ll + 4 * (size_t)t4, ein, a.status);
+    return __ldcg(reinterpret_cast<const float4 *>(ph.x) + t4);
+}
+
+// RMSNorm prologue: x and the norm weights are staged in shared memory above
+// the digit planes (one round of loads), partial v of the sum of squares
+// adds its ceil(n/256) elements in order and warp 0 runs rms_scale_w0's tree
+// -- the scale k_rmsnorm and k_gemv_fast compute, bit for bit -- then the
+// digit planes of the normed input.
+__device__ __forceinline__ void norm_prologue(const MegaArgs &a, const MegaPhase &ph, const MegaShared &S, int tid,
+                                              int nct, unsigned ein)
+{
+    const int n = ph.n_in, nq = n / 4, nb = n / 32;
+    float4 *xs = reinterpret_cast<float4 *>(S.dig + (size_t)nb * 28);   // 112 bytes a block: 16-aligned
+    float4 *ws = xs + nq;
     const float4 *w4 = reinterpret_cast<const float4 *>(ph.norm_w);
-    const float4  xa = __ldcg(x4 + tid), xb = __ldcg(x4 + tid + nct);
-    const float4  wa = __ldg(w4 + tid), wb = __ldg(w4 + tid + nct);
-    float4 *xs = reinterpret_cast<float4 *>(S.kvbuf) + 2 * nct;   // past the digit planes of 2*nct/8 blocks
-    xs[tid] = xa;
-    xs[tid + nct] = xb;
+    for (int t = tid; t < nq; t += nct) {
+        ws[t] = __ldg(w4 + t);
+        xs[t] = input4(a, ph, t, ein);
+    }
     named_bar(1, nct);
-    if (tid < 256) {
-        const int seg4 = (2 * nct) / 256;                          // float4s per partial
+    const float *xf = reinterpret_cast<const float *>(xs);
+    const int    seg = (n + 255) / 256;
+    for (int v = tid; v < 256; v += nct) {
+        const int lo = min(n, v * seg), hi = min(n, lo + seg);
         double p = 0.0;
-        for (int k = 0; k < seg4; k++) {
-            const float4 v = xs[tid * seg4 + k];
-            const double e0 = v.x, e1 = v.y, e2 = v.z, e3 = v.w;
-            p += e0 * e0;
-            p += e1 * e1;
-            p += e2 * e2;
-            p += e3 * e3;
+        for (int i = lo; i < hi; i++) {
+            const double e = xf[i];
+            p += e * e;
         }
-        S.dsum[tid] = p;
+        S.dsum[v] = p;
     }
     named_bar(1, nct);
     if (tid < 32) {
@@ -457,23 +491,18 @@ __device__ __forceinline__ void norm_digits_two(const MegaArgs &a, const MegaPha
         if (tid == 0) S.dsum[256] = v;
     }
     named_bar(1, nct);
-    const float scale = rms_from_sum(S.dsum[256], ph.n_in, a.eps);
+    const float scale = rms_from_sum(S.dsum[256], n, a.eps);
     float4 *xn4 = (ph.xn && blockIdx.x == 0) ? reinterpret_cast<float4 *>(ph.xn) : nullptr;
-    float4  va = xa, vb = xb;
-    va.x = __fmul_rn(__fmul_rn(va.x, scale), wa.x);
-    va.y = __fmul_rn(__fmul_rn(va.y, scale), wa.y);
-    va.z = __fmul_rn(__fmul_rn(va.z, scale), wa.z);
-    va.w = __fmul_rn(__fmul_rn(va.w, scale), wa.w);
-    vb.x = __fmul_rn(__fmul_rn(vb.x, scale), wb.x);
-    vb.y = __fmul_rn(__fmul_rn(vb.y, scale), wb.y);
-    vb.z = __fmul_rn(__fmul_rn(vb.z, scale), wb.z);
-    vb.w = __fmul_rn(__fmul_rn(vb.w, scale), wb.w);
-    if (xn4) {
-        xn4[tid] = va;
-        xn4[tid + nct] = vb;
+    for (int t = tid; t < nq; t += nct) {         // whole warps: nq is a multiple of 256
+        float4       v = xs[t];
+        const float4 w = ws[t];
+        v.x = __fmul_rn(__fmul_rn(v.x, scale), w.x);
+        v.y = __fmul_rn(__fmul_rn(v.y, scale), w.y);
+        v.z = __fmul_rn(__fmul_rn(v.z, scale), w.z);
+        v.w = __fmul_rn(__fmul_rn(v.w, scale), w.w);
+        if (xn4) xn4[t] = v;
+        store_digits(S, t, v);
     }
-    store_digits(S, tid, va);
-    store_digits(S, tid + nct, vb);
 }
 
 __device__ __forceinline__ void attn_prefetch(const MegaArgs &a, const MegaPhase &ph, int pos, int hd);
@@ -494,46 +523,22 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
     const unsigned row_bytes = ph.row_bytes;
 
     // ---- prologue: digit planes of every input block -----------------------
-    if (ph.norm && nb * 8 == 2 * nct) {
-        norm_digits_two(a, ph, S, tid, nct);
+    // A CTA without rows reads no input: nothing it writes would tell a later
+    // phase that it is done with the vector (the tagged vectors are reused
+    // one layer later, ordered only by what each phase reads).
+    const unsigned ein = ll_epoch(S.launch, ph.in_ep);
+    if (nrows == 0) {
+    } else if (ph.norm) {
+        norm_prologue(a, ph, S, tid, nct, ein);
     } else {
-        float scale = 1.0f;
-        if (ph.norm) scale = rms_scale_w0(ph.x, ph.n_in, a.eps, S.dsum, tid, nct, [nct] { named_bar(1, nct); });
-        const float4 *x4 = reinterpret_cast<const float4 *>(ph.x);
-        const float4 *w4 = reinterpret_cast<const float4 *>(ph.norm_w);
-        float4 *xn4 = (ph.xn && blockIdx.x == 0) ? reinterpret_cast<float4 *>(ph.xn) : nullptr;
         const int nq = nb * 8;                          // float4s of x; whole warps (nb % 32 == 0)
-        for (int base = tid; base < nq; base += 4 * nct) {
-            // the loads of up to four items first: one memory round trip
-            float4 xq[4];
-#pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const int t = base + u * nct;
-                if (t < nq) xq[u] = __ldcg(x4 + t);
-            }
-#pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const int t = base + u * nct;
-                if (t >= nq) break;                     // uniform across the warp
-                float4 v = xq[u];
-                if (ph.norm) {
-                    const float4 wq = __ldg(w4 + t);
-                    v.x = __fmul_rn(__fmul_rn(v.x, scale), wq.x);
-                    v.y = __fmul_rn(__fmul_rn(v.y, scale), wq.y);
-                    v.z = __fmul_rn(__fmul_rn(v.z, scale), wq.z);
-                    v.w = __fmul_rn(__fmul_rn(v.w, scale), wq.w);
-                    if (xn4) xn4[t] = v;
-                }
-                int   w[3];
-                float sxs;
-                digits_quad(v, w, sxs);
-                const int b = t >> 3, q = t & 7;
-                int *d = S.dig + (size_t)b * 28;
-                d[q] = w[0];
-                d[8 + q] = w[1];
-                d[16 + q] = w[2];
-                if (q == 0) d[27] = __float_as_int(sxs);
-            }
+        for (int base = tid; base < nq; base += 2 * nct) {
+            const bool   two = base + nct < nq;
+            const float4 va = input4(a, ph, base, ein);
+            float4       vb = va;
+            if (two) vb = input4(a, ph, base + nct, ein);
+            store_digits(S, base, va);
+            if (two) store_digits(S, base + nct, vb);
         }
     }
     named_bar(1, nct);
@@ -542,7 +547,9 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
     // the residual this CTA's rows add to (its own rows: no other CTA writes
     // them in this phase), fetched now so the epilogue does not wait for it
     float yprev = 0.0f;
-    if (ph.epi == EPI_ADD && tid < nrows) yprev = __ldcg(ph.y + r0 + tid);
+    if (ph.epi == EPI_ADD && tid < nrows)
+        yprev = ph.y_ep >= 0 ? ll_get(a.x_ll + r0 + tid, ll_epoch(S.launch, ph.y_ep), a.status)
+                             : __ldcg(ph.y + r0 + tid);
     // ---- main loop ------------------------------------------------------------
     const bool active = warp < nkg * rowpar;
     const int  g = active ? warp % nkg : 0, rp = active ? warp / nkg : 0;
@@ -598,17 +605,20 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
         det[3] = waited;
     }
     if (next) {
+        // next phase's descriptor: its copy was issued at this phase's start
+        mbar_wait<true>(S.dbar, (unsigned)p_idx & 1u, a.status);
         if (tid == 0) attn_prefetch(a, *next, S.pos, hd);
         for (int j = tid; j < hd; j += nct) S.cs[j] = a.rope_cs[(size_t)S.pos * hd + j];
     }
 
     // ---- epilogue over this CTA's rows --------------------------------------
-    const int epi = ph.epi;
-    float    *y = ph.y;
+    const int      epi = ph.epi;
+    float         *y = ph.y;
+    const unsigned eout = ll_epoch(S.launch, p_idx);
     if (epi == EPI_SWIGLU) {
         for (int j = tid; j < nrows / 2; j += nct) {
             const float gs = row_total(S.red, 2 * j, nkg, red8), us = row_total(S.red, 2 * j + 1, nkg, red8);
-            y[r0 / 2 + j] = silu_mul(gs, us);
+            ll_put(ph.y_ll + r0 / 2 + j, silu_mul(gs, us), eout);
         }
         if (det) det[2] = clock64();
         return;
@@ -616,8 +626,18 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
     ArgBest best{-INFINITY, -1};
     for (int r = tid; r < nrows; r += nct) {
         const float acc = row_total(S.red, r, nkg, red8);
-        if (epi == EPI_ADD) y[r0 + r] = (r == tid ? yprev : __ldcg(y + r0 + r)) + acc;
-        else y[r0 + r] = acc;
+        if (epi == EPI_ADD) {
+            const float prev = r == tid ? yprev
+                                        : (ph.y_ep >= 0 ? ll_get(a.x_ll + r0 + r, ll_epoch(S.launch, ph.y_ep), a.status)
+                                                        : __ldcg(y + r0 + r));
+            const float out = prev + acc;
+            ll_put(ph.y_ll + r0 + r, out, eout);
+            if (ph.out_plain) y[r0 + r] = out;
+        } else if (epi == EPI_STORE) {
+            ll_put(ph.y_ll + r0 + r, acc, eout);
+        } else {
+            y[r0 + r] = acc;                       // logits (argmax reads them after its ticket)
+        }
         if (epi == EPI_ARGMAX) best = arg_better(best, ArgBest{acc, r0 + r});
     }
     if (det) det[2] = clock64();
@@ -710,19 +730,21 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
     };
     if (nround > 0 && (tid & 31) == 0 && tid < 64) issue(0, tid >> 5);
     const float *cs_s = S.cs;
+    const unsigned ein = ll_epoch(S.launch, ph.in_ep);
     const int qdim = a.n_head * HD, kvdim = a.n_kv * HD;
-    for (int i = tid; i < NREP * (HD / 2); i += nct) {
+    // a CTA without a work item reads nothing (see the GEMV prologue)
+    for (int i = has ? tid : nct; i < NREP * (HD / 2); i += nct) {
         const int h = i / (HD / 2), j = i % (HD / 2), row = (g * NREP + h) * HD;
-        float x0 = __ldcg(a.qkv + row + j), x1 = __ldcg(a.qkv + row + j + HD / 2);
+        float x0 = ll_get(a.qkv_ll + row + j, ein, a.status), x1 = ll_get(a.qkv_ll + row + j + HD / 2, ein, a.status);
         if (ph.bq) { x0 = __fadd_rn(x0, ph.bq[row + j]); x1 = __fadd_rn(x1, ph.bq[row + j + HD / 2]); }
         rope_pair(x0, x1, cs_s[2 * j], cs_s[2 * j + 1]);
         q_s[h * HD + j] = x0;
         q_s[h * HD + j + HD / 2] = x1;
     }
-    for (int j = tid; j < HD / 2; j += nct) {
+    for (int j = has ? tid : nct; j < HD / 2; j += nct) {
         const int kr = qdim + g * HD, vr = qdim + kvdim + g * HD;
-        float k0 = __ldcg(a.qkv + kr + j), k1 = __ldcg(a.qkv + kr + j + HD / 2);
-        float v0 = __ldcg(a.qkv + vr + j), v1 = __ldcg(a.qkv + vr + j + HD / 2);
+        float k0 = ll_get(a.qkv_ll + kr + j, ein, a.status), k1 = ll_get(a.qkv_ll + kr + j + HD / 2, ein, a.status);
+        float v0 = ll_get(a.qkv_ll + vr + j, ein, a.status), v1 = ll_get(a.qkv_ll + vr + j + HD / 2, ein, a.status);
         if (ph.bk) { k0 = __fadd_rn(k0, ph.bk[g * HD + j]); k1 = __fadd_rn(k1, ph.bk[g * HD + j + HD / 2]); }
         if (ph.bv) { v0 = __fadd_rn(v0, ph.bv[g * HD + j]); v1 = __fadd_rn(v1, ph.bv[g * HD + j + HD / 2]); }
         rope_pair(k0, k1, cs_s[2 * j], cs_s[2 * j + 1]);
@@ -892,13 +914,20 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
         if (lane == 0) invl[hh] = L > 0.0f ? 1.0f / L : 0.0f;
     }
     named_bar(1, nct);
+    // the ticket is rewound before any output becomes visible: a CTA can
+    // reach the next layer's attention only after reading this output
+    if (tid == 0) {
+        a.att_ticket[g] = 0u;
+        __threadfence();
+    }
+    named_bar(1, nct);
+    const unsigned eout = ll_epoch(S.launch, p_idx);
     for (int i = tid; i < NREP * HD; i += nct) {
         const int hh = i / HD, d = i % HD;
         float o = 0.0f;
         for (int r = 0; r < ns; r++) o = fmaf(gat[r * PER + hh * (HD + 4) + d], wsp[hh][r], o);
-        a.att[(g * NREP + hh) * HD + d] = o * invl[hh];
+        ll_put(a.att_ll + (g * NREP + hh) * HD + d, o * invl[hh], eout);
     }
-    if (tid == 0) a.att_ticket[g] = 0u;     // for the next layer (after a grid barrier)
     // profiling: when KV head 0's merge was done (whichever CTA did it)
     if (a.phase_detail && g == 0 && tid == 0) a.phase_detail[(size_t)p_idx * 4 + 3] = globaltimer_ns();
 }
@@ -920,8 +949,9 @@ __device__ __forceinline__ void attn_prefetch(const MegaArgs &a, const MegaPhase
     prefetch_l2(ph.vc + off, bytes);
 }
 
-__device__ void mega_embed(const MegaArgs &a)
+__device__ void mega_embed(const MegaArgs &a, const MegaShared &S, int p_idx)
 {
+    const unsigned eout = ll_epoch(S.launch, p_idx);
     const int    nct = MEGA_NCW * 32, n = a.n_embd;
     const int    tok = a.st->token;
     if (tok < 0 || tok >= a.emb.n_out) {
@@ -931,7 +961,7 @@ __device__ void mega_embed(const MegaArgs &a)
     const size_t base = (size_t)tok * (size_t)n;
     for (int i = blockIdx.x * nct + threadIdx.x; i < n; i += gridDim.x * nct) {
         const size_t e = base + (size_t)i;
-        a.state[i] = mat_elem(a.emb, (int)(e / (size_t)a.emb.n_in), (int)(e % (size_t)a.emb.n_in));
+        ll_put(a.x_ll + i, mat_elem(a.emb, (int)(e / (size_t)a.emb.n_in), (int)(e % (size_t)a.emb.n_in)), eout);
     }
 }
 
@@ -958,6 +988,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a)
     __shared__ __align__(16) float cs_row[HD];
     S.rc = &ring_state;
     S.cs = cs_row;
+    S.dbar = &desc_bar;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < a.nst; s++) mbar_init(&S.full[s], 1);
@@ -982,7 +1013,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a)
     }
     __syncthreads();
     S.pos = pos_s;
-    const unsigned long long epoch = (unsigned long long)launch_s << 20;
+    S.launch = launch_s;
 
     // ---- consumers -------------------------------------------------------------
     if (a.phase_ns && blockIdx.x == 0 && threadIdx.x == 0) {
@@ -998,7 +1029,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a)
         const MegaPhase &ph = ph_s[p & 1];
         if (threadIdx.x == 0 && p + 1 < a.n_ph) {
             // the reads of that buffer (phase p-1's descriptor) are done:
-            // every thread has passed the grid barrier
+            // every thread has passed the end of phase p-1
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             mbar_expect_tx(&desc_bar, (uint32_t)sizeof(MegaPhase));
             bulk_g2s(&ph_s[(p + 1) & 1], a.ph + p + 1, (uint32_t)sizeof(MegaPhase), &desc_bar);
@@ -1009,9 +1040,16 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a)
         } else if (kind == PH_ATTN) {
             mega_attention<HD, NREP>(a, ph, S, att_sb, merges, p);
         } else {
-            mega_embed(a);
+            mega_embed(a, S, p);
         }
-        if (p + 1 < a.n_ph) grid_sync(a, p, nct, epoch);
+        // the CTA's warps leave a phase together: shared buffers (row
+        // partials, digit planes / K/V rows, the descriptor double buffer)
+        // change hands only here
+        named_bar(1, nct);
+        if (a.phase_ns && blockIdx.x == 0 && threadIdx.x == 0) {
+            a.phase_ns[p + 1] = globaltimer_ns();
+            a.phase_clk[p + 1] = clock64();
+        }
     }
     // ring and K/V copies still in flight (none, unless a wait gave up) land
     // before this CTA may exit
@@ -1029,13 +1067,13 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a)
         a.phase_ns[a.n_ph] = globaltimer_ns();
         a.phase_clk[a.n_ph] = clock64();
     }
-    // the last CTA out rewinds the barrier counter for the next launch: every
-    // CTA that counted itself here has left its last grid barrier
+    // the last CTA out rewinds the exit counter and numbers the next launch
+    // (the epochs of its tagged words differ from every word of this one)
     if (threadIdx.x == 0) {
         __threadfence();
         if (atomicAdd(a.bar + 1, 1u) == gridDim.x - 1) {
             a.bar[1] = 0u;
-            a.bar[3] = a.bar[3] + 1u;       // the next launch's epochs are above every flag
+            a.bar[3] = a.bar[3] + 1u;
             __threadfence();
         }
     }

@@ -265,8 +265,8 @@ class LlmCtx:
     def profile_steps(self, n_steps: int) -> dict:
         """{kind: (launches, total_ms, bytes_per_launch)} over n_steps eager
         decode steps with CUDA events around every kernel."""
-        arr = (EcuKprof * 64)()
-        k = lib().ecu_profile_steps(self.h, int(n_steps), arr, 64)
+        arr = (EcuKprof * 128)()
+        k = lib().ecu_profile_steps(self.h, int(n_steps), arr, 128)
         if k < 0:
             raise EngineError(last_error())
         return {arr[i].kind.decode(): (arr[i].launches, arr[i].total_ms, arr[i].bytes_per_launch)

@@ -772,9 +772,9 @@ static MegaFn mega_lookup(int hd, int rep)
     return nullptr;
 }
 
-static size_t mega_smem_total(int hd, int red_floats)
+static size_t mega_smem_total(int red_floats, unsigned ring_bytes, unsigned union_bytes)
 {
-    return hd == 128 ? mega_smem_plan<128>(red_floats).total : mega_smem_plan<64>(red_floats).total;
+    return mega_smem_plan(red_floats, ring_bytes, union_bytes).total;
 }
 
 // Q4_0 rows in SPLIT4 or Q8_0 rows in SPLIT8, n_in a multiple of 1024.
@@ -842,25 +842,33 @@ static int mega_setup(ecu_ctx *c)
     cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, c->device);
     if (!coop) return no("no cooperative launch");
     const int grid = c->sms;
-    // ring geometry: ECU_MEGA_RING stages (default 2) over MEGA_RING_BYTES
+    // ring geometry: ECU_MEGA_RING stages (default 2) over ECU_MEGA_RING_KB
+    // KB (default MEGA_RING_BYTES)
     int nst = 2;
     if (const char *r = getenv("ECU_MEGA_RING")) nst = std::max(2, std::min(MEGA_MAX_STAGES, atoi(r)));
-    const unsigned stage_bytes = (unsigned)(MEGA_RING_BYTES / nst) & ~127u;
+    size_t ring_total = MEGA_RING_BYTES;
+    if (const char *r = getenv("ECU_MEGA_RING_KB")) ring_total = (size_t)std::max(32, std::min(200, atoi(r))) * 1024;
+    if (nst > MEGA_MAX_STAGES) return no("too many ring stages");
+    const unsigned stage_bytes = (unsigned)(ring_total / nst) & ~127u;
     for (auto &ly : c->layers)
         if (ly.qkv[0].row_bytes > stage_bytes || ly.o.row_bytes > stage_bytes || ly.gu.row_bytes > stage_bytes ||
             ly.d.row_bytes > stage_bytes)
             return no("a weight row does not fit a ring stage");
     if (full && c->out.row_bytes > stage_bytes) return no("a head row does not fit a ring stage");
-    // position splits per KV head: one item per CTA at most, and the split
-    // partials of a head group must fit the shared K/V buffers for the merge
-    const size_t un = std::max((size_t)MEGA_MAX_NB * 28 * sizeof(int),
-                               hd == 128 ? attn_smem_bytes<128>() : attn_smem_bytes<64>());
+    // the shared-memory union: the digit planes of the widest GEMV input (and
+    // the RMSNorm prologue's staging of x and the norm weights above them),
+    // or the attention K/V buffers; the split partials of a head group, which
+    // the merge gathers there, set the position splits per KV head (one
+    // item per CTA at most)
+    size_t un = (size_t)4 * MEGA_ATT_SUB * hd * sizeof(float);
+    un = std::max(un, (size_t)g.n_embd / 32 * 28 * sizeof(int) + 2 * (size_t)g.n_embd * sizeof(float));
+    for (auto &ly : c->layers)
+        for (const DevMat *m : {&ly.qkv[0], &ly.o, &ly.gu, &ly.d})
+            un = std::max(un, (size_t)m->n_in / 32 * 28 * sizeof(int));
+    if (full) un = std::max(un, (size_t)c->out.n_in / 32 * 28 * sizeof(int));
     int n_split = std::min(MEGA_MAX_SPLIT, grid / g.n_head_kv);
     n_split = std::min(n_split, (int)(un / ((size_t)g.n_rep * (hd + 4) * sizeof(float))));
     n_split = std::max(1, std::min(n_split, g.n_ctx));
-    // the RMSNorm prologue stages x and the norm weights above the digit planes
-    if ((size_t)g.n_embd / 32 * 28 * sizeof(int) + 2 * (size_t)g.n_embd * sizeof(float) > un)
-        return no("n_embd too large for the staged RMSNorm prologue");
 
     std::vector<MegaPhase> ph;
     c->ph_kind.clear();
@@ -943,14 +951,18 @@ static int mega_setup(ecu_ctx *c)
     }
     if (ph.size() >= 4095) return no("more phases than the tagged vectors' epochs count");
     for (size_t i = 0; i + 1 < ph.size(); i++) ph[i].next_attn = ph[i + 1].kind == PH_ATTN ? 1 : 0;
-    int red = MEGA_NCW * (hd + 4);          // attention: the position groups' partials
+    // row partials of a whole phase (Q4_0 phases keep 8 per row and k-group
+    // when they fit); attention keeps its position groups' partials there
+    const char *r8 = getenv("ECU_MEGA_RED8");
+    const bool use_red8 = !(r8 && r8[0] == '0');
+    int red = MEGA_NCW * (hd + 4);
     for (auto &p : ph)
         if (p.kind == PH_GEMV) {
-            // Q4_0 phases keep 8 partials per row and k-group when they fit
-            p.red8 = (p.fmt == 4 && p.rpc * (p.nkg * 8 + 1) <= MEGA_RED8_MAX) ? 1 : 0;
+            p.red8 = (use_red8 && p.fmt == 4 && p.rpc * (p.nkg * 8 + 1) <= MEGA_RED8_MAX) ? 1 : 0;
             red = std::max(red, p.red8 ? p.rpc * (p.nkg * 8 + 1) : p.rpc * p.nkg);
+            if (p.epi == EPI_ADD && p.rpc > MEGA_THREADS) return no("residual rows per CTA above the thread count");
         }
-    const size_t smem = mega_smem_total(hd, red);
+    const size_t smem = mega_smem_total(red, (unsigned)nst * stage_bytes, (unsigned)un);
     cudaFuncAttributes fa;
     int optin = 0;
     if (cudaFuncGetAttributes(&fa, fn) != cudaSuccess ||
@@ -1011,6 +1023,7 @@ static int mega_setup(ecu_ctx *c)
     a.n_ctx = g.n_ctx;
     a.n_split = n_split;
     a.red_floats = red;
+    a.union_bytes = (unsigned)un;
     a.nst = nst;
     const char *pfe = getenv("ECU_MEGA_PF");
     a.pf_stages = pfe ? std::max(0, atoi(pfe)) : 0;

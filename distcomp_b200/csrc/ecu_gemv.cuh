@@ -57,47 +57,46 @@ struct GemvArgs {
 
 // ---------------------------------------------------------------- RMSNorm --
 // 1/sqrt(mean(x^2)+eps) with the sum of squares in double (src/engine.c:258-
-// 260).  The double sum runs over 256 fixed partials -- partial v covers the
-// contiguous segment [v*seg, (v+1)*seg), seg = ceil(n/256) -- combined by a
-// fixed tree, so every kernel that calls this gets the same bits whatever its
-// block size.  Each partial's loads are independent (one memory round trip).
-// Threads [0, nthreads) must all call it; `bar` synchronises them.  x is
-// read through L2 (ld.global.cg): in the persistent step kernel other CTAs
-// wrote it since this SM last looked.
-// Partial v of the sum of squares: segment [v*seg, (v+1)*seg), seg = ceil(n/256).
-__device__ __forceinline__ void rms_partials(const float *x, int n, double *dsum, int tid, int nthreads)
+// 260).  The double sum has one fixed order, whatever the block size, so
+// every kernel that normalises a vector gets the same bits:
+//
+//   P[q] = ((x[4q]^2 + x[4q+1]^2) + x[4q+2]^2) + x[4q+3]^2  (elements >= n: 0)
+//          for q < Q = ceil(n/4) rounded up to a multiple of 32;
+//   W[w] = bfly32(P[32w .. 32w+31]),  w < nW = Q/32;
+//   L[l] = ((0 + W[l]) + W[l+32]) + ...  (l < 32);     sum = bfly32(L[0..31]),
+//
+// bfly32 being the xor butterfly v_l += v_{l^o} for o = 16, 8, 4, 2, 1 (every
+// lane ends with the same bits: each pair adds the same two values).  A warp
+// computes a W from 32 consecutive float4s held one per lane, so a kernel
+// that holds its input in registers needs no shared-memory pass before it.
+// nW <= 256 (n <= 32768; the model loader enforces it).
+#define RMS_MAX_W 256
+
+__device__ __forceinline__ double rms_sq4(float4 v)
 {
-    const int seg = (n + 255) / 256;
-    for (int v = tid; v < 256; v += nthreads) {
-        const int lo = min(n, v * seg), hi = min(n, lo + seg);
-        double p = 0.0;
-        if (seg % 4 == 0 && hi - lo == seg) {
-            const float4 *x4 = reinterpret_cast<const float4 *>(x + lo);
-            float4 buf[8];
-            const int nq = seg / 4;
-            for (int base = 0; base < nq; base += 8) {
-                const int m = min(8, nq - base);
+    double p = (double)v.x * (double)v.x;
+    p += (double)v.y * (double)v.y;
+    p += (double)v.z * (double)v.z;
+    p += (double)v.w * (double)v.w;
+    return p;
+}
+
+__device__ __forceinline__ double rms_bfly32(double v)
+{
 #pragma unroll
-                for (int k = 0; k < 8; k++)
-                    if (k < m) buf[k] = __ldcg(x4 + base + k);
-#pragma unroll
-                for (int k = 0; k < 8; k++)
-                    if (k < m) {
-                        const double a = buf[k].x, b = buf[k].y, c = buf[k].z, d = buf[k].w;
-                        p += a * a;
-                        p += b * b;
-                        p += c * c;
-                        p += d * d;
-                    }
-            }
-        } else {
-            for (int i = lo; i < hi; i++) {
-                const double xv = (double)__ldcg(x + i);
-                p += xv * xv;
-            }
-        }
-        dsum[v] = p;
-    }
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Number of W terms for an n-element vector.
+__device__ __forceinline__ int rms_nw(int n) { return ((n + 3) / 4 + 31) / 32; }
+
+// sum = bfly32 of the per-lane sequential sums of W[0..nW) (one warp).
+__device__ __forceinline__ double rms_total_w(const double *W, int nW, int lane)
+{
+    double l = 0.0;
+    for (int w = lane; w < nW; w += 32) l += W[w];
+    return rms_bfly32(l);
 }
 
 __device__ __forceinline__ float rms_from_sum(double ss, int n, float eps)
@@ -106,45 +105,34 @@ __device__ __forceinline__ float rms_from_sum(double ss, int n, float eps)
     return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
 }
 
+// The scale of x[0..n) by threads [0, nthreads) (a multiple of 32), which
+// must all call it; `bar` synchronises them.  dsum: RMS_MAX_W + 1 doubles.
+// x is read through L2 (ld.global.cg).
 template <class Bar>
-__device__ float rms_scale(const float *x, int n, float eps, double *dsum, int tid,
-                           int nthreads, Bar bar)
+__device__ float rms_scale(const float *x, int n, float eps, double *dsum, int tid, int nthreads, Bar bar)
 {
-    rms_partials(x, n, dsum, tid, nthreads);
-    bar();
-    for (int stride = 128; stride > 0; stride >>= 1) {
-        for (int v = tid; v < stride; v += nthreads) dsum[v] += dsum[v + stride];
-        bar();
-    }
-    return rms_from_sum(dsum[0], n, eps);
-}
-
-// The same value with the same additions in the same order, the tree run by
-// warp 0 in registers and shuffles: two barriers instead of nine.  Lane l
-// holds partials l + 32k; strides 128, 64, 32 pair registers, strides 16..1
-// pair lanes (shfl_down), exactly dsum[v] += dsum[v + stride] for v < stride.
-template <class Bar>
-__device__ float rms_scale_w0(const float *x, int n, float eps, double *dsum, int tid,
-                              int nthreads, Bar bar)
-{
-    rms_partials(x, n, dsum, tid, nthreads);
-    bar();
-    if (tid < 32) {
-        double p[8];
-#pragma unroll
-        for (int k = 0; k < 8; k++) p[k] = dsum[tid + 32 * k];
-#pragma unroll
-        for (int k = 0; k < 4; k++) p[k] += p[k + 4];
-        p[0] += p[2];
-        p[1] += p[3];
-        p[0] += p[1];
-        double v = p[0];
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) v += __shfl_down_sync(0xffffffffu, v, o);
-        if (tid == 0) dsum[256] = v;
+    const int nW = rms_nw(n), lane = tid & 31, warp = tid >> 5, nwarps = nthreads >> 5;
+    for (int w = warp; w < nW; w += nwarps) {
+        const int q = 32 * w + lane;
+        double p = 0.0;
+        if ((n & 3) == 0) {
+            if (4 * q < n) p = rms_sq4(__ldcg(reinterpret_cast<const float4 *>(x) + q));
+        } else {
+            for (int i = 4 * q; i < min(n, 4 * q + 4); i++) {
+                const double e = (double)__ldcg(x + i);
+                p = i == 4 * q ? e * e : p + e * e;
+            }
+        }
+        p = rms_bfly32(p);
+        if (lane == 0) dsum[w] = p;
     }
     bar();
-    return rms_from_sum(dsum[256], n, eps);
+    if (warp == 0) {
+        const double t = rms_total_w(dsum, nW, lane);
+        if (lane == 0) dsum[RMS_MAX_W] = t;
+    }
+    bar();
+    return rms_from_sum(dsum[RMS_MAX_W], n, eps);
 }
 
 // ----------------------------------------------------------- argmax tail --
@@ -277,7 +265,7 @@ static __global__ void __launch_bounds__(256) k_rmsnorm(const float *x, const fl
 {
     pdl_wait();
     pdl_trigger();
-    __shared__ double dsum[256];
+    __shared__ double dsum[RMS_MAX_W + 1];
     const float s = rms_scale(x, n, eps, dsum, threadIdx.x, blockDim.x, [] { __syncthreads(); });
     for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = __fmul_rn(__fmul_rn(x[i], s), w[i]);
 }
@@ -445,7 +433,7 @@ __host__ __device__ inline FastSmem fast_smem_plan(size_t row_bytes, int stage_r
     // digit planes shared by the rowpar warps of a k-group: 28 words per block
     const size_t dig_bytes = rowpar > 1 ? (size_t)nkg * 32 * 28 * sizeof(int) : 0;
     p.dsum = p.dig + dig_bytes;
-    p.argsh = p.dsum + 256 * sizeof(double);
+    p.argsh = p.dsum + (RMS_MAX_W + 2) * sizeof(double);
     p.total = p.argsh + 32 * sizeof(ArgBest);
     return p;
 }

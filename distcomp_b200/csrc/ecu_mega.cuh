@@ -32,7 +32,8 @@
 
 #define MEGA_NCW 16                      // warps (all of them consume the ring)
 #define MEGA_THREADS (32 * MEGA_NCW)
-#define MEGA_RING_BYTES (111 * 1024)    // the weight ring, split into nst stages
+#define MEGA_RING_BYTES (111 * 1024)    // default weight ring, split into nst stages
+#define MEGA_ATT_SUB 32                  // K/V rows per buffer (4 buffers: K and V of two halves)
 #define MEGA_MAX_STAGES 8
 #define MEGA_MAX_NB 512                  // input blocks of a GEMV (n_in <= 16384)
 #define MEGA_MAX_SPLIT 64                // position splits per KV head
@@ -97,6 +98,7 @@ struct MegaArgs {
     int              layers_advance;// LAYERS: st->pos++ once the last phase is done
     int              n_embd, n_head, n_kv, n_ctx, n_split;
     int              red_floats;    // row-partial floats the largest GEMV phase keeps
+    unsigned         union_bytes;   // digit planes | attention K/V buffers
     int              nst;           // ring stages (<= MEGA_MAX_STAGES)
     int              pf_stages;     // chunks warmed in L2 ahead of the ring
     unsigned         stage_bytes;   // bytes per ring stage (multiple of 128)
@@ -106,8 +108,8 @@ struct MegaArgs {
 // ------------------------------------------------------- tagged vectors --
 // The phases hand vectors to each other without grid barriers: every element
 // is one 8-byte word {float, epoch of the phase that wrote it}, stored and
-// loaded whole (single-copy atomic), so a reader that sees the epoch it
-// expects also sees the value.  A reader spins on words that still carry an
+// loaded whole (aligned 64-bit relaxed accesses at GPU scope are single-copy
+// atomic), so a reader that sees the epoch it expects also sees the value.  A reader spins on words that still carry an
 // older epoch.  Epoch = (launch number mod 2^20) << 12 | (phase + 1): unique
 // within a launch and against the previous one, which wrote every word.
 // Every phase's input depends on all CTAs' output of an earlier phase, so
@@ -121,20 +123,20 @@ __device__ __forceinline__ unsigned ll_epoch(unsigned launch, int phase)
 __device__ __forceinline__ void ll_put(unsigned long long *p, float v, unsigned e)
 {
     const unsigned long long w = ((unsigned long long)e << 32) | __float_as_uint(v);
-    asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
 
 __device__ __forceinline__ unsigned long long ll_word(const unsigned long long *p)
 {
     unsigned long long w;
-    asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
     return w;
 }
 
 __device__ __forceinline__ ulonglong2 ll_word2(const unsigned long long *p)
 {
     ulonglong2 w;
-    asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(w.x), "=l"(w.y) : "l"(p) : "memory");
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(w.x), "=l"(w.y) : "l"(p) : "memory");
     return w;
 }
 
@@ -160,18 +162,58 @@ __device__ __forceinline__ float ll_get(const unsigned long long *p, unsigned e,
     return __uint_as_float((unsigned)w);
 }
 
-// Four consecutive tagged words (16-byte aligned) as a float4.
-__device__ __forceinline__ float4 ll_get4(const unsigned long long *p, unsigned e, int *status)
+// Four tagged words (two 16-byte loads) all carrying epoch e.
+__device__ __forceinline__ bool ll_tags4(const ulonglong2 (&w)[2], unsigned e)
 {
-    ulonglong2 a = ll_word2(p), b = ll_word2(p + 2);
-    uint64_t t0 = 0;
-    for (unsigned it = 1; ((unsigned)(a.x >> 32) != e || (unsigned)(a.y >> 32) != e || (unsigned)(b.x >> 32) != e ||
-                           (unsigned)(b.y >> 32) != e) && ll_keep_waiting(it, t0, status); it++) {
-        a = ll_word2(p);
-        b = ll_word2(p + 2);
+    return (unsigned)(w[0].x >> 32) == e && (unsigned)(w[0].y >> 32) == e && (unsigned)(w[1].x >> 32) == e &&
+           (unsigned)(w[1].y >> 32) == e;
+}
+
+// Float4s t = t0 + k*stride (k < K, t < nq) of a phase input: tagged (phase
+// in_ep of this launch) or the plain kernel input.  Every load is issued
+// before the first wait, so the K fetches cost one L2 round trip, not K.
+template <int K>
+__device__ __forceinline__ void input_batch(const MegaArgs &a, const MegaPhase &ph, int t0, int stride, int nq,
+                                            unsigned ein, float4 (&v)[K])
+{
+    if (ph.in_ep >= 0) {
+        ulonglong2 w[K][2];
+#pragma unroll
+        for (int k = 0; k < K; k++) {
+            const int t = t0 + k * stride;
+            if (t < nq) {
+                w[k][0] = ll_word2(ph.x_ll + 4 * (size_t)t);
+                w[k][1] = ll_word2(ph.x_ll + 4 * (size_t)t + 2);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < K; k++) {
+            const int t = t0 + k * stride;
+            if (t < nq) {
+                uint64_t tw = 0;
+                for (unsigned it = 1; !ll_tags4(w[k], ein) && ll_keep_waiting(it, tw, a.status); it++) {
+                    w[k][0] = ll_word2(ph.x_ll + 4 * (size_t)t);
+                    w[k][1] = ll_word2(ph.x_ll + 4 * (size_t)t + 2);
+                }
+                v[k] = make_float4(__uint_as_float((unsigned)w[k][0].x), __uint_as_float((unsigned)w[k][0].y),
+                                   __uint_as_float((unsigned)w[k][1].x), __uint_as_float((unsigned)w[k][1].y));
+            }
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < K; k++) {
+            const int t = t0 + k * stride;
+            if (t < nq) v[k] = __ldcg(reinterpret_cast<const float4 *>(ph.x) + t);
+        }
     }
-    return make_float4(__uint_as_float((unsigned)a.x), __uint_as_float((unsigned)a.y),
-                       __uint_as_float((unsigned)b.x), __uint_as_float((unsigned)b.y));
+}
+
+// A tagged word already loaded into w: re-polled until it carries epoch e.
+__device__ __forceinline__ float ll_settle(const unsigned long long *p, unsigned long long w, unsigned e, int *status)
+{
+    uint64_t t0 = 0;
+    for (unsigned it = 1; (unsigned)(w >> 32) != e && ll_keep_waiting(it, t0, status); it++) w = ll_word(p);
+    return __uint_as_float((unsigned)w);
 }
 
 // ------------------------------------------------------------ smem layout --
@@ -180,20 +222,18 @@ struct MegaSmem {
     size_t ring, bars, abar, red, un, dsum, argsh, total;
 };
 
-template <int HD>
-__host__ __device__ inline MegaSmem mega_smem_plan(int red_floats)
+__host__ __device__ inline MegaSmem mega_smem_plan(int red_floats, unsigned ring_bytes, unsigned union_bytes)
 {
     MegaSmem p;
     p.ring = 0;
-    p.bars = p.ring + (size_t)MEGA_RING_BYTES;
+    p.bars = p.ring + (size_t)ring_bytes;
     p.abar = p.bars + MEGA_MAX_STAGES * sizeof(uint64_t);
     p.red = (p.abar + 4 * sizeof(uint64_t) + 15) & ~(size_t)15;    // K/V halves, partial gather
     p.un = (p.red + (size_t)red_floats * sizeof(float) + 127) & ~(size_t)127;
-    // union: digit planes of the GEMV input | attention K/V buffers
-    const size_t dig = (size_t)MEGA_MAX_NB * 28 * sizeof(int);
-    const size_t att = attn_smem_bytes<HD>();
-    p.dsum = p.un + (dig > att ? dig : att);
-    p.argsh = p.dsum + 264 * sizeof(double);      // 256 partials + the total
+    // union: digit planes (and the RMSNorm staging) of a GEMV input | the
+    // attention K/V buffers and split-partial gather
+    p.dsum = p.un + (((size_t)union_bytes + 15) & ~(size_t)15);
+    p.argsh = p.dsum + (RMS_MAX_W + 8) * sizeof(double);   // W terms + the total
     p.total = p.argsh + 32 * sizeof(ArgBest);
     return p;
 }
@@ -281,6 +321,12 @@ struct MegaRing {
     unsigned    done[MEGA_MAX_STAGES];
 };
 
+// The ring slot this CTA's consumers read next, and its barrier parity.
+struct RingPos {
+    int      slot;
+    unsigned par;
+};
+
 struct MegaShared {
     int       pos;         // cache position of this step (read once at kernel start)
     unsigned  launch;      // launch number (epochs of the tagged vectors)
@@ -312,12 +358,15 @@ __device__ __forceinline__ void cursor_load_phase(const MegaArgs &a, ChunkCursor
     c->sr = q.sr;
 }
 
-// The chunk at the cursor, and advance it; false at the end of the list.
-__device__ __forceinline__ bool cursor_next(const MegaArgs &a, ChunkCursor *c, const uint8_t *&src, uint32_t &bytes)
+// The chunk at the cursor (its first row, rows, row bytes), and advance it;
+// false at the end of the list.
+__device__ __forceinline__ bool cursor_next(const MegaArgs &a, ChunkCursor *c, const uint8_t *&src, int &rows,
+                                            unsigned &row_bytes)
 {
     while (c->p < a.n_ph && c->i >= c->nrows) cursor_load_phase(a, c, c->p + 1);
     if (c->p >= a.n_ph) return false;
-    bytes = (uint32_t)(min(c->sr, c->nrows - c->i) * c->row_bytes);
+    rows = min(c->sr, c->nrows - c->i);
+    row_bytes = c->row_bytes;
     src = c->w + (size_t)c->i * c->row_bytes;
     c->i += c->sr;
     return true;
@@ -330,29 +379,33 @@ __device__ __forceinline__ void ring_issue(const MegaArgs &a, const MegaShared &
 {
     MegaRing      *rc = S.rc;
     const uint8_t *src;
-    uint32_t       bytes;
-    if (!cursor_next(a, &rc->cp, src, bytes)) return;
+    int            rows;
+    unsigned       rb;
+    if (!cursor_next(a, &rc->cp, src, rows, rb)) return;
+    const uint32_t bytes = (uint32_t)rows * rb;
     mbar_expect_tx(&S.full[slot], bytes);
     bulk_g2s(S.ring + (size_t)slot * a.stage_bytes, src, bytes, &S.full[slot]);
     rc->issued++;
-    if (warm && a.pf_stages > 0 && cursor_next(a, &rc->pf, src, bytes)) prefetch_l2(src, bytes);
+    if (warm && a.pf_stages > 0 && cursor_next(a, &rc->pf, src, rows, rb)) prefetch_l2(src, (uint32_t)rows * rb);
 }
 
 // Lane 0 of a warp that is done with ring slot `slot` (after __syncwarp).
 // The arrivals count up forever; the warp whose arrival makes a multiple of
-// MEGA_NCW is the last reader of this use of the slot and refills it.  The
-// acq_rel atomic orders every warp's reads of the slot (and the previous
-// refill's cursor update) before the refill; the proxy fence orders them
-// before the bulk copy's writes.  Refills happen in chunk order: the last
-// release of slot s+1 comes after every warp's release of slot s.
+// MEGA_NCW is the last reader of this use of the slot and refills it.  Every
+// arrival is a release; the refilling warp's acquire fence then orders every
+// warp's reads of the slot (and the previous refill's cursor update) before
+// the refill, and the proxy fence orders them before the bulk copy's writes.
+// Refills happen in chunk order: the last release of slot s+1 comes after
+// every warp's release of slot s.
 __device__ __forceinline__ void ring_release(const MegaArgs &a, const MegaShared &S, int slot)
 {
     unsigned old;
-    asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], 1;"
+    asm volatile("atom.release.cta.shared::cta.add.u32 %0, [%1], 1;"
                  : "=r"(old)
                  : "r"(smem_addr(&S.rc->done[slot]))
                  : "memory");
     if ((old + 1) % MEGA_NCW == 0) {
+        asm volatile("fence.acq_rel.cta;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         ring_issue(a, S, slot);
     }
@@ -380,6 +433,52 @@ __device__ __forceinline__ float sum8_tree(const float *p)
     return ((p[0] + p[4]) + (p[2] + p[6])) + ((p[1] + p[5]) + (p[3] + p[7]));
 }
 
+// block_dot for four rows (row0 + k*stride) at once: all loads first, then
+// the integer sums with each plane's low and high nibbles in separate chains
+// (24 independent chains of 4 dp4a instead of 12 of 8).  Integer addition is
+// exact, so every row gets block_dot's bits.
+template <int FMT>
+__device__ __forceinline__ void block_dot4(const uint8_t *row0, size_t stride, int nb, int b, const int (&xw)[3][8],
+                                           const int (&off)[3], float sxs, float (&v)[4])
+{
+    if (FMT == 4) {
+        uint4 q[4];
+        float d[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            q[k] = *reinterpret_cast<const uint4 *>(row0 + k * stride + (size_t)b * 16);
+            d[k] = __half2float(*reinterpret_cast<const __half *>(row0 + k * stride + (size_t)nb * 16 + 2 * b));
+        }
+        int acc[4][6];
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            acc[k][0] = off[0]; acc[k][1] = off[1]; acc[k][2] = off[2];
+            acc[k][3] = 0; acc[k][4] = 0; acc[k][5] = 0;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const uint32_t w = j == 0 ? q[k].x : j == 1 ? q[k].y : j == 2 ? q[k].z : q[k].w;
+                const int lo = (int)(w & 0x0F0F0F0Fu), hi = (int)((w >> 4) & 0x0F0F0F0Fu);
+                acc[k][0] = __dp4a(lo, xw[0][j], acc[k][0]);
+                acc[k][3] = __dp4a(hi, xw[0][4 + j], acc[k][3]);
+                acc[k][1] = __dp4a(lo, xw[1][j], acc[k][1]);
+                acc[k][4] = __dp4a(hi, xw[1][4 + j], acc[k][4]);
+                acc[k][2] = __dp4a(lo, xw[2][j], acc[k][2]);
+                acc[k][5] = __dp4a(hi, xw[2][4 + j], acc[k][5]);
+            }
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int t = (acc[k][0] + acc[k][3]) * 16384 + (acc[k][1] + acc[k][4]) * 128 + (acc[k][2] + acc[k][5]);
+            v[k] = (float)t * (d[k] * sxs);
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < 4; k++) v[k] = block_dot<FMT>(row0 + k * stride, nb, b, xw, off, sxs);
+    }
+}
+
 // Rows [0, rows) of one ring stage against this lane's block column: warp
 // (g, rp) takes rows rp, rp + rowpar, ... four at a time.  Row partials of
 // k-group g land in red[row * nkg + g], or with RED8 (the last three levels
@@ -392,12 +491,17 @@ __device__ __forceinline__ void mega_stage_rows(const uint8_t *stage, int rows, 
                                                 const int (&xw)[3][8], const int (&off)[3], float sxs,
                                                 float *red)
 {
+    static_assert(FAST_RB == 4, "four rows per warp batch");
     for (int i0 = rp; i0 < rows; i0 += FAST_RB * rowpar) {
         float v[FAST_RB];
+        if (i0 + (FAST_RB - 1) * rowpar < rows) {
+            block_dot4<FMT>(stage + (size_t)i0 * row_bytes, (size_t)rowpar * row_bytes, nb, b, xw, off, sxs, v);
+        } else {
 #pragma unroll
-        for (int k = 0; k < FAST_RB; k++) {
-            const int ii = i0 + k * rowpar;
-            v[k] = ii < rows ? block_dot<FMT>(stage + (size_t)ii * row_bytes, nb, b, xw, off, sxs) : 0.0f;
+            for (int k = 0; k < FAST_RB; k++) {
+                const int ii = i0 + k * rowpar;
+                v[k] = ii < rows ? block_dot<FMT>(stage + (size_t)ii * row_bytes, nb, b, xw, off, sxs) : 0.0f;
+            }
         }
         const int k = (lane >> 3) & 3, ii = i0 + k * rowpar;
         if (RED8) {
@@ -421,10 +525,6 @@ __device__ __forceinline__ float row_total(const float *red, int r, int nkg, boo
     return acc;
 }
 
-// One GEMV phase on the consumer side: digit planes of the (normed) input
-// into shared memory, this CTA's ring stages of the matrix, the epilogue.
-// `ring_s` counts ring stages consumed over the whole step.  One body for
-// both row formats: only the innermost loop depends on it.
 // Digit planes of the digit store for the input block of 8 lanes (t = b*8 + q).
 __device__ __forceinline__ void store_digits(const MegaShared &S, int t, float4 v)
 {
@@ -439,61 +539,46 @@ __device__ __forceinline__ void store_digits(const MegaShared &S, int t, float4 
     if (q == 0) d[27] = __float_as_int(sxs);
 }
 
-// Element t4 (a float4) of this phase's input: tagged (written by phase
-// in_ep of this launch) or the plain kernel input.
-__device__ __forceinline__ float4 input4(const MegaArgs &a, const MegaPhase &ph, int t4, unsigned ein)
-{
-    if (ph.in_ep >= 0) return ll_get4(ph.x_ll + 4 * (size_t)t4, ein, a.status);
-    return __ldcg(reinterpret_cast<const float4 *>(ph.x) + t4);
-}
-
 // RMSNorm prologue: x and the norm weights are staged in shared memory above
-// the digit planes (one round of loads), partial v of the sum of squares
-// adds its ceil(n/256) elements in order and warp 0 runs rms_scale_w0's tree
-// -- the scale k_rmsnorm and k_gemv_fast compute, bit for bit -- then the
-// digit planes of the normed input.
+// the digit planes (loads of up to four float4s per thread in flight at
+// once); each warp adds its 32 float4s' squares into one W term of the sum
+// (rms_scale's order) straight from registers, warp 0 adds the W terms --
+// the scale k_rmsnorm and k_gemv_fast compute, bit for bit -- then the digit
+// planes of the normed input.
 __device__ __forceinline__ void norm_prologue(const MegaArgs &a, const MegaPhase &ph, const MegaShared &S, int tid,
                                               int nct, unsigned ein)
 {
-    const int n = ph.n_in, nq = n / 4, nb = n / 32;
+    const int n = ph.n_in, nq = n / 4, nb = n / 32, lane = tid & 31;
     float4 *xs = reinterpret_cast<float4 *>(S.dig + (size_t)nb * 28);   // 112 bytes a block: 16-aligned
     float4 *ws = xs + nq;
     const float4 *w4 = reinterpret_cast<const float4 *>(ph.norm_w);
-    for (int t = tid; t < nq; t += nct) {
-        ws[t] = __ldg(w4 + t);
-        xs[t] = input4(a, ph, t, ein);
-    }
-    named_bar(1, nct);
-    const float *xf = reinterpret_cast<const float *>(xs);
-    const int    seg = (n + 255) / 256;
-    for (int v = tid; v < 256; v += nct) {
-        const int lo = min(n, v * seg), hi = min(n, lo + seg);
-        double p = 0.0;
-        for (int i = lo; i < hi; i++) {
-            const double e = xf[i];
-            p += e * e;
+    // whole warps throughout: nq is a multiple of 256
+    for (int base = tid; base < nq; base += 2 * nct) {
+        float4 wv[2], v[2];
+#pragma unroll
+        for (int k = 0; k < 2; k++)
+            if (base + k * nct < nq) wv[k] = __ldg(w4 + base + k * nct);
+        input_batch<2>(a, ph, base, nct, nq, ein, v);
+#pragma unroll
+        for (int k = 0; k < 2; k++) {
+            const int t = base + k * nct;
+            if (t < nq) {
+                ws[t] = wv[k];
+                xs[t] = v[k];
+                const double p = rms_bfly32(rms_sq4(v[k]));
+                if (lane == 0) S.dsum[t >> 5] = p;
+            }
         }
-        S.dsum[v] = p;
     }
     named_bar(1, nct);
     if (tid < 32) {
-        double q[8];
-#pragma unroll
-        for (int k = 0; k < 8; k++) q[k] = S.dsum[tid + 32 * k];
-#pragma unroll
-        for (int k = 0; k < 4; k++) q[k] += q[k + 4];
-        q[0] += q[2];
-        q[1] += q[3];
-        q[0] += q[1];
-        double v = q[0];
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) v += __shfl_down_sync(0xffffffffu, v, o);
-        if (tid == 0) S.dsum[256] = v;
+        const double t = rms_total_w(S.dsum, nq / 32, tid);
+        if (tid == 0) S.dsum[RMS_MAX_W] = t;
     }
     named_bar(1, nct);
-    const float scale = rms_from_sum(S.dsum[256], n, a.eps);
+    const float scale = rms_from_sum(S.dsum[RMS_MAX_W], n, a.eps);
     float4 *xn4 = (ph.xn && blockIdx.x == 0) ? reinterpret_cast<float4 *>(ph.xn) : nullptr;
-    for (int t = tid; t < nq; t += nct) {         // whole warps: nq is a multiple of 256
+    for (int t = tid; t < nq; t += nct) {
         float4       v = xs[t];
         const float4 w = ws[t];
         v.x = __fmul_rn(__fmul_rn(v.x, scale), w.x);
@@ -507,9 +592,13 @@ __device__ __forceinline__ void norm_prologue(const MegaArgs &a, const MegaPhase
 
 __device__ __forceinline__ void attn_prefetch(const MegaArgs &a, const MegaPhase &ph, int pos, int hd);
 
+// One GEMV phase on the consumer side: digit planes of the (normed) input
+// into shared memory, this CTA's ring stages of the matrix (rp_: the next
+// slot to read, carried over the whole step), the epilogue.  One body for
+// both row formats: only the innermost loop depends on it.
 // next: the following phase's descriptor when it is attention (its K/V rows
 // are warmed in L2 and the RoPE row staged once the main loop is done).
-__device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShared &S, int &ring_s, int p_idx,
+__device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShared &S, RingPos &rp_, int p_idx,
                           const MegaPhase *next, int hd)
 {
     unsigned long long *det = (a.phase_detail && blockIdx.x == 0 && threadIdx.x == 0)
@@ -521,6 +610,14 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
     const int r0 = blockIdx.x * ph.rpc;
     const int nrows = max(0, min(ph.n_out, r0 + ph.rpc) - r0);
     const unsigned row_bytes = ph.row_bytes;
+    const int epi = ph.epi;
+
+    // the residual this CTA's rows add to (its own rows: no other CTA writes
+    // them in this phase; nrows <= MEGA_THREADS for EPI_ADD): requested now,
+    // settled after the prologue
+    const bool has_res = epi == EPI_ADD && tid < nrows;
+    unsigned long long yw = 0;
+    if (has_res && ph.y_ep >= 0) yw = ll_word(a.x_ll + r0 + tid);
 
     // ---- prologue: digit planes of every input block -----------------------
     // A CTA without rows reads no input: nothing it writes would tell a later
@@ -533,23 +630,20 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
     } else {
         const int nq = nb * 8;                          // float4s of x; whole warps (nb % 32 == 0)
         for (int base = tid; base < nq; base += 2 * nct) {
-            const bool   two = base + nct < nq;
-            const float4 va = input4(a, ph, base, ein);
-            float4       vb = va;
-            if (two) vb = input4(a, ph, base + nct, ein);
-            store_digits(S, base, va);
-            if (two) store_digits(S, base + nct, vb);
+            float4 v[2];
+            input_batch<2>(a, ph, base, nct, nq, ein, v);
+#pragma unroll
+            for (int k = 0; k < 2; k++)
+                if (base + k * nct < nq) store_digits(S, base + k * nct, v[k]);
         }
     }
+    float yprev = 0.0f;
+    if (has_res)
+        yprev = ph.y_ep >= 0 ? ll_settle(a.x_ll + r0 + tid, yw, ll_epoch(S.launch, ph.y_ep), a.status)
+                             : __ldcg(ph.y + r0 + tid);
     named_bar(1, nct);
 
     if (det) det[0] = clock64();
-    // the residual this CTA's rows add to (its own rows: no other CTA writes
-    // them in this phase), fetched now so the epilogue does not wait for it
-    float yprev = 0.0f;
-    if (ph.epi == EPI_ADD && tid < nrows)
-        yprev = ph.y_ep >= 0 ? ll_get(a.x_ll + r0 + tid, ll_epoch(S.launch, ph.y_ep), a.status)
-                             : __ldcg(ph.y + r0 + tid);
     // ---- main loop ------------------------------------------------------------
     const bool active = warp < nkg * rowpar;
     const int  g = active ? warp % nkg : 0, rp = active ? warp / nkg : 0;
@@ -570,8 +664,8 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
     }
     const int sr = ph.sr;
     for (int i = 0; i < nrows; i += sr) {
-        const int slot = ring_s % a.nst;
-        const unsigned par = (unsigned)(ring_s / a.nst) & 1u;
+        const int      slot = rp_.slot;
+        const unsigned par = rp_.par;
         if (det && !mbar_test(&S.full[slot], par)) {
             const unsigned long long t0 = globaltimer_ns();
             mbar_wait<true>(&S.full[slot], par, a.status);
@@ -594,7 +688,10 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
         }
         __syncwarp();
         if (lane == 0) ring_release(a, S, slot);
-        ring_s++;
+        if (++rp_.slot == a.nst) {
+            rp_.slot = 0;
+            rp_.par ^= 1u;
+        }
     }
     // the digit planes share bytes with the attention K/V buffers, which bulk
     // copies (the async proxy) fill later: order these generic accesses first
@@ -612,7 +709,6 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
     }
 
     // ---- epilogue over this CTA's rows --------------------------------------
-    const int      epi = ph.epi;
     float         *y = ph.y;
     const unsigned eout = ll_epoch(S.launch, p_idx);
     if (epi == EPI_SWIGLU) {
@@ -627,10 +723,7 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
     for (int r = tid; r < nrows; r += nct) {
         const float acc = row_total(S.red, r, nkg, red8);
         if (epi == EPI_ADD) {
-            const float prev = r == tid ? yprev
-                                        : (ph.y_ep >= 0 ? ll_get(a.x_ll + r0 + r, ll_epoch(S.launch, ph.y_ep), a.status)
-                                                        : __ldcg(y + r0 + r));
-            const float out = prev + acc;
+            const float out = yprev + acc;         // r == tid: nrows <= MEGA_THREADS
             ll_put(ph.y_ll + r0 + r, out, eout);
             if (ph.out_plain) y[r0 + r] = out;
         } else if (epi == EPI_STORE) {
@@ -709,18 +802,18 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
     const int pos = S.pos, npos = pos + 1;
     const int chunk = (npos + a.n_split - 1) / a.n_split;
     const int t0 = min(npos, sp * chunk), t1 = has ? min(npos, t0 + chunk) : t0;
-    const int nround = (t1 - t0 + 2 * ATT_SUB - 1) / (2 * ATT_SUB);   // 64 positions a round
+    const int nround = (t1 - t0 + 2 * MEGA_ATT_SUB - 1) / (2 * MEGA_ATT_SUB);   // 2 * MEGA_ATT_SUB positions a round
     float *kbase = ph.kc + (size_t)g * a.n_ctx * HD;
     float *vbase = ph.vc + (size_t)g * a.n_ctx * HD;
-    // half hf (32 rows) of round r of the slice below the current position
+    // half hf (MEGA_ATT_SUB rows) of round r of the slice below the current position
     // (contiguous in the head-major cache): one bulk copy for K, one for V;
     // thread 0 issues half 0, thread 32 half 1
     auto issue = [&](int r, int hf) {
-        const int c0 = t0 + r * 2 * ATT_SUB + hf * ATT_SUB;
-        const int c1 = min(min(t1, c0 + ATT_SUB), pos);
+        const int c0 = t0 + r * 2 * MEGA_ATT_SUB + hf * MEGA_ATT_SUB;
+        const int c1 = min(min(t1, c0 + MEGA_ATT_SUB), pos);
         const int nr = c1 > c0 ? c1 - c0 : 0;
-        float *kb = S.kvbuf + (size_t)hf * ATT_SUB * RS;
-        float *vb = S.kvbuf + (size_t)(2 + hf) * ATT_SUB * RS;
+        float *kb = S.kvbuf + (size_t)hf * MEGA_ATT_SUB * RS;
+        float *vb = S.kvbuf + (size_t)(2 + hf) * MEGA_ATT_SUB * RS;
         const uint32_t bytes = (uint32_t)(nr * HD * sizeof(float));
         mbar_expect_tx(&S.abar[hf], 2 * bytes);
         if (nr > 0) {
@@ -732,24 +825,33 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
     const float *cs_s = S.cs;
     const unsigned ein = ll_epoch(S.launch, ph.in_ep);
     const int qdim = a.n_head * HD, kvdim = a.n_kv * HD;
-    // a CTA without a work item reads nothing (see the GEMV prologue)
-    for (int i = has ? tid : nct; i < NREP * (HD / 2); i += nct) {
-        const int h = i / (HD / 2), j = i % (HD / 2), row = (g * NREP + h) * HD;
-        float x0 = ll_get(a.qkv_ll + row + j, ein, a.status), x1 = ll_get(a.qkv_ll + row + j + HD / 2, ein, a.status);
-        if (ph.bq) { x0 = __fadd_rn(x0, ph.bq[row + j]); x1 = __fadd_rn(x1, ph.bq[row + j + HD / 2]); }
-        rope_pair(x0, x1, cs_s[2 * j], cs_s[2 * j + 1]);
-        q_s[h * HD + j] = x0;
-        q_s[h * HD + j + HD / 2] = x1;
-    }
-    for (int j = has ? tid : nct; j < HD / 2; j += nct) {
-        const int kr = qdim + g * HD, vr = qdim + kvdim + g * HD;
-        float k0 = ll_get(a.qkv_ll + kr + j, ein, a.status), k1 = ll_get(a.qkv_ll + kr + j + HD / 2, ein, a.status);
-        float v0 = ll_get(a.qkv_ll + vr + j, ein, a.status), v1 = ll_get(a.qkv_ll + vr + j + HD / 2, ein, a.status);
-        if (ph.bk) { k0 = __fadd_rn(k0, ph.bk[g * HD + j]); k1 = __fadd_rn(k1, ph.bk[g * HD + j + HD / 2]); }
-        if (ph.bv) { v0 = __fadd_rn(v0, ph.bv[g * HD + j]); v1 = __fadd_rn(v1, ph.bv[g * HD + j + HD / 2]); }
-        rope_pair(k0, k1, cs_s[2 * j], cs_s[2 * j + 1]);
-        knew[j] = k0; knew[j + HD / 2] = k1;
-        vnew[j] = v0; vnew[j + HD / 2] = v1;
+    // a CTA without a work item reads nothing (see the GEMV prologue).
+    // Items [0, NREP*HD/2): a query (head, rotation pair); then HD/2 K/V
+    // pairs; each thread's words are all requested before it waits on one
+    constexpr int NQP = NREP * (HD / 2);
+    for (int i = has ? tid : nct; i < NQP + HD / 2; i += nct) {
+        if (i < NQP) {
+            const int h = i / (HD / 2), j = i % (HD / 2), row = (g * NREP + h) * HD;
+            const unsigned long long *p0 = a.qkv_ll + row + j, *p1 = p0 + HD / 2;
+            const unsigned long long w0 = ll_word(p0), w1 = ll_word(p1);
+            float x0 = ll_settle(p0, w0, ein, a.status), x1 = ll_settle(p1, w1, ein, a.status);
+            if (ph.bq) { x0 = __fadd_rn(x0, ph.bq[row + j]); x1 = __fadd_rn(x1, ph.bq[row + j + HD / 2]); }
+            rope_pair(x0, x1, cs_s[2 * j], cs_s[2 * j + 1]);
+            q_s[h * HD + j] = x0;
+            q_s[h * HD + j + HD / 2] = x1;
+        } else {
+            const int j = i - NQP, kr = qdim + g * HD, vr = qdim + kvdim + g * HD;
+            const unsigned long long *pk0 = a.qkv_ll + kr + j, *pk1 = pk0 + HD / 2;
+            const unsigned long long *pv0 = a.qkv_ll + vr + j, *pv1 = pv0 + HD / 2;
+            const unsigned long long wk0 = ll_word(pk0), wk1 = ll_word(pk1), wv0 = ll_word(pv0), wv1 = ll_word(pv1);
+            float k0 = ll_settle(pk0, wk0, ein, a.status), k1 = ll_settle(pk1, wk1, ein, a.status);
+            float v0 = ll_settle(pv0, wv0, ein, a.status), v1 = ll_settle(pv1, wv1, ein, a.status);
+            if (ph.bk) { k0 = __fadd_rn(k0, ph.bk[g * HD + j]); k1 = __fadd_rn(k1, ph.bk[g * HD + j + HD / 2]); }
+            if (ph.bv) { v0 = __fadd_rn(v0, ph.bv[g * HD + j]); v1 = __fadd_rn(v1, ph.bv[g * HD + j + HD / 2]); }
+            rope_pair(k0, k1, cs_s[2 * j], cs_s[2 * j + 1]);
+            knew[j] = k0; knew[j + HD / 2] = k1;
+            vnew[j] = v0; vnew[j + HD / 2] = v1;
+        }
     }
     named_bar(1, nct);
     if (det) det[0] = clock64();
@@ -759,19 +861,20 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
             vbase[(size_t)pos * HD + j] = vnew[j];
         }
     // warp (h, grp): query head h, positions grp*Q .. grp*Q+Q-1 of each
-    // round's 64 (G = 16/NREP groups), so the serial V accumulation is Q long
-    constexpr int G = MEGA_NCW / NREP, Q = 2 * ATT_SUB / G;
-    static_assert(G >= 1 && Q >= 1 && Q <= ATT_SUB, "position groups");
+    // round's 2*MEGA_ATT_SUB (G = 16/NREP groups), so the serial V
+    // accumulation is Q long
+    constexpr int G = MEGA_NCW / NREP, Q = 2 * MEGA_ATT_SUB / G;
+    static_assert(G >= 1 && Q >= 1 && Q <= MEGA_ATT_SUB, "position groups");
     const int h = warp % NREP, grp = warp / NREP;
-    const int hf = (grp * Q) / ATT_SUB, off = grp * Q - hf * ATT_SUB;
+    const int hf = (grp * Q) / MEGA_ATT_SUB, off = grp * Q - hf * MEGA_ATT_SUB;
     float  m_run = -INFINITY, l_run = 0.0f;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int r = 0; r < nround; r++) {
-        const int c0 = t0 + r * 2 * ATT_SUB + grp * Q, cn = max(0, min(Q, t1 - c0));
+        const int c0 = t0 + r * 2 * MEGA_ATT_SUB + grp * Q, cn = max(0, min(Q, t1 - c0));
         if (cn > 0) {
             mbar_wait<true>(&S.abar[hf], (unsigned)(att_sb + r) & 1u, a.status);
-            const float *kb = S.kvbuf + (size_t)hf * ATT_SUB * RS + (size_t)off * RS;
-            const float *vb = S.kvbuf + (size_t)(2 + hf) * ATT_SUB * RS + (size_t)off * RS;
+            const float *kb = S.kvbuf + (size_t)hf * MEGA_ATT_SUB * RS + (size_t)off * RS;
+            const float *vb = S.kvbuf + (size_t)(2 + hf) * MEGA_ATT_SUB * RS + (size_t)off * RS;
             const float *krow = (c0 + lane == pos) ? knew : kb + lane * RS;
             float s = -INFINITY;
             if (lane < cn) {
@@ -970,7 +1073,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a)
 {
     extern __shared__ __align__(128) uint8_t smem[];
     const int      nct = MEGA_NCW * 32, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const MegaSmem P = mega_smem_plan<HD>(a.red_floats);
+    const MegaSmem P = mega_smem_plan(a.red_floats, a.nst * a.stage_bytes, a.union_bytes);
     MegaShared S;
     S.ring = smem + P.ring;
     S.full = reinterpret_cast<uint64_t *>(smem + P.bars);
@@ -1008,8 +1111,10 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a)
         // pf_stages chunks ahead of them
         S.rc->pf = S.rc->cp;
         const uint8_t *src;
-        uint32_t       bytes;
-        for (int s = 0; s < a.pf_stages && cursor_next(a, &S.rc->pf, src, bytes); s++) prefetch_l2(src, bytes);
+        int            rows;
+        unsigned       rb;
+        for (int s = 0; s < a.pf_stages && cursor_next(a, &S.rc->pf, src, rows, rb); s++)
+            prefetch_l2(src, (uint32_t)rows * rb);
     }
     __syncthreads();
     S.pos = pos_s;
@@ -1020,7 +1125,8 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a)
         a.phase_ns[0] = globaltimer_ns();
         a.phase_clk[0] = clock64();
     }
-    int ring_s = 0, att_sb = 0, merges = 0;
+    RingPos rpos{0, 0u};
+    int att_sb = 0, merges = 0;
     for (int p = 0; p < a.n_ph; p++) {
         // descriptors live in shared memory: phase p's arrived by a bulk
         // copy issued at the start of phase p-1, and phase p+1's is issued
@@ -1036,7 +1142,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a)
         }
         const int kind = ph.kind;
         if (kind == PH_GEMV) {
-            mega_gemv(a, ph, S, ring_s, p, ph.next_attn ? &ph_s[(p + 1) & 1] : nullptr, HD);
+            mega_gemv(a, ph, S, rpos, p, ph.next_attn ? &ph_s[(p + 1) & 1] : nullptr, HD);
         } else if (kind == PH_ATTN) {
             mega_attention<HD, NREP>(a, ph, S, att_sb, merges, p);
         } else {

@@ -274,6 +274,10 @@ int ecu_read_geom(const ecu_model *m, EcuGeom *g, char *err, size_t errlen)
         ecu_set_error(err, errlen, "n_embd %d is not divisible by n_head %d", g->n_embd, g->n_head);
         return -1;
     }
+    if (g->n_embd > 32768) {      // the RMSNorm kernels' partial buffers (RMS_MAX_W warps of 128)
+        ecu_set_error(err, errlen, "n_embd %d above the supported 32768", g->n_embd);
+        return -1;
+    }
     g->head_dim = g->n_embd / g->n_head;
     if (g->n_head_kv <= 0 || g->n_head % g->n_head_kv) {
         ecu_set_error(err, errlen, "n_head %d is not divisible by n_head_kv %d", g->n_head, g->n_head_kv);

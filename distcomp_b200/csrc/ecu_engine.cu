@@ -951,15 +951,15 @@ static int mega_setup(ecu_ctx *c)
     }
     if (ph.size() >= 4095) return no("more phases than the tagged vectors' epochs count");
     for (size_t i = 0; i + 1 < ph.size(); i++) ph[i].next_attn = ph[i + 1].kind == PH_ATTN ? 1 : 0;
-    // row partials of a whole phase (Q4_0 phases keep 8 per row and k-group
+    // row partials of a whole phase (Q4_0 phases keep 4 per row and k-group
     // when they fit); attention keeps its position groups' partials there
-    const char *r8 = getenv("ECU_MEGA_RED8");
-    const bool use_red8 = !(r8 && r8[0] == '0');
+    const char *r4 = getenv("ECU_MEGA_RED4");
+    const bool use_red4 = !(r4 && r4[0] == '0');
     int red = MEGA_NCW * (hd + 4);
     for (auto &p : ph)
         if (p.kind == PH_GEMV) {
-            p.red8 = (use_red8 && p.fmt == 4 && p.rpc * (p.nkg * 8 + 1) <= MEGA_RED8_MAX) ? 1 : 0;
-            red = std::max(red, p.red8 ? p.rpc * (p.nkg * 8 + 1) : p.rpc * p.nkg);
+            p.red4 = (use_red4 && p.fmt == 4 && p.rpc * (p.nkg * 4 + 1) <= MEGA_RED4_MAX) ? 1 : 0;
+            red = std::max(red, p.red4 ? p.rpc * (p.nkg * 4 + 1) : p.rpc * p.nkg);
             if (p.epi == EPI_ADD && p.rpc > MEGA_THREADS) return no("residual rows per CTA above the thread count");
         }
     const size_t smem = mega_smem_total(red, (unsigned)nst * stage_bytes, (unsigned)un);

@@ -32,12 +32,12 @@
 
 #define MEGA_NCW 16                      // warps (all of them consume the ring)
 #define MEGA_THREADS (32 * MEGA_NCW)
-#define MEGA_RING_BYTES (111 * 1024)    // default weight ring, split into nst stages
-#define MEGA_ATT_SUB 32                  // K/V rows per buffer (4 buffers: K and V of two halves)
+#define MEGA_RING_BYTES (128 * 1024)    // default weight ring, split into nst stages
+#define MEGA_ATT_SUB 24                  // K/V rows per buffer (4 buffers: K and V of two halves)
 #define MEGA_MAX_STAGES 8
 #define MEGA_MAX_NB 512                  // input blocks of a GEMV (n_in <= 16384)
 #define MEGA_MAX_SPLIT 64                // position splits per KV head
-#define MEGA_RED8_MAX 6600               // floats of 8-lane row partials a GEMV phase may keep
+#define MEGA_RED4_MAX 6600               // floats of 4-lane row partials a GEMV phase may keep
 
 enum MegaKind : int { PH_EMBED = 0, PH_GEMV = 1, PH_ATTN = 2 };
 
@@ -54,7 +54,7 @@ struct MegaPhase {
     int            sr;         // rows per ring stage
     int            nkg;        // n_in / 1024
     int            rowpar;     // consumer warps per k-group
-    int            red8;       // row partials kept per 8-lane group (8 per row and k-group)
+    int            red4;       // row partials kept per lane pair of an 8-lane group (4 per row and k-group)
     const float   *x;
     const float   *norm_w;
     float         *y;
@@ -428,9 +428,12 @@ __device__ __forceinline__ float warp_sum4_part(float v0, float v1, float v2, fl
     return c + __shfl_xor_sync(0xffffffffu, dd, 8);
 }
 
-__device__ __forceinline__ float sum8_tree(const float *p)
+// The last two levels of warp_sum4 over the four pair sums q_j = p_j + p_{j+4}
+// (j < 4) of an 8-lane group: ((p0+p4)+(p2+p6)) + ((p1+p5)+(p3+p7)), the
+// value warp_sum4's last three levels give.
+__device__ __forceinline__ float sum4_tree(const float *q)
 {
-    return ((p[0] + p[4]) + (p[2] + p[6])) + ((p[1] + p[5]) + (p[3] + p[7]));
+    return (q[0] + q[2]) + (q[1] + q[3]);
 }
 
 // block_dot for four rows (row0 + k*stride) at once: all loads first, then
@@ -481,11 +484,11 @@ __device__ __forceinline__ void block_dot4(const uint8_t *row0, size_t stride, i
 
 // Rows [0, rows) of one ring stage against this lane's block column: warp
 // (g, rp) takes rows rp, rp + rowpar, ... four at a time.  Row partials of
-// k-group g land in red[row * nkg + g], or with RED8 (the last three levels
-// of the warp reduction left to the epilogue's sum8_tree) in
-// red[row * (8 * nkg + 1) + 8 * g + lane % 8]: the odd row stride keeps the
+// k-group g land in red[row * nkg + g], or with RED4 (the last two levels of
+// the warp reduction left to the epilogue's sum4_tree) in
+// red[row * (4 * nkg + 1) + 4 * g + lane % 4]: the odd row stride keeps the
 // epilogue, one thread per row, free of bank conflicts.
-template <int FMT, bool RED8>
+template <int FMT, bool RED4>
 __device__ __forceinline__ void mega_stage_rows(const uint8_t *stage, int rows, unsigned row_bytes, int nb,
                                                 int b, int g, int rp, int rowpar, int nkg, int lane,
                                                 const int (&xw)[3][8], const int (&off)[3], float sxs,
@@ -504,9 +507,10 @@ __device__ __forceinline__ void mega_stage_rows(const uint8_t *stage, int rows, 
             }
         }
         const int k = (lane >> 3) & 3, ii = i0 + k * rowpar;
-        if (RED8) {
+        if (RED4) {
             const float part = warp_sum4_part(v[0], v[1], v[2], v[3], lane);
-            if (ii < rows) red[ii * (8 * nkg + 1) + 8 * g + (lane & 7)] = part;
+            const float pair = part + __shfl_xor_sync(0xffffffffu, part, 4);
+            if (ii < rows && (lane & 4) == 0) red[ii * (4 * nkg + 1) + 4 * g + (lane & 3)] = pair;
         } else {
             const float sum = warp_sum4(v[0], v[1], v[2], v[3], lane);
             if ((lane & 7) == 0 && ii < rows) red[ii * nkg + g] = sum;
@@ -515,11 +519,11 @@ __device__ __forceinline__ void mega_stage_rows(const uint8_t *stage, int rows, 
 }
 
 // Sum of row r's k-group partials, in k-group order.
-__device__ __forceinline__ float row_total(const float *red, int r, int nkg, bool red8)
+__device__ __forceinline__ float row_total(const float *red, int r, int nkg, bool red4)
 {
     float acc = 0.0f;
-    if (red8)
-        for (int q = 0; q < nkg; q++) acc += sum8_tree(red + (size_t)r * (8 * nkg + 1) + 8 * q);
+    if (red4)
+        for (int q = 0; q < nkg; q++) acc += sum4_tree(red + (size_t)r * (4 * nkg + 1) + 4 * q);
     else
         for (int q = 0; q < nkg; q++) acc += red[r * nkg + q];
     return acc;
@@ -604,7 +608,7 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
     unsigned long long *det = (a.phase_detail && blockIdx.x == 0 && threadIdx.x == 0)
                                   ? a.phase_detail + (size_t)p_idx * 4 : nullptr;
     unsigned long long waited = 0;
-    const bool q4 = ph.fmt == 4, red8 = q4 && ph.red8;
+    const bool q4 = ph.fmt == 4, red4 = q4 && ph.red4;
     const int nct = MEGA_NCW * 32, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nkg = ph.nkg, rowpar = ph.rowpar, nb = ph.n_in / 32;
     const int r0 = blockIdx.x * ph.rpc;
@@ -676,9 +680,9 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
         const uint8_t *stage = S.ring + (size_t)slot * a.stage_bytes;
         const int      rows = min(sr, nrows - i);
         if (active) {
-            if (q4 && red8)
+            if (q4 && red4)
                 mega_stage_rows<4, true>(stage, rows, row_bytes, nb, b, g, rp, rowpar, nkg, lane, xw, off, sxs,
-                                         S.red + (size_t)i * (8 * nkg + 1));
+                                         S.red + (size_t)i * (4 * nkg + 1));
             else if (q4)
                 mega_stage_rows<4, false>(stage, rows, row_bytes, nb, b, g, rp, rowpar, nkg, lane, xw, off, sxs,
                                           S.red + (size_t)i * nkg);
@@ -713,7 +717,7 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
     const unsigned eout = ll_epoch(S.launch, p_idx);
     if (epi == EPI_SWIGLU) {
         for (int j = tid; j < nrows / 2; j += nct) {
-            const float gs = row_total(S.red, 2 * j, nkg, red8), us = row_total(S.red, 2 * j + 1, nkg, red8);
+            const float gs = row_total(S.red, 2 * j, nkg, red4), us = row_total(S.red, 2 * j + 1, nkg, red4);
             ll_put(ph.y_ll + r0 / 2 + j, silu_mul(gs, us), eout);
         }
         if (det) det[2] = clock64();
@@ -721,7 +725,7 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
     }
     ArgBest best{-INFINITY, -1};
     for (int r = tid; r < nrows; r += nct) {
-        const float acc = row_total(S.red, r, nkg, red8);
+        const float acc = row_total(S.red, r, nkg, red4);
         if (epi == EPI_ADD) {
             const float out = yprev + acc;         // r == tid: nrows <= MEGA_THREADS
             ll_put(ph.y_ll + r0 + r, out, eout);

@@ -82,6 +82,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *s
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     for (;;) {
+#pragma unroll 1
         for (int i = 0; i < 64; i++)
             if (mbar_try_wait(bar, parity)) return true;
         const uint64_t dt = globaltimer_ns() - t0;
@@ -102,6 +103,7 @@ __device__ __forceinline__ bool mbar_drain(uint64_t *bar, uint32_t parity, uint6
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     for (;;) {
+#pragma unroll 1
         for (int i = 0; i < 64; i++)
             if (mbar_try_wait(bar, parity)) return true;
         if (globaltimer_ns() - t0 > limit_ns) return false;

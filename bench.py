@@ -56,6 +56,9 @@ def parse():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--seqs", type=int, default=8,
                     help="N > 1: independent sequences interleaved through the layer pipeline")
+    ap.add_argument("--mode", choices=["pp", "tp"], default="pp",
+                    help="N > 1: layer pipeline with interleaved sequences (pp) or batch-1 tensor "
+                         "parallelism (tp)")
     ap.add_argument("--split", choices=["bytes", "ref"], default="bytes",
                     help="N > 1: layer ranges balancing bytes per stage (head on the last GPU) or "
                          "shard.c's ceil(layers/stages) rule")
@@ -197,6 +200,9 @@ def our_arm(args, rank, world, local):
     from distcomp_b200 import engine as E
     from distcomp_b200 import synth
 
+    if world > 1 and args.mode == "tp":
+        from distcomp_b200 import tensor_parallel
+        return tensor_parallel.bench_main(args, rank, world, local, sys.modules[__name__])
     if world > 1:
         from distcomp_b200 import pipeline
         return pipeline.bench_main(args, rank, world, local, sys.modules[__name__])

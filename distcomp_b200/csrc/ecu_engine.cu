@@ -365,10 +365,21 @@ struct SharedAllocs {
     }
 };
 
+// Tensor-parallel slice of a FULL context: rank `rank` of `world` owns
+// query heads [rank*nh, ..), KV heads [rank*nkv, ..), rows [rank*ne, ..) of
+// attn_output and ffn_down, FFN channels [rank*ff, ..) and vocabulary rows
+// [v0, v1); every projection keeps its whole input (no split reductions).
+struct TpSlice {
+    int rank = 0, world = 1;
+    int nh = 0, nkv = 0, ne = 0, ff = 0, v0 = 0, v1 = 0;
+};
+
 struct ecu_ctx {
     int         device = 0, sms = 148;
     int         stage = 0, first = 0, last = 0, pos = 0;
     EcuGeom     g;
+    TpSlice     tp;
+    std::vector<void *> tp_peers;         // IPC mappings of the other ranks' tagged vectors
     cudaStream_t stream = nullptr;
     bool        pdl = true, use_graph = true;
     std::vector<void *> allocs;           // this context's own buffers
@@ -460,15 +471,16 @@ static bool zero_rule(int t, int n_in)
     return !dq_supported(t);
 }
 
-// Upload `rows` rows of tensor `src` (n_in inputs each) into device matrix
-// `m` at rows row0, row0+rstride, ...  `stage` is a device staging buffer.
+// Upload rows [src_row0, src_row0 + rows) of tensor `src` (n_in inputs
+// each) into device matrix `m` at rows row0, row0+rstride, ...  `stage` is a
+// device staging buffer.
 static int upload_rows(ecu_ctx *c, const EcuTensor *src, int n_in, int rows, DevMat &m, int row0,
-                       int rstride, uint8_t *stage)
+                       int rstride, uint8_t *stage, size_t src_row0 = 0)
 {
     if (m.zero) return 0;
     const size_t src_row = (size_t)ecu_type_nbytes(src->type, (size_t)n_in);
     const size_t nbytes = src_row * (size_t)rows;
-    CK(cudaMemcpyAsync(stage, src->data, nbytes, cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(stage, src->data + src_row0 * src_row, nbytes, cudaMemcpyHostToDevice, c->stream));
     const int nb = n_in / 32;
     const int grid = 4 * c->sms, blk = 256;
     uint8_t  *dst = const_cast<uint8_t *>(m.data);
@@ -524,6 +536,8 @@ static void ctx_free(ecu_ctx *c)
     if (!c) return;
     if (c->device >= 0) cudaSetDevice(c->device);
     if (c->graph) cudaGraphExecDestroy(c->graph);
+    for (void *p : c->tp_peers)
+        if (p) cudaIpcCloseMemHandle(p);
     for (void *p : c->allocs) cudaFree(p);
     if (c->h_st) cudaFreeHost(c->h_st);
     if (c->h_state) cudaFreeHost(c->h_state);
@@ -829,7 +843,10 @@ static int mega_setup(ecu_ctx *c)
     if ((c->stage != ECU_STAGE_FULL && c->stage != ECU_STAGE_LAYERS) || c->layers.empty())
         return no("stage without layers");
     const EcuGeom &g = c->g;
-    const int hd = g.head_dim, qdim = g.n_head * hd, kvdim = g.n_head_kv * hd;
+    const TpSlice &tp = c->tp;
+    // this rank's query and KV heads (all of them without tensor parallelism)
+    const int hd = g.head_dim, qdim = g.n_head * hd, qd_l = tp.nh * hd, kvd_l = tp.nkv * hd;
+    const bool bcast = tp.world > 1;          // outputs every rank reads go to every rank
     MegaFn fn = mega_lookup(hd, g.n_rep);
     if (!fn) return no("head_dim / query heads per KV head not instantiated");
     for (auto &ly : c->layers)
@@ -866,7 +883,7 @@ static int mega_setup(ecu_ctx *c)
         for (const DevMat *m : {&ly.qkv[0], &ly.o, &ly.gu, &ly.d})
             un = std::max(un, (size_t)m->n_in / 32 * 28 * sizeof(int));
     if (full) un = std::max(un, (size_t)c->out.n_in / 32 * 28 * sizeof(int));
-    int n_split = std::min(MEGA_MAX_SPLIT, grid / g.n_head_kv);
+    int n_split = std::min(MEGA_MAX_SPLIT, grid / tp.nkv);
     n_split = std::min(n_split, (int)(un / ((size_t)g.n_rep * (hd + 4) * sizeof(float))));
     n_split = std::max(1, std::min(n_split, g.n_ctx));
 
@@ -882,14 +899,17 @@ static int mega_setup(ecu_ctx *c)
     float *xn_tmp = full ? c->dalloc<float>((size_t)g.n_embd + 4) : nullptr;
     // tagged vectors: residual stream, fused Q/K/V, attention output, SwiGLU
     // output; 4-word padded so every vector starts 32-byte aligned
+    // (+ the argmax exchange of tensor-parallel ranks: a value and an index
+    // word per rank); the same layout on every rank
     auto pad4 = [](size_t n) { return (n + 7) & ~(size_t)3; };
-    const size_t w_x = pad4(g.n_embd), w_qkv = pad4((size_t)qdim + 2 * kvdim), w_att = pad4(qdim),
-                 w_h = pad4(g.n_ff);
-    c->mega_ll_words = w_x + w_qkv + w_att + w_h;
+    const size_t w_x = pad4(g.n_embd), w_qkv = pad4((size_t)qd_l + 2 * kvd_l), w_att = pad4(qdim),
+                 w_h = pad4(g.n_ff), w_arg = pad4(2 * ECU_MAX_TP);
+    c->mega_ll_words = w_x + w_qkv + w_att + w_h + w_arg;
     c->mega_ll = c->dalloc<unsigned long long>(c->mega_ll_words);
     if (!c->mega_ll) return -1;
     CK(cudaMemset(c->mega_ll, 0, c->mega_ll_words * sizeof(unsigned long long)));
-    unsigned long long *x_ll = c->mega_ll, *qkv_ll = x_ll + w_x, *att_ll = qkv_ll + w_qkv, *h_ll = att_ll + w_att;
+    unsigned long long *x_ll = c->mega_ll, *qkv_ll = x_ll + w_x, *att_ll = qkv_ll + w_qkv, *h_ll = att_ll + w_att,
+                       *arg_ll = h_ll + w_h;
     // x_w: the phase that last wrote the residual stream (-1: the plain
     // input state of a LAYERS stage)
     int x_w = -1;
@@ -900,7 +920,7 @@ static int mega_setup(ecu_ctx *c)
         x_w = (int)ph.size();
         add(p, "embed", 8.0 * g.n_embd + (double)ecu_type_nbytes(c->emb.type, (size_t)g.n_embd));
     }
-    const size_t plane = (size_t)g.n_head_kv * g.n_ctx * hd;
+    const size_t plane = (size_t)tp.nkv * g.n_ctx * hd;
     for (size_t li = 0; li < c->layers.size(); li++) {
         LayerDev &ly = c->layers[li];
         const bool last = li + 1 == c->layers.size();
@@ -918,7 +938,8 @@ static int mega_setup(ecu_ctx *c)
         at.bk = ly.bk;
         at.bv = ly.bv;
         at.in_ep = p_qkv;
-        at.y_ll = att_ll;
+        at.y_ll = att_ll + (size_t)tp.rank * qd_l;   // this rank's heads of the whole vector
+        at.bcast = bcast;
         const int p_at = (int)ph.size();
         add(at, "attention", -1.0);                 // position dependent: filled in by the profile
         MegaPhase o = mega_gemv_phase(ly.o, grid, stage_bytes, 0, EPI_ADD, c->att, nullptr, c->state, nullptr);
@@ -926,12 +947,16 @@ static int mega_setup(ecu_ctx *c)
         o.x_ll = att_ll;
         o.y_ep = x_w;
         o.y_ll = x_ll;
+        o.out_base = tp.rank * tp.ne;
+        o.bcast = bcast;
         x_w = (int)ph.size();
         add(o, "gemv_o", gemv_bytes(ly.o, EPI_ADD));
         MegaPhase gu = mega_gemv_phase(ly.gu, grid, stage_bytes, 1, EPI_SWIGLU, c->state, ly.ffn_norm, c->h, nullptr);
         gu.in_ep = x_w;
         gu.x_ll = x_ll;
         gu.y_ll = h_ll;
+        gu.out_base = tp.rank * tp.ff;
+        gu.bcast = bcast;
         const int p_gu = (int)ph.size();
         add(gu, "gemv_gate_up", gemv_bytes(ly.gu, EPI_SWIGLU));
         MegaPhase d = mega_gemv_phase(ly.d, grid, stage_bytes, 0, EPI_ADD, c->h, nullptr, c->state, nullptr);
@@ -939,6 +964,8 @@ static int mega_setup(ecu_ctx *c)
         d.x_ll = h_ll;
         d.y_ep = x_w;
         d.y_ll = x_ll;
+        d.out_base = tp.rank * tp.ne;
+        d.bcast = bcast;
         d.out_plain = (!full && last) ? 1 : 0;     // a LAYERS stage's output state
         x_w = (int)ph.size();
         add(d, "gemv_down", gemv_bytes(ly.d, EPI_ADD));
@@ -982,7 +1009,7 @@ static int mega_setup(ecu_ctx *c)
         return no("no SM can hold one CTA of the persistent kernel");
     }
     MegaPhase *d_ph = c->dalloc<MegaPhase>(ph.size());
-    float *apart = c->dalloc<float>((size_t)g.n_head_kv * n_split * g.n_rep * (hd + 4));
+    float *apart = c->dalloc<float>((size_t)tp.nkv * n_split * g.n_rep * (hd + 4));
     float *pval = c->dalloc<float>((size_t)grid);
     int *pidx = c->dalloc<int>((size_t)grid);
     unsigned *ctr = c->dalloc<unsigned>(4 + (size_t)g.n_head_kv);
@@ -1018,8 +1045,14 @@ static int mega_setup(ecu_ctx *c)
     a.advance_pos = full ? 1 : 0;
     a.layers_advance = full ? 0 : 1;
     a.n_embd = g.n_embd;
-    a.n_head = g.n_head;
-    a.n_kv = g.n_head_kv;
+    a.n_head = tp.nh;
+    a.n_kv = tp.nkv;
+    a.tp_rank = tp.rank;
+    a.tp_world = tp.world;
+    a.ll_block = c->mega_ll;
+    for (int k = 0; k < ECU_MAX_TP; k++) a.peer[k] = k == tp.rank ? c->mega_ll : nullptr;
+    a.arg_ll = arg_ll;
+    a.vocab_base = tp.v0;
     a.n_ctx = g.n_ctx;
     a.n_split = n_split;
     a.red_floats = red;
@@ -1041,6 +1074,10 @@ static int mega_setup(ecu_ctx *c)
 // One step: a cooperative launch of the whole-step kernel on s.
 static int mega_launch(ecu_ctx *c, cudaStream_t s, unsigned long long *phase_ns, unsigned long long *detail)
 {
+    if (c->tp.world > 1 && (int)c->tp_peers.size() != c->tp.world - 1) {
+        ecu_set_error(nullptr, 0, "tensor-parallel rank %d is not connected to its peers (ecu_tp_connect)", c->tp.rank);
+        return -1;
+    }
     MegaArgs a = c->margs;
     a.phase_ns = phase_ns;
     a.phase_clk = phase_ns ? phase_ns + a.n_ph + 1 : nullptr;   // the profile buffer's second row
@@ -1336,7 +1373,9 @@ static const char *alloc_buffers(ecu_ctx *c, bool layers, bool head)
 {
     const EcuGeom &g = c->g;
     const int wide = g.n_ff > g.n_embd ? g.n_ff : g.n_embd;
-    const int hd = g.head_dim, qd = g.n_head * hd, kvd = g.n_head_kv * hd;
+    const int hd = g.head_dim, qd = g.n_head * hd;
+    // this rank's query / KV heads (all of them without tensor parallelism)
+    const int qd_l = c->tp.nh * hd, kvd_l = c->tp.nkv * hd;
     c->state = c->dalloc<float>((size_t)g.n_embd + 4);
     c->st = c->dalloc<StepState>(1);
     c->tok_hist = c->dalloc<int>((size_t)g.n_ctx + 1);
@@ -1356,17 +1395,17 @@ static const char *alloc_buffers(ecu_ctx *c, bool layers, bool head)
         return "pinned host staging";
     memset(c->h_st, 0, sizeof(StepState) * (size_t)c->n_hslots);
     if (head) {
-        c->logits = c->dalloc<float>((size_t)g.n_vocab + 4);
+        c->logits = c->dalloc<float>((size_t)(c->tp.v1 - c->tp.v0) + 4);
         if (!c->logits) return "logits";
     }
     if (layers) {
         const size_t nl = (size_t)(c->last - c->first + 1);
-        c->qkv = c->dalloc<float>((size_t)qd + 2 * kvd + 4);
+        c->qkv = c->dalloc<float>((size_t)qd_l + 2 * kvd_l + 4);
         c->att = c->dalloc<float>((size_t)qd + 4);
         c->h = c->dalloc<float>((size_t)g.n_ff + 4);
         c->gtmp = c->dalloc<float>((size_t)g.n_ff + 4);
         c->utmp = c->dalloc<float>((size_t)g.n_ff + 4);
-        const size_t plane = (size_t)g.n_head_kv * g.n_ctx * hd;
+        const size_t plane = (size_t)c->tp.nkv * g.n_ctx * hd;
         c->kc = c->dalloc<float>(plane * nl);
         c->vc = c->dalloc<float>(plane * nl);
         if (!c->qkv || !c->att || !c->h || !c->gtmp || !c->utmp || !c->kc || !c->vc)
@@ -1376,20 +1415,29 @@ static const char *alloc_buffers(ecu_ctx *c, bool layers, bool head)
 }
 
 static int ctx_open_impl(ecu_ctx **out, const ecu_model *m, int stage, int first, int last, int n_ctx,
-                         int device, char *err, size_t errlen);
+                         int device, int tp_rank, int tp_world, char *err, size_t errlen);
 
 int ecu_ctx_open(ecu_ctx **out, const ecu_model *m, int stage, int first, int last, int n_ctx,
                  int device, char *err, size_t errlen)
 {
     if (err && errlen) err[0] = '\0';
-    const int rc = ctx_open_impl(out, m, stage, first, last, n_ctx, device, err, errlen);
+    const int rc = ctx_open_impl(out, m, stage, first, last, n_ctx, device, 0, 1, err, errlen);
     // CUDA failures deep in the upload only set the thread's last error
     if (rc != 0 && err && errlen && !err[0]) snprintf(err, errlen, "%s", ecu_get_error());
     return rc;
 }
 
+int ecu_ctx_open_tp(ecu_ctx **out, const ecu_model *m, int n_ctx, int device, int tp_rank, int tp_world,
+                    char *err, size_t errlen)
+{
+    if (err && errlen) err[0] = '\0';
+    const int rc = ctx_open_impl(out, m, ECU_STAGE_FULL, 0, 0, n_ctx, device, tp_rank, tp_world, err, errlen);
+    if (rc != 0 && err && errlen && !err[0]) snprintf(err, errlen, "%s", ecu_get_error());
+    return rc;
+}
+
 static int ctx_open_impl(ecu_ctx **out, const ecu_model *m, int stage, int first, int last, int n_ctx,
-                         int device, char *err, size_t errlen)
+                         int device, int tp_rank, int tp_world, char *err, size_t errlen)
 {
     if (!out || !m) { ecu_set_error(err, errlen, "null argument"); return -1; }
     *out = nullptr;
@@ -1417,6 +1465,28 @@ static int ctx_open_impl(ecu_ctx **out, const ecu_model *m, int stage, int first
         }
     }
     if (st.out && check_shape(st.out, g.n_embd, g.n_vocab, err, errlen)) return -1;
+    TpSlice tp;
+    tp.rank = tp_rank;
+    tp.world = tp_world;
+    if (tp_world < 1 || tp_world > ECU_MAX_TP || tp_rank < 0 || tp_rank >= tp_world) {
+        ecu_set_error(err, errlen, "tensor-parallel rank %d of %d", tp_rank, tp_world);
+        return -1;
+    }
+    if (tp_world > 1 && (stage != ECU_STAGE_FULL || g.n_head_kv % tp_world || g.n_ff % tp_world ||
+                         g.n_embd % tp_world)) {
+        ecu_set_error(err, errlen, "tensor parallelism over %d ranks needs a FULL stage with KV heads, FFN "
+                      "width and n_embd divisible by it", tp_world);
+        return -1;
+    }
+    tp.nh = g.n_head / tp_world;
+    tp.nkv = g.n_head_kv / tp_world;
+    tp.ne = g.n_embd / tp_world;
+    tp.ff = g.n_ff / tp_world;
+    {
+        const int vs = (g.n_vocab + tp_world - 1) / tp_world;
+        tp.v0 = std::min(g.n_vocab, tp_rank * vs);
+        tp.v1 = std::min(g.n_vocab, tp.v0 + vs);
+    }
     if (st.emb && (st.emb->dims[0] != (uint64_t)g.n_embd)) {
         ecu_set_error(err, errlen, "token_embd.weight has %llu inputs, n_embd is %d",
                       (unsigned long long)st.emb->dims[0], g.n_embd);
@@ -1437,6 +1507,7 @@ static int ctx_open_impl(ecu_ctx **out, const ecu_model *m, int stage, int first
 
     std::unique_ptr<ecu_ctx, void (*)(ecu_ctx *)> c(new ecu_ctx(), ctx_free);
     c->device = device;
+    c->tp = tp;
     c->sms = num_sms(device);
     c->stage = stage;
     c->first = first;
@@ -1479,13 +1550,15 @@ static int ctx_open_impl(ecu_ctx **out, const ecu_model *m, int stage, int first
         if (upload_rows(c.get(), st.emb, g.n_embd, g.n_vocab, c->emb, 0, 1, stage_buf)) return -1;
         c->srcs.push_back({"token_embd.weight", c->emb, 0, 1, (size_t)g.n_embd * g.n_vocab, g.n_embd});
     }
+    const bool whole = tp.world == 1;    // tensor-parallel ranks hold row slices
     if (st.out) {
-        c->out = make_mat(c.get(), (int)st.out->type, g.n_embd, g.n_vocab, true);
+        const int nv = tp.v1 - tp.v0;
+        c->out = make_mat(c.get(), (int)st.out->type, g.n_embd, nv, true);
         if (!c->out.zero && !c->out.data) return fail_oom("output");
-        if (upload_rows(c.get(), st.out, g.n_embd, g.n_vocab, c->out, 0, 1, stage_buf)) return -1;
+        if (upload_rows(c.get(), st.out, g.n_embd, nv, c->out, 0, 1, stage_buf, (size_t)tp.v0)) return -1;
         c->out_norm = upload_vec(c.get(), st.out_norm, (size_t)g.n_embd, stage_buf);
         if (!c->out_norm) return fail_oom("head buffers");
-        if (st.out->name == "output.weight" || !st.emb)
+        if (whole && (st.out->name == "output.weight" || !st.emb))
             c->srcs.push_back({st.out->name, c->out, 0, 1, (size_t)g.n_embd * g.n_vocab, g.n_embd});
     }
     if (!st.layers.empty()) {
@@ -1518,21 +1591,30 @@ static int ctx_open_impl(ecu_ctx **out, const ecu_model *m, int stage, int first
             LayerDev   &ly = c->layers[i];
             char        nm[160];
             const int   li = first + (int)i;
-            // Q/K/V: fused when all three share a fast layout
+            // Q/K/V: fused when all three share a fast layout (a tensor-
+            // parallel rank: its heads' rows of each)
             const int lq = choose_layout((int)l.q->type, g.n_embd);
             const bool fuse_qkv = lq != LAY_RAW && l.k->type == l.q->type && l.v->type == l.q->type;
+            const int  qd_l = tp.nh * hd, kvd_l = tp.nkv * hd;
+            if (!fuse_qkv && !whole) {
+                ecu_set_error(err, errlen, "tensor parallelism needs Q/K/V of one fast type");
+                return -1;
+            }
             if (fuse_qkv) {
-                DevMat mq = make_mat(c.get(), (int)l.q->type, g.n_embd, qd + 2 * kvd, true);
+                DevMat mq = make_mat(c.get(), (int)l.q->type, g.n_embd, qd_l + 2 * kvd_l, true);
                 if (!mq.data) return fail_oom("attn_qkv");
-                if (upload_rows(c.get(), l.q, g.n_embd, qd, mq, 0, 1, stage_buf) ||
-                    upload_rows(c.get(), l.k, g.n_embd, kvd, mq, qd, 1, stage_buf) ||
-                    upload_rows(c.get(), l.v, g.n_embd, kvd, mq, qd + kvd, 1, stage_buf))
+                if (upload_rows(c.get(), l.q, g.n_embd, qd_l, mq, 0, 1, stage_buf, (size_t)tp.rank * qd_l) ||
+                    upload_rows(c.get(), l.k, g.n_embd, kvd_l, mq, qd_l, 1, stage_buf, (size_t)tp.rank * kvd_l) ||
+                    upload_rows(c.get(), l.v, g.n_embd, kvd_l, mq, qd_l + kvd_l, 1, stage_buf,
+                                (size_t)tp.rank * kvd_l))
                     return -1;
                 ly.qkv.push_back(mq);
                 ly.qkv_off.push_back(0);
-                snprintf(nm, sizeof nm, "blk.%d.attn_q.weight", li); c->srcs.push_back({nm, mq, 0, 1, (size_t)g.n_embd * qd, g.n_embd});
-                snprintf(nm, sizeof nm, "blk.%d.attn_k.weight", li); c->srcs.push_back({nm, mq, qd, 1, (size_t)g.n_embd * kvd, g.n_embd});
-                snprintf(nm, sizeof nm, "blk.%d.attn_v.weight", li); c->srcs.push_back({nm, mq, qd + kvd, 1, (size_t)g.n_embd * kvd, g.n_embd});
+                if (whole) {
+                    snprintf(nm, sizeof nm, "blk.%d.attn_q.weight", li); c->srcs.push_back({nm, mq, 0, 1, (size_t)g.n_embd * qd, g.n_embd});
+                    snprintf(nm, sizeof nm, "blk.%d.attn_k.weight", li); c->srcs.push_back({nm, mq, qd, 1, (size_t)g.n_embd * kvd, g.n_embd});
+                    snprintf(nm, sizeof nm, "blk.%d.attn_v.weight", li); c->srcs.push_back({nm, mq, qd + kvd, 1, (size_t)g.n_embd * kvd, g.n_embd});
+                }
             } else {
                 const EcuTensor *ts[3] = {l.q, l.k, l.v};
                 const int        rows[3] = {qd, kvd, kvd}, offs[3] = {0, qd, qd + kvd};
@@ -1547,21 +1629,27 @@ static int ctx_open_impl(ecu_ctx **out, const ecu_model *m, int stage, int first
                     c->srcs.push_back({nm, mm, 0, 1, (size_t)g.n_embd * rows[k], g.n_embd});
                 }
             }
-            ly.o = make_mat(c.get(), (int)l.o->type, qd, g.n_embd, true);
+            ly.o = make_mat(c.get(), (int)l.o->type, qd, tp.ne, true);
             if (!ly.o.zero && !ly.o.data) return fail_oom("attn_output");
-            if (upload_rows(c.get(), l.o, qd, g.n_embd, ly.o, 0, 1, stage_buf)) return -1;
+            if (upload_rows(c.get(), l.o, qd, tp.ne, ly.o, 0, 1, stage_buf, (size_t)tp.rank * tp.ne)) return -1;
             snprintf(nm, sizeof nm, "blk.%d.attn_output.weight", li);
-            c->srcs.push_back({nm, ly.o, 0, 1, (size_t)qd * g.n_embd, qd});
+            if (whole) c->srcs.push_back({nm, ly.o, 0, 1, (size_t)qd * g.n_embd, qd});
             const int lg = choose_layout((int)l.g->type, g.n_embd);
             ly.gu_fused = lg != LAY_RAW && l.u->type == l.g->type;
+            if (!ly.gu_fused && !whole) {
+                ecu_set_error(err, errlen, "tensor parallelism needs gate/up of one fast type");
+                return -1;
+            }
             if (ly.gu_fused) {
-                ly.gu = make_mat(c.get(), (int)l.g->type, g.n_embd, 2 * g.n_ff, true);
+                ly.gu = make_mat(c.get(), (int)l.g->type, g.n_embd, 2 * tp.ff, true);
                 if (!ly.gu.data) return fail_oom("ffn_gate/up");
-                if (upload_rows(c.get(), l.g, g.n_embd, g.n_ff, ly.gu, 0, 2, stage_buf) ||
-                    upload_rows(c.get(), l.u, g.n_embd, g.n_ff, ly.gu, 1, 2, stage_buf))
+                if (upload_rows(c.get(), l.g, g.n_embd, tp.ff, ly.gu, 0, 2, stage_buf, (size_t)tp.rank * tp.ff) ||
+                    upload_rows(c.get(), l.u, g.n_embd, tp.ff, ly.gu, 1, 2, stage_buf, (size_t)tp.rank * tp.ff))
                     return -1;
-                snprintf(nm, sizeof nm, "blk.%d.ffn_gate.weight", li); c->srcs.push_back({nm, ly.gu, 0, 2, (size_t)g.n_embd * g.n_ff, g.n_embd});
-                snprintf(nm, sizeof nm, "blk.%d.ffn_up.weight", li); c->srcs.push_back({nm, ly.gu, 1, 2, (size_t)g.n_embd * g.n_ff, g.n_embd});
+                if (whole) {
+                    snprintf(nm, sizeof nm, "blk.%d.ffn_gate.weight", li); c->srcs.push_back({nm, ly.gu, 0, 2, (size_t)g.n_embd * g.n_ff, g.n_embd});
+                    snprintf(nm, sizeof nm, "blk.%d.ffn_up.weight", li); c->srcs.push_back({nm, ly.gu, 1, 2, (size_t)g.n_embd * g.n_ff, g.n_embd});
+                }
             } else {
                 ly.g = make_mat(c.get(), (int)l.g->type, g.n_embd, g.n_ff, true);
                 ly.u = make_mat(c.get(), (int)l.u->type, g.n_embd, g.n_ff, true);
@@ -1572,20 +1660,28 @@ static int ctx_open_impl(ecu_ctx **out, const ecu_model *m, int stage, int first
                 snprintf(nm, sizeof nm, "blk.%d.ffn_gate.weight", li); c->srcs.push_back({nm, ly.g, 0, 1, (size_t)g.n_embd * g.n_ff, g.n_embd});
                 snprintf(nm, sizeof nm, "blk.%d.ffn_up.weight", li); c->srcs.push_back({nm, ly.u, 0, 1, (size_t)g.n_embd * g.n_ff, g.n_embd});
             }
-            ly.d = make_mat(c.get(), (int)l.d->type, g.n_ff, g.n_embd, true);
+            ly.d = make_mat(c.get(), (int)l.d->type, g.n_ff, tp.ne, true);
             if (!ly.d.zero && !ly.d.data) return fail_oom("ffn_down");
-            if (upload_rows(c.get(), l.d, g.n_ff, g.n_embd, ly.d, 0, 1, stage_buf)) return -1;
+            if (upload_rows(c.get(), l.d, g.n_ff, tp.ne, ly.d, 0, 1, stage_buf, (size_t)tp.rank * tp.ne)) return -1;
             snprintf(nm, sizeof nm, "blk.%d.ffn_down.weight", li);
-            c->srcs.push_back({nm, ly.d, 0, 1, (size_t)g.n_ff * g.n_embd, g.n_ff});
+            if (whole) c->srcs.push_back({nm, ly.d, 0, 1, (size_t)g.n_ff * g.n_embd, g.n_ff});
             ly.attn_norm = upload_vec(c.get(), l.an, (size_t)g.n_embd, stage_buf);
             ly.ffn_norm = upload_vec(c.get(), l.fn, (size_t)g.n_embd, stage_buf);
+            // biases whole; a tensor-parallel rank points at its heads' part
             if (l.bq) ly.bq = upload_vec(c.get(), l.bq, (size_t)qd, stage_buf);
             if (l.bk) ly.bk = upload_vec(c.get(), l.bk, (size_t)kvd, stage_buf);
             if (l.bv) ly.bv = upload_vec(c.get(), l.bv, (size_t)kvd, stage_buf);
+            if (ly.bq) ly.bq += (size_t)tp.rank * qd_l;
+            if (ly.bk) ly.bk += (size_t)tp.rank * kvd_l;
+            if (ly.bv) ly.bv += (size_t)tp.rank * kvd_l;
             if (!ly.attn_norm || !ly.ffn_norm) return fail_oom("norm weights");
         }
     }
     if (mega_setup(c.get()) != 0) return fail_oom("persistent step buffers");
+    if (!whole && !c->mega) {
+        ecu_set_error(err, errlen, "tensor parallelism runs the persistent step only (%s)", c->path.c_str());
+        return -1;
+    }
     // setup memsets/copies ran on the legacy stream, which does not order
     // against the context's non-blocking stream: finish them all here
     if (cudaDeviceSynchronize() != cudaSuccess || cudaGetLastError() != cudaSuccess) {
@@ -1710,6 +1806,7 @@ int ecu_ctx_fork(ecu_ctx **out, ecu_ctx *base, char *err, size_t errlen)
     if (err && errlen) err[0] = '\0';
     if (!out || !base) { ecu_set_error(err, errlen, "null argument"); return -1; }
     *out = nullptr;
+    if (base->tp.world > 1) { ecu_set_error(err, errlen, "a tensor-parallel context is not forked"); return -1; }
     if (cudaSetDevice(base->device) != cudaSuccess) { ecu_set_error(err, errlen, "cudaSetDevice(%d) failed", base->device); return -1; }
     std::unique_ptr<ecu_ctx, void (*)(ecu_ctx *)> c(new ecu_ctx(), ctx_free);
     c->device = base->device;
@@ -1718,6 +1815,7 @@ int ecu_ctx_fork(ecu_ctx **out, ecu_ctx *base, char *err, size_t errlen)
     c->first = base->first;
     c->last = base->last;
     c->g = base->g;
+    c->tp = base->tp;
     c->pdl = base->pdl;
     c->use_graph = base->use_graph;
     c->shared = base->shared;
@@ -1801,7 +1899,7 @@ int ecu_pick(const ecu_ctx *c)
 
 int ecu_get_logits(const ecu_ctx *c, float *out, size_t n)
 {
-    if (!c || !out || !c->logits || n > (size_t)c->g.n_vocab) return -1;
+    if (!c || !out || !c->logits || n > (size_t)(c->tp.v1 - c->tp.v0)) return -1;
     cudaSetDevice(c->device);
     CK(cudaStreamSynchronize(c->stream));
     CK(cudaMemcpy(out, c->logits, n * sizeof(float), cudaMemcpyDeviceToHost));
@@ -2036,3 +2134,59 @@ int ecu_matvec(unsigned type, const void *w_raw, int n_in, int n_out, const floa
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------ tensor parallel --
+
+int ecu_tp_slice(const ecu_ctx *c, int *out4)
+{
+    if (!c || !out4) return -1;
+    out4[0] = c->tp.rank;
+    out4[1] = c->tp.world;
+    out4[2] = c->tp.v0;
+    out4[3] = c->tp.v1;
+    return 0;
+}
+
+int ecu_tp_handle(ecu_ctx *c, unsigned char *out)
+{
+    if (!c || !out || !c->mega || !c->mega_ll) {
+        ecu_set_error(nullptr, 0, "no persistent step to share");
+        return -1;
+    }
+    cudaSetDevice(c->device);
+    cudaIpcMemHandle_t h;
+    CK(cudaIpcGetMemHandle(&h, c->mega_ll));
+    static_assert(sizeof h == ECU_TP_HANDLE_BYTES, "IPC handle size");
+    memcpy(out, &h, sizeof h);
+    return 0;
+}
+
+int ecu_tp_connect(ecu_ctx *c, const unsigned char *handles)
+{
+    if (!c || !handles || !c->mega || c->tp.world < 2) {
+        ecu_set_error(nullptr, 0, "not a tensor-parallel context");
+        return -1;
+    }
+    if (!c->tp_peers.empty()) {
+        ecu_set_error(nullptr, 0, "tensor-parallel ranks already connected");
+        return -1;
+    }
+    cudaSetDevice(c->device);
+    for (int k = 0; k < c->tp.world; k++) {
+        if (k == c->tp.rank) continue;
+        cudaIpcMemHandle_t h;
+        memcpy(&h, handles + (size_t)k * ECU_TP_HANDLE_BYTES, sizeof h);
+        void *p = nullptr;
+        const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            ecu_set_error(nullptr, 0, "opening rank %d's tagged vectors failed: %s", k, cudaGetErrorString(e));
+            return -1;
+        }
+        c->tp_peers.push_back(p);
+        c->margs.peer[k] = reinterpret_cast<unsigned long long *>(p);
+    }
+    char buf[64];
+    snprintf(buf, sizeof buf, "persistent, tensor parallel %d/%d", c->tp.rank, c->tp.world);
+    c->path = buf;
+    return 0;
+}

@@ -38,6 +38,9 @@
 #define MEGA_MAX_NB 512                  // input blocks of a GEMV (n_in <= 16384)
 #define MEGA_MAX_SPLIT 64                // position splits per KV head
 #define MEGA_RED4_MAX 6600               // floats of 4-lane row partials a GEMV phase may keep
+#ifndef ECU_MAX_TP
+#define ECU_MAX_TP 8                     // tensor-parallel ranks
+#endif
 
 enum MegaKind : int { PH_EMBED = 0, PH_GEMV = 1, PH_ATTN = 2 };
 
@@ -68,6 +71,9 @@ struct MegaPhase {
     int            in_ep, y_ep, out_plain;
     const unsigned long long *x_ll;    // input vector, tagged
     unsigned long long       *y_ll;    // output vector, tagged
+    int            out_base;   // index of this rank's first output element in y_ll (tensor parallel)
+    int            bcast;      // outputs go to every rank's copy of y_ll
+    int            pad_[2];
 };
 static_assert(sizeof(MegaPhase) % 16 == 0, "phase descriptors are copied in 16-byte pieces");
 
@@ -96,7 +102,12 @@ struct MegaArgs {
                                     // warp 0 waited for ring stages, attention: when head 0 merged
     int              advance_pos;   // argmax epilogue advances st->pos (FULL)
     int              layers_advance;// LAYERS: st->pos++ once the last phase is done
-    int              n_embd, n_head, n_kv, n_ctx, n_split;
+    int              n_embd, n_head, n_kv, n_ctx, n_split;   // n_head, n_kv: this rank's heads
+    int              tp_rank, tp_world;
+    unsigned long long *ll_block;   // this rank's tagged vectors (x_ll ... the argmax slots)
+    unsigned long long *peer[ECU_MAX_TP];   // every rank's block (IPC mappings), this one's included
+    unsigned long long *arg_ll;     // argmax exchange: value and index word per rank
+    int              vocab_base;    // first vocabulary row of this rank's head slice
     int              red_floats;    // row-partial floats the largest GEMV phase keeps
     unsigned         union_bytes;   // digit planes | attention K/V buffers
     int              nst;           // ring stages (<= MEGA_MAX_STAGES)
@@ -108,8 +119,9 @@ struct MegaArgs {
 // ------------------------------------------------------- tagged vectors --
 // The phases hand vectors to each other without grid barriers: every element
 // is one 8-byte word {float, epoch of the phase that wrote it}, stored and
-// loaded whole (aligned 64-bit relaxed accesses at GPU scope are single-copy
-// atomic), so a reader that sees the epoch it expects also sees the value.  A reader spins on words that still carry an
+// loaded whole (aligned 64-bit relaxed accesses are single-copy atomic; system
+// scope, as tensor-parallel ranks write them into each other's memory over
+// NVLink), so a reader that sees the epoch it expects also sees the value.  A reader spins on words that still carry an
 // older epoch.  Epoch = (launch number mod 2^20) << 12 | (phase + 1): unique
 // within a launch and against the previous one, which wrote every word.
 // Every phase's input depends on all CTAs' output of an earlier phase, so
@@ -123,20 +135,32 @@ __device__ __forceinline__ unsigned ll_epoch(unsigned launch, int phase)
 __device__ __forceinline__ void ll_put(unsigned long long *p, float v, unsigned e)
 {
     const unsigned long long w = ((unsigned long long)e << 32) | __float_as_uint(v);
-    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+
+// A phase output element: into this rank's vector, or (bcast) into every
+// rank's copy at the same offset.
+__device__ __forceinline__ void ll_put_out(const MegaArgs &a, bool bcast, unsigned long long *p, float v, unsigned e)
+{
+    if (!bcast) {
+        ll_put(p, v, e);
+        return;
+    }
+    const size_t off = (size_t)(p - a.ll_block);
+    for (int k = 0; k < a.tp_world; k++) ll_put(a.peer[k] + off, v, e);
 }
 
 __device__ __forceinline__ unsigned long long ll_word(const unsigned long long *p)
 {
     unsigned long long w;
-    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
     return w;
 }
 
 __device__ __forceinline__ ulonglong2 ll_word2(const unsigned long long *p)
 {
     ulonglong2 w;
-    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(w.x), "=l"(w.y) : "l"(p) : "memory");
+    asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(w.x), "=l"(w.y) : "l"(p) : "memory");
     return w;
 }
 
@@ -621,7 +645,7 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
     // settled after the prologue
     const bool has_res = epi == EPI_ADD && tid < nrows;
     unsigned long long yw = 0;
-    if (has_res && ph.y_ep >= 0) yw = ll_word(a.x_ll + r0 + tid);
+    if (has_res && ph.y_ep >= 0) yw = ll_word(a.x_ll + ph.out_base + r0 + tid);
 
     // ---- prologue: digit planes of every input block -----------------------
     // A CTA without rows reads no input: nothing it writes would tell a later
@@ -643,7 +667,7 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
     }
     float yprev = 0.0f;
     if (has_res)
-        yprev = ph.y_ep >= 0 ? ll_settle(a.x_ll + r0 + tid, yw, ll_epoch(S.launch, ph.y_ep), a.status)
+        yprev = ph.y_ep >= 0 ? ll_settle(a.x_ll + ph.out_base + r0 + tid, yw, ll_epoch(S.launch, ph.y_ep), a.status)
                              : __ldcg(ph.y + r0 + tid);
     named_bar(1, nct);
 
@@ -718,7 +742,7 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
     if (epi == EPI_SWIGLU) {
         for (int j = tid; j < nrows / 2; j += nct) {
             const float gs = row_total(S.red, 2 * j, nkg, red4), us = row_total(S.red, 2 * j + 1, nkg, red4);
-            ll_put(ph.y_ll + r0 / 2 + j, silu_mul(gs, us), eout);
+            ll_put_out(a, ph.bcast, ph.y_ll + ph.out_base + r0 / 2 + j, silu_mul(gs, us), eout);
         }
         if (det) det[2] = clock64();
         return;
@@ -728,10 +752,10 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
         const float acc = row_total(S.red, r, nkg, red4);
         if (epi == EPI_ADD) {
             const float out = yprev + acc;         // r == tid: nrows <= MEGA_THREADS
-            ll_put(ph.y_ll + r0 + r, out, eout);
+            ll_put_out(a, ph.bcast, ph.y_ll + ph.out_base + r0 + r, out, eout);
             if (ph.out_plain) y[r0 + r] = out;
         } else if (epi == EPI_STORE) {
-            ll_put(ph.y_ll + r0 + r, acc, eout);
+            ll_put_out(a, ph.bcast, ph.y_ll + ph.out_base + r0 + r, acc, eout);
         } else {
             y[r0 + r] = acc;                       // logits (argmax reads them after its ticket)
         }
@@ -769,8 +793,26 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
         ArgBest bb{-INFINITY, -1};
         for (unsigned c = 0; c < gridDim.x; c++)
             bb = arg_better(bb, ArgBest{__ldcg(a.part_val + c), __ldcg(a.part_idx + c)});
-        const float l0 = __ldcg(y);
-        const int   tok = (bb.i < 0 || isnan(l0)) ? 0 : bb.i;
+        if (bb.i >= 0) bb.i += a.vocab_base;
+        // a NaN first logit selects token 0 (the reference's rule): as an
+        // infinite logit at index 0 it wins every comparison below
+        if (a.tp_rank == 0 && isnan(__ldcg(y))) bb = ArgBest{INFINITY, 0};
+        if (a.tp_world > 1) {
+            // every rank's best to every rank, combined in rank order: all
+            // ranks pick the same token
+            const unsigned e = ll_epoch(S.launch, p_idx);
+            const size_t   off = (size_t)(a.arg_ll - a.ll_block) + 2 * (size_t)a.tp_rank;
+            for (int k = 0; k < a.tp_world; k++) {
+                ll_put(a.peer[k] + off, bb.v, e);
+                ll_put(a.peer[k] + off + 1, __int_as_float(bb.i), e);
+            }
+            ArgBest all{-INFINITY, -1};
+            for (int k = 0; k < a.tp_world; k++)
+                all = arg_better(all, ArgBest{ll_get(a.arg_ll + 2 * k, e, a.status),
+                                              __float_as_int(ll_get(a.arg_ll + 2 * k + 1, e, a.status))});
+            bb = all;
+        }
+        const int tok = bb.i < 0 ? 0 : bb.i;
         const int   pos = S.pos;
         if (a.tok_hist) a.tok_hist[pos] = tok;
         a.st->token = tok;
@@ -1033,7 +1075,7 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
         const int hh = i / HD, d = i % HD;
         float o = 0.0f;
         for (int r = 0; r < ns; r++) o = fmaf(gat[r * PER + hh * (HD + 4) + d], wsp[hh][r], o);
-        ll_put(a.att_ll + (g * NREP + hh) * HD + d, o * invl[hh], eout);
+        ll_put_out(a, ph.bcast, ph.y_ll + (g * NREP + hh) * HD + d, o * invl[hh], eout);
     }
     // profiling: when KV head 0's merge was done (whichever CTA did it)
     if (a.phase_detail && g == 0 && tid == 0) a.phase_detail[(size_t)p_idx * 4 + 3] = globaltimer_ns();

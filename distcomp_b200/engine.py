@@ -80,6 +80,11 @@ SIGNATURES = [
     ("ecu_token_ptr", C.c_void_p, [C.c_void_p]),
     ("ecu_step_dev", C.c_int, [C.c_void_p, C.c_void_p]),
     ("ecu_ctx_fork", C.c_int, [C.POINTER(C.c_void_p), C.c_void_p, C.c_char_p, C.c_size_t]),
+    ("ecu_ctx_open_tp", C.c_int, [C.POINTER(C.c_void_p), C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
+                                  C.c_char_p, C.c_size_t]),
+    ("ecu_tp_handle", C.c_int, [C.c_void_p, C.c_char_p]),
+    ("ecu_tp_connect", C.c_int, [C.c_void_p, C.c_char_p]),
+    ("ecu_tp_slice", C.c_int, [C.c_void_p, C.POINTER(C.c_int)]),
     ("ecu_generate", C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
     ("ecu_decode_async", C.c_int, [C.c_void_p, C.c_int]),
     ("ecu_sync", C.c_int, [C.c_void_p]),
@@ -170,11 +175,15 @@ class LlmCtx:
     """One engine stage resident on one GPU (llm_ctx, src/engine.h:46-70)."""
 
     def __init__(self, model: GgufModel | None, stage: int, first: int = 0, last: int = 0, n_ctx: int = 0,
-                 device: int = 0, fork_of: "LlmCtx | None" = None):
+                 device: int = 0, fork_of: "LlmCtx | None" = None, tp: tuple[int, int] | None = None):
+        """tp = (rank, world): a tensor-parallel FULL context (ecu_ctx_open_tp);
+        connect the ranks with tp_handle / tp_connect before the first step."""
         self.h = C.c_void_p()
         err = C.create_string_buffer(512)
         if fork_of is not None:
             rc = lib().ecu_ctx_fork(C.byref(self.h), fork_of.h, err, 512)
+        elif tp is not None:
+            rc = lib().ecu_ctx_open_tp(C.byref(self.h), model.h, n_ctx, device, int(tp[0]), int(tp[1]), err, 512)
         else:
             rc = lib().ecu_ctx_open(C.byref(self.h), model.h, stage, first, last, n_ctx, device, err, 512)
         if rc != 0:
@@ -185,6 +194,9 @@ class LlmCtx:
         self.n_embd, self.n_vocab, self.n_ctx = i.n_embd, i.n_vocab, i.n_ctx
         self.stage = i.stage
         self.device = i.device
+        sl = (C.c_int * 4)()
+        lib().ecu_tp_slice(self.h, sl)
+        self.tp_rank, self.tp_world, self.vocab0, self.vocab1 = (int(v) for v in sl)
 
     # --- reference API ---------------------------------------------------
     def forward(self, token: int, out: np.ndarray) -> int:
@@ -205,10 +217,23 @@ class LlmCtx:
 
     # --- extras ----------------------------------------------------------
     def logits(self) -> np.ndarray:
-        out = np.empty(self.n_vocab, dtype=np.float32)
-        if lib().ecu_get_logits(self.h, _ptr(out), self.n_vocab) != 0:
+        """The last step's logits (a tensor-parallel rank: rows vocab0..vocab1)."""
+        n = self.vocab1 - self.vocab0
+        out = np.empty(n, dtype=np.float32)
+        if lib().ecu_get_logits(self.h, _ptr(out), n) != 0:
             raise EngineError(last_error())
         return out
+
+    def tp_handle(self) -> bytes:
+        buf = C.create_string_buffer(64)
+        if lib().ecu_tp_handle(self.h, buf) != 0:
+            raise EngineError(last_error())
+        return buf.raw
+
+    def tp_connect(self, handles: list[bytes]) -> None:
+        blob = b"".join(handles)
+        if lib().ecu_tp_connect(self.h, blob) != 0:
+            raise EngineError(last_error())
 
     def set_pos(self, pos: int) -> None:
         if lib().ecu_set_pos(self.h, int(pos)) != 0:

@@ -137,6 +137,29 @@ int  ecu_step_dev(ecu_ctx *c, void *stream);
  * interleaved sequences needs one cache each).  The weights are freed when
  * the last context holding them closes. */
 int  ecu_ctx_fork(ecu_ctx **out, ecu_ctx *base, char *err, size_t errlen);
+
+/* ---- tensor parallelism (the alternative partition to shard.c's layer
+ * ranges, src/shard.c:358-437): one FULL context per GPU, rank r of w owns
+ * query/KV heads [r*n/w, ..), the matching rows of the fused Q/K/V, rows
+ * [r*n_embd/w, ..) of attn_output and ffn_down, FFN channels [r*n_ff/w, ..)
+ * and a vocabulary slice of the head.  Every projection keeps its whole
+ * input, so each output element is computed by one rank with the one-GPU
+ * arithmetic (bit-identical results); the ranks exchange outputs inside the
+ * persistent step through each other's memory (NVLink peer stores).  Steps
+ * must be issued on every rank in the same order (ecu_forward / decode);
+ * a rank that falls more than ~2 s behind makes the others' step fail with
+ * a timeout status. */
+#define ECU_TP_HANDLE_BYTES 64
+int  ecu_ctx_open_tp(ecu_ctx **out, const ecu_model *m, int n_ctx, int device, int tp_rank, int tp_world,
+                     char *err, size_t errlen);
+/* This rank's shareable handle (ECU_TP_HANDLE_BYTES) for the other ranks. */
+int  ecu_tp_handle(ecu_ctx *c, unsigned char *out);
+/* Map every rank's handle (world * ECU_TP_HANDLE_BYTES, rank order; this
+ * rank's own entry is ignored).  Call once, on every rank, before a step. */
+int  ecu_tp_connect(ecu_ctx *c, const unsigned char *handles);
+/* out4 = {rank, world, first vocabulary row, end row} of this context's head
+ * slice (ecu_get_logits returns that slice). */
+int  ecu_tp_slice(const ecu_ctx *c, int *out4);
 /* Greedy decode on a FULL context without host round trips: feeds
  * prompt[0..n_prompt) token by token, then generates n_gen tokens, each one
  * fed back on the device.  out_tokens receives the n_gen generated ids.

@@ -120,6 +120,14 @@ class ClockSampler:
                 "reasons": sorted(reasons)}
 
 
+def prefill_params(spec) -> int:
+    """Weights a prompt token multiplies in the layers (the GEMMs of ecu_prefill)."""
+    hd = spec.n_embd // spec.n_head
+    qd, kvd = spec.n_head * hd, spec.n_head_kv * hd
+    per = spec.n_embd * (qd + 2 * kvd) + qd * spec.n_embd + 3 * spec.n_embd * spec.n_ff
+    return per * spec.n_layer
+
+
 def algorithmic_bytes_per_token(spec, pos_mean: float) -> float:
     """Weights as stored + KV rows read (positions 0..pos) and written."""
     from distcomp_b200 import synth
@@ -220,7 +228,15 @@ def our_arm(args, rank, world, local):
     if need > args.n_ctx:
         raise SystemExit(f"prompt + steps need {need} positions > n_ctx {args.n_ctx}")
 
-    ctx.generate(prompt, 1)                         # prompt token by token, as the reference does
+    # the prompt through ecu_prefill (one batch per layer on the tensor
+    # cores), timed once after a warm-up prefill of the same prompt
+    ctx.prefill(prompt)
+    ctx.reset()
+    torch.cuda.synchronize(local)
+    t_pf = time.perf_counter()
+    first_tok = ctx.prefill(prompt)
+    t_pf = time.perf_counter() - t_pf
+    pf_flops = 2.0 * args.prompt * prefill_params(spec)
     ctx.decode_async(args.warmup)
     ctx.sync()
     stream = torch.cuda.ExternalStream(ctx.stream(), device=f"cuda:{local}")
@@ -290,6 +306,10 @@ def our_arm(args, rank, world, local):
         "e2e": {"value": round(e2e, 2), "unit": "tokens/s", "h2d_bytes_per_step": 8,
                 "d2h_bytes_per_step": (spec.n_embd + 1) * 4, "api": "ecu_forward (FULL context)"},
         "gpu_launches": int(launches),
+        "prefill": {"tokens": args.prompt, "ms": round(t_pf * 1e3, 2), "tokens_per_s": round(args.prompt / t_pf, 1),
+                    "tflops_useful": round(pf_flops / t_pf / 1e12, 2),
+                    "note": "ecu_prefill wall time incl. host sync; GEMMs split-fp16 (3 tensor-core "
+                            "products per useful one), first token " + str(first_tok)},
         "step_path": ctx.path(),
         "clocks": clk,
         "setup_s": {"model_build": round(t_build, 1), "upload": round(t_up, 1)},

@@ -13,6 +13,7 @@
 #include "ecu_mega.cuh"
 #include "ecu_misc.cuh"
 #include "ecu_model.h"
+#include "ecu_prefill.cuh"
 
 #include <atomic>
 #include <cmath>
@@ -380,6 +381,16 @@ struct ecu_ctx {
     EcuGeom     g;
     TpSlice     tp;
     std::vector<void *> tp_peers;         // IPC mappings of the other ranks' tagged vectors
+
+    // batched prompt (ecu_prefill): activations of `rows` tokens, fp16 hi/lo
+    // operands, one dequantised weight matrix; allocated on first use
+    struct Prefill {
+        int     rows = 0;
+        size_t  wcap = 0;
+        float  *X = nullptr, *QKV = nullptr, *ATT = nullptr, *GU = nullptr, *H = nullptr;
+        __half *ah = nullptr, *al = nullptr, *wh = nullptr, *wl = nullptr;
+        int    *tok = nullptr;
+    } pf;
     cudaStream_t stream = nullptr;
     bool        pdl = true, use_graph = true;
     std::vector<void *> allocs;           // this context's own buffers
@@ -538,6 +549,9 @@ static void ctx_free(ecu_ctx *c)
     if (c->graph) cudaGraphExecDestroy(c->graph);
     for (void *p : c->tp_peers)
         if (p) cudaIpcCloseMemHandle(p);
+    for (void *p : {(void *)c->pf.X, (void *)c->pf.QKV, (void *)c->pf.ATT, (void *)c->pf.GU, (void *)c->pf.H,
+                    (void *)c->pf.ah, (void *)c->pf.al, (void *)c->pf.wh, (void *)c->pf.wl, (void *)c->pf.tok})
+        if (p) cudaFree(p);
     for (void *p : c->allocs) cudaFree(p);
     if (c->h_st) cudaFreeHost(c->h_st);
     if (c->h_state) cudaFreeHost(c->h_state);
@@ -2188,5 +2202,150 @@ int ecu_tp_connect(ecu_ctx *c, const unsigned char *handles)
     char buf[64];
     snprintf(buf, sizeof buf, "persistent, tensor parallel %d/%d", c->tp.rank, c->tp.world);
     c->path = buf;
+    return 0;
+}
+
+// ----------------------------------------------------------- prefill -----
+
+static int pf_reserve(ecu_ctx *c, int n)
+{
+    ecu_ctx::Prefill &P = c->pf;
+    const EcuGeom &g = c->g;
+    const size_t hd = (size_t)g.head_dim, qd = (size_t)g.n_head * hd, kvd = (size_t)g.n_head_kv * hd;
+    size_t wmax = 0;
+    for (auto &ly : c->layers)
+        for (const DevMat *m : {&ly.qkv[0], &ly.o, &ly.gu, &ly.d})
+            wmax = std::max(wmax, (size_t)m->n_out * m->n_in);
+    if (n > P.rows) {
+        for (void *p : {(void *)P.X, (void *)P.QKV, (void *)P.ATT, (void *)P.GU, (void *)P.H, (void *)P.ah,
+                        (void *)P.al, (void *)P.tok})
+            if (p) cudaFree(p);
+        P = ecu_ctx::Prefill{0, P.wcap, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, P.wh, P.wl,
+                             nullptr};
+        const size_t wide = std::max(std::max((size_t)g.n_embd, qd), (size_t)g.n_ff);
+        bool ok = cudaMalloc(&P.X, sizeof(float) * n * (size_t)g.n_embd) == cudaSuccess &&
+                  cudaMalloc(&P.QKV, sizeof(float) * n * (qd + 2 * kvd)) == cudaSuccess &&
+                  cudaMalloc(&P.ATT, sizeof(float) * n * qd) == cudaSuccess &&
+                  cudaMalloc(&P.GU, sizeof(float) * n * 2 * (size_t)g.n_ff) == cudaSuccess &&
+                  cudaMalloc(&P.H, sizeof(float) * n * (size_t)g.n_ff) == cudaSuccess &&
+                  cudaMalloc(&P.ah, sizeof(__half) * n * wide) == cudaSuccess &&
+                  cudaMalloc(&P.al, sizeof(__half) * n * wide) == cudaSuccess &&
+                  cudaMalloc(&P.tok, sizeof(int) * n) == cudaSuccess;
+        if (!ok) {
+            cudaGetLastError();
+            ecu_set_error(nullptr, 0, "out of device memory for a %d-token prefill", n);
+            return -1;
+        }
+        P.rows = n;
+    }
+    if (wmax > P.wcap) {
+        if (P.wh) cudaFree(P.wh);
+        if (P.wl) cudaFree(P.wl);
+        P.wh = P.wl = nullptr;
+        P.wcap = 0;
+        if (cudaMalloc(&P.wh, sizeof(__half) * wmax) != cudaSuccess ||
+            cudaMalloc(&P.wl, sizeof(__half) * wmax) != cudaSuccess) {
+            cudaGetLastError();
+            ecu_set_error(nullptr, 0, "out of device memory for the prefill weight operands");
+            return -1;
+        }
+        P.wcap = wmax;
+    }
+    return 0;
+}
+
+// GEMM of the prefill: C[n x m.n_out] (+R) = A[n x m.n_in] * W^T, W split first.
+static int pf_gemm(ecu_ctx *c, const DevMat &m, int n, float *C, const float *R)
+{
+    ecu_ctx::Prefill &P = c->pf;
+    k_pf_wsplit<<<8 * c->sms, 256, 0, c->stream>>>(m, P.wh, P.wl);
+    dim3 grid((unsigned)((m.n_out + PF_BN - 1) / PF_BN), (unsigned)((n + PF_BM - 1) / PF_BM));
+    k_pf_gemm<<<grid, 256, pf_gemm_smem(), c->stream>>>(P.ah, P.al, P.wh, P.wl, C, n, m.n_out, m.n_in, m.n_out, R);
+    CK(cudaGetLastError());
+    return 0;
+}
+
+int ecu_prefill(ecu_ctx *c, const int *tokens, int n, float *out)
+{
+    if (!c || !tokens || !out || n < 1) { ecu_set_error(nullptr, 0, "null argument or empty prompt"); return -1; }
+    cudaSetDevice(c->device);
+    const EcuGeom &g = c->g;
+    for (int i = 0; i < n; i++)
+        if (tokens[i] < 0 || tokens[i] >= g.n_vocab) {
+            ecu_set_error(nullptr, 0, "token %d outside the vocabulary (%d)", tokens[i], g.n_vocab);
+            return -1;
+        }
+    if (c->stage != ECU_STAGE_FULL) { ecu_set_error(nullptr, 0, "prefill runs FULL contexts"); return -1; }
+    if (c->pos + n > g.n_ctx) {
+        ecu_set_error(nullptr, 0, "prompt of %d tokens at position %d exceeds the context (%d)", n, c->pos, g.n_ctx);
+        return -1;
+    }
+    bool batched = c->tp.world == 1 && g.n_ctx <= PF_ATT_MAXPOS && (g.head_dim == 64 || g.head_dim == 128) &&
+                   g.n_embd % 8 == 0 && g.n_ff % 8 == 0;
+    for (auto &ly : c->layers) batched = batched && ly.qkv.size() == 1 && ly.gu_fused;
+    if (!batched) {
+        // shapes the batched kernels do not cover (and tensor-parallel ranks,
+        // which step together): the per-token step, prompt token by token
+        for (int i = 0; i < n; i++)
+            if (ecu_forward(c, tokens[i], out) != 0) return -1;
+        return 0;
+    }
+    static std::atomic<unsigned> attr_done{0};            // per device (bit d), set once
+    if (c->device < 32 && !(attr_done.load() & (1u << c->device))) {
+        CK(cudaFuncSetAttribute(k_pf_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pf_gemm_smem()));
+        attr_done.fetch_or(1u << c->device);
+    } else if (c->device >= 32) {
+        CK(cudaFuncSetAttribute(k_pf_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pf_gemm_smem()));
+    }
+    if (pf_reserve(c, n) != 0) return -1;
+    ecu_ctx::Prefill &P = c->pf;
+    const int hd = g.head_dim, qd = g.n_head * hd, kvd = g.n_head_kv * hd, E = g.n_embd, pos0 = c->pos;
+    const int ldq = qd + 2 * kvd;
+    const size_t plane = (size_t)g.n_head_kv * g.n_ctx * hd;
+    const float kscale = 1.0f / sqrtf((float)hd);
+    CK(cudaMemcpyAsync(P.tok, tokens, sizeof(int) * n, cudaMemcpyHostToDevice, c->stream));
+    k_pf_embed<<<4 * c->sms, 256, 0, c->stream>>>(c->emb, P.tok, n, P.X, E);
+    for (size_t li = 0; li < c->layers.size(); li++) {
+        LayerDev &ly = c->layers[li];
+        k_pf_norm_split<<<n, 256, 0, c->stream>>>(P.X, ly.attn_norm, E, g.eps, P.ah, P.al);
+        if (pf_gemm(c, ly.qkv[0], n, P.QKV, nullptr)) return -1;
+        k_pf_rope_kv<<<n, 128, 0, c->stream>>>(P.QKV, ldq, g.n_head, g.n_head_kv, hd, pos0, c->rope_cs, ly.bq, ly.bk,
+                                               ly.bv, c->kc + li * plane, c->vc + li * plane, g.n_ctx);
+        dim3 ag((unsigned)g.n_head, (unsigned)n);
+        if (hd == 128)
+            k_pf_attn<128><<<ag, 128, 0, c->stream>>>(P.QKV, ldq, g.n_head, g.n_rep, pos0, c->kc + li * plane,
+                                                      c->vc + li * plane, g.n_ctx, kscale, P.ATT);
+        else
+            k_pf_attn<64><<<ag, 64, 0, c->stream>>>(P.QKV, ldq, g.n_head, g.n_rep, pos0, c->kc + li * plane,
+                                                    c->vc + li * plane, g.n_ctx, kscale, P.ATT);
+        k_pf_split<<<4 * c->sms, 256, 0, c->stream>>>(P.ATT, (size_t)n * qd, P.ah, P.al);
+        if (pf_gemm(c, ly.o, n, P.X, P.X)) return -1;
+        k_pf_norm_split<<<n, 256, 0, c->stream>>>(P.X, ly.ffn_norm, E, g.eps, P.ah, P.al);
+        if (pf_gemm(c, ly.gu, n, P.GU, nullptr)) return -1;
+        k_pf_swiglu<<<4 * c->sms, 256, 0, c->stream>>>(P.GU, (size_t)n, g.n_ff, P.H);
+        k_pf_split<<<4 * c->sms, 256, 0, c->stream>>>(P.H, (size_t)n * g.n_ff, P.ah, P.al);
+        if (pf_gemm(c, ly.d, n, P.X, P.X)) return -1;
+        CK(cudaGetLastError());
+    }
+    // the last token through the decode step's head (norm, logits, argmax)
+    CK(cudaMemcpyAsync(c->state, P.X + (size_t)(n - 1) * E, sizeof(float) * E, cudaMemcpyDeviceToDevice, c->stream));
+    StepState *slot = c->h_st + ((pos0 + n - 1) % c->n_hslots);
+    slot->pos = pos0 + n - 1;
+    slot->token = tokens[n - 1];
+    CK(cudaMemcpyAsync(c->st, slot, 2 * sizeof(int), cudaMemcpyHostToDevice, c->stream));
+    Launcher L{c->stream, false};
+    enqueue_head(c, L, true);
+    g_launches += (uint64_t)L.count + 15 * c->layers.size() + 1;   // + embed, 15 kernels a layer
+    if (L.err != cudaSuccess) {
+        ecu_set_error(nullptr, 0, "kernel launch failed: %s", cudaGetErrorString(L.err));
+        return -1;
+    }
+    c->pos = pos0 + n;
+    c->have_logits = true;
+    const size_t ne = (size_t)E;
+    CK(cudaMemcpyAsync(c->h_state, c->state, (ne + 1) * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
+    if (check_status(c) != 0) return -1;
+    memcpy(out, c->h_state, (ne + 1) * sizeof(float));
+    c->last_pick = (int)c->h_state[ne];
     return 0;
 }

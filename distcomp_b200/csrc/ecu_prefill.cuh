@@ -1,0 +1,301 @@
+// ecu_prefill.cuh -- the prompt of a FULL context as one batch per layer.
+//
+// The reference feeds a prompt token by token (src/shard.c:911-917); every
+// projection is then a matrix-vector product.  Here the n prompt tokens of a
+// layer go through each projection together, as one GEMM on the tensor
+// cores, so every weight is read once per layer instead of n times:
+//
+//   embed rows -> per layer: RMSNorm -> QKV GEMM -> RoPE + KV append ->
+//   causal attention (each token over the cache up to its own position) ->
+//   O GEMM + residual -> RMSNorm -> gate/up GEMM -> SwiGLU -> down GEMM +
+//   residual;  then the last token through the decode step's head.
+//
+// Precision: each GEMM operand is split into two fp16 parts, v = hi + lo
+// (hi = fp16(v), lo = fp16(v - hi)), and the product is accumulated in fp32
+// as hi*hi + hi*lo + lo*hi, which keeps about 22 bits of every factor --
+// the error of the fp32 matvec the reference runs, not fp16's.  The
+// dequantised weights (exact in fp32: code * fp16 scale) are split once per
+// layer into a scratch matrix; the activations are split as they are
+// produced.  The tensor-core instruction is mma.sync m16n8k16 (fp16 in, fp32
+// accumulate).  Sums run in another order than the per-token path, so the
+// prompt's activations and logits agree with it within the 1e-3 bar, not
+// bit for bit.
+#pragma once
+#include "ecu_attn.cuh"
+#include "ecu_common.cuh"
+#include "ecu_dequant.cuh"
+#include "ecu_gemv.cuh"
+
+#include <cuda_fp16.h>
+
+// Embedding rows of the n prompt tokens (any type of the raw matrix).
+static __global__ void k_pf_embed(DevMat emb, const int *tok, int n, float *X, int E)
+{
+    const size_t total = (size_t)n * E;
+    for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
+        const int    t = (int)(e / (size_t)E), i = (int)(e % (size_t)E);
+        const size_t a = (size_t)tok[t] * (size_t)E + (size_t)i;
+        X[e] = mat_elem(emb, (int)(a / (size_t)emb.n_in), (int)(a % (size_t)emb.n_in));
+    }
+}
+
+__device__ __forceinline__ void pf_split(float v, __half &hi, __half &lo)
+{
+    hi = __float2half_rn(v);
+    lo = __float2half_rn(__fsub_rn(v, __half2float(hi)));
+}
+
+// Row t of X, RMS-normalised with weights w exactly as the decode step does
+// (rms_scale's summation order, the same two roundings per element), split
+// into fp16 hi/lo.  One CTA (256 threads) per row.
+static __global__ void __launch_bounds__(256) k_pf_norm_split(const float *X, const float *w, int E, float eps,
+                                                               __half *hi, __half *lo)
+{
+    __shared__ double dsum[RMS_MAX_W + 1];
+    const float *x = X + (size_t)blockIdx.x * E;
+    const float  s = rms_scale(x, E, eps, dsum, threadIdx.x, blockDim.x, [] { __syncthreads(); });
+    for (int i = threadIdx.x; i < E; i += blockDim.x) {
+        const float v = __fmul_rn(__fmul_rn(__ldcg(x + i), s), w[i]);
+        pf_split(v, hi[(size_t)blockIdx.x * E + i], lo[(size_t)blockIdx.x * E + i]);
+    }
+}
+
+static __global__ void k_pf_split(const float *X, size_t count, __half *hi, __half *lo)
+{
+    for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < count; e += (size_t)gridDim.x * blockDim.x)
+        pf_split(X[e], hi[e], lo[e]);
+}
+
+// A device weight matrix (any layout) dequantised and split: rows x n_in.
+static __global__ void k_pf_wsplit(DevMat m, __half *hi, __half *lo)
+{
+    const size_t total = (size_t)m.n_out * m.n_in;
+    for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x)
+        pf_split(mat_elem(m, (int)(e / (size_t)m.n_in), (int)(e % (size_t)m.n_in)), hi[e], lo[e]);
+}
+
+// ----------------------------------------------------------------- GEMM ---
+// C[M x N] (+)= A[M x K] * B[N x K]^T, A and B each given as fp16 hi/lo row-
+// major with K contiguous (K % 8 == 0); C fp32 row-major with stride ldc; R
+// (may equal C) added when non-null.  CTA tile 128 x 128, K step 32, two
+// cp.async stages; 8 warps as 2 (M) x 4 (N), 64 x 32 each; rows past M or N
+// load as zeros and are not stored.
+#define PF_BM 128
+#define PF_BN 128
+#define PF_BK 32
+#define PF_LDS 40            // halves per shared row: 80 B, conflict-free ldmatrix
+#define PF_TILE (PF_BM * PF_LDS)
+
+__host__ __device__ constexpr size_t pf_gemm_smem() { return (size_t)2 * 4 * PF_TILE * sizeof(__half); }
+
+__device__ __forceinline__ void pf_cp16(void *dst, const void *src, bool ok)
+{
+    const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+    const int      n = ok ? 16 : 0;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(n) : "memory");
+}
+
+__device__ __forceinline__ void pf_ldm4(unsigned (&r)[4], const __half *p)
+{
+    const unsigned a = (unsigned)__cvta_generic_to_shared(p);
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(a));
+}
+
+__device__ __forceinline__ void pf_mma(float (&c)[4], const unsigned (&a)[4], unsigned b0, unsigned b1)
+{
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+                 "{%8, %9}, {%0, %1, %2, %3};"
+                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+static __global__ void __launch_bounds__(256) k_pf_gemm(const __half *Ahi, const __half *Alo, const __half *Bhi,
+                                                         const __half *Blo, float *C, int M, int N, int K, int ldc,
+                                                         const float *R)
+{
+    extern __shared__ __align__(16) __half pf_sm[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int m0 = blockIdx.y * PF_BM, n0 = blockIdx.x * PF_BN;
+    const int wm = (warp >> 2) * 64, wn = (warp & 3) * 32;
+    // stage s, operand o (0 A hi, 1 A lo, 2 B hi, 3 B lo)
+    auto tile = [&](int s, int o) { return pf_sm + ((size_t)s * 4 + o) * PF_TILE; };
+    const __half *src[4] = {Ahi, Alo, Bhi, Blo};
+
+    auto load = [&](int s, int k0) {
+        // 4 tiles of 128 rows x 32 halves = 512 16-byte chunks each
+#pragma unroll
+        for (int o = 0; o < 4; o++) {
+            const int lim = o < 2 ? M : N, base = o < 2 ? m0 : n0;
+#pragma unroll
+            for (int j = 0; j < 2; j++) {
+                const int  ch = tid + j * 256, r = ch >> 2, c = (ch & 3) * 8;
+                const bool ok = base + r < lim && k0 + c < K;
+                const __half *g = src[o] + (ok ? (size_t)(base + r) * K + k0 + c : 0);
+                pf_cp16(tile(s, o) + r * PF_LDS + c, g, ok);
+            }
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+
+    float acc[4][4][4];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+#pragma unroll
+            for (int q = 0; q < 4; q++) acc[i][j][q] = 0.0f;
+
+    const int nk = (K + PF_BK - 1) / PF_BK;
+    load(0, 0);
+    for (int kt = 0; kt < nk; kt++) {
+        const int s = kt & 1;
+        if (kt + 1 < nk) {
+            load(s ^ 1, (kt + 1) * PF_BK);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        __syncthreads();
+#pragma unroll
+        for (int kk = 0; kk < PF_BK; kk += 16) {
+            unsigned ah[4][4], al[4][4], bh[2][4], bl[2][4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int off = (wm + i * 16 + (lane & 15)) * PF_LDS + kk + (lane >> 4) * 8;
+                pf_ldm4(ah[i], tile(s, 0) + off);
+                pf_ldm4(al[i], tile(s, 1) + off);
+            }
+#pragma unroll
+            for (int j = 0; j < 2; j++) {
+                // matrices: (n 0-7, k 0-7), (n 0-7, k 8-15), (n 8-15, k 0-7), (n 8-15, k 8-15)
+                const int off = (wn + j * 16 + (lane & 7) + ((lane >> 4) << 3)) * PF_LDS + kk + ((lane >> 3) & 1) * 8;
+                pf_ldm4(bh[j], tile(s, 2) + off);
+                pf_ldm4(bl[j], tile(s, 3) + off);
+            }
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const int jj = j >> 1, h = (j & 1) * 2;
+                    pf_mma(acc[i][j], ah[i], bh[jj][h], bh[jj][h + 1]);
+                    pf_mma(acc[i][j], ah[i], bl[jj][h], bl[jj][h + 1]);
+                    pf_mma(acc[i][j], al[i], bh[jj][h], bh[jj][h + 1]);
+                }
+        }
+        __syncthreads();                  // the stage is refilled next iteration
+    }
+    // C fragment: c0, c1 at (row g, cols 2t, 2t+1), c2, c3 at row g + 8
+    const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const int row = m0 + wm + i * 16 + g + h * 8;
+                if (row >= M) continue;
+#pragma unroll
+                for (int q = 0; q < 2; q++) {
+                    const int col = n0 + wn + j * 8 + 2 * t + q;
+                    if (col >= N) continue;
+                    const size_t e = (size_t)row * ldc + col;
+                    const float  v = acc[i][j][h * 2 + q];
+                    C[e] = R ? __fadd_rn(R[e], v) : v;
+                }
+            }
+}
+
+// --------------------------------------------------------- RoPE, KV, attn --
+// Row t of QKV (q | k | v of one token): biases, RoPE of q and k at position
+// pos0 + t (src/engine.c:367-378), q rotated in place, k and v appended to
+// this layer's cache planes [n_kv][n_ctx][hd].
+static __global__ void k_pf_rope_kv(float *QKV, int ld, int n_head, int n_kv, int hd, int pos0, const float *cs,
+                                    const float *bq, const float *bk, const float *bv, float *kc, float *vc, int n_ctx)
+{
+    const int t = blockIdx.x, pos = pos0 + t, half = hd / 2;
+    float    *q = QKV + (size_t)t * ld, *k = q + (size_t)n_head * hd, *v = k + (size_t)n_kv * hd;
+    const float *c = cs + (size_t)pos * hd;
+    for (int i = threadIdx.x; i < n_head * half; i += blockDim.x) {
+        const int h = i / half, j = i % half;
+        float     x0 = q[h * hd + j], x1 = q[h * hd + j + half];
+        if (bq) { x0 = __fadd_rn(x0, bq[h * hd + j]); x1 = __fadd_rn(x1, bq[h * hd + j + half]); }
+        rope_pair(x0, x1, c[2 * j], c[2 * j + 1]);
+        q[h * hd + j] = x0;
+        q[h * hd + j + half] = x1;
+    }
+    for (int i = threadIdx.x; i < n_kv * half; i += blockDim.x) {
+        const int g = i / half, j = i % half;
+        float     k0 = k[g * hd + j], k1 = k[g * hd + j + half];
+        float     v0 = v[g * hd + j], v1 = v[g * hd + j + half];
+        if (bk) { k0 = __fadd_rn(k0, bk[g * hd + j]); k1 = __fadd_rn(k1, bk[g * hd + j + half]); }
+        if (bv) { v0 = __fadd_rn(v0, bv[g * hd + j]); v1 = __fadd_rn(v1, bv[g * hd + j + half]); }
+        rope_pair(k0, k1, c[2 * j], c[2 * j + 1]);
+        float *kr = kc + ((size_t)g * n_ctx + pos) * hd, *vr = vc + ((size_t)g * n_ctx + pos) * hd;
+        kr[j] = k0;
+        kr[j + half] = k1;
+        vr[j] = v0;
+        vr[j + half] = v1;
+    }
+}
+
+// Attention of token t, query head h (one CTA of HD threads): scores over
+// cache positions 0..pos0+t in shared memory, exact max, expf, weights
+// divided by their sum once, out = sum of weighted V rows.
+#define PF_ATT_MAXPOS 8192
+template <int HD>
+static __global__ void __launch_bounds__(HD) k_pf_attn(const float *QKV, int ld, int n_head, int n_rep, int pos0,
+                                                        const float *kc, const float *vc, int n_ctx, float kscale,
+                                                        float *att)
+{
+    __shared__ float sc[PF_ATT_MAXPOS];
+    __shared__ __align__(16) float qs[HD];
+    __shared__ float red[HD / 32];
+    const int t = blockIdx.y, h = blockIdx.x, g = h / n_rep, np = pos0 + t + 1;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    qs[tid] = QKV[(size_t)t * ld + (size_t)h * HD + tid];
+    __syncthreads();
+    const float *kb = kc + (size_t)g * n_ctx * HD, *vb = vc + (size_t)g * n_ctx * HD;
+    // scores: warp w takes positions w, w + HD/32, ...; lanes over dims
+    for (int p = warp; p < np; p += HD / 32) {
+        const float *kr = kb + (size_t)p * HD;
+        float        d = 0.0f;
+        for (int j = lane; j < HD; j += 32) d = fmaf(qs[j], kr[j], d);
+        d = warp_sum(d);
+        if (lane == 0) sc[p] = d * kscale;
+    }
+    __syncthreads();
+    float m = -INFINITY;
+    for (int p = tid; p < np; p += HD) m = fmaxf(m, sc[p]);
+    m = warp_max(m);
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    m = red[0];
+    for (int w = 1; w < HD / 32; w++) m = fmaxf(m, red[w]);
+    __syncthreads();
+    float l = 0.0f;
+    for (int p = tid; p < np; p += HD) {
+        const float e = expf(sc[p] - m);
+        sc[p] = e;
+        l += e;
+    }
+    l = warp_sum(l);
+    if (lane == 0) red[warp] = l;
+    __syncthreads();
+    l = 0.0f;
+    for (int w = 0; w < HD / 32; w++) l += red[w];
+    float o = 0.0f;                               // dim tid
+    for (int p = 0; p < np; p++) o = fmaf(sc[p], vb[(size_t)p * HD + tid], o);
+    att[(size_t)t * n_head * HD + (size_t)h * HD + tid] = o / l;
+}
+
+// h[t][j] = silu(gate) * up from the interleaved gate/up rows (2j, 2j+1).
+static __global__ void k_pf_swiglu(const float *GU, size_t n_rows, int ff, float *H)
+{
+    const size_t total = n_rows * (size_t)ff;
+    for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
+        const size_t t = e / (size_t)ff, j = e % (size_t)ff;
+        H[e] = silu_mul(GU[t * 2 * ff + 2 * j], GU[t * 2 * ff + 2 * j + 1]);
+    }
+}

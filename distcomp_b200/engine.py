@@ -85,6 +85,7 @@ SIGNATURES = [
     ("ecu_tp_handle", C.c_int, [C.c_void_p, C.c_char_p]),
     ("ecu_tp_connect", C.c_int, [C.c_void_p, C.c_char_p]),
     ("ecu_tp_slice", C.c_int, [C.c_void_p, C.POINTER(C.c_int)]),
+    ("ecu_prefill", C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p]),
     ("ecu_generate", C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
     ("ecu_decode_async", C.c_int, [C.c_void_p, C.c_int]),
     ("ecu_sync", C.c_int, [C.c_void_p]),
@@ -251,6 +252,16 @@ class LlmCtx:
         if lib().ecu_generate(self.h, _ptr(p), len(p), int(n_gen), _ptr(out)) != 0:
             raise EngineError(last_error())
         return [int(t) for t in out[:n_gen]]
+
+    def prefill(self, tokens, out: np.ndarray | None = None) -> int:
+        """The prompt at once (ecu_prefill); returns the picked next token."""
+        p = np.ascontiguousarray(tokens, dtype=np.int32)
+        if out is None:
+            out = np.zeros(self.n_embd + 1, dtype=np.float32)
+        assert out.dtype == np.float32 and out.size >= self.n_embd + 1
+        if lib().ecu_prefill(self.h, _ptr(p), len(p), _ptr(out)) != 0:
+            raise EngineError(last_error())
+        return int(out[self.n_embd])
 
     def decode_async(self, n: int) -> None:
         if lib().ecu_decode_async(self.h, int(n)) != 0:

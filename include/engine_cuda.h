@@ -165,6 +165,19 @@ int  ecu_tp_slice(const ecu_ctx *c, int *out4);
  * fed back on the device.  out_tokens receives the n_gen generated ids.
  * Returns 0, or -1 when the context runs out. */
 int  ecu_generate(ecu_ctx *c, const int *prompt, int n_prompt, int n_gen, int *out_tokens);
+/* A prompt of n tokens through a FULL context at once (the reference feeds
+ * prompts token by token, src/shard.c:911-917, one llm_forward each): every
+ * layer runs its n tokens as one batch (GEMMs on the tensor cores with
+ * split-fp16 operands, about fp32 accuracy; causal attention over the
+ * cache), the cache gets the n positions, and the last token goes through
+ * the head: out = normed state (n_embd) + the picked token, as ecu_forward's
+ * out for that token, and the context's position advances by n.  Results
+ * agree with the token-by-token path within the 1e-3 bar, not bit for bit.
+ * Shapes the batched kernels do not cover (unfused projections, head_dim
+ * other than 64/128, n_ctx > 8192) and tensor-parallel ranks run the
+ * per-token step instead.  Scratch for the batch is allocated on first use
+ * and grows with the longest prompt. */
+int  ecu_prefill(ecu_ctx *c, const int *tokens, int n, float *out);
 /* Decode steps on a FULL context continuing from the token in the state
  * buffer, on the context's stream, without synchronising; used to time the
  * device-side loop.  Returns 0 or -1. */

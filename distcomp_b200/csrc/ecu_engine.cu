@@ -2254,13 +2254,19 @@ static int pf_reserve(ecu_ctx *c, int n)
     return 0;
 }
 
-// GEMM of the prefill: C[n x m.n_out] (+R) = A[n x m.n_in] * W^T, W split first.
+// GEMM of the prefill: C[n x m.n_out] (+R) = A[n x m.n_in] * W^T, W split
+// first; tcgen05 (ECU_PF_TC=0: the mma.sync kernel).
 static int pf_gemm(ecu_ctx *c, const DevMat &m, int n, float *C, const float *R)
 {
     ecu_ctx::Prefill &P = c->pf;
     k_pf_wsplit<<<8 * c->sms, 256, 0, c->stream>>>(m, P.wh, P.wl);
     dim3 grid((unsigned)((m.n_out + PF_BN - 1) / PF_BN), (unsigned)((n + PF_BM - 1) / PF_BM));
-    k_pf_gemm<<<grid, 256, pf_gemm_smem(), c->stream>>>(P.ah, P.al, P.wh, P.wl, C, n, m.n_out, m.n_in, m.n_out, R);
+    const char *e = getenv("ECU_PF_TC");
+    if (!(e && e[0] == '0'))
+        k_pf_gemm_tc<<<grid, 128, pf_tc_smem(), c->stream>>>(P.ah, P.al, P.wh, P.wl, C, n, m.n_out, m.n_in, m.n_out,
+                                                              R, &c->st->status);
+    else
+        k_pf_gemm<<<grid, 256, pf_gemm_smem(), c->stream>>>(P.ah, P.al, P.wh, P.wl, C, n, m.n_out, m.n_in, m.n_out, R);
     CK(cudaGetLastError());
     return 0;
 }
@@ -2291,11 +2297,10 @@ int ecu_prefill(ecu_ctx *c, const int *tokens, int n, float *out)
         return 0;
     }
     static std::atomic<unsigned> attr_done{0};            // per device (bit d), set once
-    if (c->device < 32 && !(attr_done.load() & (1u << c->device))) {
+    if (c->device >= 32 || !(attr_done.load() & (1u << c->device))) {
         CK(cudaFuncSetAttribute(k_pf_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pf_gemm_smem()));
-        attr_done.fetch_or(1u << c->device);
-    } else if (c->device >= 32) {
-        CK(cudaFuncSetAttribute(k_pf_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pf_gemm_smem()));
+        CK(cudaFuncSetAttribute(k_pf_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pf_tc_smem()));
+        if (c->device < 32) attr_done.fetch_or(1u << c->device);
     }
     if (pf_reserve(c, n) != 0) return -1;
     ecu_ctx::Prefill &P = c->pf;

@@ -16,8 +16,9 @@
 // the error of the fp32 matvec the reference runs, not fp16's.  The
 // dequantised weights (exact in fp32: code * fp16 scale) are split once per
 // layer into a scratch matrix; the activations are split as they are
-// produced.  The tensor-core instruction is mma.sync m16n8k16 (fp16 in, fp32
-// accumulate).  Sums run in another order than the per-token path, so the
+// produced.  The GEMM runs on tcgen05 (k_pf_gemm_tc: fp32 accumulators in
+// tensor memory); k_pf_gemm, the same product with mma.sync m16n8k16, stays
+// as the reference point (ECU_PF_TC=0).  Sums run in another order than the per-token path, so the
 // prompt's activations and logits agree with it within the 1e-3 bar, not
 // bit for bit.
 #pragma once
@@ -25,6 +26,7 @@
 #include "ecu_common.cuh"
 #include "ecu_dequant.cuh"
 #include "ecu_gemv.cuh"
+#include "ecu_pipe.cuh"
 
 #include <cuda_fp16.h>
 
@@ -205,6 +207,155 @@ static __global__ void __launch_bounds__(256) k_pf_gemm(const __half *Ahi, const
                     C[e] = R ? __fadd_rn(R[e], v) : v;
                 }
             }
+}
+
+// ------------------------------------------------ GEMM on tcgen05 (TMEM) ---
+// The same product on the 5th-generation tensor cores: one elected thread
+// issues tcgen05.mma (kind::f16, M = 128 tokens, N = 128 weight rows, K = 16
+// per instruction) on operands in shared memory, the fp32 accumulator lives
+// in tensor memory (128 columns) and is read back with tcgen05.ld for the
+// epilogue.  Operand tiles are 128 rows x 64 halves (one 128-byte swizzle
+// atom per row: 16-byte chunk c of row r sits at chunk c ^ (r & 7)), loaded
+// with cp.async, three stages; tcgen05.commit on a per-stage mbarrier tells
+// the loaders when a stage's MMAs have read it.  Same interface and limits
+// as k_pf_gemm (K % 8 == 0).
+#define PF_TC_BK 64
+#define PF_TC_STAGES 3
+#define PF_TC_TILE (128 * PF_TC_BK * 2)      // bytes of one operand tile
+
+__host__ __device__ constexpr size_t pf_tc_smem() { return (size_t)PF_TC_STAGES * 4 * PF_TC_TILE + 1024; }
+
+// K-major, 128-byte-swizzled operand: rows 128 B apart, 8-row groups 1024 B
+// apart (SBO), leading offset 1 (unused within one swizzle atom), version 1.
+__device__ __forceinline__ uint64_t pf_sdesc(uint32_t saddr)
+{
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+__device__ __forceinline__ void pf_tc_mma(uint32_t tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc)
+{
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "setp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+                 :
+                 : "r"(tmem), "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+                 : "memory");
+}
+
+static __global__ void __launch_bounds__(128, 1) k_pf_gemm_tc(const __half *Ahi, const __half *Alo,
+                                                               const __half *Bhi, const __half *Blo, float *C,
+                                                               int M, int N, int K, int ldc, const float *R,
+                                                               int *status)
+{
+    extern __shared__ uint8_t pf_tc_raw[];
+    uint8_t *sm = reinterpret_cast<uint8_t *>(((uintptr_t)pf_tc_raw + 1023) & ~(uintptr_t)1023);
+    __shared__ __align__(8) uint64_t mbar[PF_TC_STAGES];
+    __shared__ uint32_t tmem_s;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int m0 = blockIdx.y * 128, n0 = blockIdx.x * 128;
+    auto tile = [&](int s, int o) { return sm + ((size_t)s * 4 + o) * PF_TC_TILE; };
+    const __half *src[4] = {Ahi, Alo, Bhi, Blo};
+
+    if (warp == 0) {
+        const uint32_t dst = (uint32_t)__cvta_generic_to_shared(&tmem_s);
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 128;" ::"r"(dst) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    if (tid == 0) {
+        for (int s = 0; s < PF_TC_STAGES; s++) mbar_init(&mbar[s], 1);
+        mbar_init_fence();
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = tmem_s;
+
+    auto load = [&](int s, int k0) {
+        // 4 tiles x 128 rows x 8 chunks of 16 bytes
+        for (int q = tid; q < 4 * 128 * 8; q += 128) {
+            const int  o = q >> 10, r = (q >> 3) & 127, c = q & 7;
+            const int  lim = o < 2 ? M : N, row = (o < 2 ? m0 : n0) + r;
+            const bool ok = row < lim && k0 + c * 8 < K;
+            const __half *g = src[o] + (ok ? (size_t)row * K + k0 + c * 8 : 0);
+            pf_cp16(tile(s, o) + r * 128 + ((c ^ (r & 7)) << 4), g, ok);
+        }
+    };
+    const int nk = (K + PF_TC_BK - 1) / PF_TC_BK;
+    // instruction descriptor: fp32 accumulate, fp16 A and B, both K-major,
+    // N = 128 (>> 3), M = 128 (>> 4)
+    const uint32_t idesc = (1u << 4) | ((128u >> 3) << 17) | ((128u >> 4) << 24);
+    for (int s = 0; s < PF_TC_STAGES - 1; s++) {
+        if (s < nk) load(s, s * PF_TC_BK);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    }
+    for (int kt = 0; kt < nk; kt++) {
+        const int s = kt % PF_TC_STAGES, nxt = kt + PF_TC_STAGES - 1;
+        if (nxt < nk) {
+            // the stage nxt reuses was read by iteration kt - 1's MMAs
+            if (kt >= 1) mbar_wait<true>(&mbar[(kt - 1) % PF_TC_STAGES], (unsigned)((kt - 1) / PF_TC_STAGES) & 1u, status);
+            load(nxt % PF_TC_STAGES, nxt * PF_TC_BK);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        asm volatile("cp.async.wait_group %0;" ::"n"(PF_TC_STAGES - 1) : "memory");
+        // this thread's copies into stage s are done: hand them to the
+        // tensor core's (async) proxy, then to the issuing thread
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncthreads();
+        if (tid == 0) {
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t a_hi = (uint32_t)__cvta_generic_to_shared(tile(s, 0));
+            const uint32_t a_lo = (uint32_t)__cvta_generic_to_shared(tile(s, 1));
+            const uint32_t b_hi = (uint32_t)__cvta_generic_to_shared(tile(s, 2));
+            const uint32_t b_lo = (uint32_t)__cvta_generic_to_shared(tile(s, 3));
+#pragma unroll
+            for (int k = 0; k < PF_TC_BK / 16; k++) {
+                // K = 16 halves = 32 bytes further along the swizzle atom
+                const uint32_t off = (uint32_t)k * 32;
+                pf_tc_mma(tmem, pf_sdesc(a_hi + off), pf_sdesc(b_hi + off), idesc, (kt | k) ? 1u : 0u);
+                pf_tc_mma(tmem, pf_sdesc(a_hi + off), pf_sdesc(b_lo + off), idesc, 1u);
+                pf_tc_mma(tmem, pf_sdesc(a_lo + off), pf_sdesc(b_hi + off), idesc, 1u);
+            }
+            const uint32_t bar = (uint32_t)__cvta_generic_to_shared(&mbar[s]);
+            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                         : "memory");
+        }
+        __syncwarp();
+    }
+    // the last commit covers every MMA issued before it
+    mbar_wait<true>(&mbar[(nk - 1) % PF_TC_STAGES], (unsigned)((nk - 1) / PF_TC_STAGES) & 1u, status);
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    // warp w reads accumulator lanes 32w..32w+31 (tile rows), 32 columns at a time
+    const int row = m0 + warp * 32 + lane;
+    for (int ch = 0; ch < 4; ch++) {
+        uint32_t v[32];
+        const uint32_t ta = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(ch * 32);
+        asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+                     "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
+                     "%30, %31}, [%32];"
+                     : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+                       "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+                       "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]),
+                       "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]),
+                       "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+                     : "r"(ta)
+                     : "memory");
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        if (row < M) {
+#pragma unroll
+            for (int j = 0; j < 32; j++) {
+                const int col = n0 + ch * 32 + j;
+                if (col < N) {
+                    const size_t e = (size_t)row * ldc + col;
+                    const float  x = __uint_as_float(v[j]);
+                    C[e] = R ? __fadd_rn(R[e], x) : x;
+                }
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 128;" ::"r"(tmem) : "memory");
 }
 
 // --------------------------------------------------------- RoPE, KV, attn --

@@ -2259,7 +2259,10 @@ static int pf_reserve(ecu_ctx *c, int n)
 static int pf_gemm(ecu_ctx *c, const DevMat &m, int n, float *C, const float *R)
 {
     ecu_ctx::Prefill &P = c->pf;
-    k_pf_wsplit<<<8 * c->sms, 256, 0, c->stream>>>(m, P.wh, P.wl);
+    if ((m.layout == LAY_SPLIT4 || m.layout == LAY_SPLIT8) && m.n_in % 32 == 0)
+        k_pf_wsplit_fast<<<8 * c->sms, 128, 0, c->stream>>>(m, P.wh, P.wl);
+    else
+        k_pf_wsplit<<<8 * c->sms, 256, 0, c->stream>>>(m, P.wh, P.wl);
     dim3 grid((unsigned)((m.n_out + PF_BN - 1) / PF_BN), (unsigned)((n + PF_BM - 1) / PF_BM));
     const char *e = getenv("ECU_PF_TC");
     if (!(e && e[0] == '0'))
@@ -2300,6 +2303,8 @@ int ecu_prefill(ecu_ctx *c, const int *tokens, int n, float *out)
     if (c->device >= 32 || !(attr_done.load() & (1u << c->device))) {
         CK(cudaFuncSetAttribute(k_pf_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pf_gemm_smem()));
         CK(cudaFuncSetAttribute(k_pf_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pf_tc_smem()));
+        CK(cudaFuncSetAttribute(k_pf_attn2<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pf_attn2_smem<128>()));
+        CK(cudaFuncSetAttribute(k_pf_attn2<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pf_attn2_smem<64>()));
         if (c->device < 32) attr_done.fetch_or(1u << c->device);
     }
     if (pf_reserve(c, n) != 0) return -1;
@@ -2316,13 +2321,27 @@ int ecu_prefill(ecu_ctx *c, const int *tokens, int n, float *out)
         if (pf_gemm(c, ly.qkv[0], n, P.QKV, nullptr)) return -1;
         k_pf_rope_kv<<<n, 128, 0, c->stream>>>(P.QKV, ldq, g.n_head, g.n_head_kv, hd, pos0, c->rope_cs, ly.bq, ly.bk,
                                                ly.bv, c->kc + li * plane, c->vc + li * plane, g.n_ctx);
-        dim3 ag((unsigned)g.n_head, (unsigned)n);
-        if (hd == 128)
-            k_pf_attn<128><<<ag, 128, 0, c->stream>>>(P.QKV, ldq, g.n_head, g.n_rep, pos0, c->kc + li * plane,
-                                                      c->vc + li * plane, g.n_ctx, kscale, P.ATT);
-        else
-            k_pf_attn<64><<<ag, 64, 0, c->stream>>>(P.QKV, ldq, g.n_head, g.n_rep, pos0, c->kc + li * plane,
-                                                    c->vc + li * plane, g.n_ctx, kscale, P.ATT);
+        const char *ae = getenv("ECU_PF_ATTN");
+        if (PF_QB % g.n_rep == 0 && !(ae && ae[0] == '0')) {
+            // tiled over tokens: 64 query vectors a CTA
+            dim3 ag((unsigned)g.n_head_kv, (unsigned)((n + PF_QB / g.n_rep - 1) / (PF_QB / g.n_rep)));
+            if (hd == 128)
+                k_pf_attn2<128><<<ag, 256, pf_attn2_smem<128>(), c->stream>>>(P.QKV, ldq, n, g.n_head, g.n_rep, pos0,
+                                                                              c->kc + li * plane, c->vc + li * plane,
+                                                                              g.n_ctx, kscale, P.ATT);
+            else
+                k_pf_attn2<64><<<ag, 256, pf_attn2_smem<64>(), c->stream>>>(P.QKV, ldq, n, g.n_head, g.n_rep, pos0,
+                                                                            c->kc + li * plane, c->vc + li * plane,
+                                                                            g.n_ctx, kscale, P.ATT);
+        } else {
+            dim3 ag((unsigned)g.n_head, (unsigned)n);
+            if (hd == 128)
+                k_pf_attn<128><<<ag, 128, 0, c->stream>>>(P.QKV, ldq, g.n_head, g.n_rep, pos0, c->kc + li * plane,
+                                                          c->vc + li * plane, g.n_ctx, kscale, P.ATT);
+            else
+                k_pf_attn<64><<<ag, 64, 0, c->stream>>>(P.QKV, ldq, g.n_head, g.n_rep, pos0, c->kc + li * plane,
+                                                        c->vc + li * plane, g.n_ctx, kscale, P.ATT);
+        }
         k_pf_split<<<4 * c->sms, 256, 0, c->stream>>>(P.ATT, (size_t)n * qd, P.ah, P.al);
         if (pf_gemm(c, ly.o, n, P.X, P.X)) return -1;
         k_pf_norm_split<<<n, 256, 0, c->stream>>>(P.X, ly.ffn_norm, E, g.eps, P.ah, P.al);

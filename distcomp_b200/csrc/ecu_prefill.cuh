@@ -68,6 +68,48 @@ static __global__ void k_pf_split(const float *X, size_t count, __half *hi, __ha
         pf_split(X[e], hi[e], lo[e]);
 }
 
+// Q4_0 (SPLIT4) or Q8_0 (SPLIT8) rows dequantised and split, one thread per
+// 32-element block: the values mat_elem gives, 64-byte stores.
+static __global__ void k_pf_wsplit_fast(DevMat m, __half *hi, __half *lo)
+{
+    const int    nb = m.n_in / 32;
+    const size_t total = (size_t)m.n_out * nb;
+    for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
+        const size_t   row = e / (size_t)nb;
+        const int      b = (int)(e % (size_t)nb);
+        const uint8_t *r = m.data + row * m.row_bytes;
+        float          v[32];
+        if (m.layout == LAY_SPLIT4) {
+            const uint4 q = *reinterpret_cast<const uint4 *>(r + (size_t)b * 16);
+            const float d = f16x(r + (size_t)nb * 16 + 2 * b);
+            const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+                const uint32_t byte = (w[j >> 2] >> (8 * (j & 3))) & 0xFFu;
+                v[j] = __fmul_rn((float)((int)(byte & 0x0F) - 8), d);
+                v[j + 16] = __fmul_rn((float)((int)(byte >> 4) - 8), d);
+            }
+        } else {
+            const uint4 q0 = *reinterpret_cast<const uint4 *>(r + (size_t)b * 16);
+            const uint4 q1 = *reinterpret_cast<const uint4 *>(r + (size_t)(nb + b) * 16);
+            const float d = f16x(r + (size_t)nb * 32 + 2 * b);
+            const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+            for (int j = 0; j < 32; j++) v[j] = __fmul_rn(d, (float)(int8_t)((w[j >> 2] >> (8 * (j & 3))) & 0xFFu));
+        }
+        __align__(16) __half h[32], l[32];
+#pragma unroll
+        for (int j = 0; j < 32; j++) pf_split(v[j], h[j], l[j]);
+        uint4 *ho = reinterpret_cast<uint4 *>(hi + row * m.n_in + (size_t)b * 32);
+        uint4 *lo4 = reinterpret_cast<uint4 *>(lo + row * m.n_in + (size_t)b * 32);
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            ho[j] = reinterpret_cast<const uint4 *>(h)[j];
+            lo4[j] = reinterpret_cast<const uint4 *>(l)[j];
+        }
+    }
+}
+
 // A device weight matrix (any layout) dequantised and split: rows x n_in.
 static __global__ void k_pf_wsplit(DevMat m, __half *hi, __half *lo)
 {
@@ -439,6 +481,107 @@ static __global__ void __launch_bounds__(HD) k_pf_attn(const float *QKV, int ld,
     float o = 0.0f;                               // dim tid
     for (int p = 0; p < np; p++) o = fmaf(sc[p], vb[(size_t)p * HD + tid], o);
     att[(size_t)t * n_head * HD + (size_t)h * HD + tid] = o / l;
+}
+
+// The same attention tiled over tokens: a CTA (256 threads) takes KV head g
+// and 64 / n_rep consecutive tokens, i.e. 64 query vectors (query qi = token
+// qi / n_rep, head g*n_rep + qi % n_rep), and walks the cache 32 positions
+// at a time through shared memory, so every K/V row is read once per 64
+// queries instead of once per query.  Thread tid serves query tid / 4: its 8
+// scores of a chunk (positions tid % 4 + 4j), a running max and sum shared
+// by the query's 4 threads, and 32 output dims (tid % 4 + 4j; HD = 128).
+// Softmax as k_pf_attn: scores * kscale, expf against the running max, one
+// division by the sum at the end.
+#define PF_QB 64
+#define PF_KC 32
+template <int HD>
+__host__ __device__ constexpr size_t pf_attn2_smem()
+{
+    return ((size_t)PF_QB * (HD + 1) + (size_t)PF_KC * (HD + 1) + (size_t)PF_KC * HD + (size_t)PF_QB * (PF_KC + 1)) *
+           sizeof(float);
+}
+
+template <int HD>
+static __global__ void __launch_bounds__(256) k_pf_attn2(const float *QKV, int ld, int n, int n_head, int n_rep,
+                                                          int pos0, const float *kc, const float *vc, int n_ctx,
+                                                          float kscale, float *att)
+{
+    constexpr int DPT = HD / 4;                     // output dims per thread
+    extern __shared__ __align__(16) float pf_att_sm[];
+    // padded rows (HD + 1, 33): the 8 queries of a warp hit 8 banks
+    float *QS = pf_att_sm;                          // [64][HD + 1]
+    float *KS = QS + PF_QB * (HD + 1);              // [32][HD + 1]
+    float *VS = KS + PF_KC * (HD + 1);              // [32][HD]
+    float *PS = VS + PF_KC * HD;                    // [64][33]
+    const int tid = threadIdx.x, g = blockIdx.x, tb = PF_QB / n_rep, t0 = blockIdx.y * tb;
+    const int qi = tid >> 2, sub = tid & 3;
+    const int t = t0 + qi / n_rep, h = g * n_rep + qi % n_rep;
+    const bool qv = t < n;
+    for (int i = tid; i < PF_QB * HD; i += 256) {
+        const int q = i / HD, d = i % HD, tq = t0 + q / n_rep, hq = g * n_rep + q % n_rep;
+        QS[q * (HD + 1) + d] = tq < n ? QKV[(size_t)tq * ld + (size_t)hq * HD + d] : 0.0f;
+    }
+    const int   last = pos0 + min(n, t0 + tb) - 1;      // last key position any query sees
+    const int   mypos = pos0 + t;                        // this query's own position
+    const float *kb = kc + (size_t)g * n_ctx * HD, *vb = vc + (size_t)g * n_ctx * HD;
+    float m_run = -INFINITY, l_run = 0.0f, o[DPT];
+#pragma unroll
+    for (int j = 0; j < DPT; j++) o[j] = 0.0f;
+    for (int c0 = 0; c0 <= last; c0 += PF_KC) {
+        __syncthreads();                                 // previous chunk's K/V/P consumed
+        for (int i = tid; i < PF_KC * HD; i += 256) {
+            const int p = i / HD, d = i % HD, kp = c0 + p;
+            const bool ok = kp <= last;
+            KS[p * (HD + 1) + d] = ok ? kb[(size_t)kp * HD + d] : 0.0f;
+            VS[p * HD + d] = ok ? vb[(size_t)kp * HD + d] : 0.0f;
+        }
+        __syncthreads();
+        float sc[PF_KC / 4];
+#pragma unroll
+        for (int j = 0; j < PF_KC / 4; j++) sc[j] = 0.0f;
+        const float *q = QS + qi * (HD + 1);
+        for (int d = 0; d < HD; d++) {
+            const float qd = q[d];
+#pragma unroll
+            for (int j = 0; j < PF_KC / 4; j++) sc[j] = fmaf(qd, KS[(sub + 4 * j) * (HD + 1) + d], sc[j]);
+        }
+        float cm = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < PF_KC / 4; j++) {
+            const int kp = c0 + sub + 4 * j;
+            sc[j] = (qv && kp <= mypos) ? sc[j] * kscale : -INFINITY;
+            cm = fmaxf(cm, sc[j]);
+        }
+        cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 1));
+        cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 2));
+        const float mnew = fmaxf(m_run, cm);
+        const float f = mnew == -INFINITY ? 1.0f : expf(m_run - mnew);
+        float       ls = 0.0f;
+#pragma unroll
+        for (int j = 0; j < PF_KC / 4; j++) {
+            const float e = sc[j] == -INFINITY ? 0.0f : expf(sc[j] - mnew);
+            PS[qi * (PF_KC + 1) + sub + 4 * j] = e;
+            ls += e;
+        }
+        ls += __shfl_xor_sync(0xffffffffu, ls, 1);
+        ls += __shfl_xor_sync(0xffffffffu, ls, 2);
+        l_run = l_run * f + ls;
+        m_run = mnew;
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < DPT; j++) o[j] *= f;
+        for (int p = 0; p < PF_KC; p++) {
+            const float e = PS[qi * (PF_KC + 1) + p];
+            const float *vr = VS + p * HD + sub;
+#pragma unroll
+            for (int j = 0; j < DPT; j++) o[j] = fmaf(e, vr[4 * j], o[j]);
+        }
+    }
+    if (qv) {
+        float *dst = att + (size_t)t * n_head * HD + (size_t)h * HD + sub;
+#pragma unroll
+        for (int j = 0; j < DPT; j++) dst[4 * j] = o[j] / l_run;
+    }
 }
 
 // h[t][j] = silu(gate) * up from the interleaved gate/up rows (2j, 2j+1).

@@ -792,11 +792,12 @@ template <class F> static int on_stream(ecu_ctx *c, void *stream, F enq)
 
 typedef void (*MegaFn)(MegaArgs);
 
-static MegaFn mega_lookup(int hd, int rep)
+// sys: the tagged words cross GPUs (tensor-parallel ranks): system scope
+static MegaFn mega_lookup(int hd, int rep, bool sys)
 {
-    if (hd == 128 && rep == 4) return k_decode_mega<128, 4>;
-    if (hd == 128 && rep == 8) return k_decode_mega<128, 8>;
-    if (hd == 64 && rep == 4) return k_decode_mega<64, 4>;
+    if (hd == 128 && rep == 4) return sys ? k_decode_mega<128, 4, true> : k_decode_mega<128, 4, false>;
+    if (hd == 128 && rep == 8) return sys ? k_decode_mega<128, 8, true> : k_decode_mega<128, 8, false>;
+    if (hd == 64 && rep == 4) return sys ? k_decode_mega<64, 4, true> : k_decode_mega<64, 4, false>;
     return nullptr;
 }
 
@@ -861,7 +862,7 @@ static int mega_setup(ecu_ctx *c)
     // this rank's query and KV heads (all of them without tensor parallelism)
     const int hd = g.head_dim, qdim = g.n_head * hd, qd_l = tp.nh * hd, kvd_l = tp.nkv * hd;
     const bool bcast = tp.world > 1;          // outputs every rank reads go to every rank
-    MegaFn fn = mega_lookup(hd, g.n_rep);
+    MegaFn fn = mega_lookup(hd, g.n_rep, bcast);
     if (!fn) return no("head_dim / query heads per KV head not instantiated");
     for (auto &ly : c->layers)
         if (ly.qkv.size() != 1 || !ly.gu_fused || !mega_mat_ok(ly.qkv[0]) || !mega_mat_ok(ly.o) ||

@@ -119,9 +119,10 @@ struct MegaArgs {
 // ------------------------------------------------------- tagged vectors --
 // The phases hand vectors to each other without grid barriers: every element
 // is one 8-byte word {float, epoch of the phase that wrote it}, stored and
-// loaded whole (aligned 64-bit relaxed accesses are single-copy atomic; system
-// scope, as tensor-parallel ranks write them into each other's memory over
-// NVLink), so a reader that sees the epoch it expects also sees the value.  A reader spins on words that still carry an
+// loaded whole (aligned 64-bit relaxed accesses are single-copy atomic; GPU
+// scope, or system scope in the instantiation for tensor-parallel ranks,
+// which write into each other's memory over NVLink), so a reader that sees
+// the epoch it expects also sees the value.  A reader spins on words that still carry an
 // older epoch.  Epoch = (launch number mod 2^20) << 12 | (phase + 1): unique
 // within a launch and against the previous one, which wrote every word.
 // Every phase's input depends on all CTAs' output of an earlier phase, so
@@ -132,35 +133,50 @@ __device__ __forceinline__ unsigned ll_epoch(unsigned launch, int phase)
     return ((launch & 0xFFFFFu) << 12) | (unsigned)(phase + 1);
 }
 
+// SYS: system scope (tensor-parallel ranks read and write each other's
+// words over NVLink); otherwise GPU scope.
+template <bool SYS>
 __device__ __forceinline__ void ll_put(unsigned long long *p, float v, unsigned e)
 {
     const unsigned long long w = ((unsigned long long)e << 32) | __float_as_uint(v);
-    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+    if constexpr (SYS)
+        asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+    else
+        asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
 
 // A phase output element: into this rank's vector, or (bcast) into every
 // rank's copy at the same offset.
+template <bool SYS>
 __device__ __forceinline__ void ll_put_out(const MegaArgs &a, bool bcast, unsigned long long *p, float v, unsigned e)
 {
     if (!bcast) {
-        ll_put(p, v, e);
+        ll_put<SYS>(p, v, e);
         return;
     }
     const size_t off = (size_t)(p - a.ll_block);
-    for (int k = 0; k < a.tp_world; k++) ll_put(a.peer[k] + off, v, e);
+    for (int k = 0; k < a.tp_world; k++) ll_put<SYS>(a.peer[k] + off, v, e);
 }
 
+template <bool SYS>
 __device__ __forceinline__ unsigned long long ll_word(const unsigned long long *p)
 {
     unsigned long long w;
-    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    if constexpr (SYS)
+        asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    else
+        asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
     return w;
 }
 
+template <bool SYS>
 __device__ __forceinline__ ulonglong2 ll_word2(const unsigned long long *p)
 {
     ulonglong2 w;
-    asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(w.x), "=l"(w.y) : "l"(p) : "memory");
+    if constexpr (SYS)
+        asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(w.x), "=l"(w.y) : "l"(p) : "memory");
+    else
+        asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(w.x), "=l"(w.y) : "l"(p) : "memory");
     return w;
 }
 
@@ -178,11 +194,12 @@ __device__ __forceinline__ bool ll_keep_waiting(unsigned it, uint64_t &t0, int *
     return true;
 }
 
+template <bool SYS>
 __device__ __forceinline__ float ll_get(const unsigned long long *p, unsigned e, int *status)
 {
-    unsigned long long w = ll_word(p);
+    unsigned long long w = ll_word<SYS>(p);
     uint64_t t0 = 0;
-    for (unsigned it = 1; (unsigned)(w >> 32) != e && ll_keep_waiting(it, t0, status); it++) w = ll_word(p);
+    for (unsigned it = 1; (unsigned)(w >> 32) != e && ll_keep_waiting(it, t0, status); it++) w = ll_word<SYS>(p);
     return __uint_as_float((unsigned)w);
 }
 
@@ -196,7 +213,7 @@ __device__ __forceinline__ bool ll_tags4(const ulonglong2 (&w)[2], unsigned e)
 // Float4s t = t0 + k*stride (k < K, t < nq) of a phase input: tagged (phase
 // in_ep of this launch) or the plain kernel input.  Every load is issued
 // before the first wait, so the K fetches cost one L2 round trip, not K.
-template <int K>
+template <int K, bool SYS>
 __device__ __forceinline__ void input_batch(const MegaArgs &a, const MegaPhase &ph, int t0, int stride, int nq,
                                             unsigned ein, float4 (&v)[K])
 {
@@ -206,8 +223,8 @@ __device__ __forceinline__ void input_batch(const MegaArgs &a, const MegaPhase &
         for (int k = 0; k < K; k++) {
             const int t = t0 + k * stride;
             if (t < nq) {
-                w[k][0] = ll_word2(ph.x_ll + 4 * (size_t)t);
-                w[k][1] = ll_word2(ph.x_ll + 4 * (size_t)t + 2);
+                w[k][0] = ll_word2<SYS>(ph.x_ll + 4 * (size_t)t);
+                w[k][1] = ll_word2<SYS>(ph.x_ll + 4 * (size_t)t + 2);
             }
         }
 #pragma unroll
@@ -216,8 +233,8 @@ __device__ __forceinline__ void input_batch(const MegaArgs &a, const MegaPhase &
             if (t < nq) {
                 uint64_t tw = 0;
                 for (unsigned it = 1; !ll_tags4(w[k], ein) && ll_keep_waiting(it, tw, a.status); it++) {
-                    w[k][0] = ll_word2(ph.x_ll + 4 * (size_t)t);
-                    w[k][1] = ll_word2(ph.x_ll + 4 * (size_t)t + 2);
+                    w[k][0] = ll_word2<SYS>(ph.x_ll + 4 * (size_t)t);
+                    w[k][1] = ll_word2<SYS>(ph.x_ll + 4 * (size_t)t + 2);
                 }
                 v[k] = make_float4(__uint_as_float((unsigned)w[k][0].x), __uint_as_float((unsigned)w[k][0].y),
                                    __uint_as_float((unsigned)w[k][1].x), __uint_as_float((unsigned)w[k][1].y));
@@ -233,10 +250,11 @@ __device__ __forceinline__ void input_batch(const MegaArgs &a, const MegaPhase &
 }
 
 // A tagged word already loaded into w: re-polled until it carries epoch e.
+template <bool SYS>
 __device__ __forceinline__ float ll_settle(const unsigned long long *p, unsigned long long w, unsigned e, int *status)
 {
     uint64_t t0 = 0;
-    for (unsigned it = 1; (unsigned)(w >> 32) != e && ll_keep_waiting(it, t0, status); it++) w = ll_word(p);
+    for (unsigned it = 1; (unsigned)(w >> 32) != e && ll_keep_waiting(it, t0, status); it++) w = ll_word<SYS>(p);
     return __uint_as_float((unsigned)w);
 }
 
@@ -573,6 +591,7 @@ __device__ __forceinline__ void store_digits(const MegaShared &S, int t, float4 
 // (rms_scale's order) straight from registers, warp 0 adds the W terms --
 // the scale k_rmsnorm and k_gemv_fast compute, bit for bit -- then the digit
 // planes of the normed input.
+template <bool SYS>
 __device__ __forceinline__ void norm_prologue(const MegaArgs &a, const MegaPhase &ph, const MegaShared &S, int tid,
                                               int nct, unsigned ein)
 {
@@ -586,7 +605,7 @@ __device__ __forceinline__ void norm_prologue(const MegaArgs &a, const MegaPhase
 #pragma unroll
         for (int k = 0; k < 2; k++)
             if (base + k * nct < nq) wv[k] = __ldg(w4 + base + k * nct);
-        input_batch<2>(a, ph, base, nct, nq, ein, v);
+        input_batch<2, SYS>(a, ph, base, nct, nq, ein, v);
 #pragma unroll
         for (int k = 0; k < 2; k++) {
             const int t = base + k * nct;
@@ -626,6 +645,7 @@ __device__ __forceinline__ void attn_prefetch(const MegaArgs &a, const MegaPhase
 // both row formats: only the innermost loop depends on it.
 // next: the following phase's descriptor when it is attention (its K/V rows
 // are warmed in L2 and the RoPE row staged once the main loop is done).
+template <bool SYS>
 __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShared &S, RingPos &rp_, int p_idx,
                           const MegaPhase *next, int hd)
 {
@@ -645,7 +665,7 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
     // settled after the prologue
     const bool has_res = epi == EPI_ADD && tid < nrows;
     unsigned long long yw = 0;
-    if (has_res && ph.y_ep >= 0) yw = ll_word(a.x_ll + ph.out_base + r0 + tid);
+    if (has_res && ph.y_ep >= 0) yw = ll_word<SYS>(a.x_ll + ph.out_base + r0 + tid);
 
     // ---- prologue: digit planes of every input block -----------------------
     // A CTA without rows reads no input: nothing it writes would tell a later
@@ -654,12 +674,12 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
     const unsigned ein = ll_epoch(S.launch, ph.in_ep);
     if (nrows == 0) {
     } else if (ph.norm) {
-        norm_prologue(a, ph, S, tid, nct, ein);
+        norm_prologue<SYS>(a, ph, S, tid, nct, ein);
     } else {
         const int nq = nb * 8;                          // float4s of x; whole warps (nb % 32 == 0)
         for (int base = tid; base < nq; base += 2 * nct) {
             float4 v[2];
-            input_batch<2>(a, ph, base, nct, nq, ein, v);
+            input_batch<2, SYS>(a, ph, base, nct, nq, ein, v);
 #pragma unroll
             for (int k = 0; k < 2; k++)
                 if (base + k * nct < nq) store_digits(S, base + k * nct, v[k]);
@@ -667,7 +687,7 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
     }
     float yprev = 0.0f;
     if (has_res)
-        yprev = ph.y_ep >= 0 ? ll_settle(a.x_ll + ph.out_base + r0 + tid, yw, ll_epoch(S.launch, ph.y_ep), a.status)
+        yprev = ph.y_ep >= 0 ? ll_settle<SYS>(a.x_ll + ph.out_base + r0 + tid, yw, ll_epoch(S.launch, ph.y_ep), a.status)
                              : __ldcg(ph.y + r0 + tid);
     named_bar(1, nct);
 
@@ -742,7 +762,7 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
     if (epi == EPI_SWIGLU) {
         for (int j = tid; j < nrows / 2; j += nct) {
             const float gs = row_total(S.red, 2 * j, nkg, red4), us = row_total(S.red, 2 * j + 1, nkg, red4);
-            ll_put_out(a, ph.bcast, ph.y_ll + ph.out_base + r0 / 2 + j, silu_mul(gs, us), eout);
+            ll_put_out<SYS>(a, ph.bcast, ph.y_ll + ph.out_base + r0 / 2 + j, silu_mul(gs, us), eout);
         }
         if (det) det[2] = clock64();
         return;
@@ -752,10 +772,10 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
         const float acc = row_total(S.red, r, nkg, red4);
         if (epi == EPI_ADD) {
             const float out = yprev + acc;         // r == tid: nrows <= MEGA_THREADS
-            ll_put_out(a, ph.bcast, ph.y_ll + ph.out_base + r0 + r, out, eout);
+            ll_put_out<SYS>(a, ph.bcast, ph.y_ll + ph.out_base + r0 + r, out, eout);
             if (ph.out_plain) y[r0 + r] = out;
         } else if (epi == EPI_STORE) {
-            ll_put_out(a, ph.bcast, ph.y_ll + ph.out_base + r0 + r, acc, eout);
+            ll_put_out<SYS>(a, ph.bcast, ph.y_ll + ph.out_base + r0 + r, acc, eout);
         } else {
             y[r0 + r] = acc;                       // logits (argmax reads them after its ticket)
         }
@@ -803,13 +823,13 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
             const unsigned e = ll_epoch(S.launch, p_idx);
             const size_t   off = (size_t)(a.arg_ll - a.ll_block) + 2 * (size_t)a.tp_rank;
             for (int k = 0; k < a.tp_world; k++) {
-                ll_put(a.peer[k] + off, bb.v, e);
-                ll_put(a.peer[k] + off + 1, __int_as_float(bb.i), e);
+                ll_put<SYS>(a.peer[k] + off, bb.v, e);
+                ll_put<SYS>(a.peer[k] + off + 1, __int_as_float(bb.i), e);
             }
             ArgBest all{-INFINITY, -1};
             for (int k = 0; k < a.tp_world; k++)
-                all = arg_better(all, ArgBest{ll_get(a.arg_ll + 2 * k, e, a.status),
-                                              __float_as_int(ll_get(a.arg_ll + 2 * k + 1, e, a.status))});
+                all = arg_better(all, ArgBest{ll_get<SYS>(a.arg_ll + 2 * k, e, a.status),
+                                              __float_as_int(ll_get<SYS>(a.arg_ll + 2 * k + 1, e, a.status))});
             bb = all;
         }
         const int tok = bb.i < 0 ? 0 : bb.i;
@@ -825,7 +845,7 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
 // Attention work item (KV head g, position split sp) = this CTA's index;
 // query head h of the group on warp h.  Same arithmetic per split as
 // k_attention; partials go to global memory for the merge phase.
-template <int HD, int NREP>
+template <int HD, int NREP, bool SYS>
 __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const MegaShared &S, int &att_sb, int &merges,
                                int p_idx)
 {
@@ -879,8 +899,8 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
         if (i < NQP) {
             const int h = i / (HD / 2), j = i % (HD / 2), row = (g * NREP + h) * HD;
             const unsigned long long *p0 = a.qkv_ll + row + j, *p1 = p0 + HD / 2;
-            const unsigned long long w0 = ll_word(p0), w1 = ll_word(p1);
-            float x0 = ll_settle(p0, w0, ein, a.status), x1 = ll_settle(p1, w1, ein, a.status);
+            const unsigned long long w0 = ll_word<SYS>(p0), w1 = ll_word<SYS>(p1);
+            float x0 = ll_settle<SYS>(p0, w0, ein, a.status), x1 = ll_settle<SYS>(p1, w1, ein, a.status);
             if (ph.bq) { x0 = __fadd_rn(x0, ph.bq[row + j]); x1 = __fadd_rn(x1, ph.bq[row + j + HD / 2]); }
             rope_pair(x0, x1, cs_s[2 * j], cs_s[2 * j + 1]);
             q_s[h * HD + j] = x0;
@@ -889,9 +909,10 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
             const int j = i - NQP, kr = qdim + g * HD, vr = qdim + kvdim + g * HD;
             const unsigned long long *pk0 = a.qkv_ll + kr + j, *pk1 = pk0 + HD / 2;
             const unsigned long long *pv0 = a.qkv_ll + vr + j, *pv1 = pv0 + HD / 2;
-            const unsigned long long wk0 = ll_word(pk0), wk1 = ll_word(pk1), wv0 = ll_word(pv0), wv1 = ll_word(pv1);
-            float k0 = ll_settle(pk0, wk0, ein, a.status), k1 = ll_settle(pk1, wk1, ein, a.status);
-            float v0 = ll_settle(pv0, wv0, ein, a.status), v1 = ll_settle(pv1, wv1, ein, a.status);
+            const unsigned long long wk0 = ll_word<SYS>(pk0), wk1 = ll_word<SYS>(pk1), wv0 = ll_word<SYS>(pv0),
+                                     wv1 = ll_word<SYS>(pv1);
+            float k0 = ll_settle<SYS>(pk0, wk0, ein, a.status), k1 = ll_settle<SYS>(pk1, wk1, ein, a.status);
+            float v0 = ll_settle<SYS>(pv0, wv0, ein, a.status), v1 = ll_settle<SYS>(pv1, wv1, ein, a.status);
             if (ph.bk) { k0 = __fadd_rn(k0, ph.bk[g * HD + j]); k1 = __fadd_rn(k1, ph.bk[g * HD + j + HD / 2]); }
             if (ph.bv) { v0 = __fadd_rn(v0, ph.bv[g * HD + j]); v1 = __fadd_rn(v1, ph.bv[g * HD + j + HD / 2]); }
             rope_pair(k0, k1, cs_s[2 * j], cs_s[2 * j + 1]);
@@ -1075,7 +1096,7 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
         const int hh = i / HD, d = i % HD;
         float o = 0.0f;
         for (int r = 0; r < ns; r++) o = fmaf(gat[r * PER + hh * (HD + 4) + d], wsp[hh][r], o);
-        ll_put_out(a, ph.bcast, ph.y_ll + (g * NREP + hh) * HD + d, o * invl[hh], eout);
+        ll_put_out<SYS>(a, ph.bcast, ph.y_ll + (g * NREP + hh) * HD + d, o * invl[hh], eout);
     }
     // profiling: when KV head 0's merge was done (whichever CTA did it)
     if (a.phase_detail && g == 0 && tid == 0) a.phase_detail[(size_t)p_idx * 4 + 3] = globaltimer_ns();
@@ -1098,6 +1119,7 @@ __device__ __forceinline__ void attn_prefetch(const MegaArgs &a, const MegaPhase
     prefetch_l2(ph.vc + off, bytes);
 }
 
+template <bool SYS>
 __device__ void mega_embed(const MegaArgs &a, const MegaShared &S, int p_idx)
 {
     const unsigned eout = ll_epoch(S.launch, p_idx);
@@ -1110,11 +1132,11 @@ __device__ void mega_embed(const MegaArgs &a, const MegaShared &S, int p_idx)
     const size_t base = (size_t)tok * (size_t)n;
     for (int i = blockIdx.x * nct + threadIdx.x; i < n; i += gridDim.x * nct) {
         const size_t e = base + (size_t)i;
-        ll_put(a.x_ll + i, mat_elem(a.emb, (int)(e / (size_t)a.emb.n_in), (int)(e % (size_t)a.emb.n_in)), eout);
+        ll_put<SYS>(a.x_ll + i, mat_elem(a.emb, (int)(e / (size_t)a.emb.n_in), (int)(e % (size_t)a.emb.n_in)), eout);
     }
 }
 
-template <int HD, int NREP>
+template <int HD, int NREP, bool SYS>
 __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a)
 {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -1188,11 +1210,11 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a)
         }
         const int kind = ph.kind;
         if (kind == PH_GEMV) {
-            mega_gemv(a, ph, S, rpos, p, ph.next_attn ? &ph_s[(p + 1) & 1] : nullptr, HD);
+            mega_gemv<SYS>(a, ph, S, rpos, p, ph.next_attn ? &ph_s[(p + 1) & 1] : nullptr, HD);
         } else if (kind == PH_ATTN) {
-            mega_attention<HD, NREP>(a, ph, S, att_sb, merges, p);
+            mega_attention<HD, NREP, SYS>(a, ph, S, att_sb, merges, p);
         } else {
-            mega_embed(a, S, p);
+            mega_embed<SYS>(a, S, p);
         }
         // the CTA's warps leave a phase together: shared buffers (row
         // partials, digit planes / K/V rows, the descriptor double buffer)

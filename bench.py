@@ -6,8 +6,9 @@
 Workload (the 8B decode configuration): dim 4096, 32 layers, 32/8 heads,
 FFN 14336, vocab 128256, RoPE theta 5e5; N(0,0.02) weights quantised to
 Q4_0 (embedding and head Q8_0), generated on the GPU from a fixed seed;
-KV cache fp32 for 4096 positions.  A 512-token random prompt is fed
-first, then W untimed and K timed greedy decode steps.  One step = one
+KV cache fp32 for 4096 positions.  A 512-token random prompt goes in
+first through ecu_prefill (timed once: the `prefill` field), then W untimed
+and K timed greedy decode steps.  One step = one
 token through embed -> 32 layers -> head -> argmax, the next token fed back
 on the device (one persistent-kernel launch per token).  The 4.5 GB of weights
 stream from HBM every step, far above the 126 MB L2, so no flush is needed.

@@ -19,8 +19,14 @@ enum GgmlType : int {
 //   SPLIT4 row: [16 code bytes of block 0..nb-1][nb fp16 scales][pad to 16 B]
 //   SPLIT8 row: [code bytes 0..15 of block 0..nb-1][code bytes 16..31 of
 //                block 0..nb-1][nb fp16 scales][pad to 16 B]
+// SPLITK4 does the same for Q4_K (256-weight super-blocks of 144 bytes:
+// d, dmin, 12 bytes of 6-bit scales/mins, 128 code bytes): every 32-weight
+// sub-block gets 16 code bytes in the Q4_0 nibble order (byte l: weight l in
+// the low nibble, weight l+16 in the high one), then the 16-byte headers:
+//   SPLITK4 row: [16 code bytes of sub-block 0..nb-1][nb/8 headers (d, dmin,
+//                scales[12])]
 // Values are untouched; only the byte order within a row changes.
-enum Layout : int { LAY_RAW = 0, LAY_SPLIT4 = 1, LAY_SPLIT8 = 2 };
+enum Layout : int { LAY_RAW = 0, LAY_SPLIT4 = 1, LAY_SPLIT8 = 2, LAY_SPLITK4 = 3 };
 
 __host__ __device__ inline int blk_elems(int t)
 {
@@ -56,7 +62,10 @@ inline size_t type_nbytes(int t, size_t n)
     return b ? n / (size_t)blk_elems(t) * (size_t)b : 0;
 }
 
-// A weight matrix resident on the device: n_out rows of n_in inputs.
+// A weight matrix resident on the device: n_out rows of n_in inputs.  A
+// wide matrix is kept as nseg column segments (inputs [s*n_in/nseg, ..)),
+// each a complete matrix of its own, back to back seg_bytes apart; row_bytes
+// is then a segment's row.
 struct DevMat {
     int            type = -1;
     int            layout = LAY_RAW;
@@ -65,6 +74,8 @@ struct DevMat {
     size_t         total = 0;          // elements of the source tensor
     const uint8_t *data = nullptr;     // device
     bool           zero = false;       // matvec yields zeros (engine.c:317-320 rule)
+    int            nseg = 1;
+    size_t         seg_bytes = 0;
 };
 
 // Per-step device state shared by the kernels of one context.

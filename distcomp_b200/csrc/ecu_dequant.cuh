@@ -130,17 +130,32 @@ __device__ __forceinline__ float dq_elem(int t, const uint8_t *b, int i)
 __device__ __forceinline__ float mat_elem(const DevMat &m, int row, int k)
 {
     const uint8_t *r = m.data + (size_t)row * m.row_bytes;
+    int n_in = m.n_in;
+    if (m.nseg > 1) {                                // column segment of k
+        n_in /= m.nseg;
+        r += (size_t)(k / n_in) * m.seg_bytes;
+        k %= n_in;
+    }
     if (m.type == GT_F32) return reinterpret_cast<const float *>(r)[k];
     if (m.type == GT_F16) return f16x(r + 2 * (size_t)k);
+    if (m.layout == LAY_SPLITK4) {                   // Q4_K sub-block codes | headers
+        const int      nb = n_in / 32, sb = k / 32, i = k % 32;
+        const uint8_t *q = r + (size_t)sb * 16, *h = r + (size_t)nb * 16 + (size_t)(sb >> 3) * 16;
+        const int      qq = i < 16 ? (q[i] & 0x0F) : (q[i - 16] >> 4);
+        int sc, mn;
+        kq_scale_min(sb & 7, h + 4, sc, mn);         // gguf.c:569-589 arithmetic
+        const float dd = __fmul_rn(f16x(h), (float)sc), mm = __fmul_rn(f16x(h + 2), (float)mn);
+        return __fsub_rn(__fmul_rn(dd, (float)qq), mm);
+    }
     const int be = blk_elems(m.type), bi = k / be, i = k % be;
     if (m.layout == LAY_SPLIT4) {                    // Q4_0 codes | scales
-        const int nb = m.n_in / 32;
+        const int nb = n_in / 32;
         const uint8_t *q = r + (size_t)bi * 16;
         int qq = i < 16 ? (q[i] & 0x0F) : (q[i - 16] >> 4);
         return __fmul_rn((float)(qq - 8), f16x(r + (size_t)nb * 16 + 2 * bi));
     }
     if (m.layout == LAY_SPLIT8) {    // Q8_0 codes 0..15 | codes 16..31 | scales
-        const int nb = m.n_in / 32;
+        const int nb = n_in / 32;
         const uint8_t c = i < 16 ? r[(size_t)bi * 16 + i] : r[(size_t)(nb + bi) * 16 + i - 16];
         return __fmul_rn(f16x(r + (size_t)nb * 32 + 2 * bi), (float)(int8_t)c);
     }

@@ -115,8 +115,24 @@ static int num_sms(int dev)
 
 static bool fast_ok(const DevMat &m)
 {
-    return !m.zero && (m.layout == LAY_SPLIT4 || m.layout == LAY_SPLIT8) && m.n_in % 1024 == 0 &&
-           m.n_in / 1024 <= FAST_MAX_NKG;
+    return !m.zero && m.nseg == 1 && (m.layout == LAY_SPLIT4 || m.layout == LAY_SPLIT8 || m.layout == LAY_SPLITK4) &&
+           m.n_in % 1024 == 0 && m.n_in / 1024 <= FAST_MAX_NKG;
+}
+
+// Inputs of one column segment at most: the persistent step's digit planes
+// hold this many.
+#define SEG_MAX_IN (MEGA_MAX_NB * 32)
+
+// Column segment s of m as a matrix of its own.
+static DevMat seg_view(const DevMat &m, int s)
+{
+    DevMat v = m;
+    v.nseg = 1;
+    v.seg_bytes = 0;
+    v.n_in = m.n_in / m.nseg;
+    v.total = (size_t)v.n_in * m.n_out;
+    if (m.data) v.data = m.data + (size_t)s * m.seg_bytes;
+    return v;
 }
 
 // Largest dynamic shared memory a fast-GEMV launch may ask for: the
@@ -240,6 +256,10 @@ static void fast_attrs_all()
     fast_attr_once<8, false, EPI_SWIGLU>(); fast_attr_once<8, false, EPI_ARGMAX>();
     fast_attr_once<8, true, EPI_STORE>(); fast_attr_once<8, true, EPI_ADD>();
     fast_attr_once<8, true, EPI_SWIGLU>(); fast_attr_once<8, true, EPI_ARGMAX>();
+    fast_attr_once<12, false, EPI_STORE>(); fast_attr_once<12, false, EPI_ADD>();
+    fast_attr_once<12, false, EPI_SWIGLU>(); fast_attr_once<12, false, EPI_ARGMAX>();
+    fast_attr_once<12, true, EPI_STORE>(); fast_attr_once<12, true, EPI_ADD>();
+    fast_attr_once<12, true, EPI_SWIGLU>(); fast_attr_once<12, true, EPI_ARGMAX>();
 }
 
 template <int FMT, bool NORM, int EPI>
@@ -283,6 +303,25 @@ static void enqueue_gemv(Launcher &L, int sms, const DevMat &m, const float *x, 
                          float eps, float *y, int epi, const GemvScratch &s, GemvArgs a,
                          const DevMat *next = nullptr, int next_epi = EPI_STORE)
 {
+    if (m.nseg > 1) {
+        // column segments (EPI_STORE / EPI_ADD without a norm prologue): the
+        // first stores or adds W_0 x_0, the others add W_s x_s
+        const char *kind = L.kind;
+        for (int si = 0; si < m.nseg; si++) {
+            const DevMat v = seg_view(m, si);
+            const DevMat vn = si + 1 < m.nseg ? seg_view(m, si + 1) : DevMat{};
+            const bool   last = si + 1 == m.nseg;
+            L.kind = kind;
+            enqueue_gemv(L, sms, v, x + (size_t)si * v.n_in, nullptr, eps, y, si == 0 ? epi : EPI_ADD, s, a,
+                         last ? next : &vn, last ? next_epi : EPI_ADD);
+        }
+        return;
+    }
+    DevMat nv;
+    if (next && next->nseg > 1) {
+        nv = seg_view(*next, 0);
+        next = &nv;
+    }
     if (next && fast_ok(*next) && next->data) {
         const FastPlan np = plan_fast(*next, next_epi, sms);
         a.pf_ptr = next->data;
@@ -310,6 +349,9 @@ static void enqueue_gemv(Launcher &L, int sms, const DevMat &m, const float *x, 
         if (m.layout == LAY_SPLIT4) {
             if (norm) launch_fast_e<4, true>(L, a, p, epi);
             else launch_fast_e<4, false>(L, a, p, epi);
+        } else if (m.layout == LAY_SPLITK4) {
+            if (norm) launch_fast_e<12, true>(L, a, p, epi);
+            else launch_fast_e<12, false>(L, a, p, epi);
         } else {
             if (norm) launch_fast_e<8, true>(L, a, p, epi);
             else launch_fast_e<8, false>(L, a, p, epi);
@@ -456,7 +498,7 @@ static size_t align16(size_t v) { return (v + 15) & ~(size_t)15; }
 // Device row length of a matrix of type t with n_in inputs in `layout`.
 static size_t dev_row_bytes(int t, int n_in, int layout)
 {
-    if (layout == LAY_SPLIT4) return align16((size_t)n_in / 32 * 18);
+    if (layout == LAY_SPLIT4 || layout == LAY_SPLITK4) return align16((size_t)n_in / 32 * 18);
     if (layout == LAY_SPLIT8) return align16((size_t)n_in / 32 * 34);
     if (t == GT_F32) return (size_t)n_in * 4;
     if (t == GT_F16) return (size_t)n_in * 2;
@@ -468,8 +510,31 @@ static int choose_layout(int t, int n_in)
     if (n_in % 1024 == 0 && n_in / 1024 <= FAST_MAX_NKG) {
         if (t == GT_Q4_0) return LAY_SPLIT4;
         if (t == GT_Q8_0) return LAY_SPLIT8;
+        if (t == GT_Q4_K) return LAY_SPLITK4;
     }
     return LAY_RAW;
+}
+
+// Device shape of a matrix: its layout, column segments (allow_seg: a matrix
+// wider than SEG_MAX_IN inputs is cut into equal segments of whole 1024-input
+// groups when its segments take a fast layout) and a segment's row bytes.
+struct MatShape {
+    int    layout, nseg;
+    size_t row_bytes;
+};
+
+static MatShape mat_shape(int t, int n_in, bool allow_split, bool allow_seg)
+{
+    MatShape s{allow_split ? choose_layout(t, n_in) : LAY_RAW, 1, 0};
+    if (allow_split && allow_seg && n_in > SEG_MAX_IN) {
+        const int ns = (n_in + SEG_MAX_IN - 1) / SEG_MAX_IN;
+        if (n_in % (1024 * ns) == 0 && choose_layout(t, n_in / ns) != LAY_RAW) {
+            s.nseg = ns;
+            s.layout = choose_layout(t, n_in / ns);
+        }
+    }
+    s.row_bytes = dev_row_bytes(t, n_in / s.nseg, s.layout);
+    return s;
 }
 
 // Zero-output rule of the reference matvec: a quantised tensor whose n_in
@@ -490,33 +555,46 @@ static int upload_rows(ecu_ctx *c, const EcuTensor *src, int n_in, int rows, Dev
 {
     if (m.zero) return 0;
     const size_t src_row = (size_t)ecu_type_nbytes(src->type, (size_t)n_in);
-    const size_t nbytes = src_row * (size_t)rows;
-    CK(cudaMemcpyAsync(stage, src->data + src_row0 * src_row, nbytes, cudaMemcpyHostToDevice, c->stream));
-    const int nb = n_in / 32;
-    const int grid = 4 * c->sms, blk = 256;
-    uint8_t  *dst = const_cast<uint8_t *>(m.data);
-    if (m.layout == LAY_SPLIT4)
-        k_repack_q4_0<<<grid, blk, 0, c->stream>>>(stage, nb, rows, dst, m.row_bytes, row0, rstride);
-    else if (m.layout == LAY_SPLIT8)
-        k_repack_q8_0<<<grid, blk, 0, c->stream>>>(stage, nb, rows, dst, m.row_bytes, row0, rstride);
-    else
-        k_copy_rows<<<grid, blk, 0, c->stream>>>(stage, src_row, rows, dst, m.row_bytes, row0, rstride);
-    CK(cudaGetLastError());
-    CK(cudaStreamSynchronize(c->stream));   // the staging buffer is reused
+    const int    si = n_in / m.nseg;                          // inputs of a segment
+    const size_t seg_src = (size_t)ecu_type_nbytes(src->type, (size_t)si);
+    const int    grid = 4 * c->sms, blk = 256;
+    for (int sg = 0; sg < m.nseg; sg++) {
+        // segment sg's part of every source row, packed rows of seg_src bytes
+        const uint8_t *from = src->data + src_row0 * src_row + (size_t)sg * seg_src;
+        if (m.nseg == 1)
+            CK(cudaMemcpyAsync(stage, from, src_row * (size_t)rows, cudaMemcpyHostToDevice, c->stream));
+        else
+            CK(cudaMemcpy2DAsync(stage, seg_src, from, src_row, seg_src, (size_t)rows, cudaMemcpyHostToDevice,
+                                 c->stream));
+        uint8_t *dst = const_cast<uint8_t *>(m.data) + (size_t)sg * m.seg_bytes;
+        if (m.layout == LAY_SPLIT4)
+            k_repack_q4_0<<<grid, blk, 0, c->stream>>>(stage, si / 32, rows, dst, m.row_bytes, row0, rstride);
+        else if (m.layout == LAY_SPLIT8)
+            k_repack_q8_0<<<grid, blk, 0, c->stream>>>(stage, si / 32, rows, dst, m.row_bytes, row0, rstride);
+        else if (m.layout == LAY_SPLITK4)
+            k_repack_q4_k<<<grid, blk, 0, c->stream>>>(stage, si / 256, rows, dst, m.row_bytes, row0, rstride);
+        else
+            k_copy_rows<<<grid, blk, 0, c->stream>>>(stage, seg_src, rows, dst, m.row_bytes, row0, rstride);
+        CK(cudaGetLastError());
+        CK(cudaStreamSynchronize(c->stream));   // the staging buffer is reused
+    }
     return 0;
 }
 
-static DevMat make_mat(ecu_ctx *c, int type, int n_in, int n_out, bool allow_split)
+static DevMat make_mat(ecu_ctx *c, int type, int n_in, int n_out, bool allow_split, bool allow_seg = false)
 {
     DevMat m;
     m.type = type;
     m.n_in = n_in;
     m.n_out = n_out;
     m.zero = zero_rule(type, n_in);
-    m.layout = allow_split ? choose_layout(type, n_in) : LAY_RAW;
-    m.row_bytes = dev_row_bytes(type, n_in, m.layout);
+    const MatShape sh = mat_shape(type, n_in, allow_split, allow_seg && !m.zero);
+    m.layout = sh.layout;
+    m.nseg = sh.nseg;
+    m.row_bytes = sh.row_bytes;
+    m.seg_bytes = m.row_bytes * (size_t)n_out;
     m.total = (size_t)n_in * n_out;
-    if (!m.zero) m.data = c->dalloc<uint8_t>(m.row_bytes * (size_t)n_out);
+    if (!m.zero) m.data = c->dalloc<uint8_t>(m.seg_bytes * (size_t)m.nseg);
     return m;
 }
 
@@ -806,11 +884,14 @@ static size_t mega_smem_total(int red_floats, unsigned ring_bytes, unsigned unio
     return mega_smem_plan(red_floats, ring_bytes, union_bytes).total;
 }
 
-// Q4_0 rows in SPLIT4 or Q8_0 rows in SPLIT8, n_in a multiple of 1024.
+// Q4_0 rows in SPLIT4, Q8_0 rows in SPLIT8 or Q4_K rows in SPLITK4, n_in
+// (of a column segment) a multiple of 1024.
 static bool mega_mat_ok(const DevMat &m)
 {
-    return fast_ok(m) && m.n_in / 32 <= MEGA_MAX_NB && m.row_bytes <= MEGA_RING_BYTES / 2 &&
-           ((m.type == GT_Q4_0 && m.layout == LAY_SPLIT4) || (m.type == GT_Q8_0 && m.layout == LAY_SPLIT8));
+    const DevMat v = m.nseg > 1 ? seg_view(m, 0) : m;
+    return fast_ok(v) && v.n_in / 32 <= MEGA_MAX_NB && v.row_bytes <= MEGA_RING_BYTES / 2 &&
+           ((v.type == GT_Q4_0 && v.layout == LAY_SPLIT4) || (v.type == GT_Q8_0 && v.layout == LAY_SPLIT8) ||
+            (v.type == GT_Q4_K && v.layout == LAY_SPLITK4));
 }
 
 static MegaPhase mega_gemv_phase(const DevMat &m, int grid, unsigned stage_bytes, int norm, int epi,
@@ -818,7 +899,7 @@ static MegaPhase mega_gemv_phase(const DevMat &m, int grid, unsigned stage_bytes
 {
     MegaPhase p = {};
     p.kind = PH_GEMV;
-    p.fmt = m.layout == LAY_SPLIT4 ? 4 : 8;
+    p.fmt = m.layout == LAY_SPLIT4 ? 4 : m.layout == LAY_SPLITK4 ? 12 : 8;
     p.norm = norm;
     p.epi = epi;
     p.in_ep = p.y_ep = -1;                           // plain input / residual unless set
@@ -867,9 +948,9 @@ static int mega_setup(ecu_ctx *c)
     for (auto &ly : c->layers)
         if (ly.qkv.size() != 1 || !ly.gu_fused || !mega_mat_ok(ly.qkv[0]) || !mega_mat_ok(ly.o) ||
             !mega_mat_ok(ly.gu) || !mega_mat_ok(ly.d))
-            return no("a layer matrix is not Q4_0/Q8_0 in a fast layout");
+            return no("a layer matrix is not Q4_0/Q8_0/Q4_K in a fast layout");
     const bool full = c->stage == ECU_STAGE_FULL;
-    if (full && !mega_mat_ok(c->out)) return no("output head not Q4_0/Q8_0 in a fast layout");
+    if (full && !mega_mat_ok(c->out)) return no("output head not Q4_0/Q8_0/Q4_K in a fast layout");
     int coop = 0;
     cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, c->device);
     if (!coop) return no("no cooperative launch");
@@ -882,6 +963,7 @@ static int mega_setup(ecu_ctx *c)
     if (const char *r = getenv("ECU_MEGA_RING_KB")) ring_total = (size_t)std::max(32, std::min(200, atoi(r))) * 1024;
     if (nst > MEGA_MAX_STAGES) return no("too many ring stages");
     const unsigned stage_bytes = (unsigned)(ring_total / nst) & ~127u;
+    // (row_bytes and n_in / nseg are those of a column segment)
     for (auto &ly : c->layers)
         if (ly.qkv[0].row_bytes > stage_bytes || ly.o.row_bytes > stage_bytes || ly.gu.row_bytes > stage_bytes ||
             ly.d.row_bytes > stage_bytes)
@@ -896,7 +978,7 @@ static int mega_setup(ecu_ctx *c)
     un = std::max(un, (size_t)g.n_embd / 32 * 28 * sizeof(int) + 2 * (size_t)g.n_embd * sizeof(float));
     for (auto &ly : c->layers)
         for (const DevMat *m : {&ly.qkv[0], &ly.o, &ly.gu, &ly.d})
-            un = std::max(un, (size_t)m->n_in / 32 * 28 * sizeof(int));
+            un = std::max(un, (size_t)(m->n_in / m->nseg) / 32 * 28 * sizeof(int));
     if (full) un = std::max(un, (size_t)c->out.n_in / 32 * 28 * sizeof(int));
     int n_split = std::min(MEGA_MAX_SPLIT, grid / tp.nkv);
     n_split = std::min(n_split, (int)(un / ((size_t)g.n_rep * (hd + 4) * sizeof(float))));
@@ -935,6 +1017,25 @@ static int mega_setup(ecu_ctx *c)
         x_w = (int)ph.size();
         add(p, "embed", 8.0 * g.n_embd + (double)ecu_type_nbytes(c->emb.type, (size_t)g.n_embd));
     }
+    // a residual-adding GEMV (attn_output, ffn_down): one phase per column
+    // segment, each adding its W_s x_s to the residual the previous one wrote
+    auto add_resid = [&](const DevMat &m, const char *kind, const float *x, unsigned long long *xin, int in_ep,
+                         int out_plain) {
+        for (int si = 0; si < m.nseg; si++) {
+            const DevMat v = m.nseg > 1 ? seg_view(m, si) : m;
+            MegaPhase    p = mega_gemv_phase(v, grid, stage_bytes, 0, EPI_ADD, x + (size_t)si * v.n_in, nullptr,
+                                             c->state, nullptr);
+            p.in_ep = in_ep;
+            p.x_ll = xin + (size_t)si * v.n_in;
+            p.y_ep = x_w;
+            p.y_ll = x_ll;
+            p.out_base = tp.rank * tp.ne;
+            p.bcast = bcast;
+            p.out_plain = si + 1 == m.nseg ? out_plain : 0;
+            x_w = (int)ph.size();
+            add(p, kind, gemv_bytes(v, EPI_ADD));
+        }
+    };
     const size_t plane = (size_t)tp.nkv * g.n_ctx * hd;
     for (size_t li = 0; li < c->layers.size(); li++) {
         LayerDev &ly = c->layers[li];
@@ -957,15 +1058,7 @@ static int mega_setup(ecu_ctx *c)
         at.bcast = bcast;
         const int p_at = (int)ph.size();
         add(at, "attention", -1.0);                 // position dependent: filled in by the profile
-        MegaPhase o = mega_gemv_phase(ly.o, grid, stage_bytes, 0, EPI_ADD, c->att, nullptr, c->state, nullptr);
-        o.in_ep = p_at;
-        o.x_ll = att_ll;
-        o.y_ep = x_w;
-        o.y_ll = x_ll;
-        o.out_base = tp.rank * tp.ne;
-        o.bcast = bcast;
-        x_w = (int)ph.size();
-        add(o, "gemv_o", gemv_bytes(ly.o, EPI_ADD));
+        add_resid(ly.o, "gemv_o", c->att, att_ll, p_at, 0);
         MegaPhase gu = mega_gemv_phase(ly.gu, grid, stage_bytes, 1, EPI_SWIGLU, c->state, ly.ffn_norm, c->h, nullptr);
         gu.in_ep = x_w;
         gu.x_ll = x_ll;
@@ -974,16 +1067,7 @@ static int mega_setup(ecu_ctx *c)
         gu.bcast = bcast;
         const int p_gu = (int)ph.size();
         add(gu, "gemv_gate_up", gemv_bytes(ly.gu, EPI_SWIGLU));
-        MegaPhase d = mega_gemv_phase(ly.d, grid, stage_bytes, 0, EPI_ADD, c->h, nullptr, c->state, nullptr);
-        d.in_ep = p_gu;
-        d.x_ll = h_ll;
-        d.y_ep = x_w;
-        d.y_ll = x_ll;
-        d.out_base = tp.rank * tp.ne;
-        d.bcast = bcast;
-        d.out_plain = (!full && last) ? 1 : 0;     // a LAYERS stage's output state
-        x_w = (int)ph.size();
-        add(d, "gemv_down", gemv_bytes(ly.d, EPI_ADD));
+        add_resid(ly.d, "gemv_down", c->h, h_ll, p_gu, (!full && last) ? 1 : 0);   // out_plain: a LAYERS stage's output state
     }
     if (full) {
         MegaPhase hp = mega_gemv_phase(c->out, grid, stage_bytes, 1, EPI_ARGMAX, c->state, c->out_norm, c->logits, xn_tmp);
@@ -1362,15 +1446,15 @@ size_t ecu_ctx_bytes(const ecu_model *m, int stage, int first, int last, int n_c
     StageTensors st;
     if (stage_tensors(m, g, stage, first, last, &st, nullptr, 0) != 0) return 0;
     size_t b = 0;
-    auto mat = [&](const EcuTensor *t, int n_in, int n_out) {
-        int lay = choose_layout((int)t->type, n_in);
-        b += dev_row_bytes((int)t->type, n_in, lay) * (size_t)n_out;
+    auto mat = [&](const EcuTensor *t, int n_in, int n_out, bool seg = false) {
+        const MatShape sh = mat_shape((int)t->type, n_in, true, seg);
+        b += sh.row_bytes * (size_t)n_out * (size_t)sh.nseg;
     };
     const int hd = g.head_dim, qd = g.n_head * hd, kvd = g.n_head_kv * hd;
     for (auto &l : st.layers) {
         mat(l.q, g.n_embd, qd); mat(l.k, g.n_embd, kvd); mat(l.v, g.n_embd, kvd);
-        mat(l.o, qd, g.n_embd); mat(l.g, g.n_embd, g.n_ff); mat(l.u, g.n_embd, g.n_ff);
-        mat(l.d, g.n_ff, g.n_embd);
+        mat(l.o, qd, g.n_embd, true); mat(l.g, g.n_embd, g.n_ff); mat(l.u, g.n_embd, g.n_ff);
+        mat(l.d, g.n_ff, g.n_embd, true);
         b += (size_t)(2 * g.n_embd + qd + 2 * kvd) * 4;
     }
     b += 2 * st.layers.size() * (size_t)g.n_ctx * kvd * 4;          // KV cache
@@ -1644,7 +1728,7 @@ static int ctx_open_impl(ecu_ctx **out, const ecu_model *m, int stage, int first
                     c->srcs.push_back({nm, mm, 0, 1, (size_t)g.n_embd * rows[k], g.n_embd});
                 }
             }
-            ly.o = make_mat(c.get(), (int)l.o->type, qd, tp.ne, true);
+            ly.o = make_mat(c.get(), (int)l.o->type, qd, tp.ne, true, true);
             if (!ly.o.zero && !ly.o.data) return fail_oom("attn_output");
             if (upload_rows(c.get(), l.o, qd, tp.ne, ly.o, 0, 1, stage_buf, (size_t)tp.rank * tp.ne)) return -1;
             snprintf(nm, sizeof nm, "blk.%d.attn_output.weight", li);
@@ -1675,7 +1759,7 @@ static int ctx_open_impl(ecu_ctx **out, const ecu_model *m, int stage, int first
                 snprintf(nm, sizeof nm, "blk.%d.ffn_gate.weight", li); c->srcs.push_back({nm, ly.g, 0, 1, (size_t)g.n_embd * g.n_ff, g.n_embd});
                 snprintf(nm, sizeof nm, "blk.%d.ffn_up.weight", li); c->srcs.push_back({nm, ly.u, 0, 1, (size_t)g.n_embd * g.n_ff, g.n_embd});
             }
-            ly.d = make_mat(c.get(), (int)l.d->type, g.n_ff, tp.ne, true);
+            ly.d = make_mat(c.get(), (int)l.d->type, g.n_ff, tp.ne, true, true);
             if (!ly.d.zero && !ly.d.data) return fail_oom("ffn_down");
             if (upload_rows(c.get(), l.d, g.n_ff, tp.ne, ly.d, 0, 1, stage_buf, (size_t)tp.rank * tp.ne)) return -1;
             snprintf(nm, sizeof nm, "blk.%d.ffn_down.weight", li);
@@ -2119,7 +2203,7 @@ int ecu_matvec(unsigned type, const void *w_raw, int n_in, int n_out, const floa
     t.dims[1] = (uint64_t)n_out;
     t.data = (const uint8_t *)w_raw;
     t.nbytes = ecu_type_nbytes(type, (size_t)n_in * n_out);
-    DevMat m = make_mat(&tmp, (int)type, n_in, n_out, true);
+    DevMat m = make_mat(&tmp, (int)type, n_in, n_out, true, true);
     uint8_t *stage = tmp.dalloc<uint8_t>(t.nbytes + 16);
     float   *dx = tmp.dalloc<float>((size_t)n_in + 4);
     float   *dy = tmp.dalloc<float>((size_t)n_out + 4);
@@ -2260,7 +2344,7 @@ static int pf_reserve(ecu_ctx *c, int n)
 static int pf_gemm(ecu_ctx *c, const DevMat &m, int n, float *C, const float *R)
 {
     ecu_ctx::Prefill &P = c->pf;
-    if ((m.layout == LAY_SPLIT4 || m.layout == LAY_SPLIT8) && m.n_in % 32 == 0)
+    if ((m.layout == LAY_SPLIT4 || m.layout == LAY_SPLIT8 || m.layout == LAY_SPLITK4) && m.n_in % 32 == 0)
         k_pf_wsplit_fast<<<8 * c->sms, 128, 0, c->stream>>>(m, P.wh, P.wl);
     else
         k_pf_wsplit<<<8 * c->sms, 256, 0, c->stream>>>(m, P.wh, P.wl);

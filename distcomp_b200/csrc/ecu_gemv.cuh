@@ -303,7 +303,9 @@ __device__ __forceinline__ uint32_t pack_lo_bytes(uint32_t a, uint32_t b, uint32
 // FMT 4: word j<4 packs elements 4j..4j+3 (low nibbles of Q4_0 code word j),
 //        word 4+j packs 16+4j..16+4j+3 (its high nibbles).
 // FMT 8: word j packs elements 4j..4j+3.
-// off[p] = -8 * (sum of plane p's digits) for Q4_0 (the code offset), else 0.
+// FMT 12 (Q4_K in SPLITK4 rows): FMT 4's order.
+// off[p] = -8 * (sum of plane p's digits) for Q4_0 (the code offset), the
+// plain sum for Q4_K (the sub-block minimum multiplies it), else 0.
 template <int FMT>
 __device__ __forceinline__ void make_digits(const float *xv, int (&xw)[3][8], int (&off)[3],
                                             float &sxs)
@@ -330,7 +332,7 @@ __device__ __forceinline__ void make_digits(const float *xv, int (&xw)[3][8], in
     int sum[3] = {0, 0, 0};
 #pragma unroll
     for (int j = 0; j < 8; j++) {
-        const int base = (FMT == 4) ? ((j < 4) ? 4 * j : 16 + 4 * (j - 4)) : 4 * j;
+        const int base = (FMT == 4 || FMT == 12) ? ((j < 4) ? 4 * j : 16 + 4 * (j - 4)) : 4 * j;
         uint32_t b[3][4];
 #pragma unroll
         for (int i = 0; i < 4; i++) {
@@ -351,7 +353,30 @@ __device__ __forceinline__ void make_digits(const float *xv, int (&xw)[3][8], in
         }
     }
 #pragma unroll
-    for (int p = 0; p < 3; p++) off[p] = (FMT == 4) ? -8 * sum[p] : 0;
+    for (int p = 0; p < 3; p++) off[p] = (FMT == 4) ? -8 * sum[p] : (FMT == 12) ? sum[p] : 0;
+}
+
+// Sub-block j (0..7) of a Q4_K super-block from its 16-byte header h (d,
+// dmin, scales[12] as four little-endian words): dl = d*sc and ml = dmin*m,
+// the reference's two products (gguf.c:558-590).  Byte k of the scales is
+// s[k]; with jj = j & 3 the pair needs s[jj], s[4+jj] and s[8+jj] only.
+__device__ __forceinline__ void k4_scale_min(uint4 h, int j, float &dl, float &ml)
+{
+    const int      sh = 8 * (j & 3);
+    const uint32_t A = (h.y >> sh) & 0xFFu, B = (h.z >> sh) & 0xFFu, C = (h.w >> sh) & 0xFFu;
+    const uint32_t sc = j < 4 ? (A & 63u) : ((C & 0x0Fu) | ((A >> 6) << 4));
+    const uint32_t mn = j < 4 ? (B & 63u) : ((C >> 4) | ((B >> 6) << 4));
+    const float    d = __half2float(__ushort_as_half((unsigned short)(h.x & 0xFFFFu)));
+    const float    dmin = __half2float(__ushort_as_half((unsigned short)(h.x >> 16)));
+    dl = __fmul_rn(d, (float)sc);
+    ml = __fmul_rn(dmin, (float)mn);
+}
+
+// One Q4_K sub-block's dot from its merged digit sums: t = sum of code*digit,
+// sx = sum of digits (both x 2^14, 2^7, 1 per plane): dl*t - ml*sx, scaled.
+__device__ __forceinline__ float k4_finish(int t, int sx, float dl, float ml, float sxs)
+{
+    return fmaf(dl, (float)t, -(ml * (float)sx)) * sxs;
 }
 
 // Dot of the lane's block in `row` (shared memory) with its digit planes.
@@ -377,6 +402,25 @@ __device__ __forceinline__ float block_dot(const uint8_t *row, int nb, int b,
         // |a0| <= 32*8*127, |a1|,|a2| <= 32*8*64: the merged value fits int32
         const int t = a0 * 16384 + a1 * 128 + a2;
         return (float)t * (d * sxs);
+    } else if (FMT == 12) {
+        // codes 0..15: |a0| <= 32*15*127, the merged value still fits int32
+        const uint4 q = *reinterpret_cast<const uint4 *>(row + (size_t)b * 16);
+        const uint4 h = *reinterpret_cast<const uint4 *>(row + (size_t)nb * 16 + (size_t)(b >> 3) * 16);
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+        int a0 = 0, a1 = 0, a2 = 0;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int lo = (int)(w[j] & 0x0F0F0F0Fu), hi = (int)((w[j] >> 4) & 0x0F0F0F0Fu);
+            a0 = __dp4a(lo, xw[0][j], a0);
+            a0 = __dp4a(hi, xw[0][4 + j], a0);
+            a1 = __dp4a(lo, xw[1][j], a1);
+            a1 = __dp4a(hi, xw[1][4 + j], a1);
+            a2 = __dp4a(lo, xw[2][j], a2);
+            a2 = __dp4a(hi, xw[2][4 + j], a2);
+        }
+        float dl, ml;
+        k4_scale_min(h, b & 7, dl, ml);
+        return k4_finish(a0 * 16384 + a1 * 128 + a2, off[0] * 16384 + off[1] * 128 + off[2], dl, ml, sxs);
     } else {
         // SPLIT8 rows keep the first and second 16 code bytes of every block
         // in two separate runs, so both 16-byte loads are conflict-free

@@ -47,7 +47,7 @@ enum MegaKind : int { PH_EMBED = 0, PH_GEMV = 1, PH_ATTN = 2 };
 // One phase of the step.
 struct MegaPhase {
     int            kind;
-    int            fmt;        // GEMV: 4 = Q4_0 SPLIT4 rows, 8 = Q8_0 SPLIT8 rows
+    int            fmt;        // GEMV: 4 = Q4_0 SPLIT4 rows, 8 = Q8_0 SPLIT8 rows, 12 = Q4_K SPLITK4 rows
     int            norm;       // GEMV: RMSNorm of x (weights norm_w) first
     int            epi;        // GEMV: Epi
     const uint8_t *w;
@@ -337,6 +337,19 @@ __device__ __forceinline__ void digit_offsets(const int (&xw)[3][8], int (&off)[
 #pragma unroll
         for (int j = 0; j < 8; j++) s = __dp4a(xw[p][j], 0x01010101, s);
         off[p] = -8 * s;
+    }
+}
+
+// The plain sums of the block's digits per plane (block_dot<12> multiplies
+// them by the Q4_K sub-block minimum).
+__device__ __forceinline__ void digit_sums(const int (&xw)[3][8], int (&off)[3])
+{
+#pragma unroll
+    for (int p = 0; p < 3; p++) {
+        int s = 0;
+#pragma unroll
+        for (int j = 0; j < 8; j++) s = __dp4a(xw[p][j], 0x01010101, s);
+        off[p] = s;
     }
 }
 
@@ -652,7 +665,7 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
     unsigned long long *det = (a.phase_detail && blockIdx.x == 0 && threadIdx.x == 0)
                                   ? a.phase_detail + (size_t)p_idx * 4 : nullptr;
     unsigned long long waited = 0;
-    const bool q4 = ph.fmt == 4, red4 = q4 && ph.red4;
+    const bool q4 = ph.fmt == 4, k4 = ph.fmt == 12, red4 = q4 && ph.red4;
     const int nct = MEGA_NCW * 32, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nkg = ph.nkg, rowpar = ph.rowpar, nb = ph.n_in / 32;
     const int r0 = blockIdx.x * ph.rpc;
@@ -708,6 +721,7 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
         }
         sxs = __int_as_float(S.dig[(size_t)b * 28 + 27]);
         if (q4) digit_offsets(xw, off);
+        else if (k4) digit_sums(xw, off);
         else off[0] = off[1] = off[2] = 0;
     }
     const int sr = ph.sr;
@@ -730,6 +744,9 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
             else if (q4)
                 mega_stage_rows<4, false>(stage, rows, row_bytes, nb, b, g, rp, rowpar, nkg, lane, xw, off, sxs,
                                           S.red + (size_t)i * nkg);
+            else if (k4)
+                mega_stage_rows<12, false>(stage, rows, row_bytes, nb, b, g, rp, rowpar, nkg, lane, xw, off, sxs,
+                                           S.red + (size_t)i * nkg);
             else
                 mega_stage_rows<8, false>(stage, rows, row_bytes, nb, b, g, rp, rowpar, nkg, lane, xw, off, sxs,
                                           S.red + (size_t)i * nkg);

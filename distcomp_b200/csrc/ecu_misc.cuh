@@ -94,6 +94,30 @@ static __global__ void k_repack_q8_0(const uint8_t *src, int nb, int n_rows, uin
     }
 }
 
+// Q4_K rows (144-byte super-blocks) -> SPLITK4 rows.  Chunk c of a
+// super-block (code bytes 32c..32c+31) holds sub-block 2c in its low nibbles
+// and 2c+1 in its high ones (gguf.c:569-589); out byte t of sub-block 2c+h is
+// nibble h of code bytes t and t+16.  One thread per super-block.
+static __global__ void k_repack_q4_k(const uint8_t *src, int nsb, int n_rows, uint8_t *dst,
+                                     size_t dst_row_bytes, int row0, int rstride)
+{
+    const size_t total = (size_t)nsb * n_rows;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (size_t)gridDim.x * blockDim.x) {
+        const size_t   r = i / nsb, b = i % nsb;
+        const uint8_t *s = src + i * 144;
+        uint8_t       *d = dst + (size_t)(row0 + r * rstride) * dst_row_bytes;
+        for (int c = 0; c < 4; c++)
+            for (int t = 0; t < 16; t++) {
+                const uint8_t lo = s[16 + 32 * c + t], hi = s[16 + 32 * c + 16 + t];
+                d[(b * 8 + 2 * c) * 16 + t] = (uint8_t)((lo & 0x0F) | (hi << 4));
+                d[(b * 8 + 2 * c + 1) * 16 + t] = (uint8_t)((lo >> 4) | (hi & 0xF0));
+            }
+        uint8_t *h = d + (size_t)nsb * 128 + b * 16;
+        for (int k = 0; k < 16; k++) h[k] = s[k];
+    }
+}
+
 // Raw rows copied to device row row0 + r*rstride (formats kept as is).
 static __global__ void k_copy_rows(const uint8_t *src, size_t src_row_bytes, int n_rows, uint8_t *dst,
                             size_t dst_row_bytes, int row0, int rstride)

@@ -68,18 +68,31 @@ static __global__ void k_pf_split(const float *X, size_t count, __half *hi, __ha
         pf_split(X[e], hi[e], lo[e]);
 }
 
-// Q4_0 (SPLIT4) or Q8_0 (SPLIT8) rows dequantised and split, one thread per
-// 32-element block: the values mat_elem gives, 64-byte stores.
+// Q4_0 (SPLIT4), Q8_0 (SPLIT8) or Q4_K (SPLITK4) rows, column segments
+// included, dequantised and split, one thread per 32-element block: the
+// values mat_elem gives, 64-byte stores.
 static __global__ void k_pf_wsplit_fast(DevMat m, __half *hi, __half *lo)
 {
-    const int    nb = m.n_in / 32;
-    const size_t total = (size_t)m.n_out * nb;
+    const int    nbt = m.n_in / 32, nb = nbt / m.nseg;     // blocks of a row, of a segment row
+    const size_t total = (size_t)m.n_out * nbt;
     for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
-        const size_t   row = e / (size_t)nb;
-        const int      b = (int)(e % (size_t)nb);
-        const uint8_t *r = m.data + row * m.row_bytes;
+        const size_t   row = e / (size_t)nbt;
+        const int      bt = (int)(e % (size_t)nbt), b = bt % nb;
+        const uint8_t *r = m.data + (size_t)(bt / nb) * m.seg_bytes + row * m.row_bytes;
         float          v[32];
-        if (m.layout == LAY_SPLIT4) {
+        if (m.layout == LAY_SPLITK4) {
+            const uint4 q = *reinterpret_cast<const uint4 *>(r + (size_t)b * 16);
+            const uint4 h = *reinterpret_cast<const uint4 *>(r + (size_t)nb * 16 + (size_t)(b >> 3) * 16);
+            float dl, ml;
+            k4_scale_min(h, b & 7, dl, ml);
+            const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+                const uint32_t byte = (w[j >> 2] >> (8 * (j & 3))) & 0xFFu;
+                v[j] = __fsub_rn(__fmul_rn(dl, (float)(byte & 0x0F)), ml);
+                v[j + 16] = __fsub_rn(__fmul_rn(dl, (float)(byte >> 4)), ml);
+            }
+        } else if (m.layout == LAY_SPLIT4) {
             const uint4 q = *reinterpret_cast<const uint4 *>(r + (size_t)b * 16);
             const float d = f16x(r + (size_t)nb * 16 + 2 * b);
             const uint32_t w[4] = {q.x, q.y, q.z, q.w};
@@ -100,8 +113,8 @@ static __global__ void k_pf_wsplit_fast(DevMat m, __half *hi, __half *lo)
         __align__(16) __half h[32], l[32];
 #pragma unroll
         for (int j = 0; j < 32; j++) pf_split(v[j], h[j], l[j]);
-        uint4 *ho = reinterpret_cast<uint4 *>(hi + row * m.n_in + (size_t)b * 32);
-        uint4 *lo4 = reinterpret_cast<uint4 *>(lo + row * m.n_in + (size_t)b * 32);
+        uint4 *ho = reinterpret_cast<uint4 *>(hi + row * m.n_in + (size_t)bt * 32);
+        uint4 *lo4 = reinterpret_cast<uint4 *>(lo + row * m.n_in + (size_t)bt * 32);
 #pragma unroll
         for (int j = 0; j < 4; j++) {
             ho[j] = reinterpret_cast<const uint4 *>(h)[j];

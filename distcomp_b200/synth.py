@@ -56,6 +56,10 @@ SPECS = {
     # small shapes that still exercise the fast Q4_0/Q8_0 GEMV path (n_in % 1024 == 0)
     "mini-q4": LlamaSpec(2, 1024, 8, 2, 2048, 2048, 128, 500000.0, wtype=G.Q4_0),
     "mini-q8": LlamaSpec(2, 1024, 16, 4, 3072, 1536, 96, 10000.0, wtype=G.Q8_0),
+    # Q4_K layers on the fast path; "wide-q4k" has an FFN wider than one
+    # column segment (ffn_down kept as two segments of 10240 inputs)
+    "mini-q4k": LlamaSpec(2, 1024, 8, 2, 2048, 2048, 128, 500000.0, wtype=G.Q4_K),
+    "wide-q4k": LlamaSpec(2, 1024, 8, 1, 20480, 2048, 96, 10000.0, wtype=G.Q4_K),
 }
 
 
@@ -149,6 +153,48 @@ def quantize_torch(w, gtype: int):
     raise ValueError(f"quantize_torch: type {gtype} not supported")
 
 
+def quantize_q4_k_torch(w):
+    """float32 weights (a multiple of 256) -> Q4_K super-blocks, 144 bytes
+    per 256 weights, as torch uint8 on w's device.
+
+    A plain min/max rule (any byte pattern is a valid block; this one makes
+    the dequantised weights follow w): per 32-weight sub-block j, lo = min(0,
+    min x), scale_j = (max x - lo) / 15, min_j = -lo; per super-block d =
+    fp16(max scale_j / 63), dmin = fp16(max min_j / 63), 6-bit sc_j =
+    round(scale_j / d), m_j = round(min_j / dmin); codes q = round((x +
+    dmin*m_j) / (d*sc_j)) clamped to 0..15.  Bytes: d, dmin, the 12 packed
+    scale bytes (sc/m of sub-blocks 0-3 in the low 6 bits of bytes 0-3 / 4-7,
+    the low nibbles of sub-blocks 4-7 in bytes 8-11, their high 2 bits in the
+    top bits of bytes 0-7), then chunk c's 32 code bytes with sub-block 2c in
+    the low nibbles and 2c+1 in the high ones -- the layout src/gguf.c:558-590
+    decodes."""
+    import torch
+    x = w.reshape(-1, 8, 32).to(torch.float32)
+    nb = x.shape[0]
+    lo = torch.clamp(x.amin(dim=2), max=0.0)
+    sc_f = (x.amax(dim=2) - lo) / 15.0
+    mn_f = -lo
+    d = (sc_f.amax(dim=1) / 63.0).to(torch.float16)
+    dm = (mn_f.amax(dim=1) / 63.0).to(torch.float16)
+    df, dmf = d.float()[:, None], dm.float()[:, None]
+    inv_d = torch.where(df > 0, 1.0 / df, torch.zeros_like(df))
+    inv_dm = torch.where(dmf > 0, 1.0 / dmf, torch.zeros_like(dmf))
+    sc = torch.clamp(torch.round(sc_f * inv_d), 0, 63).to(torch.int32)
+    mn = torch.clamp(torch.round(mn_f * inv_dm), 0, 63).to(torch.int32)
+    dl = (df * sc.float())[..., None]
+    ml = (dmf * mn.float())[..., None]
+    inv_dl = torch.where(dl > 0, 1.0 / dl, torch.zeros_like(dl))
+    q = torch.clamp(torch.round((x + ml) * inv_dl), 0, 15).to(torch.uint8).reshape(nb, 4, 2, 32)
+    qs = (q[:, :, 0, :] | (q[:, :, 1, :] << 4)).reshape(nb, 128)
+    sb = torch.empty((nb, 12), dtype=torch.int32, device=x.device)
+    sb[:, 0:4] = sc[:, 0:4] | ((sc[:, 4:8] >> 4) << 6)
+    sb[:, 4:8] = mn[:, 0:4] | ((mn[:, 4:8] >> 4) << 6)
+    sb[:, 8:12] = (sc[:, 4:8] & 0xF) | ((mn[:, 4:8] & 0xF) << 4)
+    head = torch.cat([d.view(torch.uint8).reshape(nb, 2), dm.view(torch.uint8).reshape(nb, 2),
+                      sb.to(torch.uint8)], dim=1)
+    return torch.cat([head, qs], dim=1).reshape(-1)
+
+
 def random_kquant_blocks(rng: np.random.Generator, gtype: int, nblk: int, sigma: float = 0.02):
     """Random K-quant blocks: uniform code/scale bytes, fp16 super-block scales
     drawn as |N(0, sigma)| / 64 so that weights land around sigma.  (gguf-py
@@ -209,14 +255,18 @@ def build_model(s: LlamaSpec, seed: int = 0, device: str = "cpu") -> np.ndarray:
         if name.endswith("norm.weight"):
             view[:] = np.ones(n, dtype=np.float32).view(np.uint8)
             continue
-        if gt in (G.Q2_K, G.Q3_K, G.Q4_K, G.Q5_K, G.Q6_K, G.Q8_K):
+        if gt in (G.Q2_K, G.Q3_K, G.Q5_K, G.Q6_K, G.Q8_K):
             rng = np.random.default_rng(name_seed(seed, name))
             view[:] = random_kquant_blocks(rng, gt, n // G.BLOCK[gt][0], s.sigma)
             continue
         if device == "cpu":
             rng = np.random.default_rng(name_seed(seed, name))
             w = (rng.standard_normal(n, dtype=np.float32) * np.float32(s.sigma)).reshape(dims[::-1])
-            view[:] = quantize_numpy(w, gt)
+            if gt == G.Q4_K:
+                import torch
+                view[:] = quantize_q4_k_torch(torch.from_numpy(w)).numpy()
+            else:
+                view[:] = quantize_numpy(w, gt)
         else:
             import torch
             gen = torch.Generator(device=dev)
@@ -227,6 +277,8 @@ def build_model(s: LlamaSpec, seed: int = 0, device: str = "cpu") -> np.ndarray:
                 qb = w.view(torch.uint8)
             elif gt == G.F16:
                 qb = w.to(torch.float16).view(torch.uint8)
+            elif gt == G.Q4_K:
+                qb = quantize_q4_k_torch(w)
             else:
                 qb = quantize_torch(w, gt)
             torch.from_numpy(view).copy_(qb.cpu())

@@ -159,3 +159,18 @@ def test_matvec_extreme_inputs(eng, oracle_port):
         ref = oracle_port.matvec_f64(G.Q4_0, raw, n_in, n_out, x)
         ok, worst = gemv_tol_ok(y, ref, row_norms(oracle_port, G.Q4_0, raw, n_in, n_out), x)
         assert ok, worst
+
+
+@pytest.mark.parametrize("t", [G.Q4_0, G.Q8_0, G.Q4_K])
+@pytest.mark.parametrize("n_out,n_in", [(1024, 8192), (512, 28672)])
+def test_matvec_fast_widths(eng, oracle_port, t, n_out, n_in):
+    """Q4_K rows through the SPLITK4 fast GEMV; 28672 inputs (the 70B-shape
+    ffn_down width, above one 16384-input column segment) stored as two
+    segments whose GEMVs store and then add."""
+    rng = np.random.default_rng(n_out + n_in + 3 * t)
+    raw = random_weights(rng, t, n_in, n_out)
+    x = rng.standard_normal(n_in).astype(np.float32)
+    y = eng.matvec(t, raw, n_in, n_out, x)
+    ref = oracle_port.matvec_f64(t, raw, n_in, n_out, x)
+    ok, worst = gemv_tol_ok(y, ref, row_norms(oracle_port, t, raw, n_in, n_out), x)
+    assert ok, f"type {t} {n_out}x{n_in}: worst rel {worst:.3e}"

@@ -41,6 +41,25 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "decode tokens/s (batch 1) + % HBM roofline, 8B-shape Q4_0, 1/2/4/8 B200 vs host CPU"
 CONFIG = "llama3-8b"
+# other shapes (--model): the 70B long-context one, weights in Q4_K
+METRICS = {"llama2-70b": "decode tokens/s (batch 1) + % HBM roofline, 70B-shape Q4_K long context, B200"}
+
+
+def metric_for(key: str) -> str:
+    return METRICS.get(key, METRIC)
+
+
+def workload_text(spec, key: str) -> str:
+    from distcomp_b200 import gguf as G
+    hd = spec.n_embd // spec.n_head
+    return (f"{key}-shape {G.TYPE_NAMES[spec.wtype]} decode, batch 1 (dim {spec.n_embd}, {spec.n_layer} layers, "
+            f"{spec.n_head}/{spec.n_head_kv} heads, head_dim {hd}, ffn {spec.n_ff}, vocab {spec.n_vocab}, "
+            f"theta {spec.rope_base:g}, embedding {G.TYPE_NAMES[spec.emb_type]}, head {G.TYPE_NAMES[spec.out_type]})")
+
+
+def dtype_text(spec) -> str:
+    from distcomp_b200 import gguf as G
+    return f"{G.TYPE_NAMES[spec.wtype].lower()} codes x int8 digit planes, fp32 accumulate"
 
 
 def parse():
@@ -65,6 +84,9 @@ def parse():
                          "shard.c's ceil(layers/stages) rule")
     ap.add_argument("--layers", type=int, default=0,
                     help="override n_layer (reduced-depth runs for profiler captures; not a bench line)")
+    ap.add_argument("--model", choices=["llama3-8b", "llama2-70b"], default=CONFIG,
+                    help="model shape (one GPU): the 8B Q4_0 headline, or the 70B Q4_K long-context shape "
+                         "(use --prompt 8192 --n-ctx 8704 --steps 128 for its configuration)")
     return ap.parse_args()
 
 
@@ -216,7 +238,7 @@ def our_arm(args, rank, world, local):
         from distcomp_b200 import pipeline
         return pipeline.bench_main(args, rank, world, local, sys.modules[__name__])
 
-    spec = synth.spec(CONFIG, **({"n_layer": args.layers} if args.layers else {}))
+    spec = synth.spec(args.model, **({"n_layer": args.layers} if args.layers else {}))
     t_build = time.perf_counter()
     buf = build_model_gpu(spec, args.seed, local)
     t_build = time.perf_counter() - t_build
@@ -263,8 +285,10 @@ def our_arm(args, rank, world, local):
     prof = ctx.profile_steps(args.profile_steps)
     peak, peak_kind = peaks()
     if "decode_step" in prof:
-        dom, kname = "decode_step", "k_decode_mega<128, 4> (persistent kernel: the whole token step)"
-        traffic, scaled = load_traffic("decode_step_mega_8b.json")
+        dom = "decode_step"
+        kname = (f"k_decode_mega<{spec.n_embd // spec.n_head}, {spec.n_head // spec.n_head_kv}> "
+                 "(persistent kernel: the whole token step)")
+        traffic, scaled = load_traffic("decode_step_mega_8b.json") if args.model == CONFIG else (None, None)
     else:
         dom, kname = "gemv_gate_up", "k_gemv_fast<Q4_0, rmsnorm, swiglu> (fused ffn_gate+ffn_up)"
         traffic, scaled = load_traffic("gemv_gate_up_q4_0_8b.json")
@@ -284,15 +308,16 @@ def our_arm(args, rank, world, local):
     e2e = args.steps / e2e_s
 
     bpt = algorithmic_bytes_per_token(spec, pos0 + (args.steps - 1) / 2)
+    wbytes = algorithmic_bytes_per_token(spec, -1.0) - 2 * spec.n_head_kv * (spec.n_embd // spec.n_head) * 4 * spec.n_layer
     line = {
-        "metric": METRIC, "value": round(tps, 2), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "q4_0 codes x int8 digit planes, fp32 accumulate",
-        "data": "synthetic: seeded N(0,0.02) weights quantised to Q4_0/Q8_0 on the GPU, random prompt",
-        "config": {"workload": "llama3-8b-shape Q4_0 decode, batch 1 (dim 4096, 32 layers, 32/8 heads, "
-                               "ffn 14336, vocab 128256, theta 5e5, KV fp32 4096)",
+        "metric": metric_for(args.model), "value": round(tps, 2), "unit": "tokens/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dtype_text(spec),
+        "data": "synthetic: seeded N(0,0.02) weights quantised on the GPU, random prompt",
+        "config": {"workload": workload_text(spec, args.model) + f", KV fp32 {args.n_ctx}",
                    "prompt_tokens": args.prompt, "decode_positions": [pos0, pos0 + args.steps - 1],
-                   "l2": "inputs larger than L2 (4.49 GB of weights per step)", "n_ctx": args.n_ctx},
+                   "l2": f"inputs larger than L2 ({wbytes / 1e9:.2f} GB of weights per step)",
+                   "n_ctx": args.n_ctx},
         "token_roofline": {"bytes_per_token": bpt, "achieved_gbs": round(bpt * tps / 1e9, 1),
                            "peak_gbs": peak, "frac": round(bpt * tps / 1e9 / peak, 4),
                            "frac_of_8tbs_nominal": round(bpt * tps / 1e9 / 8000, 4), "peak_kind": peak_kind},
@@ -318,9 +343,9 @@ def our_arm(args, rank, world, local):
     if not args.no_cpu_baseline:
         v, n, thr, kind = cpu_reference_tokens_per_s(buf, spec, args.cpu_sample_s, 64)
         line["cpu_baseline"] = {"value": round(v, 4), "unit": "tokens/s", "cores": thr, "kind": kind,
-                                "sample": f"{n} decode tokens at positions 1..{n} of the same 8B Q4_0 model "
-                                          f"(embed+32 layers+head, three stages like shard.c's local run); "
-                                          f"KV reads differ from positions 512..767 by <4% of the bytes"}
+                                "sample": f"{n} decode tokens at positions 1..{n} of the same model "
+                                          f"(embed+{spec.n_layer} layers+head, three stages like shard.c's "
+                                          f"local run); KV reads differ from the timed positions"}
     print(json.dumps(line), flush=True)
     ctx.close()
     return 0

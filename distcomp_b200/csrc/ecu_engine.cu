@@ -962,7 +962,7 @@ static int mega_setup(ecu_ctx *c)
     size_t ring_total = MEGA_RING_BYTES;
     if (const char *r = getenv("ECU_MEGA_RING_KB")) ring_total = (size_t)std::max(32, std::min(200, atoi(r))) * 1024;
     if (nst > MEGA_MAX_STAGES) return no("too many ring stages");
-    const unsigned stage_bytes = (unsigned)(ring_total / nst) & ~127u;
+    unsigned stage_bytes = (unsigned)(ring_total / nst) & ~127u;
     // (row_bytes and n_in / nseg are those of a column segment)
     for (auto &ly : c->layers)
         if (ly.qkv[0].row_bytes > stage_bytes || ly.o.row_bytes > stage_bytes || ly.gu.row_bytes > stage_bytes ||
@@ -974,13 +974,31 @@ static int mega_setup(ecu_ctx *c)
     // or the attention K/V buffers; the split partials of a head group, which
     // the merge gathers there, set the position splits per KV head (one
     // item per CTA at most)
-    size_t un = (size_t)4 * MEGA_ATT_SUB * hd * sizeof(float);
-    un = std::max(un, (size_t)g.n_embd / 32 * 28 * sizeof(int) + 2 * (size_t)g.n_embd * sizeof(float));
+    size_t un = (size_t)g.n_embd / 32 * 28 * sizeof(int) + 2 * (size_t)g.n_embd * sizeof(float);
     for (auto &ly : c->layers)
         for (const DevMat *m : {&ly.qkv[0], &ly.o, &ly.gu, &ly.d})
             un = std::max(un, (size_t)(m->n_in / m->nseg) / 32 * 28 * sizeof(int));
     if (full) un = std::max(un, (size_t)c->out.n_in / 32 * 28 * sizeof(int));
+    // attention K/V buffers: two slots (each round's copies overlap the
+    // previous round's arithmetic) when the GEMV side of the union already
+    // holds two slots of >= 20 rows a buffer, else one slot of MEGA_ATT_SUB
+    // rows (ECU_MEGA_ATT=1 / 2 forces one / two slots)
+    const size_t row4 = (size_t)4 * hd * sizeof(float);      // a row in each of a slot's 4 buffers
+    int att_nsl = 1, att_sub = MEGA_ATT_SUB;
+    const int sub2 = (int)std::min<size_t>(32, un / (2 * row4)) & ~1;
+    const char *ae = getenv("ECU_MEGA_ATT");
+    if (ae && ae[0] == '2') {
+        att_nsl = 2;
+        att_sub = std::max(sub2, MEGA_ATT_SUB);
+    } else if (!(ae && ae[0] == '1') && sub2 >= 20) {
+        att_nsl = 2;
+        att_sub = sub2;
+    }
+    un = std::max(un, (size_t)att_nsl * att_sub * row4);
+    // the attention's position-group sums: [512 / (hd/4)][n_rep][hd] floats
+    un = std::max(un, (size_t)(MEGA_THREADS / (hd / 4)) * g.n_rep * hd * sizeof(float));
     int n_split = std::min(MEGA_MAX_SPLIT, grid / tp.nkv);
+    if (const char *se = getenv("ECU_MEGA_SPLIT")) n_split = std::max(1, std::min(n_split, atoi(se)));
     n_split = std::min(n_split, (int)(un / ((size_t)g.n_rep * (hd + 4) * sizeof(float))));
     n_split = std::max(1, std::min(n_split, g.n_ctx));
 
@@ -1088,12 +1106,26 @@ static int mega_setup(ecu_ctx *c)
             red = std::max(red, p.red4 ? p.rpc * (p.nkg * 4 + 1) : p.rpc * p.nkg);
             if (p.epi == EPI_ADD && p.rpc > MEGA_THREADS) return no("residual rows per CTA above the thread count");
         }
-    const size_t smem = mega_smem_total(red, (unsigned)nst * stage_bytes, (unsigned)un);
     cudaFuncAttributes fa;
     int optin = 0;
-    if (cudaFuncGetAttributes(&fa, fn) != cudaSuccess ||
-        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, c->device) != cudaSuccess ||
-        smem + fa.sharedSizeBytes > (size_t)optin ||
+    if (cudaFuncGetAttributes(&fa, fn) == cudaSuccess &&
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, c->device) == cudaSuccess &&
+        mega_smem_total(red, (unsigned)nst * stage_bytes, (unsigned)un) + fa.sharedSizeBytes > (size_t)optin) {
+        // a wide model's digit planes, norm staging and row partials leave
+        // less room: shrink the ring stages (1 KB at a time) while every
+        // GEMV row still fits one, and refit the phases' rows per stage
+        unsigned max_row = 0;
+        for (auto &p : ph)
+            if (p.kind == PH_GEMV) max_row = std::max(max_row, p.row_bytes);
+        while (stage_bytes >= max_row + 1024 &&
+               mega_smem_total(red, (unsigned)nst * stage_bytes, (unsigned)un) + fa.sharedSizeBytes > (size_t)optin)
+            stage_bytes -= 1024;
+        for (auto &p : ph)
+            if (p.kind == PH_GEMV) p.sr = (int)std::min<size_t>((size_t)p.rpc, stage_bytes / p.row_bytes);
+    }
+    cudaGetLastError();
+    const size_t smem = mega_smem_total(red, (unsigned)nst * stage_bytes, (unsigned)un);
+    if (optin == 0 || smem + fa.sharedSizeBytes > (size_t)optin ||
         cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
         cudaGetLastError();
         static char buf[160];
@@ -1160,6 +1192,10 @@ static int mega_setup(ecu_ctx *c)
     const char *pfe = getenv("ECU_MEGA_PF");
     a.pf_stages = pfe ? std::max(0, atoi(pfe)) : 0;
     a.stage_bytes = stage_bytes;
+    a.att_sub = att_sub;
+    a.att_nsl = att_nsl;
+    const char *al2 = getenv("ECU_MEGA_ATT_L2");
+    a.att_l2 = (al2 && al2[0] == '0') ? 0 : 1;
     a.eps = g.eps;
     a.kscale = 1.0f / sqrtf((float)hd);
     c->mega_fn = fn;
@@ -2374,7 +2410,11 @@ int ecu_prefill(ecu_ctx *c, const int *tokens, int n, float *out)
         ecu_set_error(nullptr, 0, "prompt of %d tokens at position %d exceeds the context (%d)", n, c->pos, g.n_ctx);
         return -1;
     }
-    bool batched = c->tp.world == 1 && g.n_ctx <= PF_ATT_MAXPOS && (g.head_dim == 64 || g.head_dim == 128) &&
+    // the token-tiled attention (k_pf_attn2) has no position limit; the
+    // one-query-per-CTA kernel keeps its scores in a PF_ATT_MAXPOS array
+    const char *ae = getenv("ECU_PF_ATTN");
+    const bool  attn2 = PF_QB % g.n_rep == 0 && !(ae && ae[0] == '0');
+    bool batched = c->tp.world == 1 && (attn2 || g.n_ctx <= PF_ATT_MAXPOS) && (g.head_dim == 64 || g.head_dim == 128) &&
                    g.n_embd % 8 == 0 && g.n_ff % 8 == 0;
     for (auto &ly : c->layers) batched = batched && ly.qkv.size() == 1 && ly.gu_fused;
     if (!batched) {
@@ -2406,8 +2446,7 @@ int ecu_prefill(ecu_ctx *c, const int *tokens, int n, float *out)
         if (pf_gemm(c, ly.qkv[0], n, P.QKV, nullptr)) return -1;
         k_pf_rope_kv<<<n, 128, 0, c->stream>>>(P.QKV, ldq, g.n_head, g.n_head_kv, hd, pos0, c->rope_cs, ly.bq, ly.bk,
                                                ly.bv, c->kc + li * plane, c->vc + li * plane, g.n_ctx);
-        const char *ae = getenv("ECU_PF_ATTN");
-        if (PF_QB % g.n_rep == 0 && !(ae && ae[0] == '0')) {
+        if (attn2) {
             // tiled over tokens: 64 query vectors a CTA
             dim3 ag((unsigned)g.n_head_kv, (unsigned)((n + PF_QB / g.n_rep - 1) / (PF_QB / g.n_rep)));
             if (hd == 128)

@@ -33,7 +33,7 @@
 #define MEGA_NCW 16                      // warps (all of them consume the ring)
 #define MEGA_THREADS (32 * MEGA_NCW)
 #define MEGA_RING_BYTES (128 * 1024)    // default weight ring, split into nst stages
-#define MEGA_ATT_SUB 24                  // K/V rows per buffer (4 buffers: K and V of two halves)
+#define MEGA_ATT_SUB 24                  // K/V rows per buffer (4 buffers: K and V of two halves), one slot
 #define MEGA_MAX_STAGES 8
 #define MEGA_MAX_NB 512                  // input blocks of a GEMV (n_in <= 16384)
 #define MEGA_MAX_SPLIT 64                // position splits per KV head
@@ -113,6 +113,9 @@ struct MegaArgs {
     int              nst;           // ring stages (<= MEGA_MAX_STAGES)
     int              pf_stages;     // chunks warmed in L2 ahead of the ring
     unsigned         stage_bytes;   // bytes per ring stage (multiple of 128)
+    int              att_sub;       // attention: K/V rows per buffer (even, <= 32)
+    int              att_nsl;       // attention: buffer slots (1, or 2: a round's copies overlap the previous round)
+    int              att_l2;        // warm the next attention's K/V rows in L2 during the GEMV before it
     float            eps, kscale;
 };
 
@@ -270,7 +273,7 @@ __host__ __device__ inline MegaSmem mega_smem_plan(int red_floats, unsigned ring
     p.ring = 0;
     p.bars = p.ring + (size_t)ring_bytes;
     p.abar = p.bars + MEGA_MAX_STAGES * sizeof(uint64_t);
-    p.red = (p.abar + 4 * sizeof(uint64_t) + 15) & ~(size_t)15;    // K/V halves, partial gather
+    p.red = (p.abar + 8 * sizeof(uint64_t) + 15) & ~(size_t)15;    // K/V halves of 2 slots, partial gather
     p.un = (p.red + (size_t)red_floats * sizeof(float) + 127) & ~(size_t)127;
     // union: digit planes (and the RMSNorm staging) of a GEMV input | the
     // attention K/V buffers and split-partial gather
@@ -769,7 +772,7 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
     if (next) {
         // next phase's descriptor: its copy was issued at this phase's start
         mbar_wait<true>(S.dbar, (unsigned)p_idx & 1u, a.status);
-        if (tid == 0) attn_prefetch(a, *next, S.pos, hd);
+        if (tid == 0 && a.att_l2) attn_prefetch(a, *next, S.pos, hd);
         for (int j = tid; j < hd; j += nct) S.cs[j] = a.rope_cs[(size_t)S.pos * hd + j];
     }
 
@@ -863,8 +866,8 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
 // query head h of the group on warp h.  Same arithmetic per split as
 // k_attention; partials go to global memory for the merge phase.
 template <int HD, int NREP, bool SYS>
-__device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const MegaShared &S, int &att_sb, int &merges,
-                               int p_idx)
+__device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const MegaShared &S, int &att_sb0,
+                               int &att_sb1, int &merges, int p_idx)
 {
     // profiling (CTA 0): after the Q/K/V prologue, after the position loop,
     // after the split ticket; and when KV head 0's merge ended
@@ -874,7 +877,7 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
     // and matrix); the score loop reads a row's float4 columns in an order
     // rotated by the lane, so the 32 lanes' rows still spread over the banks
     constexpr int RS = HD;
-    constexpr int LPR = HD / 4, RPW = 32 / LPR, NC4 = HD / 4;
+    constexpr int LPR = HD / 4, NC4 = HD / 4;
     static_assert((NC4 & (NC4 - 1)) == 0, "head_dim / 4 a power of two");
     __shared__ __align__(16) float q_s[NREP * HD];
     __shared__ __align__(16) float knew[HD], vnew[HD];
@@ -885,26 +888,33 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
     const int pos = S.pos, npos = pos + 1;
     const int chunk = (npos + a.n_split - 1) / a.n_split;
     const int t0 = min(npos, sp * chunk), t1 = has ? min(npos, t0 + chunk) : t0;
-    const int nround = (t1 - t0 + 2 * MEGA_ATT_SUB - 1) / (2 * MEGA_ATT_SUB);   // 2 * MEGA_ATT_SUB positions a round
+    const int sub = a.att_sub, nsl = a.att_nsl;
+    const int nround = (t1 - t0 + 2 * sub - 1) / (2 * sub);   // 2 * sub positions a round
     float *kbase = ph.kc + (size_t)g * a.n_ctx * HD;
     float *vbase = ph.vc + (size_t)g * a.n_ctx * HD;
-    // half hf (MEGA_ATT_SUB rows) of round r of the slice below the current position
-    // (contiguous in the head-major cache): one bulk copy for K, one for V;
-    // thread 0 issues half 0, thread 32 half 1
+    // buffer (slot s, matrix m: 0 = K, 1 = V, half hf) of sub rows
+    auto buf = [&](int s_, int m, int hf) { return S.kvbuf + (size_t)((s_ * 2 + m) * 2 + hf) * sub * RS; };
+    // half hf (sub rows) of round r of the slice below the current position
+    // (contiguous in the head-major cache) into slot r % nsl: one bulk copy
+    // for K, one for V; thread 0 issues half 0, thread 32 half 1.  A slot is
+    // refilled after the barrier that ends the round which read it; the proxy
+    // fence orders those generic reads before the copy's writes.
     auto issue = [&](int r, int hf) {
-        const int c0 = t0 + r * 2 * MEGA_ATT_SUB + hf * MEGA_ATT_SUB;
-        const int c1 = min(min(t1, c0 + MEGA_ATT_SUB), pos);
+        const int s_ = r % nsl;
+        const int c0 = t0 + r * 2 * sub + hf * sub;
+        const int c1 = min(min(t1, c0 + sub), pos);
         const int nr = c1 > c0 ? c1 - c0 : 0;
-        float *kb = S.kvbuf + (size_t)hf * MEGA_ATT_SUB * RS;
-        float *vb = S.kvbuf + (size_t)(2 + hf) * MEGA_ATT_SUB * RS;
         const uint32_t bytes = (uint32_t)(nr * HD * sizeof(float));
-        mbar_expect_tx(&S.abar[hf], 2 * bytes);
+        uint64_t *bar = &S.abar[s_ * 2 + hf];
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_expect_tx(bar, 2 * bytes);
         if (nr > 0) {
-            bulk_g2s(kb, kbase + (size_t)c0 * HD, bytes, &S.abar[hf]);
-            bulk_g2s(vb, vbase + (size_t)c0 * HD, bytes, &S.abar[hf]);
+            bulk_g2s(buf(s_, 0, hf), kbase + (size_t)c0 * HD, bytes, bar);
+            bulk_g2s(buf(s_, 1, hf), vbase + (size_t)c0 * HD, bytes, bar);
         }
     };
-    if (nround > 0 && (tid & 31) == 0 && tid < 64) issue(0, tid >> 5);
+    if ((tid & 31) == 0 && tid < 64)
+        for (int r = 0; r < min(nsl, nround); r++) issue(r, tid >> 5);
     const float *cs_s = S.cs;
     const unsigned ein = ll_epoch(S.launch, ph.in_ep);
     const int qdim = a.n_head * HD, kvdim = a.n_kv * HD;
@@ -944,108 +954,135 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
             kbase[(size_t)pos * HD + j] = knew[j];
             vbase[(size_t)pos * HD + j] = vnew[j];
         }
-    // warp (h, grp): query head h, positions grp*Q .. grp*Q+Q-1 of each
-    // round's 2*MEGA_ATT_SUB (G = 16/NREP groups), so the serial V
-    // accumulation is Q long
-    constexpr int G = MEGA_NCW / NREP, Q = 2 * MEGA_ATT_SUB / G;
-    static_assert(G >= 1 && Q >= 1 && Q <= MEGA_ATT_SUB, "position groups");
-    const int h = warp % NREP, grp = warp / NREP;
-    const int hf = (grp * Q) / MEGA_ATT_SUB, off = grp * Q - hf * MEGA_ATT_SUB;
-    float  m_run = -INFINITY, l_run = 0.0f;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    // Each round (2*sub positions) in three steps, every K and V row read
+    // from shared memory once for all NREP query heads of the KV head:
+    //  scores: 8 threads per position, thread ds holding float4 columns ds,
+    //          ds+8, ... (8 distinct bank quads per wavefront) against the
+    //          NREP queries (broadcast reads), the 8 slices added by a
+    //          butterfly; sc[h][p] = dot * kscale (-inf past the slice);
+    //  softmax: warp h takes head h's positions, a running max over rounds:
+    //          f = exp(m_old - m_new), e = exp(s - m_new), l = l*f + sum e;
+    //  values: thread (float4 column c, position group pg) rescales its NREP
+    //          accumulators by f and adds e[h][p] * V[p][c] over its group's
+    //          positions.
+    // After the last round the position groups' accumulators are added in
+    // group order through shared memory into the split's partial.
+    constexpr int C4 = HD / 4, PG = MEGA_THREADS / C4, NSL8 = 8;
+    static_assert(C4 % NSL8 == 0 && NREP <= 8 && NREP <= MEGA_NCW, "attention thread layout");
+    const int P = 2 * sub;                                 // <= 64: 8 threads a position cover 512
+    float *sc = S.red;                                     // [NREP][64] scores
+    float *es = sc + NREP * 64;                            // [64][NREP] weights
+    float *fs = es + 64 * NREP;                            // [NREP] rescale factors
+    float  m_run = -INFINITY, l_run = 0.0f;                // warp h < NREP: head h's
+    float4 acc[NREP];
+#pragma unroll
+    for (int hh = 0; hh < NREP; hh++) acc[hh] = make_float4(0.f, 0.f, 0.f, 0.f);
+    const int qp = tid >> 3, ds = tid & 7;                 // scores: position, column slice
+    const int vc = tid % C4, pg = tid / C4;                // values: float4 column, position group
     for (int r = 0; r < nround; r++) {
-        const int c0 = t0 + r * 2 * MEGA_ATT_SUB + grp * Q, cn = max(0, min(Q, t1 - c0));
-        if (cn > 0) {
-            mbar_wait<true>(&S.abar[hf], (unsigned)(att_sb + r) & 1u, a.status);
-            const float *kb = S.kvbuf + (size_t)hf * MEGA_ATT_SUB * RS + (size_t)off * RS;
-            const float *vb = S.kvbuf + (size_t)(2 + hf) * MEGA_ATT_SUB * RS + (size_t)off * RS;
-            const float *krow = (c0 + lane == pos) ? knew : kb + lane * RS;
-            float s = -INFINITY;
-            if (lane < cn) {
-                const float4 *k4 = reinterpret_cast<const float4 *>(krow);
-                const float4 *q4 = reinterpret_cast<const float4 *>(q_s + h * HD);
-                float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
-#pragma unroll 8
-                for (int j0 = 0; j0 < NC4; j0++) {
-                    const int    j = (j0 + lane) & (NC4 - 1);
-                    const float4 kv = k4[j], qv = q4[j];
-                    d0 = fmaf(qv.x, kv.x, d0);
-                    d1 = fmaf(qv.y, kv.y, d1);
-                    d2 = fmaf(qv.z, kv.z, d2);
-                    d3 = fmaf(qv.w, kv.w, d3);
+        const int s_ = r % nsl, cb = t0 + r * P;           // this round's first position
+        const int cn = min(P, t1 - cb);
+        const unsigned par = (unsigned)((s_ ? att_sb1 : att_sb0) + r / nsl) & 1u;
+        mbar_wait<true>(&S.abar[s_ * 2], par, a.status);
+        if (cn > sub) mbar_wait<true>(&S.abar[s_ * 2 + 1], par, a.status);
+        // ---- scores
+        if (qp < P) {
+            float d[NREP];
+#pragma unroll
+            for (int hh = 0; hh < NREP; hh++) d[hh] = 0.0f;
+            if (qp < cn) {
+                const float4 *k4 = (cb + qp == pos) ? reinterpret_cast<const float4 *>(knew)
+                                                   : reinterpret_cast<const float4 *>(buf(s_, 0, qp / sub) +
+                                                                                      (size_t)(qp % sub) * RS);
+#pragma unroll 1
+                for (int jj = 0; jj < C4 / NSL8; jj++) {
+                    const int    j = ds + NSL8 * jj;
+                    const float4 kv = k4[j];
+#pragma unroll
+                    for (int hh = 0; hh < NREP; hh++) {
+                        const float4 qv = reinterpret_cast<const float4 *>(q_s + hh * HD)[j];
+                        d[hh] = fmaf(qv.x, kv.x, fmaf(qv.y, kv.y, fmaf(qv.z, kv.z, fmaf(qv.w, kv.w, d[hh]))));
+                    }
                 }
-                s = ((d0 + d1) + (d2 + d3)) * a.kscale;
             }
-            const float mnew = fmaxf(m_run, warp_max(s));
+#pragma unroll
+            for (int o = 1; o < NSL8; o <<= 1)
+#pragma unroll
+                for (int hh = 0; hh < NREP; hh++) d[hh] += __shfl_xor_sync(0xffffffffu, d[hh], o);
+#pragma unroll
+            for (int hh = 0; hh < NREP; hh++)
+                if (ds == hh) sc[hh * 64 + qp] = qp < cn ? d[hh] * a.kscale : -INFINITY;
+        }
+        named_bar(1, nct);
+        // ---- softmax (running max over the rounds)
+        if (warp < NREP) {
+            const float s0 = lane < P ? sc[warp * 64 + lane] : -INFINITY;
+            const float s1 = lane + 32 < P ? sc[warp * 64 + lane + 32] : -INFINITY;
+            const float mnew = fmaxf(m_run, warp_max(fmaxf(s0, s1)));
             const float f = expf(m_run - mnew);
-            const float e = lane < cn ? expf(s - mnew) : 0.0f;
-            l_run = l_run * f + warp_sum(e);
+            const float e0 = s0 == -INFINITY ? 0.0f : expf(s0 - mnew);
+            const float e1 = s1 == -INFINITY ? 0.0f : expf(s1 - mnew);
+            if (lane < P) es[lane * NREP + warp] = e0;
+            if (lane + 32 < P) es[(lane + 32) * NREP + warp] = e1;
+            l_run = l_run * f + warp_sum(e0 + e1);
             m_run = mnew;
-            acc.x *= f; acc.y *= f; acc.z *= f; acc.w *= f;
-            const int dq = lane % LPR;
-#pragma unroll 4
-            for (int pb = 0; pb < cn; pb += RPW) {
-                const int   p = pb + lane / LPR;
-                const float ep = __shfl_sync(0xffffffffu, e, p & 31);
-                if (p < cn) {
-                    const float4 vv = (c0 + p == pos) ? reinterpret_cast<const float4 *>(vnew)[dq]
-                                                      : reinterpret_cast<const float4 *>(vb + p * RS)[dq];
-                    acc.x = fmaf(ep, vv.x, acc.x);
-                    acc.y = fmaf(ep, vv.y, acc.y);
-                    acc.z = fmaf(ep, vv.z, acc.z);
-                    acc.w = fmaf(ep, vv.w, acc.w);
+            if (lane == 0) fs[warp] = f;
+        }
+        named_bar(1, nct);
+        // ---- values
+        {
+#pragma unroll
+            for (int hh = 0; hh < NREP; hh++) {
+                const float f = fs[hh];
+                acc[hh].x *= f; acc[hh].y *= f; acc[hh].z *= f; acc[hh].w *= f;
+            }
+            for (int pp = pg; pp < cn; pp += PG) {
+                const float4 vv = (cb + pp == pos) ? reinterpret_cast<const float4 *>(vnew)[vc]
+                                                   : reinterpret_cast<const float4 *>(buf(s_, 1, pp / sub) +
+                                                                                      (size_t)(pp % sub) * RS)[vc];
+                const float *ep = es + pp * NREP;
+#pragma unroll
+                for (int hh = 0; hh < NREP; hh++) {
+                    const float e = ep[hh];
+                    acc[hh].x = fmaf(e, vv.x, acc[hh].x);
+                    acc[hh].y = fmaf(e, vv.y, acc[hh].y);
+                    acc[hh].z = fmaf(e, vv.z, acc[hh].z);
+                    acc[hh].w = fmaf(e, vv.w, acc[hh].w);
                 }
             }
         }
-        named_bar(1, nct);                          // both halves are free
-        if (r + 1 < nround && (tid & 31) == 0 && tid < 64) issue(r + 1, tid >> 5);
+        named_bar(1, nct);                          // both halves of slot s_ are free
+        if (r + nsl < nround && (tid & 31) == 0 && tid < 64) issue(r + nsl, tid >> 5);
     }
-    att_sb += nround;                               // one phase of each half barrier per round
+    // one phase of each of a slot's half barriers per round that used it
+    // (a round with at most sub positions still completes both halves: its
+    // second half's copy is empty)
+    att_sb0 += (nround + nsl - 1) / nsl;
+    att_sb1 += nsl > 1 ? nround / nsl : 0;
     if (det) det[1] = clock64();
-    // this warp's partial into shared memory; group 0 of each head merges
-    // the G group partials in group order into the CTA's partial
-    float *gpart = S.red;                           // [G][NREP][HD + 4]
-#pragma unroll
-    for (int o = LPR; o < 32; o <<= 1) {
-        acc.x += __shfl_xor_sync(0xffffffffu, acc.x, o);
-        acc.y += __shfl_xor_sync(0xffffffffu, acc.y, o);
-        acc.z += __shfl_xor_sync(0xffffffffu, acc.z, o);
-        acc.w += __shfl_xor_sync(0xffffffffu, acc.w, o);
-    }
+    // the position groups' accumulators into the K/V buffers (free now: every
+    // round's copies have landed), added in group order into the partial
     {
-        float *gp = gpart + (size_t)(grp * NREP + h) * (HD + 4);
-        if (lane < LPR) reinterpret_cast<float4 *>(gp)[lane] = acc;
-        if (lane == 0) {
-            gp[HD] = m_run;
-            gp[HD + 1] = l_run;
-        }
-    }
-    named_bar(1, nct);
-    if (has && grp == 0) {
-        float M = -INFINITY;
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        float4 *gsum = reinterpret_cast<float4 *>(S.kvbuf);  // [PG][NREP][C4]
 #pragma unroll
-        for (int q = 0; q < G; q++) M = fmaxf(M, gpart[(q * NREP + h) * (HD + 4) + HD]);
-        float  L = 0.0f;
-        float4 o4 = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-        for (int q = 0; q < G; q++) {
-            const float *gp = gpart + (size_t)(q * NREP + h) * (HD + 4);
-            const float  mq = gp[HD];
-            const float  w = mq > -INFINITY ? expf(mq - M) : 0.0f;
-            L += gp[HD + 1] * w;
-            if (lane < LPR) {
-                const float4 v = reinterpret_cast<const float4 *>(gp)[lane];
-                o4.x = fmaf(v.x, w, o4.x);
-                o4.y = fmaf(v.y, w, o4.y);
-                o4.z = fmaf(v.z, w, o4.z);
-                o4.w = fmaf(v.w, w, o4.w);
+        for (int hh = 0; hh < NREP; hh++) gsum[((size_t)pg * NREP + hh) * C4 + vc] = acc[hh];
+        named_bar(1, nct);
+        if (has)
+            for (int i = tid; i < NREP * C4; i += nct) {
+                const int hh = i / C4, c = i % C4;
+                float4    o4 = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int q = 0; q < PG; q++) {
+                    const float4 v = gsum[((size_t)q * NREP + hh) * C4 + c];
+                    o4.x += v.x; o4.y += v.y; o4.z += v.z; o4.w += v.w;
+                }
+                float *dst = a.apart + ((size_t)(g * a.n_split + sp) * NREP + hh) * (HD + 4);
+                reinterpret_cast<float4 *>(dst)[c] = o4;
             }
-        }
-        float *dst = a.apart + ((size_t)(g * a.n_split + sp) * NREP + h) * (HD + 4);
-        if (lane < LPR) reinterpret_cast<float4 *>(dst)[lane] = o4;
-        if (lane == 0) {
-            dst[HD] = M;
-            dst[HD + 1] = L;
+        if (has && warp < NREP && lane == 0) {
+            float *dst = a.apart + ((size_t)(g * a.n_split + sp) * NREP + warp) * (HD + 4);
+            dst[HD] = m_run;
+            dst[HD + 1] = l_run;
         }
     }
     // the K/V buffers were filled by the async proxy and read here; the next
@@ -1079,10 +1116,10 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
     if (tid == 0) {
         asm volatile("fence.proxy.async.global;" ::: "memory");
         const uint32_t bytes = (uint32_t)(ns * PER * sizeof(float));
-        mbar_expect_tx(&S.abar[2], bytes);
-        bulk_g2s(S.kvbuf, a.apart + (size_t)g * ns * PER, bytes, &S.abar[2]);
+        mbar_expect_tx(&S.abar[4], bytes);
+        bulk_g2s(S.kvbuf, a.apart + (size_t)g * ns * PER, bytes, &S.abar[4]);
     }
-    mbar_wait<true>(&S.abar[2], (unsigned)merges & 1u, a.status);
+    mbar_wait<true>(&S.abar[4], (unsigned)merges & 1u, a.status);
     merges++;
     const float *gat = S.kvbuf;
     if (warp < NREP) {                         // warp hh: its head's split weights, lanes over splits
@@ -1180,9 +1217,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < a.nst; s++) mbar_init(&S.full[s], 1);
-        mbar_init(&S.abar[0], 1);
-        mbar_init(&S.abar[1], 1);
-        mbar_init(&S.abar[2], 1);
+        for (int k = 0; k < 5; k++) mbar_init(&S.abar[k], 1);
         mbar_init(&desc_bar, 1);
         mbar_init_fence();
         pos_s = a.st->pos;            // stable for the whole step
@@ -1211,7 +1246,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a)
         a.phase_clk[0] = clock64();
     }
     RingPos rpos{0, 0u};
-    int att_sb = 0, merges = 0;
+    int att_sb0 = 0, att_sb1 = 0, merges = 0;
     for (int p = 0; p < a.n_ph; p++) {
         // descriptors live in shared memory: phase p's arrived by a bulk
         // copy issued at the start of phase p-1, and phase p+1's is issued
@@ -1229,7 +1264,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a)
         if (kind == PH_GEMV) {
             mega_gemv<SYS>(a, ph, S, rpos, p, ph.next_attn ? &ph_s[(p + 1) & 1] : nullptr, HD);
         } else if (kind == PH_ATTN) {
-            mega_attention<HD, NREP, SYS>(a, ph, S, att_sb, merges, p);
+            mega_attention<HD, NREP, SYS>(a, ph, S, att_sb0, att_sb1, merges, p);
         } else {
             mega_embed<SYS>(a, S, p);
         }
@@ -1249,7 +1284,10 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a)
         const int n = S.rc->issued;
         for (int j = max(0, n - a.nst); j < n; j++)
             mbar_drain(&S.full[j % a.nst], (unsigned)(j / a.nst) & 1u, ECU_WAIT_NS);
-        for (int k = 0; k < 2 && att_sb > 0; k++) mbar_drain(&S.abar[k], (unsigned)(att_sb - 1) & 1u, ECU_WAIT_NS);
+        for (int k = 0; k < 4; k++) {
+            const int n_used = k < 2 ? att_sb0 : att_sb1;
+            if (n_used > 0) mbar_drain(&S.abar[k], (unsigned)(n_used - 1) & 1u, ECU_WAIT_NS);
+        }
     }
     // a LAYERS stage advances its position once every phase is done; no
     // CTA reads it after the last attention phase

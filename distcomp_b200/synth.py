@@ -60,6 +60,8 @@ SPECS = {
     # column segment (ffn_down kept as two segments of 10240 inputs)
     "mini-q4k": LlamaSpec(2, 1024, 8, 2, 2048, 2048, 128, 500000.0, wtype=G.Q4_K),
     "wide-q4k": LlamaSpec(2, 1024, 8, 1, 20480, 2048, 96, 10000.0, wtype=G.Q4_K),
+    # one layer of the 70B shape (n_embd 8192, 64/8 heads, ffn 28672), small vocab
+    "l70-1": LlamaSpec(1, 8192, 64, 8, 28672, 2048, 64, 10000.0, wtype=G.Q4_K),
 }
 
 

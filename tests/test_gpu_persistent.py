@@ -121,3 +121,23 @@ def test_profile_phases(eng, model_buf):
     # GEMV phases also report where CTA 0 spent them
     assert prof["gemv_gate_up:main"][0] == 3 * s.n_layer
     assert 0 < total <= prof["decode_step"][1] * 1.05
+
+
+@pytest.mark.parametrize("key", ["mini-q4", "mini-q8"])
+@pytest.mark.parametrize("att,split", [("1", "1"), ("2", "1"), ("2", "3")])
+def test_attention_slots_and_splits_vs_oracle(eng, oracle_port, model_buf, key, att, split, monkeypatch):
+    """The persistent step's K/V buffers in one slot or in two (the copies
+    of round r+1 in flight while round r is computed), with one or three
+    position splits per KV head so that a split walks several rounds: the
+    oracle's greedy tokens over the whole context."""
+    import oracle
+    s = synth.spec(key)
+    buf = model_buf(key)
+    prompt = synth.prompt_tokens(5, s.n_vocab, seed=31)
+    n_gen = s.n_ctx - len(prompt) + 1
+    want = oracle.greedy(oracle_port, buf, prompt, n_gen)
+    monkeypatch.setenv("ECU_MEGA_ATT", att)
+    monkeypatch.setenv("ECU_MEGA_SPLIT", split)
+    c = open_ctx(eng, eng.GgufModel(buf), eng.STAGE_FULL)
+    assert c.path() == "persistent"
+    assert c.generate(prompt, n_gen) == want

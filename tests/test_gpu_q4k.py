@@ -136,3 +136,28 @@ def test_q4k_prefill_vs_per_token(eng, oracle_port, model_buf, key):
         tok = int(out_a[s.n_embd])
         toks.append(tok)
     assert toks == oracle.greedy(oracle_port, buf, prompt, n_gen)
+
+
+def test_q4k_70b_layer_shape_vs_oracle(eng, oracle_port, model_buf):
+    """One layer of the 70B shape: n_embd 8192 (the persistent step's ring
+    stages shrink to leave room for its norm staging), ffn_down as two
+    14336-input segments, 8 query heads per KV head."""
+    import oracle
+    key = "l70-1"
+    s = synth.spec(key)
+    buf = model_buf(key)
+    m = eng.GgufModel(buf)
+    c = open_ctx(eng, m, eng.STAGE_FULL)
+    assert c.path() == "persistent"
+    prompt = synth.prompt_tokens(3, s.n_vocab, seed=70)
+    om = oracle_port.model(buf)
+    oe, ol, oh = om.ctx(0), om.ctx(1, 0, s.n_layer - 1), om.ctx(2)
+    out, ob = np.zeros(s.n_embd + 1, np.float32), np.zeros(s.n_embd + 8, np.float32)
+    for t in prompt:
+        assert c.forward(t, out) == 0
+        for o in (oe, ol, oh):
+            assert o.forward(t, ob) == 0
+        ok, err = vec_close(c.logits(), oh.logits(s.n_vocab))
+        assert ok, f"logits rel err {err:.2e}"
+    c.reset()
+    assert c.generate(prompt, 4) == oracle.greedy(oracle_port, buf, prompt, 4)

@@ -360,12 +360,17 @@ __device__ __forceinline__ void make_digits(const float *xv, int (&xw)[3][8], in
 // dmin, scales[12] as four little-endian words): dl = d*sc and ml = dmin*m,
 // the reference's two products (gguf.c:558-590).  Byte k of the scales is
 // s[k]; with jj = j & 3 the pair needs s[jj], s[4+jj] and s[8+jj] only.
+// Sub-blocks 4-7 take their low 4 bits from s[8+jj] and the top 2 from bits
+// 6-7 of s[jj] / s[4+jj]: with lane-constant shift and masks both cases are
+// sc = ((A >> sA) & mA) | (C & mC), m = ((B >> sA) & mA) | ((C >> 4) & mC).
 __device__ __forceinline__ void k4_scale_min(uint4 h, int j, float &dl, float &ml)
 {
     const int      sh = 8 * (j & 3);
+    const bool     up = j >= 4;
+    const uint32_t sA = up ? 2u : 0u, mA = up ? 0x30u : 0x3Fu, mC = up ? 0x0Fu : 0u;
     const uint32_t A = (h.y >> sh) & 0xFFu, B = (h.z >> sh) & 0xFFu, C = (h.w >> sh) & 0xFFu;
-    const uint32_t sc = j < 4 ? (A & 63u) : ((C & 0x0Fu) | ((A >> 6) << 4));
-    const uint32_t mn = j < 4 ? (B & 63u) : ((C >> 4) | ((B >> 6) << 4));
+    const uint32_t sc = ((A >> sA) & mA) | (C & mC);
+    const uint32_t mn = ((B >> sA) & mA) | ((C >> 4) & mC);
     const float    d = __half2float(__ushort_as_half((unsigned short)(h.x & 0xFFFFu)));
     const float    dmin = __half2float(__ushort_as_half((unsigned short)(h.x >> 16)));
     dl = __fmul_rn(d, (float)sc);

@@ -534,6 +534,41 @@ __device__ __forceinline__ void block_dot4(const uint8_t *row0, size_t stride, i
             const int t = (acc[k][0] + acc[k][3]) * 16384 + (acc[k][1] + acc[k][4]) * 128 + (acc[k][2] + acc[k][5]);
             v[k] = (float)t * (d[k] * sxs);
         }
+    } else if (FMT == 12) {
+        // Q4_K (SPLITK4): the same split chains on plain codes (off holds the
+        // digit sums), then each row's sub-block scale and minimum
+        uint4 q[4], hd[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            q[k] = *reinterpret_cast<const uint4 *>(row0 + k * stride + (size_t)b * 16);
+            hd[k] = *reinterpret_cast<const uint4 *>(row0 + k * stride + (size_t)nb * 16 + (size_t)(b >> 3) * 16);
+        }
+        int acc[4][6];
+#pragma unroll
+        for (int k = 0; k < 4; k++)
+#pragma unroll
+            for (int i = 0; i < 6; i++) acc[k][i] = 0;
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const uint32_t w = j == 0 ? q[k].x : j == 1 ? q[k].y : j == 2 ? q[k].z : q[k].w;
+                const int lo = (int)(w & 0x0F0F0F0Fu), hi = (int)((w >> 4) & 0x0F0F0F0Fu);
+                acc[k][0] = __dp4a(lo, xw[0][j], acc[k][0]);
+                acc[k][3] = __dp4a(hi, xw[0][4 + j], acc[k][3]);
+                acc[k][1] = __dp4a(lo, xw[1][j], acc[k][1]);
+                acc[k][4] = __dp4a(hi, xw[1][4 + j], acc[k][4]);
+                acc[k][2] = __dp4a(lo, xw[2][j], acc[k][2]);
+                acc[k][5] = __dp4a(hi, xw[2][4 + j], acc[k][5]);
+            }
+        const int sx = off[0] * 16384 + off[1] * 128 + off[2];
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int t = (acc[k][0] + acc[k][3]) * 16384 + (acc[k][1] + acc[k][4]) * 128 + (acc[k][2] + acc[k][5]);
+            float dl, ml;
+            k4_scale_min(hd[k], b & 7, dl, ml);
+            v[k] = k4_finish(t, sx, dl, ml, sxs);
+        }
     } else {
 #pragma unroll
         for (int k = 0; k < 4; k++) v[k] = block_dot<FMT>(row0 + k * stride, nb, b, xw, off, sxs);

@@ -715,6 +715,10 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
     // them in this phase; nrows <= MEGA_THREADS for EPI_ADD): requested now,
     // settled after the prologue
     const bool has_res = epi == EPI_ADD && tid < nrows;
+    // the RoPE row the next phase (attention) needs, requested now so that
+    // its latency hides behind this phase (hd <= MEGA_THREADS)
+    float cs_next = 0.0f;
+    if (ph.next_attn && tid < hd) cs_next = __ldg(a.rope_cs + (size_t)S.pos * hd + tid);
     unsigned long long yw = 0;
     if (has_res && ph.y_ep >= 0) yw = ll_word<SYS>(a.x_ll + ph.out_base + r0 + tid);
 
@@ -808,7 +812,7 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
         // next phase's descriptor: its copy was issued at this phase's start
         mbar_wait<true>(S.dbar, (unsigned)p_idx & 1u, a.status);
         if (tid == 0 && a.att_l2) attn_prefetch(a, *next, S.pos, hd);
-        for (int j = tid; j < hd; j += nct) S.cs[j] = a.rope_cs[(size_t)S.pos * hd + j];
+        if (tid < hd) S.cs[tid] = cs_next;
     }
 
     // ---- epilogue over this CTA's rows --------------------------------------

@@ -26,9 +26,9 @@ def run_ranks(tmp_path, world, key, port):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("key", ["mini-q4", "mini-q8"])
+@pytest.mark.parametrize("key", ["mini-q4", "mini-q8", "mini-q4k"])
 def test_tp2_matches_one_gpu(tmp_path, key):
-    run_ranks(tmp_path, 2, key, 29541 if key == "mini-q4" else 29542)
+    run_ranks(tmp_path, 2, key, {"mini-q4": 29541, "mini-q8": 29542, "mini-q4k": 29544}[key])
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 4, reason="needs four GPUs")

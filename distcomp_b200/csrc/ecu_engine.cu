@@ -453,7 +453,8 @@ struct ecu_ctx {
     StepState *st = nullptr;      // device
     StepState *h_st = nullptr;    // pinned host slots, one per position: an
                                   // async copy may still be reading slot p
-                                  // while the host fills slot p+1
+                                  // while the host fills slot p+1; slot
+                                  // n_hslots receives the device state
     int        n_hslots = 0;
     float    *h_state = nullptr;  // pinned host staging, n_embd + 1
     int      *tok_hist = nullptr; // device [n_ctx]
@@ -829,9 +830,12 @@ static int run_step(ecu_ctx *c)
 
 static int check_status(ecu_ctx *c)
 {
+    // the step state comes back with the step's other results: one async
+    // copy into the pinned slot past the position slots, one synchronisation
+    StepState *hs = c->h_st + c->n_hslots;
+    CK(cudaMemcpyAsync(hs, c->st, sizeof(StepState), cudaMemcpyDeviceToHost, c->stream));
     CK(cudaStreamSynchronize(c->stream));
-    StepState s;
-    CK(cudaMemcpy(&s, c->st, sizeof s, cudaMemcpyDeviceToHost));
+    const StepState s = *hs;
     if (s.status) {
         if (c->mega) {
             // counters and launch number restart at zero: the tagged vectors
@@ -1525,10 +1529,10 @@ static const char *alloc_buffers(ecu_ctx *c, bool layers, bool head)
     cudaMemset(c->scr.counter, 0, 4 * sizeof(unsigned));
     cudaMemset(c->state, 0, ((size_t)g.n_embd + 4) * sizeof(float));
     c->n_hslots = g.n_ctx + 1;
-    if (cudaMallocHost(&c->h_st, sizeof(StepState) * (size_t)c->n_hslots) != cudaSuccess ||
+    if (cudaMallocHost(&c->h_st, sizeof(StepState) * ((size_t)c->n_hslots + 1)) != cudaSuccess ||
         cudaMallocHost(&c->h_state, ((size_t)g.n_embd + 4) * sizeof(float)) != cudaSuccess)
         return "pinned host staging";
-    memset(c->h_st, 0, sizeof(StepState) * (size_t)c->n_hslots);
+    memset(c->h_st, 0, sizeof(StepState) * ((size_t)c->n_hslots + 1));
     if (head) {
         c->logits = c->dalloc<float>((size_t)(c->tp.v1 - c->tp.v0) + 4);
         if (!c->logits) return "logits";

@@ -131,3 +131,21 @@ def test_ctx_open_geometry_errors(model_buf):
         engine.LlmCtx(m, engine.STAGE_LAYERS, 2, 9)
     with pytest.raises(engine.EngineError, match="unknown stage"):
         engine.LlmCtx(m, 7)
+
+
+def test_ctx_bytes_q4k_segments_host_only(model_buf):
+    """Q4_K weights in their device layout (18 bytes per 32 weights, the GGUF
+    size) and an ffn_down wider than one column segment cost exactly their
+    file bytes on the device: the footprint is the layers' tensor bytes plus
+    the KV cache and bounded work buffers."""
+    from distcomp_b200 import gguf as G
+    from distcomp_b200 import synth
+    s = synth.spec("wide-q4k")
+    m = engine.GgufModel(model_buf("wide-q4k"))
+    n_ctx = 96
+    got = engine.ctx_bytes(m, engine.STAGE_LAYERS, 0, s.n_layer - 1, n_ctx)
+    w = sum(G.type_nbytes(gt, int(np.prod(dims))) for name, dims, gt in synth.tensor_list(s)
+            if name.startswith("blk.") and "norm" not in name)
+    hd = s.n_embd // s.n_head
+    kv = 2 * s.n_layer * n_ctx * s.n_head_kv * hd * 4
+    assert w + kv <= got <= w + kv + (8 << 20)

@@ -502,15 +502,27 @@ static __global__ void __launch_bounds__(HD) k_pf_attn(const float *QKV, int ld,
 // at a time through shared memory, so every K/V row is read once per 64
 // queries instead of once per query.  Thread tid serves query tid / 4: its 8
 // scores of a chunk (positions tid % 4 + 4j), a running max and sum shared
-// by the query's 4 threads, and 32 output dims (tid % 4 + 4j; HD = 128).
-// Softmax as k_pf_attn: scores * kscale, expf against the running max, one
-// division by the sum at the end.
+// by the query's 4 threads, and the HD/4 contiguous output dims of quarter
+// tid % 4.  Shared memory is read in float4s: Q and K rows padded to HD + 4
+// floats (the 8 queries / 4 rows a warp reads fall in distinct bank quads),
+// V rows with 4 floats of padding after every quarter (the 4 quarters a warp
+// reads start in distinct bank quads).  Softmax as k_pf_attn: scores *
+// kscale, expf against the running max, one division by the sum at the end.
 #define PF_QB 64
 #define PF_KC 32
 template <int HD>
+struct PfAttnGeom {
+    static constexpr int QS = HD + 4;                 // Q / K row stride (floats)
+    static constexpr int DQ = HD / 4;                 // output dims of a quarter
+    static constexpr int VQ = DQ + 4;                 // V quarter stride
+    static constexpr int VS = 4 * VQ;                 // V row stride
+};
+
+template <int HD>
 __host__ __device__ constexpr size_t pf_attn2_smem()
 {
-    return ((size_t)PF_QB * (HD + 1) + (size_t)PF_KC * (HD + 1) + (size_t)PF_KC * HD + (size_t)PF_QB * (PF_KC + 1)) *
+    return ((size_t)PF_QB * PfAttnGeom<HD>::QS + (size_t)PF_KC * PfAttnGeom<HD>::QS +
+            (size_t)PF_KC * PfAttnGeom<HD>::VS + (size_t)PF_QB * (PF_KC + 1)) *
            sizeof(float);
 }
 
@@ -519,44 +531,49 @@ static __global__ void __launch_bounds__(256) k_pf_attn2(const float *QKV, int l
                                                           int pos0, const float *kc, const float *vc, int n_ctx,
                                                           float kscale, float *att)
 {
-    constexpr int DPT = HD / 4;                     // output dims per thread
+    using Gm = PfAttnGeom<HD>;
+    constexpr int QS = Gm::QS, DQ = Gm::DQ, VQ = Gm::VQ, VS = Gm::VS, C4 = HD / 4;
+    static_assert(DQ % 4 == 0, "head_dim a multiple of 16");
     extern __shared__ __align__(16) float pf_att_sm[];
-    // padded rows (HD + 1, 33): the 8 queries of a warp hit 8 banks
-    float *QS = pf_att_sm;                          // [64][HD + 1]
-    float *KS = QS + PF_QB * (HD + 1);              // [32][HD + 1]
-    float *VS = KS + PF_KC * (HD + 1);              // [32][HD]
-    float *PS = VS + PF_KC * HD;                    // [64][33]
+    float *QSm = pf_att_sm;                         // [64][QS]
+    float *KSm = QSm + PF_QB * QS;                  // [32][QS]
+    float *VSm = KSm + PF_KC * QS;                  // [32][VS]
+    float *PS = VSm + PF_KC * VS;                   // [64][33]
     const int tid = threadIdx.x, g = blockIdx.x, tb = PF_QB / n_rep, t0 = blockIdx.y * tb;
     const int qi = tid >> 2, sub = tid & 3;
     const int t = t0 + qi / n_rep, h = g * n_rep + qi % n_rep;
     const bool qv = t < n;
     for (int i = tid; i < PF_QB * HD; i += 256) {
         const int q = i / HD, d = i % HD, tq = t0 + q / n_rep, hq = g * n_rep + q % n_rep;
-        QS[q * (HD + 1) + d] = tq < n ? QKV[(size_t)tq * ld + (size_t)hq * HD + d] : 0.0f;
+        QSm[q * QS + d] = tq < n ? QKV[(size_t)tq * ld + (size_t)hq * HD + d] : 0.0f;
     }
     const int   last = pos0 + min(n, t0 + tb) - 1;      // last key position any query sees
     const int   mypos = pos0 + t;                        // this query's own position
     const float *kb = kc + (size_t)g * n_ctx * HD, *vb = vc + (size_t)g * n_ctx * HD;
-    float m_run = -INFINITY, l_run = 0.0f, o[DPT];
+    float m_run = -INFINITY, l_run = 0.0f, o[DQ];
 #pragma unroll
-    for (int j = 0; j < DPT; j++) o[j] = 0.0f;
+    for (int j = 0; j < DQ; j++) o[j] = 0.0f;
+    const float4 *q4 = reinterpret_cast<const float4 *>(QSm + qi * QS);
     for (int c0 = 0; c0 <= last; c0 += PF_KC) {
         __syncthreads();                                 // previous chunk's K/V/P consumed
         for (int i = tid; i < PF_KC * HD; i += 256) {
             const int p = i / HD, d = i % HD, kp = c0 + p;
             const bool ok = kp <= last;
-            KS[p * (HD + 1) + d] = ok ? kb[(size_t)kp * HD + d] : 0.0f;
-            VS[p * HD + d] = ok ? vb[(size_t)kp * HD + d] : 0.0f;
+            KSm[p * QS + d] = ok ? kb[(size_t)kp * HD + d] : 0.0f;
+            VSm[p * VS + (d / DQ) * VQ + d % DQ] = ok ? vb[(size_t)kp * HD + d] : 0.0f;
         }
         __syncthreads();
         float sc[PF_KC / 4];
 #pragma unroll
         for (int j = 0; j < PF_KC / 4; j++) sc[j] = 0.0f;
-        const float *q = QS + qi * (HD + 1);
-        for (int d = 0; d < HD; d++) {
-            const float qd = q[d];
+#pragma unroll 4
+        for (int c = 0; c < C4; c++) {
+            const float4 qv4 = q4[c];
 #pragma unroll
-            for (int j = 0; j < PF_KC / 4; j++) sc[j] = fmaf(qd, KS[(sub + 4 * j) * (HD + 1) + d], sc[j]);
+            for (int j = 0; j < PF_KC / 4; j++) {
+                const float4 kv = reinterpret_cast<const float4 *>(KSm + (sub + 4 * j) * QS)[c];
+                sc[j] = fmaf(qv4.x, kv.x, fmaf(qv4.y, kv.y, fmaf(qv4.z, kv.z, fmaf(qv4.w, kv.w, sc[j]))));
+            }
         }
         float cm = -INFINITY;
 #pragma unroll
@@ -582,18 +599,25 @@ static __global__ void __launch_bounds__(256) k_pf_attn2(const float *QKV, int l
         m_run = mnew;
         __syncwarp();
 #pragma unroll
-        for (int j = 0; j < DPT; j++) o[j] *= f;
+        for (int j = 0; j < DQ; j++) o[j] *= f;
         for (int p = 0; p < PF_KC; p++) {
-            const float e = PS[qi * (PF_KC + 1) + p];
-            const float *vr = VS + p * HD + sub;
+            const float   e = PS[qi * (PF_KC + 1) + p];
+            const float4 *vr = reinterpret_cast<const float4 *>(VSm + p * VS + sub * VQ);
 #pragma unroll
-            for (int j = 0; j < DPT; j++) o[j] = fmaf(e, vr[4 * j], o[j]);
+            for (int c = 0; c < DQ / 4; c++) {
+                const float4 v = vr[c];
+                o[4 * c] = fmaf(e, v.x, o[4 * c]);
+                o[4 * c + 1] = fmaf(e, v.y, o[4 * c + 1]);
+                o[4 * c + 2] = fmaf(e, v.z, o[4 * c + 2]);
+                o[4 * c + 3] = fmaf(e, v.w, o[4 * c + 3]);
+            }
         }
     }
     if (qv) {
-        float *dst = att + (size_t)t * n_head * HD + (size_t)h * HD + sub;
+        float4 *dst = reinterpret_cast<float4 *>(att + (size_t)t * n_head * HD + (size_t)h * HD + sub * DQ);
 #pragma unroll
-        for (int j = 0; j < DPT; j++) dst[4 * j] = o[j] / l_run;
+        for (int c = 0; c < DQ / 4; c++)
+            dst[c] = make_float4(o[4 * c] / l_run, o[4 * c + 1] / l_run, o[4 * c + 2] / l_run, o[4 * c + 3] / l_run);
     }
 }
 

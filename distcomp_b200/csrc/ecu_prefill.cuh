@@ -506,8 +506,10 @@ static __global__ void __launch_bounds__(HD) k_pf_attn(const float *QKV, int ld,
 // tid % 4.  Shared memory is read in float4s: Q and K rows padded to HD + 4
 // floats (the 8 queries / 4 rows a warp reads fall in distinct bank quads),
 // V rows with 4 floats of padding after every quarter (the 4 quarters a warp
-// reads start in distinct bank quads).  Softmax as k_pf_attn: scores *
-// kscale, expf against the running max, one division by the sum at the end.
+// reads start in distinct bank quads).  The K/V rows of chunk c+1 stream in
+// by cp.async (two buffers) while chunk c is computed.  Softmax as
+// k_pf_attn: scores * kscale, expf against the running max, one division by
+// the sum at the end.
 #define PF_QB 64
 #define PF_KC 32
 template <int HD>
@@ -521,8 +523,8 @@ struct PfAttnGeom {
 template <int HD>
 __host__ __device__ constexpr size_t pf_attn2_smem()
 {
-    return ((size_t)PF_QB * PfAttnGeom<HD>::QS + (size_t)PF_KC * PfAttnGeom<HD>::QS +
-            (size_t)PF_KC * PfAttnGeom<HD>::VS + (size_t)PF_QB * (PF_KC + 1)) *
+    return ((size_t)PF_QB * PfAttnGeom<HD>::QS + 2 * (size_t)PF_KC * PfAttnGeom<HD>::QS +
+            2 * (size_t)PF_KC * PfAttnGeom<HD>::VS + (size_t)PF_QB * (PF_KC + 1)) *
            sizeof(float);
 }
 
@@ -536,9 +538,9 @@ static __global__ void __launch_bounds__(256) k_pf_attn2(const float *QKV, int l
     static_assert(DQ % 4 == 0, "head_dim a multiple of 16");
     extern __shared__ __align__(16) float pf_att_sm[];
     float *QSm = pf_att_sm;                         // [64][QS]
-    float *KSm = QSm + PF_QB * QS;                  // [32][QS]
-    float *VSm = KSm + PF_KC * QS;                  // [32][VS]
-    float *PS = VSm + PF_KC * VS;                   // [64][33]
+    float *KSb = QSm + PF_QB * QS;                  // [2][32][QS]
+    float *VSb = KSb + 2 * PF_KC * QS;              // [2][32][VS]
+    float *PS = VSb + 2 * PF_KC * VS;               // [64][33]
     const int tid = threadIdx.x, g = blockIdx.x, tb = PF_QB / n_rep, t0 = blockIdx.y * tb;
     const int qi = tid >> 2, sub = tid & 3;
     const int t = t0 + qi / n_rep, h = g * n_rep + qi % n_rep;
@@ -554,15 +556,29 @@ static __global__ void __launch_bounds__(256) k_pf_attn2(const float *QKV, int l
 #pragma unroll
     for (int j = 0; j < DQ; j++) o[j] = 0.0f;
     const float4 *q4 = reinterpret_cast<const float4 *>(QSm + qi * QS);
-    for (int c0 = 0; c0 <= last; c0 += PF_KC) {
-        __syncthreads();                                 // previous chunk's K/V/P consumed
-        for (int i = tid; i < PF_KC * HD; i += 256) {
-            const int p = i / HD, d = i % HD, kp = c0 + p;
+    // K and V rows of the chunk at c into buffer b: 16-byte pieces, zero
+    // past the last position any query sees
+    auto load = [&](int c, int b) {
+        float *K = KSb + b * PF_KC * QS, *V = VSb + b * PF_KC * VS;
+        for (int i = tid; i < PF_KC * C4; i += 256) {
+            const int  p = i / C4, d = 4 * (i % C4), kp = c + p;
             const bool ok = kp <= last;
-            KSm[p * QS + d] = ok ? kb[(size_t)kp * HD + d] : 0.0f;
-            VSm[p * VS + (d / DQ) * VQ + d % DQ] = ok ? vb[(size_t)kp * HD + d] : 0.0f;
+            const size_t src = ok ? (size_t)kp * HD + d : 0;
+            pf_cp16(K + p * QS + d, kb + src, ok);
+            pf_cp16(V + p * VS + (d / DQ) * VQ + d % DQ, vb + src, ok);
         }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    __syncthreads();                                     // Q rows stored
+    load(0, 0);
+    for (int c0 = 0, ci = 0; c0 <= last; c0 += PF_KC, ci++) {
+        // the next chunk's copies (an empty group past the end keeps the
+        // count), then wait for this chunk's
+        if (c0 + PF_KC <= last) load(c0 + PF_KC, (ci + 1) & 1);
+        else asm volatile("cp.async.commit_group;" ::: "memory");
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
         __syncthreads();
+        const float *KSm = KSb + (ci & 1) * PF_KC * QS, *VSm = VSb + (ci & 1) * PF_KC * VS;
         float sc[PF_KC / 4];
 #pragma unroll
         for (int j = 0; j < PF_KC / 4; j++) sc[j] = 0.0f;
@@ -612,7 +628,9 @@ static __global__ void __launch_bounds__(256) k_pf_attn2(const float *QKV, int l
                 o[4 * c + 3] = fmaf(e, v.w, o[4 * c + 3]);
             }
         }
+        __syncthreads();                                 // this buffer and PS consumed
     }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
     if (qv) {
         float4 *dst = reinterpret_cast<float4 *>(att + (size_t)t * n_head * HD + (size_t)h * HD + sub * DQ);
 #pragma unroll

@@ -500,31 +500,32 @@ static __global__ void __launch_bounds__(HD) k_pf_attn(const float *QKV, int ld,
 // and 64 / n_rep consecutive tokens, i.e. 64 query vectors (query qi = token
 // qi / n_rep, head g*n_rep + qi % n_rep), and walks the cache 32 positions
 // at a time through shared memory, so every K/V row is read once per 64
-// queries instead of once per query.  Thread tid serves query tid / 4: its 8
-// scores of a chunk (positions tid % 4 + 4j), a running max and sum shared
-// by the query's 4 threads, and the HD/4 contiguous output dims of quarter
-// tid % 4.  Shared memory is read in float4s: Q and K rows padded to HD + 4
-// floats (the 8 queries / 4 rows a warp reads fall in distinct bank quads),
-// V rows with 4 floats of padding after every quarter (the 4 quarters a warp
-// reads start in distinct bank quads).  The K/V rows of chunk c+1 stream in
-// by cp.async (two buffers) while chunk c is computed.  Softmax as
-// k_pf_attn: scores * kscale, expf against the running max, one division by
-// the sum at the end.
+// queries instead of once per query.  Thread tid serves the query pair
+// 2*(tid/8), 2*(tid/8)+1: its 4 scores per query of a chunk (positions
+// tid % 8 + 8j), a running max and sum per query shared by the pair's 8
+// threads, and the HD/8 contiguous output dims of eighth tid % 8 for both
+// queries, so every K and V float4 read from shared memory feeds two
+// queries.  Q and K rows are padded to HD + 4 floats, V rows carry 4 floats
+// of padding after every eighth: the rows (eighths) a warp reads start in
+// distinct bank quads.  K/V rows arrive by cp.async (one buffer: two CTAs
+// of this kernel share an SM, each one's copies overlap the other's
+// arithmetic).  Softmax as k_pf_attn: scores * kscale, expf against the
+// running max, one division by the sum at the end.
 #define PF_QB 64
 #define PF_KC 32
 template <int HD>
 struct PfAttnGeom {
     static constexpr int QS = HD + 4;                 // Q / K row stride (floats)
-    static constexpr int DQ = HD / 4;                 // output dims of a quarter
-    static constexpr int VQ = DQ + 4;                 // V quarter stride
-    static constexpr int VS = 4 * VQ;                 // V row stride
+    static constexpr int DE = HD / 8;                 // output dims of an eighth
+    static constexpr int VE = DE + 4;                 // V eighth stride
+    static constexpr int VS = 8 * VE;                 // V row stride
 };
 
 template <int HD>
 __host__ __device__ constexpr size_t pf_attn2_smem()
 {
-    return ((size_t)PF_QB * PfAttnGeom<HD>::QS + 2 * (size_t)PF_KC * PfAttnGeom<HD>::QS +
-            2 * (size_t)PF_KC * PfAttnGeom<HD>::VS + (size_t)PF_QB * (PF_KC + 1)) *
+    return ((size_t)PF_QB * PfAttnGeom<HD>::QS + (size_t)PF_KC * PfAttnGeom<HD>::QS +
+            (size_t)PF_KC * PfAttnGeom<HD>::VS + (size_t)PF_QB * (PF_KC + 1)) *
            sizeof(float);
 }
 
@@ -534,108 +535,131 @@ static __global__ void __launch_bounds__(256) k_pf_attn2(const float *QKV, int l
                                                           float kscale, float *att)
 {
     using Gm = PfAttnGeom<HD>;
-    constexpr int QS = Gm::QS, DQ = Gm::DQ, VQ = Gm::VQ, VS = Gm::VS, C4 = HD / 4;
-    static_assert(DQ % 4 == 0, "head_dim a multiple of 16");
+    constexpr int QS = Gm::QS, DE = Gm::DE, VE = Gm::VE, VS = Gm::VS, C4 = HD / 4, NP = PF_KC / 8;
+    static_assert(DE % 4 == 0, "head_dim a multiple of 32");
     extern __shared__ __align__(16) float pf_att_sm[];
     float *QSm = pf_att_sm;                         // [64][QS]
-    float *KSb = QSm + PF_QB * QS;                  // [2][32][QS]
-    float *VSb = KSb + 2 * PF_KC * QS;              // [2][32][VS]
-    float *PS = VSb + 2 * PF_KC * VS;               // [64][33]
+    float *KSm = QSm + PF_QB * QS;                  // [32][QS]
+    float *VSm = KSm + PF_KC * QS;                  // [32][VS]
+    float *PS = VSm + PF_KC * VS;                   // [64][33]
     const int tid = threadIdx.x, g = blockIdx.x, tb = PF_QB / n_rep, t0 = blockIdx.y * tb;
-    const int qi = tid >> 2, sub = tid & 3;
-    const int t = t0 + qi / n_rep, h = g * n_rep + qi % n_rep;
-    const bool qv = t < n;
+    const int qa = 2 * (tid >> 3), qb = qa + 1, sub = tid & 7;
+    const int ta = t0 + qa / n_rep, ha = g * n_rep + qa % n_rep;
+    const int tq = t0 + qb / n_rep, hb = g * n_rep + qb % n_rep;
+    const bool va = ta < n, vbq = tq < n;
     for (int i = tid; i < PF_QB * HD; i += 256) {
-        const int q = i / HD, d = i % HD, tq = t0 + q / n_rep, hq = g * n_rep + q % n_rep;
-        QSm[q * QS + d] = tq < n ? QKV[(size_t)tq * ld + (size_t)hq * HD + d] : 0.0f;
+        const int q = i / HD, d = i % HD, tt = t0 + q / n_rep, hq = g * n_rep + q % n_rep;
+        QSm[q * QS + d] = tt < n ? QKV[(size_t)tt * ld + (size_t)hq * HD + d] : 0.0f;
     }
     const int   last = pos0 + min(n, t0 + tb) - 1;      // last key position any query sees
-    const int   mypos = pos0 + t;                        // this query's own position
+    const int   pa = pos0 + ta, pb = pos0 + tq;          // the queries' own positions
     const float *kb = kc + (size_t)g * n_ctx * HD, *vb = vc + (size_t)g * n_ctx * HD;
-    float m_run = -INFINITY, l_run = 0.0f, o[DQ];
+    float ma = -INFINITY, la = 0.0f, mb = -INFINITY, lb = 0.0f, oa[DE], ob[DE];
 #pragma unroll
-    for (int j = 0; j < DQ; j++) o[j] = 0.0f;
-    const float4 *q4 = reinterpret_cast<const float4 *>(QSm + qi * QS);
-    // K and V rows of the chunk at c into buffer b: 16-byte pieces, zero
-    // past the last position any query sees
-    auto load = [&](int c, int b) {
-        float *K = KSb + b * PF_KC * QS, *V = VSb + b * PF_KC * VS;
+    for (int j = 0; j < DE; j++) oa[j] = ob[j] = 0.0f;
+    const float4 *qa4 = reinterpret_cast<const float4 *>(QSm + qa * QS);
+    const float4 *qb4 = reinterpret_cast<const float4 *>(QSm + qb * QS);
+    // K and V rows of the chunk at c: 16-byte pieces, zero past the last
+    // position any query sees
+    auto load = [&](int c) {
+        float *K = KSm, *V = VSm;
         for (int i = tid; i < PF_KC * C4; i += 256) {
             const int  p = i / C4, d = 4 * (i % C4), kp = c + p;
             const bool ok = kp <= last;
             const size_t src = ok ? (size_t)kp * HD + d : 0;
             pf_cp16(K + p * QS + d, kb + src, ok);
-            pf_cp16(V + p * VS + (d / DQ) * VQ + d % DQ, vb + src, ok);
+            pf_cp16(V + p * VS + (d / DE) * VE + d % DE, vb + src, ok);
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
-    __syncthreads();                                     // Q rows stored
-    load(0, 0);
-    for (int c0 = 0, ci = 0; c0 <= last; c0 += PF_KC, ci++) {
-        // the next chunk's copies (an empty group past the end keeps the
-        // count), then wait for this chunk's
-        if (c0 + PF_KC <= last) load(c0 + PF_KC, (ci + 1) & 1);
-        else asm volatile("cp.async.commit_group;" ::: "memory");
-        asm volatile("cp.async.wait_group 1;" ::: "memory");
+    for (int c0 = 0; c0 <= last; c0 += PF_KC) {
+        __syncthreads();                                 // Q stored / previous chunk consumed
+        load(c0);
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
         __syncthreads();
-        const float *KSm = KSb + (ci & 1) * PF_KC * QS, *VSm = VSb + (ci & 1) * PF_KC * VS;
-        float sc[PF_KC / 4];
+        float sa[NP], sb[NP];
 #pragma unroll
-        for (int j = 0; j < PF_KC / 4; j++) sc[j] = 0.0f;
+        for (int j = 0; j < NP; j++) sa[j] = sb[j] = 0.0f;
 #pragma unroll 4
         for (int c = 0; c < C4; c++) {
-            const float4 qv4 = q4[c];
+            const float4 x = qa4[c], y = qb4[c];
 #pragma unroll
-            for (int j = 0; j < PF_KC / 4; j++) {
-                const float4 kv = reinterpret_cast<const float4 *>(KSm + (sub + 4 * j) * QS)[c];
-                sc[j] = fmaf(qv4.x, kv.x, fmaf(qv4.y, kv.y, fmaf(qv4.z, kv.z, fmaf(qv4.w, kv.w, sc[j]))));
+            for (int j = 0; j < NP; j++) {
+                const float4 kv = reinterpret_cast<const float4 *>(KSm + (sub + 8 * j) * QS)[c];
+                sa[j] = fmaf(x.x, kv.x, fmaf(x.y, kv.y, fmaf(x.z, kv.z, fmaf(x.w, kv.w, sa[j]))));
+                sb[j] = fmaf(y.x, kv.x, fmaf(y.y, kv.y, fmaf(y.z, kv.z, fmaf(y.w, kv.w, sb[j]))));
             }
         }
-        float cm = -INFINITY;
+        float cma = -INFINITY, cmb = -INFINITY;
 #pragma unroll
-        for (int j = 0; j < PF_KC / 4; j++) {
-            const int kp = c0 + sub + 4 * j;
-            sc[j] = (qv && kp <= mypos) ? sc[j] * kscale : -INFINITY;
-            cm = fmaxf(cm, sc[j]);
+        for (int j = 0; j < NP; j++) {
+            const int kp = c0 + sub + 8 * j;
+            sa[j] = (va && kp <= pa) ? sa[j] * kscale : -INFINITY;
+            sb[j] = (vbq && kp <= pb) ? sb[j] * kscale : -INFINITY;
+            cma = fmaxf(cma, sa[j]);
+            cmb = fmaxf(cmb, sb[j]);
         }
-        cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 1));
-        cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 2));
-        const float mnew = fmaxf(m_run, cm);
-        const float f = mnew == -INFINITY ? 1.0f : expf(m_run - mnew);
-        float       ls = 0.0f;
 #pragma unroll
-        for (int j = 0; j < PF_KC / 4; j++) {
-            const float e = sc[j] == -INFINITY ? 0.0f : expf(sc[j] - mnew);
-            PS[qi * (PF_KC + 1) + sub + 4 * j] = e;
-            ls += e;
+        for (int o = 1; o < 8; o <<= 1) {
+            cma = fmaxf(cma, __shfl_xor_sync(0xffffffffu, cma, o));
+            cmb = fmaxf(cmb, __shfl_xor_sync(0xffffffffu, cmb, o));
         }
-        ls += __shfl_xor_sync(0xffffffffu, ls, 1);
-        ls += __shfl_xor_sync(0xffffffffu, ls, 2);
-        l_run = l_run * f + ls;
-        m_run = mnew;
+        const float mna = fmaxf(ma, cma), mnb = fmaxf(mb, cmb);
+        const float fa = mna == -INFINITY ? 1.0f : expf(ma - mna);
+        const float fb = mnb == -INFINITY ? 1.0f : expf(mb - mnb);
+        float lsa = 0.0f, lsb = 0.0f;
+#pragma unroll
+        for (int j = 0; j < NP; j++) {
+            const float ea = sa[j] == -INFINITY ? 0.0f : expf(sa[j] - mna);
+            const float eb = sb[j] == -INFINITY ? 0.0f : expf(sb[j] - mnb);
+            PS[qa * (PF_KC + 1) + sub + 8 * j] = ea;
+            PS[qb * (PF_KC + 1) + sub + 8 * j] = eb;
+            lsa += ea;
+            lsb += eb;
+        }
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1) {
+            lsa += __shfl_xor_sync(0xffffffffu, lsa, o);
+            lsb += __shfl_xor_sync(0xffffffffu, lsb, o);
+        }
+        la = la * fa + lsa;
+        lb = lb * fb + lsb;
+        ma = mna;
+        mb = mnb;
         __syncwarp();
 #pragma unroll
-        for (int j = 0; j < DQ; j++) o[j] *= f;
+        for (int j = 0; j < DE; j++) {
+            oa[j] *= fa;
+            ob[j] *= fb;
+        }
         for (int p = 0; p < PF_KC; p++) {
-            const float   e = PS[qi * (PF_KC + 1) + p];
-            const float4 *vr = reinterpret_cast<const float4 *>(VSm + p * VS + sub * VQ);
+            const float   ea = PS[qa * (PF_KC + 1) + p], eb = PS[qb * (PF_KC + 1) + p];
+            const float4 *vr = reinterpret_cast<const float4 *>(VSm + p * VS + sub * VE);
 #pragma unroll
-            for (int c = 0; c < DQ / 4; c++) {
+            for (int c = 0; c < DE / 4; c++) {
                 const float4 v = vr[c];
-                o[4 * c] = fmaf(e, v.x, o[4 * c]);
-                o[4 * c + 1] = fmaf(e, v.y, o[4 * c + 1]);
-                o[4 * c + 2] = fmaf(e, v.z, o[4 * c + 2]);
-                o[4 * c + 3] = fmaf(e, v.w, o[4 * c + 3]);
+                oa[4 * c] = fmaf(ea, v.x, oa[4 * c]);
+                oa[4 * c + 1] = fmaf(ea, v.y, oa[4 * c + 1]);
+                oa[4 * c + 2] = fmaf(ea, v.z, oa[4 * c + 2]);
+                oa[4 * c + 3] = fmaf(ea, v.w, oa[4 * c + 3]);
+                ob[4 * c] = fmaf(eb, v.x, ob[4 * c]);
+                ob[4 * c + 1] = fmaf(eb, v.y, ob[4 * c + 1]);
+                ob[4 * c + 2] = fmaf(eb, v.z, ob[4 * c + 2]);
+                ob[4 * c + 3] = fmaf(eb, v.w, ob[4 * c + 3]);
             }
         }
-        __syncthreads();                                 // this buffer and PS consumed
     }
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
-    if (qv) {
-        float4 *dst = reinterpret_cast<float4 *>(att + (size_t)t * n_head * HD + (size_t)h * HD + sub * DQ);
+    if (va) {
+        float4 *dst = reinterpret_cast<float4 *>(att + (size_t)ta * n_head * HD + (size_t)ha * HD + sub * DE);
 #pragma unroll
-        for (int c = 0; c < DQ / 4; c++)
-            dst[c] = make_float4(o[4 * c] / l_run, o[4 * c + 1] / l_run, o[4 * c + 2] / l_run, o[4 * c + 3] / l_run);
+        for (int c = 0; c < DE / 4; c++)
+            dst[c] = make_float4(oa[4 * c] / la, oa[4 * c + 1] / la, oa[4 * c + 2] / la, oa[4 * c + 3] / la);
+    }
+    if (vbq) {
+        float4 *dst = reinterpret_cast<float4 *>(att + (size_t)tq * n_head * HD + (size_t)hb * HD + sub * DE);
+#pragma unroll
+        for (int c = 0; c < DE / 4; c++)
+            dst[c] = make_float4(ob[4 * c] / lb, ob[4 * c + 1] / lb, ob[4 * c + 2] / lb, ob[4 * c + 3] / lb);
     }
 }
 

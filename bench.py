@@ -76,9 +76,9 @@ def parse():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--seqs", type=int, default=8,
                     help="N > 1: independent sequences interleaved through the layer pipeline")
-    ap.add_argument("--mode", choices=["pp", "tp"], default="pp",
+    ap.add_argument("--mode", choices=["pp", "tp", "gemv"], default="pp",
                     help="N > 1: layer pipeline with interleaved sequences (pp) or batch-1 tensor "
-                         "parallelism (tp)")
+                         "parallelism (tp); gemv: the quantised-matvec microbenchmark (one GPU)")
     ap.add_argument("--split", choices=["bytes", "ref"], default="bytes",
                     help="N > 1: layer ranges balancing bytes per stage (head on the last GPU) or "
                          "shard.c's ceil(layers/stages) rule")
@@ -212,13 +212,17 @@ def build_model_gpu(spec, seed, device):
     return buf
 
 
-def load_traffic(name: str):
+def load_traffic(name: str, bytes_per_launch: float):
     """dram bytes per launch of the dominant kernel from the committed ncu
-    summary, when one exists."""
+    summary, when one exists: the captured bytes of that launch, or (for a
+    capture of a reduced case) the captured traffic / algorithmic-bytes ratio
+    applied to this launch's algorithmic bytes."""
     p = ROOT / "profiles" / name
     if p.exists():
         try:
             d = json.loads(p.read_text())
+            if d.get("traffic_over_algorithmic"):
+                return int(round(float(d["traffic_over_algorithmic"]) * bytes_per_launch)), d.get("scaled_from")
             return d.get("dram_bytes_per_launch"), d.get("scaled_from")
         except Exception:
             pass
@@ -288,11 +292,12 @@ def our_arm(args, rank, world, local):
         dom = "decode_step"
         kname = (f"k_decode_mega<{spec.n_embd // spec.n_head}, {spec.n_head // spec.n_head_kv}> "
                  "(persistent kernel: the whole token step)")
-        traffic, scaled = load_traffic("decode_step_mega_8b.json") if args.model == CONFIG else (None, None)
+        tname = "decode_step_mega_8b.json" if args.model == CONFIG and not args.layers else None
     else:
         dom, kname = "gemv_gate_up", "k_gemv_fast<Q4_0, rmsnorm, swiglu> (fused ffn_gate+ffn_up)"
-        traffic, scaled = load_traffic("gemv_gate_up_q4_0_8b.json")
+        tname = "gemv_gate_up_q4_0_8b.json"
     n_l, tot_ms, bpl = prof[dom]
+    traffic, scaled = load_traffic(tname, bpl) if tname else (None, None)
     avg_ms = tot_ms / n_l
     achieved = bpl / (avg_ms / 1e3) / 1e9
 
@@ -351,6 +356,126 @@ def our_arm(args, rank, world, local):
     return 0
 
 
+GEMV_METRIC = "quantised matvec GB/s (Q4_0/Q8_0 GEMV microbenchmark) + % HBM roofline, B200 vs host CPU"
+GEMV_SHAPES = [(4096, 4096), (14336, 4096), (4096, 14336)]      # n_out x n_in
+
+
+def dequant_np(gtype: int, raw, n_in: int, n_out: int):
+    """Q4_0 / Q8_0 blocks -> float64 [n_out, n_in] (the ggml rules: Q4_0
+    y[l] = (lo - 8) d, y[l + 16] = (hi - 8) d; Q8_0 y = d q)."""
+    import numpy as np
+    from distcomp_b200 import gguf as G
+    bb = 18 if gtype == G.Q4_0 else 34
+    blk = raw.reshape(-1, bb)
+    d = blk[:, 0:2].copy().view(np.float16).astype(np.float64)
+    if gtype == G.Q4_0:
+        q = blk[:, 2:]
+        v = np.concatenate([(q & 0xF).astype(np.int32) - 8, (q >> 4).astype(np.int32) - 8], axis=1)
+    else:
+        v = blk[:, 2:].view(np.int8).astype(np.int32)
+    return (v * d).reshape(n_out, n_in)
+
+
+def gemv_arm(args, local):
+    """The quantised-matvec microbenchmark: Q4_0 and Q8_0 at 4096x4096,
+    14336x4096 and 4096x14336 (n_out x n_in), codes uniform over each
+    format's range, fp16 scales |N(0,0.02)|/max_code, x ~ N(0,1).  Each case
+    rotates over enough device copies of its matrix to exceed the L2 three
+    times, so every launch streams its weights from HBM; CUDA events around
+    `rounds` replays of a graph of one launch per copy.  GB/s = (weight
+    bytes as stored + x + y) / time per launch.  Every case's output is
+    checked against a float64 numpy matvec of the dequantised blocks with
+    the tests' bound |y - ref| <= 1e-4 |ref| + 1e-6 ||w_o|| ||x||."""
+    import math
+    import numpy as np
+    from distcomp_b200 import engine as E
+    from distcomp_b200 import gguf as G
+    from distcomp_b200 import synth
+    peak, peak_kind = peaks()
+    l2 = 126e6
+    cases = []
+    clocks = ClockSampler(local)
+    clocks.start()
+    l0 = E.kernel_launches()
+    for gt in (G.Q4_0, G.Q8_0):
+        for n_out, n_in in GEMV_SHAPES:
+            rng = np.random.default_rng([n_out, n_in, gt])
+            raw = synth.microbench_blocks(rng, gt, n_in, n_out)
+            x = rng.standard_normal(n_in).astype(np.float32)
+            wbytes = raw.size
+            copies = max(2, math.ceil(3 * l2 / wbytes))
+            rounds = max(4, math.ceil(args.steps * 8 / copies))
+            ms, y = E.matvec_bench(gt, raw, n_in, n_out, x, copies, rounds, device=local)
+            W = dequant_np(gt, raw, n_in, n_out)
+            ref = W @ x.astype(np.float64)
+            bound = 1e-4 * np.abs(ref) + 1e-6 * np.linalg.norm(W, axis=1) * np.linalg.norm(x.astype(np.float64))
+            err = np.abs(y.astype(np.float64) - ref)
+            algo = wbytes + 4 * n_in + 4 * n_out
+            gbs = algo / (ms / 1e3) / 1e9
+            cases.append({"type": G.TYPE_NAMES[gt], "shape": f"{n_out}x{n_in}", "weight_bytes": int(wbytes),
+                          "us_per_launch": round(ms * 1e3, 3), "gbs": round(gbs, 1),
+                          "frac": round(gbs / peak, 4), "frac_of_8tbs_nominal": round(gbs / 8000, 4),
+                          "copies": copies, "launches": copies * rounds,
+                          "max_err_over_bound": round(float(np.max(err / bound)), 4),
+                          "within_tolerance": bool(np.all(err <= bound))})
+            del W
+    launches = E.kernel_launches() - l0
+    clk = clocks.stop()
+    gm = math.exp(sum(math.log(c["gbs"]) for c in cases) / len(cases))
+    line = {
+        "metric": GEMV_METRIC, "value": round(gm, 1), "unit": "GB/s (geometric mean over the 6 cases)",
+        "n_gpus": 1, "steps": args.steps, "warmup": 2, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "q4_0/q8_0 codes x int8 digit planes, fp32 accumulate",
+        "data": "synthetic: codes uniform over each format's range, fp16 scales |N(0,0.02)|/max_code, x ~ N(0,1)",
+        "config": {"workload": "quantised matvec y = W x, Q4_0 and Q8_0 at 4096x4096, 14336x4096, 4096x14336 "
+                               "(n_out x n_in)",
+                   "l2": "each case rotates over >= 3 x L2 of device copies of its matrix"},
+        "peak_gbs": peak, "peak_kind": peak_kind, "cases": cases, "gpu_launches": int(launches), "clocks": clk,
+    }
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_reference_gemv(cases)
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def cpu_reference_gemv(cases):
+    """The reference's own matvec (src/engine.c:348-357 over its thread pool,
+    compiled from its sources into oracle/_ref/libdcref_mv.so) on the host
+    cores, each case timed for about 2 s."""
+    import ctypes as C
+    import numpy as np
+    from distcomp_b200 import gguf as G
+    from distcomp_b200 import synth
+    so = ROOT / "oracle" / "_ref" / "libdcref_mv.so"
+    if not so.exists():
+        return {"unavailable": "oracle/_ref/libdcref_mv.so not built"}
+    L = C.CDLL(str(so))
+    L.refmv_matvec.restype = C.c_int
+    L.refmv_matvec.argtypes = [C.c_uint, C.c_void_p, C.c_size_t, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
+    thr = min(64, os.cpu_count() or 1)
+    L.refmv_set_threads(thr)
+    out = []
+    names = {v: k for k, v in G.TYPE_NAMES.items()}
+    for c in cases:
+        gt = names[c["type"]]
+        n_out, n_in = (int(v) for v in c["shape"].split("x"))
+        rng = np.random.default_rng([n_out, n_in, gt])
+        raw = synth.microbench_blocks(rng, gt, n_in, n_out)
+        x = rng.standard_normal(n_in).astype(np.float32)
+        y = np.empty(n_out, np.float32)
+        L.refmv_matvec(gt, raw.ctypes.data, raw.size, n_in, n_out, x.ctypes.data, y.ctypes.data)
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < 2.0:
+            L.refmv_matvec(gt, raw.ctypes.data, raw.size, n_in, n_out, x.ctypes.data, y.ctypes.data)
+            n += 1
+        dt = (time.perf_counter() - t0) / n
+        out.append({"type": c["type"], "shape": c["shape"],
+                    "gbs": round((raw.size + 4 * n_in + 4 * n_out) / dt / 1e9, 3), "ms": round(dt * 1e3, 3)})
+    return {"kind": "reference", "cores": thr, "cases": out,
+            "value": round(float(np.exp(np.mean([np.log(o["gbs"]) for o in out]))), 3), "unit": "GB/s",
+            "sample": "each case's matvec repeated for ~2 s (weights L2/LLC-resident only for the small cases)"}
+
+
 def reference_arm(args, rank, world, local):
     if rank != 0:
         return 0
@@ -386,6 +511,8 @@ def main():
             raise SystemExit("launch N>1 with torch.distributed.run (one process per GPU)")
     if args.impl == "reference":
         return reference_arm(args, rank, world, local)
+    if args.mode == "gemv":
+        return gemv_arm(args, local) if rank == 0 else 0
     return our_arm(args, rank, world, local)
 
 

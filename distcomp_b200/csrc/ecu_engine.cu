@@ -2272,6 +2272,116 @@ int ecu_matvec(unsigned type, const void *w_raw, int n_in, int n_out, const floa
     return 0;
 }
 
+int ecu_matvec_bench(unsigned type, const void *w_raw, int n_in, int n_out, const float *x, float *y, int device,
+                     int copies, int rounds, double *ms_per_launch)
+{
+    if (!w_raw || !x || !y || !ms_per_launch || n_in <= 0 || n_out <= 0 || copies < 1 || rounds < 1) {
+        ecu_set_error(nullptr, 0, "ecu_matvec_bench: bad arguments");
+        return -1;
+    }
+    CK(cudaSetDevice(device));
+    fast_attrs_all();
+    CK(cudaGetLastError());
+    ecu_ctx tmp;
+    tmp.device = device;
+    tmp.sms = num_sms(device);
+    CK(cudaStreamCreateWithFlags(&tmp.stream, cudaStreamNonBlocking));
+    cudaGraph_t     gr = nullptr;
+    cudaGraphExec_t gx = nullptr;
+    cudaEvent_t     e0 = nullptr, e1 = nullptr;
+    struct Cleanup {
+        ecu_ctx *c;
+        cudaGraphExec_t *gx;
+        cudaEvent_t *e0, *e1;
+        ~Cleanup()
+        {
+            if (*gx) cudaGraphExecDestroy(*gx);
+            if (*e0) cudaEventDestroy(*e0);
+            if (*e1) cudaEventDestroy(*e1);
+            for (void *p : c->allocs) cudaFree(p);
+            c->allocs.clear();
+            cudaStreamDestroy(c->stream);
+            c->stream = nullptr;
+        }
+    } cleanup{&tmp, &gx, &e0, &e1};
+    EcuTensor t;
+    t.type = type;
+    t.n_dims = 2;
+    t.dims[0] = (uint64_t)n_in;
+    t.dims[1] = (uint64_t)n_out;
+    t.data = (const uint8_t *)w_raw;
+    t.nbytes = ecu_type_nbytes(type, (size_t)n_in * n_out);
+    // `copies` independent device copies in the layout the engine keeps
+    // (fast SPLIT layouts where they apply), so that a rotation over them
+    // streams from HBM rather than from L2
+    std::vector<DevMat> mats;
+    uint8_t *stage = tmp.dalloc<uint8_t>(t.nbytes + 16);
+    if (!stage) { ecu_set_error(nullptr, 0, "out of memory"); return -1; }
+    for (int k = 0; k < copies; k++) {
+        DevMat m = make_mat(&tmp, (int)type, n_in, n_out, true, true);
+        if (!m.zero && !m.data) { ecu_set_error(nullptr, 0, "out of memory for copy %d", k); return -1; }
+        if (!m.zero && t.nbytes && upload_rows(&tmp, &t, n_in, n_out, m, 0, 1, stage) != 0) return -1;
+        mats.push_back(m);
+    }
+    float *dx = tmp.dalloc<float>((size_t)n_in + 4);
+    float *dy = tmp.dalloc<float>((size_t)n_out + 4);
+    GemvScratch s;
+    s.xn = tmp.dalloc<float>((size_t)n_in + 4);
+    s.part_val = tmp.dalloc<float>(4096);
+    s.part_idx = tmp.dalloc<int>(4096);
+    s.counter = tmp.dalloc<unsigned>(4);
+    s.status = tmp.dalloc<int>(4);
+    if (!dx || !dy || !s.xn || !s.part_val || !s.part_idx || !s.counter || !s.status) {
+        ecu_set_error(nullptr, 0, "out of memory");
+        return -1;
+    }
+    CK(cudaMemset(s.status, 0, 4 * sizeof(int)));
+    CK(cudaMemset(s.counter, 0, 4 * sizeof(unsigned)));
+    CK(cudaMemcpy(dx, x, (size_t)n_in * sizeof(float), cudaMemcpyHostToDevice));
+    CK(cudaDeviceSynchronize());
+    // one graph: a launch per copy, back to back with programmatic dependent
+    // launch, each warming the next copy's first rows in L2 (what the decode
+    // step does between consecutive matrices)
+    CK(cudaStreamBeginCapture(tmp.stream, cudaStreamCaptureModeThreadLocal));
+    Launcher L{tmp.stream, true};
+    for (int k = 0; k < copies; k++) {
+        GemvArgs a = {};
+        enqueue_gemv(L, tmp.sms, mats[k], dx, nullptr, 0.0f, dy, EPI_STORE, s, a, &mats[(k + 1) % copies]);
+    }
+    cudaError_t e = cudaStreamEndCapture(tmp.stream, &gr);
+    if (e != cudaSuccess || L.err != cudaSuccess) {
+        ecu_set_error(nullptr, 0, "ecu_matvec_bench: capture failed: %s",
+                      cudaGetErrorString(e != cudaSuccess ? e : L.err));
+        if (gr) cudaGraphDestroy(gr);
+        return -1;
+    }
+    e = cudaGraphInstantiate(&gx, gr, 0);
+    cudaGraphDestroy(gr);
+    if (e != cudaSuccess) {
+        ecu_set_error(nullptr, 0, "ecu_matvec_bench: graph instantiate failed: %s", cudaGetErrorString(e));
+        return -1;
+    }
+    const int per_round = L.count;
+    // warm-up: two rounds (first-touch of every copy, instruction cache)
+    for (int r = 0; r < 2; r++) CK(cudaGraphLaunch(gx, tmp.stream));
+    CK(cudaStreamSynchronize(tmp.stream));
+    CK(cudaEventCreate(&e0));
+    CK(cudaEventCreate(&e1));
+    CK(cudaEventRecord(e0, tmp.stream));
+    for (int r = 0; r < rounds; r++) CK(cudaGraphLaunch(gx, tmp.stream));
+    CK(cudaEventRecord(e1, tmp.stream));
+    CK(cudaStreamSynchronize(tmp.stream));
+    g_launches += (uint64_t)per_round * (uint64_t)(rounds + 2);
+    float ms = 0.0f;
+    CK(cudaEventElapsedTime(&ms, e0, e1));
+    *ms_per_launch = (double)ms / ((double)rounds * copies);
+    int st = 0;
+    CK(cudaMemcpy(&st, s.status, sizeof st, cudaMemcpyDeviceToHost));
+    if (st) { ecu_set_error(nullptr, 0, "bounded wait expired in the GEMV"); return -1; }
+    CK(cudaMemcpy(y, dy, (size_t)n_out * sizeof(float), cudaMemcpyDeviceToHost));
+    return 0;
+}
+
 }  // extern "C"
 
 // ------------------------------------------------------ tensor parallel --

@@ -19,13 +19,11 @@
 #include "ecu_gemv.cuh"
 #include "ecu_model.h"
 
-#include <atomic>
 #include <cstddef>
 
 #define NOALLOC_ROWS_PER_CTA 256
 #define NOALLOC_MAX_CTAS 2048
 #define NOALLOC_MAX_ROWS (NOALLOC_ROWS_PER_CTA * NOALLOC_MAX_CTAS)   // 524288
-#define NOALLOC_MAX_DEVICES 64
 
 struct NoallocScratch {
     float     part_val[NOALLOC_MAX_CTAS];
@@ -39,13 +37,12 @@ struct NoallocScratch {
 // symbol: its address must come from cudaGetSymbolAddress on each device.
 static __device__ __align__(256) uint8_t g_noalloc_scratch[sizeof(NoallocScratch)];
 
-// Device address of g_noalloc_scratch, looked up once per device.
-static std::atomic<NoallocScratch *> g_scratch_addr[NOALLOC_MAX_DEVICES];
-
+// Device address of g_noalloc_scratch on the current device.  Looked up on
+// every call (cudaGetSymbolAddress allocates nothing and is cheap): a cached
+// address would go stale if the caller tore the context down and created it
+// again (cudaDeviceReset), which reloads the module and may move the symbol.
 static NoallocScratch *scratch_for_current_device(int dev)
 {
-    NoallocScratch *p = g_scratch_addr[dev].load();
-    if (p) return p;
     void *addr = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&addr, g_noalloc_scratch);
     if (e != cudaSuccess || !addr) {
@@ -53,7 +50,6 @@ static NoallocScratch *scratch_for_current_device(int dev)
                       dev, cudaGetErrorString(e));
         return nullptr;
     }
-    g_scratch_addr[dev].store((NoallocScratch *)addr);
     return (NoallocScratch *)addr;
 }
 
@@ -77,7 +73,7 @@ extern "C" int ecu_matvec_argmax_noalloc(unsigned ggml_type, const void *d_w, in
         return -1;
     }
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= NOALLOC_MAX_DEVICES) {
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) {
         ecu_set_error(nullptr, 0, "ecu_matvec_argmax_noalloc: no usable current device");
         return -1;
     }

@@ -344,19 +344,31 @@ static __global__ void __launch_bounds__(128, 1) k_pf_gemm_tc(const __half *Ahi,
         if (s < nk) load(s, s * PF_TC_BK);
         asm volatile("cp.async.commit_group;" ::: "memory");
     }
+    // ok: every wait so far succeeded (the same value in every thread: it is
+    // combined by the loop's barrier).  A wait that gives up stops the
+    // pipeline: no further stage loads (the stage may still be an operand of
+    // MMAs in flight), no further MMAs and no C stores; the MMAs already
+    // committed are drained below before the accumulator is freed.
+    bool ok = true;
+    int  last_commit = -1;
     for (int kt = 0; kt < nk; kt++) {
         const int s = kt % PF_TC_STAGES, nxt = kt + PF_TC_STAGES - 1;
+        bool mine = true;
         if (nxt < nk) {
             // the stage nxt reuses was read by iteration kt - 1's MMAs
-            if (kt >= 1) mbar_wait<true>(&mbar[(kt - 1) % PF_TC_STAGES], (unsigned)((kt - 1) / PF_TC_STAGES) & 1u, status);
-            load(nxt % PF_TC_STAGES, nxt * PF_TC_BK);
+            if (kt >= 1)
+                mine = mbar_wait<true>(&mbar[(kt - 1) % PF_TC_STAGES], (unsigned)((kt - 1) / PF_TC_STAGES) & 1u,
+                                       status);
+            if (mine) load(nxt % PF_TC_STAGES, nxt * PF_TC_BK);
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
         asm volatile("cp.async.wait_group %0;" ::"n"(PF_TC_STAGES - 1) : "memory");
         // this thread's copies into stage s are done: hand them to the
         // tensor core's (async) proxy, then to the issuing thread
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        __syncthreads();
+        ok = __syncthreads_and(mine) != 0;
+        if (!ok) break;
+        last_commit = kt;
         if (tid == 0) {
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const uint32_t a_hi = (uint32_t)__cvta_generic_to_shared(tile(s, 0));
@@ -377,12 +389,20 @@ static __global__ void __launch_bounds__(128, 1) k_pf_gemm_tc(const __half *Ahi,
         }
         __syncwarp();
     }
-    // the last commit covers every MMA issued before it
-    mbar_wait<true>(&mbar[(nk - 1) % PF_TC_STAGES], (unsigned)((nk - 1) / PF_TC_STAGES) & 1u, status);
+    // the last commit covers every MMA issued before it; drained whatever the
+    // status word says (bounded), so that no MMA is in flight when the
+    // accumulator is read or freed
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    if (last_commit >= 0) {
+        const bool done = mbar_drain(&mbar[last_commit % PF_TC_STAGES],
+                                     (unsigned)(last_commit / PF_TC_STAGES) & 1u, ECU_WAIT_NS);
+        if (!done && status) atomicOr(status, ECU_STATUS_TIMEOUT);
+        ok = __syncthreads_and(ok && done) != 0;
+    }
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     // warp w reads accumulator lanes 32w..32w+31 (tile rows), 32 columns at a time
     const int row = m0 + warp * 32 + lane;
-    for (int ch = 0; ch < 4; ch++) {
+    for (int ch = 0; ch < 4 && ok; ch++) {
         uint32_t v[32];
         const uint32_t ta = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(ch * 32);
         asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "

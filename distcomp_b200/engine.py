@@ -95,6 +95,8 @@ SIGNATURES = [
     ("ecu_matvec", C.c_int, [C.c_uint, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_int]),
     ("ecu_matvec_argmax_noalloc", C.c_int, [C.c_uint, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
                                             C.c_void_p, C.c_void_p]),
+    ("ecu_matvec_bench", C.c_int, [C.c_uint, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_int,
+                                   C.c_int, C.c_int, C.POINTER(C.c_double)]),
     ("ecu_profile_steps", C.c_int, [C.c_void_p, C.c_int, C.POINTER(EcuKprof), C.c_int]),
     ("ecu_last_error", C.c_char_p, []),
     ("ecu_kernel_launches", C.c_uint64, []),
@@ -342,3 +344,17 @@ def matvec(gtype: int, raw: np.ndarray, n_in: int, n_out: int, x: np.ndarray, de
     if lib().ecu_matvec(gtype, _ptr(raw), n_in, n_out, _ptr(x), _ptr(y), device) != 0:
         raise EngineError(last_error())
     return y
+
+
+def matvec_bench(gtype: int, raw: np.ndarray, n_in: int, n_out: int, x: np.ndarray, copies: int, rounds: int,
+                 device: int = 0):
+    """Device time per launch (ms) of y = W x over `copies` rotated device
+    copies of the matrix, and the last launch's y (ecu_matvec_bench)."""
+    raw = np.ascontiguousarray(raw, dtype=np.uint8)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty(n_out, dtype=np.float32)
+    ms = C.c_double(0.0)
+    if lib().ecu_matvec_bench(gtype, _ptr(raw), n_in, n_out, _ptr(x), _ptr(y), device, copies, rounds,
+                              C.byref(ms)) != 0:
+        raise EngineError(last_error())
+    return ms.value, y

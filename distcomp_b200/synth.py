@@ -197,6 +197,26 @@ def quantize_q4_k_torch(w):
     return torch.cat([head, qs], dim=1).reshape(-1)
 
 
+def microbench_blocks(rng: np.random.Generator, gtype: int, n_in: int, n_out: int) -> np.ndarray:
+    """The quantised-matvec microbenchmark's weights (Q4_0 or Q8_0): codes
+    uniform over the format's range, fp16 scales |N(0, 0.02)| / max_code
+    (max_code 8 and 127)."""
+    nblk = n_in * n_out // 32
+    if gtype == G.Q4_0:
+        blk = np.empty((nblk, 18), dtype=np.uint8)
+        d = (np.abs(rng.standard_normal(nblk)) * 0.02 / 8).astype(np.float16)
+        blk[:, 0:2] = d.view(np.uint8).reshape(nblk, 2)
+        blk[:, 2:] = rng.integers(0, 256, size=(nblk, 16), dtype=np.uint8)
+    elif gtype == G.Q8_0:
+        blk = np.empty((nblk, 34), dtype=np.uint8)
+        d = (np.abs(rng.standard_normal(nblk)) * 0.02 / 127).astype(np.float16)
+        blk[:, 0:2] = d.view(np.uint8).reshape(nblk, 2)
+        blk[:, 2:] = rng.integers(-127, 128, size=(nblk, 32), dtype=np.int8).view(np.uint8)
+    else:
+        raise ValueError(f"microbench_blocks: type {gtype}")
+    return blk.reshape(-1)
+
+
 def random_kquant_blocks(rng: np.random.Generator, gtype: int, nblk: int, sigma: float = 0.02):
     """Random K-quant blocks: uniform code/scale bytes, fp16 super-block scales
     drawn as |N(0, sigma)| / 64 so that weights land around sigma.  (gguf-py
@@ -240,8 +260,15 @@ def _meta(b: G.GGUFBuilder, s: LlamaSpec):
     b.add_kv(f"{a}.vocab_size", G.T_U32, s.n_vocab)
 
 
-def build_model(s: LlamaSpec, seed: int = 0, device: str = "cpu") -> np.ndarray:
-    """The whole GGUF image as a numpy uint8 array."""
+def build_model(s: LlamaSpec, seed: int = 0, device: str = "cpu", threads: int = 1,
+                quant_device: str | None = None) -> np.ndarray:
+    """The whole GGUF image as a numpy uint8 array.
+
+    device="cpu": numpy normals (the same bytes whatever ``threads`` and
+    ``quant_device`` are: with threads > 1 the tensors are generated in
+    parallel and quantised by ``quantize_torch``, bit-identical to gguf-py's
+    rule, on ``quant_device`` (default the CPU)).  device="cuda:N": torch's
+    CUDA generator (a different stream of normals)."""
     b = G.GGUFBuilder()
     _meta(b, s)
     tl = tensor_list(s)
@@ -251,6 +278,23 @@ def build_model(s: LlamaSpec, seed: int = 0, device: str = "cpu") -> np.ndarray:
     if device != "cpu":
         import torch
         dev = torch.device(device)
+
+    def cpu_tensor(name, dims, gt):
+        view = b.tensor_view(name)
+        n = int(np.prod(dims))
+        rng = np.random.default_rng(name_seed(seed, name))
+        w = (rng.standard_normal(n, dtype=np.float32) * np.float32(s.sigma)).reshape(dims[::-1])
+        if gt == G.Q4_K or ((threads > 1 or quant_device) and gt in (G.Q4_0, G.Q8_0)):
+            import torch
+            t = torch.from_numpy(w.reshape(-1))
+            if quant_device:
+                t = t.to(quant_device)
+            qb = quantize_q4_k_torch(t) if gt == G.Q4_K else quantize_torch(t, gt)
+            view[:] = qb.cpu().numpy()
+        else:
+            view[:] = quantize_numpy(w, gt)
+
+    jobs = []
     for name, dims, gt in tl:
         view = b.tensor_view(name)
         n = int(np.prod(dims))
@@ -262,13 +306,10 @@ def build_model(s: LlamaSpec, seed: int = 0, device: str = "cpu") -> np.ndarray:
             view[:] = random_kquant_blocks(rng, gt, n // G.BLOCK[gt][0], s.sigma)
             continue
         if device == "cpu":
-            rng = np.random.default_rng(name_seed(seed, name))
-            w = (rng.standard_normal(n, dtype=np.float32) * np.float32(s.sigma)).reshape(dims[::-1])
-            if gt == G.Q4_K:
-                import torch
-                view[:] = quantize_q4_k_torch(torch.from_numpy(w)).numpy()
+            if threads > 1:
+                jobs.append((name, dims, gt))
             else:
-                view[:] = quantize_numpy(w, gt)
+                cpu_tensor(name, dims, gt)
         else:
             import torch
             gen = torch.Generator(device=dev)
@@ -285,6 +326,13 @@ def build_model(s: LlamaSpec, seed: int = 0, device: str = "cpu") -> np.ndarray:
                 qb = quantize_torch(w, gt)
             torch.from_numpy(view).copy_(qb.cpu())
             del w, qb
+    if jobs:
+        from concurrent.futures import ThreadPoolExecutor
+        # largest tensors first, so that the embedding and head overlap the rest
+        jobs.sort(key=lambda j: -int(np.prod(j[1])))
+        with ThreadPoolExecutor(threads) as ex:
+            for f in [ex.submit(cpu_tensor, *j) for j in jobs]:
+                f.result()
     return b.buf
 
 

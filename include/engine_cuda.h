@@ -218,14 +218,26 @@ int  ecu_matvec(unsigned ggml_type, const void *w_raw, int n_in, int n_out, cons
  * budget, a host that hands out device memory from its own pool, a loop
  * that cannot take cudaMalloc's device synchronisation.  It allocates
  * nothing: its scratch is one fixed 16 KiB array inside the library, which
- * limits n_out to 524288 rows (more returns -1 with a message).  The first
- * call on a device looks that array up with cudaGetSymbolAddress; make it
- * before any stream capture.  Every call shares the array, so calls that
- * may overlap on the GPU (two streams, two threads) race: serialise them. */
+ * limits n_out to 524288 rows (more returns -1 with a message).  Every
+ * call looks that array's device address up with cudaGetSymbolAddress
+ * (which allocates nothing), so the address stays right across a context
+ * torn down and created again; make the first call on a device before any
+ * stream capture.  Every call shares the array, so calls that may overlap
+ * on the GPU (two streams, two threads) race: serialise them. */
 int  ecu_matvec_argmax_noalloc(unsigned ggml_type, const void *d_w, int n_in, int n_out,
                                const float *d_x, float *d_y, int *d_token, void *stream);
 
 /* ---- measurement --------------------------------------------------------- */
+
+/* Quantised-matvec microbenchmark (the reference's matvec,
+ * src/engine.c:277-357, timed on the device): `copies` device copies of one
+ * n_out x n_in matrix of raw GGUF blocks (host array w_raw, repacked into
+ * the layouts the engine keeps), then `rounds` replays of a CUDA graph of
+ * one launch of y = W_c x per copy, back to back; *ms_per_launch = CUDA
+ * event time / launches.  Enough copies to exceed the L2 make every launch
+ * stream its matrix from HBM.  y (host) = the last launch's output. */
+int  ecu_matvec_bench(unsigned ggml_type, const void *w_raw, int n_in, int n_out, const float *x,
+                      float *y, int device, int copies, int rounds, double *ms_per_launch);
 
 /* Per-kernel-kind totals of a profiling replay. */
 typedef struct {

@@ -2,7 +2,9 @@
 """Regenerate the golden fixtures in tests/golden/ (run in a container where
 the reference tree is mounted; the GPU box never runs this).
 
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py --ref PATH_TO_REFERENCE_CHECKOUT
+
+(or set DC_REFERENCE to that path)
 
 Sources, all of them the reference's own code or tests:
   * kquant_blocks.json   the fixed Q2_K/Q3_K/Q4_K/Q6_K blocks and the 64
@@ -28,6 +30,7 @@ from __future__ import annotations
 import argparse
 import hashlib
 import json
+import os
 import re
 import subprocess
 import sys
@@ -120,8 +123,11 @@ def lib_vocab(buf):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("DC_REFERENCE"),
+                    help="the reference checkout (default: $DC_REFERENCE)")
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("give --ref or set DC_REFERENCE")
     ref = Path(args.ref)
 
     # 1. quant_test.c vectors

@@ -114,18 +114,8 @@ def test_matvec_zero_rule(eng, oracle_port):
 
 def microbench_weights(rng, t, n_in, n_out):
     """Codes uniform over the format's range, fp16 scales |N(0,0.02)|/max_code."""
-    nblk = n_in * n_out // 32
-    if t == G.Q4_0:
-        blk = np.empty((nblk, 18), dtype=np.uint8)
-        d = (np.abs(rng.standard_normal(nblk)) * 0.02 / 8).astype(np.float16)
-        blk[:, 0:2] = d.view(np.uint8).reshape(nblk, 2)
-        blk[:, 2:] = rng.integers(0, 256, size=(nblk, 16), dtype=np.uint8)
-    else:
-        blk = np.empty((nblk, 34), dtype=np.uint8)
-        d = (np.abs(rng.standard_normal(nblk)) * 0.02 / 127).astype(np.float16)
-        blk[:, 0:2] = d.view(np.uint8).reshape(nblk, 2)
-        blk[:, 2:] = rng.integers(-127, 128, size=(nblk, 32), dtype=np.int8).view(np.uint8)
-    return blk.reshape(-1)
+    from distcomp_b200 import synth
+    return synth.microbench_blocks(rng, t, n_in, n_out)
 
 
 @pytest.mark.parametrize("t", [G.Q4_0, G.Q8_0])

@@ -82,6 +82,8 @@ def parse():
     ap.add_argument("--split", choices=["bytes", "ref"], default="bytes",
                     help="N > 1: layer ranges balancing bytes per stage (head on the last GPU) or "
                          "shard.c's ceil(layers/stages) rule")
+    ap.add_argument("--gemv-case", default="",
+                    help="--mode gemv: only this case, e.g. Q4_0:14336x4096 (profiler captures)")
     ap.add_argument("--layers", type=int, default=0,
                     help="override n_layer (reduced-depth runs for profiler captures; not a bench line)")
     ap.add_argument("--model", choices=["llama3-8b", "llama2-70b"], default=CONFIG,
@@ -210,6 +212,17 @@ def build_model_gpu(spec, seed, device):
     torch.cuda.synchronize()
     torch.cuda.empty_cache()
     return buf
+
+
+def one_gpu_tokens(model, spec, args, device: int, n: int, prompt) -> list[int]:
+    """n greedy tokens after `prompt` (fed one token at a time) from a FULL
+    context on one GPU: the reference for the multi-GPU partitions' tokens."""
+    from distcomp_b200 import engine as E
+    c = E.LlmCtx(model, E.STAGE_FULL, n_ctx=args.n_ctx, device=device)
+    try:
+        return c.generate(list(prompt), n)
+    finally:
+        c.close()
 
 
 def load_traffic(name: str, bytes_per_launch: float):
@@ -399,6 +412,8 @@ def gemv_arm(args, local):
     l0 = E.kernel_launches()
     for gt in (G.Q4_0, G.Q8_0):
         for n_out, n_in in GEMV_SHAPES:
+            if args.gemv_case and args.gemv_case != f"{G.TYPE_NAMES[gt]}:{n_out}x{n_in}":
+                continue
             rng = np.random.default_rng([n_out, n_in, gt])
             raw = synth.microbench_blocks(rng, gt, n_in, n_out)
             x = rng.standard_normal(n_in).astype(np.float32)

@@ -473,7 +473,9 @@ struct ecu_ctx {
     size_t      mega_smem = 0;
     unsigned long long *mega_ll = nullptr;   // the tagged activation vectors, one block
     size_t      mega_ll_words = 0;
+    int         stall_next = -1;          // ecu_inject_wait_timeout: the phase the next launch stalls
     std::vector<const char *> ph_kind;    // per phase, for the profile
+    std::vector<int> ph_in_ep;            // per phase: GEMV input's writer phase (-1: plain input or not a GEMV)
     std::vector<double>       ph_bytes;
 
     struct SrcRef { std::string name; DevMat m; int row0, rstride; size_t elems; int n_in; };
@@ -740,20 +742,20 @@ static void enqueue_layer(ecu_ctx *c, Launcher &L, int li, int nl = -1)
 static void enqueue_head(ecu_ctx *c, Launcher &L, bool advance)
 {
     const EcuGeom &g = c->g;
-    // normed state in place: it is both HEAD's out[0..n_embd) and the GEMV input
-    L.kind = "rmsnorm";
-    L.bytes = 12.0 * g.n_embd;
-    L(k_rmsnorm, dim3(1), dim3(256), 0, (const float *)c->state, (const float *)c->out_norm, g.n_embd,
-      g.eps, c->state);
+    // RMSNorm fused into the head GEMV (the arithmetic of the persistent
+    // step's head phase): the normed state goes to scratch, and the CTA that
+    // finishes the argmax copies it over the state, HEAD's out[0..n_embd)
     GemvArgs a = {};
     a.st = c->st;
     a.tok_hist = c->tok_hist;
     a.tok_out = c->state + g.n_embd;
     a.advance_pos = advance ? 1 : 0;
+    a.xn_out = c->scr.xn;
+    a.xn_dst = c->state;
     L.kind = "gemv_head_argmax";
     // a FULL context's next token starts with layer 0's Q/K/V projection
     const DevMat *nx = (c->stage == ECU_STAGE_FULL && !c->layers.empty()) ? &c->layers[0].qkv[0] : nullptr;
-    enqueue_gemv(L, c->sms, c->out, c->state, nullptr, g.eps, c->logits, EPI_ARGMAX, c->scr, a, nx,
+    enqueue_gemv(L, c->sms, c->out, c->state, c->out_norm, g.eps, c->logits, EPI_ARGMAX, c->scr, a, nx,
                  EPI_STORE);
 }
 
@@ -883,9 +885,9 @@ static MegaFn mega_lookup(int hd, int rep, bool sys)
     return nullptr;
 }
 
-static size_t mega_smem_total(int red_floats, unsigned ring_bytes, unsigned union_bytes)
+static size_t mega_smem_total(int red_floats, unsigned ring_bytes, unsigned union_bytes, int n_ph)
 {
-    return mega_smem_plan(red_floats, ring_bytes, union_bytes).total;
+    return mega_smem_plan(red_floats, ring_bytes, union_bytes, n_ph).total;
 }
 
 // Q4_0 rows in SPLIT4, Q8_0 rows in SPLIT8 or Q4_K rows in SPLITK4, n_in
@@ -973,12 +975,11 @@ static int mega_setup(ecu_ctx *c)
             ly.d.row_bytes > stage_bytes)
             return no("a weight row does not fit a ring stage");
     if (full && c->out.row_bytes > stage_bytes) return no("a head row does not fit a ring stage");
-    // the shared-memory union: the digit planes of the widest GEMV input (and
-    // the RMSNorm prologue's staging of x and the norm weights above them),
-    // or the attention K/V buffers; the split partials of a head group, which
+    // the shared-memory union: the digit planes of the widest GEMV input, or
+    // the attention K/V buffers; the split partials of a head group, which
     // the merge gathers there, set the position splits per KV head (one
     // item per CTA at most)
-    size_t un = (size_t)g.n_embd / 32 * 28 * sizeof(int) + 2 * (size_t)g.n_embd * sizeof(float);
+    size_t un = (size_t)g.n_embd / 32 * 28 * sizeof(int);
     for (auto &ly : c->layers)
         for (const DevMat *m : {&ly.qkv[0], &ly.o, &ly.gu, &ly.d})
             un = std::max(un, (size_t)(m->n_in / m->nseg) / 32 * 28 * sizeof(int));
@@ -998,12 +999,19 @@ static int mega_setup(ecu_ctx *c)
         att_nsl = 2;
         att_sub = sub2;
     }
-    un = std::max(un, (size_t)att_nsl * att_sub * row4);
-    // the attention's position-group sums: [512 / (hd/4)][n_rep][hd] floats
+    // the first attention rounds' K/V copies are issued by the Q/K/V phase
+    // before it (ECU_MEGA_KV_EARLY=0: by the attention phase itself), into
+    // buffers above the widest Q/K/V digit planes
+    const char *ke = getenv("ECU_MEGA_KV_EARLY");
+    const bool  kv_early = !(ke && ke[0] == '0');
+    size_t qkv_dig = 0;
+    for (auto &ly : c->layers) qkv_dig = std::max(qkv_dig, (size_t)ly.qkv[0].n_in / 32 * 28 * sizeof(int));
+    const size_t kv_off = kv_early ? ((qkv_dig + 127) & ~(size_t)127) : 0;
+    un = std::max(un, kv_off + (size_t)att_nsl * att_sub * row4);
+    // the attention's position-group sums (at the union's base): [512 / (hd/4)][n_rep][hd] floats
     un = std::max(un, (size_t)(MEGA_THREADS / (hd / 4)) * g.n_rep * hd * sizeof(float));
     int n_split = std::min(MEGA_MAX_SPLIT, grid / tp.nkv);
     if (const char *se = getenv("ECU_MEGA_SPLIT")) n_split = std::max(1, std::min(n_split, atoi(se)));
-    n_split = std::min(n_split, (int)(un / ((size_t)g.n_rep * (hd + 4) * sizeof(float))));
     n_split = std::max(1, std::min(n_split, g.n_ctx));
 
     std::vector<MegaPhase> ph;
@@ -1021,14 +1029,17 @@ static int mega_setup(ecu_ctx *c)
     // (+ the argmax exchange of tensor-parallel ranks: a value and an index
     // word per rank); the same layout on every rank
     auto pad4 = [](size_t n) { return (n + 7) & ~(size_t)3; };
+    // (+ this rank's attention split partials: per KV head, split and query
+    // head the hd unnormalised sums, the running max and the weight sum)
     const size_t w_x = pad4(g.n_embd), w_qkv = pad4((size_t)qd_l + 2 * kvd_l), w_att = pad4(qdim),
-                 w_h = pad4(g.n_ff), w_arg = pad4(2 * ECU_MAX_TP);
-    c->mega_ll_words = w_x + w_qkv + w_att + w_h + w_arg;
+                 w_h = pad4(g.n_ff), w_arg = pad4(2 * ECU_MAX_TP),
+                 w_apart = pad4((size_t)tp.nkv * n_split * g.n_rep * (hd + 2));
+    c->mega_ll_words = w_x + w_qkv + w_att + w_h + w_arg + w_apart;
     c->mega_ll = c->dalloc<unsigned long long>(c->mega_ll_words);
     if (!c->mega_ll) return -1;
     CK(cudaMemset(c->mega_ll, 0, c->mega_ll_words * sizeof(unsigned long long)));
     unsigned long long *x_ll = c->mega_ll, *qkv_ll = x_ll + w_x, *att_ll = qkv_ll + w_qkv, *h_ll = att_ll + w_att,
-                       *arg_ll = h_ll + w_h;
+                       *arg_ll = h_ll + w_h, *apart_ll = arg_ll + w_arg;
     // x_w: the phase that last wrote the residual stream (-1: the plain
     // input state of a LAYERS stage)
     int x_w = -1;
@@ -1063,6 +1074,8 @@ static int mega_setup(ecu_ctx *c)
         LayerDev &ly = c->layers[li];
         const bool last = li + 1 == c->layers.size();
         MegaPhase q = mega_gemv_phase(ly.qkv[0], grid, stage_bytes, 1, EPI_STORE, c->state, ly.attn_norm, c->qkv, nullptr);
+        q.kc = c->kc + li * plane;                  // the next attention's cache planes (early K/V copies)
+        q.vc = c->vc + li * plane;
         q.in_ep = x_w;
         q.x_ll = x_ll;
         q.y_ll = qkv_ll;
@@ -1098,6 +1111,8 @@ static int mega_setup(ecu_ctx *c)
         add(hp, "gemv_head_argmax", gemv_bytes(c->out, EPI_ARGMAX) + 4.0 * g.n_embd);
     }
     if (ph.size() >= 4095) return no("more phases than the tagged vectors' epochs count");
+    c->ph_in_ep.clear();
+    for (const MegaPhase &q : ph) c->ph_in_ep.push_back(q.kind == PH_GEMV ? q.in_ep : -1);
     for (size_t i = 0; i + 1 < ph.size(); i++) ph[i].next_attn = ph[i + 1].kind == PH_ATTN ? 1 : 0;
     // row partials of a whole phase (Q4_0 phases keep 4 per row and k-group
     // when they fit); attention keeps its position groups' partials there
@@ -1114,7 +1129,7 @@ static int mega_setup(ecu_ctx *c)
     int optin = 0;
     if (cudaFuncGetAttributes(&fa, fn) == cudaSuccess &&
         cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, c->device) == cudaSuccess &&
-        mega_smem_total(red, (unsigned)nst * stage_bytes, (unsigned)un) + fa.sharedSizeBytes > (size_t)optin) {
+        mega_smem_total(red, (unsigned)nst * stage_bytes, (unsigned)un, (int)ph.size()) + fa.sharedSizeBytes > (size_t)optin) {
         // a wide model's digit planes, norm staging and row partials leave
         // less room: shrink the ring stages (1 KB at a time) while every
         // GEMV row still fits one, and refit the phases' rows per stage
@@ -1122,15 +1137,20 @@ static int mega_setup(ecu_ctx *c)
         for (auto &p : ph)
             if (p.kind == PH_GEMV) max_row = std::max(max_row, p.row_bytes);
         while (stage_bytes >= max_row + 1024 &&
-               mega_smem_total(red, (unsigned)nst * stage_bytes, (unsigned)un) + fa.sharedSizeBytes > (size_t)optin)
+               mega_smem_total(red, (unsigned)nst * stage_bytes, (unsigned)un, (int)ph.size()) + fa.sharedSizeBytes > (size_t)optin)
             stage_bytes -= 1024;
         for (auto &p : ph)
             if (p.kind == PH_GEMV) p.sr = (int)std::min<size_t>((size_t)p.rpc, stage_bytes / p.row_bytes);
     }
     cudaGetLastError();
-    const size_t smem = mega_smem_total(red, (unsigned)nst * stage_bytes, (unsigned)un);
+    const size_t smem = mega_smem_total(red, (unsigned)nst * stage_bytes, (unsigned)un, (int)ph.size());
+    // the attribute belongs to the kernel function, which every context of
+    // the same head geometry shares (stages of different depths need
+    // different amounts: the phase table): allow the device's whole opt-in
+    // size, so that no context's setting cuts another's launches short
     if (optin == 0 || smem + fa.sharedSizeBytes > (size_t)optin ||
-        cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
+        cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             optin - (int)fa.sharedSizeBytes) != cudaSuccess) {
         cudaGetLastError();
         static char buf[160];
         snprintf(buf, sizeof buf, "shared memory %zu + %zu B over the %d B limit", smem,
@@ -1143,23 +1163,38 @@ static int mega_setup(ecu_ctx *c)
         cudaGetLastError();
         return no("no SM can hold one CTA of the persistent kernel");
     }
+    // the ring cursor's phase table (copied into shared memory at launch)
+    std::vector<uint4> tab(ph.size());
+    for (size_t i = 0; i < ph.size(); i++) {
+        const MegaPhase &q = ph[i];
+        if (q.kind == PH_GEMV) {
+            if (q.row_bytes >= (1u << 20) || q.sr >= (1 << 12) || q.n_out >= (1 << 17) || q.rpc >= (1 << 15))
+                return no("a GEMV phase's geometry does not fit the phase table");
+            tab[i] = mega_tab_entry(q.w, q.row_bytes, q.sr, q.n_out, q.rpc);
+        } else {
+            tab[i] = make_uint4(0u, 0u, 0u, 0u);
+        }
+    }
+    uint4 *d_tab = c->dalloc<uint4>(ph.size());
+    if (!d_tab) return -1;
+    CK(cudaMemcpy(d_tab, tab.data(), tab.size() * sizeof(uint4), cudaMemcpyHostToDevice));
     MegaPhase *d_ph = c->dalloc<MegaPhase>(ph.size());
-    float *apart = c->dalloc<float>((size_t)tp.nkv * n_split * g.n_rep * (hd + 4));
     float *pval = c->dalloc<float>((size_t)grid);
     int *pidx = c->dalloc<int>((size_t)grid);
     unsigned *ctr = c->dalloc<unsigned>(4 + (size_t)g.n_head_kv);
-    if (!d_ph || !apart || !pval || !pidx || !ctr || (full && !xn_tmp)) return -1;
+    if (!d_ph || !pval || !pidx || !ctr || (full && !xn_tmp)) return -1;
     CK(cudaMemcpy(d_ph, ph.data(), ph.size() * sizeof(MegaPhase), cudaMemcpyHostToDevice));
     CK(cudaMemset(ctr, 0, (4 + (size_t)g.n_head_kv) * sizeof(unsigned)));
     MegaArgs &a = c->margs;
     a = MegaArgs{};
     a.ph = d_ph;
     a.n_ph = (int)ph.size();
+    a.tab = d_tab;
     a.emb = c->emb;
     a.state = c->state;
     a.qkv = c->qkv;
     a.att = c->att;
-    a.apart = apart;
+    a.apart_ll = apart_ll;
     a.xn_tmp = xn_tmp;
     a.part_val = pval;
     a.part_idx = pidx;
@@ -1200,6 +1235,9 @@ static int mega_setup(ecu_ctx *c)
     a.att_nsl = att_nsl;
     const char *al2 = getenv("ECU_MEGA_ATT_L2");
     a.att_l2 = (al2 && al2[0] == '0') ? 0 : 1;
+    a.att_early = kv_early ? 1 : 0;
+    a.stall_phase = -1;
+    a.kv_off = (unsigned)kv_off;
     a.eps = g.eps;
     a.kscale = 1.0f / sqrtf((float)hd);
     c->mega_fn = fn;
@@ -1218,6 +1256,8 @@ static int mega_launch(ecu_ctx *c, cudaStream_t s, unsigned long long *phase_ns,
         return -1;
     }
     MegaArgs a = c->margs;
+    a.stall_phase = c->stall_next;          // one launch only
+    c->stall_next = -1;
     a.phase_ns = phase_ns;
     a.phase_clk = phase_ns ? phase_ns + a.n_ph + 1 : nullptr;   // the profile buffer's second row
     a.phase_detail = detail;
@@ -2270,6 +2310,34 @@ int ecu_matvec(unsigned type, const void *w_raw, int n_in, int n_out, const floa
     if (st) { ecu_set_error(nullptr, 0, "bounded wait expired in the GEMV"); return -1; }
     CK(cudaMemcpy(y, dy, (size_t)n_out * sizeof(float), cudaMemcpyDeviceToHost));
     return 0;
+}
+
+int ecu_set_wait_ns(int device, unsigned long long ns)
+{
+    if (ns == 0) {
+        ecu_set_error(nullptr, 0, "ecu_set_wait_ns: the limit must be positive");
+        return -1;
+    }
+    CK(cudaSetDevice(device));
+    CK(cudaMemcpyToSymbol(g_wait_ns, &ns, sizeof ns));
+    return 0;
+}
+
+int ecu_inject_wait_timeout(ecu_ctx *c)
+{
+    if (!c || !c->mega) {
+        ecu_set_error(nullptr, 0, "ecu_inject_wait_timeout: only a context on the persistent step");
+        return -1;
+    }
+    // the first GEMV phase whose input is a tagged vector (written by an
+    // earlier phase of the same launch)
+    for (int p = 0; p < (int)c->ph_in_ep.size(); p++)
+        if (c->ph_in_ep[p] >= 0) {
+            c->stall_next = p;
+            return 0;
+        }
+    ecu_set_error(nullptr, 0, "ecu_inject_wait_timeout: no phase reads a tagged input");
+    return -1;
 }
 
 int ecu_matvec_bench(unsigned type, const void *w_raw, int n_in, int n_out, const float *x, float *y, int device,

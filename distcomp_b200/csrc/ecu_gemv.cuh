@@ -35,6 +35,8 @@ struct GemvArgs {
     float        eps;
     float       *y;            // output (STORE/ADD/ARGMAX: n_out; SWIGLU: n_out/2)
     float       *xn_out;       // optional: CTA 0 stores the normed input here
+    float       *xn_dst;       // argmax: the last CTA copies xn_out here (n_in floats) once every
+                               // CTA has read x (the normed state may replace x in place)
     // argmax epilogue
     float       *part_val;     // [gridDim.x]
     int         *part_idx;     // [gridDim.x]
@@ -187,6 +189,8 @@ static __device__ void argmax_finish(const GemvArgs &a, ArgBest cta_best, ArgBes
     __syncthreads();
     if (!s_last) return;
     __threadfence();
+    if (a.xn_out && a.xn_dst)
+        for (int i = threadIdx.x; i < a.m.n_in; i += blockDim.x) a.xn_dst[i] = __ldcg(a.xn_out + i);
     if (threadIdx.x == 0) {
         ArgBest b{-INFINITY, -1};
         for (unsigned c = 0; c < gridDim.x; c++) {
@@ -560,6 +564,10 @@ __global__ void __launch_bounds__(FAST_MAX_THREADS, 1) k_gemv_fast(GemvArgs a)
         const int nct = ncw * 32, ctid = threadIdx.x;
         const int g = warp % nkg, rp = warp / nkg;
         pdl_wait();                       // x comes from the previous kernel
+        // RMSNorm: the digit planes are those of x * w; the scale (one fp32
+        // factor for the whole vector) multiplies each row's sum in the
+        // epilogue, the order the persistent step uses (it knows the scale
+        // only once every input block has arrived)
         float scale = 1.0f;
         if (NORM)
             scale = rms_scale(a.x, m.n_in, a.eps, dsum, ctid, nct, [nct] { named_bar(1, nct); });
@@ -576,19 +584,22 @@ __global__ void __launch_bounds__(FAST_MAX_THREADS, 1) k_gemv_fast(GemvArgs a)
             }
             if (NORM) {
                 const float4 *w4 = reinterpret_cast<const float4 *>(a.norm_w + (size_t)b * 32);
+                float4 *o4 = (a.xn_out && blockIdx.x == 0) ? reinterpret_cast<float4 *>(a.xn_out + (size_t)b * 32)
+                                                            : nullptr;
 #pragma unroll
                 for (int k = 0; k < 8; k++) {
                     float4 t = w4[k];
-                    xv[4 * k]     = __fmul_rn(__fmul_rn(xv[4 * k], scale), t.x);
-                    xv[4 * k + 1] = __fmul_rn(__fmul_rn(xv[4 * k + 1], scale), t.y);
-                    xv[4 * k + 2] = __fmul_rn(__fmul_rn(xv[4 * k + 2], scale), t.z);
-                    xv[4 * k + 3] = __fmul_rn(__fmul_rn(xv[4 * k + 3], scale), t.w);
-                }
-                if (a.xn_out && blockIdx.x == 0) {
-                    float4 *o4 = reinterpret_cast<float4 *>(a.xn_out + (size_t)b * 32);
-#pragma unroll
-                    for (int k = 0; k < 8; k++)
-                        o4[k] = make_float4(xv[4 * k], xv[4 * k + 1], xv[4 * k + 2], xv[4 * k + 3]);
+                    // the normed input the stage outputs: (x * scale) * w, the
+                    // reference's rounding (src/engine.c:261)
+                    if (o4)
+                        o4[k] = make_float4(__fmul_rn(__fmul_rn(xv[4 * k], scale), t.x),
+                                            __fmul_rn(__fmul_rn(xv[4 * k + 1], scale), t.y),
+                                            __fmul_rn(__fmul_rn(xv[4 * k + 2], scale), t.z),
+                                            __fmul_rn(__fmul_rn(xv[4 * k + 3], scale), t.w));
+                    xv[4 * k]     = __fmul_rn(xv[4 * k], t.x);
+                    xv[4 * k + 1] = __fmul_rn(xv[4 * k + 1], t.y);
+                    xv[4 * k + 2] = __fmul_rn(xv[4 * k + 2], t.z);
+                    xv[4 * k + 3] = __fmul_rn(xv[4 * k + 3], t.w);
                 }
             }
             make_digits<FMT>(xv, xw, off, sxs);
@@ -643,6 +654,8 @@ __global__ void __launch_bounds__(FAST_MAX_THREADS, 1) k_gemv_fast(GemvArgs a)
     // ---- epilogue ----------------------------------------------------------
     const int nthr = blockDim.x;
     ArgBest   best{-INFINITY, -1};
+    // the RMSNorm scale (written by rms_scale before the barrier above)
+    const float rscale = NORM ? rms_from_sum(dsum[RMS_MAX_W], m.n_in, a.eps) : 1.0f;
     if (EPI == EPI_SWIGLU) {
         for (int j = threadIdx.x; j < nrows / 2; j += nthr) {
             float gsum = 0.0f, usum = 0.0f;
@@ -650,12 +663,17 @@ __global__ void __launch_bounds__(FAST_MAX_THREADS, 1) k_gemv_fast(GemvArgs a)
                 gsum += red[(2 * j) * nkg + q];
                 usum += red[(2 * j + 1) * nkg + q];
             }
+            if (NORM) {
+                gsum = __fmul_rn(gsum, rscale);
+                usum = __fmul_rn(usum, rscale);
+            }
             a.y[r0 / 2 + j] = silu_mul(gsum, usum);
         }
     } else {
         for (int r = threadIdx.x; r < nrows; r += nthr) {
             float acc = 0.0f;
             for (int q = 0; q < nkg; q++) acc += red[r * nkg + q];
+            if (NORM) acc = __fmul_rn(acc, rscale);
             if (EPI == EPI_ADD) a.y[r0 + r] = a.y[r0 + r] + acc;
             else a.y[r0 + r] = acc;
             if (EPI == EPI_ARGMAX) best = arg_better(best, ArgBest{acc, r0 + r});

@@ -62,7 +62,8 @@ struct MegaPhase {
     const float   *norm_w;
     float         *y;
     float         *xn;         // GEMV with norm: CTA 0 stores the normed input here
-    float         *kc, *vc;    // ATTN: this layer's cache planes [nkv][n_ctx][hd]
+    float         *kc, *vc;    // ATTN: this layer's cache planes [nkv][n_ctx][hd]; the Q/K/V GEMV
+                               // before it: the same planes (its early K/V copies)
     const float   *bq, *bk, *bv;
     int            next_attn;  // the next phase is attention
     // epoch-tagged vectors (see ll_put): the phase that wrote this phase's
@@ -80,10 +81,11 @@ static_assert(sizeof(MegaPhase) % 16 == 0, "phase descriptors are copied in 16-b
 struct MegaArgs {
     const MegaPhase *ph;
     int              n_ph;
+    const uint4     *tab;           // per phase, the ring cursor's view (mega_tab_entry); copied to shared memory
     DevMat           emb;           // PH_EMBED: the RAW embedding matrix
     float           *state;         // residual stream, n_embd (+1: token as float)
     float           *qkv, *att;
-    float           *apart;         // attention partials [n_kv][n_split][NREP][HD + 4]
+    unsigned long long *apart_ll;   // attention partials, tagged: [n_kv][n_split][NREP][HD + 2]
     float           *xn_tmp;        // head: normed state, copied to state at the end
     float           *part_val;      // argmax: per-CTA best
     int             *part_idx;
@@ -116,6 +118,11 @@ struct MegaArgs {
     int              att_sub;       // attention: K/V rows per buffer (even, <= 32)
     int              att_nsl;       // attention: buffer slots (1, or 2: a round's copies overlap the previous round)
     int              att_l2;        // warm the next attention's K/V rows in L2 during the GEMV before it
+    int              att_early;     // the Q/K/V phase issues the attention's first nsl rounds of K/V copies
+    int              stall_phase;   // failure-path testing: this GEMV phase waits for an input epoch that
+                                    // no phase writes, so its bounded waits run out (-1: none)
+    unsigned         kv_off;        // byte offset of the attention K/V buffers in the union (above the
+                                    // Q/K/V phase's digit planes when att_early)
     float            eps, kscale;
 };
 
@@ -190,7 +197,7 @@ __device__ __forceinline__ bool ll_keep_waiting(unsigned it, uint64_t &t0, int *
     if ((it & 255u) != 0) return true;
     if (it == 256) t0 = globaltimer_ns();
     if (*reinterpret_cast<volatile int *>(status) != 0) return false;
-    if (globaltimer_ns() - t0 > ECU_WAIT_NS) {
+    if (globaltimer_ns() - t0 > wait_limit_ns()) {
         atomicOr(status, ECU_STATUS_TIMEOUT);
         return false;
     }
@@ -264,10 +271,21 @@ __device__ __forceinline__ float ll_settle(const unsigned long long *p, unsigned
 // ------------------------------------------------------------ smem layout --
 
 struct MegaSmem {
-    size_t ring, bars, abar, red, un, dsum, argsh, total;
+    size_t ring, bars, abar, red, un, dsum, argsh, tab, total;
 };
 
-__host__ __device__ inline MegaSmem mega_smem_plan(int red_floats, unsigned ring_bytes, unsigned union_bytes)
+// One phase as the ring cursor sees it, 16 bytes: the weight pointer (0 for
+// a phase without weight rows), row bytes (< 2^20) | rows per stage << 20,
+// rows (< 2^17) | rows per CTA (< 2^15) << 17.
+__host__ __device__ inline uint4 mega_tab_entry(const uint8_t *w, unsigned row_bytes, int sr, int n_out, int rpc)
+{
+    const unsigned long long pw = (unsigned long long)(uintptr_t)w;
+    return make_uint4((unsigned)(pw & 0xFFFFFFFFull), (unsigned)(pw >> 32), row_bytes | ((unsigned)sr << 20),
+                      (unsigned)n_out | ((unsigned)rpc << 17));
+}
+
+__host__ __device__ inline MegaSmem mega_smem_plan(int red_floats, unsigned ring_bytes, unsigned union_bytes,
+                                                   int n_ph)
 {
     MegaSmem p;
     p.ring = 0;
@@ -279,7 +297,8 @@ __host__ __device__ inline MegaSmem mega_smem_plan(int red_floats, unsigned ring
     // attention K/V buffers and split-partial gather
     p.dsum = p.un + (((size_t)union_bytes + 15) & ~(size_t)15);
     p.argsh = p.dsum + (RMS_MAX_W + 8) * sizeof(double);   // W terms + the total
-    p.total = p.argsh + 32 * sizeof(ArgBest);
+    p.tab = (p.argsh + 32 * sizeof(ArgBest) + 15) & ~(size_t)15;
+    p.total = p.tab + (size_t)n_ph * sizeof(uint4);
     return p;
 }
 
@@ -398,31 +417,36 @@ struct MegaShared {
     uint64_t *dbar;        // completes when the next phase's descriptor has arrived
     double   *dsum;
     ArgBest  *argsh;
+    const uint4 *tab;      // the phase table (shared memory)
+    int       n_ph;
 };
 
-// Load phase p's geometry for this CTA into the ring cursor.
-__device__ __forceinline__ void cursor_load_phase(const MegaArgs &a, ChunkCursor *c, int p)
+// Load phase p's geometry for this CTA into the ring cursor (from the
+// shared-memory phase table: no global-memory round trip on the refill path).
+__device__ __forceinline__ void cursor_load_phase(const MegaShared &S, ChunkCursor *c, int p)
 {
     c->p = p;
     c->i = 0;
     c->nrows = 0;
-    if (p >= a.n_ph) return;
-    const MegaPhase &q = a.ph[p];
-    if (q.kind != PH_GEMV) return;
-    const int r0 = blockIdx.x * q.rpc;
-    c->nrows = max(0, min(q.n_out, r0 + q.rpc) - r0);
-    c->w = q.w + (size_t)r0 * q.row_bytes;
-    c->row_bytes = q.row_bytes;
-    c->sr = q.sr;
+    if (p >= S.n_ph) return;
+    const uint4 t = S.tab[p];
+    const uint8_t *w = reinterpret_cast<const uint8_t *>((uintptr_t)(((unsigned long long)t.y << 32) | t.x));
+    if (!w) return;
+    const int n_out = (int)(t.w & 0x1FFFFu), rpc = (int)(t.w >> 17);
+    const int r0 = blockIdx.x * rpc;
+    c->nrows = max(0, min(n_out, r0 + rpc) - r0);
+    c->row_bytes = t.z & 0xFFFFFu;
+    c->w = w + (size_t)r0 * c->row_bytes;
+    c->sr = (int)(t.z >> 20);
 }
 
 // The chunk at the cursor (its first row, rows, row bytes), and advance it;
 // false at the end of the list.
-__device__ __forceinline__ bool cursor_next(const MegaArgs &a, ChunkCursor *c, const uint8_t *&src, int &rows,
+__device__ __forceinline__ bool cursor_next(const MegaShared &S, ChunkCursor *c, const uint8_t *&src, int &rows,
                                             unsigned &row_bytes)
 {
-    while (c->p < a.n_ph && c->i >= c->nrows) cursor_load_phase(a, c, c->p + 1);
-    if (c->p >= a.n_ph) return false;
+    while (c->p < S.n_ph && c->i >= c->nrows) cursor_load_phase(S, c, c->p + 1);
+    if (c->p >= S.n_ph) return false;
     rows = min(c->sr, c->nrows - c->i);
     row_bytes = c->row_bytes;
     src = c->w + (size_t)c->i * c->row_bytes;
@@ -439,12 +463,12 @@ __device__ __forceinline__ void ring_issue(const MegaArgs &a, const MegaShared &
     const uint8_t *src;
     int            rows;
     unsigned       rb;
-    if (!cursor_next(a, &rc->cp, src, rows, rb)) return;
+    if (!cursor_next(S, &rc->cp, src, rows, rb)) return;
     const uint32_t bytes = (uint32_t)rows * rb;
     mbar_expect_tx(&S.full[slot], bytes);
     bulk_g2s(S.ring + (size_t)slot * a.stage_bytes, src, bytes, &S.full[slot]);
     rc->issued++;
-    if (warm && a.pf_stages > 0 && cursor_next(a, &rc->pf, src, rows, rb)) prefetch_l2(src, (uint32_t)rows * rb);
+    if (warm && a.pf_stages > 0 && cursor_next(S, &rc->pf, src, rows, rb)) prefetch_l2(src, (uint32_t)rows * rb);
 }
 
 // Lane 0 of a warp that is done with ring slot `slot` (after __syncwarp).
@@ -636,59 +660,52 @@ __device__ __forceinline__ void store_digits(const MegaShared &S, int t, float4 
     if (q == 0) d[27] = __float_as_int(sxs);
 }
 
-// RMSNorm prologue: x and the norm weights are staged in shared memory above
-// the digit planes (loads of up to four float4s per thread in flight at
-// once); each warp adds its 32 float4s' squares into one W term of the sum
-// (rms_scale's order) straight from registers, warp 0 adds the W terms --
-// the scale k_rmsnorm and k_gemv_fast compute, bit for bit -- then the digit
-// planes of the normed input.
-template <bool SYS>
-__device__ __forceinline__ void norm_prologue(const MegaArgs &a, const MegaPhase &ph, const MegaShared &S, int tid,
-                                              int nct, unsigned ein)
+__device__ __forceinline__ void attn_prefetch(const MegaArgs &a, const MegaPhase &ph, int pos, int hd);
+
+// This CTA's attention item: KV head g, position split sp, positions
+// [t0, t1) below or at pos, in rounds of 2 * att_sub positions.
+struct AttItem {
+    bool has;
+    int  g, sp, t0, t1, nround;
+};
+
+__device__ __forceinline__ AttItem att_item(const MegaArgs &a, int pos)
 {
-    const int n = ph.n_in, nq = n / 4, nb = n / 32, lane = tid & 31;
-    float4 *xs = reinterpret_cast<float4 *>(S.dig + (size_t)nb * 28);   // 112 bytes a block: 16-aligned
-    float4 *ws = xs + nq;
-    const float4 *w4 = reinterpret_cast<const float4 *>(ph.norm_w);
-    // whole warps throughout: nq is a multiple of 256
-    for (int base = tid; base < nq; base += 2 * nct) {
-        float4 wv[2], v[2];
-#pragma unroll
-        for (int k = 0; k < 2; k++)
-            if (base + k * nct < nq) wv[k] = __ldg(w4 + base + k * nct);
-        input_batch<2, SYS>(a, ph, base, nct, nq, ein, v);
-#pragma unroll
-        for (int k = 0; k < 2; k++) {
-            const int t = base + k * nct;
-            if (t < nq) {
-                ws[t] = wv[k];
-                xs[t] = v[k];
-                const double p = rms_bfly32(rms_sq4(v[k]));
-                if (lane == 0) S.dsum[t >> 5] = p;
-            }
-        }
-    }
-    named_bar(1, nct);
-    if (tid < 32) {
-        const double t = rms_total_w(S.dsum, nq / 32, tid);
-        if (tid == 0) S.dsum[RMS_MAX_W] = t;
-    }
-    named_bar(1, nct);
-    const float scale = rms_from_sum(S.dsum[RMS_MAX_W], n, a.eps);
-    float4 *xn4 = (ph.xn && blockIdx.x == 0) ? reinterpret_cast<float4 *>(ph.xn) : nullptr;
-    for (int t = tid; t < nq; t += nct) {
-        float4       v = xs[t];
-        const float4 w = ws[t];
-        v.x = __fmul_rn(__fmul_rn(v.x, scale), w.x);
-        v.y = __fmul_rn(__fmul_rn(v.y, scale), w.y);
-        v.z = __fmul_rn(__fmul_rn(v.z, scale), w.z);
-        v.w = __fmul_rn(__fmul_rn(v.w, scale), w.w);
-        if (xn4) xn4[t] = v;
-        store_digits(S, t, v);
-    }
+    AttItem it;
+    const int item = blockIdx.x;
+    it.has = item < a.n_kv * a.n_split;
+    it.g = it.has ? item / a.n_split : 0;
+    it.sp = it.has ? item % a.n_split : 0;
+    const int npos = pos + 1, chunk = (npos + a.n_split - 1) / a.n_split;
+    it.t0 = min(npos, it.sp * chunk);
+    it.t1 = it.has ? min(npos, it.t0 + chunk) : it.t0;
+    it.nround = (it.t1 - it.t0 + 2 * a.att_sub - 1) / (2 * a.att_sub);
+    return it;
 }
 
-__device__ __forceinline__ void attn_prefetch(const MegaArgs &a, const MegaPhase &ph, int pos, int hd);
+// Half hf (att_sub rows) of round r of the item's K/V rows below the
+// current position (contiguous in the head-major cache) into slot r % nsl:
+// one bulk copy for K, one for V, completing on abar[slot * 2 + hf].  The
+// proxy fence orders earlier generic accesses of those bytes before the
+// copy's writes.
+template <int HD>
+__device__ __forceinline__ void att_issue(const MegaArgs &a, const MegaShared &S, const float *kc, const float *vc,
+                                          const AttItem &it, int pos, int r, int hf)
+{
+    const int sub = a.att_sub, nsl = a.att_nsl, s_ = r % nsl;
+    const int c0 = it.t0 + r * 2 * sub + hf * sub;
+    const int c1 = min(min(it.t1, c0 + sub), pos);
+    const int nr = c1 > c0 ? c1 - c0 : 0;
+    const uint32_t bytes = (uint32_t)(nr * HD * sizeof(float));
+    uint64_t *bar = &S.abar[s_ * 2 + hf];
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    mbar_expect_tx(bar, 2 * bytes);
+    if (nr > 0) {
+        const size_t base = (size_t)it.g * a.n_ctx * HD + (size_t)c0 * HD;
+        bulk_g2s(S.kvbuf + (size_t)((s_ * 2 + 0) * 2 + hf) * sub * HD, kc + base, bytes, bar);
+        bulk_g2s(S.kvbuf + (size_t)((s_ * 2 + 1) * 2 + hf) * sub * HD, vc + base, bytes, bar);
+    }
+}
 
 // One GEMV phase on the consumer side: digit planes of the (normed) input
 // into shared memory, this CTA's ring stages of the matrix (rp_: the next
@@ -721,39 +738,77 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
     if (ph.next_attn && tid < hd) cs_next = __ldg(a.rope_cs + (size_t)S.pos * hd + tid);
     unsigned long long yw = 0;
     if (has_res && ph.y_ep >= 0) yw = ll_word<SYS>(a.x_ll + ph.out_base + r0 + tid);
+    // the next attention's first K/V rounds (rows of earlier positions: no
+    // dependence on this step) start streaming into their buffers now, above
+    // this phase's digit planes
+    if (ph.next_attn && a.att_early && (tid & 31) == 0 && tid < 64) {
+        const AttItem it = att_item(a, S.pos);
+        for (int r = 0; r < min(a.att_nsl, it.nround); r++)
+            if (hd == 128) att_issue<128>(a, S, ph.kc, ph.vc, it, S.pos, r, tid >> 5);
+            else att_issue<64>(a, S, ph.kc, ph.vc, it, S.pos, r, tid >> 5);
+    }
 
-    // ---- prologue: digit planes of every input block -----------------------
+    // ---- prologue: this warp's share of its k-group's input -------------------
+    // k-group g (inputs [1024 g, 1024 g + 1024): 32 blocks, 8 passes of four
+    // blocks) is prepared by its rowpar warps: warp rp takes passes rp,
+    // rp + rowpar, ...  A pass is one float4 a lane (lane q of an 8-lane
+    // group holds elements 4q..4q+3 of one block): the warp waits only for
+    // those tagged words, adds their squares into one W term of the RMSNorm
+    // sum (128 inputs; rms_scale's order) and stores the digit planes of x
+    // (times the norm weights) in shared memory.  The group's warps then
+    // meet at the group's own named barrier, so no warp waits for another
+    // k-group's input; the RMSNorm scale, which needs every W term,
+    // multiplies the row sums in the epilogue.
     // A CTA without rows reads no input: nothing it writes would tell a later
     // phase that it is done with the vector (the tagged vectors are reused
     // one layer later, ordered only by what each phase reads).
-    const unsigned ein = ll_epoch(S.launch, ph.in_ep);
-    if (nrows == 0) {
-    } else if (ph.norm) {
-        norm_prologue<SYS>(a, ph, S, tid, nct, ein);
-    } else {
-        const int nq = nb * 8;                          // float4s of x; whole warps (nb % 32 == 0)
-        for (int base = tid; base < nq; base += 2 * nct) {
-            float4 v[2];
-            input_batch<2, SYS>(a, ph, base, nct, nq, ein, v);
+    // (an injected stall: the epoch of phase -1 of the next launch, which no
+    // word carries)
+    const unsigned ein = p_idx == a.stall_phase ? ll_epoch(S.launch + 1u, -1) : ll_epoch(S.launch, ph.in_ep);
+    const bool active = nrows > 0 && warp < nkg * rowpar;
+    const int  g = active ? warp % nkg : 0, rp = active ? warp / nkg : 0;
+    if (active) {
+        const int     tg = g * 256 + lane;               // the group's first float4, this lane
+        const float4 *w4 = reinterpret_cast<const float4 *>(ph.norm_w);
+        for (int k0 = rp; k0 < 8; k0 += 2 * rowpar) {
+            float4 v[2], wv[2];
+            if (ph.norm)
 #pragma unroll
-            for (int k = 0; k < 2; k++)
-                if (base + k * nct < nq) store_digits(S, base + k * nct, v[k]);
+                for (int k = 0; k < 2; k++)
+                    if (k0 + k * rowpar < 8) wv[k] = __ldg(w4 + tg + 32 * (k0 + k * rowpar));
+            input_batch<2, SYS>(a, ph, tg + 32 * k0, 32 * rowpar, g * 256 + 256, ein, v);
+#pragma unroll
+            for (int k = 0; k < 2; k++) {
+                const int kk = k0 + k * rowpar;
+                if (kk < 8) {
+                    const int t = tg + 32 * kk;
+                    float4    x4 = v[k];
+                    if (ph.norm) {
+                        const double sq = rms_bfly32(rms_sq4(x4));
+                        if (lane == 0) S.dsum[t >> 5] = sq;
+                        x4.x = __fmul_rn(x4.x, wv[k].x);
+                        x4.y = __fmul_rn(x4.y, wv[k].y);
+                        x4.z = __fmul_rn(x4.z, wv[k].z);
+                        x4.w = __fmul_rn(x4.w, wv[k].w);
+                    }
+                    store_digits(S, t, x4);
+                }
+            }
         }
+        if (rowpar > 1) named_bar(2 + g, 32 * rowpar);
+        else __syncwarp();
     }
     float yprev = 0.0f;
     if (has_res)
         yprev = ph.y_ep >= 0 ? ll_settle<SYS>(a.x_ll + ph.out_base + r0 + tid, yw, ll_epoch(S.launch, ph.y_ep), a.status)
                              : __ldcg(ph.y + r0 + tid);
-    named_bar(1, nct);
 
     if (det) det[0] = clock64();
     // ---- main loop ------------------------------------------------------------
-    const bool active = warp < nkg * rowpar;
-    const int  g = active ? warp % nkg : 0, rp = active ? warp / nkg : 0;
     const int  b = g * 32 + lane;
     int   xw[3][8], off[3];
-    float sxs;
-    {
+    float sxs = 0.0f;
+    if (active) {
         const int4 *d4 = reinterpret_cast<const int4 *>(S.dig + (size_t)b * 28);
 #pragma unroll
         for (int p = 0; p < 3; p++) {
@@ -818,17 +873,40 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
     // ---- epilogue over this CTA's rows --------------------------------------
     float         *y = ph.y;
     const unsigned eout = ll_epoch(S.launch, p_idx);
+    // the RMSNorm scale: every warp adds the W terms in rms_scale's order
+    // (the same bits in every warp, so no further barrier)
+    float rscale = 1.0f;
+    if (ph.norm && nrows > 0) rscale = rms_from_sum(rms_total_w(S.dsum, nkg * 8, lane), ph.n_in, a.eps);
     if (epi == EPI_SWIGLU) {
         for (int j = tid; j < nrows / 2; j += nct) {
-            const float gs = row_total(S.red, 2 * j, nkg, red4), us = row_total(S.red, 2 * j + 1, nkg, red4);
+            float gs = row_total(S.red, 2 * j, nkg, red4), us = row_total(S.red, 2 * j + 1, nkg, red4);
+            if (ph.norm) {
+                gs = __fmul_rn(gs, rscale);
+                us = __fmul_rn(us, rscale);
+            }
             ll_put_out<SYS>(a, ph.bcast, ph.y_ll + ph.out_base + r0 / 2 + j, silu_mul(gs, us), eout);
         }
         if (det) det[2] = clock64();
         return;
     }
+    if (ph.xn && ph.norm && blockIdx.x == 0 && nrows > 0) {
+        // the normed input the stage outputs, (x * scale) * w with the
+        // reference's two roundings (src/engine.c:261); the tagged words
+        // already carry the epoch (this CTA read them all in the prologue)
+        const float4 *w4 = reinterpret_cast<const float4 *>(ph.norm_w);
+        float4       *xn4 = reinterpret_cast<float4 *>(ph.xn);
+        for (int t = tid; t < nb * 8; t += nct) {
+            float4 v[1];
+            input_batch<1, SYS>(a, ph, t, 0, nb * 8, ein, v);
+            const float4 w = __ldg(w4 + t);
+            xn4[t] = make_float4(__fmul_rn(__fmul_rn(v[0].x, rscale), w.x), __fmul_rn(__fmul_rn(v[0].y, rscale), w.y),
+                                 __fmul_rn(__fmul_rn(v[0].z, rscale), w.z), __fmul_rn(__fmul_rn(v[0].w, rscale), w.w));
+        }
+    }
     ArgBest best{-INFINITY, -1};
     for (int r = tid; r < nrows; r += nct) {
-        const float acc = row_total(S.red, r, nkg, red4);
+        float acc = row_total(S.red, r, nkg, red4);
+        if (ph.norm) acc = __fmul_rn(acc, rscale);
         if (epi == EPI_ADD) {
             const float out = yprev + acc;         // r == tid: nrows <= MEGA_THREADS
             ll_put_out<SYS>(a, ph.bcast, ph.y_ll + ph.out_base + r0 + r, out, eout);
@@ -916,44 +994,25 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
     // and matrix); the score loop reads a row's float4 columns in an order
     // rotated by the lane, so the 32 lanes' rows still spread over the banks
     constexpr int RS = HD;
-    constexpr int LPR = HD / 4, NC4 = HD / 4;
+    constexpr int NC4 = HD / 4;
     static_assert((NC4 & (NC4 - 1)) == 0, "head_dim / 4 a power of two");
     __shared__ __align__(16) float q_s[NREP * HD];
     __shared__ __align__(16) float knew[HD], vnew[HD];
     const int nct = MEGA_NCW * 32, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int item = blockIdx.x;
-    const bool has = item < a.n_kv * a.n_split;
-    const int g = has ? item / a.n_split : 0, sp = has ? item % a.n_split : 0;
-    const int pos = S.pos, npos = pos + 1;
-    const int chunk = (npos + a.n_split - 1) / a.n_split;
-    const int t0 = min(npos, sp * chunk), t1 = has ? min(npos, t0 + chunk) : t0;
+    const AttItem it = att_item(a, S.pos);
+    const bool has = it.has;
+    const int g = it.g, sp = it.sp, t0 = it.t0, t1 = it.t1, nround = it.nround;
+    const int pos = S.pos;
     const int sub = a.att_sub, nsl = a.att_nsl;
-    const int nround = (t1 - t0 + 2 * sub - 1) / (2 * sub);   // 2 * sub positions a round
     float *kbase = ph.kc + (size_t)g * a.n_ctx * HD;
     float *vbase = ph.vc + (size_t)g * a.n_ctx * HD;
     // buffer (slot s, matrix m: 0 = K, 1 = V, half hf) of sub rows
     auto buf = [&](int s_, int m, int hf) { return S.kvbuf + (size_t)((s_ * 2 + m) * 2 + hf) * sub * RS; };
-    // half hf (sub rows) of round r of the slice below the current position
-    // (contiguous in the head-major cache) into slot r % nsl: one bulk copy
-    // for K, one for V; thread 0 issues half 0, thread 32 half 1.  A slot is
-    // refilled after the barrier that ends the round which read it; the proxy
-    // fence orders those generic reads before the copy's writes.
-    auto issue = [&](int r, int hf) {
-        const int s_ = r % nsl;
-        const int c0 = t0 + r * 2 * sub + hf * sub;
-        const int c1 = min(min(t1, c0 + sub), pos);
-        const int nr = c1 > c0 ? c1 - c0 : 0;
-        const uint32_t bytes = (uint32_t)(nr * HD * sizeof(float));
-        uint64_t *bar = &S.abar[s_ * 2 + hf];
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        mbar_expect_tx(bar, 2 * bytes);
-        if (nr > 0) {
-            bulk_g2s(buf(s_, 0, hf), kbase + (size_t)c0 * HD, bytes, bar);
-            bulk_g2s(buf(s_, 1, hf), vbase + (size_t)c0 * HD, bytes, bar);
-        }
-    };
-    if ((tid & 31) == 0 && tid < 64)
-        for (int r = 0; r < min(nsl, nround); r++) issue(r, tid >> 5);
+    // the first nsl rounds' copies: issued by the Q/K/V phase (att_early),
+    // else now; a slot is refilled after the barrier that ends the round
+    // which read it
+    if (!a.att_early && (tid & 31) == 0 && tid < 64)
+        for (int r = 0; r < min(nsl, nround); r++) att_issue<HD>(a, S, ph.kc, ph.vc, it, pos, r, tid >> 5);
     const float *cs_s = S.cs;
     const unsigned ein = ll_epoch(S.launch, ph.in_ep);
     const int qdim = a.n_head * HD, kvdim = a.n_kv * HD;
@@ -1091,7 +1150,7 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
             }
         }
         named_bar(1, nct);                          // both halves of slot s_ are free
-        if (r + nsl < nround && (tid & 31) == 0 && tid < 64) issue(r + nsl, tid >> 5);
+        if (r + nsl < nround && (tid & 31) == 0 && tid < 64) att_issue<HD>(a, S, ph.kc, ph.vc, it, pos, r + nsl, tid >> 5);
     }
     // one phase of each of a slot's half barriers per round that used it
     // (a round with at most sub positions still completes both halves: its
@@ -1100,13 +1159,19 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
     att_sb1 += nsl > 1 ? nround / nsl : 0;
     if (det) det[1] = clock64();
     // the position groups' accumulators into the K/V buffers (free now: every
-    // round's copies have landed), added in group order into the partial
+    // round's copies have landed), added in group order into this split's
+    // partial, published as tagged words: per query head the HD unnormalised
+    // sums, the running max and the weight sum
+    const unsigned eout = ll_epoch(S.launch, p_idx);
+    constexpr int  PW = HD + 2;                       // words of one head's partial
+    const int      ns = a.n_split;
     {
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        float4 *gsum = reinterpret_cast<float4 *>(S.kvbuf);  // [PG][NREP][C4]
+        float4 *gsum = reinterpret_cast<float4 *>(S.dig);    // [PG][NREP][C4], the union's base
 #pragma unroll
         for (int hh = 0; hh < NREP; hh++) gsum[((size_t)pg * NREP + hh) * C4 + vc] = acc[hh];
         named_bar(1, nct);
+        unsigned long long *dst0 = a.apart_ll + (size_t)(g * ns + sp) * NREP * PW;
         if (has)
             for (int i = tid; i < NREP * C4; i += nct) {
                 const int hh = i / C4, c = i % C4;
@@ -1115,84 +1180,78 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
                     const float4 v = gsum[((size_t)q * NREP + hh) * C4 + c];
                     o4.x += v.x; o4.y += v.y; o4.z += v.z; o4.w += v.w;
                 }
-                float *dst = a.apart + ((size_t)(g * a.n_split + sp) * NREP + hh) * (HD + 4);
-                reinterpret_cast<float4 *>(dst)[c] = o4;
+                unsigned long long *dst = dst0 + (size_t)hh * PW + 4 * c;
+                ll_put<SYS>(dst, o4.x, eout);
+                ll_put<SYS>(dst + 1, o4.y, eout);
+                ll_put<SYS>(dst + 2, o4.z, eout);
+                ll_put<SYS>(dst + 3, o4.w, eout);
             }
         if (has && warp < NREP && lane == 0) {
-            float *dst = a.apart + ((size_t)(g * a.n_split + sp) * NREP + warp) * (HD + 4);
-            dst[HD] = m_run;
-            dst[HD + 1] = l_run;
+            ll_put<SYS>(dst0 + (size_t)warp * PW + HD, m_run, eout);
+            ll_put<SYS>(dst0 + (size_t)warp * PW + HD + 1, l_run, eout);
         }
     }
     // the K/V buffers were filled by the async proxy and read here; the next
     // phase writes the same bytes with ordinary stores
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-
-    // ---- the split that finishes last merges its KV head's n_rep query heads,
-    // in split order (the combination k_attention's cluster rank 0 performs)
-    __shared__ unsigned s_last;
-    __shared__ float wsp[NREP][MEGA_MAX_SPLIT], invl[NREP];
-    named_bar(1, nct);                       // every warp's partial is written
-    if (tid == 0) {
-        bool last = false;
-        if (has) {
-            __threadfence();
-            last = atomicAdd(a.att_ticket + g, 1u) == (unsigned)a.n_split - 1;
-        }
-        s_last = last;
-    }
-    named_bar(1, nct);
     if (det) det[2] = clock64();
-    if (!s_last) return;
-    __threadfence();
-    // all partials of the head group into shared memory at once (the K/V
-    // buffers are free), then the merge reads only shared memory
-    const int    ns = a.n_split;
-    constexpr int PER = NREP * (HD + 4);     // floats of one split's partials
-    // the group's partials are one contiguous run: one bulk copy (the other
-    // CTAs' stores were released before their tickets and acquired here;
-    // the proxy fence orders them for the async-proxy read)
-    if (tid == 0) {
-        asm volatile("fence.proxy.async.global;" ::: "memory");
-        const uint32_t bytes = (uint32_t)(ns * PER * sizeof(float));
-        mbar_expect_tx(&S.abar[4], bytes);
-        bulk_g2s(S.kvbuf, a.apart + (size_t)g * ns * PER, bytes, &S.abar[4]);
-    }
-    mbar_wait<true>(&S.abar[4], (unsigned)merges & 1u, a.status);
-    merges++;
-    const float *gat = S.kvbuf;
-    if (warp < NREP) {                         // warp hh: its head's split weights, lanes over splits
-        const int hh = warp;
-        float M = -INFINITY;
-        for (int r = lane; r < ns; r += 32) M = fmaxf(M, gat[r * PER + hh * (HD + 4) + HD]);
-        M = warp_max(M);
-        float L = 0.0f;
-        for (int r = lane; r < ns; r += 32) {
-            const float ms = gat[r * PER + hh * (HD + 4) + HD];
-            const float w = ms > -INFINITY ? expf(ms - M) : 0.0f;
-            wsp[hh][r] = w;
-            L += gat[r * PER + hh * (HD + 4) + HD + 1] * w;
+
+    // ---- merge, without tickets or fences: the KV head's NREP x HD outputs
+    // are T = NREP * HD / 32 tasks of 32 dimensions of one query head; task j
+    // runs on the CTA of split j % ns.  Every warp requests the splits' maxima
+    // and weight sums (lane r: split r) and its own splits' sums (warp w:
+    // splits w, w + 16, ...; lane = dimension) at once, waits until each word
+    // carries this phase's epoch, and adds exp(m_r - M) acc_r in split order;
+    // the 16 warp sums are added in warp order through shared memory:
+    // out = sum_r exp(m_r - M) acc_r / sum_r exp(m_r - M) l_r.
+    constexpr int T = NREP * (HD / 32);
+    float *msum = S.red;                              // [MEGA_NCW][32], free after the rounds
+    for (int j = sp; j < T; j += ns) {
+        if (!has) break;
+        const int hh = j / (HD / 32), d = (j % (HD / 32)) * 32 + lane;
+        const unsigned long long *base = a.apart_ll + (size_t)g * ns * NREP * PW + (size_t)hh * PW;
+        const size_t              rs = (size_t)NREP * PW;          // words between splits
+        unsigned long long wm0 = 0, wl0 = 0, wm1 = 0, wl1 = 0, wa[4];
+        if (lane < ns) { wm0 = ll_word<SYS>(base + lane * rs + HD); wl0 = ll_word<SYS>(base + lane * rs + HD + 1); }
+        if (lane + 32 < ns) {
+            wm1 = ll_word<SYS>(base + (lane + 32) * rs + HD);
+            wl1 = ll_word<SYS>(base + (lane + 32) * rs + HD + 1);
         }
-        L = warp_sum(L);
-        if (lane == 0) invl[hh] = L > 0.0f ? 1.0f / L : 0.0f;
-    }
-    named_bar(1, nct);
-    // the ticket is rewound before any output becomes visible: a CTA can
-    // reach the next layer's attention only after reading this output
-    if (tid == 0) {
-        a.att_ticket[g] = 0u;
-        __threadfence();
-    }
-    named_bar(1, nct);
-    const unsigned eout = ll_epoch(S.launch, p_idx);
-    for (int i = tid; i < NREP * HD; i += nct) {
-        const int hh = i / HD, d = i % HD;
+#pragma unroll
+        for (int k = 0; k < 4; k++)
+            if (warp + k * MEGA_NCW < ns) wa[k] = ll_word<SYS>(base + (warp + k * MEGA_NCW) * rs + d);
+        float m0 = -INFINITY, l0 = 0.f, m1 = -INFINITY, l1 = 0.f;
+        if (lane < ns) {
+            m0 = ll_settle<SYS>(base + lane * rs + HD, wm0, eout, a.status);
+            l0 = ll_settle<SYS>(base + lane * rs + HD + 1, wl0, eout, a.status);
+        }
+        if (lane + 32 < ns) {
+            m1 = ll_settle<SYS>(base + (lane + 32) * rs + HD, wm1, eout, a.status);
+            l1 = ll_settle<SYS>(base + (lane + 32) * rs + HD + 1, wl1, eout, a.status);
+        }
+        const float M = warp_max(fmaxf(m0, m1));
+        const float w0 = m0 > -INFINITY ? expf(m0 - M) : 0.0f, w1 = m1 > -INFINITY ? expf(m1 - M) : 0.0f;
         float o = 0.0f;
-        for (int r = 0; r < ns; r++) o = fmaf(gat[r * PER + hh * (HD + 4) + d], wsp[hh][r], o);
-        ll_put_out<SYS>(a, ph.bcast, ph.y_ll + (g * NREP + hh) * HD + d, o * invl[hh], eout);
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int r = warp + k * MEGA_NCW;                   // warp-uniform
+            const float wr = __shfl_sync(0xffffffffu, r < 32 ? w0 : w1, r & 31);
+            if (r < ns) o = fmaf(ll_settle<SYS>(base + r * rs + d, wa[k], eout, a.status), wr, o);
+        }
+        msum[warp * 32 + lane] = o;
+        named_bar(1, nct);
+        if (warp == 0) {
+            const float L = warp_sum(l0 * w0 + l1 * w1);
+            const float invl = L > 0.0f ? 1.0f / L : 0.0f;
+            float t = 0.0f;
+            for (int w = 0; w < MEGA_NCW; w++) t += msum[w * 32 + lane];
+            ll_put_out<SYS>(a, ph.bcast, ph.y_ll + (g * NREP + hh) * HD + d, t * invl, eout);
+        }
+        named_bar(1, nct);
     }
-    // profiling: when KV head 0's merge was done (whichever CTA did it)
-    if (a.phase_detail && g == 0 && tid == 0) a.phase_detail[(size_t)p_idx * 4 + 3] = globaltimer_ns();
+    // profiling: when KV head 0's merge was done (the CTA of split 0)
+    if (a.phase_detail && has && g == 0 && sp == 0 && tid == 0)
+        a.phase_detail[(size_t)p_idx * 4 + 3] = globaltimer_ns();
 }
 
 // L2 prefetch of the K and V rows this CTA's attention item will read (the
@@ -1234,16 +1293,18 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a)
 {
     extern __shared__ __align__(128) uint8_t smem[];
     const int      nct = MEGA_NCW * 32, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const MegaSmem P = mega_smem_plan(a.red_floats, a.nst * a.stage_bytes, a.union_bytes);
+    const MegaSmem P = mega_smem_plan(a.red_floats, a.nst * a.stage_bytes, a.union_bytes, a.n_ph);
     MegaShared S;
     S.ring = smem + P.ring;
     S.full = reinterpret_cast<uint64_t *>(smem + P.bars);
     S.abar = reinterpret_cast<uint64_t *>(smem + P.abar);
     S.red = reinterpret_cast<float *>(smem + P.red);
     S.dig = reinterpret_cast<int *>(smem + P.un);
-    S.kvbuf = reinterpret_cast<float *>(smem + P.un);
+    S.kvbuf = reinterpret_cast<float *>(smem + P.un + a.kv_off);
     S.dsum = reinterpret_cast<double *>(smem + P.dsum);
     S.argsh = reinterpret_cast<ArgBest *>(smem + P.argsh);
+    S.tab = reinterpret_cast<const uint4 *>(smem + P.tab);
+    S.n_ph = a.n_ph;
     __shared__ MegaRing ring_state;
     __shared__ int pos_s;
     __shared__ unsigned launch_s;
@@ -1254,6 +1315,9 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a)
     S.cs = cs_row;
     S.dbar = &desc_bar;
 
+    // the phase table into shared memory (the ring cursor reads only it)
+    for (int i = threadIdx.x; i < a.n_ph; i += nct) reinterpret_cast<uint4 *>(smem + P.tab)[i] = __ldg(a.tab + i);
+    __syncthreads();
     if (threadIdx.x == 0) {
         for (int s = 0; s < a.nst; s++) mbar_init(&S.full[s], 1);
         for (int k = 0; k < 5; k++) mbar_init(&S.abar[k], 1);
@@ -1263,7 +1327,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a)
         launch_s = a.bar[3];
         ph_s[0] = a.ph[0];
         S.rc->issued = 0;
-        cursor_load_phase(a, &S.rc->cp, 0);
+        cursor_load_phase(S, &S.rc->cp, 0);
         for (int s = 0; s < a.nst; s++) S.rc->done[s] = 0u;
         for (int s = 0; s < a.nst; s++) ring_issue(a, S, s, false);     // the first chunks
         // the prefetch cursor starts where the copies are and runs
@@ -1272,7 +1336,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a)
         const uint8_t *src;
         int            rows;
         unsigned       rb;
-        for (int s = 0; s < a.pf_stages && cursor_next(a, &S.rc->pf, src, rows, rb); s++)
+        for (int s = 0; s < a.pf_stages && cursor_next(S, &S.rc->pf, src, rows, rb); s++)
             prefetch_l2(src, (uint32_t)rows * rb);
     }
     __syncthreads();
@@ -1322,10 +1386,10 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a)
     if (threadIdx.x == 0) {
         const int n = S.rc->issued;
         for (int j = max(0, n - a.nst); j < n; j++)
-            mbar_drain(&S.full[j % a.nst], (unsigned)(j / a.nst) & 1u, ECU_WAIT_NS);
+            mbar_drain(&S.full[j % a.nst], (unsigned)(j / a.nst) & 1u, wait_limit_ns());
         for (int k = 0; k < 4; k++) {
             const int n_used = k < 2 ? att_sb0 : att_sb1;
-            if (n_used > 0) mbar_drain(&S.abar[k], (unsigned)(n_used - 1) & 1u, ECU_WAIT_NS);
+            if (n_used > 0) mbar_drain(&S.abar[k], (unsigned)(n_used - 1) & 1u, wait_limit_ns());
         }
     }
     // a LAYERS stage advances its position once every phase is done; no

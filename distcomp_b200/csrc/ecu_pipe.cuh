@@ -1,13 +1,21 @@
 // ecu_pipe.cuh -- mbarrier + bulk-copy primitives (sm_90+/sm_100a PTX) and
-// bounded waits.  Every wait gives up after ECU_WAIT_NS of wall time, sets
+// bounded waits.  Every wait gives up after wait_limit_ns() of wall time, sets
 // ECU_STATUS_TIMEOUT in the context's status word and lets the kernel run to
 // its end, so that a logic error can never leave a GPU spinning.
 #pragma once
 #include "ecu_common.cuh"
 
 #ifndef ECU_WAIT_NS
-#define ECU_WAIT_NS 2000000000ull   // 2 s
+#define ECU_WAIT_NS 2000000000ull   // 2 s: the default limit
 #endif
+
+// The wall-time limit of every bounded wait in this translation unit's
+// kernels, per device; ecu_set_wait_ns changes it between launches (tests of
+// the give-up path shorten it).  Read through the read-only path: it only
+// changes while no kernel runs.
+static __device__ unsigned long long g_wait_ns = ECU_WAIT_NS;
+
+__device__ __forceinline__ unsigned long long wait_limit_ns() { return __ldg(&g_wait_ns); }
 
 __device__ __forceinline__ uint32_t smem_addr(const void *p)
 {
@@ -72,7 +80,7 @@ __device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity)
     return ok != 0;
 }
 
-// Wait for phase `parity` of `bar` to complete, at most ECU_WAIT_NS.
+// Wait for phase `parity` of `bar` to complete, at most wait_limit_ns().
 // Returns false (and flags *status) on timeout.  With FAIL_FAST, a wait that
 // finds the step already flagged (by any wait) gives up at once: a kernel
 // with thousands of waits then ends after one timeout, not one per wait.
@@ -89,7 +97,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *s
         // the status word is global memory: look at it only once a wait has
         // lasted long enough to suggest trouble, not on every pass
         if (FAIL_FAST && status && dt > 20000 && *reinterpret_cast<volatile int *>(status) != 0) return false;
-        if (dt > ECU_WAIT_NS) {
+        if (dt > wait_limit_ns()) {
             if (status) atomicOr(status, ECU_STATUS_TIMEOUT);
             return false;
         }

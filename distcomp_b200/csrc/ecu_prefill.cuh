@@ -395,7 +395,7 @@ static __global__ void __launch_bounds__(128, 1) k_pf_gemm_tc(const __half *Ahi,
     asm volatile("cp.async.wait_all;" ::: "memory");
     if (last_commit >= 0) {
         const bool done = mbar_drain(&mbar[last_commit % PF_TC_STAGES],
-                                     (unsigned)(last_commit / PF_TC_STAGES) & 1u, ECU_WAIT_NS);
+                                     (unsigned)(last_commit / PF_TC_STAGES) & 1u, wait_limit_ns());
         if (!done && status) atomicOr(status, ECU_STATUS_TIMEOUT);
         ok = __syncthreads_and(ok && done) != 0;
     }

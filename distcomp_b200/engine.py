@@ -95,6 +95,8 @@ SIGNATURES = [
     ("ecu_matvec", C.c_int, [C.c_uint, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_int]),
     ("ecu_matvec_argmax_noalloc", C.c_int, [C.c_uint, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
                                             C.c_void_p, C.c_void_p]),
+    ("ecu_set_wait_ns", C.c_int, [C.c_int, C.c_ulonglong]),
+    ("ecu_inject_wait_timeout", C.c_int, [C.c_void_p]),
     ("ecu_matvec_bench", C.c_int, [C.c_uint, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_int,
                                    C.c_int, C.c_int, C.POINTER(C.c_double)]),
     ("ecu_profile_steps", C.c_int, [C.c_void_p, C.c_int, C.POINTER(EcuKprof), C.c_int]),
@@ -290,6 +292,12 @@ class LlmCtx:
         if lib().ecu_step_dev(self.h, C.c_void_p(stream or 0)) != 0:
             raise EngineError(last_error())
 
+    def inject_wait_timeout(self) -> None:
+        """The next persistent step waits for an input word no phase writes
+        (ecu_inject_wait_timeout): failure-path testing."""
+        if lib().ecu_inject_wait_timeout(self.h) != 0:
+            raise EngineError(last_error())
+
     def path(self) -> str:
         """"persistent" or "kernels: <why not>" (ecu_ctx_path)."""
         return (lib().ecu_ctx_path(self.h) or b"").decode()
@@ -358,3 +366,9 @@ def matvec_bench(gtype: int, raw: np.ndarray, n_in: int, n_out: int, x: np.ndarr
                               C.byref(ms)) != 0:
         raise EngineError(last_error())
     return ms.value, y
+
+
+def set_wait_ns(ns: int, device: int = 0) -> None:
+    """The limit after which every bounded wait in the kernels gives up."""
+    if lib().ecu_set_wait_ns(device, int(ns)) != 0:
+        raise EngineError(last_error())

@@ -414,6 +414,8 @@ def bench_main(args, rank: int, world: int, local: int, B) -> int:
         # (2) n_seq interleaved sequences: prompt, warm-up, timed, end-to-end
         total = args.prompt + args.warmup + 2 * args.steps
         sched = Schedule(world, n_seq, total, n_prompt=args.prompt)
+        if st.has_head:
+            st.record_tokens(total)
         ta = sched.step_ticks(args.prompt + args.warmup)[0]
         tb = sched.step_ticks(args.prompt + args.warmup + args.steps)[0]
         run_ticks(sched, stages, ex, t0=0, t1=ta)
@@ -432,6 +434,23 @@ def bench_main(args, rank: int, world: int, local: int, B) -> int:
         # tokens completed in the end-to-end window: every step after tb
         e2e_steps = total - (args.prompt + args.warmup + args.steps)
         e2e = n_seq * e2e_steps / (e2e_ms / 1e3)
+        # sequence 0's greedy tokens through the pipeline (the last stage's
+        # record) against one GPU's FULL context on the same prompt
+        hist = st.history[0].clone() if st.has_head else torch.zeros(total, dtype=torch.int32, device=st.dev)
+        dist.broadcast(hist, src=world - 1)
+        st.close()
+        pp_check = None
+        if rank == 0:
+            n_gen = total - args.prompt + 1
+            ref = B.one_gpu_tokens(model, spec, args, local, n_gen, prompts[0])
+            got = [int(t) for t in hist[args.prompt - 1:].cpu().tolist()]
+            pp_check = {"tokens_match_one_gpu": got == ref, "tokens_checked": n_gen, "sequence": 0}
+        dist.barrier()
+        # (3) the other partition on the same GPUs: batch-1 tensor parallel
+        from . import tensor_parallel
+        tp_prompt = synth.prompt_tokens(args.prompt, spec.n_vocab, seed=args.seed)
+        tp_ref = B.one_gpu_tokens(model, spec, args, local, 32, tp_prompt) if rank == 0 else None
+        tp = tensor_parallel.measure(args, rank, world, local, B, model, spec, ref_tokens=tp_ref)
 
         if rank == 0:
             peak, peak_kind = B.peaks()
@@ -460,9 +479,10 @@ def bench_main(args, rank: int, world: int, local: int, B) -> int:
                                "host and waits for them"},
                 "gpu_launches": int(lt.item()),
                 "clocks": clk,
+                "pp_parity": pp_check,
+                "tp": tp,
             }
             print(json.dumps(line), flush=True)
-        st.close()
         dist.barrier()
     finally:
         dist.destroy_process_group()

@@ -128,23 +128,34 @@ def quantize_torch(w, gtype: int):
     fp16(d), then q[i] | q[i+16] << 4 for i < 16.
     Q8_0: d = max|x| / 127, id = 1/d (0 when d == 0), q = round-half-away(x*id)
     as int8; bytes = fp16(d), q[0..31].
-    Every step is a single fp32 operation, so the result is bit-identical to
-    gguf-py's numpy code (checked in tests/test_synth.py)."""
+    Every step is a single fp32 operation (and the first maximum is picked
+    explicitly), so the result is bit-identical to gguf-py's numpy code on
+    the CPU and on the GPU (checked in tests/test_synth.py)."""
     import torch
     x = w.reshape(-1, 32).to(torch.float32)
     nblk = x.shape[0]
     if gtype == G.Q4_0:
-        idx = x.abs().argmax(dim=1, keepdim=True)
+        # the first element of largest magnitude, spelled out: torch.argmax
+        # on CUDA does not promise the first index on ties (x and -x both at
+        # the block maximum happen in about one block in 30,000 of N(0,1)
+        # draws), and the sign of m decides the whole block
+        ax = x.abs()
+        amax = ax.amax(dim=1, keepdim=True)
+        pos = torch.arange(32, device=x.device, dtype=torch.int64).expand_as(ax)
+        idx = torch.where(ax == amax, pos, torch.full_like(pos, 32)).amin(dim=1, keepdim=True)
         m = torch.gather(x, 1, idx)
-        d = m / -8.0
-        inv = torch.where(d == 0, torch.zeros_like(d), 1.0 / d)
+        d = m / torch.full_like(m, -8.0)
+        inv = torch.where(d == 0, torch.zeros_like(d), torch.ones_like(d) / d)
         q = torch.trunc(x * inv + 8.5).clamp(0, 15).to(torch.uint8)
         packed = q[:, :16] | (q[:, 16:] << 4)
         dh = d.to(torch.float16).view(torch.uint8).reshape(nblk, 2)
         return torch.cat([dh, packed], dim=1).reshape(-1)
     if gtype == G.Q8_0:
-        d = x.abs().amax(dim=1, keepdim=True) / 127.0
-        inv = torch.where(d == 0, torch.zeros_like(d), 1.0 / d)
+        # a tensor divisor: torch's CUDA kernel for tensor / python-scalar
+        # multiplies by the scalar's reciprocal, which is not 1/127 exactly
+        amax = x.abs().amax(dim=1, keepdim=True)
+        d = amax / torch.full_like(amax, 127.0)
+        inv = torch.where(d == 0, torch.zeros_like(d), torch.ones_like(d) / d)
         v = x * inv
         a = v.abs()
         fl = a.floor()

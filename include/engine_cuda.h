@@ -227,6 +227,22 @@ int  ecu_matvec(unsigned ggml_type, const void *w_raw, int n_in, int n_out, cons
 int  ecu_matvec_argmax_noalloc(unsigned ggml_type, const void *d_w, int n_in, int n_out,
                                const float *d_x, float *d_y, int *d_token, void *stream);
 
+/* ---- failure-path testing ------------------------------------------------ */
+
+/* No counterpart in the reference, whose failure paths are host retries and
+ * aborts (src/shard.c:533-545).  Every wait inside the engine's kernels (a
+ * tagged word from another CTA or rank, a bulk copy's barrier) is bounded:
+ * after the limit it sets the context's status word and lets the kernel run
+ * to its end, and the step returns -1.  ecu_set_wait_ns sets that limit on
+ * `device` (default 2 s; between launches).  ecu_inject_wait_timeout makes
+ * the next persistent step of `c` wait, in its first GEMV phase with a
+ * tagged input, for an input word that no phase writes: its waits run out,
+ * that step returns -1 with the timeout in ecu_last_error, and the context
+ * steps normally again afterwards (reset it: that step's cache row is not
+ * valid).  -1 for a context on the per-kernel step. */
+int  ecu_set_wait_ns(int device, unsigned long long ns);
+int  ecu_inject_wait_timeout(ecu_ctx *c);
+
 /* ---- measurement --------------------------------------------------------- */
 
 /* Quantised-matvec microbenchmark (the reference's matvec,

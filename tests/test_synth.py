@@ -15,6 +15,8 @@ def test_quantize_torch_matches_numpy_rule(t):
     w = (rng.standard_normal((64, 256)) * 0.02).astype(np.float32)
     w[3, :32] = 0.0                       # an all-zero block
     w[5, 40] = 0.5                        # a block with one large element
+    w[7, 35], w[7, 50] = -0.25, 0.25      # the block maximum twice, opposite signs: the first decides
+    w[9, 70], w[9, 66] = 0.25, -0.25
     a = synth.quantize_numpy(w, t)
     b = synth.quantize_torch(torch.from_numpy(w.reshape(-1)), t).numpy()
     assert np.array_equal(a, b)
@@ -58,3 +60,19 @@ def test_q4k_specs():
     assert s.wtype == G.Q4_K and s.n_ff > 16384 and s.n_ff % 2048 == 0
     assert all(gt == G.Q4_K for name, dims, gt in synth.tensor_list(s) if name.startswith("blk.")
                and name.endswith("weight") and "norm" not in name)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("t", [G.Q4_0, G.Q8_0])
+def test_quantize_torch_on_gpu_matches_numpy_rule(t):
+    """The same bytes on the GPU, with many blocks whose maximum magnitude
+    occurs twice with opposite signs (the first one decides a Q4_0 block)."""
+    rng = np.random.default_rng(17 + t)
+    w = (rng.standard_normal((4096, 256)) * 0.02).astype(np.float32)
+    blk = w.reshape(-1, 32)
+    for i in range(0, blk.shape[0], 3):
+        j = int(np.argmax(np.abs(blk[i])))
+        blk[i, (j + 1 + i % 31) % 32] = -blk[i, j]
+    a = synth.quantize_numpy(w, t)
+    b = synth.quantize_torch(torch.from_numpy(w.reshape(-1)).cuda(), t).cpu().numpy()
+    assert np.array_equal(a, b)

@@ -253,6 +253,8 @@ def our_arm(args, rank, world, local):
         return tensor_parallel.bench_main(args, rank, world, local, sys.modules[__name__])
     if world > 1:
         from distcomp_b200 import pipeline
+        if args.model != CONFIG:
+            return pipeline.bench_long_main(args, rank, world, local, sys.modules[__name__])
         return pipeline.bench_main(args, rank, world, local, sys.modules[__name__])
 
     spec = synth.spec(args.model, **({"n_layer": args.layers} if args.layers else {}))

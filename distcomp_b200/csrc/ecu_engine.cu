@@ -1340,12 +1340,11 @@ static int mega_profile(ecu_ctx *c, int n_steps, ecu_kprof *out, int max_kinds)
             // CTA 0's SM cycles per ns over this launch
             const double f = (double)(clk[np] - clk[0]) / (double)std::max<unsigned long long>(1, ns[np] - ns[0]);
             if (dt[0] && dt[1] && dt[2]) {
-                // attention phases: [3] is when KV head 0's merge ended
+                // [3]: ns warp 0 waited for ring stages (GEMV) / its K/V copies (attention)
                 const bool att = c->ph_bytes[p] < 0;
-                const char *part[4] = {"prologue", "main", "epilogue", att ? "merged" : "ring_wait"};
+                const char *part[4] = {"prologue", "main", "epilogue", att ? "kv_wait" : "ring_wait"};
                 const double v[4] = {(double)(dt[0] - clk[p]) / f, (double)(dt[1] - dt[0]) / f,
-                                     (double)(dt[2] - dt[1]) / f,
-                                     att ? (dt[3] > ns[p] ? (double)(dt[3] - ns[p]) : 0.0) : (double)dt[3]};
+                                     (double)(dt[2] - dt[1]) / f, (double)dt[3]};
                 for (int q = 0; q < 4; q++) {
                     char nm[32];
                     snprintf(nm, sizeof nm, "%.20s:%s", c->ph_kind[p], part[q]);
@@ -2577,35 +2576,22 @@ static int pf_gemm(ecu_ctx *c, const DevMat &m, int n, float *C, const float *R)
     return 0;
 }
 
-int ecu_prefill(ecu_ctx *c, const int *tokens, int n, float *out)
+// Can the batched kernels run this context's prompt (else: token by token)?
+static bool pf_batched(const ecu_ctx *c, bool &attn2)
 {
-    if (!c || !tokens || !out || n < 1) { ecu_set_error(nullptr, 0, "null argument or empty prompt"); return -1; }
-    cudaSetDevice(c->device);
     const EcuGeom &g = c->g;
-    for (int i = 0; i < n; i++)
-        if (tokens[i] < 0 || tokens[i] >= g.n_vocab) {
-            ecu_set_error(nullptr, 0, "token %d outside the vocabulary (%d)", tokens[i], g.n_vocab);
-            return -1;
-        }
-    if (c->stage != ECU_STAGE_FULL) { ecu_set_error(nullptr, 0, "prefill runs FULL contexts"); return -1; }
-    if (c->pos + n > g.n_ctx) {
-        ecu_set_error(nullptr, 0, "prompt of %d tokens at position %d exceeds the context (%d)", n, c->pos, g.n_ctx);
-        return -1;
-    }
     // the token-tiled attention (k_pf_attn2) has no position limit; the
     // one-query-per-CTA kernel keeps its scores in a PF_ATT_MAXPOS array
     const char *ae = getenv("ECU_PF_ATTN");
-    const bool  attn2 = PF_QB % g.n_rep == 0 && !(ae && ae[0] == '0');
+    attn2 = PF_QB % g.n_rep == 0 && !(ae && ae[0] == '0');
     bool batched = c->tp.world == 1 && (attn2 || g.n_ctx <= PF_ATT_MAXPOS) && (g.head_dim == 64 || g.head_dim == 128) &&
                    g.n_embd % 8 == 0 && g.n_ff % 8 == 0;
     for (auto &ly : c->layers) batched = batched && ly.qkv.size() == 1 && ly.gu_fused;
-    if (!batched) {
-        // shapes the batched kernels do not cover (and tensor-parallel ranks,
-        // which step together): the per-token step, prompt token by token
-        for (int i = 0; i < n; i++)
-            if (ecu_forward(c, tokens[i], out) != 0) return -1;
-        return 0;
-    }
+    return batched;
+}
+
+static int pf_attrs(const ecu_ctx *c)
+{
     static std::atomic<unsigned> attr_done{0};            // per device (bit d), set once
     if (c->device >= 32 || !(attr_done.load() & (1u << c->device))) {
         CK(cudaFuncSetAttribute(k_pf_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pf_gemm_smem()));
@@ -2614,14 +2600,19 @@ int ecu_prefill(ecu_ctx *c, const int *tokens, int n, float *out)
         CK(cudaFuncSetAttribute(k_pf_attn2<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pf_attn2_smem<64>()));
         if (c->device < 32) attr_done.fetch_or(1u << c->device);
     }
-    if (pf_reserve(c, n) != 0) return -1;
+    return 0;
+}
+
+// The context's layers over the n rows of P.X (positions pos0..pos0+n-1):
+// the KV cache filled, P.X holding the last layer's output rows.
+static int pf_layers(ecu_ctx *c, int n, int pos0, bool attn2)
+{
     ecu_ctx::Prefill &P = c->pf;
-    const int hd = g.head_dim, qd = g.n_head * hd, kvd = g.n_head_kv * hd, E = g.n_embd, pos0 = c->pos;
+    const EcuGeom &g = c->g;
+    const int hd = g.head_dim, qd = g.n_head * hd, kvd = g.n_head_kv * hd, E = g.n_embd;
     const int ldq = qd + 2 * kvd;
     const size_t plane = (size_t)g.n_head_kv * g.n_ctx * hd;
     const float kscale = 1.0f / sqrtf((float)hd);
-    CK(cudaMemcpyAsync(P.tok, tokens, sizeof(int) * n, cudaMemcpyHostToDevice, c->stream));
-    k_pf_embed<<<4 * c->sms, 256, 0, c->stream>>>(c->emb, P.tok, n, P.X, E);
     for (size_t li = 0; li < c->layers.size(); li++) {
         LayerDev &ly = c->layers[li];
         k_pf_norm_split<<<n, 256, 0, c->stream>>>(P.X, ly.attn_norm, E, g.eps, P.ah, P.al);
@@ -2657,25 +2648,129 @@ int ecu_prefill(ecu_ctx *c, const int *tokens, int n, float *out)
         if (pf_gemm(c, ly.d, n, P.X, P.X)) return -1;
         CK(cudaGetLastError());
     }
-    // the last token through the decode step's head (norm, logits, argmax)
-    CK(cudaMemcpyAsync(c->state, P.X + (size_t)(n - 1) * E, sizeof(float) * E, cudaMemcpyDeviceToDevice, c->stream));
-    StepState *slot = c->h_st + ((pos0 + n - 1) % c->n_hslots);
-    slot->pos = pos0 + n - 1;
-    slot->token = tokens[n - 1];
+    g_launches += 15 * c->layers.size();
+    return 0;
+}
+
+// Row `row` of the device rows x as the head's input: the decode step's head
+// (norm, logits, argmax) at position pos, the result (normed state + token)
+// copied to out.
+static int pf_head(ecu_ctx *c, const float *x_row, int pos, int token, float *out)
+{
+    const EcuGeom &g = c->g;
+    const size_t   ne = (size_t)g.n_embd;
+    CK(cudaMemcpyAsync(c->state, x_row, sizeof(float) * ne, cudaMemcpyDeviceToDevice, c->stream));
+    StepState *slot = c->h_st + (pos % c->n_hslots);
+    slot->pos = pos;
+    slot->token = token;
     CK(cudaMemcpyAsync(c->st, slot, 2 * sizeof(int), cudaMemcpyHostToDevice, c->stream));
     Launcher L{c->stream, false};
     enqueue_head(c, L, true);
-    g_launches += (uint64_t)L.count + 15 * c->layers.size() + 1;   // + embed, 15 kernels a layer
+    g_launches += (uint64_t)L.count;
     if (L.err != cudaSuccess) {
         ecu_set_error(nullptr, 0, "kernel launch failed: %s", cudaGetErrorString(L.err));
         return -1;
     }
-    c->pos = pos0 + n;
+    c->pos = pos + 1;
     c->have_logits = true;
-    const size_t ne = (size_t)E;
     CK(cudaMemcpyAsync(c->h_state, c->state, (ne + 1) * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
     if (check_status(c) != 0) return -1;
     memcpy(out, c->h_state, (ne + 1) * sizeof(float));
     c->last_pick = (int)c->h_state[ne];
     return 0;
+}
+
+int ecu_prefill_rows(ecu_ctx *c, const int *tokens, int n, float *x, float *out)
+{
+    if (!c || n < 1 || !x) { ecu_set_error(nullptr, 0, "null argument or empty prompt"); return -1; }
+    cudaSetDevice(c->device);
+    const EcuGeom &g = c->g;
+    const size_t   rows_bytes = sizeof(float) * (size_t)n * g.n_embd;
+    if (c->stage == ECU_STAGE_FULL) { ecu_set_error(nullptr, 0, "a FULL context prefills with ecu_prefill"); return -1; }
+    if (c->stage == ECU_STAGE_EMBED) {
+        if (!tokens) { ecu_set_error(nullptr, 0, "EMBED needs the prompt tokens"); return -1; }
+        for (int i = 0; i < n; i++)
+            if (tokens[i] < 0 || tokens[i] >= g.n_vocab) {
+                ecu_set_error(nullptr, 0, "token %d outside the vocabulary (%d)", tokens[i], g.n_vocab);
+                return -1;
+            }
+        int *tok = nullptr;
+        CK(cudaMallocAsync((void **)&tok, sizeof(int) * n, c->stream));
+        CK(cudaMemcpyAsync(tok, tokens, sizeof(int) * n, cudaMemcpyHostToDevice, c->stream));
+        k_pf_embed<<<4 * c->sms, 256, 0, c->stream>>>(c->emb, tok, n, x, g.n_embd);
+        CK(cudaGetLastError());
+        CK(cudaFreeAsync(tok, c->stream));
+        g_launches += 1;
+        c->pos += n;
+        CK(cudaStreamSynchronize(c->stream));
+        return 0;
+    }
+    if (c->stage == ECU_STAGE_HEAD) {
+        if (!out) { ecu_set_error(nullptr, 0, "HEAD needs the output buffer"); return -1; }
+        const int pos = c->pos + n - 1;
+        return pf_head(c, x + (size_t)(n - 1) * g.n_embd, pos, tokens ? tokens[n - 1] : 0, out);
+    }
+    // LAYERS
+    if (c->pos + n > g.n_ctx) {
+        ecu_set_error(nullptr, 0, "prompt of %d tokens at position %d exceeds the context (%d)", n, c->pos, g.n_ctx);
+        return -1;
+    }
+    bool attn2 = false;
+    if (!pf_batched(c, attn2)) {
+        // the per-token step, row by row
+        std::vector<float> h((size_t)g.n_embd + 8);
+        for (int i = 0; i < n; i++) {
+            CK(cudaMemcpy(h.data(), x + (size_t)i * g.n_embd, sizeof(float) * g.n_embd, cudaMemcpyDeviceToHost));
+            if (ecu_forward(c, 0, h.data()) != 0) return -1;
+            CK(cudaMemcpy(x + (size_t)i * g.n_embd, h.data(), sizeof(float) * g.n_embd, cudaMemcpyHostToDevice));
+        }
+        return 0;
+    }
+    if (pf_attrs(c) != 0 || pf_reserve(c, n) != 0) return -1;
+    const int pos0 = c->pos;
+    CK(cudaMemcpyAsync(c->pf.X, x, rows_bytes, cudaMemcpyDeviceToDevice, c->stream));
+    if (pf_layers(c, n, pos0, attn2) != 0) return -1;
+    CK(cudaMemcpyAsync(x, c->pf.X, rows_bytes, cudaMemcpyDeviceToDevice, c->stream));
+    c->pos = pos0 + n;
+    // the stage's state: the last row (what a LAYERS forward outputs)
+    CK(cudaMemcpyAsync(c->state, c->pf.X + (size_t)(n - 1) * g.n_embd, sizeof(float) * g.n_embd,
+                       cudaMemcpyDeviceToDevice, c->stream));
+    StepState *slot = c->h_st + (c->pos % c->n_hslots);
+    slot->pos = c->pos;
+    slot->token = 0;
+    CK(cudaMemcpyAsync(c->st, slot, 2 * sizeof(int), cudaMemcpyHostToDevice, c->stream));
+    return check_status(c);
+}
+
+int ecu_prefill(ecu_ctx *c, const int *tokens, int n, float *out)
+{
+    if (!c || !tokens || !out || n < 1) { ecu_set_error(nullptr, 0, "null argument or empty prompt"); return -1; }
+    cudaSetDevice(c->device);
+    const EcuGeom &g = c->g;
+    for (int i = 0; i < n; i++)
+        if (tokens[i] < 0 || tokens[i] >= g.n_vocab) {
+            ecu_set_error(nullptr, 0, "token %d outside the vocabulary (%d)", tokens[i], g.n_vocab);
+            return -1;
+        }
+    if (c->stage != ECU_STAGE_FULL) { ecu_set_error(nullptr, 0, "prefill runs FULL contexts"); return -1; }
+    if (c->pos + n > g.n_ctx) {
+        ecu_set_error(nullptr, 0, "prompt of %d tokens at position %d exceeds the context (%d)", n, c->pos, g.n_ctx);
+        return -1;
+    }
+    bool attn2 = false;
+    if (!pf_batched(c, attn2)) {
+        // shapes the batched kernels do not cover (and tensor-parallel ranks,
+        // which step together): the per-token step, prompt token by token
+        for (int i = 0; i < n; i++)
+            if (ecu_forward(c, tokens[i], out) != 0) return -1;
+        return 0;
+    }
+    if (pf_attrs(c) != 0 || pf_reserve(c, n) != 0) return -1;
+    ecu_ctx::Prefill &P = c->pf;
+    const int E = g.n_embd, pos0 = c->pos;
+    CK(cudaMemcpyAsync(P.tok, tokens, sizeof(int) * n, cudaMemcpyHostToDevice, c->stream));
+    k_pf_embed<<<4 * c->sms, 256, 0, c->stream>>>(c->emb, P.tok, n, P.X, E);
+    g_launches += 1;
+    if (pf_layers(c, n, pos0, attn2) != 0) return -1;
+    return pf_head(c, P.X + (size_t)(n - 1) * E, pos0 + n - 1, tokens[n - 1], out);
 }

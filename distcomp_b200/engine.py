@@ -86,6 +86,7 @@ SIGNATURES = [
     ("ecu_tp_connect", C.c_int, [C.c_void_p, C.c_char_p]),
     ("ecu_tp_slice", C.c_int, [C.c_void_p, C.POINTER(C.c_int)]),
     ("ecu_prefill", C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p]),
+    ("ecu_prefill_rows", C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
     ("ecu_generate", C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
     ("ecu_decode_async", C.c_int, [C.c_void_p, C.c_int]),
     ("ecu_sync", C.c_int, [C.c_void_p]),
@@ -266,6 +267,18 @@ class LlmCtx:
         if lib().ecu_prefill(self.h, _ptr(p), len(p), _ptr(out)) != 0:
             raise EngineError(last_error())
         return int(out[self.n_embd])
+
+    def prefill_rows(self, x_ptr: int, n: int, tokens=None, out: np.ndarray | None = None) -> int | None:
+        """One pipeline stage's batched prompt over n device rows at x_ptr
+        (ecu_prefill_rows); HEAD returns the picked token."""
+        tk = None if tokens is None else np.ascontiguousarray(tokens, dtype=np.int32)
+        if out is None and self.stage == STAGE_HEAD:
+            out = np.zeros(self.n_embd + 1, dtype=np.float32)
+        rc = lib().ecu_prefill_rows(self.h, None if tk is None else _ptr(tk), int(n), C.c_void_p(int(x_ptr)),
+                                    None if out is None else _ptr(out))
+        if rc != 0:
+            raise EngineError(last_error())
+        return int(out[self.n_embd]) if self.stage == STAGE_HEAD else None
 
     def decode_async(self, n: int) -> None:
         if lib().ecu_decode_async(self.h, int(n)) != 0:

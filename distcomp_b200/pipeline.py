@@ -319,6 +319,41 @@ class GpuStage:
                 c.close()
 
 
+def prefill_local(stages: dict, seq: int, prompt, send_rows=None, recv_rows=None, share_token=None) -> int | None:
+    """The prompt of sequence `seq` through the pipeline as one batch per
+    stage (ecu_prefill_rows): the reference's token-by-token prompt feed
+    (src/shard.c:911-917) becomes one hop of n rows per stage boundary.
+    stages: {rank: GpuStage} of this process, run in rank order on one row
+    buffer; with one rank per process, recv_rows(r, rows) / send_rows(r,
+    rows) carry the rows from rank r-1 / to rank r+1, and share_token(tok)
+    brings the last stage's picked token to every rank.  The first stage's
+    device token of the sequence is set to it, ready for the first decode
+    step.  Returns the token."""
+    import torch
+    n = len(prompt)
+    rows, tok = None, None
+    for r in sorted(stages):
+        st = stages[r]
+        if rows is None:
+            rows = torch.empty((n, st.n_embd), dtype=torch.float32, device=st.dev)
+        if recv_rows is not None and r > 0:
+            recv_rows(r, rows)
+            torch.cuda.current_stream(st.dev).synchronize()
+        for c in st.chains[seq]:
+            t = c.prefill_rows(rows.data_ptr(), n, tokens=prompt)
+            if t is not None:
+                tok = t
+        if send_rows is not None and r + 1 < st.n_ranks:
+            send_rows(r, rows)
+    if share_token is not None:
+        tok = share_token(tok)
+    if 0 in stages:
+        st0 = stages[0]
+        with torch.cuda.stream(st0.stream):
+            st0._token[seq][0].fill_(int(tok))
+    return tok
+
+
 def device_view(ptr: int, n: int, typestr: str, device: int):
     """A torch tensor over n elements of device memory owned by the engine
     (no copy, no ownership)."""
@@ -483,6 +518,153 @@ def bench_main(args, rank: int, world: int, local: int, B) -> int:
                 "tp": tp,
             }
             print(json.dumps(line), flush=True)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+    return 0
+
+
+def bench_long_main(args, rank: int, world: int, local: int, B) -> int:
+    """bench.py --model llama2-70b at N > 1: the 70B shape (Q4_K layers,
+    Q8_0 embedding and head) layer-pipelined over `world` GPUs, batch 1.
+    Each rank generates only its stage's tensors (synth.stage_tensors; the
+    same bytes as the whole model's); the prompt goes through the stages as
+    one batch per stage (ecu_prefill_rows, the rows handed on by NCCL
+    send/recv); then K greedy decode steps of the one sequence, one stage
+    busy at a time (the tick schedule of the 8B pipeline with one sequence).
+    B is the bench module."""
+    import datetime
+    import json
+    import time
+    import torch
+    import torch.distributed as dist
+    from . import engine as E
+    from . import synth
+
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", local),
+                            timeout=datetime.timedelta(seconds=600))
+    try:
+        spec = synth.spec(args.model, **({"n_layer": args.layers} if args.layers else {}))
+        lb = layer_bytes(spec)
+        head_b = tensor_bytes(spec, "output.weight") + tensor_bytes(spec, "output_norm.weight")
+        emb_row = tensor_bytes(spec, "token_embd.weight") // spec.n_vocab
+        plan = split_stages(spec.n_layer, world) if args.split == "ref" else \
+            split_by_bytes(lb, world, head_bytes=head_b, embed_bytes=emb_row)
+        first, last = plan[rank]
+        need = args.prompt + args.warmup + args.steps + 2
+        if need > args.n_ctx:
+            raise SystemExit(f"prompt + steps need {need} positions > n_ctx {args.n_ctx}")
+        t_b = time.perf_counter()
+        only = synth.stage_tensors(spec, first, last, rank == 0, rank == world - 1)
+        torch.cuda.set_device(local)
+        buf = synth.build_model(spec, seed=args.seed, device=f"cuda:{local}", only=only)
+        torch.cuda.empty_cache()
+        model = E.GgufModel(buf)
+        st = GpuStage(model, rank, world, first, last, spec.n_layer, 1, args.n_ctx, local)
+        del buf
+        t_b = time.perf_counter() - t_b
+        prompt = synth.prompt_tokens(args.prompt, spec.n_vocab, seed=args.seed)
+        dev = torch.device("cuda", local)
+
+        def send_rows(r, rows):
+            dist.send(rows, r + 1)
+
+        def recv_rows(r, rows):
+            dist.recv(rows, r - 1)
+
+        def share_token(tok):
+            t = torch.tensor([tok if rank == world - 1 else 0], dtype=torch.int64, device=dev)
+            dist.broadcast(t, world - 1)
+            return int(t.item())
+
+        dist.barrier()
+        t0 = time.perf_counter()
+        first_tok = prefill_local({rank: st}, 0, prompt, send_rows, recv_rows, share_token)
+        dist.barrier()
+        pf_s = time.perf_counter() - t0
+
+        n = len(prompt)
+        sched = Schedule(world, 1, args.warmup + 2 * args.steps, n_prompt=n, first_step=n)
+        ex = DistExchanger(rank)
+        stages = {rank: st}
+        ta = sched.step_ticks(n + args.warmup)[0]
+        tb = sched.step_ticks(n + args.warmup + args.steps)[0]
+        run_ticks(sched, stages, ex, t0=0, t1=ta)
+        clocks = B.ClockSampler(local)
+        if rank == 0:
+            clocks.start()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        dist.barrier()
+        torch.cuda.synchronize(local)
+        l0 = E.kernel_launches()
+        ev0.record(st.stream)
+        run_ticks(sched, stages, ex, t0=ta, t1=tb)
+        ev1.record(st.stream)
+        torch.cuda.synchronize(local)
+        launches = E.kernel_launches() - l0
+        clk = clocks.stop() if rank == 0 else None
+        ms_t = torch.tensor([ev0.elapsed_time(ev1)], dtype=torch.float64, device=dev)
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+        ms = float(ms_t.item())
+        tps = args.steps / (ms / 1e3)
+        # end to end: the last stage copies every step's token to the host
+        pinned = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+        toks = []
+
+        def tick(t):
+            w = sched.work(rank, t)
+            if w is not None and st.has_head:
+                with torch.cuda.stream(st.stream):
+                    pinned.copy_(st._token[0][-1], non_blocking=True)
+                st.stream.synchronize()
+                toks.append(int(pinned.item()))
+
+        dist.barrier()
+        torch.cuda.synchronize(local)
+        h0 = time.perf_counter()
+        run_ticks(sched, stages, ex, t0=tb, t1=sched.n_ticks, on_tick=tick)
+        st.sync()
+        e2e_t = torch.tensor([time.perf_counter() - h0], dtype=torch.float64, device=dev)
+        dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
+        e2e = args.steps / float(e2e_t.item())
+        lt = torch.tensor([launches], dtype=torch.int64, device=dev)
+        dist.all_reduce(lt)
+        tk = torch.tensor(toks[:8] + [0] * (8 - len(toks[:8])), dtype=torch.int64, device=dev)
+        dist.broadcast(tk, world - 1)
+        if rank == 0:
+            peak, peak_kind = B.peaks()
+            bpt = B.algorithmic_bytes_per_token(spec, n + args.warmup + (args.steps - 1) / 2)
+            pf_flops = 2.0 * n * B.prefill_params(spec)
+            line = {
+                "metric": B.metric_for(args.model), "value": round(tps, 2), "unit": "tokens/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": B.dtype_text(spec),
+                "data": "synthetic: seeded N(0,0.02) weights quantised on the GPU, each rank its stage's tensors; "
+                        "random prompt",
+                "config": {"workload": B.workload_text(spec, args.model) + f", KV fp32 {args.n_ctx}, layer pipeline "
+                                       f"over {world} GPUs, batch 1",
+                           "stages": [list(p_) for p_ in plan], "split": args.split, "prompt_tokens": n,
+                           "decode_positions": [n + args.warmup, n + args.warmup + args.steps - 1],
+                           "l2": f"inputs larger than L2 ({bpt / 1e9:.1f} GB per token)"},
+                "token_roofline": {"bytes_per_token": bpt, "achieved_gbs": round(bpt * tps / 1e9, 1),
+                                   "peak_gbs": peak, "frac": round(bpt * tps / 1e9 / peak, 4),
+                                   "frac_of_8tbs_nominal": round(bpt * tps / 1e9 / 8000, 4), "peak_kind": peak_kind,
+                                   "note": "batch 1 through a layer pipeline: one stage streams at a time, so the "
+                                           "bound is one GPU's HBM bandwidth"},
+                "prefill": {"tokens": n, "s": round(pf_s, 3), "tokens_per_s": round(n / pf_s, 1),
+                            "tflops_useful": round(pf_flops / pf_s / 1e12, 2),
+                            "note": "the prompt as one batch per stage (ecu_prefill_rows), the rows handed on by "
+                                    "NCCL send/recv; wall time with barriers", "first_token": first_tok},
+                "e2e": {"value": round(e2e, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 4,
+                        "api": "ecu_step_dev chain per stage; the last stage copies each token to the host"},
+                "first_decode_tokens": [int(v) for v in tk.cpu().tolist()],
+                "gpu_launches": int(lt.item()),
+                "clocks": clk,
+                "setup_s": {"stage_model_build_and_upload": round(t_b, 1)},
+            }
+            print(json.dumps(line), flush=True)
+        st.close()
         dist.barrier()
     finally:
         dist.destroy_process_group()

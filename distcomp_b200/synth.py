@@ -271,9 +271,29 @@ def _meta(b: G.GGUFBuilder, s: LlamaSpec):
     b.add_kv(f"{a}.vocab_size", G.T_U32, s.n_vocab)
 
 
+def stage_tensors(s: LlamaSpec, first: int, last: int, embed: bool, head: bool) -> set[str]:
+    """Names of the tensors a pipeline stage opens: layers first..last, plus
+    the embedding and/or the head (output norm and matrix)."""
+    names = set()
+    for name, _dims, _gt in tensor_list(s):
+        if name.startswith("blk."):
+            if first <= int(name.split(".")[1]) <= last:
+                names.add(name)
+        elif name == "token_embd.weight":
+            if embed or (head and s.tied):
+                names.add(name)
+        elif head:
+            names.add(name)
+    return names
+
+
 def build_model(s: LlamaSpec, seed: int = 0, device: str = "cpu", threads: int = 1,
-                quant_device: str | None = None) -> np.ndarray:
+                quant_device: str | None = None, only: set[str] | None = None) -> np.ndarray:
     """The whole GGUF image as a numpy uint8 array.
+
+    only: the image holds just these tensors (the same bytes as in the whole
+    model: every tensor's generator is seeded by its name), with the whole
+    model's metadata -- a pipeline rank builds its stage's part alone.
 
     device="cpu": numpy normals (the same bytes whatever ``threads`` and
     ``quant_device`` are: with threads > 1 the tensors are generated in
@@ -282,7 +302,7 @@ def build_model(s: LlamaSpec, seed: int = 0, device: str = "cpu", threads: int =
     CUDA generator (a different stream of normals)."""
     b = G.GGUFBuilder()
     _meta(b, s)
-    tl = tensor_list(s)
+    tl = [t for t in tensor_list(s) if only is None or t[0] in only]
     for name, dims, gt in tl:
         b.add_tensor(name, dims, gt)
     b.finalize()

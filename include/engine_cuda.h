@@ -178,6 +178,19 @@ int  ecu_generate(ecu_ctx *c, const int *prompt, int n_prompt, int n_gen, int *o
  * per-token step instead.  Scratch for the batch is allocated on first use
  * and grows with the longest prompt. */
 int  ecu_prefill(ecu_ctx *c, const int *tokens, int n, float *out);
+
+/* The batched prompt for one stage of a layer pipeline (src/shard.c:358-437
+ * splits the model into EMBED, LAYERS ranges and HEAD; the reference feeds
+ * the prompt through them token by token, src/shard.c:911-917).  x: device
+ * memory the caller owns, n rows of n_embd floats (the n prompt positions).
+ * EMBED: x = the embedding rows of tokens[0..n).  LAYERS: x goes through the
+ * stage's layers in place (ecu_prefill's kernels), the stage's KV cache
+ * gets positions pos..pos+n-1 and its position advances by n.  HEAD: the
+ * last row of x through the head, out = normed state + picked token as
+ * ecu_forward's (tokens may be NULL).  Every stage's rows agree bit for bit
+ * with a FULL context's ecu_prefill of the same prompt.  Synchronises the
+ * context's stream before returning. */
+int  ecu_prefill_rows(ecu_ctx *c, const int *tokens, int n, float *x, float *out);
 /* Decode steps on a FULL context continuing from the token in the state
  * buffer, on the context's stream, without synchronising; used to time the
  * device-side loop.  Returns 0 or -1. */

@@ -108,3 +108,44 @@ def test_nccl_pipeline_two_gpus(tmp_path):
     r = subprocess.run(["timeout", "-k", "30", "600"] + cmd, env=env, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
     assert (tmp_path / "ok").exists()
+
+
+def test_prefill_through_stages_matches_full_context(eng, oracle_port, model_buf):
+    """Two layers of the 70B shape (n_embd 8192, 64/8 heads, FFN 28672,
+    Q4_K) as two pipeline stages in one process -- EMBED + layer 0 | layer
+    1 + HEAD -- the prompt as one batch per stage (ecu_prefill_rows), then
+    greedy decode through the tick schedule: tokens and final logits bit for
+    bit a FULL context's (ecu_prefill + per-token decode), and the oracle's
+    greedy tokens."""
+    import oracle
+    key, over = "l70-1", {"n_layer": 2}
+    s = synth.spec(key, **over)
+    buf = model_buf(key, **over)
+    m = eng.GgufModel(buf)
+    n_prompt, n_gen, n_ctx = 8, 4, s.n_ctx
+    prompt = synth.prompt_tokens(n_prompt, s.n_vocab, seed=21)
+    full = eng.LlmCtx(m, eng.STAGE_FULL, n_ctx=n_ctx)
+    want = [full.prefill(prompt)]
+    out = np.zeros(s.n_embd + 1, dtype=np.float32)
+    while len(want) < n_gen:
+        assert full.forward(want[-1], out) == 0
+        want.append(int(out[s.n_embd]))
+    want_logits = full.logits()
+    full.close()
+    assert want == oracle.greedy(oracle_port, buf, prompt, n_gen)
+
+    stages = {r: P.GpuStage(m, r, 2, a, b, s.n_layer, 1, n_ctx, 0) for r, (a, b) in enumerate([(0, 0), (1, 1)])}
+    tok = P.prefill_local(stages, 0, prompt)
+    assert tok == want[0]
+    stages[1].record_tokens(n_prompt + n_gen)
+    S = P.Schedule(2, 1, n_gen - 1, n_prompt=n_prompt, first_step=n_prompt)
+    P.run_ticks(S, stages, P.LoopbackExchanger())
+    for st in stages.values():
+        st.sync()
+    hist = stages[1].history.cpu().numpy()[0]
+    got = [tok] + [int(t) for t in hist[n_prompt: n_prompt + n_gen - 1]]
+    assert got == want
+    got_logits = stages[1].chains[0][-1].logits()
+    assert np.array_equal(got_logits.view(np.uint32), want_logits.view(np.uint32))
+    for st in stages.values():
+        st.close()

@@ -1340,11 +1340,12 @@ static int mega_profile(ecu_ctx *c, int n_steps, ecu_kprof *out, int max_kinds)
             // CTA 0's SM cycles per ns over this launch
             const double f = (double)(clk[np] - clk[0]) / (double)std::max<unsigned long long>(1, ns[np] - ns[0]);
             if (dt[0] && dt[1] && dt[2]) {
-                // [3]: ns warp 0 waited for ring stages (GEMV) / its K/V copies (attention)
+                // attention phases: [3] is when KV head 0's merge ended
                 const bool att = c->ph_bytes[p] < 0;
-                const char *part[4] = {"prologue", "main", "epilogue", att ? "kv_wait" : "ring_wait"};
+                const char *part[4] = {"prologue", "main", "epilogue", att ? "merged" : "ring_wait"};
                 const double v[4] = {(double)(dt[0] - clk[p]) / f, (double)(dt[1] - dt[0]) / f,
-                                     (double)(dt[2] - dt[1]) / f, (double)dt[3]};
+                                     (double)(dt[2] - dt[1]) / f,
+                                     att ? (dt[3] > ns[p] ? (double)(dt[3] - ns[p]) : 0.0) : (double)dt[3]};
                 for (int q = 0; q < 4; q++) {
                     char nm[32];
                     snprintf(nm, sizeof nm, "%.20s:%s", c->ph_kind[p], part[q]);

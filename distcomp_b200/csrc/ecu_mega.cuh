@@ -101,7 +101,7 @@ struct MegaArgs {
     unsigned long long *phase_clk;  // optional, with phase_ns: CTA 0's SM clock at the same points
     unsigned long long *phase_detail; // optional, [n_ph][4]: CTA 0's SM clock after the prologue,
                                     // after the main loop, after the epilogue; [3]: GEMV: ns its
-                                    // warp 0 waited for ring stages, attention: ns thread 0 waited for its K/V copies
+                                    // warp 0 waited for ring stages, attention: when head 0 merged
     int              advance_pos;   // argmax epilogue advances st->pos (FULL)
     int              layers_advance;// LAYERS: st->pos++ once the last phase is done
     int              n_embd, n_head, n_kv, n_ctx, n_split;   // n_head, n_kv: this rank's heads
@@ -987,7 +987,7 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
                                int &att_sb1, int &merges, int p_idx)
 {
     // profiling (CTA 0): after the Q/K/V prologue, after the position loop,
-    // after the partials; [3] how long thread 0 waited for its K/V copies
+    // after the split ticket; and when KV head 0's merge ended
     unsigned long long *det = (a.phase_detail && blockIdx.x == 0 && threadIdx.x == 0)
                                   ? a.phase_detail + (size_t)p_idx * 4 : nullptr;
     // K/V rows sit unpadded in shared memory (one bulk copy per sub-chunk
@@ -999,7 +999,6 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
     __shared__ __align__(16) float q_s[NREP * HD];
     __shared__ __align__(16) float knew[HD], vnew[HD];
     const int nct = MEGA_NCW * 32, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    unsigned long long kv_waited = 0;
     const AttItem it = att_item(a, S.pos);
     const bool has = it.has;
     const int g = it.g, sp = it.sp, t0 = it.t0, t1 = it.t1, nround = it.nround;
@@ -1082,10 +1081,8 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
         const int s_ = r % nsl, cb = t0 + r * P;           // this round's first position
         const int cn = min(P, t1 - cb);
         const unsigned par = (unsigned)((s_ ? att_sb1 : att_sb0) + r / nsl) & 1u;
-        const unsigned long long tw = det ? globaltimer_ns() : 0ull;
         mbar_wait<true>(&S.abar[s_ * 2], par, a.status);
         if (cn > sub) mbar_wait<true>(&S.abar[s_ * 2 + 1], par, a.status);
-        if (det) kv_waited += globaltimer_ns() - tw;
         // ---- scores
         if (qp < P) {
             float d[NREP];
@@ -1252,8 +1249,9 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
         }
         named_bar(1, nct);
     }
-    // profiling: how long CTA 0 waited for its K/V copies
-    if (det) det[3] = kv_waited;
+    // profiling: when KV head 0's merge was done (the CTA of split 0)
+    if (a.phase_detail && has && g == 0 && sp == 0 && tid == 0)
+        a.phase_detail[(size_t)p_idx * 4 + 3] = globaltimer_ns();
 }
 
 // L2 prefetch of the K and V rows this CTA's attention item will read (the

@@ -16,12 +16,18 @@
 #include "ecu_prefill.cuh"
 
 #include <atomic>
+#include <cerrno>
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <string>
+#include <thread>
 #include <vector>
 
 static std::atomic<uint64_t> g_launches{0};
@@ -437,6 +443,7 @@ struct ecu_ctx {
     bool        pdl = true, use_graph = true;
     std::vector<void *> allocs;           // this context's own buffers
     std::shared_ptr<SharedAllocs> shared; // read-only tensors, shared with forks
+    struct Uploader *up = nullptr;        // while opening: pinned double-buffered weight staging
     bool        to_shared = false;        // dalloc target while uploading weights
     size_t      bytes = 0;
 
@@ -550,9 +557,77 @@ static bool zero_rule(int t, int n_in)
     return !dq_supported(t);
 }
 
+// Weight staging while a context opens: the host copies chunk i of a
+// tensor's rows into pinned buffer i % 2 (several threads), one async copy
+// moves it to device buffer i % 2 and the repack kernel lays it out, while
+// the host already fills the other pinned buffer; an event per buffer says
+// when it may be refilled.  The source is the caller's GGUF image or a file
+// mapping (ecu_model_open_file: only the stage's tensors are paged in).
+struct Uploader {
+    uint8_t    *pin[2] = {nullptr, nullptr}, *dev[2] = {nullptr, nullptr};
+    cudaEvent_t ev[2] = {nullptr, nullptr};
+    size_t      cap = 0;
+    int         next = 0;
+};
+
+static void uploader_free(Uploader *u)
+{
+    if (!u) return;
+    for (int b = 0; b < 2; b++) {
+        if (u->ev[b]) cudaEventSynchronize(u->ev[b]), cudaEventDestroy(u->ev[b]);
+        if (u->pin[b]) cudaFreeHost(u->pin[b]);
+        if (u->dev[b]) cudaFree(u->dev[b]);
+    }
+    delete u;
+}
+
+static Uploader *uploader_new(size_t cap)
+{
+    Uploader *u = new Uploader();
+    u->cap = cap;
+    for (int b = 0; b < 2; b++)
+        if (cudaMallocHost(&u->pin[b], cap) != cudaSuccess || cudaMalloc(&u->dev[b], cap + 256) != cudaSuccess ||
+            cudaEventCreateWithFlags(&u->ev[b], cudaEventDisableTiming) != cudaSuccess) {
+            cudaGetLastError();
+            uploader_free(u);
+            return nullptr;
+        }
+    return u;
+}
+
+// rows of `len` bytes, `stride` apart, packed into dst -- split over threads
+static void host_pack_rows(uint8_t *dst, const uint8_t *src, size_t len, size_t stride, size_t rows)
+{
+    const size_t total = len * rows;
+    const int    nt = total >= ((size_t)32 << 20) ? 8 : total >= ((size_t)4 << 20) ? 4 : 1;
+    auto part = [&](size_t r0, size_t r1) {
+        if (len == stride) memcpy(dst + r0 * len, src + r0 * stride, (r1 - r0) * len);
+        else
+            for (size_t r = r0; r < r1; r++) memcpy(dst + r * len, src + r * stride, len);
+    };
+    if (nt == 1) { part(0, rows); return; }
+    std::vector<std::thread> th;
+    for (int k = 0; k < nt; k++) th.emplace_back(part, rows * k / nt, rows * (k + 1) / nt);
+    for (auto &t : th) t.join();
+}
+
+static void launch_repack(const ecu_ctx *c, const DevMat &m, const uint8_t *stage, int si, int rows, uint8_t *dst,
+                          int row0, int rstride, size_t seg_src)
+{
+    const int grid = 4 * c->sms, blk = 256;
+    if (m.layout == LAY_SPLIT4)
+        k_repack_q4_0<<<grid, blk, 0, c->stream>>>(stage, si / 32, rows, dst, m.row_bytes, row0, rstride);
+    else if (m.layout == LAY_SPLIT8)
+        k_repack_q8_0<<<grid, blk, 0, c->stream>>>(stage, si / 32, rows, dst, m.row_bytes, row0, rstride);
+    else if (m.layout == LAY_SPLITK4)
+        k_repack_q4_k<<<grid, blk, 0, c->stream>>>(stage, si / 256, rows, dst, m.row_bytes, row0, rstride);
+    else
+        k_copy_rows<<<grid, blk, 0, c->stream>>>(stage, seg_src, rows, dst, m.row_bytes, row0, rstride);
+}
+
 // Upload rows [src_row0, src_row0 + rows) of tensor `src` (n_in inputs
 // each) into device matrix `m` at rows row0, row0+rstride, ...  `stage` is a
-// device staging buffer.
+// device staging buffer (used when no Uploader is active).
 static int upload_rows(ecu_ctx *c, const EcuTensor *src, int n_in, int rows, DevMat &m, int row0,
                        int rstride, uint8_t *stage, size_t src_row0 = 0)
 {
@@ -561,6 +636,26 @@ static int upload_rows(ecu_ctx *c, const EcuTensor *src, int n_in, int rows, Dev
     const int    si = n_in / m.nseg;                          // inputs of a segment
     const size_t seg_src = (size_t)ecu_type_nbytes(src->type, (size_t)si);
     const int    grid = 4 * c->sms, blk = 256;
+    if (Uploader *u = c->up) {
+        const size_t per = std::max<size_t>(1, u->cap / std::max<size_t>(1, seg_src));
+        if (seg_src > u->cap) { ecu_set_error(nullptr, 0, "a weight row exceeds the upload chunk"); return -1; }
+        for (int sg = 0; sg < m.nseg; sg++) {
+            const uint8_t *from = src->data + src_row0 * src_row + (size_t)sg * seg_src;
+            uint8_t       *dst = const_cast<uint8_t *>(m.data) + (size_t)sg * m.seg_bytes;
+            for (size_t r = 0; r < (size_t)rows; r += per) {
+                const size_t nr = std::min(per, (size_t)rows - r);
+                const int    b = u->next;
+                u->next ^= 1;
+                CK(cudaEventSynchronize(u->ev[b]));        // the chunk before last is done with buffer b
+                host_pack_rows(u->pin[b], from + r * src_row, seg_src, src_row, nr);
+                CK(cudaMemcpyAsync(u->dev[b], u->pin[b], nr * seg_src, cudaMemcpyHostToDevice, c->stream));
+                launch_repack(c, m, u->dev[b], si, (int)nr, dst, row0 + (int)r * rstride, rstride, seg_src);
+                CK(cudaGetLastError());
+                CK(cudaEventRecord(u->ev[b], c->stream));
+            }
+        }
+        return 0;
+    }
     for (int sg = 0; sg < m.nseg; sg++) {
         // segment sg's part of every source row, packed rows of seg_src bytes
         const uint8_t *from = src->data + src_row0 * src_row + (size_t)sg * seg_src;
@@ -570,14 +665,9 @@ static int upload_rows(ecu_ctx *c, const EcuTensor *src, int n_in, int rows, Dev
             CK(cudaMemcpy2DAsync(stage, seg_src, from, src_row, seg_src, (size_t)rows, cudaMemcpyHostToDevice,
                                  c->stream));
         uint8_t *dst = const_cast<uint8_t *>(m.data) + (size_t)sg * m.seg_bytes;
-        if (m.layout == LAY_SPLIT4)
-            k_repack_q4_0<<<grid, blk, 0, c->stream>>>(stage, si / 32, rows, dst, m.row_bytes, row0, rstride);
-        else if (m.layout == LAY_SPLIT8)
-            k_repack_q8_0<<<grid, blk, 0, c->stream>>>(stage, si / 32, rows, dst, m.row_bytes, row0, rstride);
-        else if (m.layout == LAY_SPLITK4)
-            k_repack_q4_k<<<grid, blk, 0, c->stream>>>(stage, si / 256, rows, dst, m.row_bytes, row0, rstride);
-        else
-            k_copy_rows<<<grid, blk, 0, c->stream>>>(stage, seg_src, rows, dst, m.row_bytes, row0, rstride);
+        launch_repack(c, m, stage, si, rows, dst, row0, rstride, seg_src);
+        (void)grid;
+        (void)blk;
         CK(cudaGetLastError());
         CK(cudaStreamSynchronize(c->stream));   // the staging buffer is reused
     }
@@ -627,6 +717,7 @@ static void ctx_free(ecu_ctx *c)
 {
     if (!c) return;
     if (c->device >= 0) cudaSetDevice(c->device);
+    uploader_free(c->up);
     if (c->graph) cudaGraphExecDestroy(c->graph);
     for (void *p : c->tp_peers)
         if (p) cudaIpcCloseMemHandle(p);
@@ -999,11 +1090,13 @@ static int mega_setup(ecu_ctx *c)
         att_nsl = 2;
         att_sub = sub2;
     }
-    // the first attention rounds' K/V copies are issued by the Q/K/V phase
-    // before it (ECU_MEGA_KV_EARLY=0: by the attention phase itself), into
-    // buffers above the widest Q/K/V digit planes
+    // ECU_MEGA_KV_EARLY=1: the first attention rounds' K/V copies are issued
+    // by the Q/K/V phase before it, into buffers above the widest Q/K/V digit
+    // planes (measured on the 8B shape: the attention phase gains less than
+    // the Q/K/V phase loses to the extra copies in its stream, so by default
+    // the attention phase issues them itself)
     const char *ke = getenv("ECU_MEGA_KV_EARLY");
-    const bool  kv_early = !(ke && ke[0] == '0');
+    const bool  kv_early = ke && ke[0] == '1';
     size_t qkv_dig = 0;
     for (auto &ly : c->layers) qkv_dig = std::max(qkv_dig, (size_t)ly.qkv[0].n_in / 32 * 28 * sizeof(int));
     const size_t kv_off = kv_early ? ((qkv_dig + 127) & ~(size_t)127) : 0;
@@ -1388,6 +1481,33 @@ int ecu_model_open(ecu_model **out, const void *file, size_t size, char *err, si
     return 0;
 }
 
+int ecu_model_open_file(ecu_model **out, const char *path, char *err, size_t errlen)
+{
+    if (!out || !path) { ecu_set_error(err, errlen, "null argument"); return -1; }
+    *out = nullptr;
+    const int fd = open(path, O_RDONLY);
+    if (fd < 0) { ecu_set_error(err, errlen, "cannot open %s: %s", path, strerror(errno)); return -1; }
+    struct stat sb;
+    if (fstat(fd, &sb) != 0 || sb.st_size <= 0) {
+        ecu_set_error(err, errlen, "cannot size %s", path);
+        close(fd);
+        return -1;
+    }
+    const size_t len = (size_t)sb.st_size;
+    void *p = mmap(nullptr, len, PROT_READ, MAP_PRIVATE, fd, 0);
+    close(fd);
+    if (p == MAP_FAILED) { ecu_set_error(err, errlen, "cannot map %s: %s", path, strerror(errno)); return -1; }
+    ecu_model *m = new ecu_model();
+    m->map = p;
+    m->map_len = len;
+    if (ecu_model_parse(m, p, len, err, errlen) != 0) {
+        delete m;
+        return -1;
+    }
+    *out = m;
+    return 0;
+}
+
 ecu_model *ecu_model_new(void) { return new ecu_model(); }
 
 static int set_kv(ecu_model *m, const char *key, unsigned type, double num, const char *str)
@@ -1701,11 +1821,20 @@ static int ctx_open_impl(ecu_ctx **out, const ecu_model *m, int stage, int first
         return -1;
     }
 
-    // staging buffer for raw uploads: the largest tensor this stage reads
+    // weight matrices go through pinned double-buffered chunks (ECU_UPLOAD_MB,
+    // default 64 MB per buffer); without them (no pinned memory), one
+    // pageable copy per tensor into a staging buffer as large as the largest
+    size_t up_mb = 64;
+    if (const char *ue = getenv("ECU_UPLOAD_MB")) up_mb = (size_t)std::max(1, std::min(1024, atoi(ue)));
+    c->up = uploader_new(up_mb << 20);
     size_t stage_bytes = 1 << 20;
     auto need = [&](const EcuTensor *t) { if (t && t->nbytes > stage_bytes) stage_bytes = t->nbytes; };
-    need(st.emb); need(st.out); need(st.out_norm);
-    for (auto &l : st.layers) { need(l.an); need(l.q); need(l.k); need(l.v); need(l.o); need(l.fn); need(l.g); need(l.u); need(l.d); need(l.bq); need(l.bk); need(l.bv); }
+    need(st.out_norm);
+    for (auto &l : st.layers) { need(l.an); need(l.fn); need(l.bq); need(l.bk); need(l.bv); }
+    if (!c->up) {
+        need(st.emb); need(st.out);
+        for (auto &l : st.layers) { need(l.q); need(l.k); need(l.v); need(l.o); need(l.g); need(l.u); need(l.d); }
+    }
     uint8_t *stage_buf = nullptr;
     if (cudaMalloc(&stage_buf, stage_bytes + 256) != cudaSuccess ||
         cudaMemset(stage_buf, 0, stage_bytes + 256) != cudaSuccess) {
@@ -1855,6 +1984,15 @@ static int ctx_open_impl(ecu_ctx **out, const ecu_model *m, int stage, int first
             if (ly.bv) ly.bv += (size_t)tp.rank * kvd_l;
             if (!ly.attn_norm || !ly.ffn_norm) return fail_oom("norm weights");
         }
+    }
+    // every chunk uploaded: the pinned staging goes back
+    if (c->up) {
+        if (cudaStreamSynchronize(c->stream) != cudaSuccess) {
+            ecu_set_error(err, errlen, "upload failed: %s", cudaGetErrorString(cudaGetLastError()));
+            return -1;
+        }
+        uploader_free(c->up);
+        c->up = nullptr;
     }
     if (mega_setup(c.get()) != 0) return fail_oom("persistent step buffers");
     if (!whole && !c->mega) {

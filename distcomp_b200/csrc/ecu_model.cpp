@@ -10,6 +10,11 @@
 // matters for files it cannot read correctly anyway.
 #include "ecu_model.h"
 
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -189,6 +194,11 @@ int ecu_model_parse(ecu_model *m, const void *file, size_t size, char *err, size
     m->alignment = align;
     m->index();
     return 0;
+}
+
+ecu_model::~ecu_model()
+{
+    if (map) munmap(map, map_len);
 }
 
 void ecu_model::index()

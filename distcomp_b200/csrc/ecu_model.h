@@ -34,6 +34,9 @@ struct ecu_model {
     std::vector<EcuTensor> t;
     unsigned               version = 3, alignment = 32;
     std::unordered_map<std::string, size_t> by_name;
+    void                  *map = nullptr;   // ecu_model_open_file: the read-only file mapping the tensors borrow
+    size_t                 map_len = 0;
+    ~ecu_model();
 
     void             index();
     const EcuTensor *find(const std::string &name) const;

@@ -52,6 +52,7 @@ class EcuKprof(C.Structure):
 # (name, restype, argtypes) of every symbol include/engine_cuda.h declares
 SIGNATURES = [
     ("ecu_model_open", C.c_int, [C.POINTER(C.c_void_p), C.c_void_p, C.c_size_t, C.c_char_p, C.c_size_t]),
+    ("ecu_model_open_file", C.c_int, [C.POINTER(C.c_void_p), C.c_char_p, C.c_char_p, C.c_size_t]),
     ("ecu_model_new", C.c_void_p, []),
     ("ecu_model_set_str", C.c_int, [C.c_void_p, C.c_char_p, C.c_char_p]),
     ("ecu_model_set_u32", C.c_int, [C.c_void_p, C.c_char_p, C.c_ulong]),
@@ -141,11 +142,17 @@ class GgufModel:
     """Host view of a GGUF image (the buffer must outlive every LlmCtx opened
     from it until the open call returns; weights are copied to the device)."""
 
-    def __init__(self, buf):
-        self._buf = np.frombuffer(buf, dtype=np.uint8) if not isinstance(buf, np.ndarray) else buf
+    def __init__(self, buf=None, path: str | None = None):
+        """buf: a GGUF image in host memory; or path: a GGUF file, mapped
+        (ecu_model_open_file: a stage's context pages in its tensors only)."""
         self.h = C.c_void_p()
         err = C.create_string_buffer(512)
-        rc = lib().ecu_model_open(C.byref(self.h), _ptr(self._buf), self._buf.nbytes, err, 512)
+        if path is not None:
+            self._buf = None
+            rc = lib().ecu_model_open_file(C.byref(self.h), str(path).encode(), err, 512)
+        else:
+            self._buf = np.frombuffer(buf, dtype=np.uint8) if not isinstance(buf, np.ndarray) else buf
+            rc = lib().ecu_model_open(C.byref(self.h), _ptr(self._buf), self._buf.nbytes, err, 512)
         if rc != 0:
             raise EngineError(err.value.decode(errors="replace"))
 

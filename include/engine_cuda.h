@@ -58,6 +58,12 @@ int  ecu_model_open(ecu_model **out, const void *file, size_t size, char *err, s
 /* Assemble a model from tensor views and metadata instead of a file image,
  * as dcd's shard role does when it builds a gguf_file from received tensors
  * (src/daemon.c:963-1019). */
+/* The same from a GGUF file on disk: mapped read-only, so that a context
+ * opened from it reads (pages in) only its stage's tensors, and the model
+ * owns the mapping until ecu_model_close.  Replaces the reference's whole-
+ * file fread (src/shard.c:84-104, llm_open_file) for stage nodes. */
+int  ecu_model_open_file(ecu_model **out, const char *path, char *err, size_t errlen);
+
 ecu_model *ecu_model_new(void);
 int  ecu_model_set_str(ecu_model *m, const char *key, const char *val);
 int  ecu_model_set_u32(ecu_model *m, const char *key, unsigned long val);

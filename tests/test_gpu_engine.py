@@ -200,3 +200,32 @@ def test_repacked_weights_bit_exact(eng, oracle_port, model_buf):
             rc, want = oracle_port.dequant(gt, np.frombuffer(tab[name][2], np.uint8), total, 0, total)
             assert rc == 0
             assert bits_equal(got, want), name
+
+
+def test_context_from_mapped_file(eng, oracle_port, model_buf, tmp_path, monkeypatch):
+    """A model opened from a GGUF file (ecu_model_open_file: mapped, a
+    stage's context pages in its tensors only), its weights uploaded in small
+    pinned chunks (ECU_UPLOAD_MB=1: every matrix in several chunks): the
+    oracle's greedy tokens, and a LAYERS stage's state within 1e-3."""
+    import oracle
+    key = "mini-q4"
+    s = synth.spec(key)
+    buf = model_buf(key)
+    path = tmp_path / "m.gguf"
+    path.write_bytes(buf.tobytes())
+    monkeypatch.setenv("ECU_UPLOAD_MB", "1")
+    m = eng.GgufModel(path=str(path))
+    prompt = synth.prompt_tokens(5, s.n_vocab, seed=8)
+    want = oracle.greedy(oracle_port, buf, prompt, 8)
+    c = eng.LlmCtx(m, eng.STAGE_FULL, n_ctx=32)
+    assert c.generate(prompt, 8) == want
+    lay = eng.LlmCtx(m, eng.STAGE_LAYERS, 1, 1, n_ctx=32)
+    o = oracle_port.model(buf).ctx(1, 1, 1)
+    x = np.random.default_rng(2).standard_normal(s.n_embd).astype(np.float32)
+    a, b = x.copy(), x.copy()
+    assert lay.forward(0, a) == 0 and o.forward(0, b) == 0
+    ok, err = vec_close(a, b)
+    assert ok, err
+    c.close()
+    lay.close()
+    m.close()

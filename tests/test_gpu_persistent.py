@@ -141,3 +141,21 @@ def test_attention_slots_and_splits_vs_oracle(eng, oracle_port, model_buf, key, 
     c = open_ctx(eng, eng.GgufModel(buf), eng.STAGE_FULL)
     assert c.path() == "persistent"
     assert c.generate(prompt, n_gen) == want
+
+
+@pytest.mark.parametrize("key", ["mini-q4", "mini-q8"])
+def test_early_kv_copies_vs_oracle(eng, oracle_port, model_buf, key, monkeypatch):
+    """ECU_MEGA_KV_EARLY=1: the Q/K/V phase issues the attention's first K/V
+    copies into buffers above its digit planes; the oracle's greedy tokens
+    over the whole context (several rounds per split with ECU_MEGA_SPLIT=2)."""
+    import oracle
+    s = synth.spec(key)
+    buf = model_buf(key)
+    prompt = synth.prompt_tokens(5, s.n_vocab, seed=33)
+    n_gen = s.n_ctx - len(prompt) + 1
+    want = oracle.greedy(oracle_port, buf, prompt, n_gen)
+    monkeypatch.setenv("ECU_MEGA_KV_EARLY", "1")
+    monkeypatch.setenv("ECU_MEGA_SPLIT", "2")
+    c = open_ctx(eng, eng.GgufModel(buf), eng.STAGE_FULL)
+    assert c.path() == "persistent"
+    assert c.generate(prompt, n_gen) == want

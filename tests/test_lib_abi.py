@@ -149,3 +149,22 @@ def test_ctx_bytes_q4k_segments_host_only(model_buf):
     hd = s.n_embd // s.n_head
     kv = 2 * s.n_layer * n_ctx * s.n_head_kv * hd * 4
     assert w + kv <= got <= w + kv + (8 << 20)
+
+
+def test_model_open_file_maps_the_same_tensors(model_buf, tmp_path):
+    """ecu_model_open_file maps a GGUF file: the same tensor table as the
+    in-memory open, every tensor's bytes the file's."""
+    buf = model_buf("mini-q4")
+    path = tmp_path / "m.gguf"
+    path.write_bytes(buf.tobytes())
+    a = engine.GgufModel(buf)
+    b = engine.GgufModel(path=str(path))
+    assert a.n_tensors() == b.n_tensors()
+    for name, dims, gt in synth.tensor_list(synth.spec("mini-q4")):
+        ta, da, _, na = a.tensor(name)
+        tb, db, pb, nb = b.tensor(name)
+        assert (ta, da, na) == (tb, db, nb)
+        assert bytes(G.read_tensor_table(buf)[name][2]) == C.string_at(pb, nb), name
+    b.close()
+    with pytest.raises(engine.EngineError, match="cannot open"):
+        engine.GgufModel(path=str(tmp_path / "missing.gguf"))

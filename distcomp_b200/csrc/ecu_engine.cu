@@ -2450,6 +2450,153 @@ int ecu_matvec(unsigned type, const void *w_raw, int n_in, int n_out, const floa
     return 0;
 }
 
+int ecu_matvec_stream_bench(unsigned type, const void *w_raw, int n_in, int n_out, const float *x, float *y,
+                            int device, int copies, int rounds, double *ms_per_matvec)
+{
+    if (!w_raw || !x || !y || !ms_per_matvec || n_in <= 0 || n_out <= 0 || copies < 1 || rounds < 1) {
+        ecu_set_error(nullptr, 0, "ecu_matvec_stream_bench: bad arguments");
+        return -1;
+    }
+    CK(cudaSetDevice(device));
+    ecu_ctx tmp;
+    tmp.device = device;
+    tmp.sms = num_sms(device);
+    CK(cudaStreamCreateWithFlags(&tmp.stream, cudaStreamNonBlocking));
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    struct Cleanup {
+        ecu_ctx *c;
+        cudaEvent_t *e0, *e1;
+        ~Cleanup()
+        {
+            if (*e0) cudaEventDestroy(*e0);
+            if (*e1) cudaEventDestroy(*e1);
+            for (void *q : c->allocs) cudaFree(q);
+            c->allocs.clear();
+            cudaStreamDestroy(c->stream);
+            c->stream = nullptr;
+        }
+    } cleanup{&tmp, &e0, &e1};
+    MegaFn fn = mega_lookup(128, 4, false);
+    EcuTensor t;
+    t.type = type;
+    t.n_dims = 2;
+    t.dims[0] = (uint64_t)n_in;
+    t.dims[1] = (uint64_t)n_out;
+    t.data = (const uint8_t *)w_raw;
+    t.nbytes = ecu_type_nbytes(type, (size_t)n_in * n_out);
+    uint8_t *stage = tmp.dalloc<uint8_t>(t.nbytes + 16);
+    if (!stage || !fn) { ecu_set_error(nullptr, 0, "out of memory"); return -1; }
+    // the phase list: one GEMV (plain input x, tagged output) per copy
+    const int grid = tmp.sms;
+    const unsigned stage_bytes = (MEGA_RING_BYTES / 2) & ~127u;
+    std::vector<MegaPhase> ph;
+    std::vector<uint4> tab;
+    int red = MEGA_NCW * (128 + 4);
+    const size_t w_y = ((size_t)n_out + 7) & ~(size_t)3;
+    float *dx = tmp.dalloc<float>((size_t)n_in + 4);
+    unsigned long long *yll = tmp.dalloc<unsigned long long>(w_y + 64);
+    unsigned *ctr = tmp.dalloc<unsigned>(16);
+    StepState *st = tmp.dalloc<StepState>(1);
+    if (!dx || !yll || !ctr || !st) { ecu_set_error(nullptr, 0, "out of memory"); return -1; }
+    for (int k = 0; k < copies; k++) {
+        DevMat m = make_mat(&tmp, (int)type, n_in, n_out, true, false);
+        if (!m.data) { ecu_set_error(nullptr, 0, "out of memory for copy %d", k); return -1; }
+        if (!mega_mat_ok(m)) {
+            ecu_set_error(nullptr, 0, "ecu_matvec_stream_bench: the matrix has no fast layout (Q4_0/Q8_0/Q4_K, "
+                                      "n_in a multiple of 1024)");
+            return -1;
+        }
+        if (upload_rows(&tmp, &t, n_in, n_out, m, 0, 1, stage) != 0) return -1;
+        if (m.row_bytes > stage_bytes) { ecu_set_error(nullptr, 0, "a row does not fit a ring stage"); return -1; }
+        MegaPhase q = mega_gemv_phase(m, grid, stage_bytes, 0, EPI_STORE, dx, nullptr, nullptr, nullptr);
+        q.y_ll = yll;
+        q.red4 = (q.fmt == 4 && q.rpc * (q.nkg * 4 + 1) <= MEGA_RED4_MAX) ? 1 : 0;
+        red = std::max(red, q.red4 ? q.rpc * (q.nkg * 4 + 1) : q.rpc * q.nkg);
+        ph.push_back(q);
+        tab.push_back(mega_tab_entry(q.w, q.row_bytes, q.sr, q.n_out, q.rpc));
+    }
+    const size_t un = (size_t)n_in / 32 * 28 * sizeof(int);
+    const size_t smem = mega_smem_total(red, 2 * stage_bytes, (unsigned)un, (int)ph.size());
+    cudaFuncAttributes fa;
+    int optin = 0;
+    CK(cudaFuncGetAttributes(&fa, fn));
+    CK(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
+    if (smem + fa.sharedSizeBytes > (size_t)optin) {
+        ecu_set_error(nullptr, 0, "ecu_matvec_stream_bench: shared memory plan too large");
+        return -1;
+    }
+    CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - (int)fa.sharedSizeBytes));
+    MegaPhase *d_ph = tmp.dalloc<MegaPhase>(ph.size());
+    uint4 *d_tab = tmp.dalloc<uint4>(tab.size());
+    if (!d_ph || !d_tab) { ecu_set_error(nullptr, 0, "out of memory"); return -1; }
+    CK(cudaMemcpy(d_ph, ph.data(), ph.size() * sizeof(MegaPhase), cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(d_tab, tab.data(), tab.size() * sizeof(uint4), cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(dx, x, sizeof(float) * (size_t)n_in, cudaMemcpyHostToDevice));
+    CK(cudaMemset(yll, 0, sizeof(unsigned long long) * (w_y + 64)));
+    CK(cudaMemset(ctr, 0, 16 * sizeof(unsigned)));
+    CK(cudaMemset(st, 0, sizeof(StepState)));
+    MegaArgs a = {};
+    a.ph = d_ph;
+    a.n_ph = (int)ph.size();
+    a.tab = d_tab;
+    a.bar = ctr;
+    a.ticket = ctr + 2;
+    a.att_ticket = ctr + 4;
+    a.st = st;
+    a.status = &st->status;
+    a.x_ll = a.qkv_ll = a.att_ll = a.h_ll = yll;
+    a.ll_block = yll;
+    a.peer[0] = yll;
+    a.n_embd = n_in;
+    a.n_head = 1;
+    a.n_kv = 1;
+    a.n_ctx = 1;
+    a.n_split = 1;
+    a.tp_world = 1;
+    a.red_floats = red;
+    a.union_bytes = (unsigned)un;
+    a.nst = 2;
+    a.stage_bytes = stage_bytes;
+    a.att_sub = MEGA_ATT_SUB;
+    a.att_nsl = 1;
+    a.stall_phase = -1;
+    a.eps = 1e-5f;
+    a.kscale = 1.0f;
+    CK(cudaDeviceSynchronize());
+    cudaLaunchConfig_t  cfg = {};
+    cudaLaunchAttribute at;
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(MEGA_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = tmp.stream;
+    at.id = cudaLaunchAttributeCooperative;
+    at.val.cooperative = 1;
+    cfg.attrs = &at;
+    cfg.numAttrs = 1;
+    for (int r = 0; r < 2; r++) CK(cudaLaunchKernelEx(&cfg, fn, a));     // warm-up
+    CK(cudaStreamSynchronize(tmp.stream));
+    CK(cudaEventCreate(&e0));
+    CK(cudaEventCreate(&e1));
+    CK(cudaEventRecord(e0, tmp.stream));
+    for (int r = 0; r < rounds; r++) CK(cudaLaunchKernelEx(&cfg, fn, a));
+    CK(cudaEventRecord(e1, tmp.stream));
+    CK(cudaStreamSynchronize(tmp.stream));
+    g_launches += (uint64_t)(rounds + 2);
+    float ms = 0.0f;
+    CK(cudaEventElapsedTime(&ms, e0, e1));
+    *ms_per_matvec = (double)ms / ((double)rounds * copies);
+    StepState hs;
+    CK(cudaMemcpy(&hs, st, sizeof hs, cudaMemcpyDeviceToHost));
+    if (hs.status) { ecu_set_error(nullptr, 0, "a bounded wait expired in the streamed GEMV"); return -1; }
+    std::vector<unsigned long long> w((size_t)n_out);
+    CK(cudaMemcpy(w.data(), yll, sizeof(unsigned long long) * (size_t)n_out, cudaMemcpyDeviceToHost));
+    for (int i = 0; i < n_out; i++) {
+        const unsigned u = (unsigned)(w[(size_t)i] & 0xFFFFFFFFull);
+        memcpy(&y[i], &u, sizeof u);
+    }
+    return 0;
+}
+
 int ecu_set_wait_ns(int device, unsigned long long ns)
 {
     if (ns == 0) {

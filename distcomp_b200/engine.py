@@ -101,6 +101,8 @@ SIGNATURES = [
     ("ecu_inject_wait_timeout", C.c_int, [C.c_void_p]),
     ("ecu_matvec_bench", C.c_int, [C.c_uint, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_int,
                                    C.c_int, C.c_int, C.POINTER(C.c_double)]),
+    ("ecu_matvec_stream_bench", C.c_int, [C.c_uint, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
+                                          C.c_int, C.c_int, C.c_int, C.POINTER(C.c_double)]),
     ("ecu_profile_steps", C.c_int, [C.c_void_p, C.c_int, C.POINTER(EcuKprof), C.c_int]),
     ("ecu_last_error", C.c_char_p, []),
     ("ecu_kernel_launches", C.c_uint64, []),
@@ -392,3 +394,18 @@ def set_wait_ns(ns: int, device: int = 0) -> None:
     """The limit after which every bounded wait in the kernels gives up."""
     if lib().ecu_set_wait_ns(device, int(ns)) != 0:
         raise EngineError(last_error())
+
+
+def matvec_stream_bench(gtype: int, raw: np.ndarray, n_in: int, n_out: int, x: np.ndarray, copies: int,
+                        rounds: int, device: int = 0):
+    """Device time per matvec (ms) with the copies streamed through the
+    persistent step's GEMV phases, and the last phase's y
+    (ecu_matvec_stream_bench)."""
+    raw = np.ascontiguousarray(raw, dtype=np.uint8)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty(n_out, dtype=np.float32)
+    ms = C.c_double(0.0)
+    if lib().ecu_matvec_stream_bench(gtype, _ptr(raw), n_in, n_out, _ptr(x), _ptr(y), device, copies, rounds,
+                                     C.byref(ms)) != 0:
+        raise EngineError(last_error())
+    return ms.value, y

@@ -274,6 +274,16 @@ int  ecu_inject_wait_timeout(ecu_ctx *c);
 int  ecu_matvec_bench(unsigned ggml_type, const void *w_raw, int n_in, int n_out, const float *x,
                       float *y, int device, int copies, int rounds, double *ms_per_launch);
 
+/* The same matrices streamed through the persistent step's GEMV phases: one
+ * cooperative launch runs one phase per copy (y = W_c x, plain x, each CTA's
+ * rows through its shared-memory ring, the next copy's rows already in
+ * flight while a phase ends), `rounds` launches timed with CUDA events;
+ * *ms_per_matvec = time / (rounds * copies).  The decode step consumes its
+ * weight matrices this way.  Q4_0 / Q8_0 / Q4_K with n_in a multiple of
+ * 1024 (the fast layouts); -1 otherwise. */
+int  ecu_matvec_stream_bench(unsigned ggml_type, const void *w_raw, int n_in, int n_out, const float *x,
+                             float *y, int device, int copies, int rounds, double *ms_per_matvec);
+
 /* Per-kernel-kind totals of a profiling replay. */
 typedef struct {
     char   kind[32];          /* "gemv_gate_up", "attention", ...               */

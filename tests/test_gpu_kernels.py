@@ -134,6 +134,25 @@ def test_matvec_microbench_shapes(eng, oracle_port, t, n_out, n_in):
     assert gemv_tol_ok(oracle_port.matvec(t, raw, n_in, n_out, x), ref, wn, x)[0]
 
 
+@pytest.mark.parametrize("t", [G.Q4_0, G.Q8_0, G.Q4_K])
+def test_matvec_streamed_phases(eng, oracle_port, t):
+    """The streamed microbenchmark (copies as GEMV phases of one persistent
+    launch): the last phase's y against the double-precision oracle, and a
+    matrix without a fast layout refused with a message."""
+    rng = np.random.default_rng(40 + t)
+    n_in, n_out = 4096, 1536
+    raw = microbench_weights(rng, t, n_in, n_out) if t != G.Q4_K else random_weights(rng, t, n_in, n_out)
+    x = rng.standard_normal(n_in).astype(np.float32)
+    ms, y = eng.matvec_stream_bench(t, raw, n_in, n_out, x, copies=3, rounds=2)
+    assert ms > 0
+    ref = oracle_port.matvec_f64(t, raw, n_in, n_out, x)
+    ok, worst = gemv_tol_ok(y, ref, row_norms(oracle_port, t, raw, n_in, n_out), x)
+    assert ok, f"worst rel {worst:.3e}"
+    raw2 = microbench_weights(rng, G.Q4_0, 512, 64)
+    with pytest.raises(eng.EngineError, match="fast layout"):
+        eng.matvec_stream_bench(G.Q4_0, raw2, 512, 64, x[:512], copies=2, rounds=1)
+
+
 def test_matvec_extreme_inputs(eng, oracle_port):
     """Large/small dynamic range in x (digit decomposition edge cases) and
     all-zero blocks."""

@@ -57,13 +57,17 @@ def split_stages(n_layer: int, n_nodes: int, cost=None, cap=None) -> list[tuple[
 
 
 def split_by_bytes(layer_bytes: list[int], n_stages: int, head_bytes: int = 0,
-                   embed_bytes: int = 0) -> list[tuple[int, int]]:
+                   embed_bytes: int = 0, head_alone: bool = False) -> list[tuple[int, int]]:
     """Contiguous layer ranges for n_stages GPUs that minimise the largest
     per-token byte stream of a stage, when the first stage also reads the
     embedding row and the last the output head.  Every stage gets at least
-    one layer.  (The reference's rule balances layer counts; with the head
-    folded into the last GPU, balancing bytes keeps that GPU from setting
-    the pipeline's pace.)"""
+    one layer, except that with head_alone the last stage may hold the head
+    only (an empty range (n, n - 1)): where the head weighs about as much as
+    a stage's share of the layers (the 8B shape on 8 GPUs: 558 MB against
+    5 x 123 MB), one more layer on the head's GPU would set the pace.  (The
+    reference's rule balances layer counts; with the head folded into the
+    last GPU, balancing bytes keeps that GPU from setting the pipeline's
+    pace.)"""
     n = len(layer_bytes)
     if not 1 <= n_stages <= n:
         raise ValueError(f"{n_stages} stages for {n} layers")
@@ -79,17 +83,21 @@ def split_by_bytes(layer_bytes: list[int], n_stages: int, head_bytes: int = 0,
             c += head_bytes
         return c
 
+    empty_last = head_alone and head_bytes > 0 and n_stages > 1
+
     def feasible(limit):
         cuts, a = [], 0
         for k in range(n_stages):
-            left = n_stages - k - 1          # stages after this one, one layer each at least
+            # stages after this one, one layer each at least (the head's
+            # stage none when it may stand alone)
+            left = n_stages - k - 1 - (1 if empty_last and k < n_stages - 1 else 0)
             if k == n_stages - 1:
                 b = n
-                if b <= a or stage_cost(k, a, b) > limit:
+                if (b <= a and not empty_last) or stage_cost(k, a, b) > limit:
                     return None
             else:
                 b = a + 1
-                if stage_cost(k, a, b) > limit:
+                if b > n or stage_cost(k, a, b) > limit:
                     return None
                 while b + 1 <= n - left and stage_cost(k, a, b + 1) <= limit:
                     b += 1
@@ -260,7 +268,8 @@ class GpuStage:
         base = []
         if first == 0:
             base.append(E.LlmCtx(model, E.STAGE_EMBED, 0, 0, n_ctx, device))
-        base.append(E.LlmCtx(model, E.STAGE_LAYERS, first, last, n_ctx, device))
+        if first <= last:                      # (the head's GPU may hold no layer)
+            base.append(E.LlmCtx(model, E.STAGE_LAYERS, first, last, n_ctx, device))
         if last == n_layer - 1:
             base.append(E.LlmCtx(model, E.STAGE_HEAD, 0, 0, n_ctx, device))
         self.chains = [base] + [[c.fork() for c in base] for _ in range(n_seq - 1)]
@@ -394,7 +403,7 @@ def bench_main(args, rank: int, world: int, local: int, B) -> int:
         if args.split == "ref":
             plan = split_stages(spec.n_layer, world)
         else:
-            plan = split_by_bytes(lb, world, head_bytes=head_b, embed_bytes=emb_row)
+            plan = split_by_bytes(lb, world, head_bytes=head_b, embed_bytes=emb_row, head_alone=True)
         first, last = plan[rank]
         n_seq = args.seqs
         prompts = [synth.prompt_tokens(args.prompt, spec.n_vocab, seed=args.seed + 1 + s) for s in range(n_seq)]
@@ -550,7 +559,7 @@ def bench_long_main(args, rank: int, world: int, local: int, B) -> int:
         head_b = tensor_bytes(spec, "output.weight") + tensor_bytes(spec, "output_norm.weight")
         emb_row = tensor_bytes(spec, "token_embd.weight") // spec.n_vocab
         plan = split_stages(spec.n_layer, world) if args.split == "ref" else \
-            split_by_bytes(lb, world, head_bytes=head_b, embed_bytes=emb_row)
+            split_by_bytes(lb, world, head_bytes=head_b, embed_bytes=emb_row, head_alone=True)
         first, last = plan[rank]
         need = args.prompt + args.warmup + args.steps + 2
         if need > args.n_ctx:

@@ -31,8 +31,10 @@ def full_greedy(eng, m, prompt, n_gen, n_ctx):
     return toks, logits
 
 
-@pytest.mark.parametrize("n_ranks,n_seq", [(2, 1), (2, 3), (3, 2), (4, 4)])
-def test_loopback_pipeline_matches_full_context(eng, model_buf, n_ranks, n_seq):
+@pytest.mark.parametrize("n_ranks,n_seq,head_alone", [(2, 1, False), (2, 3, False), (3, 2, False),
+                                                       (4, 4, False), (3, 3, True)])
+def test_loopback_pipeline_matches_full_context(eng, model_buf, n_ranks, n_seq, head_alone):
+    """head_alone: the last stage holds the output head and no layer."""
     key, over = "mini-q4", {"n_layer": 4}
     s = synth.spec(key, **over)
     buf = model_buf(key, **over)
@@ -40,6 +42,8 @@ def test_loopback_pipeline_matches_full_context(eng, model_buf, n_ranks, n_seq):
     n_prompt, n_gen, n_ctx = 5, 12, 64
     prompts = [synth.prompt_tokens(n_prompt, s.n_vocab, seed=11 + q) for q in range(n_seq)]
     plan = P.split_stages(s.n_layer, n_ranks)
+    if head_alone:
+        plan = P.split_stages(s.n_layer, n_ranks - 1) + [(s.n_layer, s.n_layer - 1)]
     stages = {r: P.GpuStage(m, r, n_ranks, a, b, s.n_layer, n_seq, n_ctx, 0, prompts=prompts)
               for r, (a, b) in enumerate(plan)}
     n_steps = n_prompt + n_gen - 1
@@ -134,18 +138,21 @@ def test_prefill_through_stages_matches_full_context(eng, oracle_port, model_buf
     full.close()
     assert want == oracle.greedy(oracle_port, buf, prompt, n_gen)
 
-    stages = {r: P.GpuStage(m, r, 2, a, b, s.n_layer, 1, n_ctx, 0) for r, (a, b) in enumerate([(0, 0), (1, 1)])}
-    tok = P.prefill_local(stages, 0, prompt)
-    assert tok == want[0]
-    stages[1].record_tokens(n_prompt + n_gen)
-    S = P.Schedule(2, 1, n_gen - 1, n_prompt=n_prompt, first_step=n_prompt)
-    P.run_ticks(S, stages, P.LoopbackExchanger())
-    for st in stages.values():
-        st.sync()
-    hist = stages[1].history.cpu().numpy()[0]
-    got = [tok] + [int(t) for t in hist[n_prompt: n_prompt + n_gen - 1]]
-    assert got == want
-    got_logits = stages[1].chains[0][-1].logits()
-    assert np.array_equal(got_logits.view(np.uint32), want_logits.view(np.uint32))
-    for st in stages.values():
-        st.close()
+    # two stages, then three with the head alone on the last
+    for plan in ([(0, 0), (1, 1)], [(0, 0), (1, 1), (2, 1)]):
+        k = len(plan)
+        stages = {r: P.GpuStage(m, r, k, a, b, s.n_layer, 1, n_ctx, 0) for r, (a, b) in enumerate(plan)}
+        tok = P.prefill_local(stages, 0, prompt)
+        assert tok == want[0]
+        stages[k - 1].record_tokens(n_prompt + n_gen)
+        S = P.Schedule(k, 1, n_gen - 1, n_prompt=n_prompt, first_step=n_prompt)
+        P.run_ticks(S, stages, P.LoopbackExchanger())
+        for st in stages.values():
+            st.sync()
+        hist = stages[k - 1].history.cpu().numpy()[0]
+        got = [tok] + [int(t) for t in hist[n_prompt: n_prompt + n_gen - 1]]
+        assert got == want, plan
+        got_logits = stages[k - 1].chains[0][-1].logits()
+        assert np.array_equal(got_logits.view(np.uint32), want_logits.view(np.uint32))
+        for st in stages.values():
+            st.close()

@@ -44,10 +44,13 @@ def test_split_stages_capacity():
         P.split_stages(10, 2, cost, [25, 30])      # layers left over
 
 
-def _brute(layer_bytes, k, head, emb):
+def _brute(layer_bytes, k, head, emb, head_alone=False):
     n = len(layer_bytes)
     best = None
-    for cuts in itertools.combinations(range(1, n), k - 1):
+    splits = list(itertools.combinations(range(1, n), k - 1))
+    if head_alone and head > 0:                # the head's stage may hold no layer
+        splits += [c + (n,) for c in itertools.combinations(range(1, n), k - 2)]
+    for cuts in splits:
         b = (0,) + cuts + (n,)
         c = []
         for i in range(k):
@@ -82,13 +85,36 @@ def test_split_by_bytes_optimal(seed):
         assert _cost(plan, lb, head, 3) == _brute(lb, k, head, 3)
 
 
+@pytest.mark.parametrize("seed", range(6))
+def test_split_by_bytes_head_alone_optimal(seed):
+    g = torch.Generator().manual_seed(100 + seed)
+    n = 9
+    lb = [int(x) for x in torch.randint(1, 50, (n,), generator=g)]
+    head = int(torch.randint(1, 150, (1,), generator=g))
+    for k in range(2, 6):
+        plan = P.split_by_bytes(lb, k, head_bytes=head, embed_bytes=3, head_alone=True)
+        assert len(plan) == k and plan[0][0] == 0 and plan[-1][1] == n - 1
+        assert all(a <= b for a, b in plan[:-1]) and plan[-1][0] <= plan[-1][1] + 1
+        assert all(plan[i][1] + 1 == plan[i + 1][0] for i in range(k - 1))
+        assert _cost(plan, lb, head, 3) == _brute(lb, k, head, 3, head_alone=True)
+        assert _cost(plan, lb, head, 3) <= _brute(lb, k, head, 3)
+
+
 def test_split_by_bytes_8b_shape():
     # 32 equal layers of 122.7 MB, 558 MB head: the head counts as ~4.5 layers
     lb = [122_683_392] * 32
-    plan = P.split_by_bytes(lb, 8, head_bytes=558_170_112 + 16_384, embed_bytes=4352)
+    head = 558_170_112 + 16_384
+    plan = P.split_by_bytes(lb, 8, head_bytes=head, embed_bytes=4352)
     sizes = [b - a + 1 for a, b in plan]
     assert sum(sizes) == 32 and sizes[-1] < sizes[0]
     assert P.split_by_bytes(lb, 2, head_bytes=558_170_112)[0] == (0, 17)
+    # the head alone on the 8th GPU: no stage above 5 layers' bytes
+    alone = P.split_by_bytes(lb, 8, head_bytes=head, embed_bytes=4352, head_alone=True)
+    assert alone[-1] == (32, 31)
+    assert _cost(alone, lb, head, 4352) == 5 * lb[0] < _cost(plan, lb, head, 4352)
+    # where it does not pay, the split is the same as without the option
+    assert P.split_by_bytes(lb, 2, head_bytes=head, head_alone=True) == P.split_by_bytes(lb, 2, head_bytes=head)
+    assert P.split_by_bytes(lb, 4, head_bytes=head, head_alone=True)[-1][0] <= 31
 
 
 # --------------------------------------------------------------- schedule --

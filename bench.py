@@ -79,6 +79,9 @@ def parse():
     ap.add_argument("--mode", choices=["pp", "tp", "gemv"], default="pp",
                     help="N > 1: layer pipeline with interleaved sequences (pp) or batch-1 tensor "
                          "parallelism (tp); gemv: the quantised-matvec microbenchmark (one GPU)")
+    ap.add_argument("--hops", choices=["link", "nccl"], default="link",
+                    help="N > 1 pipeline: each step writes its output into the next GPU's step (link), or NCCL "
+                         "send/recv between the steps (nccl)")
     ap.add_argument("--split", choices=["bytes", "ref"], default="bytes",
                     help="N > 1: layer ranges balancing bytes per stage (head on the last GPU) or "
                          "shard.c's ceil(layers/stages) rule")
@@ -214,13 +217,23 @@ def build_model_gpu(spec, seed, device):
     return buf
 
 
-def one_gpu_tokens(model, spec, args, device: int, n: int, prompt) -> list[int]:
-    """n greedy tokens after `prompt` (fed one token at a time) from a FULL
-    context on one GPU: the reference for the multi-GPU partitions' tokens."""
+def one_gpu_tokens(model, spec, args, device: int, n: int, prompt, prefill: bool = False) -> list[int]:
+    """n greedy tokens after `prompt` (fed one token at a time, or with
+    prefill as one batch through ecu_prefill) from a FULL context on one
+    GPU: the reference for the multi-GPU partitions' tokens."""
+    import numpy as np
     from distcomp_b200 import engine as E
     c = E.LlmCtx(model, E.STAGE_FULL, n_ctx=args.n_ctx, device=device)
     try:
-        return c.generate(list(prompt), n)
+        if not prefill:
+            return c.generate(list(prompt), n)
+        toks = [c.prefill(list(prompt))]
+        out = np.zeros(spec.n_embd + 1, dtype=np.float32)
+        while len(toks) < n:
+            if c.forward(toks[-1], out) != 0:
+                raise RuntimeError(E.last_error())
+            toks.append(int(out[spec.n_embd]))
+        return toks
     finally:
         c.close()
 

@@ -426,6 +426,7 @@ struct TpSlice {
 struct ecu_ctx {
     int         device = 0, sms = 148;
     int         stage = 0, first = 0, last = 0, pos = 0;
+    unsigned    span = 0;                 // ECU_SPAN_* of an ECU_STAGE_SPAN context
     EcuGeom     g;
     TpSlice     tp;
     std::vector<void *> tp_peers;         // IPC mappings of the other ranks' tagged vectors
@@ -481,6 +482,10 @@ struct ecu_ctx {
     unsigned long long *mega_ll = nullptr;   // the tagged activation vectors, one block
     size_t      mega_ll_words = 0;
     int         stall_next = -1;          // ecu_inject_wait_timeout: the phase the next launch stalls
+    std::vector<MegaPhase> mega_ph;       // host copy of the phase list (pipeline links patch inputs)
+    cudaEvent_t ev_step = nullptr;        // ecu_step_dev on a caller's stream: ordering with the own stream
+    void       *link_peer = nullptr;      // IPC mapping of the next stage's tagged vectors
+    bool        linked_in = false;        // the step's input arrives over a pipeline link
     std::vector<const char *> ph_kind;    // per phase, for the profile
     std::vector<int> ph_in_ep;            // per phase: GEMV input's writer phase (-1: plain input or not a GEMV)
     std::vector<double>       ph_bytes;
@@ -721,6 +726,8 @@ static void ctx_free(ecu_ctx *c)
     if (c->graph) cudaGraphExecDestroy(c->graph);
     for (void *p : c->tp_peers)
         if (p) cudaIpcCloseMemHandle(p);
+    if (c->link_peer) cudaIpcCloseMemHandle(c->link_peer);
+    if (c->ev_step) cudaEventDestroy(c->ev_step);
     for (void *p : {(void *)c->pf.X, (void *)c->pf.QKV, (void *)c->pf.ATT, (void *)c->pf.GU, (void *)c->pf.H,
                     (void *)c->pf.ah, (void *)c->pf.al, (void *)c->pf.wh, (void *)c->pf.wl, (void *)c->pf.tok})
         if (p) cudaFree(p);
@@ -731,13 +738,34 @@ static void ctx_free(ecu_ctx *c)
     delete c;
 }
 
+// What a context's step does, by stage: EMBED (embedding row), LAYERS,
+// HEAD, FULL (all three), SPAN (a layer range, first > last for none, with
+// the embedding and/or the head by its flags).
+static bool r_emb(const ecu_ctx *c)
+{
+    return c->stage == ECU_STAGE_EMBED || c->stage == ECU_STAGE_FULL ||
+           (c->stage == ECU_STAGE_SPAN && (c->span & ECU_SPAN_EMBED));
+}
+static bool r_lay(const ecu_ctx *c)
+{
+    return c->stage == ECU_STAGE_LAYERS || c->stage == ECU_STAGE_FULL ||
+           (c->stage == ECU_STAGE_SPAN && c->first <= c->last);
+}
+static bool r_head(const ecu_ctx *c)
+{
+    return c->stage == ECU_STAGE_HEAD || c->stage == ECU_STAGE_FULL ||
+           (c->stage == ECU_STAGE_SPAN && (c->span & ECU_SPAN_HEAD));
+}
+// the step advances the position (a HEAD or EMBED stage keeps none)
+static bool r_pos(const ecu_ctx *c) { return r_lay(c) || c->stage == ECU_STAGE_SPAN; }
+
 // ------------------------------------------------------------- the step --
 
 // First weight matrix the step touches after layer li's down projection.
 static const DevMat *after_layer(const ecu_ctx *c, int li, int nl)
 {
     if (li + 1 < nl) return &c->layers[li + 1].qkv[0];
-    if (c->stage == ECU_STAGE_FULL) return &c->out;
+    if (r_head(c)) return &c->out;
     return nullptr;
 }
 
@@ -844,8 +872,8 @@ static void enqueue_head(ecu_ctx *c, Launcher &L, bool advance)
     a.xn_out = c->scr.xn;
     a.xn_dst = c->state;
     L.kind = "gemv_head_argmax";
-    // a FULL context's next token starts with layer 0's Q/K/V projection
-    const DevMat *nx = (c->stage == ECU_STAGE_FULL && !c->layers.empty()) ? &c->layers[0].qkv[0] : nullptr;
+    // the next token of a context with layers starts with layer 0's Q/K/V projection
+    const DevMat *nx = !c->layers.empty() ? &c->layers[0].qkv[0] : nullptr;
     enqueue_gemv(L, c->sms, c->out, c->state, c->out_norm, g.eps, c->logits, EPI_ARGMAX, c->scr, a, nx,
                  EPI_STORE);
 }
@@ -853,24 +881,23 @@ static void enqueue_head(ecu_ctx *c, Launcher &L, bool advance)
 // Kernels of one step of the stage: nl layers (LAYERS/FULL) from layer 0.
 static void enqueue_step(ecu_ctx *c, Launcher &L, int nl)
 {
-    if (c->stage == ECU_STAGE_EMBED || c->stage == ECU_STAGE_FULL) {
+    if (r_emb(c)) {
         L.kind = "embed";
         L.bytes = 8.0 * c->g.n_embd + (double)ecu_type_nbytes(c->emb.type, (size_t)c->g.n_embd);
         L(k_embed, dim3(8), dim3(256), 0, c->emb, c->st, c->state, c->g.n_embd);
     }
-    if (c->stage == ECU_STAGE_LAYERS || c->stage == ECU_STAGE_FULL)
+    if (r_lay(c))
         for (int i = 0; i < nl; i++) enqueue_layer(c, L, i, nl);
-    if (c->stage == ECU_STAGE_LAYERS) {
+    if (r_pos(c) && !r_head(c)) {
         L.kind = "step_advance";
         L(k_step_advance, dim3(1), dim3(32), 0, c->st);
     }
-    if (c->stage == ECU_STAGE_HEAD || c->stage == ECU_STAGE_FULL)
-        enqueue_head(c, L, c->stage == ECU_STAGE_FULL);
+    if (r_head(c)) enqueue_head(c, L, r_pos(c));
 }
 
 static int n_stage_layers(const ecu_ctx *c)
 {
-    return (c->stage == ECU_STAGE_LAYERS || c->stage == ECU_STAGE_FULL) ? c->last - c->first + 1 : 0;
+    return r_lay(c) ? c->last - c->first + 1 : 0;
 }
 
 static int mega_launch(ecu_ctx *c, cudaStream_t s, unsigned long long *phase_ns,
@@ -1033,7 +1060,8 @@ static int mega_setup(ecu_ctx *c)
     // ECU_MEGA=0 selects the per-kernel step
     const char *env = getenv("ECU_MEGA");
     if (env && env[0] == '0') return no("ECU_MEGA=0");
-    if ((c->stage != ECU_STAGE_FULL && c->stage != ECU_STAGE_LAYERS) || c->layers.empty())
+    // a stage with layers, or a span of the head alone
+    if (!(r_lay(c) && !c->layers.empty()) && !(c->stage == ECU_STAGE_SPAN && r_head(c)))
         return no("stage without layers");
     const EcuGeom &g = c->g;
     const TpSlice &tp = c->tp;
@@ -1046,7 +1074,7 @@ static int mega_setup(ecu_ctx *c)
         if (ly.qkv.size() != 1 || !ly.gu_fused || !mega_mat_ok(ly.qkv[0]) || !mega_mat_ok(ly.o) ||
             !mega_mat_ok(ly.gu) || !mega_mat_ok(ly.d))
             return no("a layer matrix is not Q4_0/Q8_0/Q4_K in a fast layout");
-    const bool full = c->stage == ECU_STAGE_FULL;
+    const bool emb = r_emb(c), full = r_head(c);        // (full: the step ends with the head)
     if (full && !mega_mat_ok(c->out)) return no("output head not Q4_0/Q8_0/Q4_K in a fast layout");
     int coop = 0;
     cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, c->device);
@@ -1127,16 +1155,19 @@ static int mega_setup(ecu_ctx *c)
     const size_t w_x = pad4(g.n_embd), w_qkv = pad4((size_t)qd_l + 2 * kvd_l), w_att = pad4(qdim),
                  w_h = pad4(g.n_ff), w_arg = pad4(2 * ECU_MAX_TP),
                  w_apart = pad4((size_t)tp.nkv * n_split * g.n_rep * (hd + 2));
-    c->mega_ll_words = w_x + w_qkv + w_att + w_h + w_arg + w_apart;
+    // (+ the token word a pipeline link delivers, right after the residual
+    // stream: at the same offset in every context of the model)
+    const size_t w_tok = 4;
+    c->mega_ll_words = w_x + w_tok + w_qkv + w_att + w_h + w_arg + w_apart;
     c->mega_ll = c->dalloc<unsigned long long>(c->mega_ll_words);
     if (!c->mega_ll) return -1;
     CK(cudaMemset(c->mega_ll, 0, c->mega_ll_words * sizeof(unsigned long long)));
-    unsigned long long *x_ll = c->mega_ll, *qkv_ll = x_ll + w_x, *att_ll = qkv_ll + w_qkv, *h_ll = att_ll + w_att,
-                       *arg_ll = h_ll + w_h, *apart_ll = arg_ll + w_arg;
+    unsigned long long *x_ll = c->mega_ll, *tok_ll = x_ll + w_x, *qkv_ll = tok_ll + w_tok, *att_ll = qkv_ll + w_qkv,
+                       *h_ll = att_ll + w_att, *arg_ll = h_ll + w_h, *apart_ll = arg_ll + w_arg;
     // x_w: the phase that last wrote the residual stream (-1: the plain
     // input state of a LAYERS stage)
     int x_w = -1;
-    if (full) {
+    if (emb) {
         MegaPhase p = {};
         p.kind = PH_EMBED;
         p.y_ll = x_ll;
@@ -1195,7 +1226,7 @@ static int mega_setup(ecu_ctx *c)
         gu.bcast = bcast;
         const int p_gu = (int)ph.size();
         add(gu, "gemv_gate_up", gemv_bytes(ly.gu, EPI_SWIGLU));
-        add_resid(ly.d, "gemv_down", c->h, h_ll, p_gu, (!full && last) ? 1 : 0);   // out_plain: a LAYERS stage's output state
+        add_resid(ly.d, "gemv_down", c->h, h_ll, p_gu, (!full && last) ? 1 : 0);   // out_plain: the stage's output state
     }
     if (full) {
         MegaPhase hp = mega_gemv_phase(c->out, grid, stage_bytes, 1, EPI_ARGMAX, c->state, c->out_norm, c->logits, xn_tmp);
@@ -1278,6 +1309,7 @@ static int mega_setup(ecu_ctx *c)
     if (!d_ph || !pval || !pidx || !ctr || (full && !xn_tmp)) return -1;
     CK(cudaMemcpy(d_ph, ph.data(), ph.size() * sizeof(MegaPhase), cudaMemcpyHostToDevice));
     CK(cudaMemset(ctr, 0, (4 + (size_t)g.n_head_kv) * sizeof(unsigned)));
+    c->mega_ph = ph;
     MegaArgs &a = c->margs;
     a = MegaArgs{};
     a.ph = d_ph;
@@ -1305,8 +1337,8 @@ static int mega_setup(ecu_ctx *c)
     a.phase_ns = nullptr;
     a.phase_clk = nullptr;
     a.phase_detail = nullptr;
-    a.advance_pos = full ? 1 : 0;
-    a.layers_advance = full ? 0 : 1;
+    a.advance_pos = (full && r_pos(c)) ? 1 : 0;
+    a.layers_advance = (!full && r_pos(c)) ? 1 : 0;
     a.n_embd = g.n_embd;
     a.n_head = tp.nh;
     a.n_kv = tp.nkv;
@@ -1331,6 +1363,7 @@ static int mega_setup(ecu_ctx *c)
     a.att_early = kv_early ? 1 : 0;
     a.stall_phase = -1;
     a.kv_off = (unsigned)kv_off;
+    a.tok_ll = tok_ll;
     a.eps = g.eps;
     a.kscale = 1.0f / sqrtf((float)hd);
     c->mega_fn = fn;
@@ -1576,29 +1609,40 @@ struct StageTensors {
 };
 
 static int stage_tensors(const ecu_model *m, const EcuGeom &g, int stage, int first, int last,
-                         StageTensors *st, char *err, size_t errlen)
+                         StageTensors *st, char *err, size_t errlen, unsigned span = 0)
 {
-    if ((stage == ECU_STAGE_LAYERS || stage == ECU_STAGE_FULL) &&
-        (last < first || last >= g.n_layer || first < 0)) {
+    const bool sp = stage == ECU_STAGE_SPAN;
+    const bool emb = stage == ECU_STAGE_EMBED || stage == ECU_STAGE_FULL || (sp && (span & ECU_SPAN_EMBED));
+    const bool head = stage == ECU_STAGE_HEAD || stage == ECU_STAGE_FULL || (sp && (span & ECU_SPAN_HEAD));
+    const bool lay = stage == ECU_STAGE_LAYERS || stage == ECU_STAGE_FULL || (sp && first <= last);
+    if (sp && (span & ~(ECU_SPAN_EMBED | ECU_SPAN_HEAD))) {
+        ecu_set_error(err, errlen, "unknown span flags 0x%x", span);
+        return -1;
+    }
+    if (sp && !lay && !emb && !head) {
+        ecu_set_error(err, errlen, "a span of no layers needs the embedding or the head");
+        return -1;
+    }
+    if (lay && (last < first || last >= g.n_layer || first < 0)) {
         ecu_set_error(err, errlen, "layers %d..%d outside the model: it has %d layers", first, last, g.n_layer);
         return -1;
     }
-    if (stage != ECU_STAGE_LAYERS && g.n_vocab <= 0) {
+    if ((emb || head) && g.n_vocab <= 0) {
         ecu_set_error(err, errlen, "cannot determine the vocabulary size (n_vocab) for stage %d", stage);
         return -1;
     }
-    if (stage == ECU_STAGE_EMBED || stage == ECU_STAGE_FULL) {
+    if (emb) {
         st->emb = m->find("token_embd.weight");
         if (!st->emb) { ecu_set_error(err, errlen, "model has no token_embd.weight"); return -1; }
     }
-    if (stage == ECU_STAGE_HEAD || stage == ECU_STAGE_FULL) {
+    if (head) {
         st->out_norm = m->find("output_norm.weight");
         if (!st->out_norm) { ecu_set_error(err, errlen, "model has no output_norm.weight"); return -1; }
         st->out = m->find("output.weight");
         if (!st->out) st->out = m->find("token_embd.weight");
         if (!st->out) { ecu_set_error(err, errlen, "model has neither output.weight nor token_embd.weight"); return -1; }
     }
-    if (stage == ECU_STAGE_LAYERS || stage == ECU_STAGE_FULL) {
+    if (lay) {
         static const char *sfx[9] = {"attn_norm.weight", "attn_q.weight", "attn_k.weight",
                                      "attn_v.weight", "attn_output.weight", "ffn_norm.weight",
                                      "ffn_gate.weight", "ffn_up.weight", "ffn_down.weight"};
@@ -1714,7 +1758,7 @@ static const char *alloc_buffers(ecu_ctx *c, bool layers, bool head)
 }
 
 static int ctx_open_impl(ecu_ctx **out, const ecu_model *m, int stage, int first, int last, int n_ctx,
-                         int device, int tp_rank, int tp_world, char *err, size_t errlen);
+                         int device, int tp_rank, int tp_world, char *err, size_t errlen, unsigned span = 0);
 
 int ecu_ctx_open(ecu_ctx **out, const ecu_model *m, int stage, int first, int last, int n_ctx,
                  int device, char *err, size_t errlen)
@@ -1722,6 +1766,15 @@ int ecu_ctx_open(ecu_ctx **out, const ecu_model *m, int stage, int first, int la
     if (err && errlen) err[0] = '\0';
     const int rc = ctx_open_impl(out, m, stage, first, last, n_ctx, device, 0, 1, err, errlen);
     // CUDA failures deep in the upload only set the thread's last error
+    if (rc != 0 && err && errlen && !err[0]) snprintf(err, errlen, "%s", ecu_get_error());
+    return rc;
+}
+
+int ecu_ctx_open_span(ecu_ctx **out, const ecu_model *m, int first, int last, unsigned flags, int n_ctx,
+                      int device, char *err, size_t errlen)
+{
+    if (err && errlen) err[0] = '\0';
+    const int rc = ctx_open_impl(out, m, ECU_STAGE_SPAN, first, last, n_ctx, device, 0, 1, err, errlen, flags);
     if (rc != 0 && err && errlen && !err[0]) snprintf(err, errlen, "%s", ecu_get_error());
     return rc;
 }
@@ -1736,18 +1789,19 @@ int ecu_ctx_open_tp(ecu_ctx **out, const ecu_model *m, int n_ctx, int device, in
 }
 
 static int ctx_open_impl(ecu_ctx **out, const ecu_model *m, int stage, int first, int last, int n_ctx,
-                         int device, int tp_rank, int tp_world, char *err, size_t errlen)
+                         int device, int tp_rank, int tp_world, char *err, size_t errlen, unsigned span)
 {
     if (!out || !m) { ecu_set_error(err, errlen, "null argument"); return -1; }
     *out = nullptr;
-    if (stage < ECU_STAGE_EMBED || stage > ECU_STAGE_FULL) { ecu_set_error(err, errlen, "unknown stage %d", stage); return -1; }
+    if (stage < ECU_STAGE_EMBED || stage > ECU_STAGE_SPAN) { ecu_set_error(err, errlen, "unknown stage %d", stage); return -1; }
     EcuGeom g;
     if (ecu_read_geom(m, &g, err, errlen) != 0) return -1;
     if (n_ctx > 0) g.n_ctx = n_ctx;
     if (stage == ECU_STAGE_FULL) { first = 0; last = g.n_layer - 1; }
     if (stage == ECU_STAGE_EMBED || stage == ECU_STAGE_HEAD) { first = 0; last = 0; }
+    if (stage == ECU_STAGE_SPAN && first > last) { first = g.n_layer; last = g.n_layer - 1; }   // no layers
     StageTensors st;
-    if (stage_tensors(m, g, stage, first, last, &st, err, errlen) != 0) return -1;
+    if (stage_tensors(m, g, stage, first, last, &st, err, errlen, span) != 0) return -1;
     const int hd = g.head_dim, qd = g.n_head * hd, kvd = g.n_head_kv * hd;
     if (!st.layers.empty()) {
         if (!attn_supported(hd, g.n_rep)) {
@@ -1809,6 +1863,7 @@ static int ctx_open_impl(ecu_ctx **out, const ecu_model *m, int stage, int first
     c->tp = tp;
     c->sms = num_sms(device);
     c->stage = stage;
+    c->span = stage == ECU_STAGE_SPAN ? span : 0u;
     c->first = first;
     c->last = last;
     c->g = g;
@@ -1816,7 +1871,8 @@ static int ctx_open_impl(ecu_ctx **out, const ecu_model *m, int stage, int first
     c->pdl = !(e && e[0] == '0');
     e = getenv("ECU_GRAPH");
     c->use_graph = !(e && e[0] == '0');
-    if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
+    if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&c->ev_step, cudaEventDisableTiming) != cudaSuccess) {
         ecu_set_error(err, errlen, "cudaStreamCreate failed");
         return -1;
     }
@@ -2025,7 +2081,15 @@ int ecu_ctx_info(const ecu_ctx *c, ecu_info *i)
 
 void ecu_reset(ecu_ctx *c)
 {
-    if (c) c->pos = 0;
+    if (!c) return;
+    c->pos = 0;
+    // a linked context's tagged words start over: no word a link wrote for
+    // a position of the previous run may look like this run's input
+    if (c->mega_ll && (c->linked_in || c->margs.link_x || c->margs.link_tok)) {
+        cudaSetDevice(c->device);
+        cudaMemsetAsync(c->mega_ll, 0, c->mega_ll_words * sizeof(unsigned long long), c->stream);
+        cudaStreamSynchronize(c->stream);
+    }
 }
 
 int ecu_set_pos(ecu_ctx *c, int pos)
@@ -2042,13 +2106,13 @@ void  *ecu_stream(ecu_ctx *c) { return c ? (void *)c->stream : nullptr; }
 // Host-side checks of llm_forward (src/engine.c:468-515) before enqueueing.
 static int step_check(ecu_ctx *c, int token)
 {
-    if (c->stage == ECU_STAGE_EMBED || c->stage == ECU_STAGE_FULL) {
+    if (r_emb(c)) {
         if (token < 0 || token >= c->g.n_vocab) {
             ecu_set_error(nullptr, 0, "token %d outside the vocabulary (%d)", token, c->g.n_vocab);
             return -1;
         }
     }
-    if ((c->stage == ECU_STAGE_LAYERS || c->stage == ECU_STAGE_FULL) && c->pos >= c->g.n_ctx) {
+    if (r_pos(c) && c->pos >= c->g.n_ctx) {
         ecu_set_error(nullptr, 0, "context exhausted (%d positions)", c->g.n_ctx);
         return -1;
     }
@@ -2063,23 +2127,24 @@ static int enqueue_forward(ecu_ctx *c, int token)
     slot->token = token;
     CK(cudaMemcpyAsync(c->st, slot, 2 * sizeof(int), cudaMemcpyHostToDevice, c->stream));
     if (run_step(c) != 0) return -1;
-    if (c->stage == ECU_STAGE_LAYERS || c->stage == ECU_STAGE_FULL) c->pos++;
-    if (c->stage == ECU_STAGE_HEAD || c->stage == ECU_STAGE_FULL) c->have_logits = true;
+    if (r_pos(c)) c->pos++;
+    if (r_head(c)) c->have_logits = true;
     return 0;
 }
 
 int ecu_forward(ecu_ctx *c, int token, float *out)
 {
     if (!c || !out) return -1;
+    if (c->linked_in) { ecu_set_error(nullptr, 0, "a linked context takes its input over the link (ecu_step_dev)"); return -1; }
     cudaSetDevice(c->device);
     if (step_check(c, token) != 0) return -1;
     const size_t ne = (size_t)c->g.n_embd;
-    if (c->stage == ECU_STAGE_LAYERS || c->stage == ECU_STAGE_HEAD) {
+    if (!r_emb(c)) {
         memcpy(c->h_state, out, ne * sizeof(float));
         CK(cudaMemcpyAsync(c->state, c->h_state, ne * sizeof(float), cudaMemcpyHostToDevice, c->stream));
     }
     if (enqueue_forward(c, token) != 0) return -1;
-    const size_t nout = (c->stage == ECU_STAGE_HEAD || c->stage == ECU_STAGE_FULL) ? ne + 1 : ne;
+    const size_t nout = r_head(c) ? ne + 1 : ne;
     CK(cudaMemcpyAsync(c->h_state, c->state, nout * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
     if (check_status(c) != 0) return -1;
     memcpy(out, c->h_state, nout * sizeof(float));
@@ -2101,9 +2166,31 @@ int ecu_step_dev(ecu_ctx *c, void *stream)
 {
     if (!c) return -1;
     cudaSetDevice(c->device);
-    if ((c->stage == ECU_STAGE_LAYERS || c->stage == ECU_STAGE_FULL) && c->pos >= c->g.n_ctx) {
+    if (r_pos(c) && c->pos >= c->g.n_ctx) {
         ecu_set_error(nullptr, 0, "context exhausted (%d positions)", c->g.n_ctx);
         return -1;
+    }
+    cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
+    if (c->mega && s != c->stream) {
+        // the persistent step straight on the caller's stream (a pipeline
+        // stage's steps of every sequence share one): ordered after the
+        // context's own stream only when that has work left, and the
+        // context's stream ordered after the step for whatever follows there
+        if (cudaStreamQuery(c->stream) != cudaSuccess) {
+            cudaGetLastError();
+            CK(cudaEventRecord(c->ev_step, c->stream));
+            CK(cudaStreamWaitEvent(s, c->ev_step, 0));
+        }
+        StepState *slot = c->h_st + (c->pos % c->n_hslots);
+        slot->pos = c->pos;
+        CK(cudaMemcpyAsync(&c->st->pos, &slot->pos, sizeof(int), cudaMemcpyHostToDevice, s));
+        if (mega_launch(c, s, nullptr) != 0) return -1;
+        g_launches += 1;
+        CK(cudaEventRecord(c->ev_step, s));
+        CK(cudaStreamWaitEvent(c->stream, c->ev_step, 0));
+        if (r_pos(c)) c->pos++;
+        if (r_head(c)) c->have_logits = true;
+        return 0;
     }
     return on_stream(c, stream, [&] {
         // the position comes from the host; the token stays where the
@@ -2112,8 +2199,8 @@ int ecu_step_dev(ecu_ctx *c, void *stream)
         slot->pos = c->pos;
         CK(cudaMemcpyAsync(&c->st->pos, &slot->pos, sizeof(int), cudaMemcpyHostToDevice, c->stream));
         if (run_step(c) != 0) return -1;
-        if (c->stage == ECU_STAGE_LAYERS || c->stage == ECU_STAGE_FULL) c->pos++;
-        if (c->stage == ECU_STAGE_HEAD || c->stage == ECU_STAGE_FULL) c->have_logits = true;
+        if (r_pos(c)) c->pos++;
+        if (r_head(c)) c->have_logits = true;
         return 0;
     });
 }
@@ -2129,6 +2216,7 @@ int ecu_ctx_fork(ecu_ctx **out, ecu_ctx *base, char *err, size_t errlen)
     c->device = base->device;
     c->sms = base->sms;
     c->stage = base->stage;
+    c->span = base->span;
     c->first = base->first;
     c->last = base->last;
     c->g = base->g;
@@ -2143,12 +2231,13 @@ int ecu_ctx_fork(ecu_ctx **out, ecu_ctx *base, char *err, size_t errlen)
     c->rope_cs = base->rope_cs;
     c->n_split = base->n_split;
     c->srcs = base->srcs;
-    if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
+    if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&c->ev_step, cudaEventDisableTiming) != cudaSuccess) {
         ecu_set_error(err, errlen, "cudaStreamCreate failed");
         return -1;
     }
-    const bool layers = c->stage == ECU_STAGE_LAYERS || c->stage == ECU_STAGE_FULL;
-    const bool head = c->stage == ECU_STAGE_HEAD || c->stage == ECU_STAGE_FULL;
+    const bool layers = !c->layers.empty();
+    const bool head = r_head(c.get());
     if (const char *what = alloc_buffers(c.get(), layers, head)) {
         ecu_set_error(err, errlen, "out of device memory (%s) after %zu bytes", what, c->bytes);
         return -1;
@@ -2229,7 +2318,7 @@ int ecu_sync(ecu_ctx *c)
     cudaSetDevice(c->device);
     if (check_status(c) != 0) return -1;
     // the device-side loop leaves the argmax in state[n_embd]
-    if (c->stage == ECU_STAGE_FULL || c->stage == ECU_STAGE_HEAD) {
+    if (r_head(c)) {
         float t;
         CK(cudaMemcpy(&t, c->state + c->g.n_embd, sizeof t, cudaMemcpyDeviceToHost));
         c->last_pick = (int)t;
@@ -2284,7 +2373,7 @@ int ecu_generate(ecu_ctx *c, const int *prompt, int n_prompt, int n_gen, int *ou
 int ecu_profile_steps(ecu_ctx *c, int n_steps, ecu_kprof *out, int max_kinds)
 {
     if (!c || n_steps < 1 || !out || max_kinds < 1) return -1;
-    if (c->stage != ECU_STAGE_FULL && c->stage != ECU_STAGE_LAYERS) return -1;
+    if (!r_lay(c) && !c->mega) return -1;
     if (c->pos + n_steps > c->g.n_ctx) { ecu_set_error(nullptr, 0, "context exhausted"); return -1; }
     cudaSetDevice(c->device);
     if (c->mega) return mega_profile(c, n_steps, out, max_kinds);
@@ -2793,6 +2882,123 @@ int ecu_tp_connect(ecu_ctx *c, const unsigned char *handles)
     return 0;
 }
 
+// ------------------------------------------------------ pipeline links -----
+
+// The token word of a linked first stage, from the host (the prompt's last
+// token before the first linked step), tagged for the position `epoch`
+// encodes.
+__global__ void k_link_feed(unsigned long long *w, int token, unsigned epoch)
+{
+    const unsigned long long v = ((unsigned long long)epoch << 32) | (unsigned)token;
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(w), "l"(v) : "memory");
+}
+
+static unsigned host_link_epoch(int pos) { return (((unsigned)pos & 0xFFFFFu) << 12) | 0xFFFu; }
+
+static int link_check(ecu_ctx *c, const char *what)
+{
+    if (!c) return -1;
+    if (!c->mega || !c->mega_ll) {
+        ecu_set_error(nullptr, 0, "%s: pipeline links need the persistent step (%s)", what, c->path.c_str());
+        return -1;
+    }
+    if (c->tp.world > 1) {
+        ecu_set_error(nullptr, 0, "%s: a tensor-parallel context is not linked", what);
+        return -1;
+    }
+    return 0;
+}
+
+int ecu_link_handle(ecu_ctx *c, unsigned char *out)
+{
+    if (link_check(c, "ecu_link_handle") != 0 || !out) return -1;
+    cudaSetDevice(c->device);
+    cudaIpcMemHandle_t h;
+    CK(cudaIpcGetMemHandle(&h, c->mega_ll));
+    static_assert(sizeof h == ECU_LINK_HANDLE_BYTES, "IPC handle size");
+    memcpy(out, &h, sizeof h);
+    return 0;
+}
+
+// The next stage's tagged block at `peer`: a stage with the head sends its
+// argmax to the token word (right after the residual stream), any other
+// stage its output state to the residual stream's words.
+static void link_to(ecu_ctx *c, unsigned long long *peer)
+{
+    if (r_head(c)) {
+        c->margs.link_tok = peer + (((size_t)c->g.n_embd + 7) & ~(size_t)3);
+        c->margs.link_x = nullptr;
+    } else {
+        c->margs.link_x = peer;
+        c->margs.link_tok = nullptr;
+    }
+}
+
+int ecu_link_next(ecu_ctx *c, const unsigned char *handle)
+{
+    if (link_check(c, "ecu_link_next") != 0 || !handle) return -1;
+    if (c->link_peer) { ecu_set_error(nullptr, 0, "ecu_link_next: already linked"); return -1; }
+    cudaSetDevice(c->device);
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof h);
+    void *p = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+        ecu_set_error(nullptr, 0, "opening the next stage's tagged vectors failed: %s", cudaGetErrorString(e));
+        return -1;
+    }
+    c->link_peer = p;
+    link_to(c, reinterpret_cast<unsigned long long *>(p));
+    return 0;
+}
+
+int ecu_link_next_local(ecu_ctx *c, ecu_ctx *next)
+{
+    if (link_check(c, "ecu_link_next_local") != 0 || link_check(next, "ecu_link_next_local") != 0) return -1;
+    if (next->g.n_embd != c->g.n_embd) { ecu_set_error(nullptr, 0, "ecu_link_next_local: different models"); return -1; }
+    link_to(c, next->mega_ll);
+    return 0;
+}
+
+int ecu_link_input(ecu_ctx *c)
+{
+    if (link_check(c, "ecu_link_input") != 0) return -1;
+    if (c->linked_in) return 0;
+    cudaSetDevice(c->device);
+    if (r_emb(c)) {
+        c->margs.link_in = 1;             // the embedding waits for the token word
+    } else {
+        // the phases that read the stage's input state read the link's words
+        for (MegaPhase &q : c->mega_ph) {
+            if (q.kind == PH_GEMV && q.in_ep == MEGA_EP_PLAIN) q.in_ep = MEGA_EP_LINK;
+            if (q.kind == PH_GEMV && q.epi == EPI_ADD && q.y_ep == MEGA_EP_PLAIN) q.y_ep = MEGA_EP_LINK;
+        }
+        CK(cudaMemcpy(const_cast<MegaPhase *>(c->margs.ph), c->mega_ph.data(), c->mega_ph.size() * sizeof(MegaPhase),
+                      cudaMemcpyHostToDevice));
+    }
+    c->linked_in = true;
+    return 0;
+}
+
+int ecu_link_feed(ecu_ctx *c, int token, void *stream)
+{
+    if (link_check(c, "ecu_link_feed") != 0) return -1;
+    if (!c->linked_in || !r_emb(c)) {
+        ecu_set_error(nullptr, 0, "ecu_link_feed: not a linked first stage");
+        return -1;
+    }
+    if (token < 0 || token >= c->g.n_vocab) {
+        ecu_set_error(nullptr, 0, "token %d outside the vocabulary (%d)", token, c->g.n_vocab);
+        return -1;
+    }
+    cudaSetDevice(c->device);
+    cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
+    k_link_feed<<<1, 1, 0, s>>>(c->margs.tok_ll, token, host_link_epoch(c->pos));
+    CK(cudaGetLastError());
+    g_launches += 1;
+    return 0;
+}
+
 // ----------------------------------------------------------- prefill -----
 
 static int pf_reserve(ecu_ctx *c, int n)
@@ -2966,6 +3172,56 @@ static int pf_head(ecu_ctx *c, const float *x_row, int pos, int token, float *ou
     return 0;
 }
 
+// A span's prompt rows: the embedding rows of the tokens (ECU_SPAN_EMBED),
+// the layers in place (batched), then the head on the last row
+// (ECU_SPAN_HEAD); the position advances by n.
+static int span_prefill_rows(ecu_ctx *c, const int *tokens, int n, float *x, float *out)
+{
+    const EcuGeom &g = c->g;
+    const size_t   rows_bytes = sizeof(float) * (size_t)n * g.n_embd;
+    const int      pos0 = c->pos;
+    if (pos0 + n > g.n_ctx) {
+        ecu_set_error(nullptr, 0, "prompt of %d tokens at position %d exceeds the context (%d)", n, pos0, g.n_ctx);
+        return -1;
+    }
+    if (r_head(c) && !out) { ecu_set_error(nullptr, 0, "a span with the head needs the output buffer"); return -1; }
+    if (r_emb(c)) {
+        if (!tokens) { ecu_set_error(nullptr, 0, "a span with the embedding needs the prompt tokens"); return -1; }
+        for (int i = 0; i < n; i++)
+            if (tokens[i] < 0 || tokens[i] >= g.n_vocab) {
+                ecu_set_error(nullptr, 0, "token %d outside the vocabulary (%d)", tokens[i], g.n_vocab);
+                return -1;
+            }
+        int *tok = nullptr;
+        CK(cudaMallocAsync((void **)&tok, sizeof(int) * n, c->stream));
+        CK(cudaMemcpyAsync(tok, tokens, sizeof(int) * n, cudaMemcpyHostToDevice, c->stream));
+        k_pf_embed<<<4 * c->sms, 256, 0, c->stream>>>(c->emb, tok, n, x, g.n_embd);
+        CK(cudaGetLastError());
+        CK(cudaFreeAsync(tok, c->stream));
+        g_launches += 1;
+    }
+    if (!c->layers.empty()) {
+        bool attn2 = false;
+        if (!pf_batched(c, attn2)) {
+            ecu_set_error(nullptr, 0, "the batched prompt kernels do not cover this span's shapes");
+            return -1;
+        }
+        if (pf_attrs(c) != 0 || pf_reserve(c, n) != 0) return -1;
+        CK(cudaMemcpyAsync(c->pf.X, x, rows_bytes, cudaMemcpyDeviceToDevice, c->stream));
+        if (pf_layers(c, n, pos0, attn2) != 0) return -1;
+        CK(cudaMemcpyAsync(x, c->pf.X, rows_bytes, cudaMemcpyDeviceToDevice, c->stream));
+    }
+    if (r_head(c)) return pf_head(c, x + (size_t)(n - 1) * g.n_embd, pos0 + n - 1, tokens ? tokens[n - 1] : 0, out);
+    c->pos = pos0 + n;
+    CK(cudaMemcpyAsync(c->state, x + (size_t)(n - 1) * g.n_embd, sizeof(float) * g.n_embd, cudaMemcpyDeviceToDevice,
+                       c->stream));
+    StepState *slot = c->h_st + (c->pos % c->n_hslots);
+    slot->pos = c->pos;
+    slot->token = 0;
+    CK(cudaMemcpyAsync(c->st, slot, 2 * sizeof(int), cudaMemcpyHostToDevice, c->stream));
+    return check_status(c);
+}
+
 int ecu_prefill_rows(ecu_ctx *c, const int *tokens, int n, float *x, float *out)
 {
     if (!c || n < 1 || !x) { ecu_set_error(nullptr, 0, "null argument or empty prompt"); return -1; }
@@ -2973,6 +3229,7 @@ int ecu_prefill_rows(ecu_ctx *c, const int *tokens, int n, float *x, float *out)
     const EcuGeom &g = c->g;
     const size_t   rows_bytes = sizeof(float) * (size_t)n * g.n_embd;
     if (c->stage == ECU_STAGE_FULL) { ecu_set_error(nullptr, 0, "a FULL context prefills with ecu_prefill"); return -1; }
+    if (c->stage == ECU_STAGE_SPAN) return span_prefill_rows(c, tokens, n, x, out);
     if (c->stage == ECU_STAGE_EMBED) {
         if (!tokens) { ecu_set_error(nullptr, 0, "EMBED needs the prompt tokens"); return -1; }
         for (int i = 0; i < n; i++)

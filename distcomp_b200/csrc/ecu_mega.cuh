@@ -123,6 +123,12 @@ struct MegaArgs {
                                     // no phase writes, so its bounded waits run out (-1: none)
     unsigned         kv_off;        // byte offset of the attention K/V buffers in the union (above the
                                     // Q/K/V phase's digit planes when att_early)
+    // pipeline links (contexts on consecutive GPUs, one per stage): tagged
+    // words with link_epoch(position) written into the next stage's memory
+    unsigned long long *link_x;     // the stage's output state -> the next stage's x_ll (or null)
+    unsigned long long *link_tok;   // the head's argmax -> the first stage's token word (or null)
+    unsigned long long *tok_ll;     // this context's token word (a linked embedding reads it)
+    int              link_in;       // the embedding waits for its token in tok_ll
     float            eps, kscale;
 };
 
@@ -141,6 +147,20 @@ struct MegaArgs {
 __device__ __forceinline__ unsigned ll_epoch(unsigned launch, int phase)
 {
     return ((launch & 0xFFFFFu) << 12) | (unsigned)(phase + 1);
+}
+
+// A pipeline link: the words one stage's step writes into the next stage's
+// memory (another GPU's) carry the token position and the low 12 bits all
+// ones, which no phase epoch has (phase + 1 < 4095): the receiver knows the
+// position of its step, and a stage writes position p + 1 only after the
+// receiver's step p is over (the token has gone round the ring of stages).
+// Phase inputs marked MEGA_EP_LINK read those words (system scope: another
+// GPU wrote them); MEGA_EP_PLAIN inputs read the plain state.
+#define MEGA_EP_PLAIN (-1)
+#define MEGA_EP_LINK  (-2)
+__device__ __forceinline__ unsigned link_epoch(int pos)
+{
+    return (((unsigned)pos & 0xFFFFFu) << 12) | 0xFFFu;
 }
 
 // SYS: system scope (tensor-parallel ranks read and write each other's
@@ -190,6 +210,18 @@ __device__ __forceinline__ ulonglong2 ll_word2(const unsigned long long *p)
     return w;
 }
 
+// The same with the scope chosen at run time (system scope for words that
+// another GPU writes).
+__device__ __forceinline__ ulonglong2 ll_word2_rt(const unsigned long long *p, bool sys)
+{
+    ulonglong2 w;
+    if (sys)
+        asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(w.x), "=l"(w.y) : "l"(p) : "memory");
+    else
+        asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(w.x), "=l"(w.y) : "l"(p) : "memory");
+    return w;
+}
+
 // Spin helper: true while waiting is still allowed (bounded; gives up at
 // once when the step is already flagged as failed).
 __device__ __forceinline__ bool ll_keep_waiting(unsigned it, uint64_t &t0, int *status)
@@ -227,14 +259,16 @@ template <int K, bool SYS>
 __device__ __forceinline__ void input_batch(const MegaArgs &a, const MegaPhase &ph, int t0, int stride, int nq,
                                             unsigned ein, float4 (&v)[K])
 {
-    if (ph.in_ep >= 0) {
+    if (ph.in_ep != MEGA_EP_PLAIN) {
+        // (a pipeline link's words come from another GPU: system scope)
+        const bool sys = SYS || ph.in_ep == MEGA_EP_LINK;
         ulonglong2 w[K][2];
 #pragma unroll
         for (int k = 0; k < K; k++) {
             const int t = t0 + k * stride;
             if (t < nq) {
-                w[k][0] = ll_word2<SYS>(ph.x_ll + 4 * (size_t)t);
-                w[k][1] = ll_word2<SYS>(ph.x_ll + 4 * (size_t)t + 2);
+                w[k][0] = ll_word2_rt(ph.x_ll + 4 * (size_t)t, sys);
+                w[k][1] = ll_word2_rt(ph.x_ll + 4 * (size_t)t + 2, sys);
             }
         }
 #pragma unroll
@@ -243,8 +277,8 @@ __device__ __forceinline__ void input_batch(const MegaArgs &a, const MegaPhase &
             if (t < nq) {
                 uint64_t tw = 0;
                 for (unsigned it = 1; !ll_tags4(w[k], ein) && ll_keep_waiting(it, tw, a.status); it++) {
-                    w[k][0] = ll_word2<SYS>(ph.x_ll + 4 * (size_t)t);
-                    w[k][1] = ll_word2<SYS>(ph.x_ll + 4 * (size_t)t + 2);
+                    w[k][0] = ll_word2_rt(ph.x_ll + 4 * (size_t)t, sys);
+                    w[k][1] = ll_word2_rt(ph.x_ll + 4 * (size_t)t + 2, sys);
                 }
                 v[k] = make_float4(__uint_as_float((unsigned)w[k][0].x), __uint_as_float((unsigned)w[k][0].y),
                                    __uint_as_float((unsigned)w[k][1].x), __uint_as_float((unsigned)w[k][1].y));
@@ -738,6 +772,7 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
     if (ph.next_attn && tid < hd) cs_next = __ldg(a.rope_cs + (size_t)S.pos * hd + tid);
     unsigned long long yw = 0;
     if (has_res && ph.y_ep >= 0) yw = ll_word<SYS>(a.x_ll + ph.out_base + r0 + tid);
+    if (has_res && ph.y_ep == MEGA_EP_LINK) yw = ll_word<true>(a.x_ll + r0 + tid);
     // the next attention's first K/V rounds (rows of earlier positions: no
     // dependence on this step) start streaming into their buffers now, above
     // this phase's digit planes
@@ -764,7 +799,9 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
     // one layer later, ordered only by what each phase reads).
     // (an injected stall: the epoch of phase -1 of the next launch, which no
     // word carries)
-    const unsigned ein = p_idx == a.stall_phase ? ll_epoch(S.launch + 1u, -1) : ll_epoch(S.launch, ph.in_ep);
+    const unsigned ein = p_idx == a.stall_phase         ? ll_epoch(S.launch + 1u, -1)
+                         : ph.in_ep == MEGA_EP_LINK      ? link_epoch(S.pos)
+                                                         : ll_epoch(S.launch, ph.in_ep);
     const bool active = nrows > 0 && warp < nkg * rowpar;
     const int  g = active ? warp % nkg : 0, rp = active ? warp / nkg : 0;
     if (active) {
@@ -801,7 +838,8 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
     float yprev = 0.0f;
     if (has_res)
         yprev = ph.y_ep >= 0 ? ll_settle<SYS>(a.x_ll + ph.out_base + r0 + tid, yw, ll_epoch(S.launch, ph.y_ep), a.status)
-                             : __ldcg(ph.y + r0 + tid);
+                : ph.y_ep == MEGA_EP_LINK ? ll_settle<true>(a.x_ll + r0 + tid, yw, link_epoch(S.pos), a.status)
+                                          : __ldcg(ph.y + r0 + tid);
 
     if (det) det[0] = clock64();
     // ---- main loop ------------------------------------------------------------
@@ -910,7 +948,11 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
         if (epi == EPI_ADD) {
             const float out = yprev + acc;         // r == tid: nrows <= MEGA_THREADS
             ll_put_out<SYS>(a, ph.bcast, ph.y_ll + ph.out_base + r0 + r, out, eout);
-            if (ph.out_plain) y[r0 + r] = out;
+            if (ph.out_plain) {
+                y[r0 + r] = out;
+                // the stage's output state, also into the next stage's input
+                if (a.link_x) ll_put<true>(a.link_x + r0 + r, out, link_epoch(S.pos));
+            }
         } else if (epi == EPI_STORE) {
             ll_put_out<SYS>(a, ph.bcast, ph.y_ll + ph.out_base + r0 + r, acc, eout);
         } else {
@@ -973,6 +1015,8 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
         const int   pos = S.pos;
         if (a.tok_hist) a.tok_hist[pos] = tok;
         a.st->token = tok;
+        // the first stage's next input (position pos + 1) on its GPU
+        if (a.link_tok) ll_put<true>(a.link_tok, __int_as_float(tok), link_epoch(pos + 1));
         if (a.advance_pos) a.st->pos = pos + 1;
         a.state[a.n_embd] = (float)tok;
         *a.ticket = 0u;
@@ -1276,7 +1320,8 @@ __device__ void mega_embed(const MegaArgs &a, const MegaShared &S, int p_idx)
 {
     const unsigned eout = ll_epoch(S.launch, p_idx);
     const int    nct = MEGA_NCW * 32, n = a.n_embd;
-    const int    tok = a.st->token;
+    // a linked first stage waits for the token the last stage picked
+    const int    tok = a.link_in ? __float_as_int(ll_get<true>(a.tok_ll, link_epoch(S.pos), a.status)) : a.st->token;
     if (tok < 0 || tok >= a.emb.n_out) {
         if (blockIdx.x == 0 && threadIdx.x == 0) atomicOr(&a.st->status, ECU_STATUS_BADTOKEN);
         return;

@@ -27,7 +27,8 @@ from pathlib import Path
 
 import numpy as np
 
-STAGE_EMBED, STAGE_LAYERS, STAGE_HEAD, STAGE_FULL = 0, 1, 2, 3
+STAGE_EMBED, STAGE_LAYERS, STAGE_HEAD, STAGE_FULL, STAGE_SPAN = 0, 1, 2, 3, 4
+SPAN_EMBED, SPAN_HEAD = 1, 2
 
 _LIB = None
 _LIB_PATH = Path(__file__).resolve().parent / "libdcb200.so"
@@ -81,6 +82,13 @@ SIGNATURES = [
     ("ecu_token_ptr", C.c_void_p, [C.c_void_p]),
     ("ecu_step_dev", C.c_int, [C.c_void_p, C.c_void_p]),
     ("ecu_ctx_fork", C.c_int, [C.POINTER(C.c_void_p), C.c_void_p, C.c_char_p, C.c_size_t]),
+    ("ecu_ctx_open_span", C.c_int, [C.POINTER(C.c_void_p), C.c_void_p, C.c_int, C.c_int, C.c_uint, C.c_int,
+                                    C.c_int, C.c_char_p, C.c_size_t]),
+    ("ecu_link_handle", C.c_int, [C.c_void_p, C.c_char_p]),
+    ("ecu_link_next", C.c_int, [C.c_void_p, C.c_char_p]),
+    ("ecu_link_next_local", C.c_int, [C.c_void_p, C.c_void_p]),
+    ("ecu_link_input", C.c_int, [C.c_void_p]),
+    ("ecu_link_feed", C.c_int, [C.c_void_p, C.c_int, C.c_void_p]),
     ("ecu_ctx_open_tp", C.c_int, [C.POINTER(C.c_void_p), C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
                                   C.c_char_p, C.c_size_t]),
     ("ecu_tp_handle", C.c_int, [C.c_void_p, C.c_char_p]),
@@ -190,13 +198,19 @@ class LlmCtx:
     """One engine stage resident on one GPU (llm_ctx, src/engine.h:46-70)."""
 
     def __init__(self, model: GgufModel | None, stage: int, first: int = 0, last: int = 0, n_ctx: int = 0,
-                 device: int = 0, fork_of: "LlmCtx | None" = None, tp: tuple[int, int] | None = None):
+                 device: int = 0, fork_of: "LlmCtx | None" = None, tp: tuple[int, int] | None = None,
+                 span: int = 0):
         """tp = (rank, world): a tensor-parallel FULL context (ecu_ctx_open_tp);
-        connect the ranks with tp_handle / tp_connect before the first step."""
+        connect the ranks with tp_handle / tp_connect before the first step.
+        stage STAGE_SPAN: layers first..last (first > last: none) with the
+        embedding / head by span = SPAN_EMBED | SPAN_HEAD (ecu_ctx_open_span)."""
         self.h = C.c_void_p()
         err = C.create_string_buffer(512)
         if fork_of is not None:
             rc = lib().ecu_ctx_fork(C.byref(self.h), fork_of.h, err, 512)
+            span = fork_of.span
+        elif stage == STAGE_SPAN:
+            rc = lib().ecu_ctx_open_span(C.byref(self.h), model.h, first, last, span, n_ctx, device, err, 512)
         elif tp is not None:
             rc = lib().ecu_ctx_open_tp(C.byref(self.h), model.h, n_ctx, device, int(tp[0]), int(tp[1]), err, 512)
         else:
@@ -208,6 +222,8 @@ class LlmCtx:
         self.info = i
         self.n_embd, self.n_vocab, self.n_ctx = i.n_embd, i.n_vocab, i.n_ctx
         self.stage = i.stage
+        self.span = span if i.stage == STAGE_SPAN else 0
+        self.has_head = i.stage in (STAGE_HEAD, STAGE_FULL) or bool(self.span & SPAN_HEAD)
         self.device = i.device
         sl = (C.c_int * 4)()
         lib().ecu_tp_slice(self.h, sl)
@@ -238,6 +254,31 @@ class LlmCtx:
         if lib().ecu_get_logits(self.h, _ptr(out), n) != 0:
             raise EngineError(last_error())
         return out
+
+    # --- pipeline links ---------------------------------------------------
+    def link_handle(self) -> bytes:
+        buf = C.create_string_buffer(64)
+        if lib().ecu_link_handle(self.h, buf) != 0:
+            raise EngineError(last_error())
+        return buf.raw
+
+    def link_next(self, nxt: "LlmCtx | bytes") -> None:
+        """Send this stage's output to the next stage: a context of this
+        process, or another process's link_handle()."""
+        if isinstance(nxt, LlmCtx):
+            rc = lib().ecu_link_next_local(self.h, nxt.h)
+        else:
+            rc = lib().ecu_link_next(self.h, bytes(nxt))
+        if rc != 0:
+            raise EngineError(last_error())
+
+    def link_input(self) -> None:
+        if lib().ecu_link_input(self.h) != 0:
+            raise EngineError(last_error())
+
+    def link_feed(self, token: int, stream: int | None = None) -> None:
+        if lib().ecu_link_feed(self.h, int(token), C.c_void_p(stream) if stream else None) != 0:
+            raise EngineError(last_error())
 
     def tp_handle(self) -> bytes:
         buf = C.create_string_buffer(64)
@@ -279,15 +320,15 @@ class LlmCtx:
 
     def prefill_rows(self, x_ptr: int, n: int, tokens=None, out: np.ndarray | None = None) -> int | None:
         """One pipeline stage's batched prompt over n device rows at x_ptr
-        (ecu_prefill_rows); HEAD returns the picked token."""
+        (ecu_prefill_rows); a stage with the head returns the picked token."""
         tk = None if tokens is None else np.ascontiguousarray(tokens, dtype=np.int32)
-        if out is None and self.stage == STAGE_HEAD:
+        if out is None and self.has_head:
             out = np.zeros(self.n_embd + 1, dtype=np.float32)
         rc = lib().ecu_prefill_rows(self.h, None if tk is None else _ptr(tk), int(n), C.c_void_p(int(x_ptr)),
                                     None if out is None else _ptr(out))
         if rc != 0:
             raise EngineError(last_error())
-        return int(out[self.n_embd]) if self.stage == STAGE_HEAD else None
+        return int(out[self.n_embd]) if self.has_head else None
 
     def decode_async(self, n: int) -> None:
         if lib().ecu_decode_async(self.h, int(n)) != 0:

@@ -201,6 +201,14 @@ class LoopbackExchanger(Exchanger):
             ss.wait_stream(ds)
 
 
+class LinkedExchanger(Exchanger):
+    """Linked stages (ecu_link_*): the steps hand the state and the token to
+    the next stage themselves, so a tick has nothing to carry."""
+
+    def exchange(self, msgs, stages):
+        return
+
+
 class DistExchanger(Exchanger):
     """One rank per process over torch.distributed (NCCL between GPUs, gloo
     on the host): the tick's sends and receives of this rank as one group."""
@@ -253,35 +261,45 @@ def run_ticks(sched: Schedule, stages: dict, exchanger: Exchanger, prompts=None,
 
 
 class GpuStage:
-    """One rank's stage on one GPU: per sequence a chain of engine contexts
-    [EMBED] + LAYERS(first..last) + [HEAD], forks of sequence 0's chain, all
-    enqueued on one torch stream.  Input/output buffers are zero-copy torch
-    views of the contexts' device state (ecu_state_ptr / ecu_token_ptr)."""
+    """One rank's stage on one GPU: per sequence one engine context -- a span
+    of layers first..last with the embedding folded in on the first rank and
+    the head on the last (ecu_ctx_open_span: the reference's EMBED / LAYERS /
+    HEAD stages of one node, src/shard.c:358-437, as one persistent step) --
+    forks of sequence 0's, all enqueued on one torch stream.  Input/output
+    buffers are zero-copy torch views of the contexts' device state
+    (ecu_state_ptr / ecu_token_ptr).
+
+    Linked (link_local / link_dist): each context sends its output straight
+    into the next stage's context of the same sequence from inside its step
+    (the last stage its token into the first stage's), so a tick launches
+    the steps and carries nothing.  Stages that share one GPU must then
+    share one stream (`stream`), which runs their steps in tick order: a
+    step never waits there for one that has not run."""
 
     def __init__(self, model, rank: int, n_ranks: int, first: int, last: int, n_layer: int, n_seq: int,
-                 n_ctx: int, device: int, prompts=None):
+                 n_ctx: int, device: int, prompts=None, stream=None):
         import torch
         from . import engine as E
         self.rank, self.n_ranks, self.device = rank, n_ranks, device
         self.torch = torch
         self.dev = torch.device("cuda", device)
-        base = []
-        if first == 0:
-            base.append(E.LlmCtx(model, E.STAGE_EMBED, 0, 0, n_ctx, device))
-        if first <= last:                      # (the head's GPU may hold no layer)
-            base.append(E.LlmCtx(model, E.STAGE_LAYERS, first, last, n_ctx, device))
-        if last == n_layer - 1:
-            base.append(E.LlmCtx(model, E.STAGE_HEAD, 0, 0, n_ctx, device))
+        # the first rank embeds, the last runs the head (first > last: the
+        # head's GPU holds no layer, and the rank before it ends at the last
+        # layer without the head)
+        self.has_embed, self.has_head = rank == 0, rank == n_ranks - 1
+        flags = (E.SPAN_EMBED if self.has_embed else 0) | (E.SPAN_HEAD if self.has_head else 0)
+        base = [E.LlmCtx(model, E.STAGE_SPAN, first, last, n_ctx, device, span=flags)]
         self.chains = [base] + [[c.fork() for c in base] for _ in range(n_seq - 1)]
         self.n_embd = base[0].n_embd
-        self.has_embed, self.has_head = first == 0, last == n_layer - 1
-        self.stream = torch.cuda.Stream(device=self.dev)
+        self.stream = stream if stream is not None else torch.cuda.Stream(device=self.dev)
+        self.linked = False
         self._state = [[device_view(c.state_ptr(), self.n_embd + 1, "<f4", device) for c in ch]
                        for ch in self.chains]
         self._token = [[device_view(c.token_ptr(), 1, "<i4", device) for c in ch] for ch in self.chains]
-        self.prompts = None
+        self.prompts = self.host_prompts = None
         if prompts is not None:
             self.prompts = torch.tensor(prompts, dtype=torch.int32, device=self.dev)
+            self.host_prompts = [list(map(int, q)) for q in prompts]
         self.history = None
 
     def record_tokens(self, n_steps: int):
@@ -296,8 +314,19 @@ class GpuStage:
         return self._token[s][0] if kind == "token" else self._state[s][0][: self.n_embd]
 
     def set_token(self, s: int, k: int):
+        if self.linked:
+            self.feed(s, self.host_prompts[s][k])
+            return
         with self.torch.cuda.stream(self.stream):
             self._token[s][0].copy_(self.prompts[s, k: k + 1])
+
+    def feed(self, s: int, token: int):
+        """Sequence s's next input token from the host (first stage)."""
+        if self.linked:
+            self.chains[s][0].link_feed(int(token), self.stream.cuda_stream)
+        else:
+            with self.torch.cuda.stream(self.stream):
+                self._token[s][0].fill_(int(token))
 
     def run(self, s: int, k: int):
         torch = self.torch
@@ -326,6 +355,37 @@ class GpuStage:
         for ch in reversed(self.chains):
             for c in ch:
                 c.close()
+
+
+def link_local(stages: dict) -> None:
+    """Link the stages of this process into a ring (rank r's contexts send
+    to rank r + 1's of the same sequence, the last rank's head its token to
+    rank 0): ecu_link_next_local / ecu_link_input."""
+    ranks = sorted(stages)
+    for i, r in enumerate(ranks):
+        nxt = stages[ranks[(i + 1) % len(ranks)]]
+        for s, ch in enumerate(stages[r].chains):
+            ch[0].link_next(nxt.chains[s][0])
+    for st in stages.values():
+        for ch in st.chains:
+            ch[0].link_input()
+        st.linked = True
+
+
+def link_dist(st: "GpuStage", rank: int, world: int) -> None:
+    """link_local across processes (one rank per GPU): every rank's context
+    handles to every rank (torch.distributed), then each rank maps the next
+    rank's (ecu_link_handle / ecu_link_next)."""
+    import torch.distributed as dist
+    mine = [ch[0].link_handle() for ch in st.chains]
+    every = [None] * world
+    dist.all_gather_object(every, mine)
+    nxt = every[(rank + 1) % world]
+    for s, ch in enumerate(st.chains):
+        ch[0].link_next(nxt[s])
+        ch[0].link_input()
+    st.linked = True
+    dist.barrier()
 
 
 def prefill_local(stages: dict, seq: int, prompt, send_rows=None, recv_rows=None, share_token=None) -> int | None:
@@ -357,9 +417,7 @@ def prefill_local(stages: dict, seq: int, prompt, send_rows=None, recv_rows=None
     if share_token is not None:
         tok = share_token(tok)
     if 0 in stages:
-        st0 = stages[0]
-        with torch.cuda.stream(st0.stream):
-            st0._token[seq][0].fill_(int(tok))
+        stages[0].feed(seq, int(tok))
     return tok
 
 
@@ -414,9 +472,38 @@ def bench_main(args, rank: int, world: int, local: int, B) -> int:
                       prompts=prompts if rank == 0 else None)
         del buf
         torch.cuda.empty_cache()
-        ex = DistExchanger(rank)
+        linked = getattr(args, "hops", "link") == "link"
+        if linked:
+            # every step hands its output to the next GPU itself: no
+            # exchange between ticks, the hosts only launch
+            link_dist(st, rank, world)
+            ex = LinkedExchanger()
+        else:
+            ex = DistExchanger(rank)
         stages = {rank: st}
+        dev = st.dev
         dist.barrier()
+
+        def send_rows(r, rows):
+            dist.send(rows, r + 1)
+
+        def recv_rows(r, rows):
+            dist.recv(rows, r - 1)
+
+        def share_token(tok):
+            t = torch.tensor([tok if rank == world - 1 else 0], dtype=torch.int64, device=dev)
+            dist.broadcast(t, world - 1)
+            return int(t.item())
+
+        def prefill(seqs):
+            """Each sequence's prompt through the stages as one batch per
+            stage; returns the first generated tokens."""
+            firsts = []
+            for q in seqs:
+                firsts.append(prefill_local(stages, q, prompts[q], send_rows, recv_rows, share_token))
+                torch.cuda.synchronize(local)
+            dist.barrier()
+            return firsts
 
         def timed(sched, t0, t1, host_tokens=False):
             """Device time of ticks [t0, t1) on this rank, max over ranks (ms)."""
@@ -442,26 +529,31 @@ def bench_main(args, rank: int, world: int, local: int, B) -> int:
             torch.cuda.synchronize(local)
             host_s = time.perf_counter() - h0
             dist.barrier()
-            ms = torch.tensor([ev0.elapsed_time(ev1), host_s * 1e3], dtype=torch.float64, device=st.dev)
+            ms = torch.tensor([ev0.elapsed_time(ev1), host_s * 1e3], dtype=torch.float64, device=dev)
             dist.all_reduce(ms, op=dist.ReduceOp.MAX)
             return float(ms[0]), float(ms[1])
 
+        n = args.prompt
         # (1) one sequence alone: the batch-1 latency through all stages
-        s1 = Schedule(world, 1, args.prompt + args.warmup + args.steps, n_prompt=args.prompt)
-        w0 = s1.step_ticks(args.prompt + args.warmup)[0]
+        t_pf = time.perf_counter()
+        prefill([0])
+        pf_s = time.perf_counter() - t_pf
+        s1 = Schedule(world, 1, args.warmup + args.steps, n_prompt=0, first_step=n)
+        w0 = s1.step_ticks(n + args.warmup)[0]
         run_ticks(s1, stages, ex, t0=0, t1=w0)
         ms1, _ = timed(s1, w0, s1.n_ticks)
         b1_tps = args.steps / (ms1 / 1e3)
         st.sync()
         st.reset()
 
-        # (2) n_seq interleaved sequences: prompt, warm-up, timed, end-to-end
-        total = args.prompt + args.warmup + 2 * args.steps
-        sched = Schedule(world, n_seq, total, n_prompt=args.prompt)
+        # (2) n_seq interleaved sequences: prompts, warm-up, timed, end-to-end
+        dec = args.warmup + 2 * args.steps
+        firsts = prefill(range(n_seq))
+        sched = Schedule(world, n_seq, dec, n_prompt=0, first_step=n)
         if st.has_head:
-            st.record_tokens(total)
-        ta = sched.step_ticks(args.prompt + args.warmup)[0]
-        tb = sched.step_ticks(args.prompt + args.warmup + args.steps)[0]
+            st.record_tokens(n + dec)
+        ta = sched.step_ticks(n + args.warmup)[0]
+        tb = sched.step_ticks(n + args.warmup + args.steps)[0]
         run_ticks(sched, stages, ex, t0=0, t1=ta)
         l0 = E.kernel_launches()
         clocks = B.ClockSampler(local)
@@ -472,22 +564,24 @@ def bench_main(args, rank: int, world: int, local: int, B) -> int:
         clk = clocks.stop() if rank == 0 else None
         _, e2e_ms = timed(sched, tb, sched.n_ticks, host_tokens=True)
         st.sync()
-        lt = torch.tensor([launches], dtype=torch.int64, device=st.dev)
+        lt = torch.tensor([launches], dtype=torch.int64, device=dev)
         dist.all_reduce(lt)
         tps = n_seq * args.steps / (ms / 1e3)
         # tokens completed in the end-to-end window: every step after tb
-        e2e_steps = total - (args.prompt + args.warmup + args.steps)
+        e2e_steps = dec - (args.warmup + args.steps)
         e2e = n_seq * e2e_steps / (e2e_ms / 1e3)
-        # sequence 0's greedy tokens through the pipeline (the last stage's
-        # record) against one GPU's FULL context on the same prompt
-        hist = st.history[0].clone() if st.has_head else torch.zeros(total, dtype=torch.int32, device=st.dev)
+        # sequence 0's greedy tokens through the pipeline (the first from the
+        # staged prompt, then the last stage's record) against one GPU's FULL
+        # context on the same prompt (ecu_prefill, then per-token steps)
+        hist = st.history[0].clone() if st.has_head else torch.zeros(n + dec, dtype=torch.int32, device=dev)
         dist.broadcast(hist, src=world - 1)
+        dist.barrier()             # every rank's steps are over: no link writes into freed memory
         st.close()
         pp_check = None
         if rank == 0:
-            n_gen = total - args.prompt + 1
-            ref = B.one_gpu_tokens(model, spec, args, local, n_gen, prompts[0])
-            got = [int(t) for t in hist[args.prompt - 1:].cpu().tolist()]
+            n_gen = dec + 1
+            ref = B.one_gpu_tokens(model, spec, args, local, n_gen, prompts[0], prefill=True)
+            got = [int(firsts[0])] + [int(t) for t in hist[n: n + dec].cpu().tolist()]
             pp_check = {"tokens_match_one_gpu": got == ref, "tokens_checked": n_gen, "sequence": 0}
         dist.barrier()
         # (3) the other partition on the same GPUs: batch-1 tensor parallel
@@ -506,8 +600,12 @@ def bench_main(args, rank: int, world: int, local: int, B) -> int:
                 "vs_baseline": None, "dtype": "q4_0 codes x int8 digit planes, fp32 accumulate",
                 "data": "synthetic: seeded N(0,0.02) weights quantised to Q4_0/Q8_0 on the GPU, random prompts",
                 "config": {"workload": f"llama3-8b-shape Q4_0 decode, layer pipeline over {world} GPUs "
-                                       f"(shard.c stage layout, NCCL send/recv hops), {n_seq} interleaved "
-                                       f"sequences; a step = one token of every sequence",
+                                       f"(one span context per GPU and sequence, "
+                                       + ("linked steps: each writes its output into the next GPU's step "
+                                          "over NVLink" if linked else "NCCL send/recv hops between steps")
+                                       + f"), {n_seq} interleaved sequences; a step = one token of every "
+                                         f"sequence; prompts {n} tokens each as one batch per stage",
+                           "hops": "link" if linked else "nccl",
                            "stages": [list(p) for p in plan], "split": args.split,
                            "sequences": n_seq, "prompt_tokens": args.prompt, "n_ctx": args.n_ctx,
                            "l2": "inputs larger than L2 (4.49 GB of weights per token)"},
@@ -517,10 +615,13 @@ def bench_main(args, rank: int, world: int, local: int, B) -> int:
                 "pp_batch1": {"value": round(b1_tps, 2), "unit": "tokens/s",
                               "frac": round(bpt * b1_tps / 1e9 / peak, 4),
                               "note": "one sequence: one stage busy at a time"},
+                "prefill_one_sequence": {"tokens": n, "s": round(pf_s, 3),
+                                         "note": "ecu_prefill_rows per stage, rows over NCCL send/recv; wall "
+                                                 "time with barriers"},
                 "e2e": {"value": round(e2e, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 4 * n_seq,
-                        "api": "ecu_step_dev chain per stage; the last stage copies every step's tokens to "
-                               "host and waits for them"},
+                        "api": "ecu_step_dev per stage and sequence (the token fed back on the devices); the "
+                               "last stage copies every step's tokens to the host and waits for them"},
                 "gpu_launches": int(lt.item()),
                 "clocks": clk,
                 "pp_parity": pp_check,
@@ -587,6 +688,9 @@ def bench_long_main(args, rank: int, world: int, local: int, B) -> int:
             dist.broadcast(t, world - 1)
             return int(t.item())
 
+        linked = getattr(args, "hops", "link") == "link"
+        if linked:
+            link_dist(st, rank, world)
         dist.barrier()
         t0 = time.perf_counter()
         first_tok = prefill_local({rank: st}, 0, prompt, send_rows, recv_rows, share_token)
@@ -594,8 +698,8 @@ def bench_long_main(args, rank: int, world: int, local: int, B) -> int:
         pf_s = time.perf_counter() - t0
 
         n = len(prompt)
-        sched = Schedule(world, 1, args.warmup + 2 * args.steps, n_prompt=n, first_step=n)
-        ex = DistExchanger(rank)
+        sched = Schedule(world, 1, args.warmup + 2 * args.steps, n_prompt=0, first_step=n)
+        ex = LinkedExchanger() if linked else DistExchanger(rank)
         stages = {rank: st}
         ta = sched.step_ticks(n + args.warmup)[0]
         tb = sched.step_ticks(n + args.warmup + args.steps)[0]
@@ -652,7 +756,9 @@ def bench_long_main(args, rank: int, world: int, local: int, B) -> int:
                 "data": "synthetic: seeded N(0,0.02) weights quantised on the GPU, each rank its stage's tensors; "
                         "random prompt",
                 "config": {"workload": B.workload_text(spec, args.model) + f", KV fp32 {args.n_ctx}, layer pipeline "
-                                       f"over {world} GPUs, batch 1",
+                                       f"over {world} GPUs, batch 1, "
+                                       + ("linked steps over NVLink" if linked else "NCCL send/recv hops"),
+                           "hops": "link" if linked else "nccl",
                            "stages": [list(p_) for p_ in plan], "split": args.split, "prompt_tokens": n,
                            "decode_positions": [n + args.warmup, n + args.warmup + args.steps - 1],
                            "l2": f"inputs larger than L2 ({bpt / 1e9:.1f} GB per token)"},
@@ -673,6 +779,7 @@ def bench_long_main(args, rank: int, world: int, local: int, B) -> int:
                 "setup_s": {"stage_model_build_and_upload": round(t_b, 1)},
             }
             print(json.dumps(line), flush=True)
+        dist.barrier()             # every rank's steps are over: no link writes into freed memory
         st.close()
         dist.barrier()
     finally:

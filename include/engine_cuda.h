@@ -35,8 +35,14 @@ enum {
     ECU_STAGE_EMBED  = 0,   /* src/engine.h:24 LLM_STAGE_EMBED  */
     ECU_STAGE_LAYERS = 1,   /* src/engine.h:25 LLM_STAGE_LAYERS */
     ECU_STAGE_HEAD   = 2,   /* src/engine.h:26 LLM_STAGE_HEAD   */
-    ECU_STAGE_FULL   = 3    /* new: embed + all layers + head on one device */
+    ECU_STAGE_FULL   = 3,   /* new: embed + all layers + head on one device */
+    ECU_STAGE_SPAN   = 4    /* new: a layer range with the embedding and/or the
+                               head folded in (ecu_ctx_open_span) */
 };
+
+/* ecu_ctx_open_span flags */
+#define ECU_SPAN_EMBED 1u   /* the step starts from a token: embedding row first */
+#define ECU_SPAN_HEAD  2u   /* the step ends with the output head: argmax token */
 
 typedef struct ecu_model ecu_model;   /* host view of a GGUF file (borrowed bytes) */
 typedef struct ecu_ctx   ecu_ctx;     /* one stage resident on one device           */
@@ -86,6 +92,16 @@ size_t ecu_ctx_bytes(const ecu_model *m, int stage, int first, int last, int n_c
  * src/engine.h:79).  The same geometry and error rules as the reference. */
 int  ecu_ctx_open(ecu_ctx **out, const ecu_model *m, int stage, int first, int last, int n_ctx,
                   int device, char *err, size_t errlen);
+/* A pipeline stage that folds the reference's EMBED / LAYERS / HEAD stages
+ * of one node into one context (src/shard.c:358-437 gives a node's layer
+ * range; its entry node also embeds, its exit node also runs the head):
+ * layers first..last (first > last: none) plus the embedding and/or the
+ * head by `flags`.  One persistent step per token runs all of it.  Forward
+ * contract: input a token with ECU_SPAN_EMBED, else a state in out;
+ * output the state, plus out[n_embd] = the argmax with ECU_SPAN_HEAD.  The
+ * position advances every step.  ecu_ctx_info reports ECU_STAGE_SPAN. */
+int  ecu_ctx_open_span(ecu_ctx **out, const ecu_model *m, int first, int last, unsigned flags, int n_ctx,
+                       int device, char *err, size_t errlen);
 void ecu_ctx_close(ecu_ctx *c);
 int  ecu_ctx_info(const ecu_ctx *c, ecu_info *info);
 /* How the context runs a step: "persistent" (one cooperative kernel per
@@ -166,6 +182,34 @@ int  ecu_tp_connect(ecu_ctx *c, const unsigned char *handles);
 /* out4 = {rank, world, first vocabulary row, end row} of this context's head
  * slice (ecu_get_logits returns that slice). */
 int  ecu_tp_slice(const ecu_ctx *c, int *out4);
+/* ---- pipeline links: the stages of a layer pipeline (one context per GPU
+ * and sequence, typically spans) hand the state and the token to each
+ * other inside their persistent steps, as tagged words written straight
+ * into the next stage's memory over NVLink, instead of a host or NCCL hop
+ * between steps (the reference sends them over UDP, src/shard.c:664-723).
+ * Each stage's step then only needs launching, in the same sequence order
+ * on every GPU: a step waits (bounded, ~2 s, then the status reports a
+ * timeout) until its input has arrived.  Contexts with the persistent step
+ * only, not tensor-parallel ones; every stage of a pipeline opened from the
+ * same model.  Use ecu_step_dev on linked contexts. */
+#define ECU_LINK_HANDLE_BYTES 64
+/* This context's shareable handle (ECU_LINK_HANDLE_BYTES), for the stage
+ * before it (another process: CUDA IPC). */
+int  ecu_link_handle(ecu_ctx *c, unsigned char *out);
+/* Send this context's output to the stage whose handle this is: its output
+ * state, or with the head its argmax token (to the first stage). */
+int  ecu_link_next(ecu_ctx *c, const unsigned char *handle);
+/* The same for a context of this process (next may be on the same device;
+ * then its steps must follow this one's on one stream). */
+int  ecu_link_next_local(ecu_ctx *c, ecu_ctx *next);
+/* This context's input arrives over a link: the state for a stage without
+ * the embedding, else the token.  Once set, ecu_forward is refused. */
+int  ecu_link_input(ecu_ctx *c);
+/* A linked first stage's input token for its next step from the host (the
+ * token the prompt's last position picked), enqueued on `stream` (NULL =
+ * the context's stream) before that step. */
+int  ecu_link_feed(ecu_ctx *c, int token, void *stream);
+
 /* Greedy decode on a FULL context without host round trips: feeds
  * prompt[0..n_prompt) token by token, then generates n_gen tokens, each one
  * fed back on the device.  out_tokens receives the n_gen generated ids.
@@ -193,7 +237,8 @@ int  ecu_prefill(ecu_ctx *c, const int *tokens, int n, float *out);
  * stage's layers in place (ecu_prefill's kernels), the stage's KV cache
  * gets positions pos..pos+n-1 and its position advances by n.  HEAD: the
  * last row of x through the head, out = normed state + picked token as
- * ecu_forward's (tokens may be NULL).  Every stage's rows agree bit for bit
+ * ecu_forward's (tokens may be NULL).  SPAN: those of its parts in that
+ * order, the position advancing by n.  Every stage's rows agree bit for bit
  * with a FULL context's ecu_prefill of the same prompt.  Synchronises the
  * context's stream before returning. */
 int  ecu_prefill_rows(ecu_ctx *c, const int *tokens, int n, float *x, float *out);

@@ -53,6 +53,52 @@ def main():
                 (out / "ok").write_text("ok\n")
         st.close()
         dist.barrier()
+
+        # linked: the prompts as one batch per stage (rows over NCCL), then
+        # every step hands its output to the other GPU's step itself
+        st = P.GpuStage(m, rank, world, a, b, s.n_layer, n_seq, n_ctx, local, prompts=prompts)
+        P.link_dist(st, rank, world)
+        dev = torch.device("cuda", local)
+
+        def send_rows(r, rows):
+            dist.send(rows, r + 1)
+
+        def recv_rows(r, rows):
+            dist.recv(rows, r - 1)
+
+        def share_token(tok):
+            t = torch.tensor([tok if rank == world - 1 else 0], dtype=torch.int64, device=dev)
+            dist.broadcast(t, world - 1)
+            return int(t.item())
+
+        firsts = [P.prefill_local({rank: st}, q, prompts[q], send_rows, recv_rows, share_token) for q in range(n_seq)]
+        n_dec = n_gen - 1
+        if st.has_head:
+            st.record_tokens(n_prompt + n_dec)
+        dist.barrier()
+        S = P.Schedule(world, n_seq, n_dec, n_prompt=0, first_step=n_prompt)
+        P.run_ticks(S, {rank: st}, P.LinkedExchanger())
+        st.sync()
+        if st.has_head:
+            hist = st.history.cpu().tolist()
+            ok2 = True
+            for q in range(n_seq):
+                c = E.LlmCtx(m, E.STAGE_FULL, n_ctx=n_ctx, device=local)
+                want = [c.prefill(prompts[q])]
+                o = torch.zeros(s.n_embd + 1, dtype=torch.float32).numpy()
+                while len(want) < n_gen:
+                    assert c.forward(want[-1], o) == 0
+                    want.append(int(o[s.n_embd]))
+                c.close()
+                got = [firsts[q]] + hist[q][n_prompt: n_prompt + n_dec]
+                print(f"linked seq {q}: pipeline {got} full {want}", flush=True)
+                ok2 = ok2 and got == want
+            if ok2:
+                (out / "ok_linked").write_text("ok\n")
+            ok = ok and ok2
+        dist.barrier()             # no step writes into another rank's memory any more
+        st.close()
+        dist.barrier()
     finally:
         dist.destroy_process_group()
     return 0 if ok else 1

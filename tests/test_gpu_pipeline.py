@@ -31,6 +31,20 @@ def full_greedy(eng, m, prompt, n_gen, n_ctx):
     return toks, logits
 
 
+def full_prefill_greedy(eng, m, s, prompt, n_gen, n_ctx):
+    """A FULL context: the prompt as one batch (ecu_prefill), then greedy
+    steps; the tokens and the last step's logits."""
+    c = eng.LlmCtx(m, eng.STAGE_FULL, n_ctx=n_ctx)
+    toks = [c.prefill(prompt)]
+    out = np.zeros(s.n_embd + 1, dtype=np.float32)
+    while len(toks) < n_gen:
+        assert c.forward(toks[-1], out) == 0
+        toks.append(int(out[s.n_embd]))
+    logits = c.logits()
+    c.close()
+    return toks, logits
+
+
 @pytest.mark.parametrize("n_ranks,n_seq,head_alone", [(2, 1, False), (2, 3, False), (3, 2, False),
                                                        (4, 4, False), (3, 3, True)])
 def test_loopback_pipeline_matches_full_context(eng, model_buf, n_ranks, n_seq, head_alone):
@@ -102,9 +116,55 @@ def test_fork_shares_weights_and_keeps_own_cache(eng, model_buf):
     ref.close()
 
 
+@pytest.mark.parametrize("n_ranks,n_seq,head_alone", [(2, 1, False), (2, 3, False), (3, 4, False),
+                                                       (3, 2, True)])
+def test_linked_loopback_pipeline(eng, model_buf, n_ranks, n_seq, head_alone):
+    """Linked stages (each step writes its output into the next stage's
+    tagged words, the last stage's head its token into the first stage's) on
+    one GPU, all stages on one stream in tick order: the prompts through the
+    stages as batches (prefill_local), then greedy steps with no exchange
+    between ticks -- the FULL context's tokens and final logits bit for bit,
+    and again after a reset."""
+    key, over = "mini-q4", {"n_layer": 4}
+    s = synth.spec(key, **over)
+    m = eng.GgufModel(model_buf(key, **over))
+    n_prompt, n_gen, n_ctx = 6, 10, 64
+    prompts = [synth.prompt_tokens(n_prompt, s.n_vocab, seed=41 + q) for q in range(n_seq)]
+    plan = P.split_stages(s.n_layer, n_ranks)
+    if head_alone:
+        plan = P.split_stages(s.n_layer, n_ranks - 1) + [(s.n_layer, s.n_layer - 1)]
+    stream = torch.cuda.Stream()
+    stages = {r: P.GpuStage(m, r, n_ranks, a, b, s.n_layer, n_seq, n_ctx, 0, prompts=prompts, stream=stream)
+              for r, (a, b) in enumerate(plan)}
+    P.link_local(stages)
+    last = stages[n_ranks - 1]
+    wants = [full_prefill_greedy(eng, m, s, prompts[q], n_gen, n_ctx) for q in range(n_seq)]
+    for _run in range(2):
+        firsts = [P.prefill_local(stages, q, prompts[q]) for q in range(n_seq)]
+        n_steps = n_gen - 1
+        last.record_tokens(n_prompt + n_steps)
+        S = P.Schedule(n_ranks, n_seq, n_steps, n_prompt=0, first_step=n_prompt)
+        P.run_ticks(S, stages, P.LinkedExchanger())
+        for st in stages.values():
+            st.sync()
+        hist = last.history.cpu().numpy()
+        for q in range(n_seq):
+            want, want_logits = wants[q]
+            got = [firsts[q]] + [int(t) for t in hist[q, n_prompt: n_prompt + n_steps]]
+            assert got == want, (q, got, want)
+            got_logits = last.chains[q][-1].logits()
+            assert np.array_equal(got_logits.view(np.uint32), want_logits.view(np.uint32))
+        for st in stages.values():
+            st.reset()
+    for st in stages.values():
+        st.close()
+
+
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 def test_nccl_pipeline_two_gpus(tmp_path):
-    """bench.py's pipeline path at a small size over two real ranks."""
+    """bench.py's pipeline path at a small size over two real ranks: NCCL
+    hops with the prompts through the ticks, then linked steps after the
+    prompts as batches."""
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
            "--master-addr=127.0.0.1", "--master-port=29531", str(ROOT / "tests" / "pipeline_ranks.py"),
@@ -112,6 +172,7 @@ def test_nccl_pipeline_two_gpus(tmp_path):
     r = subprocess.run(["timeout", "-k", "30", "600"] + cmd, env=env, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
     assert (tmp_path / "ok").exists()
+    assert (tmp_path / "ok_linked").exists(), r.stdout[-2000:]
 
 
 def test_prefill_through_stages_matches_full_context(eng, oracle_port, model_buf):

@@ -131,6 +131,13 @@ def test_ctx_open_geometry_errors(model_buf):
         engine.LlmCtx(m, engine.STAGE_LAYERS, 2, 9)
     with pytest.raises(engine.EngineError, match="unknown stage"):
         engine.LlmCtx(m, 7)
+    # spans: a range inside the model, known flags, something to do
+    with pytest.raises(engine.EngineError, match="outside the model"):
+        engine.LlmCtx(m, engine.STAGE_SPAN, 1, 5, span=engine.SPAN_HEAD)
+    with pytest.raises(engine.EngineError, match="span flags"):
+        engine.LlmCtx(m, engine.STAGE_SPAN, 0, 0, span=8)
+    with pytest.raises(engine.EngineError, match="needs the embedding or the head"):
+        engine.LlmCtx(m, engine.STAGE_SPAN, 1, 0, span=0)
 
 
 def test_ctx_bytes_q4k_segments_host_only(model_buf):

@@ -1131,7 +1131,10 @@ static int mega_setup(ecu_ctx *c)
     un = std::max(un, kv_off + (size_t)att_nsl * att_sub * row4);
     // the attention's position-group sums (at the union's base): [512 / (hd/4)][n_rep][hd] floats
     un = std::max(un, (size_t)(MEGA_THREADS / (hd / 4)) * g.n_rep * hd * sizeof(float));
-    int n_split = std::min(MEGA_MAX_SPLIT, grid / tp.nkv);
+    // (counted over all KV heads of the model, so that a tensor-parallel
+    // rank splits each head's positions exactly as one GPU does: the merge
+    // then adds the same partials in the same order, bit for bit)
+    int n_split = std::min(MEGA_MAX_SPLIT, grid / g.n_head_kv);
     if (const char *se = getenv("ECU_MEGA_SPLIT")) n_split = std::max(1, std::min(n_split, atoi(se)));
     n_split = std::max(1, std::min(n_split, g.n_ctx));
 

@@ -274,7 +274,11 @@ class GpuStage:
     (the last stage its token into the first stage's), so a tick launches
     the steps and carries nothing.  Stages that share one GPU must then
     share one stream (`stream`), which runs their steps in tick order: a
-    step never waits there for one that has not run."""
+    step never waits there for one that has not run.  Across processes, a
+    rank synchronises its device before any collective: a persistent step
+    holds every SM, so a collective's kernel waiting on this GPU for another
+    rank would keep this rank's next step from launching while the other
+    rank's step waits for that step's output."""
 
     def __init__(self, model, rank: int, n_ranks: int, first: int, last: int, n_layer: int, n_seq: int,
                  n_ctx: int, device: int, prompts=None, stream=None):
@@ -508,8 +512,11 @@ def bench_main(args, rank: int, world: int, local: int, B) -> int:
         def timed(sched, t0, t1, host_tokens=False):
             """Device time of ticks [t0, t1) on this rank, max over ranks (ms)."""
             ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            dist.barrier()
+            # (linked steps still in flight finish before any collective: a
+            # collective's kernel holding an SM would keep this GPU's next
+            # step, which another GPU's step waits for, from launching)
             torch.cuda.synchronize(local)
+            dist.barrier()
             h0 = time.perf_counter()
             ev0.record(st.stream)
             if host_tokens and st.has_head:
@@ -708,8 +715,8 @@ def bench_long_main(args, rank: int, world: int, local: int, B) -> int:
         if rank == 0:
             clocks.start()
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(local)          # (no collective while linked steps are in flight)
         dist.barrier()
-        torch.cuda.synchronize(local)
         l0 = E.kernel_launches()
         ev0.record(st.stream)
         run_ticks(sched, stages, ex, t0=ta, t1=tb)
@@ -733,8 +740,8 @@ def bench_long_main(args, rank: int, world: int, local: int, B) -> int:
                 st.stream.synchronize()
                 toks.append(int(pinned.item()))
 
-        dist.barrier()
         torch.cuda.synchronize(local)
+        dist.barrier()
         h0 = time.perf_counter()
         run_ticks(sched, stages, ex, t0=tb, t1=sched.n_ticks, on_tick=tick)
         st.sync()

@@ -2373,6 +2373,43 @@ int ecu_generate(ecu_ctx *c, const int *prompt, int n_prompt, int n_gen, int *ou
     return 0;
 }
 
+int ecu_profile_cta_ns(ecu_ctx *c, unsigned long long *out, size_t n_words, int *grid, char *kinds, size_t kinds_len)
+{
+    if (!c || !out) return -1;
+    if (grid) *grid = c->mega_grid;
+    if (!c->mega) { ecu_set_error(nullptr, 0, "per-CTA phase times need the persistent step"); return -1; }
+    const size_t np = (size_t)c->margs.n_ph, need = (np + 1) * (size_t)c->mega_grid;
+    if (n_words < need) {
+        ecu_set_error(nullptr, 0, "ecu_profile_cta_ns: %zu words needed", need);
+        return -1;
+    }
+    if (c->pos >= c->g.n_ctx) { ecu_set_error(nullptr, 0, "context exhausted"); return -1; }
+    cudaSetDevice(c->device);
+    unsigned long long *d = nullptr;
+    CK(cudaMalloc(&d, need * sizeof(unsigned long long)));
+    StepState *slot = c->h_st + (c->pos % c->n_hslots);
+    slot->pos = c->pos;
+    cudaError_t e = cudaMemcpyAsync(&c->st->pos, &slot->pos, sizeof(int), cudaMemcpyHostToDevice, c->stream);
+    c->margs.cta_ns = d;
+    const int rc = e == cudaSuccess ? mega_launch(c, c->stream, nullptr) : -1;
+    c->margs.cta_ns = nullptr;
+    g_launches += 1;
+    if (rc == 0) {
+        if (r_pos(c)) c->pos++;
+        if (r_head(c)) c->have_logits = true;
+    }
+    const int st = rc == 0 ? check_status(c) : -1;
+    if (st == 0) e = cudaMemcpy(out, d, need * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
+    cudaFree(d);
+    if (st != 0 || e != cudaSuccess) return -1;
+    if (kinds && kinds_len) {
+        std::string k;
+        for (size_t i = 0; i < c->ph_kind.size(); i++) k += (i ? "," : "") + std::string(c->ph_kind[i]);
+        snprintf(kinds, kinds_len, "%s", k.c_str());
+    }
+    return (int)np;
+}
+
 int ecu_profile_steps(ecu_ctx *c, int n_steps, ecu_kprof *out, int max_kinds)
 {
     if (!c || n_steps < 1 || !out || max_kinds < 1) return -1;

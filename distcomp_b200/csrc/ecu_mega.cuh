@@ -129,6 +129,8 @@ struct MegaArgs {
     unsigned long long *link_tok;   // the head's argmax -> the first stage's token word (or null)
     unsigned long long *tok_ll;     // this context's token word (a linked embedding reads it)
     int              link_in;       // the embedding waits for its token in tok_ll
+    unsigned long long *cta_ns;     // optional, [n_ph + 1][grid]: every CTA's time at the start and at
+                                    // the end of each phase (the skew between CTAs at phase boundaries)
     float            eps, kscale;
 };
 
@@ -1393,6 +1395,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a)
         a.phase_ns[0] = globaltimer_ns();
         a.phase_clk[0] = clock64();
     }
+    if (a.cta_ns && threadIdx.x == 0) a.cta_ns[blockIdx.x] = globaltimer_ns();
     RingPos rpos{0, 0u};
     int att_sb0 = 0, att_sb1 = 0, merges = 0;
     for (int p = 0; p < a.n_ph; p++) {
@@ -1424,6 +1427,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a)
             a.phase_ns[p + 1] = globaltimer_ns();
             a.phase_clk[p + 1] = clock64();
         }
+        if (a.cta_ns && threadIdx.x == 0) a.cta_ns[(size_t)(p + 1) * gridDim.x + blockIdx.x] = globaltimer_ns();
     }
     // ring and K/V copies still in flight (none, unless a wait gave up) land
     // before this CTA may exit

@@ -112,6 +112,8 @@ SIGNATURES = [
     ("ecu_matvec_stream_bench", C.c_int, [C.c_uint, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
                                           C.c_int, C.c_int, C.c_int, C.POINTER(C.c_double)]),
     ("ecu_profile_steps", C.c_int, [C.c_void_p, C.c_int, C.POINTER(EcuKprof), C.c_int]),
+    ("ecu_profile_cta_ns", C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.POINTER(C.c_int), C.c_char_p,
+                                     C.c_size_t]),
     ("ecu_last_error", C.c_char_p, []),
     ("ecu_kernel_launches", C.c_uint64, []),
     ("ecu_version", C.c_char_p, []),
@@ -279,6 +281,19 @@ class LlmCtx:
     def link_feed(self, token: int, stream: int | None = None) -> None:
         if lib().ecu_link_feed(self.h, int(token), C.c_void_p(stream) if stream else None) != 0:
             raise EngineError(last_error())
+
+    def cta_times(self):
+        """One persistent step with every CTA's phase start/end times:
+        (phase names, int64 array [phases + 1, grid] of ns)."""
+        buf = np.zeros(4096 * 1024, dtype=np.uint64)
+        kinds = C.create_string_buffer(65536)
+        grid = C.c_int(0)
+        n = lib().ecu_profile_cta_ns(self.h, _ptr(buf), buf.size, C.byref(grid), kinds, 65536)
+        if n < 0:
+            raise EngineError(last_error())
+        names = kinds.value.decode().split(",")
+        g = grid.value
+        return names, buf[: (n + 1) * g].reshape(n + 1, g).astype(np.int64)
 
     def tp_handle(self) -> bytes:
         buf = C.create_string_buffer(64)

@@ -338,6 +338,15 @@ typedef struct {
                                  file + vectors read and written                 */
 } ecu_kprof;
 
+/* One persistent step with every CTA's time (globaltimer ns) at the start
+ * and at the end of each phase: out[(p + 1) * grid + cta] = the end of
+ * phase p, out[cta] = the start; n_words >= (phases + 1) * grid (*grid =
+ * the CTA count, the SM count).  kinds (optional) receives the phases'
+ * names, comma-separated.  Returns the number of phases, or -1.  The
+ * position advances as in a step.  For measuring the CTAs' skew at phase
+ * boundaries. */
+int  ecu_profile_cta_ns(ecu_ctx *c, unsigned long long *out, size_t n_words, int *grid, char *kinds,
+                        size_t kinds_len);
 /* Run n_steps decode steps of a FULL (or LAYERS) context without the graph,
  * with a pair of CUDA events around every kernel on the context's stream,
  * and aggregate the durations per kernel kind into out[0..max_kinds).  The

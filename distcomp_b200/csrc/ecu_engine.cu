@@ -1361,8 +1361,10 @@ static int mega_setup(ecu_ctx *c)
     a.stage_bytes = stage_bytes;
     a.att_sub = att_sub;
     a.att_nsl = att_nsl;
+    // ECU_MEGA_ATT_L2: 0 no L2 warm-up of the K/V rows, 1 at the end of the
+    // Q/K/V phase, 2 (default) at its start
     const char *al2 = getenv("ECU_MEGA_ATT_L2");
-    a.att_l2 = (al2 && al2[0] == '0') ? 0 : 1;
+    a.att_l2 = (al2 && (al2[0] == '0' || al2[0] == '1')) ? al2[0] - '0' : 2;
     a.att_early = kv_early ? 1 : 0;
     a.stall_phase = -1;
     a.kv_off = (unsigned)kv_off;
@@ -2378,7 +2380,7 @@ int ecu_profile_cta_ns(ecu_ctx *c, unsigned long long *out, size_t n_words, int 
     if (!c || !out) return -1;
     if (grid) *grid = c->mega_grid;
     if (!c->mega) { ecu_set_error(nullptr, 0, "per-CTA phase times need the persistent step"); return -1; }
-    const size_t np = (size_t)c->margs.n_ph, need = (np + 1) * (size_t)c->mega_grid;
+    const size_t np = (size_t)c->margs.n_ph, need = (np + 5) * (size_t)c->mega_grid;
     if (n_words < need) {
         ecu_set_error(nullptr, 0, "ecu_profile_cta_ns: %zu words needed", need);
         return -1;

@@ -117,7 +117,8 @@ struct MegaArgs {
     unsigned         stage_bytes;   // bytes per ring stage (multiple of 128)
     int              att_sub;       // attention: K/V rows per buffer (even, <= 32)
     int              att_nsl;       // attention: buffer slots (1, or 2: a round's copies overlap the previous round)
-    int              att_l2;        // warm the next attention's K/V rows in L2 during the GEMV before it
+    int              att_l2;        // warm the next attention's K/V rows in L2: 2 at the start of the GEMV
+                                    // before it, 1 at its end, 0 not
     int              att_early;     // the Q/K/V phase issues the attention's first nsl rounds of K/V copies
     int              stall_phase;   // failure-path testing: this GEMV phase waits for an input epoch that
                                     // no phase writes, so its bounded waits run out (-1: none)
@@ -129,8 +130,10 @@ struct MegaArgs {
     unsigned long long *link_tok;   // the head's argmax -> the first stage's token word (or null)
     unsigned long long *tok_ll;     // this context's token word (a linked embedding reads it)
     int              link_in;       // the embedding waits for its token in tok_ll
-    unsigned long long *cta_ns;     // optional, [n_ph + 1][grid]: every CTA's time at the start and at
-                                    // the end of each phase (the skew between CTAs at phase boundaries)
+    unsigned long long *cta_ns;     // optional, [n_ph + 5][grid]: every CTA's time at the start and at
+                                    // the end of each phase (the skew between CTAs at phase boundaries),
+                                    // then in the last attention phase: Q/K/V read, rounds done,
+                                    // partial published, merge done
     float            eps, kscale;
 };
 
@@ -772,6 +775,9 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
     // its latency hides behind this phase (hd <= MEGA_THREADS)
     float cs_next = 0.0f;
     if (ph.next_attn && tid < hd) cs_next = __ldg(a.rope_cs + (size_t)S.pos * hd + tid);
+    // the next attention's K/V rows into L2 while this phase streams its
+    // weights (this phase's kc / vc are the next attention's cache planes)
+    if (ph.next_attn && a.att_l2 == 2 && tid == 0) attn_prefetch(a, ph, S.pos, hd);
     unsigned long long yw = 0;
     if (has_res && ph.y_ep >= 0) yw = ll_word<SYS>(a.x_ll + ph.out_base + r0 + tid);
     if (has_res && ph.y_ep == MEGA_EP_LINK) yw = ll_word<true>(a.x_ll + r0 + tid);
@@ -906,7 +912,7 @@ __device__ void mega_gemv(const MegaArgs &a, const MegaPhase &ph, const MegaShar
     if (next) {
         // next phase's descriptor: its copy was issued at this phase's start
         mbar_wait<true>(S.dbar, (unsigned)p_idx & 1u, a.status);
-        if (tid == 0 && a.att_l2) attn_prefetch(a, *next, S.pos, hd);
+        if (tid == 0 && a.att_l2 == 1) attn_prefetch(a, *next, S.pos, hd);
         if (tid < hd) S.cs[tid] = cs_next;
     }
 
@@ -1093,6 +1099,7 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
     }
     named_bar(1, nct);
     if (det) det[0] = clock64();
+    if (a.cta_ns && tid == 0) a.cta_ns[(size_t)(a.n_ph + 1) * gridDim.x + blockIdx.x] = globaltimer_ns();
     if (has && sp == 0)
         for (int j = tid; j < HD; j += nct) {
             kbase[(size_t)pos * HD + j] = knew[j];
@@ -1204,6 +1211,7 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
     att_sb0 += (nround + nsl - 1) / nsl;
     att_sb1 += nsl > 1 ? nround / nsl : 0;
     if (det) det[1] = clock64();
+    if (a.cta_ns && tid == 0) a.cta_ns[(size_t)(a.n_ph + 2) * gridDim.x + blockIdx.x] = globaltimer_ns();
     // the position groups' accumulators into the K/V buffers (free now: every
     // round's copies have landed), added in group order into this split's
     // partial, published as tagged words: per query head the HD unnormalised
@@ -1241,6 +1249,7 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
     // phase writes the same bytes with ordinary stores
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     if (det) det[2] = clock64();
+    if (a.cta_ns && tid == 0) a.cta_ns[(size_t)(a.n_ph + 3) * gridDim.x + blockIdx.x] = globaltimer_ns();
 
     // ---- merge, without tickets or fences: the KV head's NREP x HD outputs
     // are T = NREP * HD / 32 tasks of 32 dimensions of one query head; task j
@@ -1295,6 +1304,7 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
         }
         named_bar(1, nct);
     }
+    if (a.cta_ns && tid == 0) a.cta_ns[(size_t)(a.n_ph + 4) * gridDim.x + blockIdx.x] = globaltimer_ns();
     // profiling: when KV head 0's merge was done (the CTA of split 0)
     if (a.phase_detail && has && g == 0 && sp == 0 && tid == 0)
         a.phase_detail[(size_t)p_idx * 4 + 3] = globaltimer_ns();

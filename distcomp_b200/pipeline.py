@@ -56,6 +56,15 @@ def split_stages(n_layer: int, n_nodes: int, cost=None, cap=None) -> list[tuple[
     return out
 
 
+# The output head's share of a stage's time per byte, relative to a layer's:
+# one persistent step streams the head (one GEMV phase, ~5.7 TB/s on B200)
+# about 2.4 times faster per byte than a layer (five phases and their
+# boundaries, ~2.4 TB/s), measured on the 8B shape (head 98 us for 558 MB,
+# layer 51.8 us for 123 MB).  The benches balance stages by time: head bytes
+# x HEAD_COST against layer bytes.
+HEAD_COST = 0.42
+
+
 def split_by_bytes(layer_bytes: list[int], n_stages: int, head_bytes: int = 0,
                    embed_bytes: int = 0, head_alone: bool = False) -> list[tuple[int, int]]:
     """Contiguous layer ranges for n_stages GPUs that minimise the largest
@@ -465,7 +474,7 @@ def bench_main(args, rank: int, world: int, local: int, B) -> int:
         if args.split == "ref":
             plan = split_stages(spec.n_layer, world)
         else:
-            plan = split_by_bytes(lb, world, head_bytes=head_b, embed_bytes=emb_row, head_alone=True)
+            plan = split_by_bytes(lb, world, head_bytes=int(head_b * HEAD_COST), embed_bytes=emb_row, head_alone=True)
         first, last = plan[rank]
         n_seq = args.seqs
         prompts = [synth.prompt_tokens(args.prompt, spec.n_vocab, seed=args.seed + 1 + s) for s in range(n_seq)]
@@ -667,7 +676,7 @@ def bench_long_main(args, rank: int, world: int, local: int, B) -> int:
         head_b = tensor_bytes(spec, "output.weight") + tensor_bytes(spec, "output_norm.weight")
         emb_row = tensor_bytes(spec, "token_embd.weight") // spec.n_vocab
         plan = split_stages(spec.n_layer, world) if args.split == "ref" else \
-            split_by_bytes(lb, world, head_bytes=head_b, embed_bytes=emb_row, head_alone=True)
+            split_by_bytes(lb, world, head_bytes=int(head_b * HEAD_COST), embed_bytes=emb_row, head_alone=True)
         first, last = plan[rank]
         need = args.prompt + args.warmup + args.steps + 2
         if need > args.n_ctx:

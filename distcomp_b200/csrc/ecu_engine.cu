@@ -2380,7 +2380,7 @@ int ecu_profile_cta_ns(ecu_ctx *c, unsigned long long *out, size_t n_words, int 
     if (!c || !out) return -1;
     if (grid) *grid = c->mega_grid;
     if (!c->mega) { ecu_set_error(nullptr, 0, "per-CTA phase times need the persistent step"); return -1; }
-    const size_t np = (size_t)c->margs.n_ph, need = (np + 5) * (size_t)c->mega_grid;
+    const size_t np = (size_t)c->margs.n_ph, need = (np + 1) * (size_t)c->mega_grid;
     if (n_words < need) {
         ecu_set_error(nullptr, 0, "ecu_profile_cta_ns: %zu words needed", need);
         return -1;

@@ -130,10 +130,8 @@ struct MegaArgs {
     unsigned long long *link_tok;   // the head's argmax -> the first stage's token word (or null)
     unsigned long long *tok_ll;     // this context's token word (a linked embedding reads it)
     int              link_in;       // the embedding waits for its token in tok_ll
-    unsigned long long *cta_ns;     // optional, [n_ph + 5][grid]: every CTA's time at the start and at
-                                    // the end of each phase (the skew between CTAs at phase boundaries),
-                                    // then in the last attention phase: Q/K/V read, rounds done,
-                                    // partial published, merge done
+    unsigned long long *cta_ns;     // optional, [n_ph + 1][grid]: every CTA's time at the start and at
+                                    // the end of each phase (the skew between CTAs at phase boundaries)
     float            eps, kscale;
 };
 
@@ -1099,7 +1097,6 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
     }
     named_bar(1, nct);
     if (det) det[0] = clock64();
-    if (a.cta_ns && tid == 0) a.cta_ns[(size_t)(a.n_ph + 1) * gridDim.x + blockIdx.x] = globaltimer_ns();
     if (has && sp == 0)
         for (int j = tid; j < HD; j += nct) {
             kbase[(size_t)pos * HD + j] = knew[j];
@@ -1211,7 +1208,6 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
     att_sb0 += (nround + nsl - 1) / nsl;
     att_sb1 += nsl > 1 ? nround / nsl : 0;
     if (det) det[1] = clock64();
-    if (a.cta_ns && tid == 0) a.cta_ns[(size_t)(a.n_ph + 2) * gridDim.x + blockIdx.x] = globaltimer_ns();
     // the position groups' accumulators into the K/V buffers (free now: every
     // round's copies have landed), added in group order into this split's
     // partial, published as tagged words: per query head the HD unnormalised
@@ -1249,7 +1245,6 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
     // phase writes the same bytes with ordinary stores
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     if (det) det[2] = clock64();
-    if (a.cta_ns && tid == 0) a.cta_ns[(size_t)(a.n_ph + 3) * gridDim.x + blockIdx.x] = globaltimer_ns();
 
     // ---- merge, without tickets or fences: the KV head's NREP x HD outputs
     // are T = NREP * HD / 32 tasks of 32 dimensions of one query head; task j
@@ -1304,7 +1299,6 @@ __device__ void mega_attention(const MegaArgs &a, const MegaPhase &ph, const Meg
         }
         named_bar(1, nct);
     }
-    if (a.cta_ns && tid == 0) a.cta_ns[(size_t)(a.n_ph + 4) * gridDim.x + blockIdx.x] = globaltimer_ns();
     // profiling: when KV head 0's merge was done (the CTA of split 0)
     if (a.phase_detail && has && g == 0 && sp == 0 && tid == 0)
         a.phase_detail[(size_t)p_idx * 4 + 3] = globaltimer_ns();

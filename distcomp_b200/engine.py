@@ -284,8 +284,7 @@ class LlmCtx:
 
     def cta_times(self):
         """One persistent step with every CTA's phase start/end times:
-        (phase names, int64 array [phases + 5, grid] of ns; the last four
-        rows time the last attention phase's steps)."""
+        (phase names, int64 array [phases + 1, grid] of ns)."""
         buf = np.zeros(4096 * 1024, dtype=np.uint64)
         kinds = C.create_string_buffer(65536)
         grid = C.c_int(0)
@@ -294,7 +293,7 @@ class LlmCtx:
             raise EngineError(last_error())
         names = kinds.value.decode().split(",")
         g = grid.value
-        return names, buf[: (n + 5) * g].reshape(n + 5, g).astype(np.int64)
+        return names, buf[: (n + 1) * g].reshape(n + 1, g).astype(np.int64)
 
     def tp_handle(self) -> bytes:
         buf = C.create_string_buffer(64)

@@ -340,10 +340,8 @@ typedef struct {
 
 /* One persistent step with every CTA's time (globaltimer ns) at the start
  * and at the end of each phase: out[(p + 1) * grid + cta] = the end of
- * phase p, out[cta] = the start; rows phases + 1 .. phases + 4: in the last
- * attention phase, when the CTA had its Q/K/V words, finished its position
- * rounds, published its partial and finished its merge tasks;
- * n_words >= (phases + 5) * grid (*grid = the CTA count, the SM count).  kinds (optional) receives the phases'
+ * phase p, out[cta] = the start; n_words >= (phases + 1) * grid (*grid =
+ * the CTA count, the SM count).  kinds (optional) receives the phases'
  * names, comma-separated.  Returns the number of phases, or -1.  The
  * position advances as in a step.  For measuring the CTAs' skew at phase
  * boundaries. */

@@ -175,6 +175,20 @@ def test_nccl_pipeline_two_gpus(tmp_path):
     assert (tmp_path / "ok_linked").exists(), r.stdout[-2000:]
 
 
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_nccl_pipeline_two_gpus_70b_shape(tmp_path):
+    """Two 70B-shape layers, one per GPU, each rank building only its stage's
+    tensors: the prompt as a batch per stage, then linked greedy steps; the
+    tokens the oracle's and a FULL context's, the logits bit for bit."""
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr=127.0.0.1", "--master-port=29533", str(ROOT / "tests" / "pipeline_ranks_70b.py"),
+           str(tmp_path)]
+    r = subprocess.run(["timeout", "-k", "30", "900"] + cmd, env=env, capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
+    assert (tmp_path / "ok").exists(), r.stdout[-2000:]
+
+
 def test_prefill_through_stages_matches_full_context(eng, oracle_port, model_buf):
     """Two layers of the 70B shape (n_embd 8192, 64/8 heads, FFN 28672,
     Q4_K) as two pipeline stages in one process -- EMBED + layer 0 | layer

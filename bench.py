@@ -82,9 +82,10 @@ def parse():
     ap.add_argument("--hops", choices=["link", "nccl"], default="link",
                     help="N > 1 pipeline: each step writes its output into the next GPU's step (link), or NCCL "
                          "send/recv between the steps (nccl)")
-    ap.add_argument("--split", choices=["bytes", "ref"], default="bytes",
-                    help="N > 1: layer ranges balancing bytes per stage (head on the last GPU) or "
-                         "shard.c's ceil(layers/stages) rule")
+    ap.add_argument("--split", choices=["half", "bytes", "ref"], default="half",
+                    help="N > 1: ranges of layer halves balancing each stage's time (a GPU may hold half a "
+                         "layer; 8B interleaved pipeline), whole layers balancing time per stage (bytes, the "
+                         "head at its cost per byte), or shard.c's ceil(layers/stages) rule")
     ap.add_argument("--gemv-case", default="",
                     help="--mode gemv: only this case, e.g. Q4_0:14336x4096 (profiler captures)")
     ap.add_argument("--layers", type=int, default=0,

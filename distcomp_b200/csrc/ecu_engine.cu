@@ -16,6 +16,7 @@
 #include "ecu_prefill.cuh"
 
 #include <atomic>
+#include <mutex>
 #include <cerrno>
 #include <fcntl.h>
 #include <sys/mman.h>
@@ -397,6 +398,10 @@ struct LayerDev {
     DevMat              d;
     float *attn_norm = nullptr, *ffn_norm = nullptr;
     float *bq = nullptr, *bk = nullptr, *bv = nullptr;
+    // the layer's attention half (Q/K/V, attention, attn_output) and FFN
+    // half (gate/up, down) on this context: a span may start at a layer's
+    // FFN half or end at its attention half
+    bool ha = true, hf = true;
     // source tensors, for ecu_dequant_tensor
     struct Src { std::string name; const DevMat *m; int row0, rstride, n_in; size_t elems; };
 };
@@ -779,83 +784,90 @@ static void enqueue_layer(ecu_ctx *c, Launcher &L, int li, int nl = -1)
     GemvArgs    a = {};
     a.st = c->st;
 
-    // (1) RMSNorm + Q/K/V projections
-    if (ly.qkv.size() == 1) {
-        L.kind = "gemv_qkv";
-        enqueue_gemv(L, c->sms, ly.qkv[0], c->state, ly.attn_norm, g.eps, c->qkv, EPI_STORE, c->scr, a,
-                     &ly.o, EPI_ADD);
-    } else {
-        L.kind = "rmsnorm";
-        L.bytes = 12.0 * g.n_embd;
-        L(k_rmsnorm, dim3(1), dim3(256), 0, (const float *)c->state, (const float *)ly.attn_norm,
-          g.n_embd, g.eps, c->scr.xn);
-        for (size_t i = 0; i < ly.qkv.size(); i++) {
+    if (ly.ha) {
+        // (1) RMSNorm + Q/K/V projections
+        if (ly.qkv.size() == 1) {
             L.kind = "gemv_qkv";
-            enqueue_gemv(L, c->sms, ly.qkv[i], c->scr.xn, nullptr, g.eps, c->qkv + ly.qkv_off[i],
-                         EPI_STORE, c->scr, a);
+            enqueue_gemv(L, c->sms, ly.qkv[0], c->state, ly.attn_norm, g.eps, c->qkv, EPI_STORE, c->scr, a,
+                         &ly.o, EPI_ADD);
+        } else {
+            L.kind = "rmsnorm";
+            L.bytes = 12.0 * g.n_embd;
+            L(k_rmsnorm, dim3(1), dim3(256), 0, (const float *)c->state, (const float *)ly.attn_norm,
+              g.n_embd, g.eps, c->scr.xn);
+            for (size_t i = 0; i < ly.qkv.size(); i++) {
+                L.kind = "gemv_qkv";
+                enqueue_gemv(L, c->sms, ly.qkv[i], c->scr.xn, nullptr, g.eps, c->qkv + ly.qkv_off[i],
+                             EPI_STORE, c->scr, a);
+            }
         }
-    }
-    // (2) bias + RoPE + KV append + attention
-    AttnArgs aa;
-    aa.qkv = c->qkv;
-    aa.bq = ly.bq;
-    aa.bk = ly.bk;
-    aa.bv = ly.bv;
-    aa.rope_cs = c->rope_cs;
-    const size_t plane = (size_t)g.n_head_kv * g.n_ctx * hd;
-    aa.kc = c->kc + (size_t)li * plane;
-    aa.vc = c->vc + (size_t)li * plane;
-    aa.att = c->att;
-    aa.st = c->st;
-    aa.status = &c->st->status;
-    aa.n_head = g.n_head;
-    aa.n_kv = g.n_head_kv;
-    aa.n_rep = g.n_rep;
-    aa.n_ctx = g.n_ctx;
-    aa.n_split = c->n_split;
-    aa.kscale = 1.0f / sqrtf((float)hd);
-    dim3 ag(g.n_head_kv, c->n_split);
-    L.kind = "attention";
-    L.cluster_y = (unsigned)c->n_split;
-    // K and V rows of positions 0..pos read, one row of each written, q/att
-    L.bytes = 2.0 * 4.0 * kvdim * (c->pos + 2) + 8.0 * qdim + 4.0 * (qdim + 2 * kvdim);
+        // (2) bias + RoPE + KV append + attention
+        AttnArgs aa;
+        aa.qkv = c->qkv;
+        aa.bq = ly.bq;
+        aa.bk = ly.bk;
+        aa.bv = ly.bv;
+        aa.rope_cs = c->rope_cs;
+        const size_t plane = (size_t)g.n_head_kv * g.n_ctx * hd;
+        aa.kc = c->kc + (size_t)li * plane;
+        aa.vc = c->vc + (size_t)li * plane;
+        aa.att = c->att;
+        aa.st = c->st;
+        aa.status = &c->st->status;
+        aa.n_head = g.n_head;
+        aa.n_kv = g.n_head_kv;
+        aa.n_rep = g.n_rep;
+        aa.n_ctx = g.n_ctx;
+        aa.n_split = c->n_split;
+        aa.kscale = 1.0f / sqrtf((float)hd);
+        dim3 ag(g.n_head_kv, c->n_split);
+        L.kind = "attention";
+        L.cluster_y = (unsigned)c->n_split;
+        // K and V rows of positions 0..pos read, one row of each written, q/att
+        L.bytes = 2.0 * 4.0 * kvdim * (c->pos + 2) + 8.0 * qdim + 4.0 * (qdim + 2 * kvdim);
 #define ATT_CASE(HD_, R_) \
-    if (hd == HD_ && g.n_rep == R_) { L(k_attention<HD_, R_>, ag, dim3(ATT_THREADS), attn_smem_bytes<HD_>(), aa); } else
-    ATT_CASE(128, 1) ATT_CASE(128, 2) ATT_CASE(128, 4) ATT_CASE(128, 8)
-    ATT_CASE(64, 1) ATT_CASE(64, 2) ATT_CASE(64, 4) ATT_CASE(64, 8)
-    ATT_CASE(32, 1) ATT_CASE(32, 2) ATT_CASE(32, 4) ATT_CASE(32, 8)
-    ATT_CASE(16, 1) ATT_CASE(16, 2) ATT_CASE(16, 4) ATT_CASE(16, 8) {}
+        if (hd == HD_ && g.n_rep == R_) { L(k_attention<HD_, R_>, ag, dim3(ATT_THREADS), attn_smem_bytes<HD_>(), aa); } else
+        ATT_CASE(128, 1) ATT_CASE(128, 2) ATT_CASE(128, 4) ATT_CASE(128, 8)
+        ATT_CASE(64, 1) ATT_CASE(64, 2) ATT_CASE(64, 4) ATT_CASE(64, 8)
+        ATT_CASE(32, 1) ATT_CASE(32, 2) ATT_CASE(32, 4) ATT_CASE(32, 8)
+        ATT_CASE(16, 1) ATT_CASE(16, 2) ATT_CASE(16, 4) ATT_CASE(16, 8) {}
 #undef ATT_CASE
-    (void)qdim;
-    (void)kvdim;
-    // (3) x += Wo * att
-    L.kind = "gemv_o";
-    enqueue_gemv(L, c->sms, ly.o, c->att, nullptr, g.eps, c->state, EPI_ADD, c->scr, a, gu_first,
-                 ly.gu_fused ? EPI_SWIGLU : EPI_STORE);
-    // (4) RMSNorm + gate/up + SwiGLU
-    if (ly.gu_fused) {
-        L.kind = "gemv_gate_up";
-        enqueue_gemv(L, c->sms, ly.gu, c->state, ly.ffn_norm, g.eps, c->h, EPI_SWIGLU, c->scr, a, &ly.d,
-                     EPI_ADD);
-    } else {
-        L.kind = "rmsnorm";
-        L.bytes = 12.0 * g.n_embd;
-        L(k_rmsnorm, dim3(1), dim3(256), 0, (const float *)c->state, (const float *)ly.ffn_norm,
-          g.n_embd, g.eps, c->scr.xn);
-        L.kind = "gemv_gate";
-        enqueue_gemv(L, c->sms, ly.g, c->scr.xn, nullptr, g.eps, c->gtmp, EPI_STORE, c->scr, a);
-        L.kind = "gemv_up";
-        enqueue_gemv(L, c->sms, ly.u, c->scr.xn, nullptr, g.eps, c->utmp, EPI_STORE, c->scr, a);
-        L.kind = "swiglu";
-        L.bytes = 12.0 * g.n_ff;
-        L(k_swiglu, dim3((g.n_ff + 255) / 256), dim3(256), 0, (const float *)c->gtmp,
-          (const float *)c->utmp, c->h, g.n_ff);
+        (void)qdim;
+        (void)kvdim;
+        // (3) x += Wo * att
+        L.kind = "gemv_o";
+        // (the next weights: this layer's gate/up, or with the attention half
+        // only, what follows the layer)
+        const DevMat *ox = ly.hf ? gu_first : after_layer(c, li, nl);
+        const int     oe = ly.hf ? (ly.gu_fused ? EPI_SWIGLU : EPI_STORE) : (ox == &c->out ? EPI_ARGMAX : EPI_STORE);
+        enqueue_gemv(L, c->sms, ly.o, c->att, nullptr, g.eps, c->state, EPI_ADD, c->scr, a, ox, oe);
     }
-    // (5) x += Wd * h
-    L.kind = "gemv_down";
-    const DevMat *nx = after_layer(c, li, nl);
-    enqueue_gemv(L, c->sms, ly.d, c->h, nullptr, g.eps, c->state, EPI_ADD, c->scr, a, nx,
-                 nx == &c->out ? EPI_ARGMAX : EPI_STORE);
+    if (ly.hf) {
+        // (4) RMSNorm + gate/up + SwiGLU
+        if (ly.gu_fused) {
+            L.kind = "gemv_gate_up";
+            enqueue_gemv(L, c->sms, ly.gu, c->state, ly.ffn_norm, g.eps, c->h, EPI_SWIGLU, c->scr, a, &ly.d,
+                         EPI_ADD);
+        } else {
+            L.kind = "rmsnorm";
+            L.bytes = 12.0 * g.n_embd;
+            L(k_rmsnorm, dim3(1), dim3(256), 0, (const float *)c->state, (const float *)ly.ffn_norm,
+              g.n_embd, g.eps, c->scr.xn);
+            L.kind = "gemv_gate";
+            enqueue_gemv(L, c->sms, ly.g, c->scr.xn, nullptr, g.eps, c->gtmp, EPI_STORE, c->scr, a);
+            L.kind = "gemv_up";
+            enqueue_gemv(L, c->sms, ly.u, c->scr.xn, nullptr, g.eps, c->utmp, EPI_STORE, c->scr, a);
+            L.kind = "swiglu";
+            L.bytes = 12.0 * g.n_ff;
+            L(k_swiglu, dim3((g.n_ff + 255) / 256), dim3(256), 0, (const float *)c->gtmp,
+              (const float *)c->utmp, c->h, g.n_ff);
+        }
+        // (5) x += Wd * h
+        L.kind = "gemv_down";
+        const DevMat *nx = after_layer(c, li, nl);
+        enqueue_gemv(L, c->sms, ly.d, c->h, nullptr, g.eps, c->state, EPI_ADD, c->scr, a, nx,
+                     nx == &c->out ? EPI_ARGMAX : EPI_STORE);
+    }
 }
 
 static void enqueue_head(ecu_ctx *c, Launcher &L, bool advance)
@@ -872,8 +884,11 @@ static void enqueue_head(ecu_ctx *c, Launcher &L, bool advance)
     a.xn_out = c->scr.xn;
     a.xn_dst = c->state;
     L.kind = "gemv_head_argmax";
-    // the next token of a context with layers starts with layer 0's Q/K/V projection
-    const DevMat *nx = !c->layers.empty() ? &c->layers[0].qkv[0] : nullptr;
+    // the next token of a context with layers starts with its first layer's
+    // Q/K/V projection (or gate/up, for a span that starts at an FFN half)
+    const DevMat *nx = nullptr;
+    if (!c->layers.empty())
+        nx = c->layers[0].ha ? &c->layers[0].qkv[0] : (c->layers[0].gu_fused ? &c->layers[0].gu : &c->layers[0].g);
     enqueue_gemv(L, c->sms, c->out, c->state, c->out_norm, g.eps, c->logits, EPI_ARGMAX, c->scr, a, nx,
                  EPI_STORE);
 }
@@ -1070,10 +1085,19 @@ static int mega_setup(ecu_ctx *c)
     const bool bcast = tp.world > 1;          // outputs every rank reads go to every rank
     MegaFn fn = mega_lookup(hd, g.n_rep, bcast);
     if (!fn) return no("head_dim / query heads per KV head not instantiated");
-    for (auto &ly : c->layers)
-        if (ly.qkv.size() != 1 || !ly.gu_fused || !mega_mat_ok(ly.qkv[0]) || !mega_mat_ok(ly.o) ||
-            !mega_mat_ok(ly.gu) || !mega_mat_ok(ly.d))
-            return no("a layer matrix is not Q4_0/Q8_0/Q4_K in a fast layout");
+    // the weight matrices of a layer's halves on this context
+    auto layer_mats = [](const LayerDev &ly) {
+        std::vector<const DevMat *> v;
+        if (ly.ha) { v.push_back(&ly.qkv[0]); v.push_back(&ly.o); }
+        if (ly.hf) { v.push_back(&ly.gu); v.push_back(&ly.d); }
+        return v;
+    };
+    for (auto &ly : c->layers) {
+        if ((ly.ha && ly.qkv.size() != 1) || (ly.hf && !ly.gu_fused))
+            return no("a layer's Q/K/V or gate/up are not fused");
+        for (const DevMat *m : layer_mats(ly))
+            if (!mega_mat_ok(*m)) return no("a layer matrix is not Q4_0/Q8_0/Q4_K in a fast layout");
+    }
     const bool emb = r_emb(c), full = r_head(c);        // (full: the step ends with the head)
     if (full && !mega_mat_ok(c->out)) return no("output head not Q4_0/Q8_0/Q4_K in a fast layout");
     int coop = 0;
@@ -1090,9 +1114,8 @@ static int mega_setup(ecu_ctx *c)
     unsigned stage_bytes = (unsigned)(ring_total / nst) & ~127u;
     // (row_bytes and n_in / nseg are those of a column segment)
     for (auto &ly : c->layers)
-        if (ly.qkv[0].row_bytes > stage_bytes || ly.o.row_bytes > stage_bytes || ly.gu.row_bytes > stage_bytes ||
-            ly.d.row_bytes > stage_bytes)
-            return no("a weight row does not fit a ring stage");
+        for (const DevMat *m : layer_mats(ly))
+            if (m->row_bytes > stage_bytes) return no("a weight row does not fit a ring stage");
     if (full && c->out.row_bytes > stage_bytes) return no("a head row does not fit a ring stage");
     // the shared-memory union: the digit planes of the widest GEMV input, or
     // the attention K/V buffers; the split partials of a head group, which
@@ -1100,7 +1123,7 @@ static int mega_setup(ecu_ctx *c)
     // item per CTA at most)
     size_t un = (size_t)g.n_embd / 32 * 28 * sizeof(int);
     for (auto &ly : c->layers)
-        for (const DevMat *m : {&ly.qkv[0], &ly.o, &ly.gu, &ly.d})
+        for (const DevMat *m : layer_mats(ly))
             un = std::max(un, (size_t)(m->n_in / m->nseg) / 32 * 28 * sizeof(int));
     if (full) un = std::max(un, (size_t)c->out.n_in / 32 * 28 * sizeof(int));
     // attention K/V buffers: two slots (each round's copies overlap the
@@ -1126,7 +1149,8 @@ static int mega_setup(ecu_ctx *c)
     const char *ke = getenv("ECU_MEGA_KV_EARLY");
     const bool  kv_early = ke && ke[0] == '1';
     size_t qkv_dig = 0;
-    for (auto &ly : c->layers) qkv_dig = std::max(qkv_dig, (size_t)ly.qkv[0].n_in / 32 * 28 * sizeof(int));
+    for (auto &ly : c->layers)
+        if (ly.ha) qkv_dig = std::max(qkv_dig, (size_t)ly.qkv[0].n_in / 32 * 28 * sizeof(int));
     const size_t kv_off = kv_early ? ((qkv_dig + 127) & ~(size_t)127) : 0;
     un = std::max(un, kv_off + (size_t)att_nsl * att_sub * row4);
     // the attention's position-group sums (at the union's base): [512 / (hd/4)][n_rep][hd] floats
@@ -1199,38 +1223,51 @@ static int mega_setup(ecu_ctx *c)
     const size_t plane = (size_t)tp.nkv * g.n_ctx * hd;
     for (size_t li = 0; li < c->layers.size(); li++) {
         LayerDev &ly = c->layers[li];
-        const bool last = li + 1 == c->layers.size();
-        MegaPhase q = mega_gemv_phase(ly.qkv[0], grid, stage_bytes, 1, EPI_STORE, c->state, ly.attn_norm, c->qkv, nullptr);
-        q.kc = c->kc + li * plane;                  // the next attention's cache planes (early K/V copies)
-        q.vc = c->vc + li * plane;
-        q.in_ep = x_w;
-        q.x_ll = x_ll;
-        q.y_ll = qkv_ll;
-        const int p_qkv = (int)ph.size();
-        add(q, "gemv_qkv", gemv_bytes(ly.qkv[0], EPI_STORE));
-        MegaPhase at = {};
-        at.kind = PH_ATTN;
-        at.kc = c->kc + li * plane;
-        at.vc = c->vc + li * plane;
-        at.bq = ly.bq;
-        at.bk = ly.bk;
-        at.bv = ly.bv;
-        at.in_ep = p_qkv;
-        at.y_ll = att_ll + (size_t)tp.rank * qd_l;   // this rank's heads of the whole vector
-        at.bcast = bcast;
-        const int p_at = (int)ph.size();
-        add(at, "attention", -1.0);                 // position dependent: filled in by the profile
-        add_resid(ly.o, "gemv_o", c->att, att_ll, p_at, 0);
-        MegaPhase gu = mega_gemv_phase(ly.gu, grid, stage_bytes, 1, EPI_SWIGLU, c->state, ly.ffn_norm, c->h, nullptr);
-        gu.in_ep = x_w;
-        gu.x_ll = x_ll;
-        gu.y_ll = h_ll;
-        gu.out_base = tp.rank * tp.ff;
-        gu.bcast = bcast;
-        const int p_gu = (int)ph.size();
-        add(gu, "gemv_gate_up", gemv_bytes(ly.gu, EPI_SWIGLU));
-        add_resid(ly.d, "gemv_down", c->h, h_ll, p_gu, (!full && last) ? 1 : 0);   // out_plain: the stage's output state
+        if (ly.ha) {
+            MegaPhase q = mega_gemv_phase(ly.qkv[0], grid, stage_bytes, 1, EPI_STORE, c->state, ly.attn_norm, c->qkv,
+                                          nullptr);
+            q.kc = c->kc + li * plane;              // the next attention's cache planes (early K/V copies)
+            q.vc = c->vc + li * plane;
+            q.in_ep = x_w;
+            q.x_ll = x_ll;
+            q.y_ll = qkv_ll;
+            const int p_qkv = (int)ph.size();
+            add(q, "gemv_qkv", gemv_bytes(ly.qkv[0], EPI_STORE));
+            MegaPhase at = {};
+            at.kind = PH_ATTN;
+            at.kc = c->kc + li * plane;
+            at.vc = c->vc + li * plane;
+            at.bq = ly.bq;
+            at.bk = ly.bk;
+            at.bv = ly.bv;
+            at.in_ep = p_qkv;
+            at.y_ll = att_ll + (size_t)tp.rank * qd_l;   // this rank's heads of the whole vector
+            at.bcast = bcast;
+            const int p_at = (int)ph.size();
+            add(at, "attention", -1.0);             // position dependent: filled in by the profile
+            add_resid(ly.o, "gemv_o", c->att, att_ll, p_at, 0);
+        }
+        if (ly.hf) {
+            MegaPhase gu = mega_gemv_phase(ly.gu, grid, stage_bytes, 1, EPI_SWIGLU, c->state, ly.ffn_norm, c->h,
+                                           nullptr);
+            gu.in_ep = x_w;
+            gu.x_ll = x_ll;
+            gu.y_ll = h_ll;
+            gu.out_base = tp.rank * tp.ff;
+            gu.bcast = bcast;
+            const int p_gu = (int)ph.size();
+            add(gu, "gemv_gate_up", gemv_bytes(ly.gu, EPI_SWIGLU));
+            add_resid(ly.d, "gemv_down", c->h, h_ll, p_gu, 0);
+        }
     }
+    // without the head, the last residual phase also writes the stage's
+    // output state in plain floats
+    if (!full)
+        for (size_t i = ph.size(); i-- > 0;)
+            if (ph[i].kind == PH_GEMV && ph[i].epi == EPI_ADD) {
+                ph[i].out_plain = 1;
+                break;
+            }
     if (full) {
         MegaPhase hp = mega_gemv_phase(c->out, grid, stage_bytes, 1, EPI_ARGMAX, c->state, c->out_norm, c->logits, xn_tmp);
         hp.in_ep = x_w;
@@ -1380,6 +1417,28 @@ static int mega_setup(ecu_ctx *c)
 }
 
 // One step: a cooperative launch of the whole-step kernel on s.
+// Persistent steps of one device run one after another, whatever stream
+// they are enqueued on: the CTAs of a step wait for each other's words, so
+// two steps whose CTAs shared the SMs (neither wholly resident) could only
+// end by their bounded waits running out.  Each launch waits for the
+// device's previous one (an event; free when both are on one stream).
+static std::mutex  g_mega_mu;
+static cudaEvent_t g_mega_ev[64] = {};
+
+static cudaError_t mega_launch_serial(int device, const cudaLaunchConfig_t &cfg, MegaFn fn, const MegaArgs &a)
+{
+    std::lock_guard<std::mutex> lk(g_mega_mu);
+    cudaEvent_t *ev = (device >= 0 && device < 64) ? &g_mega_ev[device] : nullptr;
+    if (ev && !*ev && cudaEventCreateWithFlags(ev, cudaEventDisableTiming) != cudaSuccess) *ev = nullptr;
+    if (ev && *ev) {
+        const cudaError_t w = cudaStreamWaitEvent(cfg.stream, *ev, 0);
+        if (w != cudaSuccess) return w;
+    }
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, fn, a);
+    if (e == cudaSuccess && ev && *ev) return cudaEventRecord(*ev, cfg.stream);
+    return e;
+}
+
 static int mega_launch(ecu_ctx *c, cudaStream_t s, unsigned long long *phase_ns, unsigned long long *detail)
 {
     if (c->tp.world > 1 && (int)c->tp_peers.size() != c->tp.world - 1) {
@@ -1402,7 +1461,7 @@ static int mega_launch(ecu_ctx *c, cudaStream_t s, unsigned long long *phase_ns,
     at.val.cooperative = 1;
     cfg.attrs = &at;
     cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, c->mega_fn, a);
+    cudaError_t e = mega_launch_serial(c->device, cfg, c->mega_fn, a);
     if (e != cudaSuccess) {
         ecu_set_error(nullptr, 0, "persistent step launch failed: %s", cudaGetErrorString(e));
         return -1;
@@ -1609,7 +1668,7 @@ int ecu_model_tensor(const ecu_model *m, const char *name, unsigned *type, unsig
 // Tensors a stage needs and their check (src/engine.c:169-213).
 struct StageTensors {
     const EcuTensor *emb = nullptr, *out_norm = nullptr, *out = nullptr;
-    struct L { const EcuTensor *an, *q, *k, *v, *o, *fn, *g, *u, *d, *bq, *bk, *bv; };
+    struct L { const EcuTensor *an, *q, *k, *v, *o, *fn, *g, *u, *d, *bq, *bk, *bv; bool ha, hf; };
     std::vector<L> layers;
 };
 
@@ -1620,7 +1679,7 @@ static int stage_tensors(const ecu_model *m, const EcuGeom &g, int stage, int fi
     const bool emb = stage == ECU_STAGE_EMBED || stage == ECU_STAGE_FULL || (sp && (span & ECU_SPAN_EMBED));
     const bool head = stage == ECU_STAGE_HEAD || stage == ECU_STAGE_FULL || (sp && (span & ECU_SPAN_HEAD));
     const bool lay = stage == ECU_STAGE_LAYERS || stage == ECU_STAGE_FULL || (sp && first <= last);
-    if (sp && (span & ~(ECU_SPAN_EMBED | ECU_SPAN_HEAD))) {
+    if (sp && (span & ~(ECU_SPAN_EMBED | ECU_SPAN_HEAD | ECU_SPAN_FFN_FIRST | ECU_SPAN_ATTN_LAST))) {
         ecu_set_error(err, errlen, "unknown span flags 0x%x", span);
         return -1;
     }
@@ -1653,15 +1712,24 @@ static int stage_tensors(const ecu_model *m, const EcuGeom &g, int stage, int fi
                                      "ffn_gate.weight", "ffn_up.weight", "ffn_down.weight"};
         for (int i = first; i <= last; i++) {
             StageTensors::L l{};
+            l.ha = !(sp && i == first && (span & ECU_SPAN_FFN_FIRST));
+            l.hf = !(sp && i == last && (span & ECU_SPAN_ATTN_LAST));
+            if (!l.ha && !l.hf) {
+                ecu_set_error(err, errlen, "layer %d would hold neither its attention nor its FFN half", i);
+                return -1;
+            }
             const EcuTensor **slot[9] = {&l.an, &l.q, &l.k, &l.v, &l.o, &l.fn, &l.g, &l.u, &l.d};
             char name[160];
             for (int k = 0; k < 9; k++) {
+                if ((k < 5 && !l.ha) || (k >= 5 && !l.hf)) continue;      // the half this span leaves out
                 snprintf(name, sizeof name, "blk.%d.%s", i, sfx[k]);
                 if (!(*slot[k] = m->find(name))) { ecu_set_error(err, errlen, "model has no tensor %s", name); return -1; }
             }
-            snprintf(name, sizeof name, "blk.%d.attn_q.bias", i); l.bq = m->find(name);
-            snprintf(name, sizeof name, "blk.%d.attn_k.bias", i); l.bk = m->find(name);
-            snprintf(name, sizeof name, "blk.%d.attn_v.bias", i); l.bv = m->find(name);
+            if (l.ha) {
+                snprintf(name, sizeof name, "blk.%d.attn_q.bias", i); l.bq = m->find(name);
+                snprintf(name, sizeof name, "blk.%d.attn_k.bias", i); l.bk = m->find(name);
+                snprintf(name, sizeof name, "blk.%d.attn_v.bias", i); l.bv = m->find(name);
+            }
             st->layers.push_back(l);
         }
     }
@@ -1815,10 +1883,12 @@ static int ctx_open_impl(ecu_ctx **out, const ecu_model *m, int stage, int first
         }
         if (hd % 2) { ecu_set_error(err, errlen, "odd head_dim %d", hd); return -1; }
         for (auto &l : st.layers) {
-            if (check_shape(l.q, g.n_embd, qd, err, errlen) || check_shape(l.k, g.n_embd, kvd, err, errlen) ||
-                check_shape(l.v, g.n_embd, kvd, err, errlen) || check_shape(l.o, qd, g.n_embd, err, errlen) ||
-                check_shape(l.g, g.n_embd, g.n_ff, err, errlen) || check_shape(l.u, g.n_embd, g.n_ff, err, errlen) ||
-                check_shape(l.d, g.n_ff, g.n_embd, err, errlen))
+            if (l.ha && (check_shape(l.q, g.n_embd, qd, err, errlen) || check_shape(l.k, g.n_embd, kvd, err, errlen) ||
+                         check_shape(l.v, g.n_embd, kvd, err, errlen) || check_shape(l.o, qd, g.n_embd, err, errlen)))
+                return -1;
+            if (l.hf && (check_shape(l.g, g.n_embd, g.n_ff, err, errlen) ||
+                         check_shape(l.u, g.n_embd, g.n_ff, err, errlen) ||
+                         check_shape(l.d, g.n_ff, g.n_embd, err, errlen)))
                 return -1;
         }
     }
@@ -1960,90 +2030,97 @@ static int ctx_open_impl(ecu_ctx **out, const ecu_model *m, int stage, int first
             LayerDev   &ly = c->layers[i];
             char        nm[160];
             const int   li = first + (int)i;
-            // Q/K/V: fused when all three share a fast layout (a tensor-
-            // parallel rank: its heads' rows of each)
-            const int lq = choose_layout((int)l.q->type, g.n_embd);
-            const bool fuse_qkv = lq != LAY_RAW && l.k->type == l.q->type && l.v->type == l.q->type;
+            ly.ha = l.ha;
+            ly.hf = l.hf;
             const int  qd_l = tp.nh * hd, kvd_l = tp.nkv * hd;
-            if (!fuse_qkv && !whole) {
-                ecu_set_error(err, errlen, "tensor parallelism needs Q/K/V of one fast type");
-                return -1;
-            }
-            if (fuse_qkv) {
-                DevMat mq = make_mat(c.get(), (int)l.q->type, g.n_embd, qd_l + 2 * kvd_l, true);
-                if (!mq.data) return fail_oom("attn_qkv");
-                if (upload_rows(c.get(), l.q, g.n_embd, qd_l, mq, 0, 1, stage_buf, (size_t)tp.rank * qd_l) ||
-                    upload_rows(c.get(), l.k, g.n_embd, kvd_l, mq, qd_l, 1, stage_buf, (size_t)tp.rank * kvd_l) ||
-                    upload_rows(c.get(), l.v, g.n_embd, kvd_l, mq, qd_l + kvd_l, 1, stage_buf,
-                                (size_t)tp.rank * kvd_l))
+            if (l.ha) {
+                // Q/K/V: fused when all three share a fast layout (a tensor-
+                // parallel rank: its heads' rows of each)
+                const int lq = choose_layout((int)l.q->type, g.n_embd);
+                const bool fuse_qkv = lq != LAY_RAW && l.k->type == l.q->type && l.v->type == l.q->type;
+                if (!fuse_qkv && !whole) {
+                    ecu_set_error(err, errlen, "tensor parallelism needs Q/K/V of one fast type");
                     return -1;
-                ly.qkv.push_back(mq);
-                ly.qkv_off.push_back(0);
-                if (whole) {
-                    snprintf(nm, sizeof nm, "blk.%d.attn_q.weight", li); c->srcs.push_back({nm, mq, 0, 1, (size_t)g.n_embd * qd, g.n_embd});
-                    snprintf(nm, sizeof nm, "blk.%d.attn_k.weight", li); c->srcs.push_back({nm, mq, qd, 1, (size_t)g.n_embd * kvd, g.n_embd});
-                    snprintf(nm, sizeof nm, "blk.%d.attn_v.weight", li); c->srcs.push_back({nm, mq, qd + kvd, 1, (size_t)g.n_embd * kvd, g.n_embd});
                 }
-            } else {
-                const EcuTensor *ts[3] = {l.q, l.k, l.v};
-                const int        rows[3] = {qd, kvd, kvd}, offs[3] = {0, qd, qd + kvd};
-                const char      *sf[3] = {"attn_q", "attn_k", "attn_v"};
-                for (int k = 0; k < 3; k++) {
-                    DevMat mm = make_mat(c.get(), (int)ts[k]->type, g.n_embd, rows[k], true);
-                    if (!mm.zero && !mm.data) return fail_oom("attn_q/k/v");
-                    if (upload_rows(c.get(), ts[k], g.n_embd, rows[k], mm, 0, 1, stage_buf)) return -1;
-                    ly.qkv.push_back(mm);
-                    ly.qkv_off.push_back(offs[k]);
-                    snprintf(nm, sizeof nm, "blk.%d.%s.weight", li, sf[k]);
-                    c->srcs.push_back({nm, mm, 0, 1, (size_t)g.n_embd * rows[k], g.n_embd});
+                if (fuse_qkv) {
+                    DevMat mq = make_mat(c.get(), (int)l.q->type, g.n_embd, qd_l + 2 * kvd_l, true);
+                    if (!mq.data) return fail_oom("attn_qkv");
+                    if (upload_rows(c.get(), l.q, g.n_embd, qd_l, mq, 0, 1, stage_buf, (size_t)tp.rank * qd_l) ||
+                        upload_rows(c.get(), l.k, g.n_embd, kvd_l, mq, qd_l, 1, stage_buf, (size_t)tp.rank * kvd_l) ||
+                        upload_rows(c.get(), l.v, g.n_embd, kvd_l, mq, qd_l + kvd_l, 1, stage_buf,
+                                    (size_t)tp.rank * kvd_l))
+                        return -1;
+                    ly.qkv.push_back(mq);
+                    ly.qkv_off.push_back(0);
+                    if (whole) {
+                        snprintf(nm, sizeof nm, "blk.%d.attn_q.weight", li); c->srcs.push_back({nm, mq, 0, 1, (size_t)g.n_embd * qd, g.n_embd});
+                        snprintf(nm, sizeof nm, "blk.%d.attn_k.weight", li); c->srcs.push_back({nm, mq, qd, 1, (size_t)g.n_embd * kvd, g.n_embd});
+                        snprintf(nm, sizeof nm, "blk.%d.attn_v.weight", li); c->srcs.push_back({nm, mq, qd + kvd, 1, (size_t)g.n_embd * kvd, g.n_embd});
+                    }
+                } else {
+                    const EcuTensor *ts[3] = {l.q, l.k, l.v};
+                    const int        rows[3] = {qd, kvd, kvd}, offs[3] = {0, qd, qd + kvd};
+                    const char      *sf[3] = {"attn_q", "attn_k", "attn_v"};
+                    for (int k = 0; k < 3; k++) {
+                        DevMat mm = make_mat(c.get(), (int)ts[k]->type, g.n_embd, rows[k], true);
+                        if (!mm.zero && !mm.data) return fail_oom("attn_q/k/v");
+                        if (upload_rows(c.get(), ts[k], g.n_embd, rows[k], mm, 0, 1, stage_buf)) return -1;
+                        ly.qkv.push_back(mm);
+                        ly.qkv_off.push_back(offs[k]);
+                        snprintf(nm, sizeof nm, "blk.%d.%s.weight", li, sf[k]);
+                        c->srcs.push_back({nm, mm, 0, 1, (size_t)g.n_embd * rows[k], g.n_embd});
+                    }
                 }
+                ly.o = make_mat(c.get(), (int)l.o->type, qd, tp.ne, true, true);
+                if (!ly.o.zero && !ly.o.data) return fail_oom("attn_output");
+                if (upload_rows(c.get(), l.o, qd, tp.ne, ly.o, 0, 1, stage_buf, (size_t)tp.rank * tp.ne)) return -1;
+                snprintf(nm, sizeof nm, "blk.%d.attn_output.weight", li);
+                if (whole) c->srcs.push_back({nm, ly.o, 0, 1, (size_t)qd * g.n_embd, qd});
+                ly.attn_norm = upload_vec(c.get(), l.an, (size_t)g.n_embd, stage_buf);
+                // biases whole; a tensor-parallel rank points at its heads' part
+                if (l.bq) ly.bq = upload_vec(c.get(), l.bq, (size_t)qd, stage_buf);
+                if (l.bk) ly.bk = upload_vec(c.get(), l.bk, (size_t)kvd, stage_buf);
+                if (l.bv) ly.bv = upload_vec(c.get(), l.bv, (size_t)kvd, stage_buf);
+                if (ly.bq) ly.bq += (size_t)tp.rank * qd_l;
+                if (ly.bk) ly.bk += (size_t)tp.rank * kvd_l;
+                if (ly.bv) ly.bv += (size_t)tp.rank * kvd_l;
+                if (!ly.attn_norm) return fail_oom("norm weights");
             }
-            ly.o = make_mat(c.get(), (int)l.o->type, qd, tp.ne, true, true);
-            if (!ly.o.zero && !ly.o.data) return fail_oom("attn_output");
-            if (upload_rows(c.get(), l.o, qd, tp.ne, ly.o, 0, 1, stage_buf, (size_t)tp.rank * tp.ne)) return -1;
-            snprintf(nm, sizeof nm, "blk.%d.attn_output.weight", li);
-            if (whole) c->srcs.push_back({nm, ly.o, 0, 1, (size_t)qd * g.n_embd, qd});
-            const int lg = choose_layout((int)l.g->type, g.n_embd);
-            ly.gu_fused = lg != LAY_RAW && l.u->type == l.g->type;
-            if (!ly.gu_fused && !whole) {
-                ecu_set_error(err, errlen, "tensor parallelism needs gate/up of one fast type");
-                return -1;
-            }
-            if (ly.gu_fused) {
-                ly.gu = make_mat(c.get(), (int)l.g->type, g.n_embd, 2 * tp.ff, true);
-                if (!ly.gu.data) return fail_oom("ffn_gate/up");
-                if (upload_rows(c.get(), l.g, g.n_embd, tp.ff, ly.gu, 0, 2, stage_buf, (size_t)tp.rank * tp.ff) ||
-                    upload_rows(c.get(), l.u, g.n_embd, tp.ff, ly.gu, 1, 2, stage_buf, (size_t)tp.rank * tp.ff))
+            if (l.hf) {
+                const int lg = choose_layout((int)l.g->type, g.n_embd);
+                ly.gu_fused = lg != LAY_RAW && l.u->type == l.g->type;
+                if (!ly.gu_fused && !whole) {
+                    ecu_set_error(err, errlen, "tensor parallelism needs gate/up of one fast type");
                     return -1;
-                if (whole) {
-                    snprintf(nm, sizeof nm, "blk.%d.ffn_gate.weight", li); c->srcs.push_back({nm, ly.gu, 0, 2, (size_t)g.n_embd * g.n_ff, g.n_embd});
-                    snprintf(nm, sizeof nm, "blk.%d.ffn_up.weight", li); c->srcs.push_back({nm, ly.gu, 1, 2, (size_t)g.n_embd * g.n_ff, g.n_embd});
                 }
-            } else {
-                ly.g = make_mat(c.get(), (int)l.g->type, g.n_embd, g.n_ff, true);
-                ly.u = make_mat(c.get(), (int)l.u->type, g.n_embd, g.n_ff, true);
-                if ((!ly.g.zero && !ly.g.data) || (!ly.u.zero && !ly.u.data)) return fail_oom("ffn_gate/up");
-                if (upload_rows(c.get(), l.g, g.n_embd, g.n_ff, ly.g, 0, 1, stage_buf) ||
-                    upload_rows(c.get(), l.u, g.n_embd, g.n_ff, ly.u, 0, 1, stage_buf))
-                    return -1;
-                snprintf(nm, sizeof nm, "blk.%d.ffn_gate.weight", li); c->srcs.push_back({nm, ly.g, 0, 1, (size_t)g.n_embd * g.n_ff, g.n_embd});
-                snprintf(nm, sizeof nm, "blk.%d.ffn_up.weight", li); c->srcs.push_back({nm, ly.u, 0, 1, (size_t)g.n_embd * g.n_ff, g.n_embd});
+                if (ly.gu_fused) {
+                    ly.gu = make_mat(c.get(), (int)l.g->type, g.n_embd, 2 * tp.ff, true);
+                    if (!ly.gu.data) return fail_oom("ffn_gate/up");
+                    if (upload_rows(c.get(), l.g, g.n_embd, tp.ff, ly.gu, 0, 2, stage_buf, (size_t)tp.rank * tp.ff) ||
+                        upload_rows(c.get(), l.u, g.n_embd, tp.ff, ly.gu, 1, 2, stage_buf, (size_t)tp.rank * tp.ff))
+                        return -1;
+                    if (whole) {
+                        snprintf(nm, sizeof nm, "blk.%d.ffn_gate.weight", li); c->srcs.push_back({nm, ly.gu, 0, 2, (size_t)g.n_embd * g.n_ff, g.n_embd});
+                        snprintf(nm, sizeof nm, "blk.%d.ffn_up.weight", li); c->srcs.push_back({nm, ly.gu, 1, 2, (size_t)g.n_embd * g.n_ff, g.n_embd});
+                    }
+                } else {
+                    ly.g = make_mat(c.get(), (int)l.g->type, g.n_embd, g.n_ff, true);
+                    ly.u = make_mat(c.get(), (int)l.u->type, g.n_embd, g.n_ff, true);
+                    if ((!ly.g.zero && !ly.g.data) || (!ly.u.zero && !ly.u.data)) return fail_oom("ffn_gate/up");
+                    if (upload_rows(c.get(), l.g, g.n_embd, g.n_ff, ly.g, 0, 1, stage_buf) ||
+                        upload_rows(c.get(), l.u, g.n_embd, g.n_ff, ly.u, 0, 1, stage_buf))
+                        return -1;
+                    snprintf(nm, sizeof nm, "blk.%d.ffn_gate.weight", li); c->srcs.push_back({nm, ly.g, 0, 1, (size_t)g.n_embd * g.n_ff, g.n_embd});
+                    snprintf(nm, sizeof nm, "blk.%d.ffn_up.weight", li); c->srcs.push_back({nm, ly.u, 0, 1, (size_t)g.n_embd * g.n_ff, g.n_embd});
+                }
+                ly.d = make_mat(c.get(), (int)l.d->type, g.n_ff, tp.ne, true, true);
+                if (!ly.d.zero && !ly.d.data) return fail_oom("ffn_down");
+                if (upload_rows(c.get(), l.d, g.n_ff, tp.ne, ly.d, 0, 1, stage_buf, (size_t)tp.rank * tp.ne)) return -1;
+                snprintf(nm, sizeof nm, "blk.%d.ffn_down.weight", li);
+                if (whole) c->srcs.push_back({nm, ly.d, 0, 1, (size_t)g.n_ff * g.n_embd, g.n_ff});
+                ly.ffn_norm = upload_vec(c.get(), l.fn, (size_t)g.n_embd, stage_buf);
+                if (!ly.ffn_norm) return fail_oom("norm weights");
             }
-            ly.d = make_mat(c.get(), (int)l.d->type, g.n_ff, tp.ne, true, true);
-            if (!ly.d.zero && !ly.d.data) return fail_oom("ffn_down");
-            if (upload_rows(c.get(), l.d, g.n_ff, tp.ne, ly.d, 0, 1, stage_buf, (size_t)tp.rank * tp.ne)) return -1;
-            snprintf(nm, sizeof nm, "blk.%d.ffn_down.weight", li);
-            if (whole) c->srcs.push_back({nm, ly.d, 0, 1, (size_t)g.n_ff * g.n_embd, g.n_ff});
-            ly.attn_norm = upload_vec(c.get(), l.an, (size_t)g.n_embd, stage_buf);
-            ly.ffn_norm = upload_vec(c.get(), l.fn, (size_t)g.n_embd, stage_buf);
-            // biases whole; a tensor-parallel rank points at its heads' part
-            if (l.bq) ly.bq = upload_vec(c.get(), l.bq, (size_t)qd, stage_buf);
-            if (l.bk) ly.bk = upload_vec(c.get(), l.bk, (size_t)kvd, stage_buf);
-            if (l.bv) ly.bv = upload_vec(c.get(), l.bv, (size_t)kvd, stage_buf);
-            if (ly.bq) ly.bq += (size_t)tp.rank * qd_l;
-            if (ly.bk) ly.bk += (size_t)tp.rank * kvd_l;
-            if (ly.bv) ly.bv += (size_t)tp.rank * kvd_l;
-            if (!ly.attn_norm || !ly.ffn_norm) return fail_oom("norm weights");
         }
     }
     // every chunk uploaded: the pinned staging goes back
@@ -2704,12 +2781,12 @@ int ecu_matvec_stream_bench(unsigned type, const void *w_raw, int n_in, int n_ou
     at.val.cooperative = 1;
     cfg.attrs = &at;
     cfg.numAttrs = 1;
-    for (int r = 0; r < 2; r++) CK(cudaLaunchKernelEx(&cfg, fn, a));     // warm-up
+    for (int r = 0; r < 2; r++) CK(mega_launch_serial(device, cfg, fn, a));     // warm-up
     CK(cudaStreamSynchronize(tmp.stream));
     CK(cudaEventCreate(&e0));
     CK(cudaEventCreate(&e1));
     CK(cudaEventRecord(e0, tmp.stream));
-    for (int r = 0; r < rounds; r++) CK(cudaLaunchKernelEx(&cfg, fn, a));
+    for (int r = 0; r < rounds; r++) CK(mega_launch_serial(device, cfg, fn, a));
     CK(cudaEventRecord(e1, tmp.stream));
     CK(cudaStreamSynchronize(tmp.stream));
     g_launches += (uint64_t)(rounds + 2);
@@ -3049,9 +3126,12 @@ static int pf_reserve(ecu_ctx *c, int n)
     const EcuGeom &g = c->g;
     const size_t hd = (size_t)g.head_dim, qd = (size_t)g.n_head * hd, kvd = (size_t)g.n_head_kv * hd;
     size_t wmax = 0;
-    for (auto &ly : c->layers)
-        for (const DevMat *m : {&ly.qkv[0], &ly.o, &ly.gu, &ly.d})
-            wmax = std::max(wmax, (size_t)m->n_out * m->n_in);
+    for (auto &ly : c->layers) {
+        if (ly.ha)
+            for (const DevMat *m : {&ly.qkv[0], &ly.o}) wmax = std::max(wmax, (size_t)m->n_out * m->n_in);
+        if (ly.hf)
+            for (const DevMat *m : {&ly.gu, &ly.d}) wmax = std::max(wmax, (size_t)m->n_out * m->n_in);
+    }
     if (n > P.rows) {
         for (void *p : {(void *)P.X, (void *)P.QKV, (void *)P.ATT, (void *)P.GU, (void *)P.H, (void *)P.ah,
                         (void *)P.al, (void *)P.tok})
@@ -3120,7 +3200,7 @@ static bool pf_batched(const ecu_ctx *c, bool &attn2)
     attn2 = PF_QB % g.n_rep == 0 && !(ae && ae[0] == '0');
     bool batched = c->tp.world == 1 && (attn2 || g.n_ctx <= PF_ATT_MAXPOS) && (g.head_dim == 64 || g.head_dim == 128) &&
                    g.n_embd % 8 == 0 && g.n_ff % 8 == 0;
-    for (auto &ly : c->layers) batched = batched && ly.qkv.size() == 1 && ly.gu_fused;
+    for (auto &ly : c->layers) batched = batched && (!ly.ha || ly.qkv.size() == 1) && (!ly.hf || ly.gu_fused);
     return batched;
 }
 
@@ -3149,37 +3229,41 @@ static int pf_layers(ecu_ctx *c, int n, int pos0, bool attn2)
     const float kscale = 1.0f / sqrtf((float)hd);
     for (size_t li = 0; li < c->layers.size(); li++) {
         LayerDev &ly = c->layers[li];
-        k_pf_norm_split<<<n, 256, 0, c->stream>>>(P.X, ly.attn_norm, E, g.eps, P.ah, P.al);
-        if (pf_gemm(c, ly.qkv[0], n, P.QKV, nullptr)) return -1;
-        k_pf_rope_kv<<<n, 128, 0, c->stream>>>(P.QKV, ldq, g.n_head, g.n_head_kv, hd, pos0, c->rope_cs, ly.bq, ly.bk,
-                                               ly.bv, c->kc + li * plane, c->vc + li * plane, g.n_ctx);
-        if (attn2) {
-            // tiled over tokens: 64 query vectors a CTA
-            dim3 ag((unsigned)g.n_head_kv, (unsigned)((n + PF_QB / g.n_rep - 1) / (PF_QB / g.n_rep)));
-            if (hd == 128)
-                k_pf_attn2<128><<<ag, 256, pf_attn2_smem<128>(), c->stream>>>(P.QKV, ldq, n, g.n_head, g.n_rep, pos0,
-                                                                              c->kc + li * plane, c->vc + li * plane,
-                                                                              g.n_ctx, kscale, P.ATT);
-            else
-                k_pf_attn2<64><<<ag, 256, pf_attn2_smem<64>(), c->stream>>>(P.QKV, ldq, n, g.n_head, g.n_rep, pos0,
-                                                                            c->kc + li * plane, c->vc + li * plane,
-                                                                            g.n_ctx, kscale, P.ATT);
-        } else {
-            dim3 ag((unsigned)g.n_head, (unsigned)n);
-            if (hd == 128)
-                k_pf_attn<128><<<ag, 128, 0, c->stream>>>(P.QKV, ldq, g.n_head, g.n_rep, pos0, c->kc + li * plane,
-                                                          c->vc + li * plane, g.n_ctx, kscale, P.ATT);
-            else
-                k_pf_attn<64><<<ag, 64, 0, c->stream>>>(P.QKV, ldq, g.n_head, g.n_rep, pos0, c->kc + li * plane,
-                                                        c->vc + li * plane, g.n_ctx, kscale, P.ATT);
+        if (ly.ha) {
+            k_pf_norm_split<<<n, 256, 0, c->stream>>>(P.X, ly.attn_norm, E, g.eps, P.ah, P.al);
+            if (pf_gemm(c, ly.qkv[0], n, P.QKV, nullptr)) return -1;
+            k_pf_rope_kv<<<n, 128, 0, c->stream>>>(P.QKV, ldq, g.n_head, g.n_head_kv, hd, pos0, c->rope_cs, ly.bq, ly.bk,
+                                                   ly.bv, c->kc + li * plane, c->vc + li * plane, g.n_ctx);
+            if (attn2) {
+                // tiled over tokens: 64 query vectors a CTA
+                dim3 ag((unsigned)g.n_head_kv, (unsigned)((n + PF_QB / g.n_rep - 1) / (PF_QB / g.n_rep)));
+                if (hd == 128)
+                    k_pf_attn2<128><<<ag, 256, pf_attn2_smem<128>(), c->stream>>>(P.QKV, ldq, n, g.n_head, g.n_rep, pos0,
+                                                                                  c->kc + li * plane, c->vc + li * plane,
+                                                                                  g.n_ctx, kscale, P.ATT);
+                else
+                    k_pf_attn2<64><<<ag, 256, pf_attn2_smem<64>(), c->stream>>>(P.QKV, ldq, n, g.n_head, g.n_rep, pos0,
+                                                                                c->kc + li * plane, c->vc + li * plane,
+                                                                                g.n_ctx, kscale, P.ATT);
+            } else {
+                dim3 ag((unsigned)g.n_head, (unsigned)n);
+                if (hd == 128)
+                    k_pf_attn<128><<<ag, 128, 0, c->stream>>>(P.QKV, ldq, g.n_head, g.n_rep, pos0, c->kc + li * plane,
+                                                              c->vc + li * plane, g.n_ctx, kscale, P.ATT);
+                else
+                    k_pf_attn<64><<<ag, 64, 0, c->stream>>>(P.QKV, ldq, g.n_head, g.n_rep, pos0, c->kc + li * plane,
+                                                            c->vc + li * plane, g.n_ctx, kscale, P.ATT);
+            }
+            k_pf_split<<<4 * c->sms, 256, 0, c->stream>>>(P.ATT, (size_t)n * qd, P.ah, P.al);
+            if (pf_gemm(c, ly.o, n, P.X, P.X)) return -1;
         }
-        k_pf_split<<<4 * c->sms, 256, 0, c->stream>>>(P.ATT, (size_t)n * qd, P.ah, P.al);
-        if (pf_gemm(c, ly.o, n, P.X, P.X)) return -1;
-        k_pf_norm_split<<<n, 256, 0, c->stream>>>(P.X, ly.ffn_norm, E, g.eps, P.ah, P.al);
-        if (pf_gemm(c, ly.gu, n, P.GU, nullptr)) return -1;
-        k_pf_swiglu<<<4 * c->sms, 256, 0, c->stream>>>(P.GU, (size_t)n, g.n_ff, P.H);
-        k_pf_split<<<4 * c->sms, 256, 0, c->stream>>>(P.H, (size_t)n * g.n_ff, P.ah, P.al);
-        if (pf_gemm(c, ly.d, n, P.X, P.X)) return -1;
+        if (ly.hf) {
+            k_pf_norm_split<<<n, 256, 0, c->stream>>>(P.X, ly.ffn_norm, E, g.eps, P.ah, P.al);
+            if (pf_gemm(c, ly.gu, n, P.GU, nullptr)) return -1;
+            k_pf_swiglu<<<4 * c->sms, 256, 0, c->stream>>>(P.GU, (size_t)n, g.n_ff, P.H);
+            k_pf_split<<<4 * c->sms, 256, 0, c->stream>>>(P.H, (size_t)n * g.n_ff, P.ah, P.al);
+            if (pf_gemm(c, ly.d, n, P.X, P.X)) return -1;
+        }
         CK(cudaGetLastError());
     }
     g_launches += 15 * c->layers.size();

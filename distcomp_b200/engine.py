@@ -28,7 +28,7 @@ from pathlib import Path
 import numpy as np
 
 STAGE_EMBED, STAGE_LAYERS, STAGE_HEAD, STAGE_FULL, STAGE_SPAN = 0, 1, 2, 3, 4
-SPAN_EMBED, SPAN_HEAD = 1, 2
+SPAN_EMBED, SPAN_HEAD, SPAN_FFN_FIRST, SPAN_ATTN_LAST = 1, 2, 4, 8
 
 _LIB = None
 _LIB_PATH = Path(__file__).resolve().parent / "libdcb200.so"

@@ -128,6 +128,51 @@ def split_by_bytes(layer_bytes: list[int], n_stages: int, head_bytes: int = 0,
     return f if f is not None else best
 
 
+def stage_text(p) -> str:
+    """A stage's range for the bench line: layers a-b, 'a:ffn' / 'b:attn' for
+    a layer the stage holds half of, 'head' for the head alone."""
+    from . import engine as E
+    a, b, flags = p
+    if a > b:
+        return "head"
+    lo = f"{a}:ffn" if flags & E.SPAN_FFN_FIRST else str(a)
+    hi = f"{b}:attn" if flags & E.SPAN_ATTN_LAST else str(b)
+    return f"{lo}-{hi}"
+
+
+def split_half_layers(attn_cost: float, ffn_cost: float, n_layer: int, n_stages: int, head_cost: float = 0,
+                      embed_cost: float = 0, scale: float = 1000.0) -> list[tuple[int, int, int]]:
+    """Contiguous ranges of layer halves (each layer = its attention half,
+    then its FFN half) for n_stages GPUs, minimising the largest per-token
+    cost of a stage (split_by_bytes over the halves, the head alone allowed
+    on the last GPU).  Returns (first, last, flags) per stage: layers
+    first..last, flags SPAN_FFN_FIRST when layer `first` contributes its FFN
+    half only and SPAN_ATTN_LAST when layer `last` contributes its attention
+    half only (first > last: no layer).  A layer whose attention half ends one
+    GPU's range and whose FFN half starts the next one's is cut between
+    them; the residual stream is the only state that crosses."""
+    from . import engine as E
+    units = []
+    for _ in range(n_layer):
+        units += [int(round(attn_cost * scale)), int(round(ffn_cost * scale))]
+    plan = split_by_bytes(units, n_stages, head_bytes=int(round(head_cost * scale)),
+                          embed_bytes=int(round(embed_cost * scale)), head_alone=True)
+    out = []
+    for u0, u1 in plan:
+        if u0 > u1:                                   # the head alone
+            out.append((n_layer, n_layer - 1, 0))
+            continue
+        flags = (E.SPAN_FFN_FIRST if u0 % 2 else 0) | (E.SPAN_ATTN_LAST if u1 % 2 == 0 else 0)
+        out.append((u0 // 2, u1 // 2, flags))
+    return out
+
+
+# Per-token time of a layer's attention half (Q/K/V, attention, O) and FFN
+# half (gate/up, down), of the head and of the embedding row, in us, as the
+# persistent step spends them on one B200 (8B shape at positions 520-780).
+HALF_COSTS = {"llama3-8b": (22.4, 29.9, 98.0, 5.0)}
+
+
 # --------------------------------------------------------------- schedule --
 
 @dataclass(frozen=True)
@@ -290,7 +335,7 @@ class GpuStage:
     rank's step waits for that step's output."""
 
     def __init__(self, model, rank: int, n_ranks: int, first: int, last: int, n_layer: int, n_seq: int,
-                 n_ctx: int, device: int, prompts=None, stream=None):
+                 n_ctx: int, device: int, prompts=None, stream=None, halves: int = 0):
         import torch
         from . import engine as E
         self.rank, self.n_ranks, self.device = rank, n_ranks, device
@@ -300,7 +345,8 @@ class GpuStage:
         # head's GPU holds no layer, and the rank before it ends at the last
         # layer without the head)
         self.has_embed, self.has_head = rank == 0, rank == n_ranks - 1
-        flags = (E.SPAN_EMBED if self.has_embed else 0) | (E.SPAN_HEAD if self.has_head else 0)
+        # halves: SPAN_FFN_FIRST / SPAN_ATTN_LAST, a range cut inside a layer
+        flags = (E.SPAN_EMBED if self.has_embed else 0) | (E.SPAN_HEAD if self.has_head else 0) | halves
         base = [E.LlmCtx(model, E.STAGE_SPAN, first, last, n_ctx, device, span=flags)]
         self.chains = [base] + [[c.fork() for c in base] for _ in range(n_seq - 1)]
         self.n_embd = base[0].n_embd
@@ -472,17 +518,20 @@ def bench_main(args, rank: int, world: int, local: int, B) -> int:
         head_b = tensor_bytes(spec, "output.weight") + tensor_bytes(spec, "output_norm.weight")
         emb_row = tensor_bytes(spec, "token_embd.weight") // spec.n_vocab
         if args.split == "ref":
-            plan = split_stages(spec.n_layer, world)
+            plan = [(a, b, 0) for a, b in split_stages(spec.n_layer, world)]
+        elif args.split == "half" and B.CONFIG in HALF_COSTS and not args.layers:
+            plan = split_half_layers(*HALF_COSTS[B.CONFIG][:2], spec.n_layer, world, *HALF_COSTS[B.CONFIG][2:])
         else:
-            plan = split_by_bytes(lb, world, head_bytes=int(head_b * HEAD_COST), embed_bytes=emb_row, head_alone=True)
-        first, last = plan[rank]
+            plan = [(a, b, 0) for a, b in
+                    split_by_bytes(lb, world, head_bytes=int(head_b * HEAD_COST), embed_bytes=emb_row, head_alone=True)]
+        first, last, halves = plan[rank]
         n_seq = args.seqs
         prompts = [synth.prompt_tokens(args.prompt, spec.n_vocab, seed=args.seed + 1 + s) for s in range(n_seq)]
         n_tok = args.prompt + args.warmup + 2 * args.steps + 2
         if n_tok > args.n_ctx:
             raise SystemExit(f"prompt + steps need {n_tok} positions > n_ctx {args.n_ctx}")
         st = GpuStage(model, rank, world, first, last, spec.n_layer, n_seq, args.n_ctx, local,
-                      prompts=prompts if rank == 0 else None)
+                      prompts=prompts if rank == 0 else None, halves=halves)
         del buf
         torch.cuda.empty_cache()
         linked = getattr(args, "hops", "link") == "link"
@@ -622,7 +671,7 @@ def bench_main(args, rank: int, world: int, local: int, B) -> int:
                                        + f"), {n_seq} interleaved sequences; a step = one token of every "
                                          f"sequence; prompts {n} tokens each as one batch per stage",
                            "hops": "link" if linked else "nccl",
-                           "stages": [list(p) for p in plan], "split": args.split,
+                           "stages": [stage_text(p) for p in plan], "split": args.split,
                            "sequences": n_seq, "prompt_tokens": args.prompt, "n_ctx": args.n_ctx,
                            "l2": "inputs larger than L2 (4.49 GB of weights per token)"},
                 "token_roofline": {"bytes_per_token": bpt, "achieved_gbs": round(bpt * tps / 1e9, 1),

@@ -43,6 +43,11 @@ enum {
 /* ecu_ctx_open_span flags */
 #define ECU_SPAN_EMBED 1u   /* the step starts from a token: embedding row first */
 #define ECU_SPAN_HEAD  2u   /* the step ends with the output head: argmax token */
+#define ECU_SPAN_FFN_FIRST 4u   /* layer `first` contributes its FFN half only (RMSNorm,
+                                   gate/up, SwiGLU, down + residual) */
+#define ECU_SPAN_ATTN_LAST 8u   /* layer `last` contributes its attention half only
+                                   (RMSNorm, Q/K/V, attention, attn_output + residual):
+                                   a pipeline may cut a layer between its halves */
 
 typedef struct ecu_model ecu_model;   /* host view of a GGUF file (borrowed bytes) */
 typedef struct ecu_ctx   ecu_ctx;     /* one stage resident on one device           */
@@ -96,7 +101,10 @@ int  ecu_ctx_open(ecu_ctx **out, const ecu_model *m, int stage, int first, int l
  * of one node into one context (src/shard.c:358-437 gives a node's layer
  * range; its entry node also embeds, its exit node also runs the head):
  * layers first..last (first > last: none) plus the embedding and/or the
- * head by `flags`.  One persistent step per token runs all of it.  Forward
+ * head by `flags`; with ECU_SPAN_FFN_FIRST / ECU_SPAN_ATTN_LAST the range
+ * starts at layer first's FFN half / ends with layer last's attention half
+ * (a layer cut between two GPUs: the residual stream is all that crosses).
+ * One persistent step per token runs all of it.  Forward
  * contract: input a token with ECU_SPAN_EMBED, else a state in out;
  * output the state, plus out[n_embd] = the argmax with ECU_SPAN_HEAD.  The
  * position advances every step.  ecu_ctx_info reports ECU_STAGE_SPAN. */

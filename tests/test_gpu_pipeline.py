@@ -116,9 +116,9 @@ def test_fork_shares_weights_and_keeps_own_cache(eng, model_buf):
     ref.close()
 
 
-@pytest.mark.parametrize("n_ranks,n_seq,head_alone", [(2, 1, False), (2, 3, False), (3, 4, False),
-                                                       (3, 2, True)])
-def test_linked_loopback_pipeline(eng, model_buf, n_ranks, n_seq, head_alone):
+@pytest.mark.parametrize("n_ranks,n_seq,layout", [(2, 1, "ref"), (2, 3, "ref"), (3, 4, "ref"),
+                                                   (3, 2, "head_alone"), (3, 3, "half")])
+def test_linked_loopback_pipeline(eng, model_buf, n_ranks, n_seq, layout):
     """Linked stages (each step writes its output into the next stage's
     tagged words, the last stage's head its token into the first stage's) on
     one GPU, all stages on one stream in tick order: the prompts through the
@@ -130,12 +130,16 @@ def test_linked_loopback_pipeline(eng, model_buf, n_ranks, n_seq, head_alone):
     m = eng.GgufModel(model_buf(key, **over))
     n_prompt, n_gen, n_ctx = 6, 10, 64
     prompts = [synth.prompt_tokens(n_prompt, s.n_vocab, seed=41 + q) for q in range(n_seq)]
-    plan = P.split_stages(s.n_layer, n_ranks)
-    if head_alone:
-        plan = P.split_stages(s.n_layer, n_ranks - 1) + [(s.n_layer, s.n_layer - 1)]
+    plan = [(a, b, 0) for a, b in P.split_stages(s.n_layer, n_ranks)]
+    if layout == "head_alone":
+        plan = [(a, b, 0) for a, b in P.split_stages(s.n_layer, n_ranks - 1)] + [(s.n_layer, s.n_layer - 1, 0)]
+    if layout == "half":                       # layers 1 and 2 each cut between two GPUs
+        plan = [(0, 1, eng.SPAN_ATTN_LAST), (1, 2, eng.SPAN_FFN_FIRST | eng.SPAN_ATTN_LAST),
+                (2, 3, eng.SPAN_FFN_FIRST)]
     stream = torch.cuda.Stream()
-    stages = {r: P.GpuStage(m, r, n_ranks, a, b, s.n_layer, n_seq, n_ctx, 0, prompts=prompts, stream=stream)
-              for r, (a, b) in enumerate(plan)}
+    stages = {r: P.GpuStage(m, r, n_ranks, a, b, s.n_layer, n_seq, n_ctx, 0, prompts=prompts, stream=stream,
+                            halves=h)
+              for r, (a, b, h) in enumerate(plan)}
     P.link_local(stages)
     last = stages[n_ranks - 1]
     wants = [full_prefill_greedy(eng, m, s, prompts[q], n_gen, n_ctx) for q in range(n_seq)]

@@ -1,11 +1,12 @@
 """Span contexts (ecu_ctx_open_span): a layer range with the embedding and/or
-the head folded in, the unit a pipeline rank runs per token.
+the head folded in, the unit a pipeline rank runs per token; a range may
+start at a layer's FFN half or end at its attention half.
 
 A chain of spans fed token by token through the host API must produce the
 FULL context's states, greedy tokens and logits bit for bit -- a span
 boundary moves the state between buffers and changes no arithmetic -- on the
 persistent step and on the per-kernel step (ECU_MEGA=0), including a span
-that holds the head alone."""
+that holds the head alone and spans that hold half of a layer."""
 import numpy as np
 import pytest
 
@@ -62,10 +63,14 @@ def test_span_chain_matches_full(eng, model_buf, monkeypatch, mega, key):
     n_gen, n_ctx = 6, 32
     want_t, want_s, want_l = full_run(eng, m, s, prompt, n_gen, n_ctx)
     E, H = eng.SPAN_EMBED, eng.SPAN_HEAD
+    FF, AL = eng.SPAN_FFN_FIRST, eng.SPAN_ATTN_LAST
     for plan in ([(0, 1, E), (2, 3, H)],              # entry node embeds, exit node picks
                  [(0, 0, E), (1, 2, 0), (3, 3, H)],   # a middle span of layers only
                  [(0, 3, E), (4, 3, H)],              # the head alone
-                 [(0, 3, E | H)]):                    # everything: FULL's work as a span
+                 [(0, 3, E | H)],                     # everything: FULL's work as a span
+                 [(0, 1, E | AL), (1, 3, FF | H)],    # layer 1 cut between its halves
+                 [(0, 0, E | AL), (0, 2, FF | AL), (2, 3, FF | H)],   # two cuts, a span cut at both ends
+                 [(0, 3, E | AL), (3, 3, FF | H)]):   # the last FFN half with the head
         got_t, got_s, got_l, paths = span_run(eng, m, s, plan, prompt, n_gen, n_ctx)
         assert got_t == want_t, plan
         for a, b in zip(got_s, want_s):

@@ -135,9 +135,11 @@ def test_ctx_open_geometry_errors(model_buf):
     with pytest.raises(engine.EngineError, match="outside the model"):
         engine.LlmCtx(m, engine.STAGE_SPAN, 1, 5, span=engine.SPAN_HEAD)
     with pytest.raises(engine.EngineError, match="span flags"):
-        engine.LlmCtx(m, engine.STAGE_SPAN, 0, 0, span=8)
+        engine.LlmCtx(m, engine.STAGE_SPAN, 0, 0, span=16)
     with pytest.raises(engine.EngineError, match="needs the embedding or the head"):
         engine.LlmCtx(m, engine.STAGE_SPAN, 1, 0, span=0)
+    with pytest.raises(engine.EngineError, match="neither its attention nor its FFN half"):
+        engine.LlmCtx(m, engine.STAGE_SPAN, 1, 1, span=engine.SPAN_FFN_FIRST | engine.SPAN_ATTN_LAST)
 
 
 def test_ctx_bytes_q4k_segments_host_only(model_buf):

@@ -277,3 +277,34 @@ def test_gloo_pipeline_matches_plain_order(tmp_path, world, n_seq):
                        nprocs=world, join=True, start_method="spawn")
     hist = torch.load(out)
     assert hist == reference_tokens(_prompts(n_seq, n_prompt), n_layer, n_steps)
+
+
+def test_split_half_layers():
+    """Ranges of layer halves: contiguous, every half placed once, optimal
+    against brute force on the units, and the 8B shape on 8 GPUs no slower
+    than whole layers (one layer's halves may sit on two GPUs)."""
+    from distcomp_b200 import engine as E
+    n, A, F, H, Em = 5, 3.0, 5.0, 7.0, 1.0
+    for k in range(2, 5):
+        plan = P.split_half_layers(A, F, n, k, H, Em)
+        assert len(plan) == k
+        units = []
+        for a, b, fl in plan:
+            if a > b:
+                continue
+            u0 = 2 * a + (1 if fl & E.SPAN_FFN_FIRST else 0)
+            u1 = 2 * b + (0 if fl & E.SPAN_ATTN_LAST else 1)
+            units.append((u0, u1))
+        assert units[0][0] == 0 and units[-1][1] == 2 * n - 1
+        assert all(units[i][1] + 1 == units[i + 1][0] for i in range(len(units) - 1))
+        costs = [int(A * 1000), int(F * 1000)] * n
+        got = _cost([(u0, u1) for u0, u1 in units] + ([(2 * n, 2 * n - 1)] if plan[-1][0] > plan[-1][1] else []),
+                    costs, int(H * 1000), int(Em * 1000))
+        assert got == _brute(costs, k, int(H * 1000), int(Em * 1000), head_alone=True)
+    half = P.split_half_layers(22.4, 29.9, 32, 8, 98.0, 5.0)
+    t = lambda p: (0 if p[0] > p[1] else
+                   sum(22.4 * (not (i == p[0] and p[2] & E.SPAN_FFN_FIRST)) +
+                       29.9 * (not (i == p[1] and p[2] & E.SPAN_ATTN_LAST)) for i in range(p[0], p[1] + 1)))
+    worst = max(t(p) + (98.0 if i == 7 else 0) + (5.0 if i == 0 else 0) for i, p in enumerate(half))
+    assert worst < 5 * (22.4 + 29.9)
+    assert P.stage_text((4, 8, E.SPAN_FFN_FIRST)) == "4:ffn-8" and P.stage_text((32, 31, 0)) == "head"

@@ -182,7 +182,7 @@ class OCtx:
 def greedy(lib: OracleLib, buf: np.ndarray, prompt, n_gen: int, n_ctx: int = 0):
     """The reference's three-stage local run (src/shard.c:470-505): embed ->
     layers -> head per token, prompt token by token, then greedy decode.
-    Returns (generated tokens, per-step logits of the first generated step)."""
+    Returns the n_gen generated tokens."""
     m = lib.model(buf)
     emb, lay, head = m.ctx(0), None, m.ctx(2)
     lay = m.ctx(1, 0, _n_layer(buf) - 1, n_ctx)

@@ -77,6 +77,40 @@ def test_prefill_in_two_pieces(eng, model_buf):
     assert continue_greedy(one, t1, 16, s.n_embd) == continue_greedy(two, t2, 16, s.n_embd)
 
 
+@pytest.mark.parametrize("key", ["mini-q4", "mini-q8"])
+def test_prefill_long_prompt(eng, oracle_port, model_buf, key):
+    """300 prompt tokens (3 row tiles of the tensor-core GEMM, ~10 key
+    chunks of the prefill attention, a partial last query block) against the
+    per-token path and the oracle; and the same prompt in two pieces, the
+    second starting at position 150 (inside a key chunk and a row tile)."""
+    import oracle
+    s = synth.spec(key)
+    buf = model_buf(key)
+    m = eng.GgufModel(buf)
+    n_ctx, n_prompt = 512, 300
+    prompt = synth.prompt_tokens(n_prompt, s.n_vocab, seed=17)
+    a = eng.LlmCtx(m, eng.STAGE_FULL, n_ctx=n_ctx)
+    b = eng.LlmCtx(m, eng.STAGE_FULL, n_ctx=n_ctx)
+    c = eng.LlmCtx(m, eng.STAGE_FULL, n_ctx=n_ctx)
+    out_b = np.zeros(s.n_embd + 1, dtype=np.float32)
+    first = a.prefill(prompt)
+    for t in prompt:
+        assert b.forward(t, out_b) == 0
+    assert first == int(out_b[s.n_embd])
+    ok, err = vec_close(a.logits(), b.logits())
+    assert ok, f"logits rel err {err:.2e}"
+    c.prefill(prompt[:150])
+    t2 = c.prefill(prompt[150:])
+    assert t2 == first and c.pos == a.pos == n_prompt
+    ok, err = vec_close(c.logits(), a.logits())
+    assert ok, f"two pieces: logits rel err {err:.2e}"
+    want = oracle.greedy(oracle_port, buf, prompt, 8, n_ctx=n_ctx)
+    assert continue_greedy(a, first, 8, s.n_embd) == want
+    assert continue_greedy(c, t2, 8, s.n_embd) == want
+    for x in (a, b, c):
+        x.close()
+
+
 def test_prefill_errors(eng, model_buf):
     key = "mini-q4"
     s = synth.spec(key)

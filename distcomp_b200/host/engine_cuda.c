@@ -12,9 +12,14 @@
  * The stage lives on CUDA device DC_CUDA_DEVICE (default 0).  The caller's
  * layer store and float arena are not used (weights, work buffers and KV
  * cache are device memory); the llm_ctx keeps the geometry fields the
- * callers read (stage, first, last, n_* , pos).  The engine handle of each
- * llm_ctx is kept in a small table keyed by the llm_ctx's address; opening
- * the same llm_ctx again closes its previous stage first.
+ * callers read (stage, first, last, n_* , pos) and, for a HEAD stage, a host
+ * copy of the last logits in `logits` (src/engine.h:67: [n_vocab], HEAD
+ * only), refreshed by every llm_forward.  A caller that sets `pos` itself
+ * (the reference's engine_stages test rewinds lay.pos between tokens) is
+ * honoured: the stage's position follows the field before each step.  The
+ * engine handle of each llm_ctx is kept in a small table keyed by the
+ * llm_ctx's address; opening the same llm_ctx again closes its previous
+ * stage first.
  */
 #include "engine.h"
 
@@ -30,6 +35,7 @@ static struct {
     const llm_ctx *key;
     ecu_model     *m;
     ecu_ctx       *c;
+    float         *logits;     /* HEAD: the host copy the llm_ctx points at */
 } g_tab[DCB_MAX_CTX];
 
 static int slot_of(const llm_ctx *c)
@@ -50,9 +56,26 @@ static void drop(int i)
     if (i < 0) return;
     if (g_tab[i].c) ecu_ctx_close(g_tab[i].c);
     if (g_tab[i].m) ecu_model_close(g_tab[i].m);
+    free(g_tab[i].logits);
     g_tab[i].key = NULL;
     g_tab[i].c = NULL;
     g_tab[i].m = NULL;
+    g_tab[i].logits = NULL;
+}
+
+/* The caller may have set c->pos (the reference's callers rewind a LAYERS
+ * stage that way): the device stage follows before the next step. */
+static void follow_pos(llm_ctx *c, ecu_ctx *e)
+{
+    ecu_info in;
+    if (ecu_ctx_info(e, &in) == 0 && in.pos != c->pos) ecu_set_pos(e, c->pos);
+}
+
+/* A HEAD stage's logits into the llm_ctx's host copy. */
+static void pull_logits(llm_ctx *c, int slot)
+{
+    if (slot >= 0 && g_tab[slot].logits && c->n_vocab > 0)
+        ecu_get_logits(g_tab[slot].c, g_tab[slot].logits, (size_t)c->n_vocab);
 }
 
 static int device_id(void)
@@ -161,15 +184,27 @@ int llm_ctx_open(llm_ctx *c, const gguf_file *g, int stage, int first, int last,
     g_tab[i].m = m;
     g_tab[i].c = e;
     copy_info(c, e);
+    if (stage == LLM_STAGE_HEAD && c->n_vocab > 0) {
+        g_tab[i].logits = calloc((size_t)c->n_vocab, sizeof(float));
+        if (!g_tab[i].logits) {
+            if (err && errlen) snprintf(err, errlen, "out of host memory for the logits");
+            drop(i);
+            return -1;
+        }
+        c->logits = g_tab[i].logits;
+    }
     return 0;
 }
 
 int llm_forward(llm_ctx *c, int token, float *out)
 {
-    ecu_ctx *e = ctx_of(c);
+    const int slot = slot_of(c);
+    ecu_ctx  *e = slot < 0 ? NULL : g_tab[slot].c;
     if (!e) return -1;
+    follow_pos(c, e);
     const int rc = ecu_forward(e, token, out);
     copy_info(c, e);
+    if (rc == 0) pull_logits(c, slot);
     return rc;
 }
 
@@ -184,13 +219,16 @@ void llm_reset(llm_ctx *c)
 int llm_layer_once(llm_ctx *c, int layer_idx, float *out)
 {
     ecu_ctx *e = ctx_of(c);
-    return e ? ecu_layer_once(e, layer_idx, out) : -1;
+    if (!e) return -1;
+    follow_pos(c, e);
+    return ecu_layer_once(e, layer_idx, out);
 }
 
 int llm_step_layers(llm_ctx *c, int n, float *out)
 {
     ecu_ctx *e = ctx_of(c);
     if (!e) return -1;
+    follow_pos(c, e);
     const int rc = ecu_step_layers(e, n, out);
     copy_info(c, e);
     return rc;
